@@ -1,0 +1,194 @@
+/*
+ * abft_b200.h - C ABI of the B200 (sm_100a) checksum-protected GEMM library.
+ *
+ * The library replaces the native entry of the reference's `pytorch/abft`
+ * fused checker and the GEMM that precedes every check:
+ *
+ *   reference                                          this library
+ *   -------------------------------------------------  ---------------------------
+ *   F.linear(x, W, b) then CheapSumChecker.check       abft_gemm_bf16 (GEMM, check,
+ *     (pytorch/abft/injector.py:152-161,                 locate and correct in one
+ *      pytorch/abft/checkers.py:55-126)                  kernel)
+ *   abft_fused(a, b, c, bias) -> [corner, sum_c]       abft_check_only
+ *     (pytorch/abft/kernels/abft_fused.cpp:11-31,
+ *      pytorch/abft/kernels/abft_fused.cu:92-141)
+ *   s_b = b.sum(dim=1) recomputed per call             abft_encode_weight (once per
+ *     (pytorch/abft/checkers.py:119)                     weight, cacheable)
+ *
+ * Conventions
+ *   - Every pointer argument that names tensor data is a DEVICE pointer.
+ *     Matrices are row-major bf16 (raw 16-bit storage); leading dimensions are
+ *     in elements.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *   - The library allocates nothing per call.  Scratch space, when a call needs
+ *     any, comes from the caller through `workspace`.
+ *   - Every entry point returns an abft_status code (0 = ABFT_OK) and never
+ *     throws.  abft_status_string() turns a code into text.
+ *   - Calls are reentrant: distinct calls on distinct buffers may run
+ *     concurrently on different streams.
+ */
+#ifndef ABFT_B200_H_
+#define ABFT_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ABFT_B200_VERSION 1
+
+/* ---- return codes ------------------------------------------------------- */
+enum abft_status {
+  ABFT_OK = 0,
+  ABFT_ERR_INVALID_ARG = -1,   /* null pointer, negative size, bad mode      */
+  ABFT_ERR_ALIGNMENT = -2,     /* base or leading dimension breaks TMA rules */
+  ABFT_ERR_UNSUPPORTED = -3,   /* shape / tile combination not built         */
+  ABFT_ERR_WORKSPACE = -4,     /* workspace missing or too small             */
+  ABFT_ERR_CUDA = -5,          /* CUDA runtime error (launch or attribute)   */
+  ABFT_ERR_NO_DEVICE = -6,     /* no sm_100 device current                   */
+  ABFT_ERR_DRIVER = -7         /* tensor-map encoder unavailable             */
+};
+
+/* ---- mode bits for abft_gemm_bf16 -------------------------------------- */
+#define ABFT_MODE_OFF      0u  /* plain GEMM (+bias); same kernel, checks compiled out */
+#define ABFT_MODE_DETECT   1u  /* per-tile weighted row checksums: detect + locate     */
+#define ABFT_MODE_CORRECT  2u  /* also correct located faults before the bf16 store    */
+#define ABFT_MODE_REF      4u  /* scalar corner-vs-sum(C) check of checkers.py:112-126 */
+
+/* ---- status bits in abft_report.status ---------------------------------- */
+#define ABFT_STATUS_FAULT          1u  /* at least one checksum mismatch          */
+#define ABFT_STATUS_UNLOCATED      2u  /* a mismatch could not be pinned to a column */
+#define ABFT_STATUS_OVERFLOW       4u  /* more faults than record slots          */
+#define ABFT_STATUS_DEVICE_TIMEOUT 8u  /* a bounded device wait gave up          */
+#define ABFT_STATUS_REF_FAIL      16u  /* scalar reference-rule check failed     */
+
+/* ---- record flags ------------------------------------------------------- */
+#define ABFT_REC_DETECTED  1u
+#define ABFT_REC_LOCATED   2u
+#define ABFT_REC_CORRECTED 4u
+
+/* One detected fault: the (row, tile-segment) whose checksums disagree.
+ * `col` is the located global column, or -1 when the weighted residual did
+ * not pin a single column. `residual` is (actual - expected) row sum over the
+ * tile segment (the fault magnitude for a single fault), `residual_w` the same
+ * for the column-index-weighted sum, `threshold` the bound it was tested on. */
+typedef struct abft_fault_record {
+  int32_t row;
+  int32_t col;
+  float residual;
+  float residual_w;
+  float threshold;
+  uint32_t flags;
+} abft_fault_record;
+
+/* Fault report, device-resident, caller-allocated with abft_report_bytes().
+ * abft_gemm_bf16 / abft_check_only reset the header on the call's stream
+ * before the kernel runs, so the caller need not zero it. */
+typedef struct abft_report {
+  uint32_t status;       /* ABFT_STATUS_* bits                               */
+  uint32_t n_faults;     /* mismatching (row, tile) segments, all of them     */
+  uint32_t n_located;    /* of those, pinned to one column                    */
+  uint32_t n_corrected;  /* of those, corrected in the stored output          */
+  uint32_t overflow;     /* records dropped for lack of capacity              */
+  uint32_t capacity;     /* record slots after this header                    */
+  uint32_t tile_m;       /* output tile the checksums were defined on         */
+  uint32_t tile_n;       /* data columns per tile (tile width - 8 with checks) */
+  float corner;          /* ABFT_MODE_REF: dot(sum_rows(A), sum_cols(B)) + M*sum(bias) */
+  float sum_c;           /* ABFT_MODE_REF: sum of the stored output            */
+  float abs_err;         /* ABFT_MODE_REF: |corner - sum_c|                    */
+  float rel_err;         /* ABFT_MODE_REF: abs_err / max(|sum_c|, 1)           */
+  int32_t ref_ok;        /* ABFT_MODE_REF: 1 pass, 0 fail; -1 not evaluated     */
+  uint32_t reserved[3];
+  /* abft_fault_record records[capacity] follows (64-byte header). */
+} abft_report;
+
+/* Arguments of the fused checksum-protected GEMM
+ *   C[M, N] = A[M, K] * B[N, K]^T (+ bias[N])
+ * B is stored like nn.Linear.weight: N rows of K contiguous elements.       */
+typedef struct abft_gemm_args {
+  const void* A;          /* bf16 [M, lda]                                    */
+  const void* B;          /* bf16 [N, ldb]                                    */
+  void* C;                /* bf16 [M, ldc] output                             */
+  const void* bias;       /* bf16 [N] or NULL                                 */
+  int64_t M, N, K;
+  int64_t lda, ldb, ldc;
+  uint32_t mode;          /* ABFT_MODE_* bits                                 */
+  int32_t tile_n;         /* 0 = choose, else 128 or 256                      */
+  float thr_scale;        /* tau in thr = tau * sqrt(K) * max|C_row_segment|  */
+  float thr_abs;          /* absolute floor added to thr                      */
+  float tol_abs, tol_rel; /* ABFT_MODE_REF tolerances (checkers.py:96-110)    */
+  const void* checksums;  /* abft_encode_weight(B, tile_n) output, or NULL    */
+  void* workspace;        /* device scratch, abft_gemm_workspace_bytes()      */
+  size_t workspace_bytes;
+  const int32_t* inject_rows;   /* debug: faults added to the fp32 accumulator */
+  const int32_t* inject_cols;   /*        before the checksum epilogue, device */
+  const float* inject_deltas;   /*        arrays of n_inject entries           */
+  int32_t n_inject;             /*        (at most ABFT_MAX_INJECT)             */
+  void* report;           /* abft_report + records, or NULL when mode == OFF  */
+  int32_t report_capacity;
+  int32_t num_sms;        /* 0 = all SMs of the current device                */
+} abft_gemm_args;
+
+#define ABFT_MAX_INJECT 64
+
+/* Library version (ABFT_B200_VERSION) and the human-readable text of a code. */
+int abft_version(void);
+const char* abft_status_string(int status);
+
+/* Bytes of a report with `capacity` records. */
+size_t abft_report_bytes(int32_t capacity);
+
+/* Tile width the library picks for an (M, N) output when tile_n == 0. */
+int32_t abft_pick_tile_n(int64_t M, int64_t N, int32_t num_sms);
+
+/* Bytes of the per-tile checksum block of a [N, K] weight for tile_n. */
+size_t abft_checksum_bytes(int64_t N, int64_t K, int32_t tile_n);
+
+/* Per-tile weighted row checksums of B (the "Be" encoding of checkers.py:119,
+ * restricted to each output tile and paired with a column-index-weighted
+ * copy), as the 8 bf16 rows the fused GEMM appends to each B-operand tile.
+ * With checks on, an output tile of width tile_n carries D = tile_n - 8 data
+ * columns. out is bf16 [ceil(N/D) * 8, K] row-major; for tile t
+ *   v1[k] = sum_j B[t*D + j, k],   v2[k] = sum_j (j+1) B[t*D + j, k]
+ * (j over the tile's valid rows, fp32 sums), rows 8t+0..2 hold v1 split into
+ * three bf16 terms (hi, mid, lo), rows 8t+3..5 the same for v2, rows 8t+6..7
+ * are zero. Cache it per weight. Replaces the per-call `b_2d.sum(dim=1)`
+ * of checkers.py:119. */
+int abft_encode_weight(const void* B, int64_t N, int64_t K, int64_t ldb,
+                       int32_t tile_n, void* out, void* stream);
+
+/* Workspace the fused GEMM needs for these arguments (0 when none). */
+size_t abft_gemm_workspace_bytes(const abft_gemm_args* args);
+
+/* The fused checksum-protected GEMM. Replaces F.linear + CheapSumChecker.check
+ * (pytorch/abft/injector.py:152-161 -> pytorch/abft/checkers.py:55-126). */
+int abft_gemm_bf16(const abft_gemm_args* args, void* stream);
+
+/* Post-hoc check of an existing output C = A * B^T (+ bias), the drop-in for
+ * the reference's abft_fused(a, b, c, bias) -> [corner, sum_c]
+ * (pytorch/abft/kernels/abft_fused.cpp:11-31, abft_fused.cu:92-141) and the
+ * "python" backend arithmetic (pytorch/abft/checkers.py:112-126):
+ *   corner = dot(sum_i A[i,:], sum_j B[j,:]) + M * sum(bias)
+ *   sum_c  = sum(C)
+ *   ok     = |corner - sum_c| <= tol_abs  or  |corner - sum_c| / max(|sum_c|, 1) <= tol_rel
+ * B is given as [N, K] (ldb) when b_kn == 0, or as [K, N] (ldb) when b_kn == 1.
+ * Results land in report->corner/sum_c/abs_err/rel_err/ref_ok. When
+ * `locate` is non-zero the call also compares every row and column sum of C
+ * with A*(B e) and (e^T A)*B and records mismatching rows and columns
+ * (row = index, col = -1 for a row record; row = -1, col = index for a column
+ * record). Needs abft_check_workspace_bytes() of workspace. */
+size_t abft_check_workspace_bytes(int64_t M, int64_t N, int64_t K);
+int abft_check_only(const void* A, int64_t lda, const void* B, int64_t ldb,
+                    int32_t b_kn, const void* C, int64_t ldc, const void* bias,
+                    int64_t M, int64_t N, int64_t K, float tol_abs,
+                    float tol_rel, int32_t locate, float thr_scale,
+                    void* workspace, size_t workspace_bytes, void* report,
+                    int32_t report_capacity, void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* ABFT_B200_H_ */

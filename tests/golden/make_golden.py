@@ -1,0 +1,160 @@
+"""Write the golden fixtures of the reference's own ABFT path.
+
+Run in the build container, where the reference is mounted read-only:
+
+    python tests/golden/make_golden.py [--reference /root/reference]
+
+It imports the reference package ``abft`` (pytorch/abft) and records, on
+seeded CPU bf16 inputs:
+
+  ref_checker_cases.npz / .json
+      CheapSumChecker.check results (python backend,
+      pytorch/abft/checkers.py:55-126) on clean and fault-injected outputs,
+      with and without bias, including a ragged shape.
+  ref_injector_sequences.json
+      the fault indices, injection flags and check counts AbftInjector
+      (pytorch/abft/injector.py:19-189) produces for several seeds,
+      probabilities and sample rates, plus one export_summary()
+      (pytorch/abft/stats.py:175-220).
+
+Nothing under tests/ reads the reference at test time: only these fixtures.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import random
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+HERE = Path(__file__).resolve().parent
+
+
+def bits(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16).copy()
+
+
+def seeded(m: int, n: int, k: int, seed: int, with_bias: bool):
+    g = torch.Generator().manual_seed(seed)
+    a = (torch.randn(m, k, generator=g) * k ** -0.5).bfloat16()
+    w = (torch.randn(n, k, generator=g) * k ** -0.5).bfloat16()
+    b = (torch.randn(n, generator=g) * 0.02).bfloat16() if with_bias else None
+    return a, w, b
+
+
+CASES = [
+    # name, M, K, N, bias, seed, fault magnitude (None = clean; "max" = 2^8 * max|C|)
+    ("small_clean", 64, 128, 96, False, 0, None),
+    ("small_fault_1", 64, 128, 96, False, 0, 1.0),
+    ("ragged_bias_clean", 200, 136, 72, True, 1, None),
+    ("ragged_bias_fault_max", 200, 136, 72, True, 1, "max"),
+    ("mid_bias_fault_1", 128, 384, 256, True, 2, 1.0),
+    ("mid_clean", 256, 256, 128, False, 3, None),
+    ("mid_fault_tiny", 256, 256, 128, False, 3, 1e-3),
+    ("wide_fault_max", 96, 512, 384, False, 4, "max"),
+]
+
+
+def run_cases(abft):
+    from abft.checkers import OpMeta
+
+    cfg = abft.AbftConfig(enable=True)
+    checker = abft.CheapSumChecker(cfg)
+    arrays = {}
+    meta = []
+    for name, m, k, n, with_bias, seed, fault in CASES:
+        a, w, b = seeded(m, n, k, seed, with_bias)
+        c = F.linear(a, w, b)
+        idx = None
+        mag = None
+        if fault is not None:
+            rng = random.Random(seed)
+            idx = rng.randrange(c.numel())
+            mag = float(2.0 ** 8 * c.float().abs().max().item()) if fault == "max" else float(fault)
+            c = c.clone()
+            c.view(-1)[idx] += mag
+        b2 = w.t()
+        res = checker.check(a, b2, c, OpMeta("linear", "prefill", "golden"), bias_1d=b)
+        arrays[f"{name}_a"] = bits(a)
+        arrays[f"{name}_w"] = bits(w)
+        arrays[f"{name}_c"] = bits(c)
+        if b is not None:
+            arrays[f"{name}_bias"] = bits(b)
+        meta.append({
+            "name": name, "M": m, "K": k, "N": n, "bias": with_bias, "seed": seed,
+            "fault_index": idx, "fault_row": None if idx is None else idx // n,
+            "fault_col": None if idx is None else idx % n, "fault_magnitude": mag,
+            "ok": bool(res.ok), "abs_err": res.abs_err, "rel_err": res.rel_err,
+            "abft_corner": res.abft_corner, "sum_c": res.sum_c,
+        })
+    return arrays, meta
+
+
+INJ_CONFIGS = [
+    {"seed": 2026, "inject_probability": 1.0, "sample_rate": 1.0},
+    {"seed": 7, "inject_probability": 0.5, "sample_rate": 1.0},
+    {"seed": 11, "inject_probability": 0.5, "sample_rate": 0.5},
+    {"seed": 3, "inject_probability": 0.0, "sample_rate": 0.5},
+]
+INJ_SHAPES = [(4, 16, 8), (3, 16, 8), (8, 32, 24), (1, 16, 8), (5, 8, 40), (4, 16, 8), (2, 64, 16), (6, 16, 8),
+              (7, 24, 8), (4, 16, 32), (9, 8, 8), (4, 16, 8)]
+
+
+def run_injector(abft):
+    out = []
+    summary = None
+    for ci, conf in enumerate(INJ_CONFIGS):
+        cfg = abft.AbftConfig(enable=True, inject_fault=True, inject_magnitude=1.0,
+                              inject_probability=conf["inject_probability"], sample_rate=conf["sample_rate"],
+                              seed=conf["seed"], enable_matmul=False, enable_bmm=False)
+        stats = abft.AbftStatsCollector()
+        checker = abft.CheapSumChecker(cfg)
+        calls = []
+        g = torch.Generator().manual_seed(100 + ci)
+        with abft.AbftInjector(cfg, checker, stats):
+            for (m, k, n) in INJ_SHAPES:
+                x = (torch.randn(m, k, generator=g) * 0.1).bfloat16()
+                w = (torch.randn(n, k, generator=g) * 0.1).bfloat16()
+                before = stats.total_checks
+                y = F.linear(x, w)
+                clean = torch.ops.aten.linear(x, w)
+                diff = (y.float() - clean.float()).abs().view(-1)
+                injected = bool(diff.max().item() > 0)
+                calls.append({"shape": [m, k, n], "injected": injected,
+                              "index": int(diff.argmax().item()) if injected else None,
+                              "checked": stats.total_checks - before})
+        entry = dict(conf)
+        entry["calls"] = calls
+        entry["total_injections"] = stats.total_injections
+        entry["detected_injections"] = stats.total_detected_injections
+        entry["total_checks"] = stats.total_checks
+        entry["total_failures"] = stats.total_failures
+        out.append(entry)
+        if ci == 0:
+            summary = stats.export_summary()
+    return out, summary
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default="/root/reference")
+    args = ap.parse_args()
+    sys.path.insert(0, str(Path(args.reference) / "pytorch"))
+    import abft  # the reference package
+
+    torch.set_num_threads(1)
+    arrays, meta = run_cases(abft)
+    np.savez_compressed(HERE / "ref_checker_cases.npz", **arrays)
+    (HERE / "ref_checker_cases.json").write_text(json.dumps(meta, indent=1))
+    inj, summary = run_injector(abft)
+    (HERE / "ref_injector_sequences.json").write_text(json.dumps({"configs": inj, "summary_config0": summary},
+                                                                 indent=1))
+    print(f"wrote {len(meta)} checker cases and {len(inj)} injector sequences to {HERE}")
+
+
+if __name__ == "__main__":
+    main()

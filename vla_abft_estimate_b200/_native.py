@@ -1,0 +1,205 @@
+"""ctypes binding of libabft_b200.so (declarations: include/abft_b200.h).
+
+The C ABI takes plain pointers and sizes only; this module maps them to
+ctypes and raises ``AbftError`` for every non-zero status. There is no
+fallback: if the library is missing, every op fails loudly.
+"""
+from __future__ import annotations
+
+import ctypes
+import struct
+from dataclasses import dataclass, field
+from typing import List, Optional
+
+from . import _build
+
+# ---- constants mirrored from include/abft_b200.h ------------------------------
+ABFT_OK = 0
+MODE_OFF = 0
+MODE_DETECT = 1
+MODE_CORRECT = 2
+MODE_REF = 4
+
+STATUS_FAULT = 1
+STATUS_UNLOCATED = 2
+STATUS_OVERFLOW = 4
+STATUS_DEVICE_TIMEOUT = 8
+STATUS_REF_FAIL = 16
+
+REC_DETECTED = 1
+REC_LOCATED = 2
+REC_CORRECTED = 4
+
+MAX_INJECT = 64
+REPORT_HEADER_BYTES = 64
+RECORD_BYTES = 24
+
+EXPORTED_SYMBOLS = (
+    "abft_version",
+    "abft_status_string",
+    "abft_report_bytes",
+    "abft_pick_tile_n",
+    "abft_checksum_bytes",
+    "abft_encode_weight",
+    "abft_gemm_workspace_bytes",
+    "abft_gemm_bf16",
+    "abft_check_workspace_bytes",
+    "abft_check_only",
+)
+
+
+class AbftError(RuntimeError):
+    """A library call returned a non-zero abft_status."""
+
+    def __init__(self, fn: str, code: int, text: str):
+        super().__init__(f"{fn} failed with status {code}: {text}")
+        self.fn = fn
+        self.code = code
+
+
+class GemmArgs(ctypes.Structure):
+    """Mirror of ``abft_gemm_args``."""
+
+    _fields_ = [
+        ("A", ctypes.c_void_p),
+        ("B", ctypes.c_void_p),
+        ("C", ctypes.c_void_p),
+        ("bias", ctypes.c_void_p),
+        ("M", ctypes.c_int64),
+        ("N", ctypes.c_int64),
+        ("K", ctypes.c_int64),
+        ("lda", ctypes.c_int64),
+        ("ldb", ctypes.c_int64),
+        ("ldc", ctypes.c_int64),
+        ("mode", ctypes.c_uint32),
+        ("tile_n", ctypes.c_int32),
+        ("thr_scale", ctypes.c_float),
+        ("thr_abs", ctypes.c_float),
+        ("tol_abs", ctypes.c_float),
+        ("tol_rel", ctypes.c_float),
+        ("checksums", ctypes.c_void_p),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_size_t),
+        ("inject_rows", ctypes.c_void_p),
+        ("inject_cols", ctypes.c_void_p),
+        ("inject_deltas", ctypes.c_void_p),
+        ("n_inject", ctypes.c_int32),
+        ("report", ctypes.c_void_p),
+        ("report_capacity", ctypes.c_int32),
+        ("num_sms", ctypes.c_int32),
+    ]
+
+
+_LIB: Optional[ctypes.CDLL] = None
+
+
+def lib() -> ctypes.CDLL:
+    """Load the in-tree shared library (built by ``_build.build()``)."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    path = _build.LIB_PATH
+    if not path.exists():
+        raise RuntimeError(
+            f"{path} is missing: build it with `python -m vla_abft_estimate_b200._build` "
+            "(or __graft_entry__.build()); there is no fallback path"
+        )
+    L = ctypes.CDLL(str(path))
+    vp, i32, i64, f32, sz = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
+    L.abft_version.restype = ctypes.c_int
+    L.abft_version.argtypes = []
+    L.abft_status_string.restype = ctypes.c_char_p
+    L.abft_status_string.argtypes = [ctypes.c_int]
+    L.abft_report_bytes.restype = sz
+    L.abft_report_bytes.argtypes = [i32]
+    L.abft_pick_tile_n.restype = i32
+    L.abft_pick_tile_n.argtypes = [i64, i64, i32]
+    L.abft_checksum_bytes.restype = sz
+    L.abft_checksum_bytes.argtypes = [i64, i64, i32]
+    L.abft_encode_weight.restype = ctypes.c_int
+    L.abft_encode_weight.argtypes = [vp, i64, i64, i64, i32, vp, vp]
+    L.abft_gemm_workspace_bytes.restype = sz
+    L.abft_gemm_workspace_bytes.argtypes = [ctypes.POINTER(GemmArgs)]
+    L.abft_gemm_bf16.restype = ctypes.c_int
+    L.abft_gemm_bf16.argtypes = [ctypes.POINTER(GemmArgs), vp]
+    L.abft_check_workspace_bytes.restype = sz
+    L.abft_check_workspace_bytes.argtypes = [i64, i64, i64]
+    L.abft_check_only.restype = ctypes.c_int
+    L.abft_check_only.argtypes = [vp, i64, vp, i64, i32, vp, i64, vp, i64, i64, i64, f32, f32, i32, f32, vp, sz,
+                                  vp, i32, vp]
+    _LIB = L
+    return L
+
+
+def status_string(code: int) -> str:
+    return lib().abft_status_string(int(code)).decode()
+
+
+def check(fn: str, code: int) -> None:
+    if code != ABFT_OK:
+        raise AbftError(fn, code, status_string(code))
+
+
+# ---- report parsing ----------------------------------------------------------------
+@dataclass
+class FaultRecord:
+    row: int
+    col: int
+    residual: float
+    residual_w: float
+    threshold: float
+    flags: int
+
+    @property
+    def located(self) -> bool:
+        return bool(self.flags & REC_LOCATED)
+
+    @property
+    def corrected(self) -> bool:
+        return bool(self.flags & REC_CORRECTED)
+
+
+@dataclass
+class FaultReport:
+    """Host copy of an ``abft_report``."""
+
+    status: int = 0
+    n_faults: int = 0
+    n_located: int = 0
+    n_corrected: int = 0
+    overflow: int = 0
+    capacity: int = 0
+    tile_m: int = 0
+    tile_n: int = 0
+    corner: float = 0.0
+    sum_c: float = 0.0
+    abs_err: float = 0.0
+    rel_err: float = 0.0
+    ref_ok: int = -1
+    records: List[FaultRecord] = field(default_factory=list)
+
+    @property
+    def fault_detected(self) -> bool:
+        return bool(self.status & STATUS_FAULT)
+
+    @property
+    def device_timeout(self) -> bool:
+        return bool(self.status & STATUS_DEVICE_TIMEOUT)
+
+    def coords(self) -> List[tuple]:
+        """Sorted (row, col) of every stored record."""
+        return sorted((r.row, r.col) for r in self.records)
+
+    @classmethod
+    def from_bytes(cls, buf: bytes) -> "FaultReport":
+        if len(buf) < REPORT_HEADER_BYTES:
+            raise ValueError("report buffer shorter than its header")
+        (status, n_faults, n_located, n_corrected, overflow, capacity, tile_m, tile_n, corner, sum_c, abs_err,
+         rel_err, ref_ok) = struct.unpack_from("<8I4fi", buf, 0)
+        rep = cls(status, n_faults, n_located, n_corrected, overflow, capacity, tile_m, tile_n, corner, sum_c,
+                  abs_err, rel_err, ref_ok)
+        n = min(n_faults, capacity, (len(buf) - REPORT_HEADER_BYTES) // RECORD_BYTES)
+        for i in range(n):
+            row, col, res, resw, thr, flags = struct.unpack_from("<iifffI", buf, REPORT_HEADER_BYTES + i * RECORD_BYTES)
+            rep.records.append(FaultRecord(row, col, res, resw, thr, flags))
+        return rep

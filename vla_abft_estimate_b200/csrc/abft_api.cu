@@ -1,0 +1,468 @@
+// abft_api.cu - the extern "C" entry points of libabft_b200.so.
+//
+// Host side of the library: argument validation, TMA tensor-map encoding,
+// workspace layout and the launch sequence of each call. Declarations and the
+// reference interface each entry replaces are in include/abft_b200.h.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <math.h>
+
+#include <mutex>
+
+#include "aux_kernels.cuh"
+#include "gemm_kernel.cuh"
+
+using namespace abft;
+
+namespace {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encoder() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+constexpr int kMaxDevices = 64;
+struct DeviceInfo {
+  bool init;
+  bool ok;
+  int sms;
+  bool attr_set[4];
+};
+DeviceInfo g_dev[kMaxDevices];
+std::mutex g_mu;
+
+int current_device(int* dev_out, DeviceInfo* info) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    return ABFT_ERR_NO_DEVICE;
+  }
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (!d.init) {
+    int major = 0, minor = 0, sms = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaGetLastError();
+    d.ok = (major == 10 && minor == 0);
+    d.sms = sms;
+    d.init = true;
+  }
+  if (!d.ok) return ABFT_ERR_NO_DEVICE;
+  *dev_out = dev;
+  *info = d;
+  return ABFT_OK;
+}
+
+template <int BN, bool CHECK>
+int ensure_smem_attr(int dev, int slot) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_dev[dev].attr_set[slot]) return ABFT_OK;
+  if (cudaFuncSetAttribute(abft_gemm_kernel<BN, CHECK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           GemmCfg<BN, CHECK>::kSmemBytes) != cudaSuccess) {
+    cudaGetLastError();
+    return ABFT_ERR_CUDA;
+  }
+  g_dev[dev].attr_set[slot] = true;
+  return ABFT_OK;
+}
+
+int make_tmap_kmajor(CUtensorMap* m, const void* ptr, int64_t inner, int64_t outer, int64_t ld, int box_outer) {
+  EncodeTiledFn enc = get_encoder();
+  if (enc == nullptr) return ABFT_ERR_DRIVER;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+  cuuint32_t box[2] = {64u, static_cast<cuuint32_t>(box_outer)};
+  cuuint32_t es[2] = {1u, 1u};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? ABFT_OK : ABFT_ERR_ALIGNMENT;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+int launch_status() {
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? ABFT_OK : ABFT_ERR_CUDA;
+}
+
+// Rows per block of a column-sum pass: enough row blocks that the grid has
+// at least two blocks per SM.
+int rows_per_block(int64_t R, int64_t C, int sms) {
+  const int64_t col_blocks = cdiv(C, 64);
+  const int64_t want_rb = cdiv(2 * static_cast<int64_t>(sms), col_blocks);
+  int64_t rpb = cdiv(R, want_rb < 1 ? 1 : want_rb);
+  rpb = cdiv(rpb, 32) * 32;
+  if (rpb < 32) rpb = 32;
+  return static_cast<int>(rpb);
+}
+
+// Column sums of a row-major [R, C] bf16 matrix into out[C] (with stats also
+// out_max[C] and out_abs[C]), through partials in `partial` ([nrb][C], and
+// 2 * [nrb][C] more with stats).
+int colsum(const void* X, int64_t ld, int64_t R, int64_t C, const float* w, float* partial, float* out,
+           float* out_max, float* out_abs, int sms, cudaStream_t s) {
+  const int rpb = rows_per_block(R, C, sms);
+  const int nrb = static_cast<int>(cdiv(R, rpb));
+  float* pstat = out_max != nullptr ? partial + static_cast<int64_t>(nrb) * C : nullptr;
+  dim3 g(static_cast<unsigned>(cdiv(C, 64)), static_cast<unsigned>(nrb));
+  colsum_partial_kernel<<<g, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(X), ld, static_cast<int>(R),
+                                          static_cast<int>(C), rpb, w, partial, pstat);
+  reduce_partials_kernel<<<static_cast<unsigned>(cdiv(C, 256)), 256, 0, s>>>(partial, pstat, nrb, static_cast<int>(C),
+                                                                             out, out_max, out_abs);
+  return launch_status();
+}
+
+size_t colsum_partial_floats(int64_t R, int64_t C, int sms, bool with_stats) {
+  const int rpb = rows_per_block(R, C, sms);
+  return static_cast<size_t>(cdiv(R, rpb)) * C * (with_stats ? 3 : 1);
+}
+
+int rowdot(const void* X, int64_t ld, int64_t R, int64_t C, const float* vec, float* out, float* out_max,
+           float* out_abs, cudaStream_t s) {
+  rowdot_kernel<<<static_cast<unsigned>(cdiv(R, 8)), 256, 0, s>>>(static_cast<const __nv_bfloat16*>(X), ld,
+                                                                   static_cast<int>(R), static_cast<int>(C), vec, out,
+                                                                   out_max, out_abs);
+  return launch_status();
+}
+
+struct GemmWs {
+  size_t v_off, pa_off, u_off, pb_off, vf_off, parts_off, total;
+};
+
+void gemm_ws_layout(const abft_gemm_args* a, int bn, int sms, GemmWs* w) {
+  const bool check = (a->mode & (ABFT_MODE_DETECT | ABFT_MODE_CORRECT)) != 0;
+  size_t off = 0;
+  w->v_off = w->pa_off = w->u_off = w->pb_off = w->vf_off = w->parts_off = 0;
+  if (check && a->checksums == nullptr) {
+    w->v_off = off;
+    off = align256(off + abft_checksum_bytes(a->N, a->K, bn));
+  }
+  if (a->mode & ABFT_MODE_REF) {
+    const int bd = check ? bn - kChkRows : bn;
+    const size_t tiles = static_cast<size_t>(cdiv(a->M, kBM) * cdiv(a->N, bd));
+    w->pa_off = off;
+    off = align256(off + 4 * colsum_partial_floats(a->M, a->K, sms, false));
+    w->u_off = off;
+    off = align256(off + 4 * static_cast<size_t>(a->K));
+    w->pb_off = off;
+    off = align256(off + 4 * colsum_partial_floats(a->N, a->K, sms, false));
+    w->vf_off = off;
+    off = align256(off + 4 * static_cast<size_t>(a->K));
+    w->parts_off = off;
+    off = align256(off + 4 * 8 * tiles);
+  }
+  w->total = off;
+}
+
+int validate_gemm(const abft_gemm_args* a) {
+  if (a == nullptr || a->A == nullptr || a->B == nullptr || a->C == nullptr) return ABFT_ERR_INVALID_ARG;
+  if (a->M < 0 || a->N < 0 || a->K < 0) return ABFT_ERR_INVALID_ARG;
+  if (a->M > (1ll << 30) || a->N > (1ll << 30) || a->K > (1ll << 30)) return ABFT_ERR_UNSUPPORTED;
+  if (a->lda < a->K || a->ldb < a->K || a->ldc < a->N) return ABFT_ERR_INVALID_ARG;
+  if ((a->K % 8) || (a->N % 8) || (a->lda % 8) || (a->ldb % 8) || (a->ldc % 8)) return ABFT_ERR_ALIGNMENT;
+  if (!aligned16(a->A) || !aligned16(a->B) || !aligned16(a->C)) return ABFT_ERR_ALIGNMENT;
+  if (a->bias != nullptr && !aligned16(a->bias)) return ABFT_ERR_ALIGNMENT;
+  if (a->mode & ~(ABFT_MODE_DETECT | ABFT_MODE_CORRECT | ABFT_MODE_REF)) return ABFT_ERR_INVALID_ARG;
+  if (a->tile_n != 0 && a->tile_n != 128 && a->tile_n != 256) return ABFT_ERR_UNSUPPORTED;
+  if (a->mode != ABFT_MODE_OFF && (a->report == nullptr || a->report_capacity < 0)) return ABFT_ERR_INVALID_ARG;
+  if (a->report != nullptr && !aligned16(a->report)) return ABFT_ERR_ALIGNMENT;
+  if (a->n_inject < 0 || a->n_inject > ABFT_MAX_INJECT) return ABFT_ERR_INVALID_ARG;
+  if (a->n_inject > 0 && (a->inject_rows == nullptr || a->inject_cols == nullptr || a->inject_deltas == nullptr))
+    return ABFT_ERR_INVALID_ARG;
+  if (a->checksums != nullptr && !aligned16(a->checksums)) return ABFT_ERR_ALIGNMENT;
+  if (!(a->thr_scale >= 0.f) || !(a->thr_abs >= 0.f)) return ABFT_ERR_INVALID_ARG;
+  return ABFT_OK;
+}
+
+template <int BN, bool CHECK>
+int launch_gemm(int dev, int slot, const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmV,
+                const GemmParams& p, int grid, cudaStream_t s) {
+  int rc = ensure_smem_attr<BN, CHECK>(dev, slot);
+  if (rc != ABFT_OK) return rc;
+  abft_gemm_kernel<BN, CHECK><<<grid, kThreads, GemmCfg<BN, CHECK>::kSmemBytes, s>>>(tmA, tmB, tmV, p);
+  return launch_status();
+}
+
+}  // namespace
+
+extern "C" {
+
+int abft_version(void) { return ABFT_B200_VERSION; }
+
+const char* abft_status_string(int status) {
+  switch (status) {
+    case ABFT_OK: return "ok";
+    case ABFT_ERR_INVALID_ARG: return "invalid argument";
+    case ABFT_ERR_ALIGNMENT: return "alignment: pointers must be 16-byte aligned, K, N and leading dimensions multiples of 8";
+    case ABFT_ERR_UNSUPPORTED: return "unsupported shape or tile width";
+    case ABFT_ERR_WORKSPACE: return "workspace missing or too small";
+    case ABFT_ERR_CUDA: return "CUDA runtime error";
+    case ABFT_ERR_NO_DEVICE: return "no sm_100 (B200) device is current";
+    case ABFT_ERR_DRIVER: return "cuTensorMapEncodeTiled unavailable from the driver";
+    default: return "unknown status";
+  }
+}
+
+size_t abft_report_bytes(int32_t capacity) {
+  if (capacity < 0) capacity = 0;
+  return sizeof(abft_report) + static_cast<size_t>(capacity) * sizeof(abft_fault_record);
+}
+
+int32_t abft_pick_tile_n(int64_t M, int64_t N, int32_t num_sms) {
+  if (num_sms <= 0) num_sms = 148;
+  const int64_t tiles256 = cdiv(M, kBM) * cdiv(N, 256);
+  return tiles256 >= num_sms ? 256 : 128;
+}
+
+size_t abft_checksum_bytes(int64_t N, int64_t K, int32_t tile_n) {
+  if (tile_n != 128 && tile_n != 256) return 0;
+  return static_cast<size_t>(cdiv(N, tile_n - kChkRows)) * kChkRows * static_cast<size_t>(K) * 2;
+}
+
+int abft_encode_weight(const void* B, int64_t N, int64_t K, int64_t ldb, int32_t tile_n, void* out, void* stream) {
+  if (B == nullptr || out == nullptr || N <= 0 || K <= 0 || ldb < K) return ABFT_ERR_INVALID_ARG;
+  if ((K % 8) || (ldb % 8) || !aligned16(B) || !aligned16(out)) return ABFT_ERR_ALIGNMENT;
+  if (tile_n != 128 && tile_n != 256) return ABFT_ERR_UNSUPPORTED;
+  if (N > (1ll << 30) || K > (1ll << 30)) return ABFT_ERR_UNSUPPORTED;
+  int dev;
+  DeviceInfo info;
+  int rc = current_device(&dev, &info);
+  if (rc != ABFT_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int bd = tile_n - kChkRows;
+  const int num_kb = static_cast<int>(cdiv(K, kBK));
+  dim3 g(static_cast<unsigned>(num_kb), static_cast<unsigned>(cdiv(N, bd)));
+  encode_weight_kernel<<<g, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(B), ldb, static_cast<int>(N),
+                                         static_cast<int>(K), bd, static_cast<__nv_bfloat16*>(out));
+  return launch_status();
+}
+
+size_t abft_gemm_workspace_bytes(const abft_gemm_args* args) {
+  if (args == nullptr) return 0;
+  int dev;
+  DeviceInfo info;
+  int sms = 148;
+  if (current_device(&dev, &info) == ABFT_OK) sms = info.sms;
+  if (args->num_sms > 0 && args->num_sms < sms) sms = args->num_sms;
+  const int bn = args->tile_n ? args->tile_n : abft_pick_tile_n(args->M, args->N, sms);
+  GemmWs w;
+  gemm_ws_layout(args, bn, sms, &w);
+  return w.total;
+}
+
+int abft_gemm_bf16(const abft_gemm_args* a, void* stream) {
+  int rc = validate_gemm(a);
+  if (rc != ABFT_OK) return rc;
+  int dev;
+  DeviceInfo info;
+  rc = current_device(&dev, &info);
+  if (rc != ABFT_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (a->report != nullptr) {
+    if (cudaMemsetAsync(a->report, 0, sizeof(abft_report), s) != cudaSuccess) return launch_status(), ABFT_ERR_CUDA;
+  }
+  if (a->M == 0 || a->N == 0) return ABFT_OK;
+  if (a->K == 0) return ABFT_ERR_UNSUPPORTED;
+
+  int sms = info.sms;
+  if (a->num_sms > 0 && a->num_sms < sms) sms = a->num_sms;
+  const int bn = a->tile_n ? a->tile_n : abft_pick_tile_n(a->M, a->N, sms);
+  const bool check = (a->mode & (ABFT_MODE_DETECT | ABFT_MODE_CORRECT)) != 0;
+  GemmWs ws;
+  gemm_ws_layout(a, bn, sms, &ws);
+  if (ws.total > 0 && (a->workspace == nullptr || a->workspace_bytes < ws.total || !aligned16(a->workspace)))
+    return ABFT_ERR_WORKSPACE;
+  uint8_t* wsb = static_cast<uint8_t*>(a->workspace);
+
+  CUtensorMap tmA, tmB;
+  rc = make_tmap_kmajor(&tmA, a->A, a->K, a->M, a->lda, kBM);
+  if (rc != ABFT_OK) return rc;
+  const int bd = check ? bn - kChkRows : bn;  // data columns per output tile
+  rc = make_tmap_kmajor(&tmB, a->B, a->K, a->N, a->ldb, bd);
+  if (rc != ABFT_OK) return rc;
+
+  CUtensorMap tmV = tmA;  // placeholder when checks are off
+  if (check) {
+    const void* V = a->checksums;
+    if (V == nullptr) {
+      void* vws = wsb + ws.v_off;
+      rc = abft_encode_weight(a->B, a->N, a->K, a->ldb, bn, vws, stream);
+      if (rc != ABFT_OK) return rc;
+      V = vws;
+    }
+    rc = make_tmap_kmajor(&tmV, V, a->K, cdiv(a->N, bd) * kChkRows, a->K, kChkRows);
+    if (rc != ABFT_OK) return rc;
+  }
+
+  GemmParams p;
+  p.C = static_cast<__nv_bfloat16*>(a->C);
+  p.ldc = a->ldc;
+  p.bias = static_cast<const __nv_bfloat16*>(a->bias);
+  p.M = static_cast<int>(a->M);
+  p.N = static_cast<int>(a->N);
+  p.K = static_cast<int>(a->K);
+  p.num_kb = static_cast<int>(cdiv(a->K, kBK));
+  p.tiles_m = static_cast<int>(cdiv(a->M, kBM));
+  p.tiles_n = static_cast<int>(cdiv(a->N, bd));
+  p.num_tiles = p.tiles_m * p.tiles_n;
+  p.group_m = 8;
+  p.mode = a->mode;
+  if (p.mode & ABFT_MODE_CORRECT) p.mode |= ABFT_MODE_DETECT;
+  p.thr_k = static_cast<float>(static_cast<double>(a->thr_scale) * sqrt(static_cast<double>(a->K)));
+  p.thr_abs = a->thr_abs;
+  p.inj_rows = a->inject_rows;
+  p.inj_cols = a->inject_cols;
+  p.inj_deltas = a->inject_deltas;
+  p.n_inj = a->n_inject;
+  p.report = static_cast<abft_report*>(a->report);
+  p.capacity = a->report_capacity;
+  p.tile_sumc = (a->mode & ABFT_MODE_REF) ? reinterpret_cast<float*>(wsb + ws.parts_off) : nullptr;
+
+  const int grid = p.num_tiles < sms ? p.num_tiles : sms;
+  if (bn == 256)
+    rc = check ? launch_gemm<256, true>(dev, 0, tmA, tmB, tmV, p, grid, s)
+               : launch_gemm<256, false>(dev, 1, tmA, tmB, tmV, p, grid, s);
+  else
+    rc = check ? launch_gemm<128, true>(dev, 2, tmA, tmB, tmV, p, grid, s)
+               : launch_gemm<128, false>(dev, 3, tmA, tmB, tmV, p, grid, s);
+  if (rc != ABFT_OK) return rc;
+
+  if (a->mode & ABFT_MODE_REF) {
+    float* pa = reinterpret_cast<float*>(wsb + ws.pa_off);
+    float* u = reinterpret_cast<float*>(wsb + ws.u_off);
+    float* pb = reinterpret_cast<float*>(wsb + ws.pb_off);
+    float* vf = reinterpret_cast<float*>(wsb + ws.vf_off);
+    rc = colsum(a->A, a->lda, a->M, a->K, nullptr, pa, u, nullptr, nullptr, sms, s);
+    if (rc != ABFT_OK) return rc;
+    rc = colsum(a->B, a->ldb, a->N, a->K, nullptr, pb, vf, nullptr, nullptr, sms, s);
+    if (rc != ABFT_OK) return rc;
+    ref_finalize_kernel<<<1, 1024, 0, s>>>(u, vf, p.K, p.bias, p.N, p.M, p.tile_sumc, p.num_tiles * 8, a->tol_abs,
+                                           a->tol_rel, p.report, p.capacity, kBM, bn);
+    rc = launch_status();
+  }
+  return rc;
+}
+
+namespace {
+struct CheckWs {
+  float *pa, *u, *pb, *v, *rsum, *rmax, *rabs, *rexp, *pc, *csum, *cmax, *cabs, *cexp;
+  size_t floats;
+};
+// Carves the check-only workspace; with base == nullptr only counts floats.
+void check_ws_layout(float* base, int64_t M, int64_t N, int64_t K, int sms, CheckWs* w) {
+  size_t off = 0;
+  auto take = [&](size_t n) {
+    float* p = base != nullptr ? base + off : nullptr;
+    off += (n + 63) & ~size_t(63);
+    return p;
+  };
+  const size_t pb_n = colsum_partial_floats(N, K, sms, false), pk_n = colsum_partial_floats(K, N, sms, false);
+  const size_t pc_n = colsum_partial_floats(M, N, sms, true);
+  w->pa = take(colsum_partial_floats(M, K, sms, false));
+  w->u = take(K);
+  w->pb = take(pb_n > pk_n ? pb_n : pk_n);
+  w->v = take(K);
+  w->rsum = take(M);
+  w->rmax = take(M);
+  w->rabs = take(M);
+  w->rexp = take(M);
+  w->pc = take(pc_n > pk_n ? pc_n : pk_n);
+  w->csum = take(N);
+  w->cmax = take(N);
+  w->cabs = take(N);
+  w->cexp = take(N);
+  w->floats = off;
+}
+}  // namespace
+
+size_t abft_check_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  int dev;
+  DeviceInfo info;
+  int sms = 148;
+  if (current_device(&dev, &info) == ABFT_OK) sms = info.sms;
+  CheckWs w;
+  check_ws_layout(nullptr, M, N, K, sms, &w);
+  return align256(w.floats * 4);
+}
+
+int abft_check_only(const void* A, int64_t lda, const void* B, int64_t ldb, int32_t b_kn, const void* C, int64_t ldc,
+                    const void* bias, int64_t M, int64_t N, int64_t K, float tol_abs, float tol_rel, int32_t locate,
+                    float thr_scale, void* workspace, size_t workspace_bytes, void* report, int32_t report_capacity,
+                    void* stream) {
+  if (A == nullptr || B == nullptr || C == nullptr || report == nullptr) return ABFT_ERR_INVALID_ARG;
+  if (M <= 0 || N <= 0 || K <= 0 || report_capacity < 0 || (b_kn != 0 && b_kn != 1)) return ABFT_ERR_INVALID_ARG;
+  if (M > (1ll << 30) || N > (1ll << 30) || K > (1ll << 30)) return ABFT_ERR_UNSUPPORTED;
+  if (lda < K || ldc < N || ldb < (b_kn ? N : K)) return ABFT_ERR_INVALID_ARG;
+  if ((K % 8) || (N % 8) || (lda % 8) || (ldb % 8) || (ldc % 8)) return ABFT_ERR_ALIGNMENT;
+  if (!aligned16(A) || !aligned16(B) || !aligned16(C) || !aligned16(report)) return ABFT_ERR_ALIGNMENT;
+  if (bias != nullptr && !aligned16(bias)) return ABFT_ERR_ALIGNMENT;
+  if (!(thr_scale >= 0.f)) return ABFT_ERR_INVALID_ARG;
+  int dev;
+  DeviceInfo info;
+  int rc = current_device(&dev, &info);
+  if (rc != ABFT_OK) return rc;
+  const size_t need = abft_check_workspace_bytes(M, N, K);
+  if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace)) return ABFT_ERR_WORKSPACE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int sms = info.sms;
+  CheckWs w;
+  check_ws_layout(static_cast<float*>(workspace), M, N, K, sms, &w);
+
+  if (cudaMemsetAsync(report, 0, sizeof(abft_report), s) != cudaSuccess) return launch_status(), ABFT_ERR_CUDA;
+  abft_report* rep = static_cast<abft_report*>(report);
+
+  // s_a = A.sum(0) and s_b = B.sum(1)   (pytorch/abft/checkers.py:117-118)
+  rc = colsum(A, lda, M, K, nullptr, w.pa, w.u, nullptr, nullptr, sms, s);
+  if (rc != ABFT_OK) return rc;
+  if (b_kn == 0)
+    rc = colsum(B, ldb, N, K, nullptr, w.pb, w.v, nullptr, nullptr, sms, s);
+  else
+    rc = rowdot(B, ldb, K, N, nullptr, w.v, nullptr, nullptr, s);
+  if (rc != ABFT_OK) return rc;
+  // row sums of C (sum_c = sum of the row sums, fixed order)
+  rc = rowdot(C, ldc, M, N, nullptr, w.rsum, w.rmax, w.rabs, s);
+  if (rc != ABFT_OK) return rc;
+  ref_finalize_kernel<<<1, 1024, 0, s>>>(w.u, w.v, static_cast<int>(K), static_cast<const __nv_bfloat16*>(bias),
+                                         static_cast<int>(N), static_cast<int>(M), w.rsum, static_cast<int>(M), tol_abs,
+                                         tol_rel, rep, report_capacity, 0, 0);
+  rc = launch_status();
+  if (rc != ABFT_OK || !locate) return rc;
+
+  // Expected row sums A (B e), expected column sums (e^T A) B, actual column sums.
+  rc = rowdot(A, lda, M, K, w.v, w.rexp, nullptr, nullptr, s);
+  if (rc != ABFT_OK) return rc;
+  if (b_kn == 0)
+    rc = rowdot(B, ldb, N, K, w.u, w.cexp, nullptr, nullptr, s);
+  else
+    rc = colsum(B, ldb, K, N, w.u, w.pb, w.cexp, nullptr, nullptr, sms, s);
+  if (rc != ABFT_OK) return rc;
+  rc = colsum(C, ldc, M, N, nullptr, w.pc, w.csum, w.cmax, w.cabs, sms, s);
+  if (rc != ABFT_OK) return rc;
+  const float thr_k = static_cast<float>(static_cast<double>(thr_scale) * sqrt(static_cast<double>(K)));
+  constexpr float kBf16Unit = 1.0f / 512.0f;  // worst-case relative rounding of a stored bf16 element
+  locate_finalize_kernel<<<1, 1024, 0, s>>>(w.rsum, w.rmax, w.rabs, w.rexp, static_cast<int>(M), w.csum, w.cmax,
+                                            w.cabs, w.cexp, static_cast<int>(N),
+                                            static_cast<const __nv_bfloat16*>(bias), thr_k, kBf16Unit, rep,
+                                            report_capacity);
+  return launch_status();
+}
+
+}  // extern "C"

@@ -1,0 +1,407 @@
+// aux_kernels.cuh - HBM-bound helper kernels of the checksum library.
+//
+//   encode_weight_kernel   per-tile plain and column-index-weighted row
+//                          checksums of B[N, K] (the "Be" of checkers.py:119),
+//                          split into bf16 terms for the check MMA
+//   colsum_partial_kernel  column sums of a row-major [R, C] bf16 matrix over
+//                          blocks of rows (optionally row-weighted, with |x| max)
+//   reduce_partials_kernel sum (and max) of those partials in fixed order
+//   rowdot_kernel          per-row sum or dot with a vector (warp per row)
+//   ref_finalize_kernel    corner = dot(u, v) + M*sum(bias), sum_c, ok flag
+//                          (pytorch/abft/checkers.py:96-126)
+//   locate_finalize_kernel global row/column mismatch search and pairing
+//
+// Every reduction runs in a fixed order, so results are bit-reproducible run
+// to run (the reference's fp32 atomics, abft_fused.cu:45-46 and :71-88, are not).
+#pragma once
+
+#include <cuda_bf16.h>
+
+#include "../../include/abft_b200.h"
+
+namespace abft {
+
+__device__ __forceinline__ void unpack8(const uint4 w, float (&x)[8]) {
+  x[0] = __uint_as_float(w.x << 16);
+  x[1] = __uint_as_float(w.x & 0xFFFF0000u);
+  x[2] = __uint_as_float(w.y << 16);
+  x[3] = __uint_as_float(w.y & 0xFFFF0000u);
+  x[4] = __uint_as_float(w.z << 16);
+  x[5] = __uint_as_float(w.z & 0xFFFF0000u);
+  x[6] = __uint_as_float(w.w << 16);
+  x[7] = __uint_as_float(w.w & 0xFFFF0000u);
+}
+
+// Split v into three bf16 terms whose sum carries 24 significant bits:
+// hi = rn(v), mid = rn(v - hi), lo = rn(v - hi - mid); both differences are
+// exact in fp32.
+__device__ __forceinline__ void split3_bf16(float v, __nv_bfloat16& hi, __nv_bfloat16& mid, __nv_bfloat16& lo) {
+  hi = __float2bfloat16_rn(v);
+  const float r1 = v - __bfloat162float(hi);
+  mid = __float2bfloat16_rn(r1);
+  const float r2 = r1 - __bfloat162float(mid);
+  lo = __float2bfloat16_rn(r2);
+}
+
+// Per-tile checksum block of B[N, K]: the 8 rows the fused GEMM appends to
+// each B-operand tile of bd data rows.
+// out is bf16 [tiles_n * 8, K] row-major; rows of tile t:
+//   8t+0..2 = split3(v1), 8t+3..5 = split3(v2), 8t+6..7 = 0, with
+//   v1[k] = sum_j B[t*bd + j, k],  v2[k] = sum_j (j+1) B[t*bd + j, k]
+// (j over the tile's valid rows; fp32 sums in a fixed order).
+// grid (ceil(K/64), tiles_n), 256 threads. K % 8 == 0.
+__global__ void __launch_bounds__(256) encode_weight_kernel(const __nv_bfloat16* __restrict__ B, int64_t ldb, int N,
+                                                            int K, int bd, __nv_bfloat16* __restrict__ out) {
+  __shared__ float red[2][32][65];
+  const int kb = blockIdx.x, nt = blockIdx.y;
+  const int t = threadIdx.x, c8 = t & 7, rg = t >> 3;
+  const int k0 = kb * 64 + c8 * 8;
+  float s1[8], s2[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) s1[e] = s2[e] = 0.f;
+  if (k0 < K) {
+    for (int j = rg; j < bd; j += 32) {
+      const int gj = nt * bd + j;
+      if (gj >= N) break;
+      const uint4 w = __ldg(reinterpret_cast<const uint4*>(B + static_cast<int64_t>(gj) * ldb + k0));
+      float x[8];
+      unpack8(w, x);
+      const float wt = static_cast<float>(j + 1);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        s1[e] += x[e];
+        s2[e] = fmaf(wt, x[e], s2[e]);
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    red[0][rg][c8 * 8 + e] = s1[e];
+    red[1][rg][c8 * 8 + e] = s2[e];
+  }
+  __syncthreads();
+  if (t < 64) {
+    const int col = kb * 64 + t;
+    if (col < K) {
+      float a1 = 0.f, a2 = 0.f;
+      for (int g = 0; g < 32; ++g) {
+        a1 += red[0][g][t];
+        a2 += red[1][g][t];
+      }
+      __nv_bfloat16 h[8];
+      split3_bf16(a1, h[0], h[1], h[2]);
+      split3_bf16(a2, h[3], h[4], h[5]);
+      h[6] = h[7] = __float2bfloat16_rn(0.f);
+      __nv_bfloat16* o = out + static_cast<int64_t>(nt) * 8 * K + col;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) o[static_cast<int64_t>(q) * K] = h[q];
+    }
+  }
+}
+
+// grid (ceil(Cc/64), nrb), 256 threads. Cc % 8 == 0.
+// out_sum[rb*Cc + c] = sum_{r in block rb} w[r] * X[r, c]   (w == nullptr: 1)
+// with stats (out_stat != nullptr): out_stat[rb*Cc + c] = max |X[r, c]| and
+// out_stat[(nrb + rb)*Cc + c] = sum |X[r, c]|.
+__global__ void __launch_bounds__(256) colsum_partial_kernel(const __nv_bfloat16* __restrict__ X, int64_t ld, int R,
+                                                             int Cc, int rows_per_block, const float* __restrict__ w,
+                                                             float* __restrict__ out_sum, float* __restrict__ out_stat) {
+  __shared__ float red[3][32][65];
+  const int cb = blockIdx.x, rb = blockIdx.y, nrb = gridDim.y;
+  const int t = threadIdx.x, c8 = t & 7, rg = t >> 3;
+  const int col0 = cb * 64 + c8 * 8;
+  const int r0 = rb * rows_per_block;
+  const int r1 = min(R, r0 + rows_per_block);
+  float s[8], m[8], a[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) s[e] = m[e] = a[e] = 0.f;
+  if (col0 < Cc) {
+    for (int r = r0 + rg; r < r1; r += 32) {
+      const uint4 q = __ldg(reinterpret_cast<const uint4*>(X + static_cast<int64_t>(r) * ld + col0));
+      float x[8];
+      unpack8(q, x);
+      const float wr = (w != nullptr) ? __ldg(w + r) : 1.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        s[e] = fmaf(wr, x[e], s[e]);
+        m[e] = fmaxf(m[e], fabsf(x[e]));
+        a[e] += fabsf(x[e]);
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    red[0][rg][c8 * 8 + e] = s[e];
+    red[1][rg][c8 * 8 + e] = m[e];
+    red[2][rg][c8 * 8 + e] = a[e];
+  }
+  __syncthreads();
+  if (t < 64) {
+    const int col = cb * 64 + t;
+    if (col < Cc) {
+      float acc = 0.f, mx = 0.f, ab = 0.f;
+      for (int g = 0; g < 32; ++g) {
+        acc += red[0][g][t];
+        mx = fmaxf(mx, red[1][g][t]);
+        ab += red[2][g][t];
+      }
+      out_sum[static_cast<int64_t>(rb) * Cc + col] = acc;
+      if (out_stat != nullptr) {
+        out_stat[static_cast<int64_t>(rb) * Cc + col] = mx;
+        out_stat[static_cast<int64_t>(nrb + rb) * Cc + col] = ab;
+      }
+    }
+  }
+}
+
+// out[c] = sum_rb in[rb*n + c]; with stats also out_max[c] = max_rb and
+// out_abs[c] = sum_rb of the two stat planes that follow in[] (see above).
+__global__ void __launch_bounds__(256) reduce_partials_kernel(const float* __restrict__ in, const float* __restrict__ in_stat,
+                                                              int nrb, int n, float* __restrict__ out,
+                                                              float* __restrict__ out_max, float* __restrict__ out_abs) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= n) return;
+  float acc = 0.f, mx = 0.f, ab = 0.f;
+  for (int rb = 0; rb < nrb; ++rb) {
+    acc += in[static_cast<int64_t>(rb) * n + c];
+    if (in_stat != nullptr) {
+      mx = fmaxf(mx, in_stat[static_cast<int64_t>(rb) * n + c]);
+      ab += in_stat[static_cast<int64_t>(nrb + rb) * n + c];
+    }
+  }
+  out[c] = acc;
+  if (in_stat != nullptr) {
+    out_max[c] = mx;
+    out_abs[c] = ab;
+  }
+}
+
+// Warp per row: out[r] = sum_c X[r,c] * (vec ? vec[c] : 1); with stats
+// out_max[r] = max_c |X[r,c]| and out_abs[r] = sum_c |X[r,c]|.
+// 256 threads (8 rows) per block. Cc % 8 == 0, vec 16-byte aligned.
+__global__ void __launch_bounds__(256) rowdot_kernel(const __nv_bfloat16* __restrict__ X, int64_t ld, int R, int Cc,
+                                                     const float* __restrict__ vec, float* __restrict__ out,
+                                                     float* __restrict__ out_max, float* __restrict__ out_abs) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.x * 8 + warp;
+  if (r >= R) return;
+  const __nv_bfloat16* row = X + static_cast<int64_t>(r) * ld;
+  float acc = 0.f, mx = 0.f, ab = 0.f;
+  for (int c = lane * 8; c < Cc; c += 256) {
+    const uint4 q = __ldg(reinterpret_cast<const uint4*>(row + c));
+    float x[8];
+    unpack8(q, x);
+    if (vec != nullptr) {
+      const float4 va = __ldg(reinterpret_cast<const float4*>(vec + c));
+      const float4 vb = __ldg(reinterpret_cast<const float4*>(vec + c + 4));
+      acc = fmaf(x[0], va.x, acc);
+      acc = fmaf(x[1], va.y, acc);
+      acc = fmaf(x[2], va.z, acc);
+      acc = fmaf(x[3], va.w, acc);
+      acc = fmaf(x[4], vb.x, acc);
+      acc = fmaf(x[5], vb.y, acc);
+      acc = fmaf(x[6], vb.z, acc);
+      acc = fmaf(x[7], vb.w, acc);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc += x[e];
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      mx = fmaxf(mx, fabsf(x[e]));
+      ab += fabsf(x[e]);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
+    mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+    ab += __shfl_xor_sync(0xFFFFFFFFu, ab, o);
+  }
+  if (lane == 0) {
+    out[r] = acc;
+    if (out_max != nullptr) out_max[r] = mx;
+    if (out_abs != nullptr) out_abs[r] = ab;
+  }
+}
+
+// Fixed-order block sum over 1024 threads.
+__device__ __forceinline__ float block_sum_1024(float v, float* scratch /*32*/) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  __syncthreads();
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  float r = 0.f;
+  if (warp == 0) {
+    r = scratch[lane];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) r += __shfl_xor_sync(0xFFFFFFFFu, r, o);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) scratch[0] = r;
+  __syncthreads();
+  return scratch[0];
+}
+
+// One block of 1024 threads. Follows pytorch/abft/checkers.py:112-126
+// (corner = dot(s_a, s_b) + m * sum(bias), sum_c = sum(C)) and :96-110
+// (diff, rel = diff / max(|sum_c|, 1), ok = diff <= tol_abs or rel <= tol_rel).
+__global__ void __launch_bounds__(1024) ref_finalize_kernel(const float* __restrict__ u, const float* __restrict__ v,
+                                                            int K, const __nv_bfloat16* __restrict__ bias, int N,
+                                                            int M, const float* __restrict__ parts, int n_parts,
+                                                            float tol_abs, float tol_rel, abft_report* rep,
+                                                            int capacity, int tile_m, int tile_n) {
+  __shared__ float scratch[32];
+  float c = 0.f;
+  for (int k = threadIdx.x; k < K; k += 1024) c = fmaf(u[k], v[k], c);
+  float corner = block_sum_1024(c, scratch);
+  if (bias != nullptr) {
+    float b = 0.f;
+    for (int j = threadIdx.x; j < N; j += 1024) b += __bfloat162float(bias[j]);
+    const float bs = block_sum_1024(b, scratch);
+    corner += static_cast<float>(M) * bs;
+  }
+  float s = 0.f;
+  for (int i = threadIdx.x; i < n_parts; i += 1024) s += parts[i];
+  const float sum_c = block_sum_1024(s, scratch);
+  if (threadIdx.x == 0) {
+    const float diff = fabsf(corner - sum_c);
+    const float rel = diff / fmaxf(fabsf(sum_c), 1.f);
+    const bool ok = (diff <= tol_abs) || (rel <= tol_rel);
+    rep->corner = corner;
+    rep->sum_c = sum_c;
+    rep->abs_err = diff;
+    rep->rel_err = rel;
+    rep->ref_ok = ok ? 1 : 0;
+    rep->capacity = static_cast<uint32_t>(capacity);
+    rep->tile_m = static_cast<uint32_t>(tile_m);
+    rep->tile_n = static_cast<uint32_t>(tile_n);
+    if (!ok) atomicOr(&rep->status, ABFT_STATUS_REF_FAIL);
+  }
+}
+
+// One block of 1024 threads: global row and column mismatch search of a
+// post-hoc check, then pairing of mismatching rows with mismatching columns
+// of matching residual (a single fault at (i, j) shifts row sum i and column
+// sum j by the same delta). The stored C is rounded to its output dtype, so
+// each bound adds the worst-case rounding of the summed elements:
+//   row i:  thr = thr_k * max_j |C[i,j]| + unit_out * sum_j |C[i,j]|
+//   col j:  thr = thr_k * max_i |C[i,j]| + unit_out * sum_i |C[i,j]|
+// with thr_k = tau * sqrt(K) and unit_out = 2^-9 for bf16.
+constexpr int kLocateMax = 256;
+__global__ void __launch_bounds__(1024) locate_finalize_kernel(
+    const float* __restrict__ row_sum, const float* __restrict__ row_max, const float* __restrict__ row_abs,
+    const float* __restrict__ row_exp, int M, const float* __restrict__ col_sum, const float* __restrict__ col_max,
+    const float* __restrict__ col_abs, const float* __restrict__ col_exp, int N, const __nv_bfloat16* __restrict__ bias,
+    float thr_k, float unit_out, abft_report* rep, int capacity) {
+  __shared__ int rows[kLocateMax], cols[kLocateMax];
+  __shared__ float rres[kLocateMax], cres[kLocateMax], rthr[kLocateMax], cthr[kLocateMax];
+  __shared__ float scratch[32];
+  __shared__ int nr, nc, dropped;
+  // bias enters every row sum once and every column sum M times (checkers.py:120-124)
+  float bsum = 0.f;
+  if (bias != nullptr) {
+    float b = 0.f;
+    for (int j = threadIdx.x; j < N; j += 1024) b += __bfloat162float(bias[j]);
+    bsum = block_sum_1024(b, scratch);
+  }
+  if (threadIdx.x == 0) nr = nc = dropped = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < M; i += 1024) {
+    const float res = row_sum[i] - (row_exp[i] + bsum);
+    const float thr = fmaf(thr_k, row_max[i], unit_out * row_abs[i]);
+    if (fabsf(res) > thr) {
+      const int s = atomicAdd(&nr, 1);
+      if (s < kLocateMax) {
+        rows[s] = i;
+        rres[s] = res;
+        rthr[s] = thr;
+      } else {
+        atomicAdd(&dropped, 1);
+      }
+    }
+  }
+  for (int j = threadIdx.x; j < N; j += 1024) {
+    const float bj = bias != nullptr ? static_cast<float>(M) * __bfloat162float(bias[j]) : 0.f;
+    const float res = col_sum[j] - (col_exp[j] + bj);
+    const float thr = fmaf(thr_k, col_max[j], unit_out * col_abs[j]);
+    if (fabsf(res) > thr) {
+      const int s = atomicAdd(&nc, 1);
+      if (s < kLocateMax) {
+        cols[s] = j;
+        cres[s] = res;
+        cthr[s] = thr;
+      } else {
+        atomicAdd(&dropped, 1);
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  const int n_r = min(nr, kLocateMax), n_c = min(nc, kLocateMax);
+  // Deterministic order: insertion sort by index.
+  for (int a = 1; a < n_r; ++a)
+    for (int b = a; b > 0 && rows[b] < rows[b - 1]; --b) {
+      int ti = rows[b]; rows[b] = rows[b - 1]; rows[b - 1] = ti;
+      float tf = rres[b]; rres[b] = rres[b - 1]; rres[b - 1] = tf;
+      tf = rthr[b]; rthr[b] = rthr[b - 1]; rthr[b - 1] = tf;
+    }
+  for (int a = 1; a < n_c; ++a)
+    for (int b = a; b > 0 && cols[b] < cols[b - 1]; --b) {
+      int ti = cols[b]; cols[b] = cols[b - 1]; cols[b - 1] = ti;
+      float tf = cres[b]; cres[b] = cres[b - 1]; cres[b - 1] = tf;
+      tf = cthr[b]; cthr[b] = cthr[b - 1]; cthr[b - 1] = tf;
+    }
+  uint32_t used_c[kLocateMax / 32];
+  for (int w = 0; w < kLocateMax / 32; ++w) used_c[w] = 0u;
+  abft_fault_record* recs = reinterpret_cast<abft_fault_record*>(rep + 1);
+  uint32_t n_out = 0, n_loc = 0, status = 0;
+  auto emit = [&](int row, int col, float res, float resw, float thr, uint32_t flags) {
+    if (n_out < static_cast<uint32_t>(capacity)) {
+      recs[n_out].row = row;
+      recs[n_out].col = col;
+      recs[n_out].residual = res;
+      recs[n_out].residual_w = resw;
+      recs[n_out].threshold = thr;
+      recs[n_out].flags = flags;
+    } else {
+      status |= ABFT_STATUS_OVERFLOW;
+      rep->overflow += 1u;
+    }
+    ++n_out;
+  };
+  for (int a = 0; a < n_r; ++a) {
+    // the unique unused column whose residual matches within both thresholds
+    int match = -1, count = 0;
+    for (int b = 0; b < n_c; ++b) {
+      if (used_c[b >> 5] & (1u << (b & 31))) continue;
+      if (fabsf(rres[a] - cres[b]) <= rthr[a] + cthr[b]) {
+        if (count == 0) match = b;
+        ++count;
+      }
+    }
+    if (count == 1) {
+      used_c[match >> 5] |= 1u << (match & 31);
+      emit(rows[a], cols[match], rres[a], cres[match], rthr[a], ABFT_REC_DETECTED | ABFT_REC_LOCATED);
+      ++n_loc;
+    } else {
+      emit(rows[a], -1, rres[a], 0.f, rthr[a], ABFT_REC_DETECTED);
+      status |= ABFT_STATUS_UNLOCATED;
+    }
+  }
+  for (int b = 0; b < n_c; ++b) {
+    if (used_c[b >> 5] & (1u << (b & 31))) continue;
+    emit(-1, cols[b], cres[b], 0.f, cthr[b], ABFT_REC_DETECTED);
+    status |= ABFT_STATUS_UNLOCATED;
+  }
+  if (dropped > 0) status |= ABFT_STATUS_OVERFLOW | ABFT_STATUS_UNLOCATED;
+  if (n_out > 0 || dropped > 0) status |= ABFT_STATUS_FAULT;
+  rep->n_faults = n_out + static_cast<uint32_t>(dropped);
+  rep->n_located = n_loc;
+  rep->overflow += static_cast<uint32_t>(dropped);
+  rep->status |= status;
+}
+
+}  // namespace abft

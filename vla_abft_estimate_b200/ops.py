@@ -1,0 +1,258 @@
+"""Torch-facing wrappers of the C ABI.
+
+PyTorch supplies device memory, the current stream and the caching allocator
+for workspaces; every computation runs in libabft_b200.so. Inputs must be CUDA
+bf16 tensors on an sm_100 device; anything else raises (no CPU fallback).
+
+Functions
+  encode_weight(weight, tile_n)          per-tile checksums of a [N, K] weight
+  abft_gemm(a, weight, bias, ...)        fused checksum-protected GEMM
+  check_only(a, b, c, bias, ...)         post-hoc check of an existing output
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from typing import Optional, Sequence, Tuple
+
+import torch
+
+from . import _native as N
+from ._native import FaultReport
+
+DEFAULT_THR_SCALE = 1e-3
+DEFAULT_CAPACITY = 64
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _require_bf16_cuda(name: str, t: torch.Tensor, dim: int) -> None:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (the library has no CPU path)")
+    if t.dtype != torch.bfloat16:
+        raise ValueError(f"{name} must be bfloat16, got {t.dtype}")
+    if t.dim() != dim:
+        raise ValueError(f"{name} must be {dim}-D, got shape {tuple(t.shape)}")
+    if t.stride(-1) != 1:
+        raise ValueError(f"{name} must have unit stride in its last dimension")
+
+
+class ReportBuffer:
+    """Device buffer holding one ``abft_report`` with ``capacity`` records."""
+
+    def __init__(self, capacity: int = DEFAULT_CAPACITY, device: Optional[torch.device] = None):
+        self.capacity = int(capacity)
+        nbytes = int(N.lib().abft_report_bytes(self.capacity))
+        self.tensor = torch.zeros(nbytes, dtype=torch.uint8, device=device or torch.device("cuda"))
+
+    def data_ptr(self) -> int:
+        return self.tensor.data_ptr()
+
+    def read(self) -> FaultReport:
+        """Copy the report to the host (synchronises with the producing stream)."""
+        return FaultReport.from_bytes(self.tensor.cpu().numpy().tobytes())
+
+    def read_header_async(self, pinned: torch.Tensor) -> None:
+        """Start a device->host copy of the 64-byte header into ``pinned``."""
+        pinned.copy_(self.tensor[: N.REPORT_HEADER_BYTES], non_blocking=True)
+
+
+def pick_tile_n(m: int, n: int, device: Optional[torch.device] = None) -> int:
+    sms = torch.cuda.get_device_properties(device or torch.device("cuda")).multi_processor_count
+    return int(N.lib().abft_pick_tile_n(int(m), int(n), int(sms)))
+
+
+def encode_weight(weight: torch.Tensor, tile_n: int) -> torch.Tensor:
+    """Per-tile checksum block of ``weight`` [N, K] for tile width ``tile_n``.
+
+    Returns bf16 [ceil(N / tile_n) * 8, K]: for each tile, the plain and the
+    column-index-weighted row checksums, each as three bf16 terms, and two
+    zero rows (the operand of the fused kernel's check MMA).
+    """
+    _require_bf16_cuda("weight", weight, 2)
+    n, k = weight.shape
+    nbytes = int(N.lib().abft_checksum_bytes(n, k, int(tile_n)))
+    if nbytes == 0:
+        raise ValueError(f"tile_n must be 128 or 256, got {tile_n}")
+    out = torch.empty((nbytes // (2 * k), k), dtype=torch.bfloat16, device=weight.device)
+    with torch.cuda.device(weight.device):
+        rc = N.lib().abft_encode_weight(_ptr(weight), n, k, weight.stride(0), int(tile_n), _ptr(out),
+                                        _stream(weight.device))
+    N.check("abft_encode_weight", rc)
+    return out
+
+
+class _Inject:
+    """Device copy of a debug fault list [(row, col, delta), ...]."""
+
+    def __init__(self, faults: Sequence[Tuple[int, int, float]], device: torch.device):
+        if len(faults) > N.MAX_INJECT:
+            raise ValueError(f"at most {N.MAX_INJECT} injected faults per call")
+        rows = [int(f[0]) for f in faults]
+        cols = [int(f[1]) for f in faults]
+        deltas = [float(f[2]) for f in faults]
+        self.n = len(faults)
+        self.rows = torch.tensor(rows or [0], dtype=torch.int32, device=device)
+        self.cols = torch.tensor(cols or [0], dtype=torch.int32, device=device)
+        self.deltas = torch.tensor(deltas or [0.0], dtype=torch.float32, device=device)
+
+
+def abft_gemm(
+    a: torch.Tensor,
+    weight: torch.Tensor,
+    bias: Optional[torch.Tensor] = None,
+    *,
+    mode: int = N.MODE_DETECT | N.MODE_CORRECT,
+    tile_n: int = 0,
+    thr_scale: float = DEFAULT_THR_SCALE,
+    thr_abs: float = 0.0,
+    tol_abs: float = 1e-2,
+    tol_rel: float = 1e-2,
+    checksums: Optional[torch.Tensor] = None,
+    inject: Optional[Sequence[Tuple[int, int, float]]] = None,
+    report: Optional[ReportBuffer] = None,
+    out: Optional[torch.Tensor] = None,
+    num_sms: int = 0,
+) -> Tuple[torch.Tensor, Optional[ReportBuffer]]:
+    """``out = a @ weight.T (+ bias)`` with the fused checksum epilogue.
+
+    ``a`` is [M, K], ``weight`` [N, K] (nn.Linear layout), ``bias`` [N].
+    ``checksums`` is ``encode_weight(weight, tile_n)`` (cache it for a fixed
+    weight); when omitted and checks are on, the call encodes into its
+    workspace. ``inject`` adds debug faults to the fp32 accumulator.
+    Returns the output and the report buffer (None when mode == MODE_OFF).
+    """
+    _require_bf16_cuda("a", a, 2)
+    _require_bf16_cuda("weight", weight, 2)
+    m, k = a.shape
+    n, k2 = weight.shape
+    if k != k2:
+        raise ValueError(f"inner dimensions differ: a {tuple(a.shape)} vs weight {tuple(weight.shape)}")
+    if weight.device != a.device:
+        raise ValueError("a and weight must be on the same device")
+    if bias is not None:
+        _require_bf16_cuda("bias", bias, 1)
+        if bias.shape[0] != n:
+            raise ValueError(f"bias has {bias.shape[0]} entries, expected {n}")
+    dev = a.device
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+    else:
+        _require_bf16_cuda("out", out, 2)
+        if tuple(out.shape) != (m, n):
+            raise ValueError(f"out must be [{m}, {n}]")
+    if mode != N.MODE_OFF and report is None:
+        report = ReportBuffer(DEFAULT_CAPACITY, dev)
+    if checksums is not None:
+        if checksums.dtype != torch.bfloat16 or not checksums.is_cuda:
+            raise ValueError("checksums must be the CUDA bf16 tensor encode_weight() returns")
+        if tile_n == 0:
+            raise ValueError("pass the tile_n the checksums were encoded for")
+        need = int(N.lib().abft_checksum_bytes(n, k, int(tile_n)))
+        if checksums.numel() * 2 < need:
+            raise ValueError("checksums were encoded for a different weight shape or tile width")
+    inj = _Inject(inject, dev) if inject else None
+
+    args = N.GemmArgs()
+    args.A, args.B, args.C, args.bias = _ptr(a), _ptr(weight), _ptr(out), _ptr(bias)
+    args.M, args.N, args.K = m, n, k
+    args.lda, args.ldb, args.ldc = a.stride(0), weight.stride(0), out.stride(0)
+    args.mode = int(mode)
+    args.tile_n = int(tile_n)
+    args.thr_scale, args.thr_abs = float(thr_scale), float(thr_abs)
+    args.tol_abs, args.tol_rel = float(tol_abs), float(tol_rel)
+    args.checksums = _ptr(checksums)
+    args.report = report.data_ptr() if report is not None else None
+    args.report_capacity = report.capacity if report is not None else 0
+    args.num_sms = int(num_sms)
+    if inj is not None:
+        args.inject_rows, args.inject_cols, args.inject_deltas = _ptr(inj.rows), _ptr(inj.cols), _ptr(inj.deltas)
+        args.n_inject = inj.n
+    L = N.lib()
+    with torch.cuda.device(dev):
+        ws_bytes = int(L.abft_gemm_workspace_bytes(ctypes.byref(args)))
+        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev) if ws_bytes else None
+        args.workspace = _ptr(ws)
+        args.workspace_bytes = ws_bytes
+        rc = L.abft_gemm_bf16(ctypes.byref(args), _stream(dev))
+    N.check("abft_gemm_bf16", rc)
+    # keep device buffers alive until the stream has consumed them
+    if ws is not None:
+        ws.record_stream(torch.cuda.current_stream(dev))
+    return out, report
+
+
+def check_only(
+    a: torch.Tensor,
+    b: torch.Tensor,
+    c: torch.Tensor,
+    bias: Optional[torch.Tensor] = None,
+    *,
+    b_layout: str = "kn",
+    tol_abs: float = 1e-2,
+    tol_rel: float = 1e-2,
+    locate: bool = False,
+    thr_scale: float = DEFAULT_THR_SCALE,
+    report: Optional[ReportBuffer] = None,
+) -> ReportBuffer:
+    """Check an existing ``c`` against ``a`` and ``b``.
+
+    ``b_layout="kn"``: b is [K, N] (the reference checker's b_2d);
+    ``b_layout="nk"``: b is an nn.Linear weight [N, K] (no transpose copy).
+    Fills report.corner / sum_c / abs_err / rel_err / ref_ok, and with
+    ``locate`` the mismatching rows and columns.
+    """
+    _require_bf16_cuda("a", a, 2)
+    _require_bf16_cuda("c", c, 2)
+    if b.dim() != 2 or not b.is_cuda or b.dtype != torch.bfloat16:
+        raise ValueError("b must be a 2-D CUDA bfloat16 tensor")
+    m, k = a.shape
+    if b_layout == "kn":
+        kn = 1
+        if b.stride(1) != 1:
+            b = b.contiguous()
+        if b.shape[0] != k:
+            raise ValueError("b [K, N] does not match a")
+        n = b.shape[1]
+    elif b_layout == "nk":
+        kn = 0
+        if b.stride(1) != 1:
+            b = b.contiguous()
+        if b.shape[1] != k:
+            raise ValueError("b [N, K] does not match a")
+        n = b.shape[0]
+    else:
+        raise ValueError("b_layout must be 'kn' or 'nk'")
+    if tuple(c.shape) != (m, n):
+        raise ValueError(f"c must be [{m}, {n}]")
+    if bias is not None:
+        _require_bf16_cuda("bias", bias, 1)
+    dev = a.device
+    if report is None:
+        report = ReportBuffer(DEFAULT_CAPACITY, dev)
+    L = N.lib()
+    with torch.cuda.device(dev):
+        ws_bytes = int(L.abft_check_workspace_bytes(m, n, k))
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+        rc = L.abft_check_only(_ptr(a), a.stride(0), _ptr(b), b.stride(0), kn, _ptr(c), c.stride(0), _ptr(bias),
+                               m, n, k, float(tol_abs), float(tol_rel), 1 if locate else 0, float(thr_scale),
+                               _ptr(ws), ws_bytes, report.data_ptr(), report.capacity, _stream(dev))
+    N.check("abft_check_only", rc)
+    ws.record_stream(torch.cuda.current_stream(dev))
+    return report
+
+
+def flops(m: int, n: int, k: int) -> float:
+    return 2.0 * m * n * k
+
+
+def thr_k(thr_scale: float, k: int) -> float:
+    return float(thr_scale) * math.sqrt(k)
