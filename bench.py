@@ -1,0 +1,408 @@
+#!/usr/bin/env python3
+"""Throughput of the fused checksum-protected GEMM on B200.
+
+Workload (one step = one protected GEMM):
+  C[M, N_r] = A[M, K] B_r[N_r, K]^T, bf16 in, fp32 accumulate, bf16 out,
+  M = N_r = K = 8192 per GPU (--size), with per-tile weighted row checksums,
+  detect + locate + correct in the kernel. A is replicated; B[N, K] with
+  N = 8192 * n_gpus is split by columns across the ranks (weak scaling: at 8
+  GPUs this is the sharded A[8192 x 8192] . B[8192 x 65536] configuration).
+  Each step ends with one all-gather of the ranks' fault reports (NCCL).
+
+Printed: one JSON line (rank 0). value = whole-job TFLOP/s (2 M N K / step
+time, max over ranks); roofline from CUDA-event timing of the fused kernel
+alone; e2e through the public API with A and B_r copied from pinned host
+memory every step and the gathered fault reports read back.
+
+``--impl reference`` times the reference's CPU path (torch.matmul + the
+python-backend corner check, restated in oracle/ref_port.py) on a row sample
+of the same workload with all host threads.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+FALLBACK_BF16_TFLOPS = 1590.0
+NOMINAL_BF16_TFLOPS = 2250.0
+REF_SAMPLE_ROWS = 512
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--size", type=int, default=8192, help="M = K = per-GPU N")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            pk = json.load(f)
+        return float(pk["bf16_tflops"]), float(pk.get("bf16_tflops_sustained", pk["bf16_tflops"])), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_BF16_TFLOPS, 1400.0, "fallback"
+
+
+def load_traffic(workload: str):
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f).get(workload)
+    except (OSError, ValueError):
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons, sampled in the background."""
+
+    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuids, period_ms=25):
+        self.uuids = {u.lower() for u in uuids}
+        self.period_ms = period_ms
+        self.samples = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          f"-lms={self.period_ms}"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                                         text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            self.samples.append((time.time(), parts))
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+
+    def summary(self, t0, t1):
+        def pick(lo, hi):
+            out = []
+            for t, p in self.samples:
+                if lo <= t <= hi and (not self.uuids or p[0].lower().replace("gpu-", "") in self.uuids
+                                      or p[0].lower() in self.uuids):
+                    out.append(p)
+            return out
+
+        window = "timed"
+        rows = pick(t0, t1)
+        if len(rows) < 3:  # timed region shorter than the sampling period: widen to the whole run
+            rows, window = pick(-math.inf, math.inf), "run"
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "window": window}
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+
+        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
+        smax = [num(r[2]) for r in rows if num(r[2]) is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        loaded = sorted(sm)[len(sm) // 2:] if sm else []
+        return {"sm_mhz": statistics.median(loaded) if loaded else None,
+                "sm_max_mhz": max(smax) if smax else None, "reasons": reasons, "samples": len(rows),
+                "window": window, "power_w_max": max((num(r[3]) or 0.0) for r in rows)}
+
+
+def init_dist(n_gpus):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def cpu_reference(size, seconds):
+    """The reference CPU path on a REF_SAMPLE_ROWS x size x size sample."""
+    import torch
+
+    from oracle.ref_port import time_reference_sample
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    per, reps, tflops = time_reference_sample(REF_SAMPLE_ROWS, size, size, min_seconds=seconds, max_reps=1)
+    return {"value": tflops, "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"A[{REF_SAMPLE_ROWS}x{size}] @ B[{size}x{size}] bf16 torch.matmul + corner check "
+                      f"(oracle/ref_port.py), {reps} reps, {per * 1e3:.1f} ms each"}
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import torch
+
+    from oracle.ref_port import reference_protected_matmul
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    s = args.size
+    g = torch.Generator().manual_seed(0)
+    a = (torch.randn(REF_SAMPLE_ROWS, s, generator=g) * s ** -0.5).bfloat16()
+    b = (torch.randn(s, s, generator=g) * s ** -0.5).bfloat16()
+    for _ in range(args.warmup):
+        reference_protected_matmul(a, b)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        reference_protected_matmul(a, b)
+    dt = (time.perf_counter() - t0) / max(args.steps, 1)
+    value = 2.0 * REF_SAMPLE_ROWS * s * s / dt / 1e12
+    sample = (f"each step: A[{REF_SAMPLE_ROWS}x{s}] @ B[{s}x{s}] bf16 on CPU + python-backend corner check "
+              f"(oracle/ref_port.py); a {REF_SAMPLE_ROWS}-row sample of the {s}x{s * world}x{s} job")
+    line = {
+        "impl": "reference", "metric": "ABFT GEMM TFLOP/s", "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"square ABFT GEMM {s}x{s}x{s} per GPU, B split by columns",
+                   "M": s, "K": s, "N_per_gpu": s, "parallelism": f"dp{world} (column shards)"},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from vla_abft_estimate_b200 import _native as N
+    from vla_abft_estimate_b200 import ops
+    from vla_abft_estimate_b200.sharded import ShardedAbftGemm, gather_reports, shard_bounds
+
+    world, rank, local = init_dist(args.gpus)
+    dev = torch.device("cuda", local if world > 1 else 0)
+    torch.cuda.set_device(dev)
+    s = args.size
+    n_total = s * world
+    c0, c1 = shard_bounds(n_total, world, rank)
+    n_r = c1 - c0
+    flops_rank = 2.0 * s * n_r * s
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[dev.index])
+
+    # inputs: A replicated (same seed), B shard per rank; both exceed L2 (126 MB) together
+    ga = torch.Generator(device=dev).manual_seed(1234)
+    gb = torch.Generator(device=dev).manual_seed(5678 + rank)
+    a = (torch.randn(s, s, device=dev, generator=ga) * s ** -0.5).bfloat16()
+    w = (torch.randn(n_r, s, device=dev, generator=gb) * s ** -0.5).bfloat16()
+    out = torch.empty(s, n_r, device=dev, dtype=torch.bfloat16)
+    gemm = ShardedAbftGemm(w, c0, mode=N.MODE_DETECT | N.MODE_CORRECT)
+    off = ShardedAbftGemm(w, c0, mode=N.MODE_OFF)
+    tile_n, _ = gemm._checksums_for(s)
+
+    # fault-detection sanity outside the timed region: one seeded fault per rank
+    from vla_abft_estimate_b200.faults import seeded_fault_positions
+
+    ref_out = gemm(a, out=out)
+    delta = 256.0 * out.float().abs().max().item()
+    (fr, fc), = seeded_fault_positions(s, n_r, 1, 100 + rank)
+    gemm(a, out=torch.empty_like(out), inject=[(fr, fc, delta)])
+    grep = gemm.global_report()
+    expected = sorted((r_fr, r_fc + shard_bounds(n_total, world, r)[0])
+                      for r, (r_fr, r_fc) in ((r, seeded_fault_positions(s, shard_bounds(n_total, world, r)[1]
+                                                                              - shard_bounds(n_total, world, r)[0],
+                                                                              1, 100 + r)[0]) for r in range(world)))
+    detect_ok = grep.coords() == expected and grep.n_corrected == world
+    del ref_out
+
+    # encode cost of B_r's checksums (a fresh weight pays it once)
+    e_enc0, e_enc1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_enc0.record()
+    for _ in range(5):
+        ops.encode_weight(w, tile_n)
+    e_enc1.record()
+
+    sampler = None
+    if local == 0:
+        uuids = []
+        for i in range(torch.cuda.device_count()):
+            try:
+                uuids.append(str(torch.cuda.get_device_properties(i).uuid))
+            except Exception:  # noqa: BLE001
+                pass
+        sampler = ClockSampler(uuids)
+        sampler.start()
+        time.sleep(0.3)
+
+    for _ in range(max(args.warmup, 3)):
+        gemm(a, out=out)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    kends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    t_begin, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    wall0 = time.time()
+    t_begin.record()
+    for i in range(args.steps):
+        starts[i].record()
+        gemm(a, out=out, gather=False)
+        kends[i].record()
+        gather_reports(gemm.report.tensor, gemm.gathered, None)
+    t_end.record()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    wall1 = time.time()
+    step_ms = t_begin.elapsed_time(t_end) / args.steps
+    kernel_ms = sum(s_.elapsed_time(e_) for s_, e_ in zip(starts, kends)) / args.steps
+    clean = gemm.global_report()
+
+    # the same kernel with checksums compiled out
+    for _ in range(3):
+        off(a, out=out)
+    torch.cuda.synchronize()
+    o0, o1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    o0.record()
+    for _ in range(args.steps):
+        off(a, out=out, gather=False)
+    o1.record()
+    torch.cuda.synchronize()
+    off_ms = o0.elapsed_time(o1) / args.steps
+
+    # end to end through the public API with host buffers
+    a_h = a.cpu().pin_memory()
+    w_h = w.cpu().pin_memory()
+    a_d, w_d = torch.empty_like(a), torch.empty_like(w)
+    rep_h = torch.empty(gemm.gathered.shape, dtype=torch.uint8).pin_memory()
+    e2e_gemm = ShardedAbftGemm(w_d, c0, mode=N.MODE_DETECT | N.MODE_CORRECT)
+
+    def e2e_step():
+        a_d.copy_(a_h, non_blocking=True)
+        w_d.copy_(w_h, non_blocking=True)
+        # the weight copy changed w_d: its checksums are part of this step
+        e2e_gemm.checksums = None
+        e2e_gemm(a_d, out=out)
+        rep_h.copy_(e2e_gemm.gathered, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    x0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    x1.record()
+    torch.cuda.synchronize()
+    e2e_ms = x0.elapsed_time(x1) / args.steps
+    enc_ms = e_enc0.elapsed_time(e_enc1) / 5
+
+    if sampler is not None:
+        sampler.stop()
+
+    # max over ranks
+    vals = torch.tensor([step_ms, kernel_ms, off_ms, e2e_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+        ok_t = torch.tensor([1 if detect_ok else 0, 1 if clean.n_faults == 0 else 0], device=dev)
+        dist.all_reduce(ok_t, op=dist.ReduceOp.MIN)
+        detect_ok, clean_ok = bool(ok_t[0].item()), bool(ok_t[1].item())
+    else:
+        clean_ok = clean.n_faults == 0
+    step_ms, kernel_ms, off_ms, e2e_ms = [float(x) for x in vals.cpu()]
+
+    if rank == 0:
+        flops_job = 2.0 * s * n_total * s
+        peak, peak_sus, peak_src = load_peaks()
+        achieved = flops_rank / (kernel_ms * 1e-3) / 1e12
+        workload = f"abft_gemm_{s}"
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            cpu = cpu_reference(s, seconds=8.0)
+        line = {
+            "metric": "ABFT GEMM TFLOP/s",
+            "value": flops_job / (step_ms * 1e-3) / 1e12,
+            "unit": "TFLOP/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": max(args.warmup, 3),
+            "ms_per_step": step_ms,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded randn * K^-1/2)",
+            "config": {"workload": f"square ABFT GEMM {s}x{s}x{s} per GPU; B[{n_total}x{s}] split by columns",
+                       "M": s, "K": s, "N": n_total, "N_per_gpu": n_r, "tile": [128, tile_n],
+                       "mode": "detect+locate+correct, weight checksums cached", "parallelism": f"dp{world} (column shards)",
+                       "l2": "inputs exceed L2 (A+B_r = %d MB > 126 MB)" % ((s * s + n_r * s) * 2 // 2 ** 20)},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": load_traffic(workload),
+                         "peak_source": f"{peak_src} (burst cuBLAS bf16)",
+                         "frac_of_nominal_2250": achieved / NOMINAL_BF16_TFLOPS},
+            "cpu_baseline": cpu,
+            "e2e": {"value": flops_job / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": (s * s + n_r * s) * 2 * world,
+                    "d2h_bytes_per_step": int(gemm.gathered.numel()) * world,
+                    "note": "A and B_r from pinned host memory + checksum encode + fused GEMM + report gather + D2H"},
+            "gpu_launches": args.steps,
+            "clocks": sampler.summary(wall0, wall1) if sampler is not None else None,
+            "unchecked_tflops": flops_job / (off_ms * 1e-3) / 1e12,
+            "overhead_pct": 100.0 * (kernel_ms / off_ms - 1.0),
+            "encode_ms": enc_ms,
+            "fault_check": {"injected_located_corrected": detect_ok, "clean_no_false_positive": clean_ok},
+        }
+        print(json.dumps(line), flush=True)
+
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -56,6 +56,7 @@ enum abft_status {
 #define ABFT_MODE_DETECT   1u  /* per-tile weighted row checksums: detect + locate     */
 #define ABFT_MODE_CORRECT  2u  /* also correct located faults before the bf16 store    */
 #define ABFT_MODE_REF      4u  /* scalar corner-vs-sum(C) check of checkers.py:112-126 */
+#define ABFT_MODE_REF_BF16 8u  /* with MODE_REF: bf16-rounded sums (python backend)    */
 
 /* ---- status bits in abft_report.status ---------------------------------- */
 #define ABFT_STATUS_FAULT          1u  /* at least one checksum mismatch          */
@@ -173,19 +174,37 @@ int abft_gemm_bf16(const abft_gemm_args* args, void* stream);
  *   corner = dot(sum_i A[i,:], sum_j B[j,:]) + M * sum(bias)
  *   sum_c  = sum(C)
  *   ok     = |corner - sum_c| <= tol_abs  or  |corner - sum_c| / max(|sum_c|, 1) <= tol_rel
- * B is given as [N, K] (ldb) when b_kn == 0, or as [K, N] (ldb) when b_kn == 1.
- * Results land in report->corner/sum_c/abs_err/rel_err/ref_ok. When
- * `locate` is non-zero the call also compares every row and column sum of C
- * with A*(B e) and (e^T A)*B and records mismatching rows and columns
- * (row = index, col = -1 for a row record; row = -1, col = index for a column
- * record). Needs abft_check_workspace_bytes() of workspace. */
-size_t abft_check_workspace_bytes(int64_t M, int64_t N, int64_t K);
-int abft_check_only(const void* A, int64_t lda, const void* B, int64_t ldb,
-                    int32_t b_kn, const void* C, int64_t ldc, const void* bias,
-                    int64_t M, int64_t N, int64_t K, float tol_abs,
-                    float tol_rel, int32_t locate, float thr_scale,
-                    void* workspace, size_t workspace_bytes, void* report,
-                    int32_t report_capacity, void* stream);
+ * Results land in report->corner/sum_c/abs_err/rel_err/ref_ok.
+ * ABFT_CHECK_BF16_SUMS rounds every intermediate (both sum vectors, the dot,
+ * the bias term, sum_c, the errors and the tolerances) to bf16, as the
+ * reference's python backend does on bf16 tensors; otherwise all sums are
+ * fp32 (the reference's force_fp32_check intent, pytorch/abft/config.py:21).
+ * ABFT_CHECK_LOCATE also compares every row and column sum of C with
+ * A (B e) and (e^T A) B and records mismatches: a row and a column whose
+ * residuals agree are one located fault (row, col); an unpaired row is
+ * recorded as (row, -1) and an unpaired column as (-1, col). */
+#define ABFT_CHECK_LOCATE    1u
+#define ABFT_CHECK_BF16_SUMS 2u
+
+typedef struct abft_check_args {
+  const void* A;          /* bf16 [M, lda]                                    */
+  const void* B;          /* bf16 [N, ldb] (b_kn == 0) or [K, ldb] (b_kn == 1) */
+  const void* C;          /* bf16 [M, ldc]                                    */
+  const void* bias;       /* bf16 [N] or NULL                                 */
+  int64_t M, N, K;
+  int64_t lda, ldb, ldc;
+  int32_t b_kn;           /* layout of B, see above                           */
+  uint32_t flags;         /* ABFT_CHECK_* bits                                */
+  float tol_abs, tol_rel; /* scalar rule tolerances (checkers.py:96-110)      */
+  float thr_scale;        /* tau of the row/column bounds (ABFT_CHECK_LOCATE) */
+  int32_t report_capacity;
+  void* report;           /* abft_report + records                            */
+  void* workspace;        /* device scratch, abft_check_workspace_bytes()     */
+  size_t workspace_bytes;
+} abft_check_args;
+
+size_t abft_check_workspace_bytes(const abft_check_args* args);
+int abft_check_only(const abft_check_args* args, void* stream);
 
 #ifdef __cplusplus
 }  /* extern "C" */

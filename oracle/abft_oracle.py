@@ -90,19 +90,30 @@ def cheap_sum_check(
     a = np.asarray(a, dtype=np.float64)
     b = np.asarray(b_kn, dtype=np.float64)
     c = np.asarray(c, dtype=np.float64)
-    r = bf16_round if emulate_bf16 else (lambda x: np.asarray(x, dtype=np.float64))
+
+    def r(x):
+        x = np.asarray(x, dtype=np.float64)
+        return bf16_round(x).astype(np.float64) if emulate_bf16 else x
+
+    def f(x) -> float:
+        return float(np.asarray(x).reshape(-1)[0])
+
     s_a = r(a.sum(axis=0))
     s_b = r(b.sum(axis=1))
-    corner = r(np.dot(np.asarray(s_a, np.float64), np.asarray(s_b, np.float64)))
+    corner = f(r(np.dot(s_a, s_b)))
     if bias is not None:
         m = a.shape[0]
-        bsum = r(np.asarray(bias, np.float64).sum())
-        corner = r(np.float64(corner) + np.float64(r(np.float64(m) * np.float64(bsum))))
-    sum_c = r(c.sum())
-    diff = r(abs(np.float64(corner) - np.float64(sum_c)))
-    denom = max(abs(float(sum_c)), 1.0)
-    rel = r(np.float64(diff) / denom)
-    ok = bool(float(diff) <= tol_abs or float(rel) <= tol_rel)
+        bsum = f(r(np.asarray(bias, np.float64).sum()))
+        corner = f(r(corner + f(r(float(m) * bsum))))
+    sum_c = f(r(c.sum()))
+    diff = f(r(abs(corner - sum_c)))
+    denom = max(abs(sum_c), 1.0)
+    rel = f(r(diff / denom))
+    if emulate_bf16:
+        # torch compares a bf16 tensor with a Python float in bf16
+        tol_abs = f(bf16_round(np.float32(tol_abs)))
+        tol_rel = f(bf16_round(np.float32(tol_rel)))
+    ok = bool(diff <= tol_abs or rel <= tol_rel)
     return CheapSumResult(ok, float(diff), float(rel), float(corner), float(sum_c))
 
 

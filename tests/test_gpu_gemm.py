@@ -1,0 +1,242 @@
+"""Parity of the sm_100a kernels with the oracle, through the C ABI.
+
+Bars: bit-exact fault coordinates and flags (detect / locate / correct)
+against the oracle; outputs within 1e-2 of max|C| of an fp32 GEMM of the
+same bf16 inputs; no record at all on clean inputs.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import abft_oracle as O
+from vla_abft_estimate_b200 import _native as N
+from vla_abft_estimate_b200 import ops
+
+pytestmark = pytest.mark.gpu
+
+OUT_TOL = 1e-2  # |C - C_ref| <= OUT_TOL * max|C_ref|
+
+
+def seeded(m, n, k, seed, bias=False):
+    g = torch.Generator().manual_seed(seed)
+    a = (torch.randn(m, k, generator=g) * k ** -0.5).bfloat16()
+    w = (torch.randn(n, k, generator=g) * k ** -0.5).bfloat16()
+    b = (torch.randn(n, generator=g) * 0.02).bfloat16() if bias else None
+    return a, w, b
+
+
+def f32(t):
+    return t.float().cpu().numpy()
+
+
+def max_rel_err(got, ref):
+    return float(np.abs(got - ref).max() / max(np.abs(ref).max(), 1e-30))
+
+
+# ------------------------------------------------------------------ encode
+@pytest.mark.parametrize("tile_n", [128, 256])
+@pytest.mark.parametrize("n,k", [(300, 200), (1024, 512), (136, 72)])
+def test_encode_weight_matches_oracle(cuda_device, tile_n, n, k):
+    _, w, _ = seeded(8, n, k, 1)
+    blk = f32(ops.encode_weight(w.to(cuda_device), tile_n)).astype(np.float64)
+    v1, v2 = O.encode_weight(f32(w), tile_n - 8)
+    t = v1.shape[0]
+    blk = blk.reshape(t, 8, k)
+    tol = 1e-5 * max(1.0, np.abs(v2).max())
+    assert np.abs(blk[:, 0] + blk[:, 1] + blk[:, 2] - v1).max() <= 1e-5
+    assert np.abs(blk[:, 3] + blk[:, 4] + blk[:, 5] - v2).max() <= tol
+    assert np.all(blk[:, 6:] == 0)
+
+
+# ------------------------------------------------------------ plain GEMM
+@pytest.mark.parametrize("m,n,k,tile_n,bias", [
+    (128, 256, 64, 256, False), (128, 128, 64, 128, False), (256, 512, 256, 0, True),
+    (200, 136, 72, 256, True), (200, 136, 72, 128, True), (1, 8, 8, 0, False), (300, 1000, 520, 0, True),
+    (1024, 1024, 1024, 0, False), (512, 4096, 4096, 0, True),
+])
+def test_plain_gemm_matches_fp32(cuda_device, m, n, k, tile_n, bias):
+    a, w, b = seeded(m, n, k, 2, bias)
+    ref = f32(a) @ f32(w).T + (f32(b) if b is not None else 0)
+    c, rep = ops.abft_gemm(a.to(cuda_device), w.to(cuda_device), None if b is None else b.to(cuda_device),
+                           mode=N.MODE_OFF, tile_n=tile_n)
+    assert rep is None
+    assert max_rel_err(f32(c), ref) <= OUT_TOL
+
+
+# ---------------------------------------------------- checked GEMM parity
+def run_checked(device, m, n, k, faults, *, tile_n=0, bias=False, mode=N.MODE_DETECT | N.MODE_CORRECT, seed=3,
+                magnitude=None):
+    a, w, b = seeded(m, n, k, seed, bias)
+    acc = f32(a).astype(np.float64) @ f32(w).astype(np.float64).T
+    delta = 256.0 * np.abs(acc).max() if magnitude is None else magnitude
+    inj = [(r, c, float(delta)) for (r, c) in faults]
+    c, rep = ops.abft_gemm(a.to(device), w.to(device), None if b is None else b.to(device), mode=mode,
+                           tile_n=tile_n, inject=inj or None)
+    r = rep.read()
+    orc = O.rowcheck_gemm(f32(a), f32(w), None if b is None else f32(b), tile_n=r.tile_n, inject=inj,
+                          correct=bool(mode & N.MODE_CORRECT))
+    return a, w, b, c, r, orc
+
+
+@pytest.mark.parametrize("tile_n", [0, 128, 256])
+@pytest.mark.parametrize("m,n,k,bias", [(256, 512, 256, False), (200, 136, 72, True), (512, 4096, 512, True),
+                                        (384, 1000, 1024, False)])
+def test_clean_inputs_have_no_records(cuda_device, tile_n, m, n, k, bias):
+    a, w, b, c, r, orc = run_checked(cuda_device, m, n, k, [], tile_n=tile_n, bias=bias)
+    assert r.status == 0 and r.n_faults == 0 and r.records == [] and orc.records == []
+    ref = f32(a) @ f32(w).T + (f32(b) if b is not None else 0)
+    assert max_rel_err(f32(c), ref) <= OUT_TOL
+    assert r.tile_m == 128 and r.tile_n in (120, 248)
+
+
+@pytest.mark.parametrize("tile_n", [128, 256])
+@pytest.mark.parametrize("count", [1, 4])
+@pytest.mark.parametrize("m,n,k", [(256, 512, 256), (512, 4096, 1024), (1024, 1024, 1024), (300, 1000, 520)])
+def test_faults_located_and_corrected_bit_exact(cuda_device, tile_n, count, m, n, k):
+    faults = O.seeded_fault_positions(m, n, count, 11 * count + m)
+    a, w, b, c, r, orc = run_checked(cuda_device, m, n, k, faults, tile_n=tile_n)
+    got = sorted((x.row, x.col, x.flags) for x in r.records)
+    assert got == orc.records
+    assert sorted((i, j) for i, j, _ in got) == sorted(faults)
+    assert r.n_faults == r.n_located == r.n_corrected == count
+    assert r.status == N.STATUS_FAULT
+    assert max_rel_err(f32(c), orc.out) <= OUT_TOL
+    clean = f32(a) @ f32(w).T
+    assert max_rel_err(f32(c), clean) <= OUT_TOL
+
+
+def test_detect_only_keeps_the_fault(cuda_device):
+    m, n, k = 256, 512, 256
+    a, w, b, c, r, orc = run_checked(cuda_device, m, n, k, [(17, 300)], mode=N.MODE_DETECT, magnitude=5.0)
+    assert [(x.row, x.col, x.flags) for x in r.records] == [(17, 300, N.REC_DETECTED | N.REC_LOCATED)]
+    assert r.n_corrected == 0
+    clean = f32(a) @ f32(w).T
+    assert abs(f32(c)[17, 300] - (clean[17, 300] + 5.0)) < 0.05
+
+
+def test_two_faults_in_one_row_segment_are_not_miscorrected(cuda_device):
+    a, w, b, c, r, orc = run_checked(cuda_device, 128, 248, 128, [(5, 10), (5, 201)], tile_n=256, magnitude=3.0)
+    assert sorted((x.row, x.col, x.flags) for x in r.records) == orc.records == [(5, -1, N.REC_DETECTED)]
+    assert r.status == N.STATUS_FAULT | N.STATUS_UNLOCATED
+
+
+def test_ragged_edges_and_bias(cuda_device):
+    a, w, b, c, r, orc = run_checked(cuda_device, 200, 136, 72, [(199, 135)], bias=True, tile_n=256)
+    assert [(x.row, x.col) for x in r.records] == [(199, 135)]
+    assert max_rel_err(f32(c), orc.out) <= OUT_TOL
+
+
+def test_report_overflow(cuda_device):
+    m, n, k = 256, 512, 128
+    a, w, _ = seeded(m, n, k, 5)
+    faults = [(i, (7 * i) % n, 50.0) for i in range(10)]
+    c, rep = ops.abft_gemm(a.to(cuda_device), w.to(cuda_device), inject=faults,
+                           report=ops.ReportBuffer(4, cuda_device))
+    r = rep.read()
+    assert r.n_faults == 10 and len(r.records) == 4 and r.overflow == 6
+    assert r.status & N.STATUS_OVERFLOW
+
+
+def test_cached_checksums_equal_inline_encode(cuda_device):
+    m, n, k = 384, 1000, 512
+    a, w, _ = seeded(m, n, k, 6)
+    ad, wd = a.to(cuda_device), w.to(cuda_device)
+    faults = [(3, 777, 9.0), (200, 5, -9.0)]
+    c1, r1 = ops.abft_gemm(ad, wd, tile_n=256, inject=faults)
+    v = ops.encode_weight(wd, 256)
+    c2, r2 = ops.abft_gemm(ad, wd, tile_n=256, checksums=v, inject=faults)
+    assert torch.equal(c1, c2)
+    assert r1.read().coords() == r2.read().coords() == [(3, 777), (200, 5)]
+
+
+def test_deterministic_bits(cuda_device):
+    m, n, k = 1024, 2048, 1024
+    a, w, b = seeded(m, n, k, 7, True)
+    ad, wd, bd = a.to(cuda_device), w.to(cuda_device), b.to(cuda_device)
+    outs = [ops.abft_gemm(ad, wd, bd, mode=N.MODE_DETECT | N.MODE_CORRECT | N.MODE_REF)[0] for _ in range(2)]
+    assert torch.equal(outs[0], outs[1])
+
+
+# ------------------------------------------------------- scalar (ref) mode
+@pytest.mark.parametrize("fault", [None, 1.0])
+def test_ref_mode_matches_oracle(cuda_device, fault):
+    m, n, k = 256, 512, 256
+    a, w, b = seeded(m, n, k, 4, True)
+    inj = [(3, 4, fault)] if fault else None
+    c, rep = ops.abft_gemm(a.to(cuda_device), w.to(cuda_device), b.to(cuda_device), mode=N.MODE_REF, inject=inj)
+    r = rep.read()
+    o = O.cheap_sum_check(f32(a), f32(w).T, f32(c), f32(b))
+    assert (r.ref_ok == 1) == o.ok
+    assert abs(r.corner - o.abft_corner) <= 1e-4 * max(1.0, abs(o.abft_corner))
+    assert abs(r.sum_c - o.sum_c) <= 1e-4 * max(1.0, abs(o.sum_c))
+
+
+def test_check_only_reproduces_reference_python_backend(cuda_device, golden_dir):
+    """bf16-sum mode on the reference's own (A, B, C, bias): same flags as the
+    reference's CheapSumChecker, values within one bf16 rounding."""
+    import json
+    import os
+
+    meta = json.load(open(os.path.join(golden_dir, "ref_checker_cases.json")))
+    arrays = np.load(os.path.join(golden_dir, "ref_checker_cases.npz"))
+
+    def dev(name):
+        return torch.from_numpy(arrays[name].view(np.int16)).view(torch.bfloat16).to(cuda_device)
+
+    for case in meta:
+        n = case["name"]
+        a, w, c = dev(n + "_a"), dev(n + "_w"), dev(n + "_c")
+        b = dev(n + "_bias") if case["bias"] else None
+        for layout, bb in (("nk", w), ("kn", w.t().contiguous())):
+            r = ops.check_only(a, bb, c, b, b_layout=layout, bf16_sums=True).read()
+            assert (r.ref_ok == 1) == case["ok"], (n, layout)
+            for key, ref in (("corner", "abft_corner"), ("sum_c", "sum_c")):
+                got = getattr(r, key)
+                assert abs(got - case[ref]) <= 2 ** -7 * max(abs(case[ref]), 1e-3), (n, key, got, case[ref])
+
+
+def test_check_only_locates_post_hoc_fault(cuda_device):
+    m, n, k = 300, 264, 136
+    a, w, b = seeded(m, n, k, 6, True)
+    c = (a.float() @ w.float().T + b.float()).bfloat16()
+    c2 = c.clone()
+    c2[17, 33] += 5.0
+    for cc, want in ((c, []), (c2, [(17, 33)])):
+        for layout, bb in (("nk", w), ("kn", w.t().contiguous())):
+            r = ops.check_only(a.to(cuda_device), bb.to(cuda_device), cc.to(cuda_device), b.to(cuda_device),
+                               b_layout=layout, locate=True).read()
+            o = O.locate_post_hoc(f32(a), f32(w).T, f32(cc), f32(b))
+            assert r.coords() == o == want
+            ref = O.cheap_sum_check(f32(a), f32(w).T, f32(cc), f32(b))
+            assert (r.ref_ok == 1) == ref.ok
+
+
+# ------------------------------------------- full-size, size-independent checks
+@pytest.mark.parametrize("m,n,k", [(512, 4096, 4096), (4096, 4096, 4096), (512, 37888, 3584)])
+def test_full_size_seeded_faults(cuda_device, m, n, k):
+    """No false positives on clean data; every seeded fault (2^8 max|C|) is
+    found at its exact coordinate and the corrected output equals the clean
+    one up to bf16 rounding."""
+    torch.manual_seed(m + n + k)
+    a = (torch.randn(m, k, device=cuda_device) * k ** -0.5).bfloat16()
+    w = (torch.randn(n, k, device=cuda_device) * k ** -0.5).bfloat16()
+    clean, r0 = ops.abft_gemm(a, w)
+    r0 = r0.read()
+    assert r0.n_faults == 0 and r0.status == 0
+    delta = 256.0 * clean.float().abs().max().item()
+    for count in (1, 4):
+        faults = O.seeded_fault_positions(m, n, count, count)
+        c, r = ops.abft_gemm(a, w, inject=[(i, j, delta) for i, j in faults])
+        r = r.read()
+        assert r.coords() == sorted(faults)
+        assert r.n_corrected == count
+        diff = (c.float() - clean.float()).abs().max().item()
+        assert diff <= OUT_TOL * clean.float().abs().max().item()
+    ref = (a.float() @ w.float().T)
+    assert (clean.float() - ref).abs().max().item() <= OUT_TOL * ref.abs().max().item()
+
+
+def test_no_device_timeouts_reported(cuda_device):
+    a, w, _ = seeded(512, 1024, 512, 9)
+    _, rep = ops.abft_gemm(a.to(cuda_device), w.to(cuda_device), mode=N.MODE_DETECT | N.MODE_REF)
+    assert not rep.read().device_timeout

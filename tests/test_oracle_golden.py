@@ -1,0 +1,163 @@
+"""The CPU oracle against outputs of the reference itself (tests/golden/).
+
+The fixtures were written by tests/golden/make_golden.py, which ran the
+reference's CheapSumChecker (pytorch/abft/checkers.py:55-126) and
+AbftInjector (pytorch/abft/injector.py) on seeded CPU bf16 inputs.
+"""
+import json
+import os
+import random
+
+import numpy as np
+import pytest
+
+from oracle import abft_oracle as O
+
+
+@pytest.fixture(scope="module")
+def cases(golden_dir):
+    meta = json.load(open(os.path.join(golden_dir, "ref_checker_cases.json")))
+    arrays = np.load(os.path.join(golden_dir, "ref_checker_cases.npz"))
+    out = []
+    for c in meta:
+        n = c["name"]
+        a = O.bf16_bits_to_f32(arrays[n + "_a"])
+        w = O.bf16_bits_to_f32(arrays[n + "_w"])
+        cc = O.bf16_bits_to_f32(arrays[n + "_c"])
+        b = O.bf16_bits_to_f32(arrays[n + "_bias"]) if c["bias"] else None
+        out.append((c, a, w, cc, b))
+    return out
+
+
+def test_bf16_round_trip():
+    x = np.array([0.0, 1.0, -2.5, 3.140625, 1e-3, 65504.0, -1e30], dtype=np.float32)
+    bits = O.f32_to_bf16_bits(x)
+    back = O.bf16_bits_to_f32(bits)
+    assert np.all(O.f32_to_bf16_bits(back) == bits)
+    # round to nearest even on the dropped 16 bits
+    assert O.f32_to_bf16_bits(np.array([1.0 + 2 ** -8], np.float32))[0] == 0x3F80
+    assert O.f32_to_bf16_bits(np.array([1.0 + 3 * 2 ** -9], np.float32))[0] == 0x3F81
+    assert O.f32_to_bf16_bits(np.array([1.0 + 3 * 2 ** -8], np.float32))[0] == 0x3F82
+
+
+def test_cheap_sum_bf16_emulation_matches_reference(cases):
+    """Bit-exact flags and values of the reference python backend."""
+    for c, a, w, cc, b in cases:
+        r = O.cheap_sum_check(a, w.T, cc, b, emulate_bf16=True)
+        assert r.ok == c["ok"], c["name"]
+        assert r.abs_err == c["abs_err"], c["name"]
+        assert r.rel_err == c["rel_err"], c["name"]
+        assert r.abft_corner == c["abft_corner"], c["name"]
+        assert r.sum_c == c["sum_c"], c["name"]
+
+
+def test_cheap_sum_fp32_flags(cases):
+    """fp32/fp64 sums agree with the reference except where its bf16 rounding
+    alone trips the 1e-2 rule on a clean or sub-tolerance output."""
+    bf16_false_positive = {"mid_clean", "mid_fault_tiny"}
+    for c, a, w, cc, b in cases:
+        r = O.cheap_sum_check(a, w.T, cc, b, emulate_bf16=False)
+        if c["name"] in bf16_false_positive:
+            assert c["ok"] is False and r.ok is True, c["name"]
+        else:
+            assert r.ok == c["ok"], c["name"]
+            assert abs(r.abft_corner - c["abft_corner"]) <= 2 ** -7 * max(1.0, abs(c["abft_corner"])) * 2
+
+
+def test_fault_positions_follow_reference_rng(cases):
+    for c, a, w, cc, b in cases:
+        if c["fault_index"] is None:
+            continue
+        idx = random.Random(c["seed"]).randrange(c["M"] * c["N"])
+        assert idx == c["fault_index"]
+        assert (idx // c["N"], idx % c["N"]) == (c["fault_row"], c["fault_col"])
+
+
+def test_injector_rng_replays_reference_sequences(golden_dir):
+    seqs = json.load(open(os.path.join(golden_dir, "ref_injector_sequences.json")))["configs"]
+    for conf in seqs:
+        rng = O.InjectorRng(conf["seed"])
+        for call in conf["calls"]:
+            m, k, n = call["shape"]
+            idx = rng.maybe_inject(m * n, True, conf["inject_probability"])
+            checked = rng.sample(conf["sample_rate"])
+            assert (idx is not None) == call["injected"], conf
+            if idx is not None:
+                assert idx == call["index"]
+            assert int(checked) == call["checked"]
+
+
+def test_seeded_fault_positions_distinct():
+    pos = O.seeded_fault_positions(512, 4096, 4, 1)
+    assert len({r for r, _ in pos}) == 4 and len({c for _, c in pos}) == 4
+    assert pos == O.seeded_fault_positions(512, 4096, 4, 1)
+
+
+# ------------------------------------------------------------ row-check oracle
+def _inputs(m, n, k, seed, bias=False):
+    rng = np.random.default_rng(seed)
+    a = O.bf16_round(rng.standard_normal((m, k)).astype(np.float32) / np.sqrt(k))
+    w = O.bf16_round(rng.standard_normal((n, k)).astype(np.float32) / np.sqrt(k))
+    b = O.bf16_round(0.02 * rng.standard_normal(n).astype(np.float32)) if bias else None
+    return a, w, b
+
+
+@pytest.mark.parametrize("tile_n", [248, 120])
+def test_rowcheck_clean_has_no_records(tile_n):
+    a, w, b = _inputs(200, 520, 136, 0, bias=True)
+    r = O.rowcheck_gemm(a, w, b, tile_n=tile_n)
+    assert r.records == []
+    ref = O.bf16_round((a.astype(np.float64) @ w.T.astype(np.float64) + b).astype(np.float32))
+    assert np.abs(r.out - ref).max() <= 2 ** -7 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("tile_n", [248, 120])
+def test_rowcheck_locates_and_corrects_distinct_faults(tile_n):
+    m, n, k = 256, 512, 256
+    a, w, _ = _inputs(m, n, k, 1)
+    clean = a.astype(np.float64) @ w.T.astype(np.float64)
+    delta = 256.0 * np.abs(clean).max()
+    for count in (1, 4):
+        pos = O.seeded_fault_positions(m, n, count, 7 + count)
+        r = O.rowcheck_gemm(a, w, tile_n=tile_n, inject=[(i, j, delta) for i, j in pos])
+        assert [(i, j) for i, j, _ in r.records] == sorted(pos)
+        assert all(f == O.REC_DETECTED | O.REC_LOCATED | O.REC_CORRECTED for _, _, f in r.records)
+        assert np.abs(r.out - O.bf16_round(clean.astype(np.float32))).max() <= 2 ** -7 * np.abs(clean).max()
+
+
+def test_rowcheck_detect_only_keeps_fault():
+    a, w, _ = _inputs(128, 248, 64, 2)
+    clean = a.astype(np.float64) @ w.T.astype(np.float64)
+    r = O.rowcheck_gemm(a, w, tile_n=248, inject=[(3, 40, 5.0)], correct=False)
+    assert r.records == [(3, 40, O.REC_DETECTED | O.REC_LOCATED)]
+    assert abs(r.out[3, 40] - (clean[3, 40] + 5.0)) < 0.05
+
+
+def test_rowcheck_two_faults_in_one_row_are_unlocated():
+    a, w, _ = _inputs(128, 248, 64, 3)
+    r = O.rowcheck_gemm(a, w, tile_n=248, inject=[(5, 10, 3.0), (5, 201, 3.0)])
+    assert r.records == [(5, -1, O.REC_DETECTED)]
+
+
+def test_rowcheck_ragged_last_tile():
+    m, n, k = 200, 136, 72
+    a, w, b = _inputs(m, n, k, 4, bias=True)
+    r = O.rowcheck_gemm(a, w, b, tile_n=120, inject=[(199, 135, 10.0)])
+    assert [(i, j) for i, j, _ in r.records] == [(199, 135)]
+
+
+def test_split3_reconstructs_24_bits():
+    rng = np.random.default_rng(0)
+    v = (rng.standard_normal(1000) * 100).astype(np.float32)
+    s = O.split3_bf16(v).astype(np.float64).sum(axis=0)
+    assert np.all(np.abs(s - v) <= np.abs(v) * 2.0 ** -23)
+
+
+def test_locate_post_hoc_single_fault():
+    m, n, k = 96, 64, 80
+    a, w, b = _inputs(m, n, k, 5, bias=True)
+    c = O.bf16_round((a.astype(np.float64) @ w.T + b).astype(np.float32))
+    assert O.locate_post_hoc(a, w.T, c, b) == []
+    c2 = c.copy()
+    c2[17, 33] += 5.0
+    assert O.locate_post_hoc(a, w.T, c2, b) == [(17, 33)]

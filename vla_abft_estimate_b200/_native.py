@@ -19,6 +19,10 @@ MODE_OFF = 0
 MODE_DETECT = 1
 MODE_CORRECT = 2
 MODE_REF = 4
+MODE_REF_BF16 = 8
+
+CHECK_LOCATE = 1
+CHECK_BF16_SUMS = 2
 
 STATUS_FAULT = 1
 STATUS_UNLOCATED = 2
@@ -90,6 +94,32 @@ class GemmArgs(ctypes.Structure):
     ]
 
 
+class CheckArgs(ctypes.Structure):
+    """Mirror of ``abft_check_args``."""
+
+    _fields_ = [
+        ("A", ctypes.c_void_p),
+        ("B", ctypes.c_void_p),
+        ("C", ctypes.c_void_p),
+        ("bias", ctypes.c_void_p),
+        ("M", ctypes.c_int64),
+        ("N", ctypes.c_int64),
+        ("K", ctypes.c_int64),
+        ("lda", ctypes.c_int64),
+        ("ldb", ctypes.c_int64),
+        ("ldc", ctypes.c_int64),
+        ("b_kn", ctypes.c_int32),
+        ("flags", ctypes.c_uint32),
+        ("tol_abs", ctypes.c_float),
+        ("tol_rel", ctypes.c_float),
+        ("thr_scale", ctypes.c_float),
+        ("report_capacity", ctypes.c_int32),
+        ("report", ctypes.c_void_p),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
 _LIB: Optional[ctypes.CDLL] = None
 
 
@@ -105,7 +135,7 @@ def lib() -> ctypes.CDLL:
             "(or __graft_entry__.build()); there is no fallback path"
         )
     L = ctypes.CDLL(str(path))
-    vp, i32, i64, f32, sz = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
+    vp, i32, i64, sz = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_size_t
     L.abft_version.restype = ctypes.c_int
     L.abft_version.argtypes = []
     L.abft_status_string.restype = ctypes.c_char_p
@@ -123,10 +153,9 @@ def lib() -> ctypes.CDLL:
     L.abft_gemm_bf16.restype = ctypes.c_int
     L.abft_gemm_bf16.argtypes = [ctypes.POINTER(GemmArgs), vp]
     L.abft_check_workspace_bytes.restype = sz
-    L.abft_check_workspace_bytes.argtypes = [i64, i64, i64]
+    L.abft_check_workspace_bytes.argtypes = [ctypes.POINTER(CheckArgs)]
     L.abft_check_only.restype = ctypes.c_int
-    L.abft_check_only.argtypes = [vp, i64, vp, i64, i32, vp, i64, vp, i64, i64, i64, f32, f32, i32, f32, vp, sz,
-                                  vp, i32, vp]
+    L.abft_check_only.argtypes = [ctypes.POINTER(CheckArgs), vp]
     _LIB = L
     return L
 

@@ -1,0 +1,155 @@
+"""Checker plugin interface of pytorch/abft/checkers.py on the B200 library.
+
+``OpMeta``, ``AbftChecker``, ``CheapSumChecker`` and ``flatten_to_2d_for_mm``
+keep the reference's names, signatures and results
+(pytorch/abft/checkers.py:16-150). The reference computes its sums with
+torch ops, a JIT CUDA extension or torch fp32 reductions depending on
+``checker_backend`` and falls back to torch ops when the extension fails
+(:79-92); here every backend name runs the native ``abft_check_only`` kernel
+sequence and a failure raises -- there is no fallback path.
+
+``RowColChecker`` is new: the same post-hoc check plus row and column
+checksums of C that locate single faults.
+"""
+from __future__ import annotations
+
+from abc import ABC, abstractmethod
+from dataclasses import dataclass
+from typing import Optional, Tuple
+
+import torch
+
+from .. import ops
+from .config import AbftConfig
+from .stats import CheckResult
+
+
+@dataclass
+class OpMeta:
+    op_name: str
+    phase: str
+    shape_key: str
+
+
+class UnsupportedOperand(ValueError):
+    """An operand the bf16 library cannot take (dtype, device, alignment)."""
+
+
+class AbftChecker(ABC):
+    @abstractmethod
+    def check(
+        self,
+        a_2d: torch.Tensor,
+        b_2d: torch.Tensor,
+        c_2d: torch.Tensor,
+        meta: OpMeta,
+        bias_1d: Optional[torch.Tensor] = None,
+    ) -> CheckResult:
+        raise NotImplementedError
+
+
+def _as_lib_operands(
+    a_2d: torch.Tensor, b_2d: torch.Tensor, c_2d: torch.Tensor, bias_1d: Optional[torch.Tensor]
+) -> Tuple[torch.Tensor, torch.Tensor, str, torch.Tensor, Optional[torch.Tensor]]:
+    """Validate and lay out (A, B, C, bias) for abft_check_only.
+
+    B arrives as [K, N] (checkers.py:145-150). When it is the transposed view
+    of an nn.Linear weight, the weight itself is passed ([N, K], no copy;
+    the reference copies it, fused_backend.py:53-58).
+    """
+    for name, t in (("a", a_2d), ("b", b_2d), ("c", c_2d)):
+        if not t.is_cuda:
+            raise UnsupportedOperand(f"{name} is not a CUDA tensor; the library has no CPU path")
+        if t.dtype != torch.bfloat16:
+            raise UnsupportedOperand(f"{name} is {t.dtype}; the library checks bfloat16 operands")
+    k = a_2d.shape[1]
+    n = b_2d.shape[1]
+    if k % 8 or n % 8:
+        raise UnsupportedOperand(f"K={k} and N={n} must be multiples of 8")
+    a = a_2d if a_2d.stride(1) == 1 and a_2d.stride(0) % 8 == 0 else a_2d.contiguous()
+    c = c_2d if c_2d.stride(1) == 1 and c_2d.stride(0) % 8 == 0 else c_2d.contiguous()
+    bt = b_2d.t()
+    if bt.stride(1) == 1 and bt.stride(0) % 8 == 0:
+        b, layout = bt, "nk"
+    elif b_2d.stride(1) == 1 and b_2d.stride(0) % 8 == 0:
+        b, layout = b_2d, "kn"
+    else:
+        b, layout = b_2d.contiguous(), "kn"
+    bias = None
+    if bias_1d is not None:
+        if not bias_1d.is_cuda or bias_1d.dtype != torch.bfloat16:
+            raise UnsupportedOperand("bias must be a CUDA bfloat16 tensor")
+        bias = bias_1d.contiguous()
+    return a, b, layout, c, bias
+
+
+class CheapSumChecker(AbftChecker):
+    """Scalar full-checksum check (checkers.py:36-126) on libabft_b200.
+
+    s_a = A.sum(0), s_b = B.sum(1), corner = dot(s_a, s_b) (+ M * sum(bias)),
+    sum_c = C.sum(); ok = |corner - sum_c| <= tol_abs or
+    |corner - sum_c| / max(|sum_c|, 1) <= tol_rel. Sums are fp32 unless
+    ``cfg.bf16_sums`` (checker_backend "python" or force_fp32_check=False),
+    which rounds them to bf16 exactly as the reference's python backend.
+    The result is read back to the host, as in the reference (:103).
+    """
+
+    locate: bool = False
+
+    def __init__(self, cfg: AbftConfig) -> None:
+        self.cfg = cfg
+
+    def check(
+        self,
+        a_2d: torch.Tensor,
+        b_2d: torch.Tensor,
+        c_2d: torch.Tensor,
+        meta: OpMeta,
+        bias_1d: Optional[torch.Tensor] = None,
+    ) -> CheckResult:
+        if not self.cfg.record_enable:
+            # The reference computes and discards the sums here (:74-75);
+            # the result it returns does not depend on them.
+            return CheckResult(ok=True, abs_err=0.0, rel_err=0.0, abft_corner=0.0, sum_c=0.0)
+        a, b, layout, c, bias = _as_lib_operands(a_2d, b_2d, c_2d, bias_1d)
+        rep = ops.check_only(a, b, c, bias, b_layout=layout, tol_abs=self.cfg.tol_abs, tol_rel=self.cfg.tol_rel,
+                             locate=self.locate, bf16_sums=self.cfg.bf16_sums, thr_scale=self.cfg.thr_scale,
+                             report=ops.ReportBuffer(self.cfg.report_capacity, a.device)).read()
+        located = tuple((r.row, r.col) for r in rep.records if r.row >= 0 and r.col >= 0)
+        ok = rep.ref_ok == 1 and (not self.locate or rep.n_faults == 0)
+        return CheckResult(ok=ok, abs_err=float(rep.abs_err), rel_err=float(rep.rel_err),
+                           abft_corner=float(rep.corner), sum_c=float(rep.sum_c), n_faults=int(rep.n_faults),
+                           n_located=len(located), n_corrected=0, located=located)
+
+
+class RowColChecker(CheapSumChecker):
+    """CheapSumChecker plus row and column checksums of C.
+
+    Each row sum of C is compared with A (B e) and each column sum with
+    (e^T A) B under tau sqrt(K) max|C| plus the bf16 rounding of the summed
+    elements; a mismatching row and column with agreeing residuals locate a
+    fault at their crossing. ``ok`` is False when the scalar rule fails or
+    any row or column mismatches.
+    """
+
+    locate = True
+
+
+def flatten_to_2d_for_mm(x: torch.Tensor, right_operand: bool = False) -> Optional[torch.Tensor]:
+    """Left operand [..., m, k] -> [m*, k]; right operand [..., k, n] -> [k, n]
+    only when the batch prefix is 1 (checkers.py:129-150)."""
+    if x.dim() < 2:
+        return None
+    if not right_operand:
+        k = x.shape[-1]
+        return x.reshape(-1, k)
+    k = x.shape[-2]
+    n = x.shape[-1]
+    if x.dim() == 2:
+        return x
+    prefix = 1
+    for d in x.shape[:-2]:
+        prefix *= int(d)
+    if prefix != 1:
+        return None
+    return x.reshape(k, n)

@@ -1,0 +1,309 @@
+"""AbftInjector: the operator hook of pytorch/abft/injector.py on libabft_b200.
+
+Inside ``with AbftInjector(cfg, checker, stats):`` the module attributes
+``F.linear``, ``torch.matmul`` and ``torch.bmm`` are replaced by wrappers, as
+in the reference (injector.py:31-51), and restored on exit.
+
+* ``torch.matmul`` / ``torch.bmm`` keep the reference flow: run the op,
+  maybe perturb one output element, then ``checker.check`` on the flattened
+  operands (injector.py:164-187).
+* ``F.linear`` with ``checker_backend="b200"`` and ``fused_linear`` replaces
+  "torch GEMM, then check" by one call of the fused kernel
+  (``abft_gemm_bf16``): the GEMM, its per-tile weighted row checksums and
+  the compare run in one launch, a drawn fault is added to the fp32
+  accumulator before the compare, and with ``detect_only=False`` located
+  faults are corrected before the bf16 store. Other backends, or operands
+  the library cannot take, follow the reference flow.
+
+The random stream is the reference's: one ``random.Random(cfg.seed)`` per
+injector, consumed in the same order -- the injection coin and index after
+the op (:58-75), then the sampling coin inside the check gate (:53-56,
+:77-99) -- so a seed selects the same faults on both implementations.
+
+Reports of fused linears can be deferred (``defer_reports=True``): the
+fault report stays on the device and is read at ``flush()`` (called on exit)
+instead of forcing a device->host sync per GEMM like the reference (:103).
+"""
+from __future__ import annotations
+
+import random
+from contextlib import AbstractContextManager
+from typing import Any, Callable, List, Optional, Tuple
+
+import torch
+import torch.nn.functional as F
+
+from .. import _native as N
+from .. import ops
+from .checkers import AbftChecker, OpMeta, UnsupportedOperand, flatten_to_2d_for_mm
+from .config import AbftConfig
+from .stats import AbftStatsCollector, CheckResult
+
+
+def _shape_key(a2: torch.Tensor, b2: torch.Tensor, c2: torch.Tensor) -> str:
+    return f"A{tuple(a2.shape)}_B{tuple(b2.shape)}_C{tuple(c2.shape)}"
+
+
+def result_from_report(rep: N.FaultReport) -> CheckResult:
+    """CheckResult of a fused-linear report.
+
+    ok: no checksum mismatch. abs_err: the largest |row-sum residual| of the
+    recorded faults; rel_err: the largest residual / bound ratio (> 1 for a
+    detected fault). abft_corner / sum_c stay 0: the fused check compares
+    per-tile row checksums, not the scalar corner.
+    """
+    abs_err = max((abs(r.residual) for r in rep.records), default=0.0)
+    rel_err = max((abs(r.residual) / r.threshold if r.threshold > 0 else float("inf") for r in rep.records),
+                  default=0.0)
+    located = tuple((r.row, r.col) for r in rep.records if r.located)
+    return CheckResult(ok=rep.n_faults == 0, abs_err=float(abs_err), rel_err=float(rel_err), abft_corner=0.0,
+                       sum_c=0.0, n_faults=int(rep.n_faults), n_located=int(rep.n_located),
+                       n_corrected=int(rep.n_corrected), located=located)
+
+
+class WeightChecksumCache:
+    """Per-weight checksum blocks (``ops.encode_weight``), reused across calls.
+
+    Keyed by storage pointer, shape, strides, tile width and the tensor's
+    version counter, so an in-place update of the weight re-encodes it.
+    """
+
+    def __init__(self, max_entries: int = 4096):
+        self.max_entries = max_entries
+        self._d: dict = {}
+
+    def get(self, weight: torch.Tensor, tile_n: int) -> torch.Tensor:
+        key = (weight.data_ptr(), tuple(weight.shape), tuple(weight.stride()), weight._version, tile_n,
+               weight.device.index)
+        v = self._d.get(key)
+        if v is None:
+            if len(self._d) >= self.max_entries:
+                self._d.pop(next(iter(self._d)))
+            v = ops.encode_weight(weight, tile_n)
+            self._d[key] = v
+        return v
+
+    def clear(self) -> None:
+        self._d.clear()
+
+
+class AbftInjector(AbstractContextManager):
+    def __init__(self, cfg: AbftConfig, checker: AbftChecker, stats: AbftStatsCollector,
+                 defer_reports: bool = False):
+        self.cfg = cfg
+        self.checker = checker
+        self.stats = stats
+        self.rng = random.Random(cfg.seed)
+        self.defer_reports = defer_reports
+        self.checksums = WeightChecksumCache()
+
+        self._orig_linear: Optional[Callable[..., torch.Tensor]] = None
+        self._orig_matmul: Optional[Callable[..., torch.Tensor]] = None
+        self._orig_bmm: Optional[Callable[..., torch.Tensor]] = None
+        self._dump_done: bool = False
+        self._pending: List[Tuple[ops.ReportBuffer, str, str, str, bool]] = []
+
+    # ------------------------------------------------------------------ context
+    def __enter__(self) -> "AbftInjector":
+        self._orig_linear = F.linear
+        self._orig_matmul = torch.matmul
+        self._orig_bmm = torch.bmm
+        if self.cfg.enable_linear:
+            F.linear = self._wrap_linear(self._orig_linear)
+        if self.cfg.enable_matmul:
+            torch.matmul = self._wrap_matmul(self._orig_matmul)
+        if self.cfg.enable_bmm:
+            torch.bmm = self._wrap_bmm(self._orig_bmm)
+        return self
+
+    def __exit__(self, exc_type, exc, tb) -> None:
+        if self._orig_linear is not None:
+            F.linear = self._orig_linear
+        if self._orig_matmul is not None:
+            torch.matmul = self._orig_matmul
+        if self._orig_bmm is not None:
+            torch.bmm = self._orig_bmm
+        if exc_type is None:
+            self.flush()
+        return None
+
+    def flush(self) -> None:
+        """Record every deferred fused-linear report (one host sync)."""
+        pending, self._pending = self._pending, []
+        saved = self.stats.current_phase
+        try:
+            for rep_buf, op_name, phase, shape_key, injected in pending:
+                self.stats.current_phase = phase
+                self.stats.record_check(op_name=op_name, shape_key=shape_key,
+                                        result=result_from_report(rep_buf.read()), injected=injected)
+        finally:
+            self.stats.current_phase = saved
+
+    # -------------------------------------------------------- reference gates
+    def _sample(self) -> bool:
+        if self.cfg.sample_rate >= 1.0:
+            return True
+        return self.rng.random() < self.cfg.sample_rate
+
+    def _draw_fault(self, numel: int) -> Optional[int]:
+        """The injection decision of injector.py:58-75 without the tensor op."""
+        if not self.cfg.inject_fault:
+            return None
+        if not self.cfg.inject_phase_enabled(self.stats.current_phase):
+            return None
+        if self.cfg.inject_probability <= 0.0:
+            return None
+        if self.rng.random() >= self.cfg.inject_probability:
+            return None
+        if numel == 0:
+            return None
+        idx = self.rng.randrange(numel)
+        self.stats.record_injection()
+        return idx
+
+    def _maybe_inject_fault(self, out: torch.Tensor) -> Tuple[torch.Tensor, bool]:
+        idx = self._draw_fault(out.numel())
+        if idx is None:
+            return out, False
+        perturbed = out.clone()
+        perturbed.reshape(-1)[idx] += self.cfg.inject_magnitude
+        return perturbed, True
+
+    def _check_gate(self, a_2d, b_2d, c_2d) -> bool:
+        """Gates of injector.py:86-99, in order (the sample coin is drawn third)."""
+        if not self.cfg.enable:
+            return False
+        if not self.cfg.check_enable:
+            return False
+        if not self.cfg.phase_enabled(self.stats.current_phase):
+            return False
+        if not self._sample():
+            return False
+        if a_2d is None or b_2d is None or c_2d is None:
+            return False
+        if a_2d.numel() == 0 or b_2d.numel() == 0 or c_2d.numel() == 0:
+            return False
+        if a_2d.shape[1] != b_2d.shape[0]:
+            return False
+        return True
+
+    def _maybe_check(self, op_name: str, a_2d, b_2d, c_2d, injected: bool,
+                     bias_1d: Optional[torch.Tensor] = None) -> None:
+        if not self._check_gate(a_2d, b_2d, c_2d):
+            return
+        shape_key = _shape_key(a_2d, b_2d, c_2d)
+        try:
+            result = self.checker.check(
+                a_2d, b_2d, c_2d, OpMeta(op_name=op_name, phase=self.stats.current_phase, shape_key=shape_key),
+                bias_1d=bias_1d)
+        except UnsupportedOperand:
+            self.stats.record_skip_unsupported()
+            return
+        if self.cfg.record_enable:
+            self.stats.record_check(op_name=op_name, shape_key=shape_key, result=result, injected=injected)
+        self._maybe_dump_tensors(op_name, shape_key, a_2d, b_2d, c_2d, bias_1d)
+
+    def _maybe_dump_tensors(self, op_name, shape_key, a_2d, b_2d, c_2d, bias_1d) -> None:
+        if self._dump_done or not self.cfg.dump_file or not self.cfg.dump_shape_key:
+            return
+        if not self.cfg.dump_phase_enabled(self.stats.current_phase):
+            return
+        if shape_key != self.cfg.dump_shape_key:
+            return
+        payload = {
+            "meta": {"phase": self.stats.current_phase, "op_name": op_name, "shape_key": shape_key},
+            "a": a_2d.detach().cpu(),
+            "b": b_2d.detach().cpu(),
+            "c": c_2d.detach().cpu(),
+            "bias": None if bias_1d is None else bias_1d.detach().cpu(),
+        }
+        torch.save(payload, self.cfg.dump_file)
+        self._dump_done = True
+
+    # ---------------------------------------------------------- fused linear
+    def _fused_linear_ok(self, x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor]) -> bool:
+        if self.cfg.checker_backend != "b200" or not self.cfg.fused_linear:
+            return False
+        if not (x.is_cuda and weight.is_cuda) or x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+            return False
+        if weight.dim() != 2 or x.dim() < 1 or x.shape[-1] != weight.shape[1]:
+            return False
+        n, k = weight.shape
+        if k % 8 or n % 8 or k == 0 or x.numel() == 0:
+            return False
+        if weight.stride(1) != 1 or weight.stride(0) % 8 or weight.data_ptr() % 16:
+            return False
+        if bias is not None and (not bias.is_cuda or bias.dtype != torch.bfloat16 or bias.dim() != 1):
+            return False
+        return True
+
+    def _fused_linear(self, x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor]) -> torch.Tensor:
+        n, k = weight.shape
+        x2 = x.reshape(-1, k)
+        if x2.stride(1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
+            x2 = x2.contiguous()
+        m = x2.shape[0]
+        # injection first, then the check gate: the reference's rng order
+        idx = self._draw_fault(m * n)
+        injected = idx is not None
+        b2 = weight.t()
+        c_shape = torch.Size((m, n))
+        check = self._check_gate(x2, b2, torch.empty(c_shape, device="meta"))
+        mode = N.MODE_OFF
+        if check:
+            mode = N.MODE_DETECT | (0 if self.cfg.detect_only else N.MODE_CORRECT)
+        tile_n = ops.pick_tile_n(m, n, x2.device)
+        cks = self.checksums.get(weight, tile_n) if check else None
+        inject = [(idx // n, idx % n, float(self.cfg.inject_magnitude))] if injected else None
+        rep = ops.ReportBuffer(self.cfg.report_capacity, x2.device) if check else None
+        out, rep = ops.abft_gemm(x2, weight, None if bias is None else bias.contiguous(), mode=mode, tile_n=tile_n,
+                                 thr_scale=self.cfg.thr_scale, thr_abs=self.cfg.thr_abs, checksums=cks,
+                                 inject=inject, report=rep)
+        if check:
+            shape_key = f"A{tuple(x2.shape)}_B{tuple(b2.shape)}_C{tuple(c_shape)}"
+            if self.cfg.record_enable:
+                if self.defer_reports:
+                    self._pending.append((rep, "linear", self.stats.current_phase, shape_key, injected))
+                else:
+                    self.stats.record_check(op_name="linear", shape_key=shape_key,
+                                            result=result_from_report(rep.read()), injected=injected)
+            self._maybe_dump_tensors("linear", shape_key, x2, b2, out, bias)
+        return out.reshape(*x.shape[:-1], n)
+
+    # ------------------------------------------------------------- wrappers
+    def _wrap_linear(self, fn: Callable[..., torch.Tensor]) -> Callable[..., torch.Tensor]:
+        def wrapped(input: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+            if self._fused_linear_ok(input, weight, bias):
+                return self._fused_linear(input, weight, bias)
+            out = fn(input, weight, bias)
+            out2, injected = self._maybe_inject_fault(out)
+            a2 = flatten_to_2d_for_mm(input, right_operand=False)
+            b2 = flatten_to_2d_for_mm(weight.t(), right_operand=True)  # [k, n]
+            c2 = flatten_to_2d_for_mm(out2, right_operand=False)
+            self._maybe_check("linear", a2, b2, c2, injected, bias_1d=bias)
+            return out2
+
+        return wrapped
+
+    def _wrap_matmul(self, fn: Callable[..., torch.Tensor]) -> Callable[..., torch.Tensor]:
+        def wrapped(input: torch.Tensor, other: torch.Tensor, *args: Any, **kwargs: Any) -> torch.Tensor:
+            out = fn(input, other, *args, **kwargs)
+            out2, injected = self._maybe_inject_fault(out)
+            a2 = flatten_to_2d_for_mm(input, right_operand=False)
+            b2 = flatten_to_2d_for_mm(other, right_operand=True)
+            c2 = flatten_to_2d_for_mm(out2, right_operand=False)
+            self._maybe_check("matmul", a2, b2, c2, injected)
+            return out2
+
+        return wrapped
+
+    def _wrap_bmm(self, fn: Callable[..., torch.Tensor]) -> Callable[..., torch.Tensor]:
+        def wrapped(input: torch.Tensor, mat2: torch.Tensor, *args: Any, **kwargs: Any) -> torch.Tensor:
+            out = fn(input, mat2, *args, **kwargs)
+            out2, injected = self._maybe_inject_fault(out)
+            # per-batch 2-D checks, as the reference (injector.py:180-186)
+            for bi in range(input.shape[0]):
+                self._maybe_check("bmm", input[bi], mat2[bi], out2[bi], injected)
+            return out2
+
+        return wrapped

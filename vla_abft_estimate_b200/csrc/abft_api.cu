@@ -179,7 +179,7 @@ int validate_gemm(const abft_gemm_args* a) {
   if ((a->K % 8) || (a->N % 8) || (a->lda % 8) || (a->ldb % 8) || (a->ldc % 8)) return ABFT_ERR_ALIGNMENT;
   if (!aligned16(a->A) || !aligned16(a->B) || !aligned16(a->C)) return ABFT_ERR_ALIGNMENT;
   if (a->bias != nullptr && !aligned16(a->bias)) return ABFT_ERR_ALIGNMENT;
-  if (a->mode & ~(ABFT_MODE_DETECT | ABFT_MODE_CORRECT | ABFT_MODE_REF)) return ABFT_ERR_INVALID_ARG;
+  if (a->mode & ~(ABFT_MODE_DETECT | ABFT_MODE_CORRECT | ABFT_MODE_REF | ABFT_MODE_REF_BF16)) return ABFT_ERR_INVALID_ARG;
   if (a->tile_n != 0 && a->tile_n != 128 && a->tile_n != 256) return ABFT_ERR_UNSUPPORTED;
   if (a->mode != ABFT_MODE_OFF && (a->report == nullptr || a->report_capacity < 0)) return ABFT_ERR_INVALID_ARG;
   if (a->report != nullptr && !aligned16(a->report)) return ABFT_ERR_ALIGNMENT;
@@ -354,7 +354,8 @@ int abft_gemm_bf16(const abft_gemm_args* a, void* stream) {
     rc = colsum(a->B, a->ldb, a->N, a->K, nullptr, pb, vf, nullptr, nullptr, sms, s);
     if (rc != ABFT_OK) return rc;
     ref_finalize_kernel<<<1, 1024, 0, s>>>(u, vf, p.K, p.bias, p.N, p.M, p.tile_sumc, p.num_tiles * 8, a->tol_abs,
-                                           a->tol_rel, p.report, p.capacity, kBM, bn);
+                                           a->tol_rel, (a->mode & ABFT_MODE_REF_BF16) ? 1 : 0, p.report, p.capacity,
+                                           kBM, bd);
     rc = launch_status();
   }
   return rc;
@@ -392,76 +393,77 @@ void check_ws_layout(float* base, int64_t M, int64_t N, int64_t K, int sms, Chec
 }
 }  // namespace
 
-size_t abft_check_workspace_bytes(int64_t M, int64_t N, int64_t K) {
-  if (M <= 0 || N <= 0 || K <= 0) return 0;
+size_t abft_check_workspace_bytes(const abft_check_args* c) {
+  if (c == nullptr || c->M <= 0 || c->N <= 0 || c->K <= 0) return 0;
   int dev;
   DeviceInfo info;
   int sms = 148;
   if (current_device(&dev, &info) == ABFT_OK) sms = info.sms;
   CheckWs w;
-  check_ws_layout(nullptr, M, N, K, sms, &w);
+  check_ws_layout(nullptr, c->M, c->N, c->K, sms, &w);
   return align256(w.floats * 4);
 }
 
-int abft_check_only(const void* A, int64_t lda, const void* B, int64_t ldb, int32_t b_kn, const void* C, int64_t ldc,
-                    const void* bias, int64_t M, int64_t N, int64_t K, float tol_abs, float tol_rel, int32_t locate,
-                    float thr_scale, void* workspace, size_t workspace_bytes, void* report, int32_t report_capacity,
-                    void* stream) {
-  if (A == nullptr || B == nullptr || C == nullptr || report == nullptr) return ABFT_ERR_INVALID_ARG;
-  if (M <= 0 || N <= 0 || K <= 0 || report_capacity < 0 || (b_kn != 0 && b_kn != 1)) return ABFT_ERR_INVALID_ARG;
+int abft_check_only(const abft_check_args* c, void* stream) {
+  if (c == nullptr || c->A == nullptr || c->B == nullptr || c->C == nullptr || c->report == nullptr)
+    return ABFT_ERR_INVALID_ARG;
+  const int64_t M = c->M, N = c->N, K = c->K;
+  if (M <= 0 || N <= 0 || K <= 0 || c->report_capacity < 0 || (c->b_kn != 0 && c->b_kn != 1))
+    return ABFT_ERR_INVALID_ARG;
+  if (c->flags & ~(ABFT_CHECK_LOCATE | ABFT_CHECK_BF16_SUMS)) return ABFT_ERR_INVALID_ARG;
   if (M > (1ll << 30) || N > (1ll << 30) || K > (1ll << 30)) return ABFT_ERR_UNSUPPORTED;
-  if (lda < K || ldc < N || ldb < (b_kn ? N : K)) return ABFT_ERR_INVALID_ARG;
-  if ((K % 8) || (N % 8) || (lda % 8) || (ldb % 8) || (ldc % 8)) return ABFT_ERR_ALIGNMENT;
-  if (!aligned16(A) || !aligned16(B) || !aligned16(C) || !aligned16(report)) return ABFT_ERR_ALIGNMENT;
-  if (bias != nullptr && !aligned16(bias)) return ABFT_ERR_ALIGNMENT;
-  if (!(thr_scale >= 0.f)) return ABFT_ERR_INVALID_ARG;
+  if (c->lda < K || c->ldc < N || c->ldb < (c->b_kn ? N : K)) return ABFT_ERR_INVALID_ARG;
+  if ((K % 8) || (N % 8) || (c->lda % 8) || (c->ldb % 8) || (c->ldc % 8)) return ABFT_ERR_ALIGNMENT;
+  if (!aligned16(c->A) || !aligned16(c->B) || !aligned16(c->C) || !aligned16(c->report)) return ABFT_ERR_ALIGNMENT;
+  if (c->bias != nullptr && !aligned16(c->bias)) return ABFT_ERR_ALIGNMENT;
+  if (!(c->thr_scale >= 0.f)) return ABFT_ERR_INVALID_ARG;
   int dev;
   DeviceInfo info;
   int rc = current_device(&dev, &info);
   if (rc != ABFT_OK) return rc;
-  const size_t need = abft_check_workspace_bytes(M, N, K);
-  if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace)) return ABFT_ERR_WORKSPACE;
+  const size_t need = abft_check_workspace_bytes(c);
+  if (c->workspace == nullptr || c->workspace_bytes < need || !aligned16(c->workspace)) return ABFT_ERR_WORKSPACE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int sms = info.sms;
   CheckWs w;
-  check_ws_layout(static_cast<float*>(workspace), M, N, K, sms, &w);
+  check_ws_layout(static_cast<float*>(c->workspace), M, N, K, sms, &w);
+  const __nv_bfloat16* bias = static_cast<const __nv_bfloat16*>(c->bias);
 
-  if (cudaMemsetAsync(report, 0, sizeof(abft_report), s) != cudaSuccess) return launch_status(), ABFT_ERR_CUDA;
-  abft_report* rep = static_cast<abft_report*>(report);
+  if (cudaMemsetAsync(c->report, 0, sizeof(abft_report), s) != cudaSuccess) return launch_status(), ABFT_ERR_CUDA;
+  abft_report* rep = static_cast<abft_report*>(c->report);
 
   // s_a = A.sum(0) and s_b = B.sum(1)   (pytorch/abft/checkers.py:117-118)
-  rc = colsum(A, lda, M, K, nullptr, w.pa, w.u, nullptr, nullptr, sms, s);
+  rc = colsum(c->A, c->lda, M, K, nullptr, w.pa, w.u, nullptr, nullptr, sms, s);
   if (rc != ABFT_OK) return rc;
-  if (b_kn == 0)
-    rc = colsum(B, ldb, N, K, nullptr, w.pb, w.v, nullptr, nullptr, sms, s);
+  if (c->b_kn == 0)
+    rc = colsum(c->B, c->ldb, N, K, nullptr, w.pb, w.v, nullptr, nullptr, sms, s);
   else
-    rc = rowdot(B, ldb, K, N, nullptr, w.v, nullptr, nullptr, s);
+    rc = rowdot(c->B, c->ldb, K, N, nullptr, w.v, nullptr, nullptr, s);
   if (rc != ABFT_OK) return rc;
   // row sums of C (sum_c = sum of the row sums, fixed order)
-  rc = rowdot(C, ldc, M, N, nullptr, w.rsum, w.rmax, w.rabs, s);
+  rc = rowdot(c->C, c->ldc, M, N, nullptr, w.rsum, w.rmax, w.rabs, s);
   if (rc != ABFT_OK) return rc;
-  ref_finalize_kernel<<<1, 1024, 0, s>>>(w.u, w.v, static_cast<int>(K), static_cast<const __nv_bfloat16*>(bias),
-                                         static_cast<int>(N), static_cast<int>(M), w.rsum, static_cast<int>(M), tol_abs,
-                                         tol_rel, rep, report_capacity, 0, 0);
+  ref_finalize_kernel<<<1, 1024, 0, s>>>(w.u, w.v, static_cast<int>(K), bias, static_cast<int>(N), static_cast<int>(M),
+                                         w.rsum, static_cast<int>(M), c->tol_abs, c->tol_rel,
+                                         (c->flags & ABFT_CHECK_BF16_SUMS) ? 1 : 0, rep, c->report_capacity, 0, 0);
   rc = launch_status();
-  if (rc != ABFT_OK || !locate) return rc;
+  if (rc != ABFT_OK || !(c->flags & ABFT_CHECK_LOCATE)) return rc;
 
   // Expected row sums A (B e), expected column sums (e^T A) B, actual column sums.
-  rc = rowdot(A, lda, M, K, w.v, w.rexp, nullptr, nullptr, s);
+  rc = rowdot(c->A, c->lda, M, K, w.v, w.rexp, nullptr, nullptr, s);
   if (rc != ABFT_OK) return rc;
-  if (b_kn == 0)
-    rc = rowdot(B, ldb, N, K, w.u, w.cexp, nullptr, nullptr, s);
+  if (c->b_kn == 0)
+    rc = rowdot(c->B, c->ldb, N, K, w.u, w.cexp, nullptr, nullptr, s);
   else
-    rc = colsum(B, ldb, K, N, w.u, w.pb, w.cexp, nullptr, nullptr, sms, s);
+    rc = colsum(c->B, c->ldb, K, N, w.u, w.pb, w.cexp, nullptr, nullptr, sms, s);
   if (rc != ABFT_OK) return rc;
-  rc = colsum(C, ldc, M, N, nullptr, w.pc, w.csum, w.cmax, w.cabs, sms, s);
+  rc = colsum(c->C, c->ldc, M, N, nullptr, w.pc, w.csum, w.cmax, w.cabs, sms, s);
   if (rc != ABFT_OK) return rc;
-  const float thr_k = static_cast<float>(static_cast<double>(thr_scale) * sqrt(static_cast<double>(K)));
+  const float thr_k = static_cast<float>(static_cast<double>(c->thr_scale) * sqrt(static_cast<double>(K)));
   constexpr float kBf16Unit = 1.0f / 512.0f;  // worst-case relative rounding of a stored bf16 element
   locate_finalize_kernel<<<1, 1024, 0, s>>>(w.rsum, w.rmax, w.rabs, w.rexp, static_cast<int>(M), w.csum, w.cmax,
-                                            w.cabs, w.cexp, static_cast<int>(N),
-                                            static_cast<const __nv_bfloat16*>(bias), thr_k, kBf16Unit, rep,
-                                            report_capacity);
+                                            w.cabs, w.cexp, static_cast<int>(N), bias, thr_k, kBf16Unit, rep,
+                                            c->report_capacity);
   return launch_status();
 }
 

@@ -245,31 +245,54 @@ __device__ __forceinline__ float block_sum_1024(float v, float* scratch /*32*/) 
   return scratch[0];
 }
 
+__device__ __forceinline__ float round_bf16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
 // One block of 1024 threads. Follows pytorch/abft/checkers.py:112-126
 // (corner = dot(s_a, s_b) + m * sum(bias), sum_c = sum(C)) and :96-110
 // (diff, rel = diff / max(|sum_c|, 1), ok = diff <= tol_abs or rel <= tol_rel).
+// With bf16_sums every intermediate is rounded to bf16, as the python
+// backend's bf16 tensors are (s_a, s_b, dot, bias sum, m * bias sum,
+// corner, sum_c, diff, rel) and the tolerances are compared as bf16 values.
 __global__ void __launch_bounds__(1024) ref_finalize_kernel(const float* __restrict__ u, const float* __restrict__ v,
                                                             int K, const __nv_bfloat16* __restrict__ bias, int N,
                                                             int M, const float* __restrict__ parts, int n_parts,
-                                                            float tol_abs, float tol_rel, abft_report* rep,
-                                                            int capacity, int tile_m, int tile_n) {
+                                                            float tol_abs, float tol_rel, int bf16_sums,
+                                                            abft_report* rep, int capacity, int tile_m, int tile_n) {
   __shared__ float scratch[32];
   float c = 0.f;
-  for (int k = threadIdx.x; k < K; k += 1024) c = fmaf(u[k], v[k], c);
+  for (int k = threadIdx.x; k < K; k += 1024) {
+    const float uk = bf16_sums ? round_bf16(u[k]) : u[k];
+    const float vk = bf16_sums ? round_bf16(v[k]) : v[k];
+    c = fmaf(uk, vk, c);
+  }
   float corner = block_sum_1024(c, scratch);
+  if (bf16_sums) corner = round_bf16(corner);
   if (bias != nullptr) {
     float b = 0.f;
     for (int j = threadIdx.x; j < N; j += 1024) b += __bfloat162float(bias[j]);
-    const float bs = block_sum_1024(b, scratch);
-    corner += static_cast<float>(M) * bs;
+    float bs = block_sum_1024(b, scratch);
+    if (bf16_sums) {
+      bs = round_bf16(bs);
+      corner = round_bf16(corner + round_bf16(static_cast<float>(M) * bs));
+    } else {
+      corner += static_cast<float>(M) * bs;
+    }
   }
   float s = 0.f;
   for (int i = threadIdx.x; i < n_parts; i += 1024) s += parts[i];
-  const float sum_c = block_sum_1024(s, scratch);
+  float sum_c = block_sum_1024(s, scratch);
+  if (bf16_sums) sum_c = round_bf16(sum_c);
   if (threadIdx.x == 0) {
-    const float diff = fabsf(corner - sum_c);
-    const float rel = diff / fmaxf(fabsf(sum_c), 1.f);
-    const bool ok = (diff <= tol_abs) || (rel <= tol_rel);
+    float diff = fabsf(corner - sum_c);
+    float rel = diff / fmaxf(fabsf(sum_c), 1.f);
+    float ta = tol_abs, tr = tol_rel;
+    if (bf16_sums) {
+      diff = round_bf16(diff);
+      rel = round_bf16(diff / fmaxf(fabsf(sum_c), 1.f));
+      ta = round_bf16(tol_abs);
+      tr = round_bf16(tol_rel);
+    }
+    const bool ok = (diff <= ta) || (rel <= tr);
     rep->corner = corner;
     rep->sum_c = sum_c;
     rep->abs_err = diff;

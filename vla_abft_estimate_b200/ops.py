@@ -200,15 +200,17 @@ def check_only(
     tol_abs: float = 1e-2,
     tol_rel: float = 1e-2,
     locate: bool = False,
+    bf16_sums: bool = False,
     thr_scale: float = DEFAULT_THR_SCALE,
     report: Optional[ReportBuffer] = None,
 ) -> ReportBuffer:
-    """Check an existing ``c`` against ``a`` and ``b``.
+    """Check an existing ``c`` against ``a`` and ``b`` (no GEMM).
 
     ``b_layout="kn"``: b is [K, N] (the reference checker's b_2d);
     ``b_layout="nk"``: b is an nn.Linear weight [N, K] (no transpose copy).
-    Fills report.corner / sum_c / abs_err / rel_err / ref_ok, and with
-    ``locate`` the mismatching rows and columns.
+    Fills report.corner / sum_c / abs_err / rel_err / ref_ok; ``bf16_sums``
+    rounds the intermediates to bf16 like the reference's python backend;
+    ``locate`` also records mismatching rows and columns.
     """
     _require_bf16_cuda("a", a, 2)
     _require_bf16_cuda("c", c, 2)
@@ -217,20 +219,18 @@ def check_only(
     m, k = a.shape
     if b_layout == "kn":
         kn = 1
-        if b.stride(1) != 1:
-            b = b.contiguous()
         if b.shape[0] != k:
             raise ValueError("b [K, N] does not match a")
         n = b.shape[1]
     elif b_layout == "nk":
         kn = 0
-        if b.stride(1) != 1:
-            b = b.contiguous()
         if b.shape[1] != k:
             raise ValueError("b [N, K] does not match a")
         n = b.shape[0]
     else:
         raise ValueError("b_layout must be 'kn' or 'nk'")
+    if b.stride(1) != 1:
+        b = b.contiguous()
     if tuple(c.shape) != (m, n):
         raise ValueError(f"c must be [{m}, {n}]")
     if bias is not None:
@@ -238,13 +238,20 @@ def check_only(
     dev = a.device
     if report is None:
         report = ReportBuffer(DEFAULT_CAPACITY, dev)
+    args = N.CheckArgs()
+    args.A, args.B, args.C, args.bias = _ptr(a), _ptr(b), _ptr(c), _ptr(bias)
+    args.M, args.N, args.K = m, n, k
+    args.lda, args.ldb, args.ldc = a.stride(0), b.stride(0), c.stride(0)
+    args.b_kn = kn
+    args.flags = (N.CHECK_LOCATE if locate else 0) | (N.CHECK_BF16_SUMS if bf16_sums else 0)
+    args.tol_abs, args.tol_rel, args.thr_scale = float(tol_abs), float(tol_rel), float(thr_scale)
+    args.report, args.report_capacity = report.data_ptr(), report.capacity
     L = N.lib()
     with torch.cuda.device(dev):
-        ws_bytes = int(L.abft_check_workspace_bytes(m, n, k))
+        ws_bytes = int(L.abft_check_workspace_bytes(ctypes.byref(args)))
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
-        rc = L.abft_check_only(_ptr(a), a.stride(0), _ptr(b), b.stride(0), kn, _ptr(c), c.stride(0), _ptr(bias),
-                               m, n, k, float(tol_abs), float(tol_rel), 1 if locate else 0, float(thr_scale),
-                               _ptr(ws), ws_bytes, report.data_ptr(), report.capacity, _stream(dev))
+        args.workspace, args.workspace_bytes = _ptr(ws), ws_bytes
+        rc = L.abft_check_only(ctypes.byref(args), _stream(dev))
     N.check("abft_check_only", rc)
     ws.record_stream(torch.cuda.current_stream(dev))
     return report
