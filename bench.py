@@ -47,6 +47,9 @@ def parse_args():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--size", type=int, default=8192, help="M = K = per-GPU N")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-case", choices=["off", "check", "both"], default=None,
+                    help="only run two rounds of the fused GEMM (unchecked then checked for 'both') "
+                         "on randn inputs, for an ncu capture")
     return ap.parse_args()
 
 
@@ -396,8 +399,36 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def profile_case(args):
+    """Two rounds of the fused GEMM at --size: the capture target of ncu."""
+    import torch
+
+    from vla_abft_estimate_b200 import _native as N
+    from vla_abft_estimate_b200 import ops
+
+    dev = torch.device("cuda", 0)
+    s = args.size
+    a = (torch.randn(s, s, device=dev) * s ** -0.5).bfloat16()
+    w = (torch.randn(s, s, device=dev) * s ** -0.5).bfloat16()
+    out = torch.empty(s, s, device=dev, dtype=torch.bfloat16)
+    tile_n = ops.pick_tile_n(s, s, dev, N.MODE_DETECT | N.MODE_CORRECT)
+    cks = ops.encode_weight(w, tile_n)
+    rep = ops.ReportBuffer(64, dev)
+    for _ in range(2):
+        if args.profile_case in ("off", "both"):
+            ops.abft_gemm(a, w, mode=N.MODE_OFF, out=out, tile_n=ops.pick_tile_n(s, s, dev, N.MODE_OFF))
+        if args.profile_case in ("check", "both"):
+            ops.abft_gemm(a, w, mode=N.MODE_DETECT | N.MODE_CORRECT, out=out, tile_n=tile_n, checksums=cks,
+                          report=rep)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": args.profile_case, "size": s, "faults": rep.read().n_faults}))
+
+
 def main():
     args = parse_args()
+    if args.profile_case:
+        profile_case(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -141,8 +141,10 @@ const char* abft_status_string(int status);
 /* Bytes of a report with `capacity` records. */
 size_t abft_report_bytes(int32_t capacity);
 
-/* Tile width the library picks for an (M, N) output when tile_n == 0. */
-int32_t abft_pick_tile_n(int64_t M, int64_t N, int32_t num_sms);
+/* Tile width (256 or 128) the library picks for an (M, N) output and mode
+ * when tile_n == 0: the one with the fewest waves of tiles over num_sms,
+ * weighting a 128-wide tile as 0.55 of a 256-wide one. */
+int32_t abft_pick_tile_n(int64_t M, int64_t N, int32_t num_sms, uint32_t mode);
 
 /* Bytes of the per-tile checksum block of a [N, K] weight for tile_n. */
 size_t abft_checksum_bytes(int64_t N, int64_t K, int32_t tile_n);

@@ -225,10 +225,24 @@ size_t abft_report_bytes(int32_t capacity) {
   return sizeof(abft_report) + static_cast<size_t>(capacity) * sizeof(abft_fault_record);
 }
 
-int32_t abft_pick_tile_n(int64_t M, int64_t N, int32_t num_sms) {
+int32_t abft_pick_tile_n(int64_t M, int64_t N, int32_t num_sms, uint32_t mode) {
   if (num_sms <= 0) num_sms = 148;
-  const int64_t tiles256 = cdiv(M, kBM) * cdiv(N, 256);
-  return tiles256 >= num_sms ? 256 : 128;
+  if (M <= 0 || N <= 0) return 256;
+  const bool check = (mode & (ABFT_MODE_DETECT | ABFT_MODE_CORRECT)) != 0;
+  // Cost of a launch ~ waves x per-tile time; a 128-wide tile takes about
+  // 0.55 of a 256-wide tile's time (same A stream and epilogue, half the MMA).
+  double best_cost = 0.0;
+  int32_t best = 256;
+  for (int32_t bn : {256, 128}) {
+    const int64_t d = check ? bn - kChkRows : bn;
+    const int64_t tiles = cdiv(M, kBM) * cdiv(N, d);
+    const double cost = static_cast<double>(cdiv(tiles, num_sms)) * (bn == 256 ? 1.0 : 0.55);
+    if (bn == 256 || cost < best_cost) {
+      best_cost = cost;
+      best = bn;
+    }
+  }
+  return best;
 }
 
 size_t abft_checksum_bytes(int64_t N, int64_t K, int32_t tile_n) {
@@ -261,7 +275,7 @@ size_t abft_gemm_workspace_bytes(const abft_gemm_args* args) {
   int sms = 148;
   if (current_device(&dev, &info) == ABFT_OK) sms = info.sms;
   if (args->num_sms > 0 && args->num_sms < sms) sms = args->num_sms;
-  const int bn = args->tile_n ? args->tile_n : abft_pick_tile_n(args->M, args->N, sms);
+  const int bn = args->tile_n ? args->tile_n : abft_pick_tile_n(args->M, args->N, sms, args->mode);
   GemmWs w;
   gemm_ws_layout(args, bn, sms, &w);
   return w.total;
@@ -283,7 +297,7 @@ int abft_gemm_bf16(const abft_gemm_args* a, void* stream) {
 
   int sms = info.sms;
   if (a->num_sms > 0 && a->num_sms < sms) sms = a->num_sms;
-  const int bn = a->tile_n ? a->tile_n : abft_pick_tile_n(a->M, a->N, sms);
+  const int bn = a->tile_n ? a->tile_n : abft_pick_tile_n(a->M, a->N, sms, a->mode);
   const bool check = (a->mode & (ABFT_MODE_DETECT | ABFT_MODE_CORRECT)) != 0;
   GemmWs ws;
   gemm_ws_layout(a, bn, sms, &ws);
@@ -322,7 +336,7 @@ int abft_gemm_bf16(const abft_gemm_args* a, void* stream) {
   p.tiles_m = static_cast<int>(cdiv(a->M, kBM));
   p.tiles_n = static_cast<int>(cdiv(a->N, bd));
   p.num_tiles = p.tiles_m * p.tiles_n;
-  p.group_m = 8;
+  p.group_m = 16;
   p.mode = a->mode;
   if (p.mode & ABFT_MODE_CORRECT) p.mode |= ABFT_MODE_DETECT;
   p.thr_k = static_cast<float>(static_cast<double>(a->thr_scale) * sqrt(static_cast<double>(a->K)));
