@@ -208,6 +208,32 @@ typedef struct abft_check_args {
 size_t abft_check_workspace_bytes(const abft_check_args* args);
 int abft_check_only(const abft_check_args* args, void* stream);
 
+/* abft_check_only without a caller-provided workspace; it allocates nothing.
+ * No counterpart in the reference (its check allocates its outputs with
+ * torch::zeros on every call, pytorch/abft/kernels/abft_fused.cu:98-99).
+ *
+ * For callers that cannot call cudaMalloc: a serving loop that may not
+ * stall on the device synchronisation cudaMalloc implies, an engine whose
+ * memory pool already reserves the device memory, or a binding from a
+ * runtime with no device allocator of its own. They still pass A, B, C,
+ * bias and the report; `workspace` and `workspace_bytes` are ignored.
+ *
+ * Scratch comes from one fixed device array of ABFT_NO_ALLOC_SCRATCH_BYTES
+ * (4 MiB) inside the library, which every GPU that loads the library holds
+ * until the process exits. A shape whose abft_check_workspace_bytes()
+ * exceeds it is rejected with ABFT_ERR_WORKSPACE before any device work.
+ * The need grows mostly with N: 4096^3 takes 0.55 MiB, 16384^3 1.25 MiB,
+ * 65536^3 3.75 MiB, while M = K = 8192 with N = 131072 (4.3 MiB) is rejected.
+ * The first call on each device looks up the array's device address once,
+ * with that device current; make that first call before any stream capture.
+ * All calls share the array and every call overwrites the part it uses
+ * before reading it (nothing has to start at zero; the report header is
+ * reset on the call's stream as in abft_check_only). Calls that overlap on
+ * the GPU -- on different streams, or on different host threads for the
+ * same device -- race on the array: serialise them. */
+#define ABFT_NO_ALLOC_SCRATCH_BYTES (4u << 20)
+int abft_check_only_noalloc(const abft_check_args* args, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -49,7 +49,10 @@ EXPORTED_SYMBOLS = (
     "abft_gemm_bf16",
     "abft_check_workspace_bytes",
     "abft_check_only",
+    "abft_check_only_noalloc",
 )
+
+NO_ALLOC_SCRATCH_BYTES = 4 << 20
 
 
 class AbftError(RuntimeError):
@@ -156,6 +159,8 @@ def lib() -> ctypes.CDLL:
     L.abft_check_workspace_bytes.argtypes = [ctypes.POINTER(CheckArgs)]
     L.abft_check_only.restype = ctypes.c_int
     L.abft_check_only.argtypes = [ctypes.POINTER(CheckArgs), vp]
+    L.abft_check_only_noalloc.restype = ctypes.c_int
+    L.abft_check_only_noalloc.argtypes = [ctypes.POINTER(CheckArgs), vp]
     _LIB = L
     return L
 

@@ -481,4 +481,40 @@ int abft_check_only(const abft_check_args* c, void* stream) {
   return launch_status();
 }
 
+// ---- abft_check_only_noalloc -------------------------------------------------
+// The fixed scratch of the no-allocation entry point (include/abft_b200.h).
+// Host code must not use the array's name as an address: the device address
+// comes from cudaGetSymbolAddress, once per device, with that device current.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[ABFT_NO_ALLOC_SCRATCH_BYTES];
+
+namespace {
+void* g_noalloc_ptr[kMaxDevices];  // per-device address of g_noalloc_scratch, guarded by g_mu
+}  // namespace
+
+int abft_check_only_noalloc(const abft_check_args* args, void* stream) {
+  if (args == nullptr) return ABFT_ERR_INVALID_ARG;
+  int dev;
+  DeviceInfo info;
+  int rc = current_device(&dev, &info);
+  if (rc != ABFT_OK) return rc;
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (g_noalloc_ptr[dev] == nullptr) {
+      void* p = nullptr;
+      if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) {
+        cudaGetLastError();
+        return ABFT_ERR_CUDA;
+      }
+      g_noalloc_ptr[dev] = p;
+    }
+    scratch = g_noalloc_ptr[dev];
+  }
+  if (abft_check_workspace_bytes(args) > ABFT_NO_ALLOC_SCRATCH_BYTES) return ABFT_ERR_WORKSPACE;
+  abft_check_args c = *args;
+  c.workspace = scratch;
+  c.workspace_bytes = ABFT_NO_ALLOC_SCRATCH_BYTES;
+  return abft_check_only(&c, stream);
+}
+
 }  // extern "C"
