@@ -141,10 +141,11 @@ const char* abft_status_string(int status);
 /* Bytes of a report with `capacity` records. */
 size_t abft_report_bytes(int32_t capacity);
 
-/* Tile width (256 or 128) the library picks for an (M, N) output and mode
- * when tile_n == 0: the one with the fewest waves of tiles over num_sms,
- * weighting a 128-wide tile as 0.55 of a 256-wide one. */
-int32_t abft_pick_tile_n(int64_t M, int64_t N, int32_t num_sms, uint32_t mode);
+/* Tile width (256 or 128) the library picks for an M x N x K GEMM in `mode`
+ * when tile_n == 0: the shorter estimated schedule over num_sms (whole-tile
+ * waves, with stream-K for a last wave that would leave SMs idle), a
+ * 128-wide tile counted as 0.8 of a 256-wide one. */
+int32_t abft_pick_tile_n(int64_t M, int64_t N, int64_t K, int32_t num_sms, uint32_t mode);
 
 /* Bytes of the per-tile checksum block of a [N, K] weight for tile_n. */
 size_t abft_checksum_bytes(int64_t N, int64_t K, int32_t tile_n);

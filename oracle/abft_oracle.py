@@ -179,10 +179,22 @@ def split3_bf16(v: np.ndarray) -> np.ndarray:
     return np.stack([hi, mid, lo])
 
 
-def encode_weight(w: np.ndarray, tile_n: int) -> Tuple[np.ndarray, np.ndarray]:
+def col_signs(n: int) -> np.ndarray:
+    """+1 / -1 by the parity of the set bits of 0..n-1 (Thue-Morse)."""
+    j = np.arange(n)
+    par = np.zeros(n, dtype=np.int64)
+    x = j.copy()
+    while np.any(x):
+        par ^= x & 1
+        x >>= 1
+    return np.where(par == 1, -1.0, 1.0)
+
+
+def encode_weight(w: np.ndarray, tile_n: int) -> Tuple[np.ndarray, np.ndarray, np.ndarray]:
     """Per-tile checksums of a [N, K] weight (float64).
 
-    v1[t, k] = sum_j w[t*tile_n + j, k];  v2[t, k] = sum_j (j+1) w[t*tile_n + j, k]
+    v1[t, k] = sum_j w[t*tile_n + j, k];  v2[t, k] = sum_j (j+1) w[t*tile_n + j, k];
+    v3[t, k] = sum_j sign(j) w[t*tile_n + j, k] (sign: Thue-Morse parity of j)
     over the tile's valid rows j. Row-checksum "Be" of checkers.py:119 per tile.
     """
     w = np.asarray(w, dtype=np.float64)
@@ -190,12 +202,14 @@ def encode_weight(w: np.ndarray, tile_n: int) -> Tuple[np.ndarray, np.ndarray]:
     tiles = -(-n // tile_n)
     v1 = np.zeros((tiles, k))
     v2 = np.zeros((tiles, k))
+    v3 = np.zeros((tiles, k))
     for t in range(tiles):
         blk = w[t * tile_n:(t + 1) * tile_n]
         wt = np.arange(1, blk.shape[0] + 1, dtype=np.float64)
         v1[t] = blk.sum(axis=0)
         v2[t] = wt @ blk
-    return v1, v2
+        v3[t] = col_signs(blk.shape[0]) @ blk
+    return v1, v2, v3
 
 
 @dataclass
@@ -228,9 +242,11 @@ def rowcheck_gemm(
     over the tile's valid columns (local index) and acc = A W^T + injected:
       s1 = sum_j acc[i,j]            e1 = A[i,:] . v1
       s2 = sum_j (j+1) acc[i,j]      e2 = A[i,:] . v2
-      res1 = s1 - e1, res2 = s2 - e2, thr = tau*sqrt(K) * max_j |acc[i,j]| + thr_abs
+      s3 = sum_j sg(j) acc[i,j]      e3 = A[i,:] . v3      (sg = Thue-Morse sign)
+      res_q = s_q - e_q, thr = tau*sqrt(K) * max_j |acc[i,j]| + thr_abs
       detected: |res1| > thr or |res2| > thr * ncols
-      located:  |res1| > thr and p = res2/res1 within 0.1 of an integer in [1, ncols]
+      located:  |res1| > thr, p = res2/res1 within 0.1 of an integer in [1, ncols]
+                and |res3 - sg(p-1) res1| <= res1 / 2
                 -> column p-1; corrected (if enabled) by acc[i, col] -= res1.
     Output = bf16(acc (+ bias)).
     """
@@ -243,7 +259,7 @@ def rowcheck_gemm(
         acc[r, c] += d
     fixed = acc.copy()
     tk = thr_k(thr_scale, k)
-    v1, v2 = encode_weight(w, tile_n)
+    v1, v2, v3 = encode_weight(w, tile_n)
     records: List[Tuple[int, int, int]] = []
     residuals: Dict[Tuple[int, int], Tuple[float, float, float]] = {}
     for t in range(v1.shape[0]):
@@ -251,14 +267,18 @@ def rowcheck_gemm(
         c1 = min(n, c0 + tile_n)
         nc = c1 - c0
         wt = np.arange(1, nc + 1, dtype=np.float64)
+        sg = col_signs(nc)
         seg = acc[:, c0:c1]
         s1 = seg.sum(axis=1)
         s2 = seg @ wt
+        s3 = seg @ sg
         e1 = a @ v1[t]
         e2 = a @ v2[t]
+        e3 = a @ v3[t]
         amax = np.abs(seg).max(axis=1)
         res1 = s1 - e1
         res2 = s2 - e2
+        res3 = s3 - e3
         thr = tk * amax + thr_abs
         det = (np.abs(res1) > thr) | (np.abs(res2) > thr * nc)
         for i in np.nonzero(det)[0]:
@@ -268,8 +288,10 @@ def rowcheck_gemm(
                 pos = res2[i] / res1[i]
                 pr = float(np.rint(pos))
                 if abs(pos - pr) <= 0.1 and 1.0 <= pr <= nc:
-                    col = int(pr) - 1
-                    flags |= REC_LOCATED
+                    c = int(pr) - 1
+                    if abs(res3[i] - sg[c] * res1[i]) <= 0.5 * abs(res1[i]):
+                        col = c
+                        flags |= REC_LOCATED
             if col >= 0 and correct:
                 fixed[i, c0 + col] -= res1[i]
                 flags |= REC_CORRECTED

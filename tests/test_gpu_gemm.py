@@ -39,13 +39,14 @@ def max_rel_err(got, ref):
 def test_encode_weight_matches_oracle(cuda_device, tile_n, n, k):
     _, w, _ = seeded(8, n, k, 1)
     blk = f32(ops.encode_weight(w.to(cuda_device), tile_n)).astype(np.float64)
-    v1, v2 = O.encode_weight(f32(w), tile_n - 8)
+    v1, v2, v3 = O.encode_weight(f32(w), tile_n - 8)
     t = v1.shape[0]
     blk = blk.reshape(t, 8, k)
     tol = 1e-5 * max(1.0, np.abs(v2).max())
     assert np.abs(blk[:, 0] + blk[:, 1] + blk[:, 2] - v1).max() <= 1e-5
     assert np.abs(blk[:, 3] + blk[:, 4] + blk[:, 5] - v2).max() <= tol
-    assert np.all(blk[:, 6:] == 0)
+    # two bf16 terms carry 16 significant bits
+    assert np.abs(blk[:, 6] + blk[:, 7] - v3).max() <= 2.0 ** -15 * max(1.0, np.abs(v3).max())
 
 
 # ------------------------------------------------------------ plain GEMM
@@ -105,6 +106,35 @@ def test_faults_located_and_corrected_bit_exact(cuda_device, tile_n, count, m, n
     assert max_rel_err(f32(c), clean) <= OUT_TOL
 
 
+@pytest.mark.parametrize("m,n,k", [
+    (512, 4096, 4096),    # 68 tiles on 148 SMs: every tile split across ~2 CTAs
+    (512, 3584, 18944),   # long K: 2-3 CTAs per tile
+    (256, 1024, 8192),    # 10 tiles: ~15 CTAs per tile
+    (512, 37888, 3584),   # 4 whole-tile waves, then a stream-K tail of 20 tiles
+])
+@pytest.mark.parametrize("mode", [N.MODE_OFF, N.MODE_DETECT | N.MODE_CORRECT])
+def test_stream_k_schedules(cuda_device, m, n, k, mode):
+    """Shapes whose schedule splits tiles across CTAs: same output as the
+    fp32 GEMM, bit-identical across runs, faults found and corrected."""
+    torch.manual_seed(m * 7 + n + k)
+    a = (torch.randn(m, k, device=cuda_device) * k ** -0.5).bfloat16()
+    w = (torch.randn(n, k, device=cuda_device) * k ** -0.5).bfloat16()
+    ref = a.float() @ w.float().T
+    c1, r1 = ops.abft_gemm(a, w, mode=mode)
+    c2, _ = ops.abft_gemm(a, w, mode=mode)
+    assert torch.equal(c1, c2)
+    assert (c1.float() - ref).abs().max().item() <= OUT_TOL * ref.abs().max().item()
+    if mode == N.MODE_OFF:
+        return
+    assert r1.read().n_faults == 0
+    delta = 256.0 * ref.abs().max().item()
+    faults = O.seeded_fault_positions(m, n, 4, m + k)
+    c3, r3 = ops.abft_gemm(a, w, mode=mode, inject=[(i, j, delta) for i, j in faults])
+    r3 = r3.read()
+    assert r3.coords() == sorted(faults) and r3.n_corrected == 4
+    assert (c3.float() - ref).abs().max().item() <= OUT_TOL * ref.abs().max().item()
+
+
 def test_detect_only_keeps_the_fault(cuda_device):
     m, n, k = 256, 512, 256
     a, w, b, c, r, orc = run_checked(cuda_device, m, n, k, [(17, 300)], mode=N.MODE_DETECT, magnitude=5.0)
@@ -115,9 +145,14 @@ def test_detect_only_keeps_the_fault(cuda_device):
 
 
 def test_two_faults_in_one_row_segment_are_not_miscorrected(cuda_device):
-    a, w, b, c, r, orc = run_checked(cuda_device, 128, 248, 128, [(5, 10), (5, 201)], tile_n=256, magnitude=3.0)
-    assert sorted((x.row, x.col, x.flags) for x in r.records) == orc.records == [(5, -1, N.REC_DETECTED)]
-    assert r.status == N.STATUS_FAULT | N.STATUS_UNLOCATED
+    # (10, 201): mean column not an integer; (40, 42): integer mean 41, rejected
+    # by the sign checksum (no three consecutive columns share a sign)
+    for pair in ([(5, 10), (5, 201)], [(5, 40), (5, 42)], [(9, 0), (9, 2)]):
+        a, w, b, c, r, orc = run_checked(cuda_device, 128, 248, 128, pair, tile_n=256, magnitude=3.0)
+        row = pair[0][0]
+        assert sorted((x.row, x.col, x.flags) for x in r.records) == orc.records == [(row, -1, N.REC_DETECTED)]
+        assert r.status == N.STATUS_FAULT | N.STATUS_UNLOCATED
+        assert r.n_corrected == 0
 
 
 def test_ragged_edges_and_bias(cuda_device):

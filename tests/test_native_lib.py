@@ -40,10 +40,12 @@ def test_host_only_helpers():
     L = N.lib()
     assert L.abft_report_bytes(0) == 64
     assert L.abft_report_bytes(10) == 64 + 10 * 24
-    assert L.abft_pick_tile_n(512, 4096, 148, 3) == 128  # 68 tiles of 128x248: one wave, half-filled
-    assert L.abft_pick_tile_n(8192, 8192, 148, 3) == 256
-    assert L.abft_pick_tile_n(512, 37888, 148, 0) == 256  # 592 tiles: exactly 4 waves
-    assert L.abft_pick_tile_n(512, 37888, 148, 3) == 128  # 612 checked 256-wide tiles spill into a 5th wave
+    assert L.abft_pick_tile_n(512, 4096, 4096, 148, 3) == 256  # 68 wide tiles, stream-K over 148 SMs
+    assert L.abft_pick_tile_n(8192, 8192, 8192, 148, 3) == 256
+    assert L.abft_pick_tile_n(4096, 4096, 4096, 148, 0) == 256  # 4 waves of 256 beat 7 waves of 128
+    assert L.abft_pick_tile_n(512, 37888, 3584, 148, 0) == 256  # 592 tiles: exactly 4 waves
+    assert L.abft_pick_tile_n(512, 37888, 3584, 148, 3) == 256  # 4 waves + a stream-K tail
+    assert L.abft_pick_tile_n(1024, 1024, 64, 148, 0) == 128  # one k-block: nothing to stream
     assert L.abft_checksum_bytes(4096, 4096, 256) == 17 * 8 * 4096 * 2  # ceil(4096/248) tiles
     assert L.abft_checksum_bytes(4096, 4096, 128) == 35 * 8 * 4096 * 2  # ceil(4096/120) tiles
     assert L.abft_checksum_bytes(4096, 4096, 64) == 0

@@ -139,6 +139,28 @@ def test_rowcheck_two_faults_in_one_row_are_unlocated():
     assert r.records == [(5, -1, O.REC_DETECTED)]
 
 
+def test_sign_checksum_rejects_integer_mean_double_faults():
+    a, w, _ = _inputs(64, 248, 64, 8)
+    # adjacent-pair means (c, c+2) are always rejected: no three consecutive
+    # Thue-Morse signs are equal
+    for c in range(0, 240, 7):
+        r = O.rowcheck_gemm(a, w, tile_n=248, inject=[(3, c, 2.0), (3, c + 2, 2.0)])
+        assert r.records == [(3, -1, O.REC_DETECTED)], c
+    # over all equal-magnitude pairs with an integer mean, at most 1/3 slip through
+    slipped = total = 0
+    for c1 in range(0, 64, 3):
+        for c2 in range(c1 + 2, 64, 2):
+            r = O.rowcheck_gemm(a, w, tile_n=248, inject=[(3, c1, 2.0), (3, c2, 2.0)])
+            total += 1
+            slipped += r.records[0][1] >= 0
+    assert slipped <= total // 3
+
+
+def test_col_signs_thue_morse():
+    s = O.col_signs(16)
+    assert list(s) == [1, -1, -1, 1, -1, 1, 1, -1, -1, 1, 1, -1, 1, -1, -1, 1]
+
+
 def test_rowcheck_ragged_last_tile():
     m, n, k = 200, 136, 72
     a, w, b = _inputs(m, n, k, 4, bias=True)

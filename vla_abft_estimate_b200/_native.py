@@ -146,7 +146,7 @@ def lib() -> ctypes.CDLL:
     L.abft_report_bytes.restype = sz
     L.abft_report_bytes.argtypes = [i32]
     L.abft_pick_tile_n.restype = i32
-    L.abft_pick_tile_n.argtypes = [i64, i64, i32, ctypes.c_uint32]
+    L.abft_pick_tile_n.argtypes = [i64, i64, i64, i32, ctypes.c_uint32]
     L.abft_checksum_bytes.restype = sz
     L.abft_checksum_bytes.argtypes = [i64, i64, i32]
     L.abft_encode_weight.restype = ctypes.c_int

@@ -252,7 +252,7 @@ class AbftInjector(AbstractContextManager):
         mode = N.MODE_OFF
         if check:
             mode = N.MODE_DETECT | (0 if self.cfg.detect_only else N.MODE_CORRECT)
-        tile_n = ops.pick_tile_n(m, n, x2.device, mode)
+        tile_n = ops.pick_tile_n(m, n, k, x2.device, mode)
         cks = self.checksums.get(weight, tile_n) if check else None
         inject = [(idx // n, idx % n, float(self.cfg.inject_magnitude))] if injected else None
         rep = ops.ReportBuffer(self.cfg.report_capacity, x2.device) if check else None

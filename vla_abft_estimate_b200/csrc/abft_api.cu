@@ -142,14 +142,55 @@ int rowdot(const void* X, int64_t ld, int64_t R, int64_t C, const float* vec, fl
   return launch_status();
 }
 
+// Tile schedule of one launch. Whole-tile (data-parallel) waves first; when
+// the last wave would leave SMs idle and its tiles carry enough k-blocks,
+// those tiles run stream-K over the full grid instead: every CTA gets an
+// equal share of their k-block iterations, and partial tiles meet in the
+// workspace. Times below are in k-block units.
+// Hand-off cost of a stream-K tile (partial store, flag, reload) in k-blocks.
+constexpr double kStreamKCost = 8.0;
+
+struct Schedule {
+  int grid;
+  int dp_tiles;
+  int sk;
+  int64_t sk_iters;
+};
+
+Schedule make_schedule(int64_t tiles, int num_kb, int sms) {
+  Schedule s;
+  s.sk = 0;
+  s.sk_iters = 0;
+  s.dp_tiles = static_cast<int>(tiles);
+  s.grid = static_cast<int>(tiles < sms ? tiles : sms);
+  const int64_t full = tiles / sms, rem = tiles % sms;
+  if (rem == 0) return s;
+  const int64_t w = rem * num_kb;
+  if (w < 4 * static_cast<int64_t>(sms)) return s;  // too little left to spread
+  const double t_dp = static_cast<double>(full + 1) * num_kb;
+  const double t_sk = static_cast<double>(full) * num_kb + static_cast<double>(w) / sms + kStreamKCost;
+  if (t_sk >= t_dp) return s;
+  s.sk = 1;
+  s.sk_iters = w;
+  s.dp_tiles = static_cast<int>(full * sms);
+  s.grid = sms;
+  return s;
+}
+
+// Estimated duration of a schedule in k-block steps of one CTA.
+double schedule_time(const Schedule& s, int64_t tiles, int num_kb, int sms) {
+  if (!s.sk) return static_cast<double>(cdiv(tiles, sms)) * num_kb;
+  return static_cast<double>(s.dp_tiles / sms) * num_kb + static_cast<double>(s.sk_iters) / sms + kStreamKCost;
+}
+
 struct GemmWs {
-  size_t v_off, pa_off, u_off, pb_off, vf_off, parts_off, total;
+  size_t v_off, pa_off, u_off, pb_off, vf_off, parts_off, sk_part_off, sk_flag_off, total;
 };
 
 void gemm_ws_layout(const abft_gemm_args* a, int bn, int sms, GemmWs* w) {
   const bool check = (a->mode & (ABFT_MODE_DETECT | ABFT_MODE_CORRECT)) != 0;
   size_t off = 0;
-  w->v_off = w->pa_off = w->u_off = w->pb_off = w->vf_off = w->parts_off = 0;
+  w->v_off = w->pa_off = w->u_off = w->pb_off = w->vf_off = w->parts_off = w->sk_part_off = w->sk_flag_off = 0;
   if (check && a->checksums == nullptr) {
     w->v_off = off;
     off = align256(off + abft_checksum_bytes(a->N, a->K, bn));
@@ -167,6 +208,17 @@ void gemm_ws_layout(const abft_gemm_args* a, int bn, int sms, GemmWs* w) {
     off = align256(off + 4 * static_cast<size_t>(a->K));
     w->parts_off = off;
     off = align256(off + 4 * 8 * tiles);
+  }
+  {
+    const int bd = check ? bn - kChkRows : bn;
+    const int64_t tiles = cdiv(a->M, kBM) * cdiv(a->N, bd);
+    const Schedule sch = make_schedule(tiles, static_cast<int>(cdiv(a->K, kBK)), sms);
+    if (sch.sk) {
+      w->sk_part_off = off;
+      off = align256(off + static_cast<size_t>(sch.grid) * kBM * bn * sizeof(float));
+      w->sk_flag_off = off;
+      off = align256(off + static_cast<size_t>(sch.grid) * sizeof(int));
+    }
   }
   w->total = off;
 }
@@ -225,18 +277,18 @@ size_t abft_report_bytes(int32_t capacity) {
   return sizeof(abft_report) + static_cast<size_t>(capacity) * sizeof(abft_fault_record);
 }
 
-int32_t abft_pick_tile_n(int64_t M, int64_t N, int32_t num_sms, uint32_t mode) {
+int32_t abft_pick_tile_n(int64_t M, int64_t N, int64_t K, int32_t num_sms, uint32_t mode) {
   if (num_sms <= 0) num_sms = 148;
-  if (M <= 0 || N <= 0) return 256;
+  if (M <= 0 || N <= 0 || K <= 0) return 256;
   const bool check = (mode & (ABFT_MODE_DETECT | ABFT_MODE_CORRECT)) != 0;
-  // Cost of a launch ~ waves x per-tile time; a 128-wide tile takes about
-  // 0.55 of a 256-wide tile's time (same A stream and epilogue, half the MMA).
+  const int num_kb = static_cast<int>(cdiv(K, kBK));
   double best_cost = 0.0;
   int32_t best = 256;
   for (int32_t bn : {256, 128}) {
     const int64_t d = check ? bn - kChkRows : bn;
     const int64_t tiles = cdiv(M, kBM) * cdiv(N, d);
-    const double cost = static_cast<double>(cdiv(tiles, num_sms)) * (bn == 256 ? 1.0 : 0.55);
+    const double cost = schedule_time(make_schedule(tiles, num_kb, num_sms), tiles, num_kb, num_sms) *
+                        (bn == 256 ? 1.0 : 0.8);
     if (bn == 256 || cost < best_cost) {
       best_cost = cost;
       best = bn;
@@ -275,7 +327,7 @@ size_t abft_gemm_workspace_bytes(const abft_gemm_args* args) {
   int sms = 148;
   if (current_device(&dev, &info) == ABFT_OK) sms = info.sms;
   if (args->num_sms > 0 && args->num_sms < sms) sms = args->num_sms;
-  const int bn = args->tile_n ? args->tile_n : abft_pick_tile_n(args->M, args->N, sms, args->mode);
+  const int bn = args->tile_n ? args->tile_n : abft_pick_tile_n(args->M, args->N, args->K, sms, args->mode);
   GemmWs w;
   gemm_ws_layout(args, bn, sms, &w);
   return w.total;
@@ -297,7 +349,7 @@ int abft_gemm_bf16(const abft_gemm_args* a, void* stream) {
 
   int sms = info.sms;
   if (a->num_sms > 0 && a->num_sms < sms) sms = a->num_sms;
-  const int bn = a->tile_n ? a->tile_n : abft_pick_tile_n(a->M, a->N, sms, a->mode);
+  const int bn = a->tile_n ? a->tile_n : abft_pick_tile_n(a->M, a->N, a->K, sms, a->mode);
   const bool check = (a->mode & (ABFT_MODE_DETECT | ABFT_MODE_CORRECT)) != 0;
   GemmWs ws;
   gemm_ws_layout(a, bn, sms, &ws);
@@ -349,7 +401,19 @@ int abft_gemm_bf16(const abft_gemm_args* a, void* stream) {
   p.capacity = a->report_capacity;
   p.tile_sumc = (a->mode & ABFT_MODE_REF) ? reinterpret_cast<float*>(wsb + ws.parts_off) : nullptr;
 
-  const int grid = p.num_tiles < sms ? p.num_tiles : sms;
+  const Schedule sch = make_schedule(p.num_tiles, p.num_kb, sms);
+  const int grid = sch.grid;
+  p.dp_tiles = sch.dp_tiles;
+  p.sk = sch.sk;
+  p.sk_iters = sch.sk_iters;
+  p.partials = nullptr;
+  p.flags = nullptr;
+  if (sch.sk) {
+    p.partials = reinterpret_cast<float*>(wsb + ws.sk_part_off);
+    p.flags = reinterpret_cast<int*>(wsb + ws.sk_flag_off);
+    if (cudaMemsetAsync(p.flags, 0, static_cast<size_t>(grid) * sizeof(int), s) != cudaSuccess)
+      return launch_status(), ABFT_ERR_CUDA;
+  }
   if (bn == 256)
     rc = check ? launch_gemm<256, true>(dev, 0, tmA, tmB, tmV, p, grid, s)
                : launch_gemm<256, false>(dev, 1, tmA, tmB, tmV, p, grid, s);

@@ -43,22 +43,28 @@ __device__ __forceinline__ void split3_bf16(float v, __nv_bfloat16& hi, __nv_bfl
   lo = __float2bfloat16_rn(r2);
 }
 
+// Sign of local column j in the third checksum: +1 when j has an even number
+// of set bits, -1 otherwise (the Thue-Morse sequence; no three consecutive
+// columns share a sign).
+__host__ __device__ __forceinline__ float col_sign(int j) { return (__builtin_popcount(j) & 1) ? -1.f : 1.f; }
+
 // Per-tile checksum block of B[N, K]: the 8 rows the fused GEMM appends to
 // each B-operand tile of bd data rows.
 // out is bf16 [tiles_n * 8, K] row-major; rows of tile t:
-//   8t+0..2 = split3(v1), 8t+3..5 = split3(v2), 8t+6..7 = 0, with
-//   v1[k] = sum_j B[t*bd + j, k],  v2[k] = sum_j (j+1) B[t*bd + j, k]
+//   8t+0..2 = split3(v1), 8t+3..5 = split3(v2), 8t+6..7 = split2(v3), with
+//   v1[k] = sum_j B[t*bd + j, k],  v2[k] = sum_j (j+1) B[t*bd + j, k],
+//   v3[k] = sum_j col_sign(j) B[t*bd + j, k]
 // (j over the tile's valid rows; fp32 sums in a fixed order).
 // grid (ceil(K/64), tiles_n), 256 threads. K % 8 == 0.
 __global__ void __launch_bounds__(256) encode_weight_kernel(const __nv_bfloat16* __restrict__ B, int64_t ldb, int N,
                                                             int K, int bd, __nv_bfloat16* __restrict__ out) {
-  __shared__ float red[2][32][65];
+  __shared__ float red[3][32][65];
   const int kb = blockIdx.x, nt = blockIdx.y;
   const int t = threadIdx.x, c8 = t & 7, rg = t >> 3;
   const int k0 = kb * 64 + c8 * 8;
-  float s1[8], s2[8];
+  float s1[8], s2[8], s3[8];
 #pragma unroll
-  for (int e = 0; e < 8; ++e) s1[e] = s2[e] = 0.f;
+  for (int e = 0; e < 8; ++e) s1[e] = s2[e] = s3[e] = 0.f;
   if (k0 < K) {
     for (int j = rg; j < bd; j += 32) {
       const int gj = nt * bd + j;
@@ -67,10 +73,12 @@ __global__ void __launch_bounds__(256) encode_weight_kernel(const __nv_bfloat16*
       float x[8];
       unpack8(w, x);
       const float wt = static_cast<float>(j + 1);
+      const float sg = col_sign(j);
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         s1[e] += x[e];
         s2[e] = fmaf(wt, x[e], s2[e]);
+        s3[e] = fmaf(sg, x[e], s3[e]);
       }
     }
   }
@@ -78,20 +86,23 @@ __global__ void __launch_bounds__(256) encode_weight_kernel(const __nv_bfloat16*
   for (int e = 0; e < 8; ++e) {
     red[0][rg][c8 * 8 + e] = s1[e];
     red[1][rg][c8 * 8 + e] = s2[e];
+    red[2][rg][c8 * 8 + e] = s3[e];
   }
   __syncthreads();
   if (t < 64) {
     const int col = kb * 64 + t;
     if (col < K) {
-      float a1 = 0.f, a2 = 0.f;
+      float a1 = 0.f, a2 = 0.f, a3 = 0.f;
       for (int g = 0; g < 32; ++g) {
         a1 += red[0][g][t];
         a2 += red[1][g][t];
+        a3 += red[2][g][t];
       }
       __nv_bfloat16 h[8];
       split3_bf16(a1, h[0], h[1], h[2]);
       split3_bf16(a2, h[3], h[4], h[5]);
-      h[6] = h[7] = __float2bfloat16_rn(0.f);
+      h[6] = __float2bfloat16_rn(a3);
+      h[7] = __float2bfloat16_rn(a3 - __bfloat162float(h[6]));
       __nv_bfloat16* o = out + static_cast<int64_t>(nt) * 8 * K + col;
 #pragma unroll
       for (int q = 0; q < 8; ++q) o[static_cast<int64_t>(q) * K] = h[q];

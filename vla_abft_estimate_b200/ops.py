@@ -65,11 +65,11 @@ class ReportBuffer:
         pinned.copy_(self.tensor[: N.REPORT_HEADER_BYTES], non_blocking=True)
 
 
-def pick_tile_n(m: int, n: int, device: Optional[torch.device] = None,
+def pick_tile_n(m: int, n: int, k: int, device: Optional[torch.device] = None,
                 mode: int = N.MODE_DETECT | N.MODE_CORRECT) -> int:
-    """Tile width the library would pick for an [m, n] output in ``mode``."""
+    """Tile width the library would pick for an m x n x k GEMM in ``mode``."""
     sms = torch.cuda.get_device_properties(device or torch.device("cuda")).multi_processor_count
-    return int(N.lib().abft_pick_tile_n(int(m), int(n), int(sms), int(mode)))
+    return int(N.lib().abft_pick_tile_n(int(m), int(n), int(k), int(sms), int(mode)))
 
 
 def encode_weight(weight: torch.Tensor, tile_n: int) -> torch.Tensor:

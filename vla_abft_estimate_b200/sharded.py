@@ -114,7 +114,7 @@ class ShardedAbftGemm:
             self.col_offsets = [int(x) for x in all_offs.cpu()]
 
     def _checksums_for(self, m: int) -> Tuple[int, Optional[torch.Tensor]]:
-        tile_n = self.tile_n or ops.pick_tile_n(m, self.weight.shape[0], self.device, self.mode)
+        tile_n = self.tile_n or ops.pick_tile_n(m, self.weight.shape[0], self.weight.shape[1], self.device, self.mode)
         if self.mode & (N.MODE_DETECT | N.MODE_CORRECT):
             if self.checksums is None or self.checksums[0] != tile_n:
                 self.checksums = (tile_n, ops.encode_weight(self.weight, tile_n))
