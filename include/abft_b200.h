@@ -130,6 +130,10 @@ typedef struct abft_gemm_args {
   void* report;           /* abft_report + records, or NULL when mode == OFF  */
   int32_t report_capacity;
   int32_t num_sms;        /* 0 = all SMs of the current device                */
+  int32_t tile_m;         /* 0 = choose; 128; or 256: each tile is shared by  */
+                          /* a 2-CTA cluster (one pair MMA, M = 256), which    */
+                          /* needs tile_n 256                                 */
+  int32_t reserved0;      /* set to 0                                         */
 } abft_gemm_args;
 
 #define ABFT_MAX_INJECT 64
@@ -146,6 +150,11 @@ size_t abft_report_bytes(int32_t capacity);
  * waves, with stream-K for a last wave that would leave SMs idle), a
  * 128-wide tile counted as 0.8 of a 256-wide one. */
 int32_t abft_pick_tile_n(int64_t M, int64_t N, int64_t K, int32_t num_sms, uint32_t mode);
+
+/* Tile height (128, or 256 = CTA pairs) the library picks when tile_m == 0,
+ * for a given tile_n: the shorter estimated schedule, pairs over num_sms / 2
+ * units at a per-SM speed-up of 1.1 (128 whenever tile_n != 256). */
+int32_t abft_pick_tile_m(int64_t M, int64_t N, int64_t K, int32_t num_sms, uint32_t mode, int32_t tile_n);
 
 /* Bytes of the per-tile checksum block of a [N, K] weight for tile_n. */
 size_t abft_checksum_bytes(int64_t N, int64_t K, int32_t tile_n);

@@ -65,14 +65,14 @@ def test_plain_gemm_matches_fp32(cuda_device, m, n, k, tile_n, bias):
 
 
 # ---------------------------------------------------- checked GEMM parity
-def run_checked(device, m, n, k, faults, *, tile_n=0, bias=False, mode=N.MODE_DETECT | N.MODE_CORRECT, seed=3,
-                magnitude=None):
+def run_checked(device, m, n, k, faults, *, tile_n=0, tile_m=0, bias=False, mode=N.MODE_DETECT | N.MODE_CORRECT,
+                seed=3, magnitude=None):
     a, w, b = seeded(m, n, k, seed, bias)
     acc = f32(a).astype(np.float64) @ f32(w).astype(np.float64).T
     delta = 256.0 * np.abs(acc).max() if magnitude is None else magnitude
     inj = [(r, c, float(delta)) for (r, c) in faults]
     c, rep = ops.abft_gemm(a.to(device), w.to(device), None if b is None else b.to(device), mode=mode,
-                           tile_n=tile_n, inject=inj or None)
+                           tile_n=tile_n, tile_m=tile_m, inject=inj or None)
     r = rep.read()
     orc = O.rowcheck_gemm(f32(a), f32(w), None if b is None else f32(b), tile_n=r.tile_n, inject=inj,
                           correct=bool(mode & N.MODE_CORRECT))
@@ -87,7 +87,7 @@ def test_clean_inputs_have_no_records(cuda_device, tile_n, m, n, k, bias):
     assert r.status == 0 and r.n_faults == 0 and r.records == [] and orc.records == []
     ref = f32(a) @ f32(w).T + (f32(b) if b is not None else 0)
     assert max_rel_err(f32(c), ref) <= OUT_TOL
-    assert r.tile_m == 128 and r.tile_n in (120, 248)
+    assert r.tile_m in (128, 256) and r.tile_n in (120, 248)
 
 
 @pytest.mark.parametrize("tile_n", [128, 256])
@@ -275,3 +275,79 @@ def test_no_device_timeouts_reported(cuda_device):
     a, w, _ = seeded(512, 1024, 512, 9)
     _, rep = ops.abft_gemm(a.to(cuda_device), w.to(cuda_device), mode=N.MODE_DETECT | N.MODE_REF)
     assert not rep.read().device_timeout
+
+
+# ------------------------------------------------ 2-CTA pairs (256-row tiles)
+@pytest.mark.parametrize("m,n,k,bias", [
+    (256, 256, 64, False), (200, 136, 72, True), (300, 1000, 520, True), (1024, 1024, 1024, False),
+    (1, 8, 8, False), (2048, 2048, 4096, True),
+])
+@pytest.mark.parametrize("mode", [N.MODE_OFF, N.MODE_DETECT | N.MODE_CORRECT])
+def test_pair_tiles_match_fp32(cuda_device, m, n, k, bias, mode):
+    a, w, b = seeded(m, n, k, 12, bias)
+    ref = f32(a) @ f32(w).T + (f32(b) if b is not None else 0)
+    c, rep = ops.abft_gemm(a.to(cuda_device), w.to(cuda_device), None if b is None else b.to(cuda_device),
+                           mode=mode, tile_n=256, tile_m=256)
+    assert max_rel_err(f32(c), ref) <= OUT_TOL
+    if mode != N.MODE_OFF:
+        r = rep.read()
+        assert r.status == 0 and r.n_faults == 0 and r.tile_m == 256 and r.tile_n == 248
+
+
+@pytest.mark.parametrize("count", [1, 4])
+@pytest.mark.parametrize("m,n,k", [(256, 512, 256), (512, 4096, 1024), (1024, 1024, 1024), (300, 1000, 520)])
+def test_pair_faults_located_and_corrected_bit_exact(cuda_device, count, m, n, k):
+    faults = O.seeded_fault_positions(m, n, count, 13 * count + m)
+    a, w, b, c, r, orc = run_checked(cuda_device, m, n, k, faults, tile_n=256, tile_m=256)
+    got = sorted((x.row, x.col, x.flags) for x in r.records)
+    assert got == orc.records
+    assert r.n_faults == r.n_located == r.n_corrected == count
+    assert max_rel_err(f32(c), orc.out) <= OUT_TOL
+    assert max_rel_err(f32(c), f32(a) @ f32(w).T) <= OUT_TOL
+
+
+@pytest.mark.parametrize("m,n,k", [
+    (512, 4096, 4096),    # 34 pair tiles on 74 pairs: stream-K only
+    (256, 1024, 8192),    # 5 tiles: many pairs per tile
+    (512, 37888, 3584),   # 306 tiles: whole-tile waves, then a stream-K tail
+    (4096, 4096, 4096),
+])
+@pytest.mark.parametrize("mode", [N.MODE_OFF, N.MODE_DETECT | N.MODE_CORRECT])
+def test_pair_stream_k_schedules(cuda_device, m, n, k, mode):
+    torch.manual_seed(m * 5 + n + k)
+    a = (torch.randn(m, k, device=cuda_device) * k ** -0.5).bfloat16()
+    w = (torch.randn(n, k, device=cuda_device) * k ** -0.5).bfloat16()
+    ref = a.float() @ w.float().T
+    c1, r1 = ops.abft_gemm(a, w, mode=mode, tile_n=256, tile_m=256)
+    c2, _ = ops.abft_gemm(a, w, mode=mode, tile_n=256, tile_m=256)
+    assert torch.equal(c1, c2)
+    assert (c1.float() - ref).abs().max().item() <= OUT_TOL * ref.abs().max().item()
+    if mode == N.MODE_OFF:
+        return
+    r1 = r1.read()
+    assert r1.n_faults == 0 and not r1.device_timeout
+    delta = 256.0 * ref.abs().max().item()
+    faults = O.seeded_fault_positions(m, n, 4, m + k + 1)
+    c3, r3 = ops.abft_gemm(a, w, mode=mode, tile_n=256, tile_m=256, inject=[(i, j, delta) for i, j in faults])
+    r3 = r3.read()
+    assert r3.coords() == sorted(faults) and r3.n_corrected == 4
+    assert (c3.float() - ref).abs().max().item() <= OUT_TOL * ref.abs().max().item()
+
+
+@pytest.mark.parametrize("fault", [None, 1.0])
+def test_pair_ref_mode_matches_oracle(cuda_device, fault):
+    m, n, k = 384, 512, 256
+    a, w, b = seeded(m, n, k, 14, True)
+    inj = [(300, 4, fault)] if fault else None
+    c, rep = ops.abft_gemm(a.to(cuda_device), w.to(cuda_device), b.to(cuda_device), mode=N.MODE_REF, inject=inj,
+                           tile_n=256, tile_m=256)
+    r = rep.read()
+    o = O.cheap_sum_check(f32(a), f32(w).T, f32(c), f32(b))
+    assert (r.ref_ok == 1) == o.ok
+    assert abs(r.sum_c - o.sum_c) <= 1e-4 * max(1.0, abs(o.sum_c))
+
+
+def test_pair_needs_256_wide_tiles(cuda_device):
+    a, w, _ = seeded(256, 256, 64, 15)
+    with pytest.raises(N.AbftError):
+        ops.abft_gemm(a.to(cuda_device), w.to(cuda_device), tile_n=128, tile_m=256)

@@ -43,6 +43,7 @@ EXPORTED_SYMBOLS = (
     "abft_status_string",
     "abft_report_bytes",
     "abft_pick_tile_n",
+    "abft_pick_tile_m",
     "abft_checksum_bytes",
     "abft_encode_weight",
     "abft_gemm_workspace_bytes",
@@ -94,6 +95,8 @@ class GemmArgs(ctypes.Structure):
         ("report", ctypes.c_void_p),
         ("report_capacity", ctypes.c_int32),
         ("num_sms", ctypes.c_int32),
+        ("tile_m", ctypes.c_int32),
+        ("reserved0", ctypes.c_int32),
     ]
 
 
@@ -147,6 +150,8 @@ def lib() -> ctypes.CDLL:
     L.abft_report_bytes.argtypes = [i32]
     L.abft_pick_tile_n.restype = i32
     L.abft_pick_tile_n.argtypes = [i64, i64, i64, i32, ctypes.c_uint32]
+    L.abft_pick_tile_m.restype = i32
+    L.abft_pick_tile_m.argtypes = [i64, i64, i64, i32, ctypes.c_uint32, i32]
     L.abft_checksum_bytes.restype = sz
     L.abft_checksum_bytes.argtypes = [i64, i64, i32]
     L.abft_encode_weight.restype = ctypes.c_int

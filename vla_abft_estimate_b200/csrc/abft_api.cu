@@ -38,7 +38,8 @@ struct DeviceInfo {
   bool init;
   bool ok;
   int sms;
-  bool attr_set[4];
+  bool attr_set[6];
+  int pair_clusters[2];  // co-resident 2-CTA clusters of the pair kernels [check], 0 = not asked yet
 };
 DeviceInfo g_dev[kMaxDevices];
 std::mutex g_mu;
@@ -67,17 +68,60 @@ int current_device(int* dev_out, DeviceInfo* info) {
   return ABFT_OK;
 }
 
-template <int BN, bool CHECK>
-int ensure_smem_attr(int dev, int slot) {
-  std::lock_guard<std::mutex> lk(g_mu);
+template <int BN, bool CHECK, bool PAIR>
+int ensure_smem_attr_locked(int dev, int slot) {
   if (g_dev[dev].attr_set[slot]) return ABFT_OK;
-  if (cudaFuncSetAttribute(abft_gemm_kernel<BN, CHECK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           GemmCfg<BN, CHECK>::kSmemBytes) != cudaSuccess) {
+  if (cudaFuncSetAttribute(abft_gemm_kernel<BN, CHECK, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           GemmCfg<BN, CHECK, PAIR>::kSmemBytes) != cudaSuccess) {
     cudaGetLastError();
     return ABFT_ERR_CUDA;
   }
   g_dev[dev].attr_set[slot] = true;
   return ABFT_OK;
+}
+
+template <int BN, bool CHECK, bool PAIR>
+int ensure_smem_attr(int dev, int slot) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  return ensure_smem_attr_locked<BN, CHECK, PAIR>(dev, slot);
+}
+
+constexpr int kPairSlot[2] = {5, 4};  // attr_set slots of the pair kernels [check]
+
+cudaLaunchAttribute pair_cluster_attr() {
+  cudaLaunchAttribute at;
+  at.id = cudaLaunchAttributeClusterDimension;
+  at.val.clusterDim.x = 2;
+  at.val.clusterDim.y = 1;
+  at.val.clusterDim.z = 1;
+  return at;
+}
+
+// How many 2-CTA clusters of the pair kernel can be resident at once on
+// device `dev` (every unit of a persistent launch must be resident: stream-K
+// finishers wait for later units). Falls back to sms / 2 if the query fails.
+template <bool CHECK>
+int pair_units_on(int dev, int sms) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (d.pair_clusters[CHECK] == 0) {
+    int n = 0;
+    if (ensure_smem_attr_locked<256, CHECK, true>(dev, kPairSlot[CHECK]) == ABFT_OK) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2 * static_cast<unsigned>(sms / 2));
+      cfg.blockDim = dim3(kThreads);
+      cfg.dynamicSmemBytes = GemmCfg<256, CHECK, true>::kSmemBytes;
+      cudaLaunchAttribute at = pair_cluster_attr();
+      cfg.attrs = &at;
+      cfg.numAttrs = 1;
+      if (cudaOccupancyMaxActiveClusters(&n, abft_gemm_kernel<256, CHECK, true>, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+      }
+    }
+    d.pair_clusters[CHECK] = n > 0 ? n : sms / 2;
+  }
+  return d.pair_clusters[CHECK] < sms / 2 ? d.pair_clusters[CHECK] : sms / 2;
 }
 
 int make_tmap_kmajor(CUtensorMap* m, const void* ptr, int64_t inner, int64_t outer, int64_t ld, int box_outer) {
@@ -143,84 +187,131 @@ int rowdot(const void* X, int64_t ld, int64_t R, int64_t C, const float* vec, fl
 }
 
 // Tile schedule of one launch. Whole-tile (data-parallel) waves first; when
-// the last wave would leave SMs idle and its tiles carry enough k-blocks,
-// those tiles run stream-K over the full grid instead: every CTA gets an
-// equal share of their k-block iterations, and partial tiles meet in the
-// workspace. Times below are in k-block units.
-// Hand-off cost of a stream-K tile (partial store, flag, reload) in k-blocks.
-constexpr double kStreamKCost = 8.0;
+// the last wave would leave SMs idle, its tiles may instead run stream-K
+// over the first sk_ctas CTAs: each gets an equal share of the tail's k-block
+// iterations, and partial tiles meet in the workspace. More CTAs shorten the
+// tail but cut each tile into more pieces, and every extra piece costs the
+// finisher one partial fold. Estimated times, in k-block steps of one CTA:
+//   data-parallel tail   (full + 1) * num_kb
+//   stream-K over G CTAs full * num_kb + ceil(W / G) + kSkStore + kSkFold * (pieces - 1)
+// with W = rem * num_kb and pieces the most CTA ranges one tile can meet.
+constexpr double kSkStore = 4.0;  // contributor: partial tile to global memory, flag
+constexpr double kSkFold = 3.0;   // finisher: fold one partial tile into TMEM
 
 struct Schedule {
   int grid;
   int dp_tiles;
   int sk;
+  int sk_ctas;
   int64_t sk_iters;
+  double est;  // estimated duration in k-block steps
 };
 
 Schedule make_schedule(int64_t tiles, int num_kb, int sms) {
   Schedule s;
   s.sk = 0;
+  s.sk_ctas = 0;
   s.sk_iters = 0;
   s.dp_tiles = static_cast<int>(tiles);
   s.grid = static_cast<int>(tiles < sms ? tiles : sms);
+  s.est = static_cast<double>(cdiv(tiles, sms)) * num_kb;
   const int64_t full = tiles / sms, rem = tiles % sms;
-  if (rem == 0) return s;
+  if (rem == 0 || num_kb < 2) return s;
   const int64_t w = rem * num_kb;
-  if (w < 4 * static_cast<int64_t>(sms)) return s;  // too little left to spread
-  const double t_dp = static_cast<double>(full + 1) * num_kb;
-  const double t_sk = static_cast<double>(full) * num_kb + static_cast<double>(w) / sms + kStreamKCost;
-  if (t_sk >= t_dp) return s;
+  int64_t best_g = 0;
+  for (int64_t g = rem + 1; g <= sms && g <= w; ++g) {
+    const int64_t lmin = w / g;  // shortest CTA range
+    const int64_t pieces = cdiv(num_kb - 1, lmin) + 1;
+    const double t = static_cast<double>(full * num_kb + cdiv(w, g)) + kSkStore + kSkFold * (pieces - 1);
+    if (t < s.est) {
+      s.est = t;
+      best_g = g;
+    }
+  }
+  if (best_g == 0) return s;
   s.sk = 1;
+  s.sk_ctas = static_cast<int>(best_g);
   s.sk_iters = w;
   s.dp_tiles = static_cast<int>(full * sms);
-  s.grid = sms;
+  s.grid = full > 0 ? sms : static_cast<int>(best_g);
   return s;
 }
 
-// Estimated duration of a schedule in k-block steps of one CTA.
-double schedule_time(const Schedule& s, int64_t tiles, int num_kb, int sms) {
-  if (!s.sk) return static_cast<double>(cdiv(tiles, sms)) * num_kb;
-  return static_cast<double>(s.dp_tiles / sms) * num_kb + static_cast<double>(s.sk_iters) / sms + kStreamKCost;
+// A CTA pair runs a 128 x 256 share of a tile per SM about this much faster
+// than a single CTA (each CTA stages half the B-operand tile per k-block).
+constexpr double kPairSpeedup = 1.10;
+
+// Estimated time (single-CTA k-block steps) of an M x N x K launch with
+// 128- or 256-row tiles (256: CTA pairs over `units` pairs).
+double est_time(int64_t M, int64_t N, int64_t K, int bd, int tile_m, int units) {
+  const int64_t tiles = cdiv(M, tile_m) * cdiv(N, bd);
+  const double t = make_schedule(tiles, static_cast<int>(cdiv(K, kBK)), units).est;
+  return tile_m == 256 ? t / kPairSpeedup : t;
 }
 
-struct GemmWs {
+int pick_tile_m(int64_t M, int64_t N, int64_t K, int sms, uint32_t mode, int bn) {
+  if (bn != 256 || sms < 2 || M <= 0 || N <= 0 || K <= 0) return 128;
+  const bool check = (mode & (ABFT_MODE_DETECT | ABFT_MODE_CORRECT)) != 0;
+  const int bd = check ? bn - kChkRows : bn;
+  return est_time(M, N, K, bd, 256, sms / 2) < est_time(M, N, K, bd, 128, sms) ? 256 : 128;
+}
+
+// Everything about a launch that depends only on the arguments and the
+// device: tile shape, unit count, schedule and workspace layout.
+struct Plan {
+  bool check, pair;
+  int bn, bd, tile_m, units, grid, num_kb;
+  int64_t tiles;
+  Schedule sch;
   size_t v_off, pa_off, u_off, pb_off, vf_off, parts_off, sk_part_off, sk_flag_off, total;
 };
 
-void gemm_ws_layout(const abft_gemm_args* a, int bn, int sms, GemmWs* w) {
-  const bool check = (a->mode & (ABFT_MODE_DETECT | ABFT_MODE_CORRECT)) != 0;
+// dev < 0: no device to ask (co-resident pairs assumed sms / 2).
+int make_plan(const abft_gemm_args* a, int dev, int sms, Plan* pl) {
+  pl->check = (a->mode & (ABFT_MODE_DETECT | ABFT_MODE_CORRECT)) != 0;
+  pl->bn = a->tile_n ? a->tile_n : abft_pick_tile_n(a->M, a->N, a->K, sms, a->mode);
+  pl->tile_m = a->tile_m ? a->tile_m : pick_tile_m(a->M, a->N, a->K, sms, a->mode, pl->bn);
+  if (pl->tile_m != 128 && pl->tile_m != 256) return ABFT_ERR_UNSUPPORTED;
+  if (pl->tile_m == 256 && (pl->bn != 256 || sms < 2)) return ABFT_ERR_UNSUPPORTED;
+  pl->pair = pl->tile_m == 256;
+  pl->bd = pl->check ? pl->bn - kChkRows : pl->bn;
+  pl->num_kb = static_cast<int>(cdiv(a->K, kBK));
+  pl->tiles = cdiv(a->M, pl->tile_m) * cdiv(a->N, pl->bd);
+  if (!pl->pair)
+    pl->units = sms;
+  else if (dev < 0)
+    pl->units = sms / 2;
+  else
+    pl->units = pl->check ? pair_units_on<true>(dev, sms) : pair_units_on<false>(dev, sms);
+  pl->sch = make_schedule(pl->tiles, pl->num_kb, pl->units);
+  pl->grid = pl->sch.grid * (pl->pair ? 2 : 1);
+
   size_t off = 0;
-  w->v_off = w->pa_off = w->u_off = w->pb_off = w->vf_off = w->parts_off = w->sk_part_off = w->sk_flag_off = 0;
-  if (check && a->checksums == nullptr) {
-    w->v_off = off;
-    off = align256(off + abft_checksum_bytes(a->N, a->K, bn));
+  pl->v_off = pl->pa_off = pl->u_off = pl->pb_off = pl->vf_off = pl->parts_off = pl->sk_part_off = pl->sk_flag_off = 0;
+  if (pl->check && a->checksums == nullptr) {
+    pl->v_off = off;
+    off = align256(off + abft_checksum_bytes(a->N, a->K, pl->bn));
   }
   if (a->mode & ABFT_MODE_REF) {
-    const int bd = check ? bn - kChkRows : bn;
-    const size_t tiles = static_cast<size_t>(cdiv(a->M, kBM) * cdiv(a->N, bd));
-    w->pa_off = off;
+    pl->pa_off = off;
     off = align256(off + 4 * colsum_partial_floats(a->M, a->K, sms, false));
-    w->u_off = off;
+    pl->u_off = off;
     off = align256(off + 4 * static_cast<size_t>(a->K));
-    w->pb_off = off;
+    pl->pb_off = off;
     off = align256(off + 4 * colsum_partial_floats(a->N, a->K, sms, false));
-    w->vf_off = off;
+    pl->vf_off = off;
     off = align256(off + 4 * static_cast<size_t>(a->K));
-    w->parts_off = off;
-    off = align256(off + 4 * 8 * tiles);
+    pl->parts_off = off;  // 8 partial sums per 128-row slab of a tile
+    off = align256(off + 4 * 8 * static_cast<size_t>(pl->tiles) * (pl->pair ? 2 : 1));
   }
-  {
-    const int bd = check ? bn - kChkRows : bn;
-    const int64_t tiles = cdiv(a->M, kBM) * cdiv(a->N, bd);
-    const Schedule sch = make_schedule(tiles, static_cast<int>(cdiv(a->K, kBK)), sms);
-    if (sch.sk) {
-      w->sk_part_off = off;
-      off = align256(off + static_cast<size_t>(sch.grid) * kBM * bn * sizeof(float));
-      w->sk_flag_off = off;
-      off = align256(off + static_cast<size_t>(sch.grid) * sizeof(int));
-    }
+  if (pl->sch.sk) {
+    pl->sk_part_off = off;
+    off = align256(off + static_cast<size_t>(pl->grid) * kBM * pl->bn * sizeof(float));
+    pl->sk_flag_off = off;
+    off = align256(off + static_cast<size_t>(pl->grid) * sizeof(int));
   }
-  w->total = off;
+  pl->total = off;
+  return ABFT_OK;
 }
 
 int validate_gemm(const abft_gemm_args* a) {
@@ -233,6 +324,8 @@ int validate_gemm(const abft_gemm_args* a) {
   if (a->bias != nullptr && !aligned16(a->bias)) return ABFT_ERR_ALIGNMENT;
   if (a->mode & ~(ABFT_MODE_DETECT | ABFT_MODE_CORRECT | ABFT_MODE_REF | ABFT_MODE_REF_BF16)) return ABFT_ERR_INVALID_ARG;
   if (a->tile_n != 0 && a->tile_n != 128 && a->tile_n != 256) return ABFT_ERR_UNSUPPORTED;
+  if (a->tile_m != 0 && a->tile_m != 128 && a->tile_m != 256) return ABFT_ERR_UNSUPPORTED;
+  if (a->tile_m == 256 && a->tile_n == 128) return ABFT_ERR_UNSUPPORTED;
   if (a->mode != ABFT_MODE_OFF && (a->report == nullptr || a->report_capacity < 0)) return ABFT_ERR_INVALID_ARG;
   if (a->report != nullptr && !aligned16(a->report)) return ABFT_ERR_ALIGNMENT;
   if (a->n_inject < 0 || a->n_inject > ABFT_MAX_INJECT) return ABFT_ERR_INVALID_ARG;
@@ -243,12 +336,26 @@ int validate_gemm(const abft_gemm_args* a) {
   return ABFT_OK;
 }
 
-template <int BN, bool CHECK>
-int launch_gemm(int dev, int slot, const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmV,
-                const GemmParams& p, int grid, cudaStream_t s) {
-  int rc = ensure_smem_attr<BN, CHECK>(dev, slot);
+template <int BN, bool CHECK, bool PAIR>
+int launch_gemm(int dev, int slot, const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmB2,
+                const CUtensorMap& tmV, const GemmParams& p, int grid, cudaStream_t s) {
+  int rc = ensure_smem_attr<BN, CHECK, PAIR>(dev, slot);
   if (rc != ABFT_OK) return rc;
-  abft_gemm_kernel<BN, CHECK><<<grid, kThreads, GemmCfg<BN, CHECK>::kSmemBytes, s>>>(tmA, tmB, tmV, p);
+  constexpr size_t smem = GemmCfg<BN, CHECK, PAIR>::kSmemBytes;
+  if constexpr (!PAIR) {
+    abft_gemm_kernel<BN, CHECK, false><<<grid, kThreads, smem, s>>>(tmA, tmB, tmB2, tmV, p);
+  } else {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at = pair_cluster_attr();
+    cfg.attrs = &at;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, abft_gemm_kernel<BN, CHECK, true>, tmA, tmB, tmB2, tmV, p) != cudaSuccess)
+      return launch_status(), ABFT_ERR_CUDA;
+  }
   return launch_status();
 }
 
@@ -287,8 +394,11 @@ int32_t abft_pick_tile_n(int64_t M, int64_t N, int64_t K, int32_t num_sms, uint3
   for (int32_t bn : {256, 128}) {
     const int64_t d = check ? bn - kChkRows : bn;
     const int64_t tiles = cdiv(M, kBM) * cdiv(N, d);
-    const double cost = schedule_time(make_schedule(tiles, num_kb, num_sms), tiles, num_kb, num_sms) *
-                        (bn == 256 ? 1.0 : 0.8);
+    double cost = make_schedule(tiles, num_kb, num_sms).est * (bn == 256 ? 1.0 : 0.8);
+    if (bn == 256 && num_sms >= 2) {
+      const double tp = est_time(M, N, K, static_cast<int>(d), 256, num_sms / 2);
+      if (tp < cost) cost = tp;
+    }
     if (bn == 256 || cost < best_cost) {
       best_cost = cost;
       best = bn;
@@ -325,12 +435,17 @@ size_t abft_gemm_workspace_bytes(const abft_gemm_args* args) {
   int dev;
   DeviceInfo info;
   int sms = 148;
-  if (current_device(&dev, &info) == ABFT_OK) sms = info.sms;
+  const bool have_dev = current_device(&dev, &info) == ABFT_OK;
+  if (have_dev) sms = info.sms;
   if (args->num_sms > 0 && args->num_sms < sms) sms = args->num_sms;
-  const int bn = args->tile_n ? args->tile_n : abft_pick_tile_n(args->M, args->N, args->K, sms, args->mode);
-  GemmWs w;
-  gemm_ws_layout(args, bn, sms, &w);
-  return w.total;
+  Plan pl;
+  if (make_plan(args, have_dev ? dev : -1, sms, &pl) != ABFT_OK) return 0;
+  return pl.total;
+}
+
+int32_t abft_pick_tile_m(int64_t M, int64_t N, int64_t K, int32_t num_sms, uint32_t mode, int32_t tile_n) {
+  if (num_sms <= 0) num_sms = 148;
+  return pick_tile_m(M, N, K, num_sms, mode, tile_n);
 }
 
 int abft_gemm_bf16(const abft_gemm_args* a, void* stream) {
@@ -349,20 +464,28 @@ int abft_gemm_bf16(const abft_gemm_args* a, void* stream) {
 
   int sms = info.sms;
   if (a->num_sms > 0 && a->num_sms < sms) sms = a->num_sms;
-  const int bn = a->tile_n ? a->tile_n : abft_pick_tile_n(a->M, a->N, a->K, sms, a->mode);
-  const bool check = (a->mode & (ABFT_MODE_DETECT | ABFT_MODE_CORRECT)) != 0;
-  GemmWs ws;
-  gemm_ws_layout(a, bn, sms, &ws);
+  Plan ws;
+  rc = make_plan(a, dev, sms, &ws);
+  if (rc != ABFT_OK) return rc;
+  const int bn = ws.bn;
+  const bool check = ws.check;
   if (ws.total > 0 && (a->workspace == nullptr || a->workspace_bytes < ws.total || !aligned16(a->workspace)))
     return ABFT_ERR_WORKSPACE;
   uint8_t* wsb = static_cast<uint8_t*>(a->workspace);
 
-  CUtensorMap tmA, tmB;
+  // B-operand boxes: the whole data width of a tile, or in a pair the even
+  // CTA's 128 rows (tmB) and the odd CTA's remaining data rows (tmB2).
+  CUtensorMap tmA, tmB, tmB2;
   rc = make_tmap_kmajor(&tmA, a->A, a->K, a->M, a->lda, kBM);
   if (rc != ABFT_OK) return rc;
-  const int bd = check ? bn - kChkRows : bn;  // data columns per output tile
-  rc = make_tmap_kmajor(&tmB, a->B, a->K, a->N, a->ldb, bd);
+  const int bd = ws.bd;  // data columns per output tile
+  rc = make_tmap_kmajor(&tmB, a->B, a->K, a->N, a->ldb, ws.pair ? bn / 2 : bd);
   if (rc != ABFT_OK) return rc;
+  tmB2 = tmB;
+  if (ws.pair && check) {
+    rc = make_tmap_kmajor(&tmB2, a->B, a->K, a->N, a->ldb, bd - bn / 2);
+    if (rc != ABFT_OK) return rc;
+  }
 
   CUtensorMap tmV = tmA;  // placeholder when checks are off
   if (check) {
@@ -385,7 +508,7 @@ int abft_gemm_bf16(const abft_gemm_args* a, void* stream) {
   p.N = static_cast<int>(a->N);
   p.K = static_cast<int>(a->K);
   p.num_kb = static_cast<int>(cdiv(a->K, kBK));
-  p.tiles_m = static_cast<int>(cdiv(a->M, kBM));
+  p.tiles_m = static_cast<int>(cdiv(a->M, ws.tile_m));
   p.tiles_n = static_cast<int>(cdiv(a->N, bd));
   p.num_tiles = p.tiles_m * p.tiles_n;
   p.group_m = 16;
@@ -401,10 +524,11 @@ int abft_gemm_bf16(const abft_gemm_args* a, void* stream) {
   p.capacity = a->report_capacity;
   p.tile_sumc = (a->mode & ABFT_MODE_REF) ? reinterpret_cast<float*>(wsb + ws.parts_off) : nullptr;
 
-  const Schedule sch = make_schedule(p.num_tiles, p.num_kb, sms);
-  const int grid = sch.grid;
+  const Schedule& sch = ws.sch;
+  const int grid = ws.grid;
   p.dp_tiles = sch.dp_tiles;
   p.sk = sch.sk;
+  p.sk_ctas = sch.sk_ctas;
   p.sk_iters = sch.sk_iters;
   p.partials = nullptr;
   p.flags = nullptr;
@@ -414,12 +538,15 @@ int abft_gemm_bf16(const abft_gemm_args* a, void* stream) {
     if (cudaMemsetAsync(p.flags, 0, static_cast<size_t>(grid) * sizeof(int), s) != cudaSuccess)
       return launch_status(), ABFT_ERR_CUDA;
   }
-  if (bn == 256)
-    rc = check ? launch_gemm<256, true>(dev, 0, tmA, tmB, tmV, p, grid, s)
-               : launch_gemm<256, false>(dev, 1, tmA, tmB, tmV, p, grid, s);
+  if (ws.pair)
+    rc = check ? launch_gemm<256, true, true>(dev, kPairSlot[1], tmA, tmB, tmB2, tmV, p, grid, s)
+               : launch_gemm<256, false, true>(dev, kPairSlot[0], tmA, tmB, tmB2, tmV, p, grid, s);
+  else if (bn == 256)
+    rc = check ? launch_gemm<256, true, false>(dev, 0, tmA, tmB, tmB2, tmV, p, grid, s)
+               : launch_gemm<256, false, false>(dev, 1, tmA, tmB, tmB2, tmV, p, grid, s);
   else
-    rc = check ? launch_gemm<128, true>(dev, 2, tmA, tmB, tmV, p, grid, s)
-               : launch_gemm<128, false>(dev, 3, tmA, tmB, tmV, p, grid, s);
+    rc = check ? launch_gemm<128, true, false>(dev, 2, tmA, tmB, tmB2, tmV, p, grid, s)
+               : launch_gemm<128, false, false>(dev, 3, tmA, tmB, tmB2, tmV, p, grid, s);
   if (rc != ABFT_OK) return rc;
 
   if (a->mode & ABFT_MODE_REF) {
@@ -431,9 +558,10 @@ int abft_gemm_bf16(const abft_gemm_args* a, void* stream) {
     if (rc != ABFT_OK) return rc;
     rc = colsum(a->B, a->ldb, a->N, a->K, nullptr, pb, vf, nullptr, nullptr, sms, s);
     if (rc != ABFT_OK) return rc;
-    ref_finalize_kernel<<<1, 1024, 0, s>>>(u, vf, p.K, p.bias, p.N, p.M, p.tile_sumc, p.num_tiles * 8, a->tol_abs,
+    ref_finalize_kernel<<<1, 1024, 0, s>>>(u, vf, p.K, p.bias, p.N, p.M, p.tile_sumc,
+                                           p.num_tiles * 8 * (ws.pair ? 2 : 1), a->tol_abs,
                                            a->tol_rel, (a->mode & ABFT_MODE_REF_BF16) ? 1 : 0, p.report, p.capacity,
-                                           kBM, bd);
+                                           ws.tile_m, bd);
     rc = launch_status();
   }
   return rc;

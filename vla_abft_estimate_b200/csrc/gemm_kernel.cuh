@@ -53,23 +53,38 @@ constexpr int kEpiWarp0 = 2;
 constexpr int kEpiThreads = 256;
 constexpr int kChkRows = 8;  // rows of the per-tile checksum block
 
-template <int BN, bool CHECK>
+// PAIR: a 2-CTA cluster shares one 256 x BN output tile. Each CTA holds 128
+// rows of A and BN/2 rows of the B-operand tile per stage; one pair MMA
+// (M = 256) issued by the even CTA reads both CTAs' halves and accumulates
+// each CTA's 128 rows into that CTA's own TMEM.
+template <int BN, bool CHECK, bool PAIR = false>
 struct GemmCfg {
-  static constexpr int kStages = (BN == 256) ? 4 : 6;
+  static_assert(!PAIR || BN == 256, "CTA pairs use 256-wide tiles");
+  static constexpr int kStages = PAIR ? 6 : ((BN == 256) ? 4 : 6);
   static constexpr int kBD = CHECK ? BN - kChkRows : BN;  // data columns per tile
+  static constexpr int kTileM = PAIR ? 2 * kBM : kBM;    // output rows per tile
+  static constexpr int kBRows = PAIR ? BN / 2 : BN;      // B-operand rows this CTA stages
   static constexpr int kABytes = kBM * kBK * 2;
-  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kBBytes = kBRows * kBK * 2;
   static constexpr int kTmemCols = 2 * BN;
   static constexpr int kOffA = 0;
   static constexpr int kOffB = kOffA + kStages * kABytes;
   static constexpr int kOffX = kOffB + kStages * kBBytes;  // row-half partial exchange
   static constexpr int kXBytes = 2 * 2 * kBM * 16;         // [tile parity][half][row] float4
-  static constexpr int kOffBar = kOffX + (CHECK ? kXBytes : 0);
+  // Per epilogue warp, one 32-row x 32-column bf16 block of the output on
+  // its way to global memory (rows transposed across lanes so that a warp
+  // store covers 8 rows x 64 contiguous bytes).
+  static constexpr int kStageBytes = 32 * 32 * 2;
+  static constexpr int kOffStage = kOffX + (CHECK ? kXBytes : 0);
+  static constexpr int kOffBar = kOffStage + 8 * kStageBytes;
   static constexpr int kNumBars = 2 * kStages + 2 * 3 + 2;  // full, empty, tfull, tempty, xbar, drain, pbar
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffMisc + 64 + 1024;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
-  static_assert((kBD * 128) % 1024 == 0, "checksum rows must start on a swizzle atom");
+  // Row of the staged B-operand tile where the checksum block starts: after
+  // all BD data rows, or, in a pair, after the odd CTA's BD - 128.
+  static constexpr int kChkRow0 = PAIR ? kBD - kBRows : kBD;
+  static_assert((kChkRow0 * 128) % 1024 == 0, "checksum rows must start on a swizzle atom");
 };
 
 struct GemmParams {
@@ -90,37 +105,43 @@ struct GemmParams {
   float* tile_sumc;  // ABFT_MODE_REF: [num_tiles][8] partial sums of the stored outputs
   // Hybrid schedule: tiles [0, dp_tiles) are data-parallel (whole tiles,
   // blockIdx.x + j*gridDim.x); with sk != 0 the remaining tiles are
-  // stream-K: CTA c owns k-block iterations [c*W/G, (c+1)*W/G) of the
-  // W = sk_iters = (num_tiles - dp_tiles) * num_kb that follow, G = gridDim.x.
+  // stream-K: CTA c < G owns k-block iterations [c*W/G, (c+1)*W/G) of the
+  // W = sk_iters = (num_tiles - dp_tiles) * num_kb that follow,
+  // G = sk_ctas <= gridDim.x (fewer CTAs, fewer pieces per tile).
   int dp_tiles;
   int sk;
+  int sk_ctas;  // stream-K units: CTAs, or CTA pairs
   int64_t sk_iters;
-  float* partials;  // [G][128][BN] fp32: a CTA's share of a tile it does not finish
+  float* partials;  // [G][BN][128] fp32, column-major: a CTA's share of a tile it does not finish
   int* flags;       // [G]: set to 1 once that CTA's partial is visible
 };
 
 // Walks the (tile, k-block range) segments one CTA owns. Data-parallel:
 // whole tiles blockIdx.x, +gridDim.x, ...; stream-K: consecutive slices of
 // the CTA's iteration range, cut at tile boundaries.
+// A unit is one CTA, or one CTA pair (both CTAs walk the same segments).
 struct SegmentIter {
   int64_t it, end;
-  int tile_dp;
-  __device__ __forceinline__ explicit SegmentIter(const GemmParams& p) {
-    tile_dp = blockIdx.x;
+  int tile_dp, stride;
+  __device__ __forceinline__ SegmentIter(const GemmParams& p, int unit, int nunits) {
+    tile_dp = unit;
+    stride = nunits;
     const int64_t base = static_cast<int64_t>(p.dp_tiles) * p.num_kb;
-    it = base + sk_begin(p, blockIdx.x);
-    end = base + sk_begin(p, blockIdx.x + 1);
+    it = base + sk_begin(p, unit);
+    end = base + sk_begin(p, unit + 1);
   }
-  // First stream-K iteration of CTA c, relative to the stream-K region.
+  // First stream-K iteration of unit c, relative to the stream-K region
+  // (units from sk_ctas on own none).
   __device__ __forceinline__ static int64_t sk_begin(const GemmParams& p, int c) {
-    return (static_cast<int64_t>(c) * p.sk_iters) / gridDim.x;
+    if (c >= p.sk_ctas) return p.sk_iters;
+    return (static_cast<int64_t>(c) * p.sk_iters) / p.sk_ctas;
   }
   __device__ __forceinline__ bool next(const GemmParams& p, int& tile, int& kb0, int& kb1) {
     if (tile_dp < p.dp_tiles) {
       tile = tile_dp;
       kb0 = 0;
       kb1 = p.num_kb;
-      tile_dp += gridDim.x;
+      tile_dp += stride;
       return true;
     }
     if (!p.sk || it >= end) return false;
@@ -216,15 +237,17 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-template <int BN, bool CHECK, bool SPLIT>
+template <int BN, bool CHECK, bool SPLIT, bool PAIR>
 __device__ __forceinline__ bool mma_mainloop(uint8_t* smem, uint64_t* full, uint64_t* empty, int& stage,
                                              uint32_t& phase, int kb0, int kb1, uint32_t d, uint32_t idesc,
                                              volatile int* abort_flag) {
-  using Cfg = GemmCfg<BN, CHECK>;
+  using Cfg = GemmCfg<BN, CHECK, PAIR>;
   constexpr int S = Cfg::kStages;
   constexpr int BD = Cfg::kBD;
-  constexpr uint32_t idesc_full = umma_idesc_bf16(kBM, BN);
+  constexpr int G = PAIR ? 2 : 1;
+  constexpr uint32_t idesc_full = umma_idesc_bf16(Cfg::kTileM, BN);
   constexpr uint32_t idesc_chk = umma_idesc_bf16(kBM, kChkRows);
+  static_assert(!(SPLIT && PAIR), "pairs run tail tiles at full width");
   for (int kb = kb0; kb < kb1; ++kb) {
     if (!mbar_wait(&full[stage], phase, abort_flag)) return false;
     tc_fence_after();
@@ -234,14 +257,18 @@ __device__ __forceinline__ bool mma_mainloop(uint8_t* smem, uint64_t* full, uint
     for (int k = 0; k < kBK / 16; ++k) {
       const uint64_t adesc = sw128_kmajor_desc(a_addr + k * 32);
       const uint32_t accum = ((kb - kb0) | k) != 0 ? 1u : 0u;
-      if (!SPLIT) {
-        umma_bf16_ss(d, adesc, sw128_kmajor_desc(b_addr + k * 32), idesc_full, accum);
+      if constexpr (!SPLIT) {
+        umma_bf16_ss_g<G>(d, adesc, sw128_kmajor_desc(b_addr + k * 32), idesc_full, accum);
       } else {
         umma_bf16_ss(d, adesc, sw128_kmajor_desc(b_addr + k * 32), idesc, accum);
         umma_bf16_ss(d + BD, adesc, sw128_kmajor_desc(b_addr + BD * 128 + k * 32), idesc_chk, accum);
       }
     }
-    umma_commit(&empty[stage]);
+    // The stage is free in both CTAs of a pair once these MMAs have read it.
+    if constexpr (PAIR)
+      umma_commit_pair_both(&empty[stage], 0x3);
+    else
+      umma_commit(&empty[stage]);
     if (++stage == S) {
       stage = 0;
       phase ^= 1u;
@@ -250,13 +277,17 @@ __device__ __forceinline__ bool mma_mainloop(uint8_t* smem, uint64_t* full, uint
   return true;
 }
 
-template <int BN, bool CHECK>
+// tmB2 (pairs with checks only): B rows for the odd CTA, whose share of a
+// tile's data rows is BD - 128 rather than 128.
+template <int BN, bool CHECK, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     abft_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const __grid_constant__ CUtensorMap tmV, const GemmParams p) {
-  using Cfg = GemmCfg<BN, CHECK>;
+                     const __grid_constant__ CUtensorMap tmB2, const __grid_constant__ CUtensorMap tmV,
+                     const GemmParams p) {
+  using Cfg = GemmCfg<BN, CHECK, PAIR>;
   constexpr int S = Cfg::kStages;
   constexpr int BD = Cfg::kBD;
+  constexpr int G = PAIR ? 2 : 1;
   constexpr int NV = BN / 2;  // accumulator columns per epilogue thread
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -274,6 +305,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;  // 0 = the pair's MMA issuer
+  const int unit = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int nunits = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -282,7 +316,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], kEpiThreads);
+      // Pairs: one arrival per epilogue warp of either CTA, on the even CTA's barrier.
+      mbar_init(&tempty[b], PAIR ? 2 * (kEpiThreads / 32) : kEpiThreads);
       mbar_init(&xbar[b], kEpiThreads);
     }
     mbar_init(drain, 1);
@@ -293,19 +328,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (PAIR && CHECK) tma_prefetch_desc(&tmB2);
     if (CHECK) tma_prefetch_desc(&tmV);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, Cfg::kTmemCols);
-    tmem_relinquish();
+    tmem_alloc_g<G>(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish_g<G>();
   }
   tc_fence_before();
-  __syncthreads();
+  // Pairs: the barriers and TMEM of both CTAs exist before either CTA's
+  // TMA, MMA or remote arrive can touch them.
+  if constexpr (PAIR)
+    cluster_sync_all();
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   if (blockIdx.x == 0 && threadIdx.x == 0 && p.report != nullptr) {
     p.report->capacity = static_cast<uint32_t>(p.capacity);
-    p.report->tile_m = kBM;
+    p.report->tile_m = Cfg::kTileM;
     p.report->tile_n = BD;
     if (!(p.mode & ABFT_MODE_REF)) p.report->ref_ok = -1;
   }
@@ -317,22 +358,40 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       uint32_t issued_mask = 0, issued_phase = 0;
       bool ok = true;
-      constexpr uint32_t kTx = Cfg::kABytes + Cfg::kBBytes;
-      SegmentIter seg(p);
+      // Pairs: both CTAs' copies complete on the even CTA's full barrier,
+      // which expects the bytes of both.
+      constexpr uint32_t kTx = G * (Cfg::kABytes + Cfg::kBBytes);
+      SegmentIter seg(p, unit, nunits);
       int tile, kb0, kb1;
       while (ok && seg.next(p, tile, kb0, kb1)) {
         int mt, nt;
         tile_coords(tile, p, mt, nt);
+        const int arow = mt * Cfg::kTileM + static_cast<int>(rank) * kBM;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
             ok = false;
             break;
           }
+          uint8_t* sa = smem + Cfg::kOffA + stage * Cfg::kABytes;
           uint8_t* sb = smem + Cfg::kOffB + stage * Cfg::kBBytes;
-          mbar_arrive_expect_tx(&full[stage], kTx);
-          tma_load_2d(smem + Cfg::kOffA + stage * Cfg::kABytes, &tmA, &full[stage], kb * kBK, mt * kBM);
-          tma_load_2d(sb, &tmB, &full[stage], kb * kBK, nt * BD);
-          if (CHECK) tma_load_2d(sb + BD * 128, &tmV, &full[stage], kb * kBK, nt * kChkRows);
+          if constexpr (PAIR) {
+            const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+            if (rank == 0) mbar_arrive_expect_tx(&full[stage], kTx);
+            tma_load_2d_pair(sa, &tmA, fb, kb * kBK, arow);
+            if (!CHECK) {
+              tma_load_2d_pair(sb, &tmB, fb, kb * kBK, nt * BN + static_cast<int>(rank) * Cfg::kBRows);
+            } else if (rank == 0) {
+              tma_load_2d_pair(sb, &tmB, fb, kb * kBK, nt * BD);
+            } else {
+              tma_load_2d_pair(sb, &tmB2, fb, kb * kBK, nt * BD + Cfg::kBRows);
+              tma_load_2d_pair(sb + Cfg::kChkRow0 * 128, &tmV, fb, kb * kBK, nt * kChkRows);
+            }
+          } else {
+            mbar_arrive_expect_tx(&full[stage], kTx);
+            tma_load_2d(sa, &tmA, &full[stage], kb * kBK, arow);
+            tma_load_2d(sb, &tmB, &full[stage], kb * kBK, nt * BD);
+            if (CHECK) tma_load_2d(sb + BD * 128, &tmV, &full[stage], kb * kBK, nt * kChkRows);
+          }
           issued_mask |= 1u << stage;
           issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
           if (++stage == S) {
@@ -343,29 +402,38 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) {
         // Unwinding: let every issued copy land before the CTA can exit.
-        for (int s = 0; s < S; ++s)
-          if (issued_mask & (1u << s)) mbar_wait_unwind(&full[s], (issued_phase >> s) & 1u);
+        if constexpr (PAIR) {
+          // The copies complete on the even CTA's barriers: give them a
+          // fixed, generous time instead.
+          const uint64_t t0 = global_timer_ns();
+          while (issued_mask && global_timer_ns() - t0 < 200000ull) {
+          }
+        } else {
+          for (int s = 0; s < S; ++s)
+            if (issued_mask & (1u << s)) mbar_wait_unwind(&full[s], (issued_phase >> s) & 1u);
+        }
       }
     }
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc_full = umma_idesc_bf16(kBM, BN);
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc_full = umma_idesc_bf16(Cfg::kTileM, BN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      SegmentIter seg(p);
+      SegmentIter seg(p, unit, nunits);
       int tile, kb0, kb1;
       while (ok && seg.next(p, tile, kb0, kb1)) {
         int mt, nt;
         tile_coords(tile, p, mt, nt);
         // A checked tail tile narrower than BD multiplies only its valid data
         // rows, then the checksum rows separately into columns [BD, BN).
+        // Pairs multiply the full width (the rows past N are zero-filled).
         const int ncols = min(BD, p.N - nt * BD);
-        const bool split = CHECK && ncols < BD;
+        const bool split = !PAIR && CHECK && ncols < BD;
         const uint32_t idesc_data = split ? umma_idesc_bf16(kBM, ncols) : idesc_full;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag)) break;
         tc_fence_after();
@@ -373,18 +441,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Full tiles keep every instruction descriptor a compile-time
         // constant; only a checked tail tile takes the runtime-N path.
         if (!split)
-          ok = mma_mainloop<BN, CHECK, false>(smem, full, empty, stage, phase, kb0, kb1, d, idesc_full, abort_flag);
-        else
-          ok = mma_mainloop<BN, CHECK, true>(smem, full, empty, stage, phase, kb0, kb1, d, idesc_data, abort_flag);
+          ok = mma_mainloop<BN, CHECK, false, PAIR>(smem, full, empty, stage, phase, kb0, kb1, d, idesc_full,
+                                                    abort_flag);
+        else if constexpr (!PAIR)
+          ok = mma_mainloop<BN, CHECK, true, false>(smem, full, empty, stage, phase, kb0, kb1, d, idesc_data,
+                                                    abort_flag);
         if (!ok) break;
-        umma_commit(&tfull[acc]);
+        if constexpr (PAIR)
+          umma_commit_pair_both(&tfull[acc], 0x3);
+        else
+          umma_commit(&tfull[acc]);
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1u;
         }
       }
       // Every MMA this thread issued must finish before TMEM is released.
-      umma_commit(drain);
+      umma_commit_g<G>(drain);
       mbar_wait_unwind(drain, 0);
     }
     __syncwarp();
@@ -401,10 +474,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int ep = warp - kEpiWarp0;        // 0..7
     constexpr int NCH = NV / 32;            // 32-column chunks per thread
     float4* xchg = reinterpret_cast<float4*>(smem + Cfg::kOffX);
+    // This warp's staging block: 32 rows of 64 bytes, the four 16-byte
+    // pieces of row y permuted by XOR with (y >> 1) & 3 so that both the
+    // row-per-lane writes and the 8-rows-per-instruction reads are free of
+    // bank conflicts.
+    uint8_t* stg = smem + Cfg::kOffStage + ep * Cfg::kStageBytes;
+    const int rd_row = lane >> 2;  // read side: row (within 8) and piece of this lane
+    const int rd_piece = lane & 3;
     int acc = 0;
     uint32_t acc_phase = 0;
     int xuse = 0;  // uses of the row-half exchange buffers
-    SegmentIter seg(p);
+    // Hand the accumulator back to the MMA issuer (in a pair, the even CTA:
+    // one arrival per warp after all its lanes' TMEM reads).
+    auto release_acc = [&](int a) {
+      tc_fence_before();
+      if constexpr (PAIR) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[a]), 0));
+      } else {
+        mbar_arrive(&tempty[a]);
+      }
+    };
+    SegmentIter seg(p, unit, nunits);
     int tile, kb0, kb1;
     while (seg.next(p, tile, kb0, kb1)) {
       int mt, nt;
@@ -418,10 +509,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (kb0 != 0) {
         // Stream-K contributor: the tile's first k-blocks belong to a lower
         // CTA, which finishes the tile. Hand it the fp32 partial (all BN
-        // columns, checksum columns included). A segment that starts inside
+        // columns, checksum columns included), column-major so that each
+        // warp store is 32 consecutive words. A segment that starts inside
         // a tile is the first segment of this CTA, so it is stored before
         // this CTA waits for anything: the wait chain is one link long.
-        float4* dst = reinterpret_cast<float4*>(p.partials + (static_cast<size_t>(blockIdx.x) * kBM + r) * BN + h * NV);
+        float* dst = p.partials + (static_cast<size_t>(blockIdx.x) * BN + h * NV) * kBM + r;
 #pragma unroll 1
         for (int c = 0; c < NCH; ++c) {
           uint32_t v[32];
@@ -429,12 +521,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld_32x32b_x32(tcol + c * 32, v);
           tmem_ld_wait();
 #pragma unroll
-          for (int g = 0; g < 8; ++g)
-            dst[c * 8 + g] = make_float4(__uint_as_float(v[4 * g]), __uint_as_float(v[4 * g + 1]),
-                                         __uint_as_float(v[4 * g + 2]), __uint_as_float(v[4 * g + 3]));
+          for (int e = 0; e < 32; ++e) __stcg(dst + (c * 32 + e) * kBM, __uint_as_float(v[e]));
         }
-        tc_fence_before();
-        mbar_arrive(&tempty[acc]);
+        release_acc(acc);
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1u;
@@ -452,20 +541,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_wait();
       }
       if (kb1 != p.num_kb) {
-        // Stream-K finisher (this CTA owns the tile's first k-blocks): fold
-        // in the partials of the CTAs that own its later k-blocks (CTAs
-        // blockIdx.x+1, +2, ..., cmax), in that order, writing the sums back
-        // to TMEM chunk by chunk.
+        // Stream-K finisher (this unit owns the tile's first k-blocks): fold
+        // in the partials of the units that own its later k-blocks (units
+        // unit+1, +2, ..., umax; in a pair, their CTAs of the same rank), in
+        // that order, writing the sums back to TMEM chunk by chunk.
         const int64_t tile_end = static_cast<int64_t>(tile - p.dp_tiles + 1) * p.num_kb;
-        int cmax = static_cast<int>(blockIdx.x);
+        int umax = unit;
         bool okp = true;
-        for (int c = static_cast<int>(blockIdx.x) + 1; c < static_cast<int>(gridDim.x); ++c) {
+        for (int c = unit + 1; c < p.sk_ctas; ++c) {
           if (SegmentIter::sk_begin(p, c) >= tile_end) break;
-          if (!wait_flag(&p.flags[c], abort_flag)) {
+          if (!wait_flag(&p.flags[c * G + static_cast<int>(rank)], abort_flag)) {
             okp = false;
             break;
           }
-          cmax = c;
+          umax = c;
         }
         if (!__all_sync(0xFFFFFFFFu, okp)) break;
 #pragma unroll 1
@@ -474,32 +563,29 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           tmem_ld_32x32b_x32(tcol + c * 32, v);
           tmem_ld_wait();
-          for (int cc = static_cast<int>(blockIdx.x) + 1; cc <= cmax; ++cc) {
-            const float4* src =
-                reinterpret_cast<const float4*>(p.partials + (static_cast<size_t>(cc) * kBM + r) * BN + h * NV) + c * 8;
+#pragma unroll 1
+          for (int u = unit + 1; u <= umax; ++u) {
+            const int cc = u * G + static_cast<int>(rank);
+            const float* src = p.partials + (static_cast<size_t>(cc) * BN + h * NV + c * 32) * kBM + r;
 #pragma unroll
-            for (int g = 0; g < 8; ++g) {
-              const float4 q4 = src[g];
-              v[4 * g] = __float_as_uint(__uint_as_float(v[4 * g]) + q4.x);
-              v[4 * g + 1] = __float_as_uint(__uint_as_float(v[4 * g + 1]) + q4.y);
-              v[4 * g + 2] = __float_as_uint(__uint_as_float(v[4 * g + 2]) + q4.z);
-              v[4 * g + 3] = __float_as_uint(__uint_as_float(v[4 * g + 3]) + q4.w);
-            }
+            for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) + __ldcg(src + e * kBM));
           }
           __syncwarp();
           tmem_st_32x32b_x32(tcol + c * 32, v);
         }
         tmem_st_wait();
         if (CHECK) {
-          for (int cc = static_cast<int>(blockIdx.x) + 1; cc <= cmax; ++cc) {
-            const float* row = p.partials + (static_cast<size_t>(cc) * kBM + r) * BN + BD;
+          for (int u = unit + 1; u <= umax; ++u) {
+            const int cc = u * G + static_cast<int>(rank);
+            const float* col = p.partials + (static_cast<size_t>(cc) * BN + BD) * kBM + r;
 #pragma unroll
-            for (int e = 0; e < kChkRows; ++e) chk[e] = __float_as_uint(__uint_as_float(chk[e]) + row[e]);
+            for (int e = 0; e < kChkRows; ++e) chk[e] = __float_as_uint(__uint_as_float(chk[e]) + __ldcg(col + e * kBM));
           }
         }
       }
 
-      const int grow = mt * kBM + r;
+      const int row0 = mt * Cfg::kTileM + static_cast<int>(rank) * kBM;  // first row of this CTA's slab
+      const int grow = row0 + r;
       const int col0 = nt * BD;
       const int ncols = min(BD, p.N - col0);
       const int hcol0 = h * NV;  // first local column of this thread
@@ -541,20 +627,49 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           tmem_ld_32x32b_x32(tcol + c * 32, v);
           tmem_ld_wait();
+          if (n_my) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            float x = __uint_as_float(v[e]);
-            const int lc = c * 32 + e;  // column within this thread's half
-            if (n_my) {
+            for (int e = 0; e < 32; ++e) {
+              float x = __uint_as_float(v[e]);
 #pragma unroll
-              for (int i = 0; i < kMaxInj; ++i) x += (inj_c[i] == lc) ? inj_d[i] : 0.f;
+              for (int i = 0; i < kMaxInj; ++i) x += (inj_c[i] == c * 32 + e) ? inj_d[i] : 0.f;
+              v[e] = __float_as_uint(x);
             }
-            const int col = hcol0 + lc;
-            if (col < ncols) {
-              s1 += x;
-              s2 = fmaf(static_cast<float>(col + 1), x, s2);
-              s3 += (__popc(col) & 1) ? -x : x;
-              amax = fmaxf(amax, fabsf(x));
+          }
+          const int base = hcol0 + c * 32;  // first local column of the chunk (a multiple of 32)
+          if (base + 32 <= ncols) {
+            // Whole chunk valid: the column weights split into the chunk's
+            // base plus a compile-time offset, and the Thue-Morse sign of
+            // base + e is sg(base) * sg(e) (base has its low 5 bits clear).
+            float a0 = 0.f, a1 = 0.f, w0 = 0.f, w1 = 0.f, t0 = 0.f, t1 = 0.f;
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              const float x0 = __uint_as_float(v[e]);
+              const float x1 = __uint_as_float(v[e + 1]);
+              a0 += x0;
+              a1 += x1;
+              w0 = fmaf(static_cast<float>(e), x0, w0);
+              w1 = fmaf(static_cast<float>(e + 1), x1, w1);
+              t0 += (__builtin_popcount(e) & 1) ? -x0 : x0;
+              t1 += (__builtin_popcount(e + 1) & 1) ? -x1 : x1;
+              amax = fmaxf(amax, fmaxf(fabsf(x0), fabsf(x1)));
+            }
+            const float a = a0 + a1;
+            const float t = t0 + t1;
+            s1 += a;
+            s2 += fmaf(static_cast<float>(base + 1), a, w0 + w1);
+            s3 += (__popc(base) & 1) ? -t : t;
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const float x = __uint_as_float(v[e]);
+              const int col = base + e;
+              if (col < ncols) {
+                s1 += x;
+                s2 = fmaf(static_cast<float>(col + 1), x, s2);
+                s3 += (__popc(col) & 1) ? -x : x;
+                amax = fmaxf(amax, fabsf(x));
+              }
             }
           }
         }
@@ -626,11 +741,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
 
-      // Pass 2: final values -> bf16 -> global.
+      // Pass 2: final values -> bf16 -> staging block -> global.
       const int fix_local = fix_col - hcol0;  // column within this thread's half, or out of range
       float row_out_sum = 0.f;
-      __nv_bfloat16* crow = p.C + static_cast<int64_t>(grow) * p.ldc + col0 + hcol0;
       const uint4* bp = reinterpret_cast<const uint4*>(p.bias + col0 + hcol0);
+      const int rd_grow = row0 + q * 32 + rd_row;  // global row of this lane's first read-side row
 #pragma unroll 1
       for (int c = 0; c < NCH; ++c) {
         uint32_t v[32];
@@ -639,21 +754,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_wait();
         float x[32];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          x[e] = __uint_as_float(v[e]);
-          const int lc = c * 32 + e;
-          if (n_my) {
+        for (int e = 0; e < 32; ++e) x[e] = __uint_as_float(v[e]);
+        if (n_my) {
 #pragma unroll
-            for (int i = 0; i < kMaxInj; ++i) x[e] += (inj_c[i] == lc) ? inj_d[i] : 0.f;
+          for (int e = 0; e < 32; ++e) {
+#pragma unroll
+            for (int i = 0; i < kMaxInj; ++i) x[e] += (inj_c[i] == c * 32 + e) ? inj_d[i] : 0.f;
           }
-          if (fix_col >= 0) x[e] -= (fix_local == lc) ? fix_delta : 0.f;
         }
+        if (static_cast<unsigned>(fix_local - c * 32) < 32u) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) x[e] -= (fix_local == c * 32 + e) ? fix_delta : 0.f;
+        }
+        const int base = hcol0 + c * 32;
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
-          const int gcol = c * 32 + g * 8;  // first column of this 8-column group within the half
-          const bool gvalid = row_ok && (hcol0 + gcol < ncols);
+          const bool gvalid = row_ok && (base + g * 8 < ncols);
           if (p.bias != nullptr && gvalid) {
-            const uint4 bw = __ldg(bp + (gcol >> 3));
+            const uint4 bw = __ldg(bp + c * 4 + g);
             x[g * 8 + 0] += bf16_lo(bw.x);
             x[g * 8 + 1] += bf16_hi(bw.x);
             x[g * 8 + 2] += bf16_lo(bw.y);
@@ -666,17 +784,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint4 packed =
               make_uint4(pack_bf16x2(x[g * 8 + 0], x[g * 8 + 1]), pack_bf16x2(x[g * 8 + 2], x[g * 8 + 3]),
                          pack_bf16x2(x[g * 8 + 4], x[g * 8 + 5]), pack_bf16x2(x[g * 8 + 6], x[g * 8 + 7]));
-          if (gvalid) {
-            reinterpret_cast<uint4*>(crow)[gcol >> 3] = packed;
-            if (p.mode & ABFT_MODE_REF) {
-              row_out_sum += ((bf16_lo(packed.x) + bf16_hi(packed.x)) + (bf16_lo(packed.y) + bf16_hi(packed.y))) +
-                             ((bf16_lo(packed.z) + bf16_hi(packed.z)) + (bf16_lo(packed.w) + bf16_hi(packed.w)));
-            }
+          *reinterpret_cast<uint4*>(stg + lane * 64 + ((g ^ ((lane >> 1) & 3)) << 4)) = packed;
+          if ((p.mode & ABFT_MODE_REF) && gvalid) {
+            row_out_sum += ((bf16_lo(packed.x) + bf16_hi(packed.x)) + (bf16_lo(packed.y) + bf16_hi(packed.y))) +
+                           ((bf16_lo(packed.z) + bf16_hi(packed.z)) + (bf16_lo(packed.w) + bf16_hi(packed.w)));
           }
         }
+        __syncwarp();
+        // Read side: instruction i covers rows 8i..8i+7 of the block, four
+        // lanes per row, each lane one 16-byte piece (8 columns).
+        const int lcol = base + rd_piece * 8;  // local column of this lane's piece
+        const bool col_ok = lcol < ncols;
+        __nv_bfloat16* cbase = p.C + static_cast<int64_t>(rd_grow) * p.ldc + col0 + lcol;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int y = i * 8 + rd_row;
+          const uint4 val = *reinterpret_cast<const uint4*>(stg + y * 64 + ((rd_piece ^ ((y >> 1) & 3)) << 4));
+          if (col_ok && rd_grow + i * 8 < p.M) *reinterpret_cast<uint4*>(cbase + static_cast<int64_t>(i * 8) * p.ldc) = val;
+        }
       }
-      tc_fence_before();
-      mbar_arrive(&tempty[acc]);
+      release_acc(acc);
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
@@ -687,16 +814,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         // warp order by the finishing kernel.
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) row_out_sum += __shfl_xor_sync(0xFFFFFFFFu, row_out_sum, o);
-        if (lane == 0) p.tile_sumc[tile * 8 + ep] = row_out_sum;
+        if (lane == 0) p.tile_sumc[(tile * G + static_cast<int>(rank)) * 8 + ep] = row_out_sum;
       }
-      if (aborted) break;
+      // Leave the tile loop together: the TMEM loads above are warp-collective.
+      if (__any_sync(0xFFFFFFFFu, aborted)) break;
     }
   }
 
-  __syncthreads();
+  tc_fence_before();
+  // Pairs: the even CTA's MMAs (which write both CTAs' TMEM and read both
+  // CTAs' shared memory) and the odd CTA's remote arrivals are all done
+  // before either CTA frees TMEM or exits.
+  if constexpr (PAIR)
+    cluster_sync_all();
+  else
+    __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+    tmem_dealloc_g<G>(tmem_base, Cfg::kTmemCols);
   }
   if (threadIdx.x == 0 && *abort_flag && p.report != nullptr) atomicOr(&p.report->status, ABFT_STATUS_DEVICE_TIMEOUT);
 }

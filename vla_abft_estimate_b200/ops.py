@@ -72,6 +72,13 @@ def pick_tile_n(m: int, n: int, k: int, device: Optional[torch.device] = None,
     return int(N.lib().abft_pick_tile_n(int(m), int(n), int(k), int(sms), int(mode)))
 
 
+def pick_tile_m(m: int, n: int, k: int, tile_n: int, device: Optional[torch.device] = None,
+                mode: int = N.MODE_DETECT | N.MODE_CORRECT) -> int:
+    """Tile height (128, or 256 = one 2-CTA pair per tile) the library would pick."""
+    sms = torch.cuda.get_device_properties(device or torch.device("cuda")).multi_processor_count
+    return int(N.lib().abft_pick_tile_m(int(m), int(n), int(k), int(sms), int(mode), int(tile_n)))
+
+
 def encode_weight(weight: torch.Tensor, tile_n: int) -> torch.Tensor:
     """Per-tile checksum block of ``weight`` [N, K] for tile width ``tile_n``.
 
@@ -114,6 +121,7 @@ def abft_gemm(
     *,
     mode: int = N.MODE_DETECT | N.MODE_CORRECT,
     tile_n: int = 0,
+    tile_m: int = 0,
     thr_scale: float = DEFAULT_THR_SCALE,
     thr_abs: float = 0.0,
     tol_abs: float = 1e-2,
@@ -129,7 +137,9 @@ def abft_gemm(
     ``a`` is [M, K], ``weight`` [N, K] (nn.Linear layout), ``bias`` [N].
     ``checksums`` is ``encode_weight(weight, tile_n)`` (cache it for a fixed
     weight); when omitted and checks are on, the call encodes into its
-    workspace. ``inject`` adds debug faults to the fp32 accumulator.
+    workspace. ``tile_m`` 256 runs each 256-row tile on a 2-CTA pair (needs
+    tile_n 256); 0 lets the library choose. ``inject`` adds debug faults to
+    the fp32 accumulator.
     Returns the output and the report buffer (None when mode == MODE_OFF).
     """
     _require_bf16_cuda("a", a, 2)
@@ -169,6 +179,7 @@ def abft_gemm(
     args.lda, args.ldb, args.ldc = a.stride(0), weight.stride(0), out.stride(0)
     args.mode = int(mode)
     args.tile_n = int(tile_n)
+    args.tile_m = int(tile_m)
     args.thr_scale, args.thr_abs = float(thr_scale), float(thr_abs)
     args.tol_abs, args.tol_rel = float(tol_abs), float(tol_rel)
     args.checksums = _ptr(checksums)
