@@ -351,3 +351,28 @@ def test_pair_needs_256_wide_tiles(cuda_device):
     a, w, _ = seeded(256, 256, 64, 15)
     with pytest.raises(N.AbftError):
         ops.abft_gemm(a.to(cuda_device), w.to(cuda_device), tile_n=128, tile_m=256)
+
+
+# --------------------------------------------- compact tail tiles (last column)
+@pytest.mark.parametrize("tile_n,tile_m", [(256, 128), (256, 256), (128, 128)])
+@pytest.mark.parametrize("n", [8, 16, 24, 40, 136, 248 + 8, 248 + 128, 248 + 232, 4096, 120 + 112])
+@pytest.mark.parametrize("mode", [N.MODE_OFF, N.MODE_DETECT | N.MODE_CORRECT])
+def test_tail_tile_widths(cuda_device, tile_n, tile_m, n, mode):
+    """Every width of the last tile column: outputs match, and a fault in
+    the tail's last data column is located and corrected."""
+    m, k = 384, 320
+    a, w, b = seeded(m, n, k, 16 + n, True)
+    ad, wd, bd = a.to(cuda_device), w.to(cuda_device), b.to(cuda_device)
+    ref = f32(a) @ f32(w).T + f32(b)
+    c, rep = ops.abft_gemm(ad, wd, bd, mode=mode, tile_n=tile_n, tile_m=tile_m)
+    assert max_rel_err(f32(c), ref) <= OUT_TOL
+    if mode == N.MODE_OFF:
+        return
+    assert rep.read().n_faults == 0
+    faults = [(m - 1, n - 1), (5, max(0, n - 9))]
+    a2, w2, b2, c2, r, orc = run_checked(cuda_device, m, n, k, faults, tile_n=tile_n, tile_m=tile_m, bias=True,
+                                          seed=16 + n)
+    got = sorted((x.row, x.col, x.flags) for x in r.records)
+    assert got == orc.records
+    assert r.n_corrected == len(faults)
+    assert max_rel_err(f32(c2), orc.out) <= OUT_TOL

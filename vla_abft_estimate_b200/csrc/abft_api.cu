@@ -338,12 +338,12 @@ int validate_gemm(const abft_gemm_args* a) {
 
 template <int BN, bool CHECK, bool PAIR>
 int launch_gemm(int dev, int slot, const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmB2,
-                const CUtensorMap& tmV, const GemmParams& p, int grid, cudaStream_t s) {
+                const CUtensorMap& tmV, const CUtensorMap& tmBt, const GemmParams& p, int grid, cudaStream_t s) {
   int rc = ensure_smem_attr<BN, CHECK, PAIR>(dev, slot);
   if (rc != ABFT_OK) return rc;
   constexpr size_t smem = GemmCfg<BN, CHECK, PAIR>::kSmemBytes;
   if constexpr (!PAIR) {
-    abft_gemm_kernel<BN, CHECK, false><<<grid, kThreads, smem, s>>>(tmA, tmB, tmB2, tmV, p);
+    abft_gemm_kernel<BN, CHECK, false><<<grid, kThreads, smem, s>>>(tmA, tmB, tmB2, tmV, tmBt, p);
   } else {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(grid));
@@ -353,7 +353,7 @@ int launch_gemm(int dev, int slot, const CUtensorMap& tmA, const CUtensorMap& tm
     cudaLaunchAttribute at = pair_cluster_attr();
     cfg.attrs = &at;
     cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, abft_gemm_kernel<BN, CHECK, true>, tmA, tmB, tmB2, tmV, p) != cudaSuccess)
+    if (cudaLaunchKernelEx(&cfg, abft_gemm_kernel<BN, CHECK, true>, tmA, tmB, tmB2, tmV, tmBt, p) != cudaSuccess)
       return launch_status(), ABFT_ERR_CUDA;
   }
   return launch_status();
@@ -524,6 +524,37 @@ int abft_gemm_bf16(const abft_gemm_args* a, void* stream) {
   p.capacity = a->report_capacity;
   p.tile_sumc = (a->mode & ABFT_MODE_REF) ? reinterpret_cast<float*>(wsb + ws.parts_off) : nullptr;
 
+  // Compact tail tile: when the last tile column holds ncols < bd data
+  // columns, its B-operand tile is those rows (then, with checks, the 8
+  // checksum rows) and one MMA of N = round16(ncols [+ 8]) covers it.
+  p.tail_n = 0;
+  p.tail_box = 0;
+  p.tail_tx = 0;
+  CUtensorMap tmBt = tmA;  // placeholder unless a tail box is needed
+  {
+    const int ncols = static_cast<int>(a->N - static_cast<int64_t>(p.tiles_n - 1) * bd);
+    const int tn = (ncols + (check ? kChkRows : 0) + 15) / 16 * 16;
+    if (ncols < bd && tn < bn) {
+      const uint32_t a_bytes = static_cast<uint32_t>(kBM * kBK * 2);
+      const uint32_t row_bytes = static_cast<uint32_t>(kBK * 2);  // one B row of one k-block
+      p.tail_n = tn;
+      if (!check) {
+        p.tail_tx = ws.pair ? 2 * (a_bytes + (bn / 2) * row_bytes) : a_bytes + bn * row_bytes;
+      } else {
+        // Data rows copied by the tail box into this CTA (a pair: the odd
+        // CTA holds the rows from tn / 2 on; the even CTA keeps its usual box).
+        const int box = ws.pair ? ncols - tn / 2 : ncols;
+        p.tail_box = box;
+        if (box > 0) {
+          rc = make_tmap_kmajor(&tmBt, a->B, a->K, a->N, a->ldb, box);
+          if (rc != ABFT_OK) return rc;
+        }
+        p.tail_tx = (ws.pair ? 2 * a_bytes + (bn / 2) * row_bytes : a_bytes) +
+                    static_cast<uint32_t>(box + kChkRows) * row_bytes;
+      }
+    }
+  }
+
   const Schedule& sch = ws.sch;
   const int grid = ws.grid;
   p.dp_tiles = sch.dp_tiles;
@@ -539,14 +570,14 @@ int abft_gemm_bf16(const abft_gemm_args* a, void* stream) {
       return launch_status(), ABFT_ERR_CUDA;
   }
   if (ws.pair)
-    rc = check ? launch_gemm<256, true, true>(dev, kPairSlot[1], tmA, tmB, tmB2, tmV, p, grid, s)
-               : launch_gemm<256, false, true>(dev, kPairSlot[0], tmA, tmB, tmB2, tmV, p, grid, s);
+    rc = check ? launch_gemm<256, true, true>(dev, kPairSlot[1], tmA, tmB, tmB2, tmV, tmBt, p, grid, s)
+               : launch_gemm<256, false, true>(dev, kPairSlot[0], tmA, tmB, tmB2, tmV, tmBt, p, grid, s);
   else if (bn == 256)
-    rc = check ? launch_gemm<256, true, false>(dev, 0, tmA, tmB, tmB2, tmV, p, grid, s)
-               : launch_gemm<256, false, false>(dev, 1, tmA, tmB, tmB2, tmV, p, grid, s);
+    rc = check ? launch_gemm<256, true, false>(dev, 0, tmA, tmB, tmB2, tmV, tmBt, p, grid, s)
+               : launch_gemm<256, false, false>(dev, 1, tmA, tmB, tmB2, tmV, tmBt, p, grid, s);
   else
-    rc = check ? launch_gemm<128, true, false>(dev, 2, tmA, tmB, tmB2, tmV, p, grid, s)
-               : launch_gemm<128, false, false>(dev, 3, tmA, tmB, tmB2, tmV, p, grid, s);
+    rc = check ? launch_gemm<128, true, false>(dev, 2, tmA, tmB, tmB2, tmV, tmBt, p, grid, s)
+               : launch_gemm<128, false, false>(dev, 3, tmA, tmB, tmB2, tmV, tmBt, p, grid, s);
   if (rc != ABFT_OK) return rc;
 
   if (a->mode & ABFT_MODE_REF) {

@@ -114,6 +114,12 @@ struct GemmParams {
   int64_t sk_iters;
   float* partials;  // [G][BN][128] fp32, column-major: a CTA's share of a tile it does not finish
   int* flags;       // [G]: set to 1 once that CTA's partial is visible
+  // Last tile column when it holds fewer than BD data columns (tail_n != 0):
+  // its B-operand tile is compact (data rows, then with checks the 8
+  // checksum rows) and one MMA of N = tail_n (a multiple of 16) covers it.
+  int tail_n;
+  int tail_box;      // data rows the tail box copies into this CTA (odd CTA of a pair), 0 = none
+  uint32_t tail_tx;  // bytes one stage of a tail tile delivers (both CTAs of a pair)
 };
 
 // Walks the (tile, k-block range) segments one CTA owns. Data-parallel:
@@ -219,11 +225,6 @@ __device__ __forceinline__ void tmem_ld_32x32b_x8(uint32_t taddr, uint32_t (&r)[
                : "r"(taddr));
 }
 
-// The k loop of one output tile: per 64-wide k-block wait for the stage, issue
-// four K=16 MMAs and release the stage when they complete. With SPLIT (a
-// checked tail tile of fewer than BD data columns) each step issues the data
-// MMA with the runtime descriptor `idesc` and a separate N=8 MMA of the
-// checksum rows into accumulator columns [BD, BN).
 __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
@@ -237,17 +238,19 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-template <int BN, bool CHECK, bool SPLIT, bool PAIR>
+// The k loop of one output tile: per 64-wide k-block wait for the stage, issue
+// four K=16 MMAs of width NM and release the stage when they complete. NM is
+// a template argument so that every instruction descriptor is a compile-time
+// constant (a runtime descriptor slowed the issue loop down severalfold).
+template <int BN, bool CHECK, bool PAIR, int NM>
 __device__ __forceinline__ bool mma_mainloop(uint8_t* smem, uint64_t* full, uint64_t* empty, int& stage,
-                                             uint32_t& phase, int kb0, int kb1, uint32_t d, uint32_t idesc,
+                                             uint32_t& phase, int kb0, int kb1, uint32_t d,
                                              volatile int* abort_flag) {
   using Cfg = GemmCfg<BN, CHECK, PAIR>;
   constexpr int S = Cfg::kStages;
-  constexpr int BD = Cfg::kBD;
   constexpr int G = PAIR ? 2 : 1;
-  constexpr uint32_t idesc_full = umma_idesc_bf16(Cfg::kTileM, BN);
-  constexpr uint32_t idesc_chk = umma_idesc_bf16(kBM, kChkRows);
-  static_assert(!(SPLIT && PAIR), "pairs run tail tiles at full width");
+  constexpr uint32_t idesc = umma_idesc_bf16(Cfg::kTileM, NM);
+  static_assert(NM % 16 == 0 && NM >= 16 && NM <= BN, "MMA width");
   for (int kb = kb0; kb < kb1; ++kb) {
     if (!mbar_wait(&full[stage], phase, abort_flag)) return false;
     tc_fence_after();
@@ -257,12 +260,7 @@ __device__ __forceinline__ bool mma_mainloop(uint8_t* smem, uint64_t* full, uint
     for (int k = 0; k < kBK / 16; ++k) {
       const uint64_t adesc = sw128_kmajor_desc(a_addr + k * 32);
       const uint32_t accum = ((kb - kb0) | k) != 0 ? 1u : 0u;
-      if constexpr (!SPLIT) {
-        umma_bf16_ss_g<G>(d, adesc, sw128_kmajor_desc(b_addr + k * 32), idesc_full, accum);
-      } else {
-        umma_bf16_ss(d, adesc, sw128_kmajor_desc(b_addr + k * 32), idesc, accum);
-        umma_bf16_ss(d + BD, adesc, sw128_kmajor_desc(b_addr + BD * 128 + k * 32), idesc_chk, accum);
-      }
+      umma_bf16_ss_g<G>(d, adesc, sw128_kmajor_desc(b_addr + k * 32), idesc, accum);
     }
     // The stage is free in both CTAs of a pair once these MMAs have read it.
     if constexpr (PAIR)
@@ -277,13 +275,29 @@ __device__ __forceinline__ bool mma_mainloop(uint8_t* smem, uint64_t* full, uint
   return true;
 }
 
+// mma_mainloop for a runtime width n (a multiple of 16 in [16, BN]): one
+// compile-time instance per width.
+template <int BN, bool CHECK, bool PAIR, int NM = 16>
+__device__ __forceinline__ bool mma_mainloop_n(int n, uint8_t* smem, uint64_t* full, uint64_t* empty, int& stage,
+                                               uint32_t& phase, int kb0, int kb1, uint32_t d,
+                                               volatile int* abort_flag) {
+  if constexpr (NM <= BN) {
+    if (n == NM) return mma_mainloop<BN, CHECK, PAIR, NM>(smem, full, empty, stage, phase, kb0, kb1, d, abort_flag);
+    return mma_mainloop_n<BN, CHECK, PAIR, NM + 16>(n, smem, full, empty, stage, phase, kb0, kb1, d, abort_flag);
+  } else {
+    return false;
+  }
+}
+
 // tmB2 (pairs with checks only): B rows for the odd CTA, whose share of a
-// tile's data rows is BD - 128 rather than 128.
+// tile's data rows is BD - 128 rather than 128. tmBt: the data rows of the
+// tail tile column that the compact tail tile needs in this CTA (box
+// p.tail_box rows), when checks are on.
 template <int BN, bool CHECK, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     abft_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmB2, const __grid_constant__ CUtensorMap tmV,
-                     const GemmParams p) {
+                     const __grid_constant__ CUtensorMap tmBt, const GemmParams p) {
   using Cfg = GemmCfg<BN, CHECK, PAIR>;
   constexpr int S = Cfg::kStages;
   constexpr int BD = Cfg::kBD;
@@ -330,6 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmB);
     if (PAIR && CHECK) tma_prefetch_desc(&tmB2);
     if (CHECK) tma_prefetch_desc(&tmV);
+    if (CHECK && p.tail_box > 0) tma_prefetch_desc(&tmBt);
   }
   if (warp == 1) {
     tmem_alloc_g<G>(tmem_slot, Cfg::kTmemCols);
@@ -367,6 +382,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         int mt, nt;
         tile_coords(tile, p, mt, nt);
         const int arow = mt * Cfg::kTileM + static_cast<int>(rank) * kBM;
+        // Compact tail tile: this CTA's data rows come from the tail box (and
+        // the checksum rows follow them); in a pair the odd CTA's rows start
+        // at tail_n / 2 within the tile.
+        const bool tail = p.tail_n != 0 && nt == p.tiles_n - 1;
+        const uint32_t tx = tail ? p.tail_tx : kTx;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
             ok = false;
@@ -376,21 +396,30 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sb = smem + Cfg::kOffB + stage * Cfg::kBBytes;
           if constexpr (PAIR) {
             const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
-            if (rank == 0) mbar_arrive_expect_tx(&full[stage], kTx);
+            if (rank == 0) mbar_arrive_expect_tx(&full[stage], tx);
             tma_load_2d_pair(sa, &tmA, fb, kb * kBK, arow);
             if (!CHECK) {
-              tma_load_2d_pair(sb, &tmB, fb, kb * kBK, nt * BN + static_cast<int>(rank) * Cfg::kBRows);
+              const int half = tail ? p.tail_n / 2 : Cfg::kBRows;
+              tma_load_2d_pair(sb, &tmB, fb, kb * kBK, nt * BN + static_cast<int>(rank) * half);
             } else if (rank == 0) {
               tma_load_2d_pair(sb, &tmB, fb, kb * kBK, nt * BD);
-            } else {
+            } else if (!tail) {
               tma_load_2d_pair(sb, &tmB2, fb, kb * kBK, nt * BD + Cfg::kBRows);
               tma_load_2d_pair(sb + Cfg::kChkRow0 * 128, &tmV, fb, kb * kBK, nt * kChkRows);
+            } else {
+              if (p.tail_box > 0) tma_load_2d_pair(sb, &tmBt, fb, kb * kBK, nt * BD + p.tail_n / 2);
+              tma_load_2d_pair(sb + p.tail_box * 128, &tmV, fb, kb * kBK, nt * kChkRows);
             }
           } else {
-            mbar_arrive_expect_tx(&full[stage], kTx);
+            mbar_arrive_expect_tx(&full[stage], tx);
             tma_load_2d(sa, &tmA, &full[stage], kb * kBK, arow);
-            tma_load_2d(sb, &tmB, &full[stage], kb * kBK, nt * BD);
-            if (CHECK) tma_load_2d(sb + BD * 128, &tmV, &full[stage], kb * kBK, nt * kChkRows);
+            if (!(CHECK && tail)) {
+              tma_load_2d(sb, &tmB, &full[stage], kb * kBK, nt * BD);
+              if (CHECK) tma_load_2d(sb + BD * 128, &tmV, &full[stage], kb * kBK, nt * kChkRows);
+            } else {
+              if (p.tail_box > 0) tma_load_2d(sb, &tmBt, &full[stage], kb * kBK, nt * BD);
+              tma_load_2d(sb + p.tail_box * 128, &tmV, &full[stage], kb * kBK, nt * kChkRows);
+            }
           }
           issued_mask |= 1u << stage;
           issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
@@ -418,7 +447,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && rank == 0) {
-      constexpr uint32_t idesc_full = umma_idesc_bf16(Cfg::kTileM, BN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -429,23 +457,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       while (ok && seg.next(p, tile, kb0, kb1)) {
         int mt, nt;
         tile_coords(tile, p, mt, nt);
-        // A checked tail tile narrower than BD multiplies only its valid data
-        // rows, then the checksum rows separately into columns [BD, BN).
-        // Pairs multiply the full width (the rows past N are zero-filled).
-        const int ncols = min(BD, p.N - nt * BD);
-        const bool split = !PAIR && CHECK && ncols < BD;
-        const uint32_t idesc_data = split ? umma_idesc_bf16(kBM, ncols) : idesc_full;
+        const bool tail = p.tail_n != 0 && nt == p.tiles_n - 1;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
-        // Full tiles keep every instruction descriptor a compile-time
-        // constant; only a checked tail tile takes the runtime-N path.
-        if (!split)
-          ok = mma_mainloop<BN, CHECK, false, PAIR>(smem, full, empty, stage, phase, kb0, kb1, d, idesc_full,
-                                                    abort_flag);
-        else if constexpr (!PAIR)
-          ok = mma_mainloop<BN, CHECK, true, false>(smem, full, empty, stage, phase, kb0, kb1, d, idesc_data,
-                                                    abort_flag);
+        if (!tail)
+          ok = mma_mainloop<BN, CHECK, PAIR, BN>(smem, full, empty, stage, phase, kb0, kb1, d, abort_flag);
+        else
+          ok = mma_mainloop_n<BN, CHECK, PAIR>(p.tail_n, smem, full, empty, stage, phase, kb0, kb1, d, abort_flag);
         if (!ok) break;
         if constexpr (PAIR)
           umma_commit_pair_both(&tfull[acc], 0x3);
@@ -534,10 +553,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         continue;
       }
 
+      // Accumulator column of the expected checksums: BD, or right after the
+      // data columns of a compact tail tile.
+      const int chk_col = (p.tail_n != 0 && nt == p.tiles_n - 1) ? p.N - nt * BD : BD;
       uint32_t chk[kChkRows];
       if (CHECK) {
         __syncwarp();
-        tmem_ld_32x32b_x8(tacc + BD, chk);
+        tmem_ld_32x32b_x8(tacc + static_cast<uint32_t>(chk_col), chk);
         tmem_ld_wait();
       }
       if (kb1 != p.num_kb) {
@@ -577,7 +599,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (CHECK) {
           for (int u = unit + 1; u <= umax; ++u) {
             const int cc = u * G + static_cast<int>(rank);
-            const float* col = p.partials + (static_cast<size_t>(cc) * BN + BD) * kBM + r;
+            const float* col = p.partials + (static_cast<size_t>(cc) * BN + chk_col) * kBM + r;
 #pragma unroll
             for (int e = 0; e < kChkRows; ++e) chk[e] = __float_as_uint(__uint_as_float(chk[e]) + __ldcg(col + e * kBM));
           }
