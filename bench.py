@@ -42,7 +42,7 @@ REF_SAMPLE_ROWS = 512
 def parse_args():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--size", type=int, default=8192, help="M = K = per-GPU N")
@@ -143,8 +143,7 @@ class ClockSampler:
         smax = [num(r[2]) for r in rows if num(r[2]) is not None]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
-        loaded = sorted(sm)[len(sm) // 2:] if sm else []
-        return {"sm_mhz": statistics.median(loaded) if loaded else None,
+        return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(smax) if smax else None, "reasons": reasons, "samples": len(rows),
                 "window": window, "power_w_max": max((num(r[3]) or 0.0) for r in rows)}
 
@@ -242,6 +241,7 @@ def run_ours(args):
     gemm = ShardedAbftGemm(w, c0, mode=N.MODE_DETECT | N.MODE_CORRECT)
     off = ShardedAbftGemm(w, c0, mode=N.MODE_OFF)
     tile_n, _ = gemm._checksums_for(s)
+    tile_m = ops.pick_tile_m(s, n_r, s, tile_n, dev)
 
     # fault-detection sanity outside the timed region: one seeded fault per rank
     from vla_abft_estimate_b200.faults import seeded_fault_positions
@@ -303,17 +303,23 @@ def run_ours(args):
     kernel_ms = sum(s_.elapsed_time(e_) for s_, e_ in zip(starts, kends)) / args.steps
     clean = gemm.global_report()
 
-    # the same kernel with checksums compiled out
+    # overhead: the same kernel with checksums compiled out, launches
+    # interleaved with checked ones so that both see the same clocks
     for _ in range(3):
         off(a, out=out)
     torch.cuda.synchronize()
-    o0, o1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    o0.record()
-    for _ in range(args.steps):
+    n_pair = min(args.steps, 100)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(n_pair)]
+    torch.cuda._sleep(50_000_000)
+    for e in ev:
+        e[0].record()
         off(a, out=out, gather=False)
-    o1.record()
+        e[1].record()
+        gemm(a, out=out, gather=False)
+        e[2].record()
     torch.cuda.synchronize()
-    off_ms = o0.elapsed_time(o1) / args.steps
+    off_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / n_pair
+    chk_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / n_pair
 
     # end to end through the public API with host buffers
     a_h = a.cpu().pin_memory()
@@ -335,19 +341,20 @@ def run_ours(args):
     torch.cuda.synchronize()
     barrier()
     x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = min(args.steps, 50)
     x0.record()
-    for _ in range(args.steps):
+    for _ in range(e2e_steps):
         e2e_step()
     x1.record()
     torch.cuda.synchronize()
-    e2e_ms = x0.elapsed_time(x1) / args.steps
+    e2e_ms = x0.elapsed_time(x1) / e2e_steps
     enc_ms = e_enc0.elapsed_time(e_enc1) / 5
 
     if sampler is not None:
         sampler.stop()
 
     # max over ranks
-    vals = torch.tensor([step_ms, kernel_ms, off_ms, e2e_ms], device=dev, dtype=torch.float64)
+    vals = torch.tensor([step_ms, kernel_ms, off_ms, e2e_ms, chk_ms], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
         ok_t = torch.tensor([1 if detect_ok else 0, 1 if clean.n_faults == 0 else 0], device=dev)
@@ -355,11 +362,16 @@ def run_ours(args):
         detect_ok, clean_ok = bool(ok_t[0].item()), bool(ok_t[1].item())
     else:
         clean_ok = clean.n_faults == 0
-    step_ms, kernel_ms, off_ms, e2e_ms = [float(x) for x in vals.cpu()]
+    step_ms, kernel_ms, off_ms, e2e_ms, chk_ms = [float(x) for x in vals.cpu()]
 
     if rank == 0:
         flops_job = 2.0 * s * n_total * s
-        peak, peak_sus, peak_src = load_peaks()
+        peak_burst, peak_sus, peak_src = load_peaks()
+        # a timed region long enough to reach the power cap is compared with
+        # the sustained cuBLAS figure, a short one with the burst figure
+        timed_s = step_ms * args.steps * 1e-3
+        sustained = timed_s >= 0.1 and peak_sus is not None
+        peak = peak_sus if sustained else peak_burst
         achieved = flops_rank / (kernel_ms * 1e-3) / 1e12
         workload = f"abft_gemm_{s}"
         cpu = None
@@ -379,12 +391,15 @@ def run_ours(args):
             "dtype": "bf16",
             "data": "synthetic (seeded randn * K^-1/2)",
             "config": {"workload": f"square ABFT GEMM {s}x{s}x{s} per GPU; B[{n_total}x{s}] split by columns",
-                       "M": s, "K": s, "N": n_total, "N_per_gpu": n_r, "tile": [128, tile_n],
+                       "M": s, "K": s, "N": n_total, "N_per_gpu": n_r, "tile": [tile_m, tile_n],
+                       "cta_pairs": tile_m == 256,
                        "mode": "detect+locate+correct, weight checksums cached", "parallelism": f"dp{world} (column shards)",
                        "l2": "inputs exceed L2 (A+B_r = %d MB > 126 MB)" % ((s * s + n_r * s) * 2 // 2 ** 20)},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": load_traffic(workload),
-                         "peak_source": f"{peak_src} (burst cuBLAS bf16)",
+                         "peak_source": f"{peak_src} ({'sustained' if sustained else 'burst'} cuBLAS bf16, "
+                                        f"timed region {timed_s:.3f} s)",
+                         "frac_of_burst": achieved / peak_burst,
                          "frac_of_nominal_2250": achieved / NOMINAL_BF16_TFLOPS},
             "cpu_baseline": cpu,
             "e2e": {"value": flops_job / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
@@ -394,7 +409,8 @@ def run_ours(args):
             "gpu_launches": args.steps,
             "clocks": sampler.summary(wall0, wall1) if sampler is not None else None,
             "unchecked_tflops": flops_job / (off_ms * 1e-3) / 1e12,
-            "overhead_pct": 100.0 * (kernel_ms / off_ms - 1.0),
+            "overhead_pct": 100.0 * (chk_ms / off_ms - 1.0),
+            "overhead_method": f"{n_pair} checked and {n_pair} unchecked launches interleaved",
             "encode_ms": enc_ms,
             "fault_check": {"injected_located_corrected": detect_ok, "clean_no_false_positive": clean_ok},
         }

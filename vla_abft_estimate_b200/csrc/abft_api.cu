@@ -187,19 +187,22 @@ int rowdot(const void* X, int64_t ld, int64_t R, int64_t C, const float* vec, fl
 }
 
 // Tile schedule of one launch. Whole-tile (data-parallel) waves first; when
-// the last wave would leave SMs idle, its tiles may instead run stream-K
-// over the first sk_ctas CTAs: each gets an equal share of the tail's k-block
-// iterations, and partial tiles meet in the workspace. More CTAs shorten the
-// tail but cut each tile into more pieces, and every extra piece costs the
-// finisher one partial fold. Estimated times, in k-block steps of one CTA:
-//   data-parallel tail   (full + 1) * num_kb
-//   stream-K over G CTAs full * num_kb + ceil(W / G) + kSkStore + kSkFold * (pieces - 1)
-// with W = rem * num_kb and pieces the most CTA ranges one tile can meet.
+// the last wave would leave units idle, its tiles may instead run stream-K
+// over the first sk_ctas units: each gets an equal share of those tiles'
+// k-block iterations, and partial tiles meet in the workspace. More units
+// shorten the tail but cut each tile into more pieces, and every extra piece
+// costs the finisher one partial fold. Estimated times, in k-block steps of
+// one unit:
+//   data-parallel tail   (waves + 1) * num_kb
+//   stream-K over G      waves * num_kb + ceil(W / G) + kSkStore + kSkFold * (pieces - 1)
+// with W = rem * num_kb and pieces the most unit ranges one tile can meet.
+// A compact tail tile counts as a full one: its narrow MMA is cheap, but it
+// streams the same A slices through the load pipeline.
 constexpr double kSkStore = 4.0;  // contributor: partial tile to global memory, flag
 constexpr double kSkFold = 3.0;   // finisher: fold one partial tile into TMEM
 
 struct Schedule {
-  int grid;
+  int grid;  // units
   int dp_tiles;
   int sk;
   int sk_ctas;
@@ -207,22 +210,31 @@ struct Schedule {
   double est;  // estimated duration in k-block steps
 };
 
-Schedule make_schedule(int64_t tiles, int num_kb, int sms) {
+// MMA width of the last tile column's compact tile (its data rows, then with
+// checks the 8 checksum rows), or 0 when that column needs no narrower MMA.
+int tail_width(int64_t N, int bd, int bn, bool check) {
+  const int64_t tiles_n = cdiv(N, bd);
+  const int ncols = static_cast<int>(N - (tiles_n - 1) * bd);
+  const int tn = (ncols + (check ? kChkRows : 0) + 15) / 16 * 16;
+  return (ncols < bd && tn < bn) ? tn : 0;
+}
+
+Schedule make_schedule(int64_t tiles, int num_kb, int units) {
   Schedule s;
   s.sk = 0;
   s.sk_ctas = 0;
   s.sk_iters = 0;
   s.dp_tiles = static_cast<int>(tiles);
-  s.grid = static_cast<int>(tiles < sms ? tiles : sms);
-  s.est = static_cast<double>(cdiv(tiles, sms)) * num_kb;
-  const int64_t full = tiles / sms, rem = tiles % sms;
+  s.grid = static_cast<int>(tiles < units ? tiles : units);
+  s.est = static_cast<double>(cdiv(tiles, units)) * num_kb;
+  const int64_t waves = tiles / units, rem = tiles % units;
   if (rem == 0 || num_kb < 2) return s;
   const int64_t w = rem * num_kb;
   int64_t best_g = 0;
-  for (int64_t g = rem + 1; g <= sms && g <= w; ++g) {
-    const int64_t lmin = w / g;  // shortest CTA range
+  for (int64_t g = rem + 1; g <= units && g <= w; ++g) {
+    const int64_t lmin = w / g;  // shortest unit range
     const int64_t pieces = cdiv(num_kb - 1, lmin) + 1;
-    const double t = static_cast<double>(full * num_kb + cdiv(w, g)) + kSkStore + kSkFold * (pieces - 1);
+    const double t = static_cast<double>(waves * num_kb + cdiv(w, g)) + kSkStore + kSkFold * (pieces - 1);
     if (t < s.est) {
       s.est = t;
       best_g = g;
@@ -232,9 +244,15 @@ Schedule make_schedule(int64_t tiles, int num_kb, int sms) {
   s.sk = 1;
   s.sk_ctas = static_cast<int>(best_g);
   s.sk_iters = w;
-  s.dp_tiles = static_cast<int>(full * sms);
-  s.grid = full > 0 ? sms : static_cast<int>(best_g);
+  s.dp_tiles = static_cast<int>(waves * units);
+  s.grid = waves > 0 ? units : static_cast<int>(best_g);
   return s;
+}
+
+// Schedule of an M x N x K launch with tile_m x bn tiles (bd data columns)
+// over `units` units.
+Schedule schedule_for(int64_t M, int64_t N, int64_t K, int tile_m, int bd, int units) {
+  return make_schedule(cdiv(M, tile_m) * cdiv(N, bd), static_cast<int>(cdiv(K, kBK)), units);
 }
 
 // A CTA pair runs a 128 x 256 share of a tile per SM about this much faster
@@ -243,17 +261,16 @@ constexpr double kPairSpeedup = 1.10;
 
 // Estimated time (single-CTA k-block steps) of an M x N x K launch with
 // 128- or 256-row tiles (256: CTA pairs over `units` pairs).
-double est_time(int64_t M, int64_t N, int64_t K, int bd, int tile_m, int units) {
-  const int64_t tiles = cdiv(M, tile_m) * cdiv(N, bd);
-  const double t = make_schedule(tiles, static_cast<int>(cdiv(K, kBK)), units).est;
+double est_time(int64_t M, int64_t N, int64_t K, int bn, bool check, int tile_m, int units) {
+  const int bd = check ? bn - kChkRows : bn;
+  const double t = schedule_for(M, N, K, tile_m, bd, units).est;
   return tile_m == 256 ? t / kPairSpeedup : t;
 }
 
 int pick_tile_m(int64_t M, int64_t N, int64_t K, int sms, uint32_t mode, int bn) {
   if (bn != 256 || sms < 2 || M <= 0 || N <= 0 || K <= 0) return 128;
   const bool check = (mode & (ABFT_MODE_DETECT | ABFT_MODE_CORRECT)) != 0;
-  const int bd = check ? bn - kChkRows : bn;
-  return est_time(M, N, K, bd, 256, sms / 2) < est_time(M, N, K, bd, 128, sms) ? 256 : 128;
+  return est_time(M, N, K, bn, check, 256, sms / 2) < est_time(M, N, K, bn, check, 128, sms) ? 256 : 128;
 }
 
 // Everything about a launch that depends only on the arguments and the
@@ -283,7 +300,7 @@ int make_plan(const abft_gemm_args* a, int dev, int sms, Plan* pl) {
     pl->units = sms / 2;
   else
     pl->units = pl->check ? pair_units_on<true>(dev, sms) : pair_units_on<false>(dev, sms);
-  pl->sch = make_schedule(pl->tiles, pl->num_kb, pl->units);
+  pl->sch = schedule_for(a->M, a->N, a->K, pl->tile_m, pl->bd, pl->units);
   pl->grid = pl->sch.grid * (pl->pair ? 2 : 1);
 
   size_t off = 0;
@@ -388,15 +405,12 @@ int32_t abft_pick_tile_n(int64_t M, int64_t N, int64_t K, int32_t num_sms, uint3
   if (num_sms <= 0) num_sms = 148;
   if (M <= 0 || N <= 0 || K <= 0) return 256;
   const bool check = (mode & (ABFT_MODE_DETECT | ABFT_MODE_CORRECT)) != 0;
-  const int num_kb = static_cast<int>(cdiv(K, kBK));
   double best_cost = 0.0;
   int32_t best = 256;
   for (int32_t bn : {256, 128}) {
-    const int64_t d = check ? bn - kChkRows : bn;
-    const int64_t tiles = cdiv(M, kBM) * cdiv(N, d);
-    double cost = make_schedule(tiles, num_kb, num_sms).est * (bn == 256 ? 1.0 : 0.8);
+    double cost = est_time(M, N, K, bn, check, 128, num_sms) * (bn == 256 ? 1.0 : 0.8);
     if (bn == 256 && num_sms >= 2) {
-      const double tp = est_time(M, N, K, static_cast<int>(d), 256, num_sms / 2);
+      const double tp = est_time(M, N, K, bn, check, 256, num_sms / 2);
       if (tp < cost) cost = tp;
     }
     if (bn == 256 || cost < best_cost) {
@@ -533,8 +547,8 @@ int abft_gemm_bf16(const abft_gemm_args* a, void* stream) {
   CUtensorMap tmBt = tmA;  // placeholder unless a tail box is needed
   {
     const int ncols = static_cast<int>(a->N - static_cast<int64_t>(p.tiles_n - 1) * bd);
-    const int tn = (ncols + (check ? kChkRows : 0) + 15) / 16 * 16;
-    if (ncols < bd && tn < bn) {
+    const int tn = tail_width(a->N, bd, bn, check);
+    if (tn != 0) {
       const uint32_t a_bytes = static_cast<uint32_t>(kBM * kBK * 2);
       const uint32_t row_bytes = static_cast<uint32_t>(kBK * 2);  // one B row of one k-block
       p.tail_n = tn;
@@ -554,6 +568,10 @@ int abft_gemm_bf16(const abft_gemm_args* a, void* stream) {
       }
     }
   }
+
+  // Tile order: full tiles first, then the tail column's (one per tile row).
+  p.tiles_n_full = p.tiles_n - (p.tail_n ? 1 : 0);
+  p.full_tiles = p.tiles_m * p.tiles_n_full;
 
   const Schedule& sch = ws.sch;
   const int grid = ws.grid;

@@ -103,11 +103,13 @@ struct GemmParams {
   abft_report* report;
   int capacity;
   float* tile_sumc;  // ABFT_MODE_REF: [num_tiles][8] partial sums of the stored outputs
+  // Tile order: the full tiles [0, full_tiles) in grouped raster order over
+  // tiles_n_full columns, then the tail column's tiles (one per tile row).
+  int full_tiles, tiles_n_full;
   // Hybrid schedule: tiles [0, dp_tiles) are data-parallel (whole tiles,
-  // blockIdx.x + j*gridDim.x); with sk != 0 the remaining tiles are
-  // stream-K: CTA c < G owns k-block iterations [c*W/G, (c+1)*W/G) of the
-  // W = sk_iters = (num_tiles - dp_tiles) * num_kb that follow,
-  // G = sk_ctas <= gridDim.x (fewer CTAs, fewer pieces per tile).
+  // unit + j*units); with sk != 0 the remaining tiles are stream-K: unit
+  // c < G owns k-block iterations [c*W/G, (c+1)*W/G) of the W = sk_iters
+  // that follow, G = sk_ctas <= units (fewer units, fewer pieces per tile).
   int dp_tiles;
   int sk;
   int sk_ctas;  // stream-K units: CTAs, or CTA pairs
@@ -137,7 +139,8 @@ struct SegmentIter {
     end = base + sk_begin(p, unit + 1);
   }
   // First stream-K iteration of unit c, relative to the stream-K region
-  // (units from sk_ctas on own none).
+  // (units from sk_ctas on own none). Every range is non-empty: the host
+  // keeps sk_ctas <= sk_iters.
   __device__ __forceinline__ static int64_t sk_begin(const GemmParams& p, int c) {
     if (c >= p.sk_ctas) return p.sk_iters;
     return (static_cast<int64_t>(c) * p.sk_iters) / p.sk_ctas;
@@ -194,7 +197,12 @@ __device__ __forceinline__ bool wait_flag(const int* f, volatile int* abort_flag
 }
 
 __device__ __forceinline__ void tile_coords(int tile, const GemmParams& p, int& mt, int& nt) {
-  const int group = p.group_m * p.tiles_n;
+  if (tile >= p.full_tiles) {
+    mt = tile - p.full_tiles;
+    nt = p.tiles_n - 1;
+    return;
+  }
+  const int group = p.group_m * p.tiles_n_full;
   const int g = tile / group;
   const int first_m = g * p.group_m;
   const int gm = min(p.tiles_m - first_m, p.group_m);
