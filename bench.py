@@ -17,6 +17,10 @@ memory every step and the gathered fault reports read back.
 ``--impl reference`` times the reference's CPU path (torch.matmul + the
 python-backend corner check, restated in oracle/ref_port.py) on a row sample
 of the same workload with all host threads.
+
+``--model qwen2-7b`` times a Qwen2-7B-shaped prefill of 512 tokens (batch 1,
+random init N(0, 0.02), every nn.Linear protected through AbftInjector's
+fused path) against plain torch and against the same kernel with checks off.
 """
 from __future__ import annotations
 
@@ -50,6 +54,9 @@ def parse_args():
     ap.add_argument("--sweep", action="store_true",
                     help="one JSON line per shape of the square sweep, the 512x4096x4096 case and the "
                          "Qwen2-7B layer GEMMs: checked / unchecked TFLOP/s and 1- and 4-fault outcomes")
+    ap.add_argument("--model", choices=["qwen2-7b"], default=None,
+                    help="prefill-512 tokens/s of a random-init Qwen2-7B-shaped decoder with every linear "
+                         "ABFT-protected (one JSON line)")
     ap.add_argument("--profile-case", choices=["off", "check", "both"], default=None,
                     help="only run two rounds of the fused GEMM (unchecked then checked for 'both') "
                          "on randn inputs, for an ncu capture")
@@ -518,8 +525,218 @@ def sweep(args):
         del a, w, out, ref, cks
 
 
+# ------------------------------------------------------------------ model path
+QWEN2_7B = dict(hidden=3584, inter=18944, layers=28, heads=28, kv_heads=4, head_dim=128, vocab=152064,
+                rope_theta=1000000.0, eps=1e-6)
+
+
+def build_qwen2(cfg, device, seed=0):
+    """Qwen2-style decoder: RMSNorm, fused QKV (with bias) + RoPE + GQA
+    attention (SDPA), SwiGLU MLP with fused gate+up, tied-free lm_head.
+    Every projection is an nn.Linear, so F.linear hooks see all of them."""
+    import torch
+    import torch.nn as nn
+    import torch.nn.functional as F
+
+    class RMSNorm(nn.Module):
+        def __init__(self, h):
+            super().__init__()
+            self.weight = nn.Parameter(torch.ones(h))
+
+        def forward(self, x):
+            xf = x.float()
+            return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + cfg["eps"])).to(x.dtype) * self.weight
+
+    def rope(x, cos, sin):  # x [T, H, D]
+        x1, x2 = x[..., : x.shape[-1] // 2], x[..., x.shape[-1] // 2:]
+        return x * cos + torch.cat((-x2, x1), dim=-1) * sin
+
+    class Layer(nn.Module):
+        def __init__(self):
+            super().__init__()
+            h, nh, nkv, hd, it = cfg["hidden"], cfg["heads"], cfg["kv_heads"], cfg["head_dim"], cfg["inter"]
+            self.ln1, self.ln2 = RMSNorm(h), RMSNorm(h)
+            self.qkv = nn.Linear(h, (nh + 2 * nkv) * hd, bias=True)
+            self.o = nn.Linear(nh * hd, h, bias=False)
+            self.gate_up = nn.Linear(h, 2 * it, bias=False)
+            self.down = nn.Linear(it, h, bias=False)
+
+        def forward(self, x, cos, sin):
+            nh, nkv, hd = cfg["heads"], cfg["kv_heads"], cfg["head_dim"]
+            t = x.shape[0]
+            q, k, v = self.qkv(self.ln1(x)).split([nh * hd, nkv * hd, nkv * hd], dim=-1)
+            q = rope(q.view(t, nh, hd), cos, sin).transpose(0, 1)
+            k = rope(k.view(t, nkv, hd), cos, sin).transpose(0, 1)
+            v = v.view(t, nkv, hd).transpose(0, 1)
+            a = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
+            x = x + self.o(a.transpose(0, 1).reshape(t, nh * hd))
+            g, u = self.gate_up(self.ln2(x)).chunk(2, dim=-1)
+            return x + self.down(F.silu(g) * u)
+
+    class Model(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.embed = nn.Embedding(cfg["vocab"], cfg["hidden"])
+            self.layers = nn.ModuleList([Layer() for _ in range(cfg["layers"])])
+            self.norm = RMSNorm(cfg["hidden"])
+            self.lm_head = nn.Linear(cfg["hidden"], cfg["vocab"], bias=False)
+
+        def forward(self, ids):
+            t = ids.shape[0]
+            hd = cfg["head_dim"]
+            inv = 1.0 / (cfg["rope_theta"] ** (torch.arange(0, hd, 2, device=ids.device).float() / hd))
+            ang = torch.outer(torch.arange(t, device=ids.device).float(), inv)
+            ang = torch.cat((ang, ang), dim=-1)[:, None, :]
+            cos, sin = ang.cos().to(torch.bfloat16), ang.sin().to(torch.bfloat16)
+            x = self.embed(ids)
+            for layer in self.layers:
+                x = layer(x, cos, sin)
+            return self.lm_head(self.norm(x))
+
+    torch.manual_seed(seed)
+    with torch.device(device):
+        model = Model().to(torch.bfloat16)
+    with torch.no_grad():
+        for mod in model.modules():
+            if isinstance(mod, (nn.Linear, nn.Embedding)):
+                mod.weight.normal_(0.0, 0.02)
+                if getattr(mod, "bias", None) is not None:
+                    mod.bias.zero_()
+    return model.eval()
+
+
+def cpu_model_baseline(cfg, tokens, seconds):
+    """Reference flow on the host CPU for one decoder layer's four linears
+    (torch.matmul + corner check, oracle/ref_port.py), scaled to a full
+    prefill: layers x (that time) + the lm_head sample's time."""
+    import torch
+
+    from oracle.ref_port import time_reference_sample
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    h, it, nh, nkv, hd, V = (cfg["hidden"], cfg["inter"], cfg["heads"], cfg["kv_heads"], cfg["head_dim"],
+                             cfg["vocab"])
+    shapes = [(h, (nh + 2 * nkv) * hd), (nh * hd, h), (h, 2 * it), (it, h)]
+    per_layer = 0.0
+    t_end = time.perf_counter() + seconds
+    for k, n in shapes:
+        per, _, _ = time_reference_sample(tokens, k, n, max_reps=1)
+        per_layer += per
+    # lm_head: time a 1/16 column slice, scale by 16
+    per_head, _, _ = time_reference_sample(tokens, h, V // 16, max_reps=1)
+    total = per_layer * cfg["layers"] + per_head * 16
+    del t_end
+    return {"value": tokens / total, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"one decoder layer's 4 linears + 1/16 of lm_head at M={tokens} through the reference "
+                      f"flow (torch.matmul + corner check, oracle/ref_port.py), scaled to "
+                      f"{cfg['layers']} layers + lm_head; attention and norms excluded"}
+
+
+def run_model(args):
+    import torch
+
+    from vla_abft_estimate_b200.abft import AbftConfig, AbftInjector, AbftStatsCollector, CheapSumChecker
+
+    cfg = QWEN2_7B
+    tokens = 512
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    model = build_qwen2(cfg, dev)
+    ids = torch.randint(0, cfg["vocab"], (tokens,), device=dev, generator=torch.Generator(device=dev).manual_seed(7))
+    reps = max(args.steps, 3) if args.steps < 300 else 10
+
+    def timed_forward(ctx_factory):
+        times = []
+        out = None
+        with torch.inference_mode():
+            for i in range(max(args.warmup, 2) + reps):
+                ctx = ctx_factory()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                torch.cuda.synchronize()
+                e0.record()
+                with ctx:
+                    out = model(ids)
+                e1.record()
+                torch.cuda.synchronize()
+                if i >= max(args.warmup, 2):
+                    times.append(e0.elapsed_time(e1))
+        return statistics.median(times), out, ctx
+
+    import contextlib
+
+    # one injector per leg, reused across repetitions (its weight checksum
+    # cache is what a serving process keeps); flush() at exit reads the
+    # deferred reports once per forward
+    stats_chk = AbftStatsCollector()
+    cfg_chk = AbftConfig(enable=True, checker_backend="b200", detect_only=False)
+    inj_chk = AbftInjector(cfg_chk, CheapSumChecker(cfg_chk), stats_chk, defer_reports=True)
+    stats_off = AbftStatsCollector()
+    cfg_off = AbftConfig(enable=True, check_enable=False, checker_backend="b200")
+    inj_off = AbftInjector(cfg_off, CheapSumChecker(cfg_off), stats_off, defer_reports=True)
+
+    t_torch, ref_logits, _ = timed_forward(contextlib.nullcontext)
+    t_off, off_logits, _ = timed_forward(lambda: inj_off)
+    t_chk, chk_logits, _ = timed_forward(lambda: inj_chk)
+    summ = stats_chk.export_summary()
+    n_checks = summ["abft"]["checks_total"]
+
+    # fault leg: every linear of one forward may be hit (probability 0.05),
+    # each fault +1.0 on the fp32 accumulator; detect + locate + correct
+    stats_f = AbftStatsCollector()
+    cfg_f = AbftConfig(enable=True, checker_backend="b200", detect_only=False, inject_fault=True,
+                       inject_probability=0.05, inject_magnitude=1.0, seed=11)
+    inj_f = AbftInjector(cfg_f, CheapSumChecker(cfg_f), stats_f, defer_reports=True)
+    with torch.inference_mode(), inj_f:
+        f_logits = model(ids)
+    torch.cuda.synchronize()
+    fs = stats_f.export_summary()
+    flt = {k: v for k, v in fs["abft"]["faults"].items() if k != "located"}
+    max_diff = (f_logits.float() - chk_logits.float()).abs().max().item()
+    logits_scale = chk_logits.float().abs().max().item()
+
+    linear_flops = 0.0
+    h, it, nh, nkv, hd, V = (cfg["hidden"], cfg["inter"], cfg["heads"], cfg["kv_heads"], cfg["head_dim"],
+                             cfg["vocab"])
+    for k, n in [(h, (nh + 2 * nkv) * hd), (nh * hd, h), (h, 2 * it), (it, h)]:
+        linear_flops += 2.0 * tokens * k * n * cfg["layers"]
+    linear_flops += 2.0 * tokens * h * V
+    cpu = None if args.no_cpu_baseline else cpu_model_baseline(cfg, tokens, 20.0)
+    line = {
+        "metric": "Qwen2-7B prefill-512 tokens/s (every linear ABFT-protected)",
+        "value": tokens / (t_chk * 1e-3), "unit": "tokens/s", "n_gpus": 1, "steps": reps,
+        "warmup": max(args.warmup, 2), "ms_per_step": t_chk, "higher_is_better": True, "scaling": "none",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random init N(0,0.02), random token ids)",
+        "config": {"workload": "Qwen2-7B-shaped decoder prefill, batch 1, 512 tokens", **cfg,
+                   "fused_shapes": "qkv 3584->4608 (bias), o 3584->3584, gate_up 3584->37888, down 18944->3584, "
+                                   "lm_head 3584->152064",
+                   "abft": "b200 backend: one fused GEMM + row-checksum check + correct per linear, "
+                           "reports deferred to one read per forward"},
+        "torch_tokens_per_s": tokens / (t_torch * 1e-3),
+        "unchecked_kernel_tokens_per_s": tokens / (t_off * 1e-3),
+        "ms": {"torch": t_torch, "b200_unchecked": t_off, "b200_abft": t_chk},
+        "overhead_vs_torch_pct": 100.0 * (t_chk / t_torch - 1.0),
+        "overhead_vs_unchecked_pct": 100.0 * (t_chk / t_off - 1.0),
+        "linear_tflops_abft": linear_flops / (t_chk * 1e-3) / 1e12,
+        "checked_linears_per_forward": n_checks // (reps + max(args.warmup, 2)),
+        "clean_false_positives": summ["abft"]["faults"]["detected_total"],
+        "fault_leg": {"injected": fs["fault_injection"]["injections_total"],
+                      "detected_injections": fs["fault_injection"]["detected_injections_total"],
+                      "faults": flt,
+                      "max_abs_logit_diff_vs_clean": max_diff, "max_abs_logit": logits_scale},
+        "logits_max_abs_diff_torch_vs_abft": (ref_logits.float() - chk_logits.float()).abs().max().item(),
+        "cpu_baseline": cpu,
+        "reference_published": {"tokens_per_s_no_abft": 7217, "tokens_per_s_abft_python": 5909,
+                                "source": "pytorch/baseline_7b_prefill512.json:44, "
+                                          "pytorch/abft_7b_prefill512_nsys.json:44 (GPU unrecorded)"},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
+    if args.model:
+        run_model(args)
+        return
     if args.sweep:
         sweep(args)
         return

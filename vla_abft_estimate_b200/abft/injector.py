@@ -87,6 +87,43 @@ class WeightChecksumCache:
         self._d.clear()
 
 
+class _ReportArena:
+    """Device slots for the reports of deferred fused linears.
+
+    Each fused call writes its report into the next slot (the kernel resets
+    the header on the call's stream); ``drain()`` copies every used slot of a
+    chunk to the host in one transfer. Chunks are added when one fills.
+    """
+
+    def __init__(self, capacity: int, device: torch.device, slots: int = 256):
+        self.capacity = capacity
+        self.device = device
+        self.slot_bytes = (int(N.lib().abft_report_bytes(capacity)) + 255) // 256 * 256
+        self.slots = slots
+        self.chunks: List[torch.Tensor] = []
+        self.used = 0  # slots taken in the last chunk
+
+    def take(self) -> ops.ReportBuffer:
+        if not self.chunks or self.used == self.slots:
+            self.chunks.append(torch.empty(self.slots * self.slot_bytes, dtype=torch.uint8, device=self.device))
+            self.used = 0
+        off = self.used * self.slot_bytes
+        self.used += 1
+        return ops.ReportBuffer(self.capacity, tensor=self.chunks[-1][off:off + self.slot_bytes])
+
+    def drain(self) -> List[N.FaultReport]:
+        reports: List[N.FaultReport] = []
+        for i, chunk in enumerate(self.chunks):
+            n = self.slots if i < len(self.chunks) - 1 else self.used
+            host = chunk[: n * self.slot_bytes].cpu().numpy().tobytes()
+            reports.extend(N.FaultReport.from_bytes(host[j * self.slot_bytes:(j + 1) * self.slot_bytes])
+                           for j in range(n))
+        # keep the first chunk for the next forward
+        self.chunks = self.chunks[:1]
+        self.used = 0
+        return reports
+
+
 class AbftInjector(AbstractContextManager):
     def __init__(self, cfg: AbftConfig, checker: AbftChecker, stats: AbftStatsCollector,
                  defer_reports: bool = False):
@@ -101,7 +138,9 @@ class AbftInjector(AbstractContextManager):
         self._orig_matmul: Optional[Callable[..., torch.Tensor]] = None
         self._orig_bmm: Optional[Callable[..., torch.Tensor]] = None
         self._dump_done: bool = False
-        self._pending: List[Tuple[ops.ReportBuffer, str, str, str, bool]] = []
+        self._pending: List[Tuple[int, str, str, str, bool]] = []
+        self._arenas: dict = {}
+        self._tile_n: dict = {}
 
     # ------------------------------------------------------------------ context
     def __enter__(self) -> "AbftInjector":
@@ -128,14 +167,18 @@ class AbftInjector(AbstractContextManager):
         return None
 
     def flush(self) -> None:
-        """Record every deferred fused-linear report (one host sync)."""
+        """Record every deferred fused-linear report (one copy per device)."""
         pending, self._pending = self._pending, []
+        if not pending:
+            return
+        reports = {dev: iter(arena.drain()) for dev, arena in self._arenas.items()}
         saved = self.stats.current_phase
         try:
-            for rep_buf, op_name, phase, shape_key, injected in pending:
+            for dev, op_name, phase, shape_key, injected in pending:
+                rep = next(reports[dev])
                 self.stats.current_phase = phase
-                self.stats.record_check(op_name=op_name, shape_key=shape_key,
-                                        result=result_from_report(rep_buf.read()), injected=injected)
+                self.stats.record_check(op_name=op_name, shape_key=shape_key, result=result_from_report(rep),
+                                        injected=injected)
         finally:
             self.stats.current_phase = saved
 
@@ -252,10 +295,22 @@ class AbftInjector(AbstractContextManager):
         mode = N.MODE_OFF
         if check:
             mode = N.MODE_DETECT | (0 if self.cfg.detect_only else N.MODE_CORRECT)
-        tile_n = ops.pick_tile_n(m, n, k, x2.device, mode)
+        tkey = (m, n, k, mode, x2.device.index)
+        tile_n = self._tile_n.get(tkey)
+        if tile_n is None:
+            tile_n = self._tile_n[tkey] = ops.pick_tile_n(m, n, k, x2.device, mode)
         cks = self.checksums.get(weight, tile_n) if check else None
         inject = [(idx // n, idx % n, float(self.cfg.inject_magnitude))] if injected else None
-        rep = ops.ReportBuffer(self.cfg.report_capacity, x2.device) if check else None
+        rep = None
+        if check:
+            if self.defer_reports and self.cfg.record_enable:
+                # one arena per device: reports of one device are drained in call order
+                arena = self._arenas.get(x2.device.index)
+                if arena is None:
+                    arena = self._arenas[x2.device.index] = _ReportArena(self.cfg.report_capacity, x2.device)
+                rep = arena.take()
+            else:
+                rep = ops.ReportBuffer(self.cfg.report_capacity, x2.device)
         out, rep = ops.abft_gemm(x2, weight, None if bias is None else bias.contiguous(), mode=mode, tile_n=tile_n,
                                  thr_scale=self.cfg.thr_scale, thr_abs=self.cfg.thr_abs, checksums=cks,
                                  inject=inject, report=rep)
@@ -263,7 +318,7 @@ class AbftInjector(AbstractContextManager):
             shape_key = f"A{tuple(x2.shape)}_B{tuple(b2.shape)}_C{tuple(c_shape)}"
             if self.cfg.record_enable:
                 if self.defer_reports:
-                    self._pending.append((rep, "linear", self.stats.current_phase, shape_key, injected))
+                    self._pending.append((x2.device.index, "linear", self.stats.current_phase, shape_key, injected))
                 else:
                     self.stats.record_check(op_name="linear", shape_key=shape_key,
                                             result=result_from_report(rep.read()), injected=injected)

@@ -12,6 +12,7 @@ Functions
 from __future__ import annotations
 
 import ctypes
+import functools
 import math
 from typing import Optional, Sequence, Tuple
 
@@ -48,10 +49,15 @@ def _require_bf16_cuda(name: str, t: torch.Tensor, dim: int) -> None:
 class ReportBuffer:
     """Device buffer holding one ``abft_report`` with ``capacity`` records."""
 
-    def __init__(self, capacity: int = DEFAULT_CAPACITY, device: Optional[torch.device] = None):
+    def __init__(self, capacity: int = DEFAULT_CAPACITY, device: Optional[torch.device] = None,
+                 tensor: Optional[torch.Tensor] = None):
         self.capacity = int(capacity)
         nbytes = int(N.lib().abft_report_bytes(self.capacity))
-        self.tensor = torch.zeros(nbytes, dtype=torch.uint8, device=device or torch.device("cuda"))
+        if tensor is None:
+            tensor = torch.zeros(nbytes, dtype=torch.uint8, device=device or torch.device("cuda"))
+        elif tensor.dtype != torch.uint8 or tensor.numel() < nbytes or tensor.data_ptr() % 16:
+            raise ValueError(f"a report of capacity {capacity} needs {nbytes} 16-byte aligned bytes")
+        self.tensor = tensor
 
     def data_ptr(self) -> int:
         return self.tensor.data_ptr()
@@ -65,17 +71,28 @@ class ReportBuffer:
         pinned.copy_(self.tensor[: N.REPORT_HEADER_BYTES], non_blocking=True)
 
 
+@functools.lru_cache(maxsize=None)
+def _sm_count(index: int) -> int:
+    return torch.cuda.get_device_properties(index).multi_processor_count
+
+
+def _device_index(device: Optional[torch.device]) -> int:
+    if device is None or device.index is None:
+        return torch.cuda.current_device()
+    return device.index
+
+
 def pick_tile_n(m: int, n: int, k: int, device: Optional[torch.device] = None,
                 mode: int = N.MODE_DETECT | N.MODE_CORRECT) -> int:
     """Tile width the library would pick for an m x n x k GEMM in ``mode``."""
-    sms = torch.cuda.get_device_properties(device or torch.device("cuda")).multi_processor_count
+    sms = _sm_count(_device_index(device))
     return int(N.lib().abft_pick_tile_n(int(m), int(n), int(k), int(sms), int(mode)))
 
 
 def pick_tile_m(m: int, n: int, k: int, tile_n: int, device: Optional[torch.device] = None,
                 mode: int = N.MODE_DETECT | N.MODE_CORRECT) -> int:
     """Tile height (128, or 256 = one 2-CTA pair per tile) the library would pick."""
-    sms = torch.cuda.get_device_properties(device or torch.device("cuda")).multi_processor_count
+    sms = _sm_count(_device_index(device))
     return int(N.lib().abft_pick_tile_m(int(m), int(n), int(k), int(sms), int(mode), int(tile_n)))
 
 
