@@ -84,9 +84,11 @@ typedef struct abft_fault_record {
   uint32_t flags;
 } abft_fault_record;
 
-/* Fault report, device-resident, caller-allocated with abft_report_bytes().
- * abft_gemm_bf16 / abft_check_only reset the header on the call's stream
- * before the kernel runs, so the caller need not zero it. */
+/* Fault report, device-resident, caller-allocated with abft_report_bytes(),
+ * 16-byte aligned. abft_gemm_bf16 / abft_check_only reset the header on the
+ * call's stream (the fused kernel resets it itself and publishes launch_tag,
+ * a value unique to the launch, once the header is valid), so the caller
+ * need not zero it. */
 typedef struct abft_report {
   uint32_t status;       /* ABFT_STATUS_* bits                               */
   uint32_t n_faults;     /* mismatching (row, tile) segments, all of them     */
@@ -101,7 +103,8 @@ typedef struct abft_report {
   float abs_err;         /* ABFT_MODE_REF: |corner - sum_c|                    */
   float rel_err;         /* ABFT_MODE_REF: abs_err / max(|sum_c|, 1)           */
   int32_t ref_ok;        /* ABFT_MODE_REF: 1 pass, 0 fail; -1 not evaluated     */
-  uint32_t reserved[3];
+  uint32_t reserved;
+  uint64_t launch_tag;   /* fused GEMM: tag of the launch that wrote the header */
   /* abft_fault_record records[capacity] follows (64-byte header). */
 } abft_report;
 
@@ -146,9 +149,10 @@ const char* abft_status_string(int status);
 size_t abft_report_bytes(int32_t capacity);
 
 /* Tile width (256 or 128) the library picks for an M x N x K GEMM in `mode`
- * when tile_n == 0: the shorter estimated schedule over num_sms (whole-tile
- * waves, with stream-K for a last wave that would leave SMs idle), a
- * 128-wide tile counted as 0.8 of a 256-wide one. */
+ * when tile_n == 0: the shorter estimated time over num_sms (whole-tile
+ * waves, with stream-K for a last wave that would leave SMs idle; a 128-wide
+ * tile's k-block counted as 0.6 of a 256-wide one; for 256-wide tiles the
+ * better of 128-row tiles and CTA pairs). */
 int32_t abft_pick_tile_n(int64_t M, int64_t N, int64_t K, int32_t num_sms, uint32_t mode);
 
 /* Tile height (128, or 256 = CTA pairs) the library picks when tile_m == 0,

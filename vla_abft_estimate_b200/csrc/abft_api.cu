@@ -7,7 +7,9 @@
 #include <cuda_runtime.h>
 #include <math.h>
 
+#include <atomic>
 #include <mutex>
+#include <random>
 
 #include "aux_kernels.cuh"
 #include "gemm_kernel.cuh"
@@ -141,6 +143,21 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
+// A value unique to one fused launch: stream-K flags and report->launch_tag
+// carry it, so neither needs clearing before the launch (a stale value from
+// another launch differs). Distinct for 2^64 calls in a process (an odd
+// multiplier makes the counter map one-to-one); the random salt separates
+// processes; never 0, the content of zeroed memory.
+uint64_t next_launch_nonce() {
+  static std::atomic<uint64_t> counter{0};
+  static const uint64_t salt = [] {
+    std::random_device rd;
+    return (static_cast<uint64_t>(rd()) << 32) ^ static_cast<uint64_t>(rd());
+  }();
+  const uint64_t n = salt + (counter.fetch_add(1, std::memory_order_relaxed) + 1) * 0x9E3779B97F4A7C15ull;
+  return n != 0 ? n : 1;
+}
+
 int launch_status() {
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? ABFT_OK : ABFT_ERR_CUDA;
@@ -194,12 +211,22 @@ int rowdot(const void* X, int64_t ld, int64_t R, int64_t C, const float* vec, fl
 // costs the finisher one partial fold. Estimated times, in k-block steps of
 // one unit:
 //   data-parallel tail   (waves + 1) * num_kb
-//   stream-K over G      waves * num_kb + ceil(W / G) + kSkStore + kSkFold * (pieces - 1)
+//   stream-K over G      waves * num_kb + ceil(W / G) + store + fold * (pieces - 1)
 // with W = rem * num_kb and pieces the most unit ranges one tile can meet.
 // A compact tail tile counts as a full one: its narrow MMA is cheap, but it
 // streams the same A slices through the load pipeline.
-constexpr double kSkStore = 4.0;  // contributor: partial tile to global memory, flag
-constexpr double kSkFold = 3.0;   // finisher: fold one partial tile into TMEM
+// store: a contributor writes its partial tile and publishes the flag, and
+// the finisher sees it; fold: the finisher adds one partial into TMEM.
+// Measured in microseconds; one k-block step of a 256-wide tile takes about
+// kKbUs256 (half that for a 128-wide tile).
+constexpr double kSkStoreUs = 3.0;
+constexpr double kSkFoldUs = 1.0;
+constexpr double kKbUs256 = 0.33;
+// A 128-wide tile's k-block takes this fraction of a 256-wide one: half the
+// MMA work, but the same A slice streams from shared memory.
+constexpr double kKbFrac128 = 0.6;
+
+double kb_us(int bn) { return bn == 256 ? kKbUs256 : kKbUs256 * kKbFrac128; }
 
 struct Schedule {
   int grid;  // units
@@ -219,7 +246,8 @@ int tail_width(int64_t N, int bd, int bn, bool check) {
   return (ncols < bd && tn < bn) ? tn : 0;
 }
 
-Schedule make_schedule(int64_t tiles, int num_kb, int units) {
+Schedule make_schedule(int64_t tiles, int num_kb, int units, int bn) {
+  const double store = kSkStoreUs / kb_us(bn), fold = kSkFoldUs / kb_us(bn);
   Schedule s;
   s.sk = 0;
   s.sk_ctas = 0;
@@ -234,7 +262,7 @@ Schedule make_schedule(int64_t tiles, int num_kb, int units) {
   for (int64_t g = rem + 1; g <= units && g <= w; ++g) {
     const int64_t lmin = w / g;  // shortest unit range
     const int64_t pieces = cdiv(num_kb - 1, lmin) + 1;
-    const double t = static_cast<double>(waves * num_kb + cdiv(w, g)) + kSkStore + kSkFold * (pieces - 1);
+    const double t = static_cast<double>(waves * num_kb + cdiv(w, g)) + store + fold * (pieces - 1);
     if (t < s.est) {
       s.est = t;
       best_g = g;
@@ -251,19 +279,19 @@ Schedule make_schedule(int64_t tiles, int num_kb, int units) {
 
 // Schedule of an M x N x K launch with tile_m x bn tiles (bd data columns)
 // over `units` units.
-Schedule schedule_for(int64_t M, int64_t N, int64_t K, int tile_m, int bd, int units) {
-  return make_schedule(cdiv(M, tile_m) * cdiv(N, bd), static_cast<int>(cdiv(K, kBK)), units);
+Schedule schedule_for(int64_t M, int64_t N, int64_t K, int tile_m, int bn, int bd, int units) {
+  return make_schedule(cdiv(M, tile_m) * cdiv(N, bd), static_cast<int>(cdiv(K, kBK)), units, bn);
 }
 
 // A CTA pair runs a 128 x 256 share of a tile per SM about this much faster
 // than a single CTA (each CTA stages half the B-operand tile per k-block).
 constexpr double kPairSpeedup = 1.10;
 
-// Estimated time (single-CTA k-block steps) of an M x N x K launch with
-// 128- or 256-row tiles (256: CTA pairs over `units` pairs).
+// Estimated time (microseconds) of an M x N x K launch with tile_m x bn
+// tiles (tile_m 256: CTA pairs over `units` pairs).
 double est_time(int64_t M, int64_t N, int64_t K, int bn, bool check, int tile_m, int units) {
   const int bd = check ? bn - kChkRows : bn;
-  const double t = schedule_for(M, N, K, tile_m, bd, units).est;
+  const double t = schedule_for(M, N, K, tile_m, bn, bd, units).est * kb_us(bn);
   return tile_m == 256 ? t / kPairSpeedup : t;
 }
 
@@ -300,7 +328,7 @@ int make_plan(const abft_gemm_args* a, int dev, int sms, Plan* pl) {
     pl->units = sms / 2;
   else
     pl->units = pl->check ? pair_units_on<true>(dev, sms) : pair_units_on<false>(dev, sms);
-  pl->sch = schedule_for(a->M, a->N, a->K, pl->tile_m, pl->bd, pl->units);
+  pl->sch = schedule_for(a->M, a->N, a->K, pl->tile_m, pl->bn, pl->bd, pl->units);
   pl->grid = pl->sch.grid * (pl->pair ? 2 : 1);
 
   size_t off = 0;
@@ -325,7 +353,7 @@ int make_plan(const abft_gemm_args* a, int dev, int sms, Plan* pl) {
     pl->sk_part_off = off;
     off = align256(off + static_cast<size_t>(pl->grid) * kBM * pl->bn * sizeof(float));
     pl->sk_flag_off = off;
-    off = align256(off + static_cast<size_t>(pl->grid) * sizeof(int));
+    off = align256(off + static_cast<size_t>(pl->grid) * sizeof(unsigned long long));
   }
   pl->total = off;
   return ABFT_OK;
@@ -408,7 +436,7 @@ int32_t abft_pick_tile_n(int64_t M, int64_t N, int64_t K, int32_t num_sms, uint3
   double best_cost = 0.0;
   int32_t best = 256;
   for (int32_t bn : {256, 128}) {
-    double cost = est_time(M, N, K, bn, check, 128, num_sms) * (bn == 256 ? 1.0 : 0.8);
+    double cost = est_time(M, N, K, bn, check, 128, num_sms);
     if (bn == 256 && num_sms >= 2) {
       const double tp = est_time(M, N, K, bn, check, 256, num_sms / 2);
       if (tp < cost) cost = tp;
@@ -470,10 +498,12 @@ int abft_gemm_bf16(const abft_gemm_args* a, void* stream) {
   rc = current_device(&dev, &info);
   if (rc != ABFT_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (a->report != nullptr) {
-    if (cudaMemsetAsync(a->report, 0, sizeof(abft_report), s) != cudaSuccess) return launch_status(), ABFT_ERR_CUDA;
+  if (a->M == 0 || a->N == 0) {
+    // No kernel runs: reset the report here (the kernel resets it otherwise).
+    if (a->report != nullptr && cudaMemsetAsync(a->report, 0, sizeof(abft_report), s) != cudaSuccess)
+      return launch_status(), ABFT_ERR_CUDA;
+    return ABFT_OK;
   }
-  if (a->M == 0 || a->N == 0) return ABFT_OK;
   if (a->K == 0) return ABFT_ERR_UNSUPPORTED;
 
   int sms = info.sms;
@@ -581,11 +611,10 @@ int abft_gemm_bf16(const abft_gemm_args* a, void* stream) {
   p.sk_iters = sch.sk_iters;
   p.partials = nullptr;
   p.flags = nullptr;
+  p.nonce = next_launch_nonce();
   if (sch.sk) {
     p.partials = reinterpret_cast<float*>(wsb + ws.sk_part_off);
-    p.flags = reinterpret_cast<int*>(wsb + ws.sk_flag_off);
-    if (cudaMemsetAsync(p.flags, 0, static_cast<size_t>(grid) * sizeof(int), s) != cudaSuccess)
-      return launch_status(), ABFT_ERR_CUDA;
+    p.flags = reinterpret_cast<unsigned long long*>(wsb + ws.sk_flag_off);
   }
   if (ws.pair)
     rc = check ? launch_gemm<256, true, true>(dev, kPairSlot[1], tmA, tmB, tmB2, tmV, tmBt, p, grid, s)

@@ -114,8 +114,9 @@ struct GemmParams {
   int sk;
   int sk_ctas;  // stream-K units: CTAs, or CTA pairs
   int64_t sk_iters;
-  float* partials;  // [G][BN][128] fp32, column-major: a CTA's share of a tile it does not finish
-  int* flags;       // [G]: set to 1 once that CTA's partial is visible
+  float* partials;  // [G][BN/4][128][4] fp32: a CTA's share of a tile it does not finish
+  unsigned long long* flags;  // [G]: set to `nonce` once that CTA's partial is visible
+  uint64_t nonce;   // unique to this launch: stream-K flags and report->launch_tag carry it
   // Last tile column when it holds fewer than BD data columns (tail_n != 0):
   // its B-operand tile is compact (data rows, then with checks the 8
   // checksum rows) and one MMA of N = tail_n (a multiple of 16) covers it.
@@ -163,37 +164,55 @@ struct SegmentIter {
   }
 };
 
-__device__ __forceinline__ int ld_acquire_flag(const int* f) {
-  int v;
-  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+__device__ __forceinline__ uint64_t ld_acquire_u64(const unsigned long long* f) {
+  uint64_t v;
+  asm volatile("ld.acquire.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(f) : "memory");
   return v;
 }
+__device__ __forceinline__ void st_release_u64(unsigned long long* f, uint64_t v) {
+  asm volatile("st.release.gpu.global.b64 [%0], %1;" ::"l"(f), "l"(v) : "memory");
+}
 
-// Bounded wait for another CTA's flag (stream-K partials), warp-collective:
-// lane 0 polls with back-off so that a waiting CTA puts a handful of
-// requests on L2 rather than one per thread, then every lane re-reads the
-// flag with acquire semantics before it touches the partial. All CTAs of
-// the persistent grid are resident, and a CTA only waits for the first
-// segment of higher-index CTAs, which is stored before they wait for
-// anything.
-__device__ __forceinline__ bool wait_flag(const int* f, volatile int* abort_flag) {
+// Bounded wait for another CTA's flag (stream-K partials) to hold this
+// launch's nonce, warp-collective: lane 0 polls with back-off so that a
+// waiting CTA puts a handful of requests on L2 rather than one per thread,
+// then every lane re-reads the flag with acquire semantics before it
+// touches the partial. All CTAs of the persistent grid are resident, and a
+// CTA only waits for the first segment of higher-index CTAs, which is
+// stored before they wait for anything. Flags left by earlier launches
+// hold other nonces, so the workspace needs no clearing.
+__device__ __forceinline__ bool wait_flag(const unsigned long long* f, uint64_t nonce, volatile int* abort_flag) {
   int ok = 1;
   if ((threadIdx.x & 31) == 0) {
     const uint64_t t0 = global_timer_ns();
     uint32_t backoff = 32;
-    while (ld_acquire_flag(f) == 0) {
+    while (ld_acquire_u64(f) != nonce) {
       if (*abort_flag || global_timer_ns() - t0 > kWaitTimeoutNs) {
         *abort_flag = 1;
         ok = 0;
         break;
       }
       __nanosleep(backoff);
-      if (backoff < 512) backoff <<= 1;
+      if (backoff < 128) backoff <<= 1;
     }
   }
   ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
-  if (ok) (void)ld_acquire_flag(f);
+  if (ok) (void)ld_acquire_u64(f);
   return ok != 0;
+}
+
+// Bounded wait (one thread) until CTA 0 has reset the report header of this
+// launch; every atomic on the report comes after it.
+__device__ __forceinline__ bool report_ready(const GemmParams& p, volatile int* abort_flag) {
+  const uint64_t t0 = global_timer_ns();
+  while (ld_acquire_u64(reinterpret_cast<const unsigned long long*>(&p.report->launch_tag)) != p.nonce) {
+    if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+      *abort_flag = 1;
+      return false;
+    }
+    __nanosleep(64);
+  }
+  return true;
 }
 
 __device__ __forceinline__ void tile_coords(int tile, const GemmParams& p, int& mt, int& nt) {
@@ -321,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tempty = tfull + 2;    // [2]
   uint64_t* xbar = tempty + 2;     // [2] row-half partials exchanged
   uint64_t* drain = xbar + 2;
-  uint64_t* pbar = drain + 1;  // epilogue threads stored their stream-K partial
+  uint64_t* pbar = drain + 1;  // epilogue threads stored their stream-K partial (once per launch)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::kOffMisc + 4);
 
@@ -368,10 +387,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   if (blockIdx.x == 0 && threadIdx.x == 0 && p.report != nullptr) {
-    p.report->capacity = static_cast<uint32_t>(p.capacity);
-    p.report->tile_m = Cfg::kTileM;
-    p.report->tile_n = BD;
-    if (!(p.mode & ABFT_MODE_REF)) p.report->ref_ok = -1;
+    // Reset the header, then publish this launch's tag: other CTAs touch the
+    // report only after they have seen the tag (report_ready).
+    abft_report* r = p.report;
+    r->status = 0;
+    r->n_faults = 0;
+    r->n_located = 0;
+    r->n_corrected = 0;
+    r->overflow = 0;
+    r->capacity = static_cast<uint32_t>(p.capacity);
+    r->tile_m = Cfg::kTileM;
+    r->tile_n = BD;
+    r->corner = 0.f;
+    r->sum_c = 0.f;
+    r->abs_err = 0.f;
+    r->rel_err = 0.f;
+    r->ref_ok = -1;
+    r->reserved = 0;
+    __threadfence();
+    st_release_u64(reinterpret_cast<unsigned long long*>(&r->launch_tag), p.nonce);
   }
 
   if (warp == 0) {
@@ -540,7 +574,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         // warp store is 32 consecutive words. A segment that starts inside
         // a tile is the first segment of this CTA, so it is stored before
         // this CTA waits for anything: the wait chain is one link long.
-        float* dst = p.partials + (static_cast<size_t>(blockIdx.x) * BN + h * NV) * kBM + r;
+        // Layout [cta][column group of 4][row][4]: a warp's float4 store
+        // covers 32 consecutive rows, 512 contiguous bytes.
+        float4* dst = reinterpret_cast<float4*>(p.partials) + (static_cast<size_t>(blockIdx.x) * (BN / 4) + h * NV / 4) * kBM + r;
 #pragma unroll 1
         for (int c = 0; c < NCH; ++c) {
           uint32_t v[32];
@@ -548,16 +584,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld_32x32b_x32(tcol + c * 32, v);
           tmem_ld_wait();
 #pragma unroll
-          for (int e = 0; e < 32; ++e) __stcg(dst + (c * 32 + e) * kBM, __uint_as_float(v[e]));
+          for (int g = 0; g < 8; ++g)
+            __stcg(dst + (c * 8 + g) * kBM, make_float4(__uint_as_float(v[4 * g]), __uint_as_float(v[4 * g + 1]),
+                                                        __uint_as_float(v[4 * g + 2]), __uint_as_float(v[4 * g + 3])));
         }
         release_acc(acc);
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1u;
         }
-        __threadfence();
+        // Every epilogue thread's stores precede its arrival (release); one
+        // thread waits for all of them (acquire, bounded), makes them
+        // visible device-wide and publishes the flag. A CTA stores at most
+        // one partial per launch, so pbar completes once (parity 0).
         mbar_arrive(pbar);
-        if (ep == 0 && lane == 0 && mbar_wait(pbar, 0, abort_flag)) atomicExch(&p.flags[blockIdx.x], 1);
+        if (ep == 0 && lane == 0 && mbar_wait(pbar, 0, abort_flag)) {
+          __threadfence();
+          st_release_u64(&p.flags[blockIdx.x], p.nonce);
+        }
         continue;
       }
 
@@ -575,43 +619,48 @@ __global__ void __launch_bounds__(kThreads, 1)
         // in the partials of the units that own its later k-blocks (units
         // unit+1, +2, ..., umax; in a pair, their CTAs of the same rank), in
         // that order, writing the sums back to TMEM chunk by chunk.
+        // Each contributor is folded as soon as its flag holds this launch's
+        // nonce (units in increasing order: a fixed summation order).
         const int64_t tile_end = static_cast<int64_t>(tile - p.dp_tiles + 1) * p.num_kb;
-        int umax = unit;
         bool okp = true;
-        for (int c = unit + 1; c < p.sk_ctas; ++c) {
-          if (SegmentIter::sk_begin(p, c) >= tile_end) break;
-          if (!wait_flag(&p.flags[c * G + static_cast<int>(rank)], abort_flag)) {
+#pragma unroll 1
+        for (int u = unit + 1; u < p.sk_ctas; ++u) {
+          if (SegmentIter::sk_begin(p, u) >= tile_end) break;
+          const int cc = u * G + static_cast<int>(rank);
+          if (!wait_flag(&p.flags[cc], p.nonce, abort_flag)) {
             okp = false;
             break;
           }
-          umax = c;
+          const float4* src = reinterpret_cast<const float4*>(p.partials) + static_cast<size_t>(cc) * (BN / 4) * kBM + r;
+#pragma unroll 1
+          for (int c = 0; c < NCH; ++c) {
+            float4 q4[8];
+#pragma unroll
+            for (int g = 0; g < 8; ++g) q4[g] = __ldcg(src + (h * NV / 4 + c * 8 + g) * kBM);
+            uint32_t v[32];
+            __syncwarp();
+            tmem_ld_32x32b_x32(tcol + c * 32, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int g = 0; g < 8; ++g) {
+              v[4 * g] = __float_as_uint(__uint_as_float(v[4 * g]) + q4[g].x);
+              v[4 * g + 1] = __float_as_uint(__uint_as_float(v[4 * g + 1]) + q4[g].y);
+              v[4 * g + 2] = __float_as_uint(__uint_as_float(v[4 * g + 2]) + q4[g].z);
+              v[4 * g + 3] = __float_as_uint(__uint_as_float(v[4 * g + 3]) + q4[g].w);
+            }
+            __syncwarp();
+            tmem_st_32x32b_x32(tcol + c * 32, v);
+          }
+          tmem_st_wait();
+          if (CHECK) {
+            const float4 c0 = __ldcg(src + (chk_col / 4) * kBM);
+            const float4 c1 = __ldcg(src + (chk_col / 4 + 1) * kBM);
+            const float add[kChkRows] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+            for (int e = 0; e < kChkRows; ++e) chk[e] = __float_as_uint(__uint_as_float(chk[e]) + add[e]);
+          }
         }
         if (!__all_sync(0xFFFFFFFFu, okp)) break;
-#pragma unroll 1
-        for (int c = 0; c < NCH; ++c) {
-          uint32_t v[32];
-          __syncwarp();
-          tmem_ld_32x32b_x32(tcol + c * 32, v);
-          tmem_ld_wait();
-#pragma unroll 1
-          for (int u = unit + 1; u <= umax; ++u) {
-            const int cc = u * G + static_cast<int>(rank);
-            const float* src = p.partials + (static_cast<size_t>(cc) * BN + h * NV + c * 32) * kBM + r;
-#pragma unroll
-            for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) + __ldcg(src + e * kBM));
-          }
-          __syncwarp();
-          tmem_st_32x32b_x32(tcol + c * 32, v);
-        }
-        tmem_st_wait();
-        if (CHECK) {
-          for (int u = unit + 1; u <= umax; ++u) {
-            const int cc = u * G + static_cast<int>(rank);
-            const float* col = p.partials + (static_cast<size_t>(cc) * BN + chk_col) * kBM + r;
-#pragma unroll
-            for (int e = 0; e < kChkRows; ++e) chk[e] = __float_as_uint(__uint_as_float(chk[e]) + __ldcg(col + e * kBM));
-          }
-        }
       }
 
       const int row0 = mt * Cfg::kTileM + static_cast<int>(rank) * kBM;  // first row of this CTA's slab
@@ -747,7 +796,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               fix_delta = res1;
               flags |= ABFT_REC_CORRECTED;
             }
-            if (h == 0) {
+            if (h == 0 && report_ready(p, abort_flag)) {
               abft_report* rep = p.report;
               const uint32_t slot = atomicAdd(&rep->n_faults, 1u);
               if (flags & ABFT_REC_LOCATED) atomicAdd(&rep->n_located, 1u);
@@ -863,7 +912,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc_g<G>(tmem_base, Cfg::kTmemCols);
   }
-  if (threadIdx.x == 0 && *abort_flag && p.report != nullptr) atomicOr(&p.report->status, ABFT_STATUS_DEVICE_TIMEOUT);
+  if (threadIdx.x == 0 && *abort_flag && p.report != nullptr) {
+    // Bounded: report_ready gives up if CTA 0 never published the header;
+    // the status is then lost with the header.
+    if (report_ready(p, abort_flag)) atomicOr(&p.report->status, ABFT_STATUS_DEVICE_TIMEOUT);
+  }
 }
 
 }  // namespace abft
