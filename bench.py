@@ -459,6 +459,9 @@ SWEEP_SHAPES = [
     ("single_512x4096x4096", 512, 4096, 4096),
     ("qwen7b_qkv", 512, 4608, 3584), ("qwen7b_o", 512, 3584, 3584), ("qwen7b_gate_up", 512, 37888, 3584),
     ("qwen7b_down", 512, 3584, 18944), ("qwen7b_lm_head", 512, 152064, 3584),
+    # decode: few token rows, HBM-bound on the weight (operands swapped)
+    ("decode_m1_qkv", 1, 4608, 3584), ("decode_m1_gate_up", 1, 37888, 3584), ("decode_m1_down", 1, 3584, 18944),
+    ("decode_m32_gate_up", 32, 37888, 3584), ("decode_m32_down", 32, 3584, 18944),
 ]
 
 
@@ -511,7 +514,7 @@ def sweep(args):
         ref = out.clone()
         delta = 256.0 * ref.float().abs().max().item()
         for count in (1, 4):
-            faults = seeded_fault_positions(m, n, count, count)
+            faults = seeded_fault_positions(m, n, min(count, m), count)
             c, r = ops.abft_gemm(a, w, mode=chk_mode, tile_n=tn_chk, checksums=cks,
                                  inject=[(i, j, delta) for i, j in faults])
             r = r.read()
@@ -519,7 +522,10 @@ def sweep(args):
             outcomes[f"{count}_fault"] = {"located_exact": r.coords() == sorted(faults),
                                           "corrected": r.n_corrected, "max_rel_err_vs_clean": err}
         fl = 2.0 * m * n * k
+        wbytes = 2.0 * n * k  # the weight streams once: the HBM-bound term at few rows
         print(json.dumps({"shape": name, "M": m, "N": n, "K": k, "tile_n": [tn_off, tn_chk],
+                          "weight_gbs": {"cublas": wbytes / t_cublas / 1e6, "unchecked": wbytes / t_off / 1e6,
+                                         "checked": wbytes / t_chk / 1e6},
                           "cublas_tflops": fl / t_cublas / 1e9,
                           "unchecked_tflops": fl / t_off / 1e9, "checked_tflops": fl / t_chk / 1e9,
                           "overhead_pct": 100.0 * (t_chk / t_off - 1.0), "unchecked_ms": t_off, "checked_ms": t_chk,
@@ -563,14 +569,18 @@ def build_qwen2(cfg, device, seed=0):
             self.gate_up = nn.Linear(h, 2 * it, bias=False)
             self.down = nn.Linear(it, h, bias=False)
 
-        def forward(self, x, cos, sin):
+        def forward(self, x, cos, sin, cache=None, pos=0):
             nh, nkv, hd = cfg["heads"], cfg["kv_heads"], cfg["head_dim"]
             t = x.shape[0]
             q, k, v = self.qkv(self.ln1(x)).split([nh * hd, nkv * hd, nkv * hd], dim=-1)
             q = rope(q.view(t, nh, hd), cos, sin).transpose(0, 1)
             k = rope(k.view(t, nkv, hd), cos, sin).transpose(0, 1)
             v = v.view(t, nkv, hd).transpose(0, 1)
-            a = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
+            if cache is not None:  # [2, nkv, T_max, hd]: keys and values of positions < pos + t
+                cache[0, :, pos:pos + t] = k
+                cache[1, :, pos:pos + t] = v
+                k, v = cache[0, :, :pos + t], cache[1, :, :pos + t]
+            a = F.scaled_dot_product_attention(q, k, v, is_causal=(t > 1), enable_gqa=True)
             x = x + self.o(a.transpose(0, 1).reshape(t, nh * hd))
             g, u = self.gate_up(self.ln2(x)).chunk(2, dim=-1)
             return x + self.down(F.silu(g) * u)
@@ -583,17 +593,21 @@ def build_qwen2(cfg, device, seed=0):
             self.norm = RMSNorm(cfg["hidden"])
             self.lm_head = nn.Linear(cfg["hidden"], cfg["vocab"], bias=False)
 
-        def forward(self, ids):
+        def forward(self, ids, caches=None, pos=0):
             t = ids.shape[0]
             hd = cfg["head_dim"]
             inv = 1.0 / (cfg["rope_theta"] ** (torch.arange(0, hd, 2, device=ids.device).float() / hd))
-            ang = torch.outer(torch.arange(t, device=ids.device).float(), inv)
+            ang = torch.outer(torch.arange(pos, pos + t, device=ids.device).float(), inv)
             ang = torch.cat((ang, ang), dim=-1)[:, None, :]
             cos, sin = ang.cos().to(torch.bfloat16), ang.sin().to(torch.bfloat16)
             x = self.embed(ids)
-            for layer in self.layers:
-                x = layer(x, cos, sin)
+            for i, layer in enumerate(self.layers):
+                x = layer(x, cos, sin, None if caches is None else caches[i], pos)
             return self.lm_head(self.norm(x))
+
+        def new_caches(self, t_max):
+            return [torch.zeros(2, cfg["kv_heads"], t_max, cfg["head_dim"], dtype=torch.bfloat16,
+                                device=self.embed.weight.device) for _ in range(cfg["layers"])]
 
     torch.manual_seed(seed)
     with torch.device(device):
@@ -707,6 +721,30 @@ def run_model(args):
     max_diff = (f_logits.float() - chk_logits.float()).abs().max().item()
     logits_scale = chk_logits.float().abs().max().item()
 
+    # decode: prefill 512 tokens into a KV cache, then time single-token steps
+    def timed_decode(ctx_factory, steps=32):
+        caches = model.new_caches(tokens + steps + 8)
+        with torch.inference_mode():
+            with ctx_factory():
+                model(ids, caches, 0)
+            nxt = ids[-1:].clone()
+            for i in range(4):  # warm-up steps
+                with ctx_factory():
+                    model(nxt, caches, tokens + i)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for i in range(steps):
+                with ctx_factory():
+                    model(nxt, caches, tokens + 4 + i)
+            e1.record()
+            torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    d_torch = timed_decode(contextlib.nullcontext)
+    d_off = timed_decode(lambda: inj_off)
+    d_chk = timed_decode(lambda: inj_chk)
+
     linear_flops = 0.0
     h, it, nh, nkv, hd, V = (cfg["hidden"], cfg["inter"], cfg["heads"], cfg["kv_heads"], cfg["head_dim"],
                              cfg["vocab"])
@@ -729,6 +767,10 @@ def run_model(args):
         "ms": {"torch": t_torch, "b200_unchecked": t_off, "b200_abft": t_chk},
         "device_ms": {"torch": g_torch, "b200_unchecked": g_off, "b200_abft": g_chk,
                       "note": "kernels only: the host queued the forward behind a device sleep"},
+        "decode_ms_per_token": {"torch": d_torch, "b200_unchecked": d_off, "b200_abft": d_chk,
+                                "abft_overhead_vs_torch_pct": 100.0 * (d_chk / d_torch - 1.0),
+                                "note": "after a 512-token prefill into a KV cache; every linear at M = 1 "
+                                        "(operands swapped: weight on the MMA's 128-row side)"},
         "overhead_vs_torch_pct": 100.0 * (t_chk / t_torch - 1.0),
         "overhead_vs_unchecked_pct": 100.0 * (t_chk / t_off - 1.0),
         "linear_tflops_abft": linear_flops / (t_chk * 1e-3) / 1e12,
@@ -741,6 +783,7 @@ def run_model(args):
         "logits_max_abs_diff_torch_vs_abft": (ref_logits.float() - chk_logits.float()).abs().max().item(),
         "cpu_baseline": cpu,
         "reference_published": {"tokens_per_s_no_abft": 7217, "tokens_per_s_abft_python": 5909,
+                                "decode_ms_no_abft": 29.90, "decode_ms_abft_python": 73.97,
                                 "source": "pytorch/baseline_7b_prefill512.json:44, "
                                           "pytorch/abft_7b_prefill512_nsys.json:44 (GPU unrecorded)"},
     }

@@ -136,7 +136,12 @@ typedef struct abft_gemm_args {
   int32_t tile_m;         /* 0 = choose; 128; or 256: each tile is shared by  */
                           /* a 2-CTA cluster (one pair MMA, M = 256), which    */
                           /* needs tile_n 256                                 */
-  int32_t reserved0;      /* set to 0                                         */
+  int32_t swap_ab;        /* 0 = choose; 1 = never; 2 = always: compute C^T =  */
+                          /* B A^T with the weight on the MMA's 128-row side   */
+                          /* and the few rows of A as a narrow tile (chosen    */
+                          /* for M <= 64 when tile_m is 0); checksums then     */
+                          /* come from A, per                                  */
+                          /* call, and `checksums` is not used                */
 } abft_gemm_args;
 
 #define ABFT_MAX_INJECT 64

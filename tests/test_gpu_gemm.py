@@ -376,3 +376,54 @@ def test_tail_tile_widths(cuda_device, tile_n, tile_m, n, mode):
     assert got == orc.records
     assert r.n_corrected == len(faults)
     assert max_rel_err(f32(c2), orc.out) <= OUT_TOL
+
+
+# ------------------------------------- swapped operands (few rows: decode)
+def run_swapped(device, m, n, k, faults, *, bias=True, mode=N.MODE_DETECT | N.MODE_CORRECT, swap_ab=0, seed=21):
+    """The library computes out^T = W a^T; the oracle checks that transposed
+    product (W rows against the tokens' checksums, 120 tokens per tile)."""
+    a, w, b = seeded(m, n, k, seed, bias)
+    acc = f32(a).astype(np.float64) @ f32(w).astype(np.float64).T
+    delta = 256.0 * np.abs(acc).max()
+    inj = [(r, c, float(delta)) for (r, c) in faults]
+    c, rep = ops.abft_gemm(a.to(device), w.to(device), None if b is None else b.to(device), mode=mode,
+                           inject=inj or None, swap_ab=swap_ab)
+    r = rep.read() if rep is not None else None
+    orc = O.rowcheck_gemm(f32(w), f32(a), None, tile_n=120, inject=[(cc, rr, d) for rr, cc, d in inj],
+                          correct=bool(mode & N.MODE_CORRECT))
+    return a, w, b, c, r, orc
+
+
+@pytest.mark.parametrize("m", [1, 2, 8, 16, 31, 32, 64])
+@pytest.mark.parametrize("n,k", [(256, 64), (1000, 520), (4608, 3584)])
+def test_swapped_small_m_matches_fp32(cuda_device, m, n, k):
+    for mode in (N.MODE_OFF, N.MODE_DETECT | N.MODE_CORRECT):
+        a, w, b, c, r, orc = run_swapped(cuda_device, m, n, k, [], mode=mode)
+        ref = f32(a) @ f32(w).T + f32(b)
+        assert max_rel_err(f32(c), ref) <= OUT_TOL
+        if r is not None:
+            assert r.n_faults == 0 and r.status == 0 and orc.records == []
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 1000, 520), (8, 4608, 3584), (32, 3584, 18944 // 4), (64, 4096, 1024)])
+def test_swapped_faults_located_in_output_coordinates(cuda_device, m, n, k):
+    faults = O.seeded_fault_positions(m, n, min(m, 4), 31 + m)
+    a, w, b, c, r, orc = run_swapped(cuda_device, m, n, k, faults)
+    # oracle records are (feature, token): map to (token, feature)
+    want = sorted((cc, rr, fl) if cc >= 0 else (-1, rr, fl) for rr, cc, fl in orc.records)
+    got = sorted((x.row, x.col, x.flags) for x in r.records)
+    assert got == want
+    assert r.coords() == sorted(faults) and r.n_corrected == len(faults)
+    clean = f32(a) @ f32(w).T + f32(b)
+    assert max_rel_err(f32(c), clean) <= OUT_TOL
+
+
+def test_swap_forced_and_refused(cuda_device):
+    m, n, k = 200, 512, 256  # swapped by request: 2 token tiles
+    faults = [(3, 7), (150, 400)]
+    a, w, b, c, r, orc = run_swapped(cuda_device, m, n, k, faults, swap_ab=2)
+    assert r.coords() == sorted(faults) and r.n_corrected == 2
+    assert max_rel_err(f32(c), f32(a) @ f32(w).T + f32(b)) <= OUT_TOL
+    # few rows, swap refused: the ordinary row checks
+    a, w, b, c, r, orc = run_swapped(cuda_device, 8, 512, 256, [(2, 100)], swap_ab=1)
+    assert r.coords() == [(2, 100)] and r.tile_n in (120, 248)

@@ -96,7 +96,7 @@ class GemmArgs(ctypes.Structure):
         ("report_capacity", ctypes.c_int32),
         ("num_sms", ctypes.c_int32),
         ("tile_m", ctypes.c_int32),
-        ("reserved0", ctypes.c_int32),
+        ("swap_ab", ctypes.c_int32),
     ]
 
 

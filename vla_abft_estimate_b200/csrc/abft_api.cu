@@ -237,13 +237,20 @@ struct Schedule {
   double est;  // estimated duration in k-block steps
 };
 
+// Rows of the last tile column's data box: its data columns rounded up to 8,
+// so that the checksum rows after them start on a 1024-byte swizzle atom
+// (the rows past N are zero-filled by the copy).
+int tail_rows(int64_t N, int bd) {
+  const int64_t tiles_n = cdiv(N, bd);
+  return (static_cast<int>(N - (tiles_n - 1) * bd) + 7) / 8 * 8;
+}
+
 // MMA width of the last tile column's compact tile (its data rows, then with
 // checks the 8 checksum rows), or 0 when that column needs no narrower MMA.
 int tail_width(int64_t N, int bd, int bn, bool check) {
-  const int64_t tiles_n = cdiv(N, bd);
-  const int ncols = static_cast<int>(N - (tiles_n - 1) * bd);
-  const int tn = (ncols + (check ? kChkRows : 0) + 15) / 16 * 16;
-  return (ncols < bd && tn < bn) ? tn : 0;
+  const int rows = tail_rows(N, bd);
+  const int tn = (rows + (check ? kChkRows : 0) + 15) / 16 * 16;
+  return (rows < bd && tn < bn) ? tn : 0;
 }
 
 Schedule make_schedule(int64_t tiles, int num_kb, int units, int bn) {
@@ -299,6 +306,35 @@ int pick_tile_m(int64_t M, int64_t N, int64_t K, int sms, uint32_t mode, int bn)
   if (bn != 256 || sms < 2 || M <= 0 || N <= 0 || K <= 0) return 128;
   const bool check = (mode & (ABFT_MODE_DETECT | ABFT_MODE_CORRECT)) != 0;
   return est_time(M, N, K, bn, check, 256, sms / 2) < est_time(M, N, K, bn, check, 128, sms) ? 256 : 128;
+}
+
+// Swapped operands: with few output rows the weight goes on the MMA's
+// 128-row side and the rows of A form one narrow tile, C^T = B A^T.
+bool use_swap(const abft_gemm_args* a) {
+  if (a->swap_ab == 1) return false;
+  if (a->swap_ab == 2) return true;
+  // automatic only when the caller left the tile height to the library
+  return a->tile_m == 0 && a->M <= 64 && a->N >= 2 * a->M;
+}
+
+// The arguments in the swapped frame: A' = B (the weight, [N, K]), B' = A
+// ([M, K]); C, ldc and the bias keep their memory meaning (the kernel stores
+// transposed and indexes the bias by its row); checksums of A' are made per
+// call; injected faults keep their C coordinates by exchanging the arrays.
+abft_gemm_args swapped_args(const abft_gemm_args* a) {
+  abft_gemm_args s = *a;
+  s.A = a->B;
+  s.B = a->A;
+  s.M = a->N;
+  s.N = a->M;
+  s.lda = a->ldb;
+  s.ldb = a->lda;
+  s.checksums = nullptr;
+  s.tile_n = 128;
+  s.tile_m = 128;
+  s.inject_rows = a->inject_cols;
+  s.inject_cols = a->inject_rows;
+  return s;
 }
 
 // Everything about a launch that depends only on the arguments and the
@@ -371,6 +407,7 @@ int validate_gemm(const abft_gemm_args* a) {
   if (a->tile_n != 0 && a->tile_n != 128 && a->tile_n != 256) return ABFT_ERR_UNSUPPORTED;
   if (a->tile_m != 0 && a->tile_m != 128 && a->tile_m != 256) return ABFT_ERR_UNSUPPORTED;
   if (a->tile_m == 256 && a->tile_n == 128) return ABFT_ERR_UNSUPPORTED;
+  if (a->swap_ab < 0 || a->swap_ab > 2) return ABFT_ERR_INVALID_ARG;
   if (a->mode != ABFT_MODE_OFF && (a->report == nullptr || a->report_capacity < 0)) return ABFT_ERR_INVALID_ARG;
   if (a->report != nullptr && !aligned16(a->report)) return ABFT_ERR_ALIGNMENT;
   if (a->n_inject < 0 || a->n_inject > ABFT_MAX_INJECT) return ABFT_ERR_INVALID_ARG;
@@ -481,7 +518,8 @@ size_t abft_gemm_workspace_bytes(const abft_gemm_args* args) {
   if (have_dev) sms = info.sms;
   if (args->num_sms > 0 && args->num_sms < sms) sms = args->num_sms;
   Plan pl;
-  if (make_plan(args, have_dev ? dev : -1, sms, &pl) != ABFT_OK) return 0;
+  const abft_gemm_args sw = swapped_args(args);
+  if (make_plan(use_swap(args) ? &sw : args, have_dev ? dev : -1, sms, &pl) != ABFT_OK) return 0;
   return pl.total;
 }
 
@@ -490,9 +528,12 @@ int32_t abft_pick_tile_m(int64_t M, int64_t N, int64_t K, int32_t num_sms, uint3
   return pick_tile_m(M, N, K, num_sms, mode, tile_n);
 }
 
-int abft_gemm_bf16(const abft_gemm_args* a, void* stream) {
-  int rc = validate_gemm(a);
+int abft_gemm_bf16(const abft_gemm_args* args, void* stream) {
+  int rc = validate_gemm(args);
   if (rc != ABFT_OK) return rc;
+  const bool swap = use_swap(args);
+  const abft_gemm_args sw = swapped_args(args);
+  const abft_gemm_args* a = swap ? &sw : args;
   int dev;
   DeviceInfo info;
   rc = current_device(&dev, &info);
@@ -567,6 +608,7 @@ int abft_gemm_bf16(const abft_gemm_args* a, void* stream) {
   p.report = static_cast<abft_report*>(a->report);
   p.capacity = a->report_capacity;
   p.tile_sumc = (a->mode & ABFT_MODE_REF) ? reinterpret_cast<float*>(wsb + ws.parts_off) : nullptr;
+  p.swap = swap ? 1 : 0;
 
   // Compact tail tile: when the last tile column holds ncols < bd data
   // columns, its B-operand tile is those rows (then, with checks, the 8
@@ -576,7 +618,7 @@ int abft_gemm_bf16(const abft_gemm_args* a, void* stream) {
   p.tail_tx = 0;
   CUtensorMap tmBt = tmA;  // placeholder unless a tail box is needed
   {
-    const int ncols = static_cast<int>(a->N - static_cast<int64_t>(p.tiles_n - 1) * bd);
+    const int ncols = tail_rows(a->N, bd);  // data rows of the tail box, a multiple of 8
     const int tn = tail_width(a->N, bd, bn, check);
     if (tn != 0) {
       const uint32_t a_bytes = static_cast<uint32_t>(kBM * kBK * 2);
@@ -588,6 +630,7 @@ int abft_gemm_bf16(const abft_gemm_args* a, void* stream) {
         // Data rows copied by the tail box into this CTA (a pair: the odd
         // CTA holds the rows from tn / 2 on; the even CTA keeps its usual box).
         const int box = ws.pair ? ncols - tn / 2 : ncols;
+        if (box < 0 || box % 8) return ABFT_ERR_UNSUPPORTED;  // checksum rows must start on a swizzle atom
         p.tail_box = box;
         if (box > 0) {
           rc = make_tmap_kmajor(&tmBt, a->B, a->K, a->N, a->ldb, box);
@@ -636,7 +679,9 @@ int abft_gemm_bf16(const abft_gemm_args* a, void* stream) {
     if (rc != ABFT_OK) return rc;
     rc = colsum(a->B, a->ldb, a->N, a->K, nullptr, pb, vf, nullptr, nullptr, sms, s);
     if (rc != ABFT_OK) return rc;
-    ref_finalize_kernel<<<1, 1024, 0, s>>>(u, vf, p.K, p.bias, p.N, p.M, p.tile_sumc,
+    // corner + (rows of C) * sum(bias): the bias runs along the kernel's
+    // rows when the operands are swapped
+    ref_finalize_kernel<<<1, 1024, 0, s>>>(u, vf, p.K, p.bias, swap ? p.M : p.N, swap ? p.N : p.M, p.tile_sumc,
                                            p.num_tiles * 8 * (ws.pair ? 2 : 1), a->tol_abs,
                                            a->tol_rel, (a->mode & ABFT_MODE_REF_BF16) ? 1 : 0, p.report, p.capacity,
                                            ws.tile_m, bd);

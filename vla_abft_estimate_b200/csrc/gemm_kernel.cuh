@@ -123,6 +123,11 @@ struct GemmParams {
   int tail_n;
   int tail_box;      // data rows the tail box copies into this CTA (odd CTA of a pair), 0 = none
   uint32_t tail_tx;  // bytes one stage of a tail tile delivers (both CTAs of a pair)
+  // Swapped operands (few output rows): the kernel computes C^T = W X^T, so
+  // its rows are C's columns and its columns are C's rows. The output is
+  // stored transposed (C[col * ldc + row]), the bias is indexed by the
+  // kernel row, and fault records carry C's coordinates.
+  int swap;
 };
 
 // Walks the (tile, k-block range) segments one CTA owns. Data-parallel:
@@ -606,8 +611,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
 
       // Accumulator column of the expected checksums: BD, or right after the
-      // data columns of a compact tail tile.
-      const int chk_col = (p.tail_n != 0 && nt == p.tiles_n - 1) ? p.N - nt * BD : BD;
+      // data rows of a compact tail tile (its data columns rounded up to 8).
+      const int chk_col = (p.tail_n != 0 && nt == p.tiles_n - 1) ? ((p.N - nt * BD + 7) & ~7) : BD;
       uint32_t chk[kChkRows];
       if (CHECK) {
         __syncwarp();
@@ -702,6 +707,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         float s1 = 0.f, s2 = 0.f, s3 = 0.f, amax = 0.f;
 #pragma unroll 1
         for (int c = 0; c < NCH; ++c) {
+          if (hcol0 + c * 32 >= ncols) break;  // warp-uniform: nothing valid from here on
           uint32_t v[32];
           __syncwarp();
           tmem_ld_32x32b_x32(tcol + c * 32, v);
@@ -804,8 +810,13 @@ __global__ void __launch_bounds__(kThreads, 1)
               uint32_t st = ABFT_STATUS_FAULT | ((flags & ABFT_REC_LOCATED) ? 0u : ABFT_STATUS_UNLOCATED);
               if (slot < static_cast<uint32_t>(p.capacity)) {
                 abft_fault_record* rec = reinterpret_cast<abft_fault_record*>(rep + 1) + slot;
-                rec->row = grow;
-                rec->col = col >= 0 ? col0 + col : -1;
+                if (!p.swap) {
+                  rec->row = grow;
+                  rec->col = col >= 0 ? col0 + col : -1;
+                } else {
+                  rec->row = col >= 0 ? col0 + col : -1;
+                  rec->col = grow;
+                }
                 rec->residual = res1;
                 rec->residual_w = res2;
                 rec->threshold = thr;
@@ -820,13 +831,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
 
-      // Pass 2: final values -> bf16 -> staging block -> global.
+      // Pass 2: final values -> bf16 -> staging block -> global (swapped
+      // operands: straight to C's transposed position).
       const int fix_local = fix_col - hcol0;  // column within this thread's half, or out of range
       float row_out_sum = 0.f;
       const uint4* bp = reinterpret_cast<const uint4*>(p.bias + col0 + hcol0);
       const int rd_grow = row0 + q * 32 + rd_row;  // global row of this lane's first read-side row
+      const float row_bias = (p.swap && p.bias != nullptr && row_ok) ? __bfloat162float(p.bias[grow]) : 0.f;
 #pragma unroll 1
       for (int c = 0; c < NCH; ++c) {
+        if (p.swap && hcol0 + c * 32 >= ncols) break;  // warp-uniform
         uint32_t v[32];
         __syncwarp();
         tmem_ld_32x32b_x32(tcol + c * 32, v);
@@ -846,6 +860,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int e = 0; e < 32; ++e) x[e] -= (fix_local == c * 32 + e) ? fix_delta : 0.f;
         }
         const int base = hcol0 + c * 32;
+        if (p.swap) {
+          // Lane l holds kernel row row0 + q*32 + l = C column: for each of
+          // this chunk's C rows a warp writes 32 consecutive columns.
+          if (row_ok) {
+            __nv_bfloat16* cc = p.C + static_cast<int64_t>(col0 + base) * p.ldc + grow;
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              if (base + e < ncols) {
+                const __nv_bfloat16 o = __float2bfloat16_rn(x[e] + row_bias);
+                cc[static_cast<int64_t>(e) * p.ldc] = o;
+                if (p.mode & ABFT_MODE_REF) row_out_sum += __bfloat162float(o);
+              }
+            }
+          }
+          continue;
+        }
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
           const bool gvalid = row_ok && (base + g * 8 < ncols);

@@ -139,6 +139,7 @@ def abft_gemm(
     mode: int = N.MODE_DETECT | N.MODE_CORRECT,
     tile_n: int = 0,
     tile_m: int = 0,
+    swap_ab: int = 0,
     thr_scale: float = DEFAULT_THR_SCALE,
     thr_abs: float = 0.0,
     tol_abs: float = 1e-2,
@@ -155,8 +156,11 @@ def abft_gemm(
     ``checksums`` is ``encode_weight(weight, tile_n)`` (cache it for a fixed
     weight); when omitted and checks are on, the call encodes into its
     workspace. ``tile_m`` 256 runs each 256-row tile on a 2-CTA pair (needs
-    tile_n 256); 0 lets the library choose. ``inject`` adds debug faults to
-    the fp32 accumulator.
+    tile_n 256); 0 lets the library choose. ``swap_ab`` (0 choose, 1 never,
+    2 always) computes out^T = weight a^T instead, for few rows of ``a``:
+    the weight then streams through the MMA's 128-row side, the checksums
+    come from ``a`` per call and fault records keep ``out``'s coordinates.
+    ``inject`` adds debug faults to the fp32 accumulator.
     Returns the output and the report buffer (None when mode == MODE_OFF).
     """
     _require_bf16_cuda("a", a, 2)
@@ -197,6 +201,7 @@ def abft_gemm(
     args.mode = int(mode)
     args.tile_n = int(tile_n)
     args.tile_m = int(tile_m)
+    args.swap_ab = int(swap_ab)
     args.thr_scale, args.thr_abs = float(thr_scale), float(thr_abs)
     args.tol_abs, args.tol_rel = float(tol_abs), float(tol_rel)
     args.checksums = _ptr(checksums)
