@@ -521,6 +521,10 @@ def sweep(args):
             err = (c.float() - ref.float()).abs().max().item() / max(ref.float().abs().max().item(), 1e-30)
             outcomes[f"{count}_fault"] = {"located_exact": r.coords() == sorted(faults),
                                           "corrected": r.n_corrected, "max_rel_err_vs_clean": err}
+            if r.coords() != sorted(faults):  # keep the evidence of a mismatch
+                outcomes[f"{count}_fault"]["report"] = {
+                    "injected": sorted(faults), "n_faults": r.n_faults, "status": r.status,
+                    "records": [(x.row, x.col, x.flags, x.residual, x.residual_w, x.threshold) for x in r.records]}
         fl = 2.0 * m * n * k
         wbytes = 2.0 * n * k  # the weight streams once: the HBM-bound term at few rows
         print(json.dumps({"shape": name, "M": m, "N": n, "K": k, "tile_n": [tn_off, tn_chk],

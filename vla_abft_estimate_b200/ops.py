@@ -82,6 +82,25 @@ def _device_index(device: Optional[torch.device]) -> int:
     return device.index
 
 
+_WORKSPACES: dict = {}
+
+
+def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Scratch for the current stream of ``device``, grown on demand.
+
+    One buffer per (device, stream): calls on one stream run in order, so
+    reusing it is safe; a buffer replaced by a larger one is freed in stream
+    order by the caching allocator.
+    """
+    stream = torch.cuda.current_stream(device)
+    key = (device.index, stream.cuda_stream)
+    ws = _WORKSPACES.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _WORKSPACES[key] = ws
+    return ws
+
+
 def pick_tile_n(m: int, n: int, k: int, device: Optional[torch.device] = None,
                 mode: int = N.MODE_DETECT | N.MODE_CORRECT) -> int:
     """Tile width the library would pick for an m x n x k GEMM in ``mode``."""
@@ -214,14 +233,12 @@ def abft_gemm(
     L = N.lib()
     with torch.cuda.device(dev):
         ws_bytes = int(L.abft_gemm_workspace_bytes(ctypes.byref(args)))
-        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev) if ws_bytes else None
-        args.workspace = _ptr(ws)
-        args.workspace_bytes = ws_bytes
+        if ws_bytes:
+            ws = _workspace(dev, ws_bytes)
+            args.workspace = ws.data_ptr()
+            args.workspace_bytes = ws.numel()
         rc = L.abft_gemm_bf16(ctypes.byref(args), _stream(dev))
     N.check("abft_gemm_bf16", rc)
-    # keep device buffers alive until the stream has consumed them
-    if ws is not None:
-        ws.record_stream(torch.cuda.current_stream(dev))
     return out, report
 
 
