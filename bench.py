@@ -54,9 +54,10 @@ def parse_args():
     ap.add_argument("--sweep", action="store_true",
                     help="one JSON line per shape of the square sweep, the 512x4096x4096 case and the "
                          "Qwen2-7B layer GEMMs: checked / unchecked TFLOP/s and 1- and 4-fault outcomes")
-    ap.add_argument("--model", choices=["qwen2-7b"], default=None,
-                    help="prefill-512 tokens/s of a random-init Qwen2-7B-shaped decoder with every linear "
-                         "ABFT-protected (one JSON line)")
+    ap.add_argument("--model", choices=["qwen2-7b", "cogact"], default=None,
+                    help="qwen2-7b: prefill-512 tokens/s and decode of a random-init Qwen2-7B-shaped decoder; "
+                         "cogact: one CogACT-style VLA forward (ViT-L + SigLIP + Llama-2-7B + DiT-B, 10 "
+                         "denoising steps); every linear ABFT-protected (one JSON line)")
     ap.add_argument("--profile-case", choices=["off", "check", "both"], default=None,
                     help="only run two rounds of the fused GEMM (unchecked then checked for 'both') "
                          "on randn inputs, for an ncu capture")
@@ -794,8 +795,235 @@ def run_model(args):
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------- VLA (CogACT-style)
+COGACT = dict(
+    vit=dict(hidden=1024, mlp=4096, layers=24, heads=16),        # ViT-L/14 at 224^2
+    siglip=dict(hidden=1152, mlp=4304, layers=27, heads=16),     # SigLIP-So400m/14 at 224^2
+    llm=dict(hidden=4096, mlp=11008, layers=32, heads=32),       # Llama-2-7B
+    dit=dict(hidden=768, mlp=3072, layers=12, heads=12),         # DiT-B action head
+    patches=256, text_tokens=32, action_tokens=16, action_dim=7, denoise_steps=10, vocab=32000)
+
+
+def build_cogact(cfg, device, seed=0):
+    """Random-init CogACT-style VLA: two ViT encoders (patch conv, pre-norm
+    blocks with fused QKV + GELU MLP), an MLP projector, a Llama-style
+    decoder (RMSNorm, RoPE, fused QKV, SwiGLU with fused gate+up) and a
+    DiT-B action head (adaLN-zero blocks conditioned on the decoder's last
+    hidden state and the denoising step). Every projection is an nn.Linear."""
+    import torch
+    import torch.nn as nn
+    import torch.nn.functional as F
+
+    class RMSNorm(nn.Module):
+        def __init__(self, h):
+            super().__init__()
+            self.weight = nn.Parameter(torch.ones(h))
+
+        def forward(self, x):
+            xf = x.float()
+            return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)).to(x.dtype) * self.weight
+
+    def attend(qkv, heads, causal, cos=None, sin=None):
+        t, three_h = qkv.shape
+        hd = three_h // 3 // heads
+        q, k, v = qkv.view(t, 3, heads, hd).unbind(1)
+        if cos is not None:
+            def rope(x):
+                x1, x2 = x[..., : hd // 2], x[..., hd // 2:]
+                return x * cos + torch.cat((-x2, x1), dim=-1) * sin
+            q, k = rope(q), rope(k)
+        o = F.scaled_dot_product_attention(q.transpose(0, 1), k.transpose(0, 1), v.transpose(0, 1), is_causal=causal)
+        return o.transpose(0, 1).reshape(t, heads * hd)
+
+    class VitBlock(nn.Module):
+        def __init__(self, c):
+            super().__init__()
+            h = c["hidden"]
+            self.heads = c["heads"]
+            self.n1, self.n2 = nn.LayerNorm(h), nn.LayerNorm(h)
+            self.qkv, self.o = nn.Linear(h, 3 * h), nn.Linear(h, h)
+            self.fc1, self.fc2 = nn.Linear(h, c["mlp"]), nn.Linear(c["mlp"], h)
+
+        def forward(self, x):
+            x = x + self.o(attend(self.qkv(self.n1(x)), self.heads, False))
+            return x + self.fc2(F.gelu(self.fc1(self.n2(x)), approximate="tanh"))
+
+    class Vit(nn.Module):
+        def __init__(self, c):
+            super().__init__()
+            self.patch = nn.Conv2d(3, c["hidden"], kernel_size=14, stride=14)
+            self.pos = nn.Parameter(torch.zeros(cfg["patches"], c["hidden"]))
+            self.blocks = nn.ModuleList([VitBlock(c) for _ in range(c["layers"])])
+            self.norm = nn.LayerNorm(c["hidden"])
+
+        def forward(self, img):
+            x = self.patch(img).flatten(2).transpose(1, 2)[0] + self.pos
+            for b in self.blocks:
+                x = b(x)
+            return self.norm(x)
+
+    class LlamaBlock(nn.Module):
+        def __init__(self, c):
+            super().__init__()
+            h = c["hidden"]
+            self.heads = c["heads"]
+            self.n1, self.n2 = RMSNorm(h), RMSNorm(h)
+            self.qkv, self.o = nn.Linear(h, 3 * h, bias=False), nn.Linear(h, h, bias=False)
+            self.gate_up, self.down = nn.Linear(h, 2 * c["mlp"], bias=False), nn.Linear(c["mlp"], h, bias=False)
+
+        def forward(self, x, cos, sin):
+            x = x + self.o(attend(self.qkv(self.n1(x)), self.heads, True, cos, sin))
+            g, u = self.gate_up(self.n2(x)).chunk(2, dim=-1)
+            return x + self.down(F.silu(g) * u)
+
+    class DitBlock(nn.Module):
+        def __init__(self, c):
+            super().__init__()
+            h = c["hidden"]
+            self.heads = c["heads"]
+            self.n1 = nn.LayerNorm(h, elementwise_affine=False)
+            self.n2 = nn.LayerNorm(h, elementwise_affine=False)
+            self.qkv, self.o = nn.Linear(h, 3 * h), nn.Linear(h, h)
+            self.fc1, self.fc2 = nn.Linear(h, c["mlp"]), nn.Linear(c["mlp"], h)
+            self.ada = nn.Linear(h, 6 * h)
+
+        def forward(self, x, c):
+            s1, b1, g1, s2, b2, g2 = self.ada(F.silu(c)).chunk(6, dim=-1)
+            x = x + g1 * self.o(attend(self.qkv(self.n1(x) * (1 + s1) + b1), self.heads, False))
+            return x + g2 * self.fc2(F.gelu(self.fc1(self.n2(x) * (1 + s2) + b2), approximate="tanh"))
+
+    class Vla(nn.Module):
+        def __init__(self):
+            super().__init__()
+            v, s, l, d = cfg["vit"], cfg["siglip"], cfg["llm"], cfg["dit"]
+            self.vit, self.siglip = Vit(v), Vit(s)
+            self.proj1 = nn.Linear(v["hidden"] + s["hidden"], l["hidden"])
+            self.proj2 = nn.Linear(l["hidden"], l["hidden"])
+            self.embed = nn.Embedding(cfg["vocab"], l["hidden"])
+            self.llm = nn.ModuleList([LlamaBlock(l) for _ in range(l["layers"])])
+            self.llm_norm = RMSNorm(l["hidden"])
+            self.cond = nn.Linear(l["hidden"], d["hidden"])
+            self.t_embed = nn.Linear(256, d["hidden"])
+            self.act_in = nn.Linear(cfg["action_dim"], d["hidden"])
+            self.dit = nn.ModuleList([DitBlock(d) for _ in range(d["layers"])])
+            self.act_out = nn.Linear(d["hidden"], cfg["action_dim"])
+
+        def forward(self, img, text_ids, noise):
+            vis = torch.cat((self.vit(img), self.siglip(img)), dim=-1)
+            vis = self.proj2(F.gelu(self.proj1(vis), approximate="tanh"))
+            x = torch.cat((vis, self.embed(text_ids)), dim=0)
+            t, hd = x.shape[0], cfg["llm"]["hidden"] // cfg["llm"]["heads"]
+            inv = 1.0 / (10000.0 ** (torch.arange(0, hd, 2, device=x.device).float() / hd))
+            ang = torch.outer(torch.arange(t, device=x.device).float(), inv)
+            ang = torch.cat((ang, ang), dim=-1)[:, None, :]
+            cos, sin = ang.cos().to(x.dtype), ang.sin().to(x.dtype)
+            for b in self.llm:
+                x = b(x, cos, sin)
+            cog = self.cond(self.llm_norm(x)[-1:])  # cognition feature of the last token
+            a = noise
+            for step in range(cfg["denoise_steps"]):
+                freq = torch.exp(-torch.arange(128, device=x.device).float() * (9.21 / 128)) * (1000.0 * step)
+                temb = torch.cat((freq.sin(), freq.cos()))[None].to(x.dtype)
+                c = cog + self.t_embed(temb)
+                h = self.act_in(a)
+                for b in self.dit:
+                    h = b(h, c)
+                a = a - 0.1 * self.act_out(h)
+            return a
+
+    torch.manual_seed(seed)
+    with torch.device(device):
+        model = Vla().to(torch.bfloat16)
+    with torch.no_grad():
+        for mod in model.modules():
+            if isinstance(mod, (nn.Linear, nn.Embedding, nn.Conv2d)):
+                mod.weight.normal_(0.0, 0.02)
+                if getattr(mod, "bias", None) is not None:
+                    mod.bias.zero_()
+    return model.eval()
+
+
+def run_cogact(args):
+    import contextlib
+
+    import torch
+
+    from vla_abft_estimate_b200.abft import AbftConfig, AbftInjector, AbftStatsCollector, CheapSumChecker
+
+    cfg = COGACT
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    model = build_cogact(cfg, dev)
+    g = torch.Generator(device=dev).manual_seed(3)
+    img = torch.randn(1, 3, 224, 224, device=dev, generator=g).bfloat16()
+    text = torch.randint(0, cfg["vocab"], (cfg["text_tokens"],), device=dev, generator=g)
+    noise = torch.randn(cfg["action_tokens"], cfg["action_dim"], device=dev, generator=g).bfloat16()
+    reps = max(min(args.steps, 10), 3)
+
+    def timed(ctx_factory):
+        times = []
+        out = None
+        with torch.inference_mode():
+            for i in range(2 + reps):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                torch.cuda.synchronize()
+                e0.record()
+                with ctx_factory():
+                    out = model(img, text, noise)
+                e1.record()
+                torch.cuda.synchronize()
+                if i >= 2:
+                    times.append(e0.elapsed_time(e1))
+        return statistics.median(times), out
+
+    stats_chk = AbftStatsCollector()
+    cfg_chk = AbftConfig(enable=True, checker_backend="b200", detect_only=False)
+    inj_chk = AbftInjector(cfg_chk, CheapSumChecker(cfg_chk), stats_chk, defer_reports=True)
+    stats_off = AbftStatsCollector()
+    cfg_off = AbftConfig(enable=True, check_enable=False, checker_backend="b200")
+    inj_off = AbftInjector(cfg_off, CheapSumChecker(cfg_off), stats_off, defer_reports=True)
+    t_torch, a_torch = timed(contextlib.nullcontext)
+    t_off, _ = timed(lambda: inj_off)
+    t_chk, a_chk = timed(lambda: inj_chk)
+    summ = stats_chk.export_summary()
+
+    stats_f = AbftStatsCollector()
+    cfg_f = AbftConfig(enable=True, checker_backend="b200", detect_only=False, inject_fault=True,
+                       inject_probability=0.02, inject_magnitude=4.0, seed=5)
+    inj_f = AbftInjector(cfg_f, CheapSumChecker(cfg_f), stats_f, defer_reports=True)
+    with torch.inference_mode(), inj_f:
+        a_f = model(img, text, noise)
+    torch.cuda.synchronize()
+    fs = stats_f.export_summary()
+    per_fwd = summ["abft"]["checks_total"] // (2 + reps)
+    line = {
+        "metric": "CogACT-style VLA forward latency (every linear ABFT-protected)",
+        "value": t_chk, "unit": "ms", "n_gpus": 1, "steps": reps, "warmup": 2, "ms_per_step": t_chk,
+        "higher_is_better": False, "scaling": "none", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random init N(0,0.02), random image, text ids and action noise)",
+        "config": {"workload": "ViT-L/14 + SigLIP-So400m/14 (256 patches) -> MLP projector -> Llama-2-7B-shaped "
+                               "decoder over 256 + 32 tokens -> DiT-B action head, 16 action tokens x 7, "
+                               f"{cfg['denoise_steps']} denoising steps, batch 1", **{k: v for k, v in cfg.items()}},
+        "ms": {"torch": t_torch, "b200_unchecked": t_off, "b200_abft": t_chk},
+        "overhead_vs_torch_pct": 100.0 * (t_chk / t_torch - 1.0),
+        "overhead_vs_unchecked_pct": 100.0 * (t_chk / t_off - 1.0),
+        "checked_linears_per_forward": per_fwd,
+        "skipped_unsupported_per_forward": summ["abft"]["faults"]["skipped_unsupported"] // (2 + reps),
+        "clean_detections": summ["abft"]["faults"]["detected_total"],
+        "fault_leg": {"injected": fs["fault_injection"]["injections_total"],
+                      "detected_injections": fs["fault_injection"]["detected_injections_total"],
+                      "faults": {k: v for k, v in fs["abft"]["faults"].items() if k != "located"},
+                      "max_abs_action_diff_vs_clean": (a_f.float() - a_chk.float()).abs().max().item()},
+        "actions_max_abs_diff_torch_vs_abft": (a_torch.float() - a_chk.float()).abs().max().item(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
+    if args.model == "cogact":
+        run_cogact(args)
+        return
     if args.model:
         run_model(args)
         return

@@ -427,3 +427,29 @@ def test_swap_forced_and_refused(cuda_device):
     # few rows, swap refused: the ordinary row checks
     a, w, b, c, r, orc = run_swapped(cuda_device, 8, 512, 256, [(2, 100)], swap_ab=1)
     assert r.coords() == [(2, 100)] and r.tile_n in (120, 248)
+
+
+# ------------------------------------- stress: back-to-back stream-K launches
+@pytest.mark.parametrize("m,n,k,tile_m", [(288, 12288, 4096, 256), (288, 4096, 11008, 128), (512, 4608, 3584, 0),
+                                          (4096, 4096, 4096, 0), (24, 4096, 4096, 0)])
+def test_back_to_back_stream_k_launches_stay_clean(cuda_device, m, n, k, tile_m):
+    """Many launches queued without a host sync (each with its own report):
+    no record on clean data, every output equal to the first. Stream-K
+    partials must be fully visible before a contributor's flag is."""
+    torch.manual_seed(m + n + k)
+    a = (torch.randn(m, k, device=cuda_device) * k ** -0.5).bfloat16()
+    w = (torch.randn(n, k, device=cuda_device) * k ** -0.5).bfloat16()
+    tn = ops.pick_tile_n(m, n, k, cuda_device)
+    cks = ops.encode_weight(w, tn)
+    calls = 80
+    arena = torch.zeros(calls * 2048, dtype=torch.uint8, device=cuda_device)
+    outs = []
+    for i in range(calls):
+        rep = ops.ReportBuffer(64, cuda_device, tensor=arena[i * 2048:(i + 1) * 2048])
+        outs.append(ops.abft_gemm(a, w, tile_n=tn, tile_m=tile_m, checksums=cks, report=rep)[0])
+    torch.cuda.synchronize()
+    host = arena.cpu().numpy().tobytes()
+    for i in range(calls):
+        r = N.FaultReport.from_bytes(host[i * 2048:(i + 1) * 2048])
+        assert r.n_faults == 0 and r.status == 0, (i, r.records[:3])
+        assert torch.equal(outs[i], outs[0]), i

@@ -389,7 +389,7 @@ int make_plan(const abft_gemm_args* a, int dev, int sms, Plan* pl) {
     pl->sk_part_off = off;
     off = align256(off + static_cast<size_t>(pl->grid) * kBM * pl->bn * sizeof(float));
     pl->sk_flag_off = off;
-    off = align256(off + static_cast<size_t>(pl->grid) * sizeof(unsigned long long));
+    off = align256(off + static_cast<size_t>(pl->grid) * 8 * sizeof(unsigned long long));  // a flag per epilogue warp
   }
   pl->total = off;
   return ABFT_OK;

@@ -77,7 +77,7 @@ struct GemmCfg {
   static constexpr int kStageBytes = 32 * 32 * 2;
   static constexpr int kOffStage = kOffX + (CHECK ? kXBytes : 0);
   static constexpr int kOffBar = kOffStage + 8 * kStageBytes;
-  static constexpr int kNumBars = 2 * kStages + 2 * 3 + 2;  // full, empty, tfull, tempty, xbar, drain, pbar
+  static constexpr int kNumBars = 2 * kStages + 2 * 3 + 1;  // full, empty, tfull, tempty, xbar, drain
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffMisc + 64 + 1024;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
@@ -115,7 +115,7 @@ struct GemmParams {
   int sk_ctas;  // stream-K units: CTAs, or CTA pairs
   int64_t sk_iters;
   float* partials;  // [G][BN/4][128][4] fp32: a CTA's share of a tile it does not finish
-  unsigned long long* flags;  // [G]: set to `nonce` once that CTA's partial is visible
+  unsigned long long* flags;  // [G][8]: per epilogue warp, set to `nonce` once its share of the partial is visible
   uint64_t nonce;   // unique to this launch: stream-K flags and report->launch_tag carry it
   // Last tile column when it holds fewer than BD data columns (tail_n != 0):
   // its B-operand tile is compact (data rows, then with checks the 8
@@ -345,7 +345,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tempty = tfull + 2;    // [2]
   uint64_t* xbar = tempty + 2;     // [2] row-half partials exchanged
   uint64_t* drain = xbar + 2;
-  uint64_t* pbar = drain + 1;  // epilogue threads stored their stream-K partial (once per launch)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::kOffMisc + 4);
 
@@ -367,7 +366,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&xbar[b], kEpiThreads);
     }
     mbar_init(drain, 1);
-    mbar_init(pbar, kEpiThreads);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -598,15 +596,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           acc = 0;
           acc_phase ^= 1u;
         }
-        // Every epilogue thread's stores precede its arrival (release); one
-        // thread waits for all of them (acquire, bounded), makes them
-        // visible device-wide and publishes the flag. A CTA stores at most
-        // one partial per launch, so pbar completes once (parity 0).
-        mbar_arrive(pbar);
-        if (ep == 0 && lane == 0 && mbar_wait(pbar, 0, abort_flag)) {
-          __threadfence();
-          st_release_u64(&p.flags[blockIdx.x], p.nonce);
-        }
+        // Each warp publishes its own share (32 rows x one column half):
+        // every lane makes its stores visible device-wide, then lane 0
+        // releases the warp's flag. A finisher warp waits only for the
+        // warps whose rows and columns it reads; no CTA-wide hand-off.
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) st_release_u64(&p.flags[blockIdx.x * 8 + ep], p.nonce);
         continue;
       }
 
@@ -632,7 +628,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int u = unit + 1; u < p.sk_ctas; ++u) {
           if (SegmentIter::sk_begin(p, u) >= tile_end) break;
           const int cc = u * G + static_cast<int>(rank);
-          if (!wait_flag(&p.flags[cc], p.nonce, abort_flag)) {
+          // this warp's rows and column half; with checks also the warp of
+          // the same rows that stored the checksum columns (the other half
+          // when chk_col lies there: 248 of a full tile, anywhere in a tail)
+          const int chk_ep = (ep & 3) + (chk_col >= NV ? 4 : 0);
+          if (!wait_flag(&p.flags[cc * 8 + ep], p.nonce, abort_flag) ||
+              (CHECK && chk_ep != ep && !wait_flag(&p.flags[cc * 8 + chk_ep], p.nonce, abort_flag))) {
             okp = false;
             break;
           }
