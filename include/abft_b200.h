@@ -14,6 +14,9 @@
  *      pytorch/abft/kernels/abft_fused.cu:92-141)
  *   s_b = b.sum(dim=1) recomputed per call             abft_encode_weight (once per
  *     (pytorch/abft/checkers.py:119)                     weight, cacheable)
+ *   torch.bmm(a, b) then a Python loop of per-batch    abft_gemm_bf16 with batch > 1
+ *     2-D checks (pytorch/abft/injector.py:176-187)     (all batches in one launch,
+ *                                                        per-batch fault counts)
  *
  * Conventions
  *   - Every pointer argument that names tensor data is a DEVICE pointer.
@@ -37,7 +40,7 @@
 extern "C" {
 #endif
 
-#define ABFT_B200_VERSION 1
+#define ABFT_B200_VERSION 2
 
 /* ---- return codes ------------------------------------------------------- */
 enum abft_status {
@@ -72,7 +75,8 @@ enum abft_status {
 
 /* One detected fault: the (row, tile-segment) whose checksums disagree.
  * `col` is the located global column, or -1 when the weighted residual did
- * not pin a single column. `residual` is (actual - expected) row sum over the
+ * not pin a single column. In a batched call `row` is flattened over the
+ * batch: b * M + i for row i of batch b. `residual` is (actual - expected) row sum over the
  * tile segment (the fault magnitude for a single fault), `residual_w` the same
  * for the column-index-weighted sum, `threshold` the bound it was tested on. */
 typedef struct abft_fault_record {
@@ -103,9 +107,12 @@ typedef struct abft_report {
   float abs_err;         /* ABFT_MODE_REF: |corner - sum_c|                    */
   float rel_err;         /* ABFT_MODE_REF: abs_err / max(|sum_c|, 1)           */
   int32_t ref_ok;        /* ABFT_MODE_REF: 1 pass, 0 fail; -1 not evaluated     */
-  uint32_t reserved;
+  uint32_t batch;        /* per-batch counter entries after the records (0 = none) */
   uint64_t launch_tag;   /* fused GEMM: tag of the launch that wrote the header */
-  /* abft_fault_record records[capacity] follows (64-byte header). */
+  /* abft_fault_record records[capacity] follows (64-byte header); a batched
+   * fused call (batch > 1) then writes uint32_t counts[batch][4] = {faults,
+   * located, corrected, 0} of each batch, complete even when records
+   * overflowed. Size such a report with abft_report_bytes_batched(). */
 } abft_report;
 
 /* Arguments of the fused checksum-protected GEMM
@@ -142,6 +149,23 @@ typedef struct abft_gemm_args {
                           /* for M <= 64 when tile_m is 0); checksums then     */
                           /* come from A, per                                  */
                           /* call, and `checksums` is not used                */
+  /* Batched products (torch.bmm): C[b] = A[b] B[b]^T for b < batch, in one
+   * launch. batch 0 or 1 is a single product and the strides are ignored.
+   * With batch > 1, matrix b of each operand starts stride_* elements after
+   * matrix b - 1 (multiples of 8; stride_c a multiple of ldc of at least
+   * M * ldc: C's batches are disjoint row blocks), `checksums` (optional)
+   * holds the blocks
+   * of all batches back to back (abft_encode_weight_batched), inject_rows
+   * and the records use rows flattened over the batch, the report needs
+   * abft_report_bytes_batched(report_capacity, batch) bytes, and
+   * ABFT_MODE_REF is not supported. */
+  int32_t batch;
+  /* Layout of B: 0 = [N, ldb] (K-major, nn.Linear.weight); 1 = [K, ldb]
+   * with N columns (N-major, torch.bmm's mat2 as stored), copied K-major
+   * into the workspace by the call (its checksums computed on the way;
+   * `checksums` must then be NULL). */
+  int32_t b_kn;
+  int64_t stride_a, stride_b, stride_c;
 } abft_gemm_args;
 
 #define ABFT_MAX_INJECT 64
@@ -152,6 +176,10 @@ const char* abft_status_string(int status);
 
 /* Bytes of a report with `capacity` records. */
 size_t abft_report_bytes(int32_t capacity);
+
+/* Bytes of the report of a batched fused call: `capacity` records and the
+ * per-batch counters (equal to abft_report_bytes(capacity) for batch <= 1). */
+size_t abft_report_bytes_batched(int32_t capacity, int32_t batch);
 
 /* Tile width (256 or 128) the library picks for an M x N x K GEMM in `mode`
  * when tile_n == 0: the shorter estimated time over num_sms (whole-tile
@@ -180,6 +208,12 @@ size_t abft_checksum_bytes(int64_t N, int64_t K, int32_t tile_n);
  * of checkers.py:119. */
 int abft_encode_weight(const void* B, int64_t N, int64_t K, int64_t ldb,
                        int32_t tile_n, void* out, void* stream);
+
+/* abft_encode_weight of `batch` matrices B + b * stride_b (stride_b a
+ * multiple of 8 elements); block b lands at out + b * abft_checksum_bytes(N,
+ * K, tile_n). */
+int abft_encode_weight_batched(const void* B, int64_t N, int64_t K, int64_t ldb, int64_t stride_b,
+                               int32_t batch, int32_t tile_n, void* out, void* stream);
 
 /* Workspace the fused GEMM needs for these arguments (0 when none). */
 size_t abft_gemm_workspace_bytes(const abft_gemm_args* args);

@@ -123,3 +123,140 @@ def test_report_arena_spans_chunks(cuda_device):
     assert s["fault_injection"]["injections_total"] == n_inj
     assert s["fault_injection"]["detected_injections_total"] == n_inj
     assert s["abft"]["faults"]["corrected_total"] == n_inj
+
+
+# ------------------------------------------------------------ torch.bmm / matmul
+# (batch, M, N, K, layout of mat2): row-major [B, K, N], or the transpose of a
+# K-major [B, N, K] (attention scores, q @ k^T); M = 1 is decode-shaped.
+BMM_CALLS = [(4, 96, 256, 128, "rowmajor"), (8, 1, 512, 128, "view"), (3, 64, 136, 72, "rowmajor"),
+             (2, 200, 248, 256, "view")]
+
+
+def bmm_operands(device, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    out = []
+    for bsz, m, n, k, lay in BMM_CALLS:
+        a = (torch.randn(bsz, m, k, generator=g) * k ** -0.5).bfloat16().to(device)
+        w = (torch.randn(bsz, n, k, generator=g) * k ** -0.5).bfloat16().to(device)
+        out.append((a, w.transpose(1, 2).contiguous() if lay == "rowmajor" else w.transpose(1, 2)))
+    return out
+
+
+def run_bmms(operands, cfg, defer):
+    stats = AbftStatsCollector()
+    inj = AbftInjector(cfg, CheapSumChecker(cfg), stats, defer_reports=defer)
+    with torch.inference_mode(), inj:
+        outs = [torch.bmm(a, b) for a, b in operands]
+    torch.cuda.synchronize()
+    return outs, stats.export_summary()
+
+
+def expected_bmm(cfg):
+    """(call, batch, row, col) of each drawn fault and the sample coin of
+    every batch, in the reference's order: the injection draw over the
+    whole output, then one check gate per batch (injector.py:176-187)."""
+    rng = O.InjectorRng(cfg.seed)
+    faults, gates = [], []
+    for ci, (bsz, m, n, _, _) in enumerate(BMM_CALLS):
+        idx = rng.maybe_inject(bsz * m * n, cfg.inject_fault, cfg.inject_probability)
+        gates.append([rng.sample(cfg.sample_rate) for _ in range(bsz)])
+        if idx is not None:
+            faults.append((ci, idx // (m * n), (idx // n) % m, idx % n))
+    return faults, gates
+
+
+def test_bmm_clean_one_check_per_batch(cuda_device):
+    operands = bmm_operands(cuda_device)
+    for defer in (False, True):
+        cfg = AbftConfig(enable=True, checker_backend="b200", detect_only=False)
+        outs, s = run_bmms(operands, cfg, defer)
+        assert s["abft"]["checks_total"] == sum(c[0] for c in BMM_CALLS)
+        assert s["abft"]["checks_by_op"] == {"bmm": sum(c[0] for c in BMM_CALLS)}
+        assert s["abft"]["fail_total"] == 0 and s["abft"]["faults"]["detected_total"] == 0
+        for (a, b), o in zip(operands, outs):
+            ref = torch.bmm(a.float(), b.float())
+            assert (o.float() - ref).abs().max().item() <= 1e-2 * ref.abs().max().item()
+
+
+@pytest.mark.parametrize("seed,prob", [(4, 1.0), (12, 0.6)])
+def test_bmm_faults_located_corrected_with_reference_rng(cuda_device, seed, prob):
+    operands = bmm_operands(cuda_device)
+    with torch.inference_mode():
+        clean = [torch.bmm(a, b) for a, b in operands]
+    cfg = AbftConfig(enable=True, checker_backend="b200", detect_only=False, inject_fault=True,
+                     inject_probability=prob, inject_magnitude=500.0, seed=seed)
+    want, _ = expected_bmm(cfg)
+    summaries = []
+    for defer in (False, True):
+        outs, s = run_bmms(operands, cfg, defer)
+        f = s["abft"]["faults"]
+        assert s["fault_injection"]["injections_total"] == len(want)
+        # only the faulty batch's check fails; every batch's check carries the call's injected flag
+        assert s["fault_injection"]["detected_injections_total"] == len(want)
+        assert s["abft"]["fail_total"] == len(want) and f["corrected_total"] == len(want)
+        assert sorted((p["row"], p["col"]) for p in f["located"]) == sorted((r, c) for _, _, r, c in want)
+        for o, c in zip(outs, clean):
+            assert (o.float() - c.float()).abs().max().item() <= 1e-2 * c.float().abs().max().item()
+        summaries.append(s)
+    assert summaries[0]["abft"] == summaries[1]["abft"]
+
+
+def test_bmm_sampled_batches_only(cuda_device):
+    """sample_rate < 1: each batch draws its own coin, as in the reference's
+    loop; only sampled batches are checked (and corrected)."""
+    operands = bmm_operands(cuda_device)
+    cfg = AbftConfig(enable=True, checker_backend="b200", detect_only=False, inject_fault=True,
+                     inject_probability=1.0, inject_magnitude=500.0, seed=8, sample_rate=0.5)
+    want, gates = expected_bmm(cfg)
+    outs, s = run_bmms(operands, cfg, True)
+    assert s["abft"]["checks_total"] == sum(sum(g) for g in gates)
+    caught = [(ci, b, r, c) for ci, b, r, c in want if gates[ci][b]]
+    missed = [(ci, b, r, c) for ci, b, r, c in want if not gates[ci][b]]
+    assert s["fault_injection"]["detected_injections_total"] == len(caught)
+    assert sorted((p["row"], p["col"]) for p in s["abft"]["faults"]["located"]) == sorted((r, c) for _, _, r, c in caught)
+    with torch.inference_mode():
+        for ci, b, r, c in missed:  # an unchecked batch keeps its fault
+            a, m2 = operands[ci]
+            ref = torch.bmm(a[b:b + 1].float(), m2[b:b + 1].float())[0, r, c].item()
+            assert abs(outs[ci][b, r, c].float().item() - ref) > 250.0
+
+
+def test_matmul_two_d_fused_and_batched_rhs_follows_reference(cuda_device):
+    """torch.matmul with a 2-D right operand: one fused check over the
+    flattened rows. With a batched right operand the reference checks
+    nothing but still draws its sample coin; check_batched_matmul checks
+    every batch."""
+    g = torch.Generator().manual_seed(3)
+    x = (torch.randn(2, 48, 128, generator=g) * 128 ** -0.5).bfloat16().to(cuda_device)
+    w = (torch.randn(128, 256, generator=g) * 128 ** -0.5).bfloat16().to(cuda_device)
+    q = (torch.randn(2, 4, 32, 64, generator=g) * 64 ** -0.5).bfloat16().to(cuda_device)
+    kt = (torch.randn(2, 4, 64, 32, generator=g) * 64 ** -0.5).bfloat16().to(cuda_device)
+    for check_batched in (False, True):
+        cfg = AbftConfig(enable=True, checker_backend="b200", detect_only=False, inject_fault=True,
+                         inject_probability=1.0, inject_magnitude=500.0, seed=21, sample_rate=0.99,
+                         check_batched_matmul=check_batched)
+        rng = O.InjectorRng(cfg.seed)
+        i1 = rng.maybe_inject(96 * 256, True, 1.0)
+        g1 = rng.sample(cfg.sample_rate)
+        i2 = rng.maybe_inject(2 * 4 * 32 * 32, True, 1.0)
+        g2 = rng.sample(cfg.sample_rate)
+        stats = AbftStatsCollector()
+        inj = AbftInjector(cfg, CheapSumChecker(cfg), stats, defer_reports=True)
+        with torch.inference_mode(), inj:
+            y = torch.matmul(x, w)
+            sc = torch.matmul(q, kt)
+        s = stats.export_summary()
+        ref = torch.matmul(x.float(), w.float())
+        assert tuple(y.shape) == (2, 48, 256)
+        assert (y.float() - ref).abs().max().item() <= 1e-2 * ref.abs().max().item()
+        n_checks = int(g1) + (8 * int(g2) if check_batched else 0)
+        assert s["abft"]["checks_total"] == n_checks
+        located = sorted((p["row"], p["col"]) for p in s["abft"]["faults"]["located"])
+        want = ([(i1 // 256, i1 % 256)] if g1 else []) + ([((i2 // 32) % 32, i2 % 32)] if g2 and check_batched else [])
+        assert located == sorted(want)
+        flat = sc.reshape(-1)
+        clean = torch.matmul(q.float(), kt.float()).reshape(-1)
+        if not check_batched:  # unchecked: the drawn fault stays in the scores
+            assert abs(flat[i2].float().item() - clean[i2].item()) > 250.0
+        else:
+            assert (flat.float() - clean).abs().max().item() <= 1e-2 * clean.abs().max().item()

@@ -27,7 +27,7 @@ def test_library_exports_every_declared_symbol():
     L = N.lib()
     for name in declared_functions():
         assert hasattr(L, name), name
-    assert L.abft_version() == 1
+    assert L.abft_version() == N.LIB_VERSION == 2
 
 
 def test_status_strings():
@@ -40,6 +40,8 @@ def test_host_only_helpers():
     L = N.lib()
     assert L.abft_report_bytes(0) == 64
     assert L.abft_report_bytes(10) == 64 + 10 * 24
+    assert L.abft_report_bytes_batched(10, 1) == 64 + 10 * 24
+    assert L.abft_report_bytes_batched(10, 32) == 64 + 10 * 24 + 32 * 16  # counters after the records
     assert L.abft_pick_tile_n(512, 4096, 4096, 148, 3) == 128  # 140 narrow tiles: one wave, no partials
     assert L.abft_pick_tile_m(512, 4608, 3584, 148, 3, 256) == 256  # 38 pair tiles beat 39 x 4 narrow ones
     assert L.abft_pick_tile_m(8192, 8192, 8192, 148, 3, 256) == 256
@@ -79,6 +81,35 @@ def test_gemm_argument_validation_without_gpu():
     a.n_inject = N.MAX_INJECT + 1
     assert L.abft_gemm_bf16(ctypes.byref(a), None) == -1
     a.n_inject = 0
+    # batched products
+    a.batch = -1
+    assert L.abft_gemm_bf16(ctypes.byref(a), None) == -1
+    a.batch = 4
+    a.stride_a, a.stride_b, a.stride_c = 128 * 72, 256 * 72, 128 * 256
+    a.stride_b += 4
+    assert L.abft_gemm_bf16(ctypes.byref(a), None) == -2  # stride not a multiple of 8
+    a.stride_b -= 4
+    a.stride_c = 127 * 256
+    assert L.abft_gemm_bf16(ctypes.byref(a), None) == -1  # C batches would overlap
+    a.stride_c = 128 * 256 + 8
+    assert L.abft_gemm_bf16(ctypes.byref(a), None) == -1  # not whole rows of ldc
+    a.stride_c = 128 * 256
+    a.mode = N.MODE_REF
+    assert L.abft_gemm_bf16(ctypes.byref(a), None) == -3  # scalar check is per product only
+    a.mode = N.MODE_DETECT
+    a.batch = 70000
+    assert L.abft_gemm_bf16(ctypes.byref(a), None) == -3
+    a.batch = 4
+    a.b_kn = 2
+    assert L.abft_gemm_bf16(ctypes.byref(a), None) == -1
+    a.b_kn = 1
+    assert L.abft_gemm_bf16(ctypes.byref(a), None) == -1  # [K, ldb] needs ldb >= N (72 < 256)
+    a.ldb = 256
+    a.checksums = 0x50000
+    assert L.abft_gemm_bf16(ctypes.byref(a), None) == -1  # an N-major B gets its checksums from the copy
+    a.checksums = None
+    assert L.abft_encode_weight_batched(ctypes.c_void_p(0x10000), 8, 8, 8, 12, 2, 256, ctypes.c_void_p(0x20000),
+                                        None) == -2
     # valid arguments: the next step is the device query, which fails cleanly here
     import torch
 
@@ -109,14 +140,16 @@ def test_struct_layouts_match_c(tmp_path):
     src = tmp_path / "sz.c"
     src.write_text(
         '#include <stdio.h>\n#include <stddef.h>\n#include "abft_b200.h"\n'
-        "int main(void){printf(\"%zu %zu %zu %zu %zu %zu\\n\", sizeof(abft_gemm_args), "
-        "offsetof(abft_gemm_args, report), sizeof(abft_check_args), offsetof(abft_check_args, workspace), "
+        "int main(void){printf(\"%zu %zu %zu %zu %zu %zu %zu %zu\\n\", sizeof(abft_gemm_args), "
+        "offsetof(abft_gemm_args, report), offsetof(abft_gemm_args, batch), offsetof(abft_gemm_args, stride_c), "
+        "sizeof(abft_check_args), offsetof(abft_check_args, workspace), "
         "sizeof(abft_report), sizeof(abft_fault_record));return 0;}\n")
     exe = tmp_path / "sz"
     subprocess.check_call(["gcc", f"-I{_build.INCLUDE_DIR}", str(src), "-o", str(exe)])
     vals = [int(x) for x in subprocess.check_output([str(exe)]).split()]
-    assert vals == [ctypes.sizeof(N.GemmArgs), N.GemmArgs.report.offset, ctypes.sizeof(N.CheckArgs),
-                    N.CheckArgs.workspace.offset, N.REPORT_HEADER_BYTES, N.RECORD_BYTES]
+    assert vals == [ctypes.sizeof(N.GemmArgs), N.GemmArgs.report.offset, N.GemmArgs.batch.offset,
+                    N.GemmArgs.stride_c.offset, ctypes.sizeof(N.CheckArgs), N.CheckArgs.workspace.offset,
+                    N.REPORT_HEADER_BYTES, N.RECORD_BYTES]
 
 
 def test_report_parsing_round_trip():
@@ -128,3 +161,27 @@ def test_report_parsing_round_trip():
     assert rep.status == 3 and rep.n_faults == 2 and rep.tile_n == 248 and rep.ref_ok == 0
     assert rep.coords() == [(7, 9), (8, -1)]
     assert rep.records[0].corrected and not rep.records[1].located
+
+
+def test_batched_report_parsing_and_views():
+    """A batched report: records with rows flattened over the batch, then
+    {faults, located, corrected, 0} per batch after the record slots."""
+    import struct
+
+    cap, nb, rows = 4, 3, 10
+    hdr = struct.pack("<8I4fi3I", 3, 3, 2, 2, 0, cap, 128, 248, 0.0, 0.0, 0.0, 0.0, -1, nb, 0, 0)
+    recs = (struct.pack("<iifffI", 12, 5, 3.0, 18.0, 0.1, 7) + struct.pack("<iifffI", 25, -1, 2.0, 5.0, 0.1, 1)
+            + struct.pack("<iifffI", 3, 0, 1.0, 1.0, 0.1, 7) + bytes(24))
+    counts = struct.pack("<4I", 1, 1, 1, 0) + struct.pack("<4I", 1, 1, 1, 0) + struct.pack("<4I", 1, 0, 0, 0)
+    rep = N.FaultReport.from_bytes(hdr + recs + counts)
+    assert rep.batch_counts == [(1, 1, 1), (1, 1, 1), (1, 0, 0)]
+    v0, v1, v2 = (rep.batch_view(b, rows) for b in range(nb))
+    assert [(r.row, r.col) for r in v0.records] == [(3, 0)]
+    assert [(r.row, r.col) for r in v1.records] == [(2, 5)]
+    assert [(r.row, r.col) for r in v2.records] == [(5, -1)]
+    assert v2.status == N.STATUS_FAULT | N.STATUS_UNLOCATED and v2.n_located == 0
+    assert v0.status == N.STATUS_FAULT and v0.n_corrected == 1
+    # a one-product report has no counters: batch 0 carries the header counts
+    single = N.FaultReport.from_bytes(struct.pack("<8I4fi3I", 1, 1, 1, 0, 0, 0, 128, 248, 0, 0, 0, 0, -1, 0, 0, 0))
+    assert single.batch_counts == [] and single.batch_view(0, 5).n_faults == 1
+    assert single.batch_view(1, 5).n_faults == 0

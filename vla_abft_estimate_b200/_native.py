@@ -37,15 +37,19 @@ REC_CORRECTED = 4
 MAX_INJECT = 64
 REPORT_HEADER_BYTES = 64
 RECORD_BYTES = 24
+BATCH_COUNT_BYTES = 16  # uint32 {faults, located, corrected, 0} per batch after the records
+LIB_VERSION = 2
 
 EXPORTED_SYMBOLS = (
     "abft_version",
     "abft_status_string",
     "abft_report_bytes",
+    "abft_report_bytes_batched",
     "abft_pick_tile_n",
     "abft_pick_tile_m",
     "abft_checksum_bytes",
     "abft_encode_weight",
+    "abft_encode_weight_batched",
     "abft_gemm_workspace_bytes",
     "abft_gemm_bf16",
     "abft_check_workspace_bytes",
@@ -97,6 +101,11 @@ class GemmArgs(ctypes.Structure):
         ("num_sms", ctypes.c_int32),
         ("tile_m", ctypes.c_int32),
         ("swap_ab", ctypes.c_int32),
+        ("batch", ctypes.c_int32),
+        ("b_kn", ctypes.c_int32),
+        ("stride_a", ctypes.c_int64),
+        ("stride_b", ctypes.c_int64),
+        ("stride_c", ctypes.c_int64),
     ]
 
 
@@ -144,10 +153,15 @@ def lib() -> ctypes.CDLL:
     vp, i32, i64, sz = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_size_t
     L.abft_version.restype = ctypes.c_int
     L.abft_version.argtypes = []
+    if L.abft_version() != LIB_VERSION:
+        raise RuntimeError(f"{path} has ABI version {L.abft_version()}, this binding needs {LIB_VERSION}: "
+                           "rebuild it with `python -m vla_abft_estimate_b200._build`")
     L.abft_status_string.restype = ctypes.c_char_p
     L.abft_status_string.argtypes = [ctypes.c_int]
     L.abft_report_bytes.restype = sz
     L.abft_report_bytes.argtypes = [i32]
+    L.abft_report_bytes_batched.restype = sz
+    L.abft_report_bytes_batched.argtypes = [i32, i32]
     L.abft_pick_tile_n.restype = i32
     L.abft_pick_tile_n.argtypes = [i64, i64, i64, i32, ctypes.c_uint32]
     L.abft_pick_tile_m.restype = i32
@@ -156,6 +170,8 @@ def lib() -> ctypes.CDLL:
     L.abft_checksum_bytes.argtypes = [i64, i64, i32]
     L.abft_encode_weight.restype = ctypes.c_int
     L.abft_encode_weight.argtypes = [vp, i64, i64, i64, i32, vp, vp]
+    L.abft_encode_weight_batched.restype = ctypes.c_int
+    L.abft_encode_weight_batched.argtypes = [vp, i64, i64, i64, i64, i32, i32, vp, vp]
     L.abft_gemm_workspace_bytes.restype = sz
     L.abft_gemm_workspace_bytes.argtypes = [ctypes.POINTER(GemmArgs)]
     L.abft_gemm_bf16.restype = ctypes.c_int
@@ -216,6 +232,8 @@ class FaultReport:
     rel_err: float = 0.0
     ref_ok: int = -1
     records: List[FaultRecord] = field(default_factory=list)
+    # batched calls: (faults, located, corrected) of each batch
+    batch_counts: List[tuple] = field(default_factory=list)
 
     @property
     def fault_detected(self) -> bool:
@@ -235,10 +253,33 @@ class FaultReport:
             raise ValueError("report buffer shorter than its header")
         (status, n_faults, n_located, n_corrected, overflow, capacity, tile_m, tile_n, corner, sum_c, abs_err,
          rel_err, ref_ok) = struct.unpack_from("<8I4fi", buf, 0)
+        (batch,) = struct.unpack_from("<I", buf, 52)
         rep = cls(status, n_faults, n_located, n_corrected, overflow, capacity, tile_m, tile_n, corner, sum_c,
                   abs_err, rel_err, ref_ok)
         n = min(n_faults, capacity, (len(buf) - REPORT_HEADER_BYTES) // RECORD_BYTES)
         for i in range(n):
             row, col, res, resw, thr, flags = struct.unpack_from("<iifffI", buf, REPORT_HEADER_BYTES + i * RECORD_BYTES)
             rep.records.append(FaultRecord(row, col, res, resw, thr, flags))
+        base = REPORT_HEADER_BYTES + capacity * RECORD_BYTES
+        if batch and len(buf) >= base + batch * BATCH_COUNT_BYTES:
+            rep.batch_counts = [struct.unpack_from("<3I", buf, base + b * BATCH_COUNT_BYTES) for b in range(batch)]
         return rep
+
+    def batch_view(self, b: int, rows: int) -> "FaultReport":
+        """The part of a batched report that belongs to batch ``b`` (``rows``
+        rows of C per batch): its counts, and its records with rows local to
+        the batch. Without per-batch counters (a one-product call, or an
+        empty launch whose header is zero) batch 0 has the header's counts."""
+        if b < len(self.batch_counts):
+            f, loc, cor = self.batch_counts[b]
+        elif not self.batch_counts and b == 0:  # a one-product call: the header counts
+            f, loc, cor = self.n_faults, self.n_located, self.n_corrected
+        else:
+            f, loc, cor = 0, 0, 0
+        recs = [FaultRecord(r.row - b * rows, r.col, r.residual, r.residual_w, r.threshold, r.flags)
+                for r in self.records if b * rows <= r.row < (b + 1) * rows]
+        status = (STATUS_FAULT if f else 0) | (STATUS_UNLOCATED if f > loc else 0)
+        status |= STATUS_OVERFLOW if len(recs) < f and (self.status & STATUS_OVERFLOW) else 0
+        status |= self.status & STATUS_DEVICE_TIMEOUT
+        return FaultReport(status, f, loc, cor, max(f - len(recs), 0), self.capacity, self.tile_m, self.tile_n,
+                           records=recs)

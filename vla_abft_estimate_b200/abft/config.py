@@ -48,6 +48,14 @@ class AbftConfig:
 
     # ---- B200 library additions -------------------------------------------------
     fused_linear: bool = True  # b200 backend: one fused GEMM+check kernel per F.linear
+    # b200 backend: torch.bmm (all batches) and torch.matmul with a 2-D right
+    # operand run as one fused GEMM+check launch, per-batch results as the
+    # reference's per-batch loop records them
+    fused_matmul: bool = True
+    # torch.matmul with a batched right operand (attention scores): the
+    # reference leaves it unchecked (its b_2d is None); True checks every
+    # batch through the fused kernel (b200 backend), recorded as "matmul"
+    check_batched_matmul: bool = False
     thr_scale: float = 1e-3  # tau of the per-tile row-checksum bound tau*sqrt(K)*max|C|
     thr_abs: float = 0.0  # absolute floor added to that bound
     report_capacity: int = 64  # fault records kept per call

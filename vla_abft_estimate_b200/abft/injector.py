@@ -4,24 +4,30 @@ Inside ``with AbftInjector(cfg, checker, stats):`` the module attributes
 ``F.linear``, ``torch.matmul`` and ``torch.bmm`` are replaced by wrappers, as
 in the reference (injector.py:31-51), and restored on exit.
 
-* ``torch.matmul`` / ``torch.bmm`` keep the reference flow: run the op,
-  maybe perturb one output element, then ``checker.check`` on the flattened
-  operands (injector.py:164-187).
 * ``F.linear`` with ``checker_backend="b200"`` and ``fused_linear`` replaces
   "torch GEMM, then check" by one call of the fused kernel
   (``abft_gemm_bf16``): the GEMM, its per-tile weighted row checksums and
   the compare run in one launch, a drawn fault is added to the fp32
   accumulator before the compare, and with ``detect_only=False`` located
-  faults are corrected before the bf16 store. Other backends, or operands
-  the library cannot take, follow the reference flow.
+  faults are corrected before the bf16 store.
+* ``torch.bmm`` and ``torch.matmul`` with a 2-D right operand, with
+  ``fused_matmul``, run the same way as one batched launch; a bmm records
+  one check per batch, as the reference's per-batch loop does
+  (injector.py:176-187). ``torch.matmul`` with a batched right operand is
+  unchecked in the reference (its ``b_2d`` is None, checkers.py:145-149);
+  ``check_batched_matmul`` checks it per batch.
+* Other backends, operands the library cannot take (CPU, non-bf16, K or N
+  not a multiple of 8) and calls that need autograd follow the reference
+  flow: run the op, maybe perturb one output element, then
+  ``checker.check`` on the flattened operands (injector.py:152-187).
 
 The random stream is the reference's: one ``random.Random(cfg.seed)`` per
 injector, consumed in the same order -- the injection coin and index after
 the op (:58-75), then the sampling coin inside the check gate (:53-56,
 :77-99) -- so a seed selects the same faults on both implementations.
 
-Reports of fused linears can be deferred (``defer_reports=True``): the
-fault report stays on the device and is read at ``flush()`` (called on exit)
+Reports of fused calls can be deferred (``defer_reports=True``): the fault
+report stays on the device and is read at ``flush()`` (called on exit)
 instead of forcing a device->host sync per GEMM like the reference (:103).
 """
 from __future__ import annotations
@@ -142,7 +148,10 @@ class AbftInjector(AbstractContextManager):
         self._orig_matmul: Optional[Callable[..., torch.Tensor]] = None
         self._orig_bmm: Optional[Callable[..., torch.Tensor]] = None
         self._dump_done: bool = False
-        self._pending: List[Tuple[int, str, str, str, bool]] = []
+        # deferred records: (device, op, phase, shape key, injected, batched)
+        # with batched = None (next report of the device's arena) or
+        # (report buffer, batches, rows per batch, gates)
+        self._pending: List[Tuple[int, str, str, Any, bool, Any]] = []
         self._arenas: dict = {}
         self._tile_n: dict = {}
 
@@ -171,23 +180,34 @@ class AbftInjector(AbstractContextManager):
         return None
 
     def flush(self) -> None:
-        """Record every deferred fused-linear report (one copy per device)."""
+        """Record every deferred fused-call report, in call order (one copy
+        per device for the fused linears, one per batched call)."""
         pending, self._pending = self._pending, []
         if not pending:
             return
         reports = {dev: iter(arena.drain()) for dev, arena in self._arenas.items()}
         saved = self.stats.current_phase
         try:
-            for dev, op_name, phase, shape_key, injected in pending:
-                rep = next(reports[dev])
-                if isinstance(shape_key, tuple):  # (m, k, n) of a fused linear
+            for dev, op_name, phase, shape_key, injected, batched in pending:
+                if isinstance(shape_key, tuple):  # (m, k, n) of a fused call
                     m, k, n = shape_key
                     shape_key = f"A{(m, k)}_B{(k, n)}_C{(m, n)}"
                 self.stats.current_phase = phase
-                self.stats.record_check(op_name=op_name, shape_key=shape_key, result=result_from_report(rep),
-                                        injected=injected)
+                if batched is None:
+                    self.stats.record_check(op_name=op_name, shape_key=shape_key,
+                                            result=result_from_report(next(reports[dev])), injected=injected)
+                else:
+                    rb, nb, rows, gates = batched
+                    self._record_batches(op_name, shape_key, rb.read(), nb, rows, gates, injected)
         finally:
             self.stats.current_phase = saved
+
+    def _record_batches(self, op_name: str, shape_key: str, rep: N.FaultReport, nb: int, rows: int,
+                        gates: List[bool], injected: bool) -> None:
+        for bi in range(nb):
+            if gates[bi]:
+                self.stats.record_check(op_name=op_name, shape_key=shape_key,
+                                        result=result_from_report(rep.batch_view(bi, rows)), injected=injected)
 
     # -------------------------------------------------------- reference gates
     def _sample(self) -> bool:
@@ -282,8 +302,16 @@ class AbftInjector(AbstractContextManager):
         self._dump_done = True
 
     # ---------------------------------------------------------- fused linear
+    @staticmethod
+    def _needs_grad(*ts: Optional[torch.Tensor]) -> bool:
+        """The fused kernels have no backward: calls that autograd records
+        take the reference flow."""
+        return torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in ts)
+
     def _fused_linear_ok(self, x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor]) -> bool:
         if self.cfg.checker_backend != "b200" or not self.cfg.fused_linear:
+            return False
+        if self._needs_grad(x, weight, bias):
             return False
         if not (x.is_cuda and weight.is_cuda) or x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
             return False
@@ -338,13 +366,110 @@ class AbftInjector(AbstractContextManager):
         if check:
             if self.cfg.record_enable:
                 if self.defer_reports:
-                    self._pending.append((x2.device.index, "linear", self.stats.current_phase, (m, k, n), injected))
+                    self._pending.append((x2.device.index, "linear", self.stats.current_phase, (m, k, n), injected,
+                                          None))
                 else:
                     self.stats.record_check(op_name="linear", shape_key=f"A{(m, k)}_B{(k, n)}_C{(m, n)}",
                                             result=result_from_report(rep.read()), injected=injected)
             if self.cfg.dump_file:
                 self._maybe_dump_tensors("linear", f"A{(m, k)}_B{(k, n)}_C{(m, n)}", x2, b2, out, bias)
         return out.reshape(*x.shape[:-1], n)
+
+    # -------------------------------------------------- fused bmm / matmul
+    def _fused_mm_ok(self, a: torch.Tensor, b: torch.Tensor) -> bool:
+        """[..., M, K] x [..., K, N] operands the batched fused kernel takes."""
+        if self.cfg.checker_backend != "b200" or not self.cfg.fused_matmul:
+            return False
+        if not isinstance(a, torch.Tensor) or not isinstance(b, torch.Tensor) or a.dim() < 2 or b.dim() < 2:
+            return False
+        if not (a.is_cuda and b.is_cuda) or a.device != b.device:
+            return False
+        if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16 or self._needs_grad(a, b):
+            return False
+        k, n = b.shape[-2], b.shape[-1]
+        return a.shape[-1] == k and k % 8 == 0 and n % 8 == 0 and k > 0 and n > 0 and a.numel() > 0
+
+    def _run_batched(self, op_name: str, a3: torch.Tensor, b3: torch.Tensor, idx: Optional[int],
+                     gates: List[bool]) -> torch.Tensor:
+        """out[i] = a3[i] @ b3[i] through the fused kernel: the drawn fault
+        (flat index into out) goes into the accumulator, batches whose gate
+        passed are checked and recorded one check each. Gates that differ
+        across batches (sample_rate < 1) take one launch per batch, so that
+        only sampled batches are checked or corrected."""
+        bsz, m, _ = a3.shape
+        n = b3.shape[2]
+        injected = idx is not None
+        mag = float(self.cfg.inject_magnitude)
+        if bsz > 1 and any(gates) and not all(gates):
+            outs = []
+            for bi in range(bsz):
+                inj = None
+                if injected and idx // (m * n) == bi:
+                    inj = [(idx // n - bi * m, idx % n, mag)]
+                outs.append(self._launch_batched(op_name, a3[bi:bi + 1], b3[bi:bi + 1], inj, [gates[bi]], injected))
+            return torch.cat(outs)
+        inj = [(idx // n, idx % n, mag)] if injected else None
+        return self._launch_batched(op_name, a3, b3, inj, gates, injected)
+
+    def _launch_batched(self, op_name: str, a3: torch.Tensor, b3: torch.Tensor, inject, gates: List[bool],
+                        injected: bool) -> torch.Tensor:
+        bsz, m, k = a3.shape
+        n = b3.shape[2]
+        check = bool(gates[0])
+        mode = N.MODE_OFF
+        rep = None
+        if check:
+            mode = N.MODE_DETECT | (0 if self.cfg.detect_only else N.MODE_CORRECT)
+            rep = ops.ReportBuffer(self.cfg.report_capacity, a3.device, batch=bsz)
+        out, rep = ops.abft_bmm(a3, b3, mode=mode, thr_scale=self.cfg.thr_scale, thr_abs=self.cfg.thr_abs,
+                                inject=inject, report=rep)
+        if check:
+            key = f"A{(m, k)}_B{(k, n)}_C{(m, n)}"
+            if self.cfg.record_enable:
+                if self.defer_reports:
+                    self._pending.append((a3.device.index, op_name, self.stats.current_phase, key, injected,
+                                          (rep, bsz, m, list(gates))))
+                else:
+                    self._record_batches(op_name, key, rep.read(), bsz, m, gates, injected)
+            if self.cfg.dump_file:
+                for bi in range(bsz):
+                    self._maybe_dump_tensors(op_name, key, a3[bi], b3[bi], out[bi], None)
+        return out
+
+    def _fused_bmm(self, a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+        bsz, m, k = a.shape
+        n = b.shape[2]
+        # the reference's rng order: the injection draw over out, then one
+        # check gate (sample coin) per batch (injector.py:176-187)
+        idx = self._draw_fault(bsz * m * n)
+        gates = [self._check_gate_dims(m, k, n) for _ in range(bsz)]
+        return self._run_batched("bmm", a, b, idx, gates)
+
+    def _fused_matmul(self, a: torch.Tensor, b: torch.Tensor) -> Optional[torch.Tensor]:
+        """torch.matmul through the fused kernel, or None for the reference
+        flow (nothing drawn from the rng yet)."""
+        k, n = b.shape[-2], b.shape[-1]
+        if b.dim() == 2:
+            # checked by the reference as one 2-D product [M*, K] x [K, N]
+            a2 = a.reshape(-1, k)
+            m = a2.shape[0]
+            idx = self._draw_fault(m * n)
+            gate = self._check_gate_dims(m, k, n)
+            out = self._run_batched("matmul", a2.unsqueeze(0), b.unsqueeze(0), idx, [gate])
+            return out.reshape(*a.shape[:-1], n)
+        if not self.cfg.check_batched_matmul or a.dim() != b.dim() or a.shape[:-2] != b.shape[:-2]:
+            return None
+        # batched right operand: one sample coin for the call, as in the
+        # reference (whose check then stops at b_2d None); every batch checked
+        a3 = a.reshape(-1, a.shape[-2], k)
+        b3 = b.reshape(-1, k, n)
+        bsz, m = a3.shape[0], a3.shape[1]
+        if bsz > 65535:
+            return None
+        idx = self._draw_fault(bsz * m * n)
+        gate = self._check_gate_dims(m, k, n)
+        out = self._run_batched("matmul", a3, b3, idx, [gate] * bsz)
+        return out.reshape(*a.shape[:-1], n)
 
     # ------------------------------------------------------------- wrappers
     def _wrap_linear(self, fn: Callable[..., torch.Tensor]) -> Callable[..., torch.Tensor]:
@@ -363,6 +488,10 @@ class AbftInjector(AbstractContextManager):
 
     def _wrap_matmul(self, fn: Callable[..., torch.Tensor]) -> Callable[..., torch.Tensor]:
         def wrapped(input: torch.Tensor, other: torch.Tensor, *args: Any, **kwargs: Any) -> torch.Tensor:
+            if not args and not kwargs and self._fused_mm_ok(input, other):
+                out = self._fused_matmul(input, other)
+                if out is not None:
+                    return out
             out = fn(input, other, *args, **kwargs)
             out2, injected = self._maybe_inject_fault(out)
             a2 = flatten_to_2d_for_mm(input, right_operand=False)
@@ -375,6 +504,9 @@ class AbftInjector(AbstractContextManager):
 
     def _wrap_bmm(self, fn: Callable[..., torch.Tensor]) -> Callable[..., torch.Tensor]:
         def wrapped(input: torch.Tensor, mat2: torch.Tensor, *args: Any, **kwargs: Any) -> torch.Tensor:
+            if (not args and not kwargs and self._fused_mm_ok(input, mat2) and input.dim() == 3 and mat2.dim() == 3
+                    and input.shape[0] == mat2.shape[0] and 0 < input.shape[0] <= 65535):
+                return self._fused_bmm(input, mat2)
             out = fn(input, mat2, *args, **kwargs)
             out2, injected = self._maybe_inject_fault(out)
             # per-batch 2-D checks, as the reference (injector.py:180-186)

@@ -126,14 +126,22 @@ int pair_units_on(int dev, int sms) {
   return d.pair_clusters[CHECK] < sms / 2 ? d.pair_clusters[CHECK] : sms / 2;
 }
 
-int make_tmap_kmajor(CUtensorMap* m, const void* ptr, int64_t inner, int64_t outer, int64_t ld, int box_outer) {
+// A 3-D map over `batch` row-major [outer, ld] bf16 matrices, matrix b at
+// ptr + b * bstride elements (bstride ignored for batch <= 1), read in boxes
+// of 64 (inner) x box_outer rows x 1 matrix with 128-byte swizzle.
+int make_tmap_kmajor(CUtensorMap* m, const void* ptr, int64_t inner, int64_t outer, int64_t ld, int box_outer,
+                     int64_t batch = 1, int64_t bstride = 0) {
   EncodeTiledFn enc = get_encoder();
   if (enc == nullptr) return ABFT_ERR_DRIVER;
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
-  cuuint32_t box[2] = {64u, static_cast<cuuint32_t>(box_outer)};
-  cuuint32_t es[2] = {1u, 1u};
-  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, es,
+  if (batch <= 1) {
+    batch = 1;
+    bstride = ld * outer;
+  }
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer), static_cast<cuuint64_t>(batch)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 2, static_cast<cuuint64_t>(bstride) * 2};
+  cuuint32_t box[3] = {64u, static_cast<cuuint32_t>(box_outer), 1u};
+  cuuint32_t es[3] = {1u, 1u, 1u};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, es,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? ABFT_OK : ABFT_ERR_ALIGNMENT;
@@ -284,10 +292,10 @@ Schedule make_schedule(int64_t tiles, int num_kb, int units, int bn) {
   return s;
 }
 
-// Schedule of an M x N x K launch with tile_m x bn tiles (bd data columns)
-// over `units` units.
-Schedule schedule_for(int64_t M, int64_t N, int64_t K, int tile_m, int bn, int bd, int units) {
-  return make_schedule(cdiv(M, tile_m) * cdiv(N, bd), static_cast<int>(cdiv(K, kBK)), units, bn);
+// Schedule of `batch` M x N x K products with tile_m x bn tiles (bd data
+// columns) over `units` units.
+Schedule schedule_for(int64_t M, int64_t N, int64_t K, int tile_m, int bn, int bd, int units, int64_t batch = 1) {
+  return make_schedule(batch * cdiv(M, tile_m) * cdiv(N, bd), static_cast<int>(cdiv(K, kBK)), units, bn);
 }
 
 // A CTA pair runs a 128 x 256 share of a tile per SM about this much faster
@@ -296,17 +304,41 @@ constexpr double kPairSpeedup = 1.10;
 
 // Estimated time (microseconds) of an M x N x K launch with tile_m x bn
 // tiles (tile_m 256: CTA pairs over `units` pairs).
-double est_time(int64_t M, int64_t N, int64_t K, int bn, bool check, int tile_m, int units) {
+double est_time(int64_t M, int64_t N, int64_t K, int bn, bool check, int tile_m, int units, int64_t batch = 1) {
   const int bd = check ? bn - kChkRows : bn;
-  const double t = schedule_for(M, N, K, tile_m, bn, bd, units).est * kb_us(bn);
+  const double t = schedule_for(M, N, K, tile_m, bn, bd, units, batch).est * kb_us(bn);
   return tile_m == 256 ? t / kPairSpeedup : t;
 }
 
-int pick_tile_m(int64_t M, int64_t N, int64_t K, int sms, uint32_t mode, int bn) {
+int pick_tile_m(int64_t M, int64_t N, int64_t K, int sms, uint32_t mode, int bn, int64_t batch = 1) {
   if (bn != 256 || sms < 2 || M <= 0 || N <= 0 || K <= 0) return 128;
   const bool check = (mode & (ABFT_MODE_DETECT | ABFT_MODE_CORRECT)) != 0;
-  return est_time(M, N, K, bn, check, 256, sms / 2) < est_time(M, N, K, bn, check, 128, sms) ? 256 : 128;
+  return est_time(M, N, K, bn, check, 256, sms / 2, batch) < est_time(M, N, K, bn, check, 128, sms, batch) ? 256
+                                                                                                           : 128;
 }
+
+// abft_pick_tile_n for `batch` products.
+int pick_tile_n(int64_t M, int64_t N, int64_t K, int sms, uint32_t mode, int64_t batch) {
+  if (sms <= 0) sms = 148;
+  if (M <= 0 || N <= 0 || K <= 0) return 256;
+  const bool check = (mode & (ABFT_MODE_DETECT | ABFT_MODE_CORRECT)) != 0;
+  double best_cost = 0.0;
+  int best = 256;
+  for (int bn : {256, 128}) {
+    double cost = est_time(M, N, K, bn, check, 128, sms, batch);
+    if (bn == 256 && sms >= 2) {
+      const double tp = est_time(M, N, K, bn, check, 256, sms / 2, batch);
+      if (tp < cost) cost = tp;
+    }
+    if (bn == 256 || cost < best_cost) {
+      best_cost = cost;
+      best = bn;
+    }
+  }
+  return best;
+}
+
+inline int64_t batch_of(const abft_gemm_args* a) { return a->batch > 1 ? a->batch : 1; }
 
 // Swapped operands: with few output rows the weight goes on the MMA's
 // 128-row side and the rows of A form one narrow tile, C^T = B A^T.
@@ -329,6 +361,8 @@ abft_gemm_args swapped_args(const abft_gemm_args* a) {
   s.N = a->M;
   s.lda = a->ldb;
   s.ldb = a->lda;
+  s.stride_a = a->stride_b;
+  s.stride_b = a->stride_a;
   s.checksums = nullptr;
   s.tile_n = 128;
   s.tile_m = 128;
@@ -349,29 +383,31 @@ struct Plan {
 
 // dev < 0: no device to ask (co-resident pairs assumed sms / 2).
 int make_plan(const abft_gemm_args* a, int dev, int sms, Plan* pl) {
+  const int64_t nb = batch_of(a);
   pl->check = (a->mode & (ABFT_MODE_DETECT | ABFT_MODE_CORRECT)) != 0;
-  pl->bn = a->tile_n ? a->tile_n : abft_pick_tile_n(a->M, a->N, a->K, sms, a->mode);
-  pl->tile_m = a->tile_m ? a->tile_m : pick_tile_m(a->M, a->N, a->K, sms, a->mode, pl->bn);
+  pl->bn = a->tile_n ? a->tile_n : pick_tile_n(a->M, a->N, a->K, sms, a->mode, nb);
+  pl->tile_m = a->tile_m ? a->tile_m : pick_tile_m(a->M, a->N, a->K, sms, a->mode, pl->bn, nb);
   if (pl->tile_m != 128 && pl->tile_m != 256) return ABFT_ERR_UNSUPPORTED;
   if (pl->tile_m == 256 && (pl->bn != 256 || sms < 2)) return ABFT_ERR_UNSUPPORTED;
   pl->pair = pl->tile_m == 256;
   pl->bd = pl->check ? pl->bn - kChkRows : pl->bn;
   pl->num_kb = static_cast<int>(cdiv(a->K, kBK));
-  pl->tiles = cdiv(a->M, pl->tile_m) * cdiv(a->N, pl->bd);
+  pl->tiles = nb * cdiv(a->M, pl->tile_m) * cdiv(a->N, pl->bd);
+  if (pl->tiles >= (1ll << 31)) return ABFT_ERR_UNSUPPORTED;
   if (!pl->pair)
     pl->units = sms;
   else if (dev < 0)
     pl->units = sms / 2;
   else
     pl->units = pl->check ? pair_units_on<true>(dev, sms) : pair_units_on<false>(dev, sms);
-  pl->sch = schedule_for(a->M, a->N, a->K, pl->tile_m, pl->bn, pl->bd, pl->units);
+  pl->sch = schedule_for(a->M, a->N, a->K, pl->tile_m, pl->bn, pl->bd, pl->units, nb);
   pl->grid = pl->sch.grid * (pl->pair ? 2 : 1);
 
   size_t off = 0;
   pl->v_off = pl->pa_off = pl->u_off = pl->pb_off = pl->vf_off = pl->parts_off = pl->sk_part_off = pl->sk_flag_off = 0;
   if (pl->check && a->checksums == nullptr) {
     pl->v_off = off;
-    off = align256(off + abft_checksum_bytes(a->N, a->K, pl->bn));
+    off = align256(off + static_cast<size_t>(nb) * abft_checksum_bytes(a->N, a->K, pl->bn));
   }
   if (a->mode & ABFT_MODE_REF) {
     pl->pa_off = off;
@@ -397,9 +433,21 @@ int make_plan(const abft_gemm_args* a, int dev, int sms, Plan* pl) {
 
 int validate_gemm(const abft_gemm_args* a) {
   if (a == nullptr || a->A == nullptr || a->B == nullptr || a->C == nullptr) return ABFT_ERR_INVALID_ARG;
-  if (a->M < 0 || a->N < 0 || a->K < 0) return ABFT_ERR_INVALID_ARG;
+  if (a->M < 0 || a->N < 0 || a->K < 0 || a->batch < 0) return ABFT_ERR_INVALID_ARG;
   if (a->M > (1ll << 30) || a->N > (1ll << 30) || a->K > (1ll << 30)) return ABFT_ERR_UNSUPPORTED;
-  if (a->lda < a->K || a->ldb < a->K || a->ldc < a->N) return ABFT_ERR_INVALID_ARG;
+  if (a->b_kn != 0 && a->b_kn != 1) return ABFT_ERR_INVALID_ARG;
+  if (a->lda < a->K || a->ldb < (a->b_kn ? a->N : a->K) || a->ldc < a->N) return ABFT_ERR_INVALID_ARG;
+  if (a->b_kn && a->checksums != nullptr) return ABFT_ERR_INVALID_ARG;
+  if (a->batch > 1) {
+    // flattened rows (batch * M, batch * N) are 32-bit in the kernel
+    if (a->M * a->batch >= (1ll << 31) || a->N * a->batch >= (1ll << 31)) return ABFT_ERR_UNSUPPORTED;
+    if (a->stride_a < 0 || a->stride_b < 0 || a->stride_c < 0) return ABFT_ERR_INVALID_ARG;
+    if ((a->stride_a % 8) || (a->stride_b % 8) || (a->stride_c % 8)) return ABFT_ERR_ALIGNMENT;
+    // C's batches are whole groups of ldc rows, disjoint: row b * (stride_c / ldc) starts batch b
+    if (a->stride_c % a->ldc || a->stride_c / a->ldc < a->M) return ABFT_ERR_INVALID_ARG;
+    if ((a->stride_c / a->ldc) * a->batch >= (1ll << 31)) return ABFT_ERR_UNSUPPORTED;
+    if (a->mode & ABFT_MODE_REF) return ABFT_ERR_UNSUPPORTED;
+  }
   if ((a->K % 8) || (a->N % 8) || (a->lda % 8) || (a->ldb % 8) || (a->ldc % 8)) return ABFT_ERR_ALIGNMENT;
   if (!aligned16(a->A) || !aligned16(a->B) || !aligned16(a->C)) return ABFT_ERR_ALIGNMENT;
   if (a->bias != nullptr && !aligned16(a->bias)) return ABFT_ERR_ALIGNMENT;
@@ -410,12 +458,38 @@ int validate_gemm(const abft_gemm_args* a) {
   if (a->swap_ab < 0 || a->swap_ab > 2) return ABFT_ERR_INVALID_ARG;
   if (a->mode != ABFT_MODE_OFF && (a->report == nullptr || a->report_capacity < 0)) return ABFT_ERR_INVALID_ARG;
   if (a->report != nullptr && !aligned16(a->report)) return ABFT_ERR_ALIGNMENT;
+  if (a->batch > 65535) return ABFT_ERR_UNSUPPORTED;  // grid z of the encode passes
   if (a->n_inject < 0 || a->n_inject > ABFT_MAX_INJECT) return ABFT_ERR_INVALID_ARG;
   if (a->n_inject > 0 && (a->inject_rows == nullptr || a->inject_cols == nullptr || a->inject_deltas == nullptr))
     return ABFT_ERR_INVALID_ARG;
   if (a->checksums != nullptr && !aligned16(a->checksums)) return ABFT_ERR_ALIGNMENT;
   if (!(a->thr_scale >= 0.f) || !(a->thr_abs >= 0.f)) return ABFT_ERR_INVALID_ARG;
   return ABFT_OK;
+}
+
+// The frames of a call: `r` has B K-major (an N-major B replaced by its
+// copy at the start of the workspace, `copy`; any aligned placeholder while
+// only sizes are wanted), `k` is the frame the kernel runs in (r, or r with
+// swapped operands for few-row products).
+struct Frames {
+  abft_gemm_args r, k;
+  bool kn, swap;
+  size_t copy_bytes;
+};
+
+void make_frames(const abft_gemm_args* a, void* copy, Frames* f) {
+  f->kn = a->b_kn == 1;
+  f->r = *a;
+  f->copy_bytes = 0;
+  if (f->kn) {
+    f->copy_bytes = align256(static_cast<size_t>(batch_of(a)) * a->N * a->K * 2);
+    f->r.b_kn = 0;
+    f->r.B = copy;
+    f->r.ldb = a->K;
+    f->r.stride_b = a->N * a->K;
+  }
+  f->swap = use_swap(&f->r);
+  f->k = f->swap ? swapped_args(&f->r) : f->r;
 }
 
 template <int BN, bool CHECK, bool PAIR>
@@ -466,24 +540,12 @@ size_t abft_report_bytes(int32_t capacity) {
   return sizeof(abft_report) + static_cast<size_t>(capacity) * sizeof(abft_fault_record);
 }
 
+size_t abft_report_bytes_batched(int32_t capacity, int32_t batch) {
+  return abft_report_bytes(capacity) + (batch > 1 ? static_cast<size_t>(batch) * 4 * sizeof(uint32_t) : 0);
+}
+
 int32_t abft_pick_tile_n(int64_t M, int64_t N, int64_t K, int32_t num_sms, uint32_t mode) {
-  if (num_sms <= 0) num_sms = 148;
-  if (M <= 0 || N <= 0 || K <= 0) return 256;
-  const bool check = (mode & (ABFT_MODE_DETECT | ABFT_MODE_CORRECT)) != 0;
-  double best_cost = 0.0;
-  int32_t best = 256;
-  for (int32_t bn : {256, 128}) {
-    double cost = est_time(M, N, K, bn, check, 128, num_sms);
-    if (bn == 256 && num_sms >= 2) {
-      const double tp = est_time(M, N, K, bn, check, 256, num_sms / 2);
-      if (tp < cost) cost = tp;
-    }
-    if (bn == 256 || cost < best_cost) {
-      best_cost = cost;
-      best = bn;
-    }
-  }
-  return best;
+  return pick_tile_n(M, N, K, num_sms, mode, 1);
 }
 
 size_t abft_checksum_bytes(int64_t N, int64_t K, int32_t tile_n) {
@@ -491,11 +553,13 @@ size_t abft_checksum_bytes(int64_t N, int64_t K, int32_t tile_n) {
   return static_cast<size_t>(cdiv(N, tile_n - kChkRows)) * kChkRows * static_cast<size_t>(K) * 2;
 }
 
-int abft_encode_weight(const void* B, int64_t N, int64_t K, int64_t ldb, int32_t tile_n, void* out, void* stream) {
-  if (B == nullptr || out == nullptr || N <= 0 || K <= 0 || ldb < K) return ABFT_ERR_INVALID_ARG;
-  if ((K % 8) || (ldb % 8) || !aligned16(B) || !aligned16(out)) return ABFT_ERR_ALIGNMENT;
+int abft_encode_weight_batched(const void* B, int64_t N, int64_t K, int64_t ldb, int64_t stride_b, int32_t batch,
+                               int32_t tile_n, void* out, void* stream) {
+  if (B == nullptr || out == nullptr || N <= 0 || K <= 0 || ldb < K || batch < 1 || stride_b < 0)
+    return ABFT_ERR_INVALID_ARG;
+  if ((K % 8) || (ldb % 8) || (stride_b % 8) || !aligned16(B) || !aligned16(out)) return ABFT_ERR_ALIGNMENT;
   if (tile_n != 128 && tile_n != 256) return ABFT_ERR_UNSUPPORTED;
-  if (N > (1ll << 30) || K > (1ll << 30)) return ABFT_ERR_UNSUPPORTED;
+  if (N > (1ll << 30) || K > (1ll << 30) || batch > 65535) return ABFT_ERR_UNSUPPORTED;
   int dev;
   DeviceInfo info;
   int rc = current_device(&dev, &info);
@@ -503,10 +567,15 @@ int abft_encode_weight(const void* B, int64_t N, int64_t K, int64_t ldb, int32_t
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int bd = tile_n - kChkRows;
   const int num_kb = static_cast<int>(cdiv(K, kBK));
-  dim3 g(static_cast<unsigned>(num_kb), static_cast<unsigned>(cdiv(N, bd)));
+  dim3 g(static_cast<unsigned>(num_kb), static_cast<unsigned>(cdiv(N, bd)), static_cast<unsigned>(batch));
   encode_weight_kernel<<<g, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(B), ldb, static_cast<int>(N),
-                                         static_cast<int>(K), bd, static_cast<__nv_bfloat16*>(out));
+                                         static_cast<int>(K), bd, static_cast<__nv_bfloat16*>(out), stride_b,
+                                         static_cast<int64_t>(abft_checksum_bytes(N, K, tile_n) / 2));
   return launch_status();
+}
+
+int abft_encode_weight(const void* B, int64_t N, int64_t K, int64_t ldb, int32_t tile_n, void* out, void* stream) {
+  return abft_encode_weight_batched(B, N, K, ldb, 0, 1, tile_n, out, stream);
 }
 
 size_t abft_gemm_workspace_bytes(const abft_gemm_args* args) {
@@ -518,9 +587,10 @@ size_t abft_gemm_workspace_bytes(const abft_gemm_args* args) {
   if (have_dev) sms = info.sms;
   if (args->num_sms > 0 && args->num_sms < sms) sms = args->num_sms;
   Plan pl;
-  const abft_gemm_args sw = swapped_args(args);
-  if (make_plan(use_swap(args) ? &sw : args, have_dev ? dev : -1, sms, &pl) != ABFT_OK) return 0;
-  return pl.total;
+  Frames f;
+  make_frames(args, args->workspace, &f);
+  if (make_plan(&f.k, have_dev ? dev : -1, sms, &pl) != ABFT_OK) return 0;
+  return f.copy_bytes + pl.total;
 }
 
 int32_t abft_pick_tile_m(int64_t M, int64_t N, int64_t K, int32_t num_sms, uint32_t mode, int32_t tile_n) {
@@ -531,57 +601,64 @@ int32_t abft_pick_tile_m(int64_t M, int64_t N, int64_t K, int32_t num_sms, uint3
 int abft_gemm_bf16(const abft_gemm_args* args, void* stream) {
   int rc = validate_gemm(args);
   if (rc != ABFT_OK) return rc;
-  const bool swap = use_swap(args);
-  const abft_gemm_args sw = swapped_args(args);
-  const abft_gemm_args* a = swap ? &sw : args;
   int dev;
   DeviceInfo info;
   rc = current_device(&dev, &info);
   if (rc != ABFT_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (a->M == 0 || a->N == 0) {
-    // No kernel runs: reset the report here (the kernel resets it otherwise).
-    if (a->report != nullptr && cudaMemsetAsync(a->report, 0, sizeof(abft_report), s) != cudaSuccess)
+  const int64_t nb = batch_of(args);
+  if (args->M == 0 || args->N == 0) {
+    // No kernel runs: reset the report here (the kernel resets it otherwise;
+    // batch 0 in the header: no per-batch counters follow).
+    if (args->report != nullptr && cudaMemsetAsync(args->report, 0, sizeof(abft_report), s) != cudaSuccess)
       return launch_status(), ABFT_ERR_CUDA;
     return ABFT_OK;
   }
-  if (a->K == 0) return ABFT_ERR_UNSUPPORTED;
+  if (args->K == 0) return ABFT_ERR_UNSUPPORTED;
 
   int sms = info.sms;
-  if (a->num_sms > 0 && a->num_sms < sms) sms = a->num_sms;
+  if (args->num_sms > 0 && args->num_sms < sms) sms = args->num_sms;
+  Frames fr;
+  make_frames(args, args->workspace, &fr);
+  abft_gemm_args* a = &fr.k;
+  const bool swap = fr.swap;
   Plan ws;
   rc = make_plan(a, dev, sms, &ws);
   if (rc != ABFT_OK) return rc;
   const int bn = ws.bn;
   const bool check = ws.check;
-  if (ws.total > 0 && (a->workspace == nullptr || a->workspace_bytes < ws.total || !aligned16(a->workspace)))
+  const size_t need = fr.copy_bytes + ws.total;
+  if (need > 0 && (args->workspace == nullptr || args->workspace_bytes < need || !aligned16(args->workspace)))
     return ABFT_ERR_WORKSPACE;
-  uint8_t* wsb = static_cast<uint8_t*>(a->workspace);
+  // the K-major copy of an N-major B first, then the plan's regions
+  uint8_t* wsb = static_cast<uint8_t*>(args->workspace) + fr.copy_bytes;
+  const int bd = ws.bd;  // data columns per output tile
+
+  // Every tensor map is encoded before the first launch of the call, so a
+  // layout the encoder rejects returns an error with no device work queued.
+  // An N-major B is copied K-major by a pre-pass that, unless the operands
+  // are swapped (the copy is then the kernel's A and the checksums come
+  // from the rows of A), also forms the checksum block.
+  const bool enc_kn = fr.kn && check && !swap;
+  const bool enc_plain = check && a->checksums == nullptr && !enc_kn;
+  const void* V = check ? (a->checksums != nullptr ? a->checksums : wsb + ws.v_off) : nullptr;
 
   // B-operand boxes: the whole data width of a tile, or in a pair the even
   // CTA's 128 rows (tmB) and the odd CTA's remaining data rows (tmB2).
   CUtensorMap tmA, tmB, tmB2;
-  rc = make_tmap_kmajor(&tmA, a->A, a->K, a->M, a->lda, kBM);
+  rc = make_tmap_kmajor(&tmA, a->A, a->K, a->M, a->lda, kBM, nb, a->stride_a);
   if (rc != ABFT_OK) return rc;
-  const int bd = ws.bd;  // data columns per output tile
-  rc = make_tmap_kmajor(&tmB, a->B, a->K, a->N, a->ldb, ws.pair ? bn / 2 : bd);
+  rc = make_tmap_kmajor(&tmB, a->B, a->K, a->N, a->ldb, ws.pair ? bn / 2 : bd, nb, a->stride_b);
   if (rc != ABFT_OK) return rc;
   tmB2 = tmB;
   if (ws.pair && check) {
-    rc = make_tmap_kmajor(&tmB2, a->B, a->K, a->N, a->ldb, bd - bn / 2);
+    rc = make_tmap_kmajor(&tmB2, a->B, a->K, a->N, a->ldb, bd - bn / 2, nb, a->stride_b);
     if (rc != ABFT_OK) return rc;
   }
-
   CUtensorMap tmV = tmA;  // placeholder when checks are off
   if (check) {
-    const void* V = a->checksums;
-    if (V == nullptr) {
-      void* vws = wsb + ws.v_off;
-      rc = abft_encode_weight(a->B, a->N, a->K, a->ldb, bn, vws, stream);
-      if (rc != ABFT_OK) return rc;
-      V = vws;
-    }
-    rc = make_tmap_kmajor(&tmV, V, a->K, cdiv(a->N, bd) * kChkRows, a->K, kChkRows);
+    const int64_t vrows = cdiv(a->N, bd) * kChkRows;
+    rc = make_tmap_kmajor(&tmV, V, a->K, vrows, a->K, kChkRows, nb, vrows * a->K);
     if (rc != ABFT_OK) return rc;
   }
 
@@ -609,6 +686,11 @@ int abft_gemm_bf16(const abft_gemm_args* args, void* stream) {
   p.capacity = a->report_capacity;
   p.tile_sumc = (a->mode & ABFT_MODE_REF) ? reinterpret_cast<float*>(wsb + ws.parts_off) : nullptr;
   p.swap = swap ? 1 : 0;
+  p.batch = static_cast<int>(nb);
+  p.c_rows = nb > 1 ? static_cast<int>(a->stride_c / a->ldc) : 0;
+  p.bcounts = (nb > 1 && a->report != nullptr)
+                  ? reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(a->report) + abft_report_bytes(a->report_capacity))
+                  : nullptr;
 
   // Compact tail tile: when the last tile column holds ncols < bd data
   // columns, its B-operand tile is those rows (then, with checks, the 8
@@ -633,7 +715,7 @@ int abft_gemm_bf16(const abft_gemm_args* args, void* stream) {
         if (box < 0 || box % 8) return ABFT_ERR_UNSUPPORTED;  // checksum rows must start on a swizzle atom
         p.tail_box = box;
         if (box > 0) {
-          rc = make_tmap_kmajor(&tmBt, a->B, a->K, a->N, a->ldb, box);
+          rc = make_tmap_kmajor(&tmBt, a->B, a->K, a->N, a->ldb, box, nb, a->stride_b);
           if (rc != ABFT_OK) return rc;
         }
         p.tail_tx = (ws.pair ? 2 * a_bytes + (bn / 2) * row_bytes : a_bytes) +
@@ -658,6 +740,23 @@ int abft_gemm_bf16(const abft_gemm_args* args, void* stream) {
   if (sch.sk) {
     p.partials = reinterpret_cast<float*>(wsb + ws.sk_part_off);
     p.flags = reinterpret_cast<unsigned long long*>(wsb + ws.sk_flag_off);
+  }
+  if (fr.kn) {
+    const int cbd = enc_kn ? bd : 256;
+    dim3 g(static_cast<unsigned>(cdiv(args->K, kBK)), static_cast<unsigned>(cdiv(args->N, cbd)),
+           static_cast<unsigned>(nb));
+    transpose_encode_kernel<<<g, 256, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(args->B), args->ldb, nb > 1 ? args->stride_b : 0, static_cast<int>(args->N),
+        static_cast<int>(args->K), cbd, static_cast<__nv_bfloat16*>(args->workspace),
+        enc_kn ? static_cast<__nv_bfloat16*>(const_cast<void*>(V)) : nullptr,
+        enc_kn ? static_cast<int64_t>(abft_checksum_bytes(args->N, args->K, bn) / 2) : 0);
+    rc = launch_status();
+    if (rc != ABFT_OK) return rc;
+  }
+  if (enc_plain) {
+    rc = abft_encode_weight_batched(a->B, a->N, a->K, a->ldb, nb > 1 ? a->stride_b : 0, static_cast<int32_t>(nb), bn,
+                                    const_cast<void*>(V), stream);
+    if (rc != ABFT_OK) return rc;
   }
   if (ws.pair)
     rc = check ? launch_gemm<256, true, true>(dev, kPairSlot[1], tmA, tmB, tmB2, tmV, tmBt, p, grid, s)

@@ -3,6 +3,9 @@
 //   encode_weight_kernel   per-tile plain and column-index-weighted row
 //                          checksums of B[N, K] (the "Be" of checkers.py:119),
 //                          split into bf16 terms for the check MMA
+//   transpose_encode_kernel  K-major copy of an N-major right operand
+//                          B[K, N] (torch.bmm's mat2), with the same
+//                          checksum block computed on the way
 //   colsum_partial_kernel  column sums of a row-major [R, C] bf16 matrix over
 //                          blocks of rows (optionally row-weighted, with |x| max)
 //   reduce_partials_kernel sum (and max) of those partials in fixed order
@@ -55,10 +58,24 @@ __host__ __device__ __forceinline__ float col_sign(int j) { return (__builtin_po
 //   v1[k] = sum_j B[t*bd + j, k],  v2[k] = sum_j (j+1) B[t*bd + j, k],
 //   v3[k] = sum_j col_sign(j) B[t*bd + j, k]
 // (j over the tile's valid rows; fp32 sums in a fixed order).
-// grid (ceil(K/64), tiles_n), 256 threads. K % 8 == 0.
+// grid (ceil(K/64), tiles_n, batch), 256 threads. K % 8 == 0. Batch z reads
+// B + z * b_stride and writes out + z * out_stride.
+__device__ __forceinline__ void write_checksum_rows(float a1, float a2, float a3, __nv_bfloat16* o, int K) {
+  __nv_bfloat16 h[8];
+  split3_bf16(a1, h[0], h[1], h[2]);
+  split3_bf16(a2, h[3], h[4], h[5]);
+  h[6] = __float2bfloat16_rn(a3);
+  h[7] = __float2bfloat16_rn(a3 - __bfloat162float(h[6]));
+#pragma unroll
+  for (int q = 0; q < 8; ++q) o[static_cast<int64_t>(q) * K] = h[q];
+}
+
 __global__ void __launch_bounds__(256) encode_weight_kernel(const __nv_bfloat16* __restrict__ B, int64_t ldb, int N,
-                                                            int K, int bd, __nv_bfloat16* __restrict__ out) {
+                                                            int K, int bd, __nv_bfloat16* __restrict__ out,
+                                                            int64_t b_stride, int64_t out_stride) {
   __shared__ float red[3][32][65];
+  B += static_cast<int64_t>(blockIdx.z) * b_stride;
+  out += static_cast<int64_t>(blockIdx.z) * out_stride;
   const int kb = blockIdx.x, nt = blockIdx.y;
   const int t = threadIdx.x, c8 = t & 7, rg = t >> 3;
   const int k0 = kb * 64 + c8 * 8;
@@ -98,15 +115,87 @@ __global__ void __launch_bounds__(256) encode_weight_kernel(const __nv_bfloat16*
         a2 += red[1][g][t];
         a3 += red[2][g][t];
       }
-      __nv_bfloat16 h[8];
-      split3_bf16(a1, h[0], h[1], h[2]);
-      split3_bf16(a2, h[3], h[4], h[5]);
-      h[6] = __float2bfloat16_rn(a3);
-      h[7] = __float2bfloat16_rn(a3 - __bfloat162float(h[6]));
-      __nv_bfloat16* o = out + static_cast<int64_t>(nt) * 8 * K + col;
-#pragma unroll
-      for (int q = 0; q < 8; ++q) o[static_cast<int64_t>(q) * K] = h[q];
+      write_checksum_rows(a1, a2, a3, out + static_cast<int64_t>(nt) * 8 * K + col, K);
     }
+  }
+}
+
+// K-major copy of an N-major right operand plus (out != nullptr) its
+// checksum block: per batch z, Bkn[k * ldb + n] (K rows of N columns) is
+// written to Bt[n * K + k] (N rows of K, at z * N * K) and the checksum rows
+// of tile nt (columns [nt*bd, nt*bd + bd) of Bkn, the same sums as
+// encode_weight_kernel over the copy) to out + z * out_stride.
+// One block moves a 64 (k) x bd (n) slab through shared memory: coalesced
+// 16-byte reads along n, coalesced 128-byte row pieces along k on the way
+// out. The slab is stored as 16-byte chunks, chunk c of k row kk at
+// position c ^ tr_swz(kk), so that the column reads (8 k rows, one n) and
+// the checksum row reads (8 k rows, one chunk) each hit 8 distinct chunks.
+// grid (ceil(K/64), ceil(N/bd), batch), 256 threads; N % 8 == 0,
+// K % 8 == 0, ldb % 8 == 0, bd <= 256 and a multiple of 8.
+__device__ __forceinline__ int tr_swz(int kk) { return (kk ^ (kk >> 3)) & 7; }
+__device__ __forceinline__ int tr_off(int kk, int c) { return kk * 256 + ((c ^ tr_swz(kk)) << 3); }
+
+__global__ void __launch_bounds__(256) transpose_encode_kernel(const __nv_bfloat16* __restrict__ Bkn, int64_t ldb,
+                                                               int64_t b_stride, int N, int K, int bd,
+                                                               __nv_bfloat16* __restrict__ Bt,
+                                                               __nv_bfloat16* __restrict__ out, int64_t out_stride) {
+  __shared__ __align__(16) __nv_bfloat16 tile[64 * 256];
+  __shared__ float red[3][4][64];
+  const int z = blockIdx.z;
+  Bkn += static_cast<int64_t>(z) * b_stride;
+  Bt += static_cast<int64_t>(z) * N * K;
+  const int k0 = blockIdx.x * 64, n0 = blockIdx.y * bd;
+  const int nv = min(bd, N - n0);  // valid columns of the slab, a multiple of 8
+  const int nc8 = bd / 8;
+  const int t = threadIdx.x;
+  for (int i = t; i < 64 * nc8; i += 256) {
+    const int kk = i / nc8, c = i - kk * nc8;
+    uint4 w = make_uint4(0u, 0u, 0u, 0u);
+    if (k0 + kk < K && c * 8 < nv)
+      w = __ldg(reinterpret_cast<const uint4*>(Bkn + static_cast<int64_t>(k0 + kk) * ldb + n0 + c * 8));
+    *reinterpret_cast<uint4*>(tile + tr_off(kk, c)) = w;
+  }
+  __syncthreads();
+  // rows n of the copy: 8 consecutive k per thread, one 16-byte store
+  for (int i = t; i < nv * 8; i += 256) {
+    const int n = i >> 3, kc = (i & 7) * 8;
+    if (k0 + kc >= K) continue;
+    uint32_t wd[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const uint32_t lo = __bfloat16_as_ushort(tile[tr_off(kc + 2 * e, n >> 3) + (n & 7)]);
+      const uint32_t hi = __bfloat16_as_ushort(tile[tr_off(kc + 2 * e + 1, n >> 3) + (n & 7)]);
+      wd[e] = lo | (hi << 16);
+    }
+    *reinterpret_cast<uint4*>(Bt + static_cast<int64_t>(n0 + n) * K + k0 + kc) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+  }
+  if (out == nullptr) return;
+  // checksums: thread (k row kk, group g) sums the chunks c = g, g+4, ...
+  // (columns j ascending within each), then the 4 groups are added in order
+  const int kk = t & 63, g = t >> 6;
+  float s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  for (int c = g; c * 8 < nv; c += 4) {
+    float x[8];
+    unpack8(*reinterpret_cast<const uint4*>(tile + tr_off(kk, c)), x);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int j = c * 8 + e;
+      s1 += x[e];
+      s2 = fmaf(static_cast<float>(j + 1), x[e], s2);
+      s3 = fmaf(col_sign(j), x[e], s3);
+    }
+  }
+  red[0][g][kk] = s1;
+  red[1][g][kk] = s2;
+  red[2][g][kk] = s3;
+  __syncthreads();
+  if (t < 64 && k0 + t < K) {
+    const float a1 = (red[0][0][t] + red[0][1][t]) + (red[0][2][t] + red[0][3][t]);
+    const float a2 = (red[1][0][t] + red[1][1][t]) + (red[1][2][t] + red[1][3][t]);
+    const float a3 = (red[2][0][t] + red[2][1][t]) + (red[2][2][t] + red[2][3][t]);
+    write_checksum_rows(a1, a2, a3,
+                        out + static_cast<int64_t>(z) * out_stride + static_cast<int64_t>(blockIdx.y) * 8 * K + k0 + t,
+                        K);
   }
 }
 

@@ -2,6 +2,10 @@
 //
 //   C[M, N] = A[M, K] * B[N, K]^T (+ bias)      (B = nn.Linear weight layout)
 //
+// or a batch of such products C[b] = A[b] B[b]^T in one launch (torch.bmm):
+// every tensor map has the batch as its outermost coordinate and the tiles
+// of all batches form one schedule.
+//
 // One persistent CTA per SM walks output tiles. Warp roles:
 //   warp 0      TMA producer: per 64-wide k-block the A tile (128 rows) and
 //               the B-operand tile (BN rows) into a STAGES-deep shared-memory
@@ -128,6 +132,16 @@ struct GemmParams {
   // stored transposed (C[col * ldc + row]), the bias is indexed by the
   // kernel row, and fault records carry C's coordinates.
   int swap;
+  // Batched launch: `batch` products, C[b] at row b * c_rows of C (a batch
+  // stride that is a whole number of ldc rows keeps the address arithmetic
+  // in one 32-bit row index). Tile order:
+  // the full tiles of batch 0, 1, ..., then the tail-column tiles batch by
+  // batch. Fault records and injected faults use rows flattened over the
+  // batch (C's row b * rows + i); bcounts ([batch][4] after the report's
+  // records, or null) counts each batch's faults, located and corrected.
+  int batch;
+  int c_rows;
+  uint32_t* bcounts;
 };
 
 // Walks the (tile, k-block range) segments one CTA owns. Data-parallel:
@@ -220,12 +234,17 @@ __device__ __forceinline__ bool report_ready(const GemmParams& p, volatile int* 
   return true;
 }
 
-__device__ __forceinline__ void tile_coords(int tile, const GemmParams& p, int& mt, int& nt) {
-  if (tile >= p.full_tiles) {
-    mt = tile - p.full_tiles;
+__device__ __forceinline__ void tile_coords(int tile, const GemmParams& p, int& b, int& mt, int& nt) {
+  const int all_full = p.batch * p.full_tiles;
+  if (tile >= all_full) {
+    const int t = tile - all_full;
+    b = t / p.tiles_m;
+    mt = t - b * p.tiles_m;
     nt = p.tiles_n - 1;
     return;
   }
+  b = tile / p.full_tiles;
+  tile -= b * p.full_tiles;
   const int group = p.group_m * p.tiles_n_full;
   const int g = tile / group;
   const int first_m = g * p.group_m;
@@ -369,6 +388,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     *abort_flag = 0;
     fence_barrier_init();
   }
+  if (blockIdx.x == 0 && p.bcounts != nullptr) {
+    // Per-batch counters, zeroed before CTA 0 publishes the report header
+    // (other CTAs touch them only after report_ready).
+    for (int i = threadIdx.x; i < 4 * p.batch; i += kThreads) p.bcounts[i] = 0u;
+    __threadfence();
+  }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -406,7 +431,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     r->abs_err = 0.f;
     r->rel_err = 0.f;
     r->ref_ok = -1;
-    r->reserved = 0;
+    r->batch = p.bcounts != nullptr ? static_cast<uint32_t>(p.batch) : 0u;
     __threadfence();
     st_release_u64(reinterpret_cast<unsigned long long*>(&r->launch_tag), p.nonce);
   }
@@ -424,8 +449,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       SegmentIter seg(p, unit, nunits);
       int tile, kb0, kb1;
       while (ok && seg.next(p, tile, kb0, kb1)) {
-        int mt, nt;
-        tile_coords(tile, p, mt, nt);
+        int bz, mt, nt;
+        tile_coords(tile, p, bz, mt, nt);
         const int arow = mt * Cfg::kTileM + static_cast<int>(rank) * kBM;
         // Compact tail tile: this CTA's data rows come from the tail box (and
         // the checksum rows follow them); in a pair the odd CTA's rows start
@@ -439,31 +464,32 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint8_t* sa = smem + Cfg::kOffA + stage * Cfg::kABytes;
           uint8_t* sb = smem + Cfg::kOffB + stage * Cfg::kBBytes;
+          const int kx = kb * kBK;
           if constexpr (PAIR) {
             const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
             if (rank == 0) mbar_arrive_expect_tx(&full[stage], tx);
-            tma_load_2d_pair(sa, &tmA, fb, kb * kBK, arow);
+            tma_load_3d_pair(sa, &tmA, fb, kx, arow, bz);
             if (!CHECK) {
               const int half = tail ? p.tail_n / 2 : Cfg::kBRows;
-              tma_load_2d_pair(sb, &tmB, fb, kb * kBK, nt * BN + static_cast<int>(rank) * half);
+              tma_load_3d_pair(sb, &tmB, fb, kx, nt * BN + static_cast<int>(rank) * half, bz);
             } else if (rank == 0) {
-              tma_load_2d_pair(sb, &tmB, fb, kb * kBK, nt * BD);
+              tma_load_3d_pair(sb, &tmB, fb, kx, nt * BD, bz);
             } else if (!tail) {
-              tma_load_2d_pair(sb, &tmB2, fb, kb * kBK, nt * BD + Cfg::kBRows);
-              tma_load_2d_pair(sb + Cfg::kChkRow0 * 128, &tmV, fb, kb * kBK, nt * kChkRows);
+              tma_load_3d_pair(sb, &tmB2, fb, kx, nt * BD + Cfg::kBRows, bz);
+              tma_load_3d_pair(sb + Cfg::kChkRow0 * 128, &tmV, fb, kx, nt * kChkRows, bz);
             } else {
-              if (p.tail_box > 0) tma_load_2d_pair(sb, &tmBt, fb, kb * kBK, nt * BD + p.tail_n / 2);
-              tma_load_2d_pair(sb + p.tail_box * 128, &tmV, fb, kb * kBK, nt * kChkRows);
+              if (p.tail_box > 0) tma_load_3d_pair(sb, &tmBt, fb, kx, nt * BD + p.tail_n / 2, bz);
+              tma_load_3d_pair(sb + p.tail_box * 128, &tmV, fb, kx, nt * kChkRows, bz);
             }
           } else {
             mbar_arrive_expect_tx(&full[stage], tx);
-            tma_load_2d(sa, &tmA, &full[stage], kb * kBK, arow);
+            tma_load_3d(sa, &tmA, &full[stage], kx, arow, bz);
             if (!(CHECK && tail)) {
-              tma_load_2d(sb, &tmB, &full[stage], kb * kBK, nt * BD);
-              if (CHECK) tma_load_2d(sb + BD * 128, &tmV, &full[stage], kb * kBK, nt * kChkRows);
+              tma_load_3d(sb, &tmB, &full[stage], kx, nt * BD, bz);
+              if (CHECK) tma_load_3d(sb + BD * 128, &tmV, &full[stage], kx, nt * kChkRows, bz);
             } else {
-              if (p.tail_box > 0) tma_load_2d(sb, &tmBt, &full[stage], kb * kBK, nt * BD);
-              tma_load_2d(sb + p.tail_box * 128, &tmV, &full[stage], kb * kBK, nt * kChkRows);
+              if (p.tail_box > 0) tma_load_3d(sb, &tmBt, &full[stage], kx, nt * BD, bz);
+              tma_load_3d(sb + p.tail_box * 128, &tmV, &full[stage], kx, nt * kChkRows, bz);
             }
           }
           issued_mask |= 1u << stage;
@@ -500,8 +526,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       SegmentIter seg(p, unit, nunits);
       int tile, kb0, kb1;
       while (ok && seg.next(p, tile, kb0, kb1)) {
-        int mt, nt;
-        tile_coords(tile, p, mt, nt);
+        int bz, mt, nt;
+        tile_coords(tile, p, bz, mt, nt);
+        (void)bz;
+        (void)mt;
         const bool tail = p.tail_n != 0 && nt == p.tiles_n - 1;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag)) break;
         tc_fence_after();
@@ -562,8 +590,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     SegmentIter seg(p, unit, nunits);
     int tile, kb0, kb1;
     while (seg.next(p, tile, kb0, kb1)) {
-      int mt, nt;
-      tile_coords(tile, p, mt, nt);
+      int bz, mt, nt;
+      tile_coords(tile, p, bz, mt, nt);
       // Warp-uniform outcome: the tcgen05.ld below are warp-collective.
       if (!__all_sync(0xFFFFFFFFu, mbar_wait(&tfull[acc], acc_phase, abort_flag))) break;
       tc_fence_after();
@@ -687,9 +715,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         inj_d[i] = 0.f;
       }
       if (p.n_inj > 0 && row_ok) {
+        // Batch offsets of the flattened fault coordinates: C's rows are the
+        // kernel's rows, or its columns with swapped operands.
+        const int inj_row = p.swap ? grow : bz * p.M + grow;
+        const int inj_coff = p.swap ? bz * p.N : 0;
         for (int i = 0; i < p.n_inj; ++i) {
-          const int ic = p.inj_cols[i] - col0 - hcol0;
-          if (p.inj_rows[i] == grow && ic >= 0 && ic < NV && hcol0 + ic < ncols && n_my < kMaxInj) {
+          const int ic = p.inj_cols[i] - inj_coff - col0 - hcol0;
+          if (p.inj_rows[i] == inj_row && ic >= 0 && ic < NV && hcol0 + ic < ncols && n_my < kMaxInj) {
 #pragma unroll
             for (int j = 0; j < kMaxInj; ++j)
               if (j == n_my) {
@@ -812,10 +844,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (slot < static_cast<uint32_t>(p.capacity)) {
                 abft_fault_record* rec = reinterpret_cast<abft_fault_record*>(rep + 1) + slot;
                 if (!p.swap) {
-                  rec->row = grow;
+                  rec->row = bz * p.M + grow;
                   rec->col = col >= 0 ? col0 + col : -1;
                 } else {
-                  rec->row = col >= 0 ? col0 + col : -1;
+                  rec->row = col >= 0 ? bz * p.N + col0 + col : -1;
                   rec->col = grow;
                 }
                 rec->residual = res1;
@@ -827,6 +859,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 st |= ABFT_STATUS_OVERFLOW;
               }
               atomicOr(&rep->status, st);
+              if (p.bcounts != nullptr) {
+                uint32_t* bc = p.bcounts + 4 * bz;
+                atomicAdd(bc, 1u);
+                if (flags & ABFT_REC_LOCATED) atomicAdd(bc + 1, 1u);
+                if (flags & ABFT_REC_CORRECTED) atomicAdd(bc + 2, 1u);
+              }
             }
           }
         }
@@ -839,6 +877,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint4* bp = reinterpret_cast<const uint4*>(p.bias + col0 + hcol0);
       const int rd_grow = row0 + q * 32 + rd_row;  // global row of this lane's first read-side row
       const float row_bias = (p.swap && p.bias != nullptr && row_ok) ? __bfloat162float(p.bias[grow]) : 0.f;
+      const int crow0 = bz * p.c_rows;  // this batch's first row of C
 #pragma unroll 1
       for (int c = 0; c < NCH; ++c) {
         if (p.swap && hcol0 + c * 32 >= ncols) break;  // warp-uniform
@@ -865,7 +904,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // Lane l holds kernel row row0 + q*32 + l = C column: for each of
           // this chunk's C rows a warp writes 32 consecutive columns.
           if (row_ok) {
-            __nv_bfloat16* cc = p.C + static_cast<int64_t>(col0 + base) * p.ldc + grow;
+            __nv_bfloat16* cc = p.C + static_cast<int64_t>(crow0 + col0 + base) * p.ldc + grow;
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
               if (base + e < ncols) {
@@ -905,7 +944,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // lanes per row, each lane one 16-byte piece (8 columns).
         const int lcol = base + rd_piece * 8;  // local column of this lane's piece
         const bool col_ok = lcol < ncols;
-        __nv_bfloat16* cbase = p.C + static_cast<int64_t>(rd_grow) * p.ldc + col0 + lcol;
+        __nv_bfloat16* cbase = p.C + static_cast<int64_t>(crow0 + rd_grow) * p.ldc + col0 + lcol;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int y = i * 8 + rd_row;

@@ -79,12 +79,14 @@ __device__ __forceinline__ void tma_prefetch_desc(const void* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// 2-D tiled load, no multicast. x = innermost coordinate (elements).
-__device__ __forceinline__ void tma_load_2d(void* dst, const void* map, uint64_t* bar, int32_t x, int32_t y) {
+// 3-D tiled load, no multicast. x = innermost coordinate (elements), y =
+// row, z = batch (0 for a single matrix).
+__device__ __forceinline__ void tma_load_3d(void* dst, const void* map, uint64_t* bar, int32_t x, int32_t y,
+                                            int32_t z) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
-          smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
 
@@ -120,15 +122,15 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-// 2-D tiled load into this CTA's shared memory whose completion is counted
+// 3-D tiled load into this CTA's shared memory whose completion is counted
 // on an mbarrier of either CTA of the pair (`bar_caddr`, shared::cluster
 // address). No multicast: every CTA loads its own operand halves.
-__device__ __forceinline__ void tma_load_2d_pair(void* dst, const void* map, uint32_t bar_caddr, int32_t x,
-                                                 int32_t y) {
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const void* map, uint32_t bar_caddr, int32_t x,
+                                                 int32_t y, int32_t z) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
-      "%4}], [%2];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_caddr), "r"(x), "r"(y)
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+      "%4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_caddr), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
 

@@ -7,6 +7,8 @@ bf16 tensors on an sm_100 device; anything else raises (no CPU fallback).
 Functions
   encode_weight(weight, tile_n)          per-tile checksums of a [N, K] weight
   abft_gemm(a, weight, bias, ...)        fused checksum-protected GEMM
+  abft_bmm(a, b, ...)                    the same for a batch of products
+                                         (torch.bmm), one launch
   check_only(a, b, c, bias, ...)         post-hoc check of an existing output
 """
 from __future__ import annotations
@@ -47,12 +49,14 @@ def _require_bf16_cuda(name: str, t: torch.Tensor, dim: int) -> None:
 
 
 class ReportBuffer:
-    """Device buffer holding one ``abft_report`` with ``capacity`` records."""
+    """Device buffer holding one ``abft_report`` with ``capacity`` records
+    (and, for a batched call, the per-batch counters of ``batch`` products)."""
 
     def __init__(self, capacity: int = DEFAULT_CAPACITY, device: Optional[torch.device] = None,
-                 tensor: Optional[torch.Tensor] = None):
+                 tensor: Optional[torch.Tensor] = None, batch: int = 1):
         self.capacity = int(capacity)
-        nbytes = int(N.lib().abft_report_bytes(self.capacity))
+        self.batch = max(int(batch), 1)
+        nbytes = int(N.lib().abft_report_bytes_batched(self.capacity, self.batch))
         if tensor is None:
             tensor = torch.zeros(nbytes, dtype=torch.uint8, device=device or torch.device("cuda"))
         elif tensor.dtype != torch.uint8 or tensor.numel() < nbytes or tensor.data_ptr() % 16:
@@ -240,6 +244,141 @@ def abft_gemm(
         rc = L.abft_gemm_bf16(ctypes.byref(args), _stream(dev))
     N.check("abft_gemm_bf16", rc)
     return out, report
+
+
+def _mat_layout(t: torch.Tensor) -> Optional[Tuple[int, int]]:
+    """(leading dimension, batch stride) in elements under which the library
+    can read the [batch, rows, cols] tensor ``t`` in place (unit stride in
+    cols, both strides multiples of 8, 16-byte aligned), else None. Strides
+    of size-1 dimensions are not used and get a valid stand-in."""
+    bsz, rows, cols = t.shape
+    if t.stride(2) != 1 and cols > 1:
+        return None
+    ld = t.stride(1) if rows > 1 else (cols + 7) // 8 * 8
+    bs = t.stride(0) if bsz > 1 else rows * ld
+    if ld < cols or ld % 8 or bs % 8 or bs < 0 or t.data_ptr() % 16:
+        return None
+    return ld, bs
+
+
+def abft_bmm(
+    a: torch.Tensor,
+    b: torch.Tensor,
+    bias: Optional[torch.Tensor] = None,
+    *,
+    b_layout: str = "kn",
+    mode: int = N.MODE_DETECT | N.MODE_CORRECT,
+    tile_n: int = 0,
+    tile_m: int = 0,
+    swap_ab: int = 0,
+    thr_scale: float = DEFAULT_THR_SCALE,
+    thr_abs: float = 0.0,
+    inject: Optional[Sequence[Tuple[int, int, float]]] = None,
+    report: Optional[ReportBuffer] = None,
+    out: Optional[torch.Tensor] = None,
+    num_sms: int = 0,
+) -> Tuple[torch.Tensor, Optional[ReportBuffer]]:
+    """Batched ``out[i] = a[i] @ b[i] (+ bias)`` with the fused checksum
+    epilogue: every product of the batch in one launch.
+
+    ``a`` is [B, M, K]. ``b_layout="kn"``: ``b`` is [B, K, N], torch.bmm's
+    ``mat2``; a ``b`` whose K dimension has unit stride (the transpose of a
+    [B, N, K] tensor, e.g. ``k.transpose(1, 2)``) is read in place, a
+    row-major one is copied K-major by the call (with its checksums formed
+    on the way). ``b_layout="nk"``: ``b`` is [B, N, K] (weight layout).
+    ``inject`` rows and the report's record rows are flattened over the
+    batch (row ``i`` of batch ``j`` is ``j * M + i``); ``report.read()
+    .batch_view(j, M)`` gives batch ``j`` alone. Returns ``out`` [B, M, N]
+    and the report (None when mode == MODE_OFF).
+    """
+    if a.dim() != 3 or b.dim() != 3:
+        raise ValueError(f"abft_bmm takes 3-D operands, got {tuple(a.shape)} and {tuple(b.shape)}")
+    for name, t in (("a", a), ("b", b)):
+        if not t.is_cuda or t.dtype != torch.bfloat16:
+            raise ValueError(f"{name} must be a CUDA bfloat16 tensor (the library has no CPU path)")
+    bsz, m, k = a.shape
+    n_dim = 2 if b_layout == "kn" else 1
+    if k % 8 or b.shape[n_dim] % 8:
+        raise ValueError(f"K and N must be multiples of 8 (K={k}, N={b.shape[n_dim]})")
+    if b_layout == "kn":
+        if b.shape[0] != bsz or b.shape[1] != k:
+            raise ValueError(f"b {tuple(b.shape)} does not match a {tuple(a.shape)} as [B, K, N]")
+        n = b.shape[2]
+        bt = b.transpose(1, 2)  # [B, N, K]
+        if _mat_layout(bt) is not None:
+            bmat, b_kn = bt, 0
+        else:
+            bmat, b_kn = (b if _mat_layout(b) is not None else b.contiguous()), 1
+    elif b_layout == "nk":
+        if b.shape[0] != bsz or b.shape[2] != k:
+            raise ValueError(f"b {tuple(b.shape)} does not match a {tuple(a.shape)} as [B, N, K]")
+        n = b.shape[1]
+        bmat, b_kn = (b if _mat_layout(b) is not None else b.contiguous()), 0
+    else:
+        raise ValueError("b_layout must be 'kn' or 'nk'")
+    if b.device != a.device:
+        raise ValueError("a and b must be on the same device")
+    if _mat_layout(a) is None:
+        a = a.contiguous()
+    if bias is not None:
+        _require_bf16_cuda("bias", bias, 1)
+        if bias.shape[0] != n:
+            raise ValueError(f"bias has {bias.shape[0]} entries, expected {n}")
+    dev = a.device
+    if out is None:
+        out = torch.empty((bsz, m, n), dtype=torch.bfloat16, device=dev)
+    elif (out.dtype != torch.bfloat16 or tuple(out.shape) != (bsz, m, n) or not out.is_contiguous()):
+        raise ValueError(f"out must be a contiguous bf16 [{bsz}, {m}, {n}] tensor")
+    if mode != N.MODE_OFF:
+        if report is None:
+            report = ReportBuffer(DEFAULT_CAPACITY, dev, batch=bsz)
+        elif report.batch < bsz:
+            raise ValueError(f"the report holds counters for {report.batch} batches, the call has {bsz}")
+
+    try:
+        return _bmm_call(a, bmat, b_kn, bias, out, bsz, m, n, k, mode, tile_n, tile_m, swap_ab, thr_scale, thr_abs,
+                         inject, report, num_sms)
+    except N.AbftError as e:
+        # Strides the tensor-map encoder rejects (e.g. heads interleaved
+        # along rows): the call queued no device work; run on packed copies.
+        if e.code != -2 or (a.is_contiguous() and bmat.is_contiguous()):
+            raise
+        return _bmm_call(a.contiguous(), bmat.contiguous(), b_kn, bias, out, bsz, m, n, k, mode, tile_n, tile_m,
+                         swap_ab, thr_scale, thr_abs, inject, report, num_sms)
+
+
+def _bmm_call(a, bmat, b_kn, bias, out, bsz, m, n, k, mode, tile_n, tile_m, swap_ab, thr_scale, thr_abs, inject,
+              report, num_sms):
+    dev = a.device
+    inj = _Inject(inject, dev) if inject else None
+    lda, sa = _mat_layout(a)
+    ldb, sb = _mat_layout(bmat)
+    args = N.GemmArgs()
+    args.A, args.B, args.C, args.bias = _ptr(a), _ptr(bmat), _ptr(out), _ptr(bias)
+    args.M, args.N, args.K = m, n, k
+    args.lda, args.ldb, args.ldc = lda, ldb, max(n, 1)
+    args.batch, args.b_kn = bsz, b_kn
+    args.stride_a, args.stride_b, args.stride_c = sa, sb, m * max(n, 1)
+    args.mode = int(mode)
+    args.tile_n, args.tile_m, args.swap_ab = int(tile_n), int(tile_m), int(swap_ab)
+    args.thr_scale, args.thr_abs = float(thr_scale), float(thr_abs)
+    args.tol_abs, args.tol_rel = 1e-2, 1e-2
+    args.report = report.data_ptr() if report is not None and mode != N.MODE_OFF else None
+    args.report_capacity = report.capacity if report is not None and mode != N.MODE_OFF else 0
+    args.num_sms = int(num_sms)
+    if inj is not None:
+        args.inject_rows, args.inject_cols, args.inject_deltas = _ptr(inj.rows), _ptr(inj.cols), _ptr(inj.deltas)
+        args.n_inject = inj.n
+    L = N.lib()
+    with torch.cuda.device(dev):
+        ws_bytes = int(L.abft_gemm_workspace_bytes(ctypes.byref(args)))
+        if ws_bytes:
+            ws = _workspace(dev, ws_bytes)
+            args.workspace = ws.data_ptr()
+            args.workspace_bytes = ws.numel()
+        rc = L.abft_gemm_bf16(ctypes.byref(args), _stream(dev))
+    N.check("abft_gemm_bf16", rc)
+    return out, (report if mode != N.MODE_OFF else None)
 
 
 def check_only(
