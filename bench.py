@@ -54,6 +54,11 @@ def parse_args():
     ap.add_argument("--sweep", action="store_true",
                     help="one JSON line per shape of the square sweep, the 512x4096x4096 case and the "
                          "Qwen2-7B layer GEMMs: checked / unchecked TFLOP/s and 1- and 4-fault outcomes")
+    ap.add_argument("--bmm-sweep", action="store_true",
+                    help="batched products (torch.bmm, attention-shaped): cuBLAS vs the fused kernel vs the "
+                         "reference's per-batch check loop")
+    ap.add_argument("--profile-bmm", default=None, metavar="SHAPE",
+                    help="two rounds (checks off, then on) of one --bmm-sweep shape: an ncu capture target")
     ap.add_argument("--model", choices=["qwen2-7b", "cogact"], default=None,
                     help="qwen2-7b: prefill-512 tokens/s and decode of a random-init Qwen2-7B-shaped decoder; "
                          "cogact: one CogACT-style VLA forward (ViT-L + SigLIP + Llama-2-7B + DiT-B, 10 "
@@ -536,6 +541,140 @@ def sweep(args):
                           "overhead_pct": 100.0 * (t_chk / t_off - 1.0), "unchecked_ms": t_off, "checked_ms": t_chk,
                           **outcomes}), flush=True)
         del a, w, out, ref, cks
+
+
+BMM_SHAPES = [
+    # (name, batch, M, N, K, mat2 layout): "view" = the transpose of a K-major
+    # [B, N, K] tensor (q @ k^T), "rowmajor" = a row-major [B, K, N] (p @ v)
+    ("qwen7b_prefill512_scores", 28, 512, 512, 128, "view"),
+    ("qwen7b_prefill512_pv", 28, 512, 128, 512, "rowmajor"),
+    ("s4096_scores_h32", 32, 4096, 4096, 128, "view"),
+    ("s4096_pv_h32", 32, 4096, 128, 4096, "rowmajor"),
+    ("decode_scores_kv4096", 28, 1, 4096, 128, "view"),
+    ("decode_pv_kv4096", 28, 1, 128, 4096, "rowmajor"),
+    ("batched_2048_b8", 8, 2048, 2048, 2048, "rowmajor"),
+]
+
+
+def profile_bmm(args):
+    """Two rounds of one batched shape, checks off then on: the ncu target."""
+    import torch
+
+    from vla_abft_estimate_b200 import _native as N
+    from vla_abft_estimate_b200 import ops
+
+    shape = {s[0]: s for s in BMM_SHAPES}[args.profile_bmm]
+    _, bsz, m, n, k, lay = shape
+    dev = torch.device("cuda", 0)
+    a = (torch.randn(bsz, m, k, device=dev) * k ** -0.5).bfloat16()
+    w = (torch.randn(bsz, n, k, device=dev) * k ** -0.5).bfloat16()
+    b = w.transpose(1, 2) if lay == "view" else w.transpose(1, 2).contiguous()
+    out = torch.empty(bsz, m, n, device=dev, dtype=torch.bfloat16)
+    rep = ops.ReportBuffer(64, dev, batch=bsz)
+    for _ in range(2):
+        ops.abft_bmm(a, b, mode=N.MODE_OFF, out=out)
+        ops.abft_bmm(a, b, mode=N.MODE_DETECT | N.MODE_CORRECT, out=out, report=rep)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_bmm": args.profile_bmm, "faults": rep.read().n_faults}))
+
+
+def reference_bmm_flow(a, b):
+    """What the reference's bmm hook runs on the GPU: torch.bmm, then per
+    batch the python-backend corner check (pytorch/abft/checkers.py:112-126)
+    ending in a host read (:103), inside the loop of injector.py:180-186."""
+    import torch
+
+    out = torch.bmm(a, b)
+    ok = True
+    for bi in range(a.shape[0]):
+        s_a = a[bi].sum(dim=0)
+        s_b = b[bi].sum(dim=1)
+        corner = torch.dot(s_a, s_b)
+        sum_c = out[bi].sum()
+        diff = torch.abs(corner - sum_c)
+        rel = diff / torch.clamp(torch.abs(sum_c), min=1.0)
+        ok &= bool((diff <= 1e-2) or (rel <= 1e-2))
+    return out, ok
+
+
+def bmm_sweep(args):
+    """Batched products: device times (L2 flushed) of cuBLAS bmm, the fused
+    kernel with checks off and on; wall times of the reference's hook flow
+    (bmm + per-batch checks with a host read each) and of AbftInjector's
+    fused bmm (deferred reports), both per call."""
+    import torch
+
+    from vla_abft_estimate_b200 import _native as N
+    from vla_abft_estimate_b200 import ops
+    from vla_abft_estimate_b200.abft import AbftConfig, AbftInjector, AbftStatsCollector, CheapSumChecker
+
+    dev = torch.device("cuda", 0)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    iters = max(args.steps, 5)
+    chk = N.MODE_DETECT | N.MODE_CORRECT
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        torch.cuda._sleep(200_000_000)
+        pairs = []
+        for _ in range(iters):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            pairs.append((e0, e1))
+        torch.cuda.synchronize()
+        ms = sorted(e0.elapsed_time(e1) for e0, e1 in pairs)
+        return ms[len(ms) // 2]
+
+    def wall(fn, reps):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            fn()
+        torch.cuda.synchronize()
+        return (time.perf_counter() - t0) * 1e3 / reps
+
+    for name, bsz, m, n, k, lay in BMM_SHAPES:
+        torch.manual_seed(bsz + m + n + k)
+        a = (torch.randn(bsz, m, k, device=dev) * k ** -0.5).bfloat16()
+        w = (torch.randn(bsz, n, k, device=dev) * k ** -0.5).bfloat16()
+        b = w.transpose(1, 2) if lay == "view" else w.transpose(1, 2).contiguous()
+        out = torch.empty(bsz, m, n, device=dev, dtype=torch.bfloat16)
+        rep = ops.ReportBuffer(64, dev, batch=bsz)
+        t_cublas = timed(lambda: torch.bmm(a, b, out=out))
+        t_off = timed(lambda: ops.abft_bmm(a, b, mode=N.MODE_OFF, out=out))
+        t_chk = timed(lambda: ops.abft_bmm(a, b, mode=chk, out=out, report=rep))
+        clean = rep.read().n_faults
+        ref = out.clone()
+        delta = 256.0 * ref.float().abs().max().item()
+        bf = bsz // 2
+        _, r1 = ops.abft_bmm(a, b, mode=chk, inject=[(bf * m + m // 2, n // 3, delta)])
+        r1 = r1.read()
+        reps = max(5, min(50, iters // 4))
+        t_ref = wall(lambda: reference_bmm_flow(a, b), reps)
+        cfg = AbftConfig(enable=True, checker_backend="b200", detect_only=False)
+        stats = AbftStatsCollector()
+        inj = AbftInjector(cfg, CheapSumChecker(cfg), stats, defer_reports=True)
+        with torch.inference_mode(), inj:
+            t_inj = wall(lambda: torch.bmm(a, b), reps)
+        s = stats.export_summary()["abft"]
+        fl = 2.0 * bsz * m * n * k
+        print(json.dumps({
+            "shape": name, "batch": bsz, "M": m, "N": n, "K": k, "mat2": lay,
+            "cublas_tflops": fl / t_cublas / 1e9, "unchecked_tflops": fl / t_off / 1e9,
+            "checked_tflops": fl / t_chk / 1e9, "cublas_ms": t_cublas, "unchecked_ms": t_off, "checked_ms": t_chk,
+            "overhead_vs_cublas_pct": 100.0 * (t_chk / t_cublas - 1.0),
+            "reference_flow_ms": t_ref, "injector_fused_ms": t_inj, "speedup_vs_reference_flow": t_ref / t_inj,
+            "injector_checks": s["checks_total"], "injector_fails": s["fail_total"],
+            "clean_records": clean, "fault_located_exact": r1.coords() == [(bf * m + m // 2, n // 3)],
+            "fault_batch_counts": r1.batch_counts[bf] if r1.batch_counts else None}), flush=True)
+        del a, w, b, out, ref
 
 
 # ------------------------------------------------------------------ model path
@@ -1029,6 +1168,12 @@ def main():
         return
     if args.sweep:
         sweep(args)
+        return
+    if args.bmm_sweep:
+        bmm_sweep(args)
+        return
+    if args.profile_bmm:
+        profile_bmm(args)
         return
     if args.profile_case:
         profile_case(args)

@@ -147,6 +147,26 @@ int make_tmap_kmajor(CUtensorMap* m, const void* ptr, int64_t inner, int64_t out
   return r == CUDA_SUCCESS ? ABFT_OK : ABFT_ERR_ALIGNMENT;
 }
 
+// The output map: `batch` row-major [rows, ld] bf16 matrices (matrix b at
+// ptr + b * bstride elements), stored in 32 x 32 boxes whose shared-memory
+// source uses the 64-byte swizzle (an epilogue warp's staging block).
+int make_tmap_store(CUtensorMap* m, void* ptr, int64_t cols, int64_t rows, int64_t ld, int64_t batch,
+                    int64_t bstride) {
+  EncodeTiledFn enc = get_encoder();
+  if (enc == nullptr) return ABFT_ERR_DRIVER;
+  if (batch <= 1) {
+    batch = 1;
+    bstride = ld * rows;
+  }
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(batch)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 2, static_cast<cuuint64_t>(bstride) * 2};
+  cuuint32_t box[3] = {32u, 32u, 1u};
+  cuuint32_t es[3] = {1u, 1u, 1u};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, ptr, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? ABFT_OK : ABFT_ERR_ALIGNMENT;
+}
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -494,12 +514,13 @@ void make_frames(const abft_gemm_args* a, void* copy, Frames* f) {
 
 template <int BN, bool CHECK, bool PAIR>
 int launch_gemm(int dev, int slot, const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmB2,
-                const CUtensorMap& tmV, const CUtensorMap& tmBt, const GemmParams& p, int grid, cudaStream_t s) {
+                const CUtensorMap& tmV, const CUtensorMap& tmBt, const CUtensorMap& tmC, const GemmParams& p, int grid,
+                cudaStream_t s) {
   int rc = ensure_smem_attr<BN, CHECK, PAIR>(dev, slot);
   if (rc != ABFT_OK) return rc;
   constexpr size_t smem = GemmCfg<BN, CHECK, PAIR>::kSmemBytes;
   if constexpr (!PAIR) {
-    abft_gemm_kernel<BN, CHECK, false><<<grid, kThreads, smem, s>>>(tmA, tmB, tmB2, tmV, tmBt, p);
+    abft_gemm_kernel<BN, CHECK, false><<<grid, kThreads, smem, s>>>(tmA, tmB, tmB2, tmV, tmBt, tmC, p);
   } else {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(grid));
@@ -509,7 +530,7 @@ int launch_gemm(int dev, int slot, const CUtensorMap& tmA, const CUtensorMap& tm
     cudaLaunchAttribute at = pair_cluster_attr();
     cfg.attrs = &at;
     cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, abft_gemm_kernel<BN, CHECK, true>, tmA, tmB, tmB2, tmV, tmBt, p) != cudaSuccess)
+    if (cudaLaunchKernelEx(&cfg, abft_gemm_kernel<BN, CHECK, true>, tmA, tmB, tmB2, tmV, tmBt, tmC, p) != cudaSuccess)
       return launch_status(), ABFT_ERR_CUDA;
   }
   return launch_status();
@@ -661,6 +682,11 @@ int abft_gemm_bf16(const abft_gemm_args* args, void* stream) {
     rc = make_tmap_kmajor(&tmV, V, a->K, vrows, a->K, kChkRows, nb, vrows * a->K);
     if (rc != ABFT_OK) return rc;
   }
+  CUtensorMap tmC = tmA;  // placeholder with swapped operands (transposed plain stores)
+  if (!swap) {
+    rc = make_tmap_store(&tmC, a->C, a->N, a->M, a->ldc, nb, nb > 1 ? (a->stride_c / a->ldc) * a->ldc : 0);
+    if (rc != ABFT_OK) return rc;
+  }
 
   GemmParams p;
   p.C = static_cast<__nv_bfloat16*>(a->C);
@@ -759,14 +785,14 @@ int abft_gemm_bf16(const abft_gemm_args* args, void* stream) {
     if (rc != ABFT_OK) return rc;
   }
   if (ws.pair)
-    rc = check ? launch_gemm<256, true, true>(dev, kPairSlot[1], tmA, tmB, tmB2, tmV, tmBt, p, grid, s)
-               : launch_gemm<256, false, true>(dev, kPairSlot[0], tmA, tmB, tmB2, tmV, tmBt, p, grid, s);
+    rc = check ? launch_gemm<256, true, true>(dev, kPairSlot[1], tmA, tmB, tmB2, tmV, tmBt, tmC, p, grid, s)
+               : launch_gemm<256, false, true>(dev, kPairSlot[0], tmA, tmB, tmB2, tmV, tmBt, tmC, p, grid, s);
   else if (bn == 256)
-    rc = check ? launch_gemm<256, true, false>(dev, 0, tmA, tmB, tmB2, tmV, tmBt, p, grid, s)
-               : launch_gemm<256, false, false>(dev, 1, tmA, tmB, tmB2, tmV, tmBt, p, grid, s);
+    rc = check ? launch_gemm<256, true, false>(dev, 0, tmA, tmB, tmB2, tmV, tmBt, tmC, p, grid, s)
+               : launch_gemm<256, false, false>(dev, 1, tmA, tmB, tmB2, tmV, tmBt, tmC, p, grid, s);
   else
-    rc = check ? launch_gemm<128, true, false>(dev, 2, tmA, tmB, tmB2, tmV, tmBt, p, grid, s)
-               : launch_gemm<128, false, false>(dev, 3, tmA, tmB, tmB2, tmV, tmBt, p, grid, s);
+    rc = check ? launch_gemm<128, true, false>(dev, 2, tmA, tmB, tmB2, tmV, tmBt, tmC, p, grid, s)
+               : launch_gemm<128, false, false>(dev, 3, tmA, tmB, tmB2, tmV, tmBt, tmC, p, grid, s);
   if (rc != ABFT_OK) return rc;
 
   if (a->mode & ABFT_MODE_REF) {

@@ -343,12 +343,15 @@ __device__ __forceinline__ bool mma_mainloop_n(int n, uint8_t* smem, uint64_t* f
 // tmB2 (pairs with checks only): B rows for the odd CTA, whose share of a
 // tile's data rows is BD - 128 rather than 128. tmBt: the data rows of the
 // tail tile column that the compact tail tile needs in this CTA (box
-// p.tail_box rows), when checks are on.
+// p.tail_box rows), when checks are on. tmC: the output [batch][M][N] in
+// 32 x 32 boxes with 64-byte swizzle, the layout of an epilogue warp's
+// staging block (unused with swapped operands).
 template <int BN, bool CHECK, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     abft_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmB2, const __grid_constant__ CUtensorMap tmV,
-                     const __grid_constant__ CUtensorMap tmBt, const GemmParams p) {
+                     const __grid_constant__ CUtensorMap tmBt, const __grid_constant__ CUtensorMap tmC,
+                     const GemmParams p) {
   using Cfg = GemmCfg<BN, CHECK, PAIR>;
   constexpr int S = Cfg::kStages;
   constexpr int BD = Cfg::kBD;
@@ -400,6 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (PAIR && CHECK) tma_prefetch_desc(&tmB2);
     if (CHECK) tma_prefetch_desc(&tmV);
     if (CHECK && p.tail_box > 0) tma_prefetch_desc(&tmBt);
+    if (!p.swap) tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
     tmem_alloc_g<G>(tmem_slot, Cfg::kTmemCols);
@@ -576,15 +580,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     int xuse = 0;  // uses of the row-half exchange buffers
+    // This warp's staging block is the source of a bulk store that may not
+    // have read it yet (lane 0 issued it; warp-uniform).
+    bool stg_busy = false;
     // Hand the accumulator back to the MMA issuer (in a pair, the even CTA:
-    // one arrival per warp after all its lanes' TMEM reads).
+    // one arrival per warp after all its lanes' TMEM reads). The reads have
+    // completed (tcgen05.wait::ld) and the fence orders them before the
+    // arrival; the MMA that overwrites the accumulator reads nothing this
+    // thread wrote, so the arrival need not wait for the output stores.
     auto release_acc = [&](int a) {
       tc_fence_before();
       if constexpr (PAIR) {
         __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[a]), 0));
+        if (lane == 0) mbar_arrive_cluster_relaxed(mapa_shared(smem_u32(&tempty[a]), 0));
       } else {
-        mbar_arrive(&tempty[a]);
+        mbar_arrive_relaxed(&tempty[a]);
       }
     };
     SegmentIter seg(p, unit, nunits);
@@ -704,57 +714,61 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int hcol0 = h * NV;  // first local column of this thread
       const bool row_ok = grow < p.M;
 
-      // Debug faults added to the fp32 accumulator (same values in both passes).
-      constexpr int kMaxInj = 4;
-      int inj_c[kMaxInj];
-      float inj_d[kMaxInj];
-      int n_my = 0;
-#pragma unroll
-      for (int i = 0; i < kMaxInj; ++i) {
-        inj_c[i] = -1;
-        inj_d[i] = 0.f;
-      }
+      // Debug faults added to the fp32 accumulator: does this row (and
+      // column half) hold any? The rare rows that do scan the list again
+      // per chunk (inj_add) rather than keep it in registers. Batch offsets
+      // of the flattened fault coordinates: C's rows are the kernel's rows,
+      // or its columns with swapped operands.
+      const int inj_row = p.swap ? grow : bz * p.M + grow;
+      const int inj_cbase = (p.swap ? bz * p.N : 0) + col0 + hcol0;  // list column of local column 0 of this half
+      bool n_my = false;
       if (p.n_inj > 0 && row_ok) {
-        // Batch offsets of the flattened fault coordinates: C's rows are the
-        // kernel's rows, or its columns with swapped operands.
-        const int inj_row = p.swap ? grow : bz * p.M + grow;
-        const int inj_coff = p.swap ? bz * p.N : 0;
         for (int i = 0; i < p.n_inj; ++i) {
-          const int ic = p.inj_cols[i] - inj_coff - col0 - hcol0;
-          if (p.inj_rows[i] == inj_row && ic >= 0 && ic < NV && hcol0 + ic < ncols && n_my < kMaxInj) {
-#pragma unroll
-            for (int j = 0; j < kMaxInj; ++j)
-              if (j == n_my) {
-                inj_c[j] = ic;
-                inj_d[j] = p.inj_deltas[i];
-              }
-            ++n_my;
-          }
+          const int ic = p.inj_cols[i] - inj_cbase;
+          n_my |= p.inj_rows[i] == inj_row && ic >= 0 && ic < NV && hcol0 + ic < ncols;
         }
       }
+      // Sum of the injected deltas at local column lc (of this half).
+      auto inj_add = [&](int lc) {
+        float d = 0.f;
+        for (int i = 0; i < p.n_inj; ++i)
+          if (p.inj_rows[i] == inj_row && p.inj_cols[i] - inj_cbase == lc) d += p.inj_deltas[i];
+        return d;
+      };
 
-      int fix_col = -1;  // local column to correct, if any
-      float fix_delta = 0.f;
-      bool aborted = false;
-      if (CHECK) {
-        float s1 = 0.f, s2 = 0.f, s3 = 0.f, amax = 0.f;
+      // One pass over the accumulator in 32-column chunks: each chunk feeds
+      // the row checksums (with checks on) and is rounded, staged and stored
+      // at once (swapped operands: straight to C's transposed position).
+      // The first column half starts its sums from the negated expected
+      // checksums (split checksum columns added up), so the two halves'
+      // partials add up to the residuals.
+      float s1 = 0.f, s2 = 0.f, s3 = 0.f, amax = 0.f;
+      if (CHECK && h == 0) {
+        s1 = -((__uint_as_float(chk[0]) + __uint_as_float(chk[1])) + __uint_as_float(chk[2]));
+        s2 = -((__uint_as_float(chk[3]) + __uint_as_float(chk[4])) + __uint_as_float(chk[5]));
+        s3 = -(__uint_as_float(chk[6]) + __uint_as_float(chk[7]));
+      }
+      float row_out_sum = 0.f;
+      const uint4* bp = reinterpret_cast<const uint4*>(p.bias + col0 + hcol0);
+      const int rd_grow = row0 + q * 32 + rd_row;  // global row of this lane's first read-side row
+      const float row_bias = (p.swap && p.bias != nullptr && row_ok) ? __bfloat162float(p.bias[grow]) : 0.f;
+      const int crow0 = bz * p.c_rows;  // this batch's first row of C
 #pragma unroll 1
-        for (int c = 0; c < NCH; ++c) {
-          if (hcol0 + c * 32 >= ncols) break;  // warp-uniform: nothing valid from here on
-          uint32_t v[32];
-          __syncwarp();
-          tmem_ld_32x32b_x32(tcol + c * 32, v);
-          tmem_ld_wait();
-          if (n_my) {
+      for (int c = 0; c < NCH; ++c) {
+        const int base = hcol0 + c * 32;  // first local column of the chunk (a multiple of 32)
+        if (base >= ncols) break;         // warp-uniform: nothing valid from here on
+        uint32_t v[32];
+        __syncwarp();
+        tmem_ld_32x32b_x32(tcol + c * 32, v);
+        tmem_ld_wait();
+        float x[32];
 #pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              float x = __uint_as_float(v[e]);
+        for (int e = 0; e < 32; ++e) x[e] = __uint_as_float(v[e]);
+        if (n_my) {
 #pragma unroll
-              for (int i = 0; i < kMaxInj; ++i) x += (inj_c[i] == c * 32 + e) ? inj_d[i] : 0.f;
-              v[e] = __float_as_uint(x);
-            }
-          }
-          const int base = hcol0 + c * 32;  // first local column of the chunk (a multiple of 32)
+          for (int e = 0; e < 32; ++e) x[e] += inj_add(c * 32 + e);
+        }
+        if constexpr (CHECK) {
           if (base + 32 <= ncols) {
             // Whole chunk valid: the column weights split into the chunk's
             // base plus a compile-time offset, and the Thue-Morse sign of
@@ -762,8 +776,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             float a0 = 0.f, a1 = 0.f, w0 = 0.f, w1 = 0.f, t0 = 0.f, t1 = 0.f;
 #pragma unroll
             for (int e = 0; e < 32; e += 2) {
-              const float x0 = __uint_as_float(v[e]);
-              const float x1 = __uint_as_float(v[e + 1]);
+              const float x0 = x[e];
+              const float x1 = x[e + 1];
               a0 += x0;
               a1 += x1;
               w0 = fmaf(static_cast<float>(e), x0, w0);
@@ -780,19 +794,95 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else {
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
-              const float x = __uint_as_float(v[e]);
               const int col = base + e;
               if (col < ncols) {
-                s1 += x;
-                s2 = fmaf(static_cast<float>(col + 1), x, s2);
-                s3 += (__popc(col) & 1) ? -x : x;
-                amax = fmaxf(amax, fabsf(x));
+                s1 += x[e];
+                s2 = fmaf(static_cast<float>(col + 1), x[e], s2);
+                s3 += (__popc(col) & 1) ? -x[e] : x[e];
+                amax = fmaxf(amax, fabsf(x[e]));
               }
             }
           }
         }
-        // Exchange the half-row partials with the partner thread (other half);
-        // amax >= 0 and s3 rides in .w.
+        if (p.swap) {
+          // Lane l holds kernel row row0 + q*32 + l = C column: for each of
+          // this chunk's C rows a warp writes 32 consecutive columns.
+          if (row_ok) {
+            __nv_bfloat16* cc = p.C + static_cast<int64_t>(crow0 + col0 + base) * p.ldc + grow;
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              if (base + e < ncols) {
+                const __nv_bfloat16 o = __float2bfloat16_rn(x[e] + row_bias);
+                cc[static_cast<int64_t>(e) * p.ldc] = o;
+                if (p.mode & ABFT_MODE_REF) row_out_sum += __bfloat162float(o);
+              }
+            }
+          }
+          continue;
+        }
+        if (stg_busy) {
+          if (lane == 0) bulk_wait_read_all();
+          __syncwarp();
+          stg_busy = false;
+        }
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const bool gvalid = row_ok && (base + g * 8 < ncols);
+          if (p.bias != nullptr && gvalid) {
+            const uint4 bw = __ldg(bp + c * 4 + g);
+            x[g * 8 + 0] += bf16_lo(bw.x);
+            x[g * 8 + 1] += bf16_hi(bw.x);
+            x[g * 8 + 2] += bf16_lo(bw.y);
+            x[g * 8 + 3] += bf16_hi(bw.y);
+            x[g * 8 + 4] += bf16_lo(bw.z);
+            x[g * 8 + 5] += bf16_hi(bw.z);
+            x[g * 8 + 6] += bf16_lo(bw.w);
+            x[g * 8 + 7] += bf16_hi(bw.w);
+          }
+          const uint4 packed =
+              make_uint4(pack_bf16x2(x[g * 8 + 0], x[g * 8 + 1]), pack_bf16x2(x[g * 8 + 2], x[g * 8 + 3]),
+                         pack_bf16x2(x[g * 8 + 4], x[g * 8 + 5]), pack_bf16x2(x[g * 8 + 6], x[g * 8 + 7]));
+          *reinterpret_cast<uint4*>(stg + lane * 64 + ((g ^ ((lane >> 1) & 3)) << 4)) = packed;
+          if ((p.mode & ABFT_MODE_REF) && gvalid) {
+            row_out_sum += ((bf16_lo(packed.x) + bf16_hi(packed.x)) + (bf16_lo(packed.y) + bf16_hi(packed.y))) +
+                           ((bf16_lo(packed.z) + bf16_hi(packed.z)) + (bf16_lo(packed.w) + bf16_hi(packed.w)));
+          }
+        }
+        if (base + 32 <= ncols) {
+          // A whole 32 x 32 block: one bulk tensor store (rows past M are
+          // clipped by the map); the next write of the block waits for it
+          // to have been read.
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&tmC, stg, col0 + base, row0 + q * 32, bz);
+            bulk_commit_group();
+          }
+          stg_busy = true;
+          continue;
+        }
+        __syncwarp();
+        // Partial block (next to the checksum columns, or the last tile
+        // column): plain stores. Instruction i covers rows 8i..8i+7 of the
+        // block, four lanes per row, each lane one 16-byte piece (8 columns).
+        const int lcol = base + rd_piece * 8;  // local column of this lane's piece
+        const bool col_ok = lcol < ncols;
+        __nv_bfloat16* cbase = p.C + static_cast<int64_t>(crow0 + rd_grow) * p.ldc + col0 + lcol;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int y = i * 8 + rd_row;
+          const uint4 val = *reinterpret_cast<const uint4*>(stg + y * 64 + ((rd_piece ^ ((y >> 1) & 3)) << 4));
+          if (col_ok && rd_grow + i * 8 < p.M) *reinterpret_cast<uint4*>(cbase + static_cast<int64_t>(i * 8) * p.ldc) = val;
+        }
+      }
+
+      bool aborted = false;
+      if constexpr (CHECK) {
+        // Exchange the half-row partials with the partner thread (other
+        // half); amax >= 0 and s3 rides in .w. The barrier (release/acquire)
+        // also orders every chunk store of both halves before a rewrite.
+        int fix_col = -1;  // local column to correct, if any
+        float fix_delta = 0.f;
         const int xb = xuse & 1;
         const uint32_t xphase = (xuse >> 1) & 1u;
         ++xuse;
@@ -803,16 +893,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
           const float4 p0 = xchg[(xb * 2 + 0) * kBM + r];
           const float4 p1 = xchg[(xb * 2 + 1) * kBM + r];
-          const float t1 = p0.x + p1.x;
-          const float t2 = p0.y + p1.y;
-          const float t3 = p0.w + p1.w;
+          const float res1 = p0.x + p1.x;
+          const float res2 = p0.y + p1.y;
+          const float res3 = p0.w + p1.w;
           const float tmax = fmaxf(p0.z, p1.z);
-          const float e1 = (__uint_as_float(chk[0]) + __uint_as_float(chk[1])) + __uint_as_float(chk[2]);
-          const float e2 = (__uint_as_float(chk[3]) + __uint_as_float(chk[4])) + __uint_as_float(chk[5]);
-          const float e3 = __uint_as_float(chk[6]) + __uint_as_float(chk[7]);
-          const float res1 = t1 - e1;
-          const float res2 = t2 - e2;
-          const float res3 = t3 - e3;
           const float thr = fmaf(p.thr_k, tmax, p.thr_abs);
           const bool det = row_ok && (fabsf(res1) > thr || fabsf(res2) > thr * static_cast<float>(ncols));
           if (det) {
@@ -868,88 +952,46 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-      }
-
-      // Pass 2: final values -> bf16 -> staging block -> global (swapped
-      // operands: straight to C's transposed position).
-      const int fix_local = fix_col - hcol0;  // column within this thread's half, or out of range
-      float row_out_sum = 0.f;
-      const uint4* bp = reinterpret_cast<const uint4*>(p.bias + col0 + hcol0);
-      const int rd_grow = row0 + q * 32 + rd_row;  // global row of this lane's first read-side row
-      const float row_bias = (p.swap && p.bias != nullptr && row_ok) ? __bfloat162float(p.bias[grow]) : 0.f;
-      const int crow0 = bz * p.c_rows;  // this batch's first row of C
-#pragma unroll 1
-      for (int c = 0; c < NCH; ++c) {
-        if (p.swap && hcol0 + c * 32 >= ncols) break;  // warp-uniform
-        uint32_t v[32];
-        __syncwarp();
-        tmem_ld_32x32b_x32(tcol + c * 32, v);
-        tmem_ld_wait();
-        float x[32];
-#pragma unroll
-        for (int e = 0; e < 32; ++e) x[e] = __uint_as_float(v[e]);
-        if (n_my) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-#pragma unroll
-            for (int i = 0; i < kMaxInj; ++i) x[e] += (inj_c[i] == c * 32 + e) ? inj_d[i] : 0.f;
+        // Correction: the owner of the located column (this half) reads the
+        // fp32 accumulator of that element again -- the chunk holding it,
+        // warp-collectively -- and stores accumulator - residual (+ bias)
+        // over the value stored above, in the same arithmetic order as the
+        // chunk pass (injected delta, correction, bias).
+        const int fix_local = fix_col - hcol0;
+        const bool mine = fix_col >= 0 && fix_local >= 0 && fix_local < NV;
+        uint32_t need = __ballot_sync(0xFFFFFFFFu, mine);
+        if (need != 0u && stg_busy) {
+          // The element was written by this warp's bulk stores: let them
+          // complete before the rewrite.
+          if (lane == 0) {
+            bulk_wait_all();
+            fence_proxy_async_global();
           }
+          __syncwarp();
+          stg_busy = false;
         }
-        if (static_cast<unsigned>(fix_local - c * 32) < 32u) {
+        while (need != 0u) {
+          const int cfix = __shfl_sync(0xFFFFFFFFu, fix_local >> 5, __ffs(need) - 1);
+          uint32_t v[32];
+          __syncwarp();
+          tmem_ld_32x32b_x32(tcol + cfix * 32, v);
+          tmem_ld_wait();
+          const bool here = mine && (fix_local >> 5) == cfix;
+          if (here) {
+            const int e0 = fix_local & 31;
+            float val = 0.f;
 #pragma unroll
-          for (int e = 0; e < 32; ++e) x[e] -= (fix_local == c * 32 + e) ? fix_delta : 0.f;
-        }
-        const int base = hcol0 + c * 32;
-        if (p.swap) {
-          // Lane l holds kernel row row0 + q*32 + l = C column: for each of
-          // this chunk's C rows a warp writes 32 consecutive columns.
-          if (row_ok) {
-            __nv_bfloat16* cc = p.C + static_cast<int64_t>(crow0 + col0 + base) * p.ldc + grow;
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              if (base + e < ncols) {
-                const __nv_bfloat16 o = __float2bfloat16_rn(x[e] + row_bias);
-                cc[static_cast<int64_t>(e) * p.ldc] = o;
-                if (p.mode & ABFT_MODE_REF) row_out_sum += __bfloat162float(o);
-              }
-            }
+            for (int e = 0; e < 32; ++e) val = (e == e0) ? __uint_as_float(v[e]) : val;
+            if (n_my) val += inj_add(fix_local);
+            const float bcol = p.swap ? row_bias : (p.bias != nullptr ? __bfloat162float(p.bias[col0 + fix_col]) : 0.f);
+            const __nv_bfloat16 o_old = __float2bfloat16_rn(val + bcol);
+            const __nv_bfloat16 o_new = __float2bfloat16_rn((val - fix_delta) + bcol);
+            const int64_t off = p.swap ? static_cast<int64_t>(crow0 + col0 + fix_col) * p.ldc + grow
+                                       : static_cast<int64_t>(crow0 + grow) * p.ldc + col0 + fix_col;
+            p.C[off] = o_new;
+            if (p.mode & ABFT_MODE_REF) row_out_sum += __bfloat162float(o_new) - __bfloat162float(o_old);
           }
-          continue;
-        }
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          const bool gvalid = row_ok && (base + g * 8 < ncols);
-          if (p.bias != nullptr && gvalid) {
-            const uint4 bw = __ldg(bp + c * 4 + g);
-            x[g * 8 + 0] += bf16_lo(bw.x);
-            x[g * 8 + 1] += bf16_hi(bw.x);
-            x[g * 8 + 2] += bf16_lo(bw.y);
-            x[g * 8 + 3] += bf16_hi(bw.y);
-            x[g * 8 + 4] += bf16_lo(bw.z);
-            x[g * 8 + 5] += bf16_hi(bw.z);
-            x[g * 8 + 6] += bf16_lo(bw.w);
-            x[g * 8 + 7] += bf16_hi(bw.w);
-          }
-          const uint4 packed =
-              make_uint4(pack_bf16x2(x[g * 8 + 0], x[g * 8 + 1]), pack_bf16x2(x[g * 8 + 2], x[g * 8 + 3]),
-                         pack_bf16x2(x[g * 8 + 4], x[g * 8 + 5]), pack_bf16x2(x[g * 8 + 6], x[g * 8 + 7]));
-          *reinterpret_cast<uint4*>(stg + lane * 64 + ((g ^ ((lane >> 1) & 3)) << 4)) = packed;
-          if ((p.mode & ABFT_MODE_REF) && gvalid) {
-            row_out_sum += ((bf16_lo(packed.x) + bf16_hi(packed.x)) + (bf16_lo(packed.y) + bf16_hi(packed.y))) +
-                           ((bf16_lo(packed.z) + bf16_hi(packed.z)) + (bf16_lo(packed.w) + bf16_hi(packed.w)));
-          }
-        }
-        __syncwarp();
-        // Read side: instruction i covers rows 8i..8i+7 of the block, four
-        // lanes per row, each lane one 16-byte piece (8 columns).
-        const int lcol = base + rd_piece * 8;  // local column of this lane's piece
-        const bool col_ok = lcol < ncols;
-        __nv_bfloat16* cbase = p.C + static_cast<int64_t>(crow0 + rd_grow) * p.ldc + col0 + lcol;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int y = i * 8 + rd_row;
-          const uint4 val = *reinterpret_cast<const uint4*>(stg + y * 64 + ((rd_piece ^ ((y >> 1) & 3)) << 4));
-          if (col_ok && rd_grow + i * 8 < p.M) *reinterpret_cast<uint4*>(cbase + static_cast<int64_t>(i * 8) * p.ldc) = val;
+          need &= ~__ballot_sync(0xFFFFFFFFu, here);
         }
       }
       release_acc(acc);
@@ -968,6 +1010,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Leave the tile loop together: the TMEM loads above are warp-collective.
       if (__any_sync(0xFFFFFFFFu, aborted)) break;
     }
+    // Bulk stores still in flight read this CTA's shared memory.
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
   }
 
   tc_fence_before();
