@@ -79,8 +79,7 @@ class WeightChecksumCache:
         self._d: dict = {}
 
     def get(self, weight: torch.Tensor, tile_n: int) -> torch.Tensor:
-        key = (weight.data_ptr(), tuple(weight.shape), tuple(weight.stride()), weight._version, tile_n,
-               weight.device.index)
+        key = (weight.data_ptr(), weight.shape, weight.stride(), weight._version, tile_n, weight.get_device())
         v = self._d.get(key)
         if v is None:
             if len(self._d) >= self.max_entries:
@@ -91,6 +90,20 @@ class WeightChecksumCache:
 
     def clear(self) -> None:
         self._d.clear()
+
+
+class _Slot:
+    """A report slot of an arena chunk: what the fused call needs of a
+    ReportBuffer (its capacity and device address), without a tensor view."""
+
+    __slots__ = ("capacity", "ptr")
+
+    def __init__(self, capacity: int, ptr: int):
+        self.capacity = capacity
+        self.ptr = ptr
+
+    def data_ptr(self) -> int:
+        return self.ptr
 
 
 class _ReportArena:
@@ -109,17 +122,14 @@ class _ReportArena:
         self.chunks: List[torch.Tensor] = []
         self.used = 0  # slots taken in the last chunk
 
-    def take(self) -> ops.ReportBuffer:
+    def take(self) -> "_Slot":
         if not self.chunks or self.used == self.slots:
             self.chunks.append(torch.empty(self.slots * self.slot_bytes, dtype=torch.uint8, device=self.device))
+            self.base = self.chunks[-1].data_ptr()
             self.used = 0
-        off = self.used * self.slot_bytes
+        ptr = self.base + self.used * self.slot_bytes
         self.used += 1
-        # a ReportBuffer over the slot, without the per-call size query
-        rb = ops.ReportBuffer.__new__(ops.ReportBuffer)
-        rb.capacity = self.capacity
-        rb.tensor = self.chunks[-1][off:off + self.slot_bytes]
-        return rb
+        return _Slot(self.capacity, ptr)
 
     def drain(self) -> List[N.FaultReport]:
         reports: List[N.FaultReport] = []
@@ -130,6 +140,7 @@ class _ReportArena:
                            for j in range(n))
         # keep the first chunk for the next forward
         self.chunks = self.chunks[:1]
+        self.base = self.chunks[0].data_ptr() if self.chunks else 0
         self.used = 0
         return reports
 
@@ -332,15 +343,15 @@ class AbftInjector(AbstractContextManager):
         if x2.stride(1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
             x2 = x2.contiguous()
         m = x2.shape[0]
+        dix = x2.get_device()
         # injection first, then the check gate: the reference's rng order
         idx = self._draw_fault(m * n)
         injected = idx is not None
-        b2 = weight.t()
         check = self._check_gate_dims(m, k, n)
         mode = N.MODE_OFF
         if check:
             mode = N.MODE_DETECT | (0 if self.cfg.detect_only else N.MODE_CORRECT)
-        tkey = (m, n, k, mode, x2.device.index)
+        tkey = (m, n, k, mode, dix)
         tile_n = self._tile_n.get(tkey)
         if tile_n is None:
             tile_n = self._tile_n[tkey] = ops.pick_tile_n(m, n, k, x2.device, mode)
@@ -353,26 +364,27 @@ class AbftInjector(AbstractContextManager):
         if check:
             if self.defer_reports and self.cfg.record_enable:
                 # one arena per device: reports of one device are drained in call order
-                arena = self._arenas.get(x2.device.index)
+                arena = self._arenas.get(dix)
                 if arena is None:
-                    arena = self._arenas[x2.device.index] = _ReportArena(self.cfg.report_capacity, x2.device)
+                    arena = self._arenas[dix] = _ReportArena(self.cfg.report_capacity, x2.device)
                 rep = arena.take()
             else:
                 rep = ops.ReportBuffer(self.cfg.report_capacity, x2.device)
-        out, rep = ops.abft_gemm(x2, weight, None if bias is None else bias.contiguous(), mode=mode,
-                                 tile_n=0 if swapped else tile_n,
-                                 thr_scale=self.cfg.thr_scale, thr_abs=self.cfg.thr_abs, checksums=cks,
-                                 inject=inject, report=rep)
+        if bias is not None and not bias.is_contiguous():
+            bias = bias.contiguous()
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=x2.device)
+        # operands checked by _fused_linear_ok: straight to the launch
+        ops._gemm_launch(x2, weight, bias, out, m, n, k, mode, 0 if swapped else tile_n, 0, 0, self.cfg.thr_scale,
+                         self.cfg.thr_abs, 1e-2, 1e-2, cks, inject, rep, 0)
         if check:
             if self.cfg.record_enable:
                 if self.defer_reports:
-                    self._pending.append((x2.device.index, "linear", self.stats.current_phase, (m, k, n), injected,
-                                          None))
+                    self._pending.append((dix, "linear", self.stats.current_phase, (m, k, n), injected, None))
                 else:
                     self.stats.record_check(op_name="linear", shape_key=f"A{(m, k)}_B{(k, n)}_C{(m, n)}",
                                             result=result_from_report(rep.read()), injected=injected)
             if self.cfg.dump_file:
-                self._maybe_dump_tensors("linear", f"A{(m, k)}_B{(k, n)}_C{(m, n)}", x2, b2, out, bias)
+                self._maybe_dump_tensors("linear", f"A{(m, k)}_B{(k, n)}_C{(m, n)}", x2, weight.t(), out, bias)
         return out.reshape(*x.shape[:-1], n)
 
     # -------------------------------------------------- fused bmm / matmul

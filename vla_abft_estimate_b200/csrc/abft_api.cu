@@ -126,17 +126,52 @@ int pair_units_on(int dev, int sms) {
   return d.pair_clusters[CHECK] < sms / 2 ? d.pair_clusters[CHECK] : sms / 2;
 }
 
+// Encoded tensor maps are a pure function of (kind, address, extents,
+// strides, box): a small per-thread direct-mapped cache skips the encoder
+// for operands seen before (weights every call; activation and output
+// buffers whenever the caller's allocator hands back the same block).
+struct TmapKey {
+  const void* ptr;
+  int64_t inner, outer, ld, batch, bstride;
+  int box, kind;
+  bool operator==(const TmapKey& o) const {
+    return ptr == o.ptr && inner == o.inner && outer == o.outer && ld == o.ld && batch == o.batch &&
+           bstride == o.bstride && box == o.box && kind == o.kind;
+  }
+};
+struct TmapEntry {
+  TmapKey key;
+  CUtensorMap map;
+  bool valid;
+};
+constexpr int kTmapCacheSize = 64;
+thread_local TmapEntry t_tmaps[kTmapCacheSize];
+
+TmapEntry& tmap_slot(const TmapKey& k) {
+  uint64_t h = reinterpret_cast<uintptr_t>(k.ptr) >> 4;
+  h ^= static_cast<uint64_t>(k.outer) * 0x9E3779B97F4A7C15ull;
+  h ^= static_cast<uint64_t>(k.box * 8 + k.kind) * 0xC2B2AE3D27D4EB4Full;
+  h ^= h >> 29;
+  return t_tmaps[h % kTmapCacheSize];
+}
+
 // A 3-D map over `batch` row-major [outer, ld] bf16 matrices, matrix b at
 // ptr + b * bstride elements (bstride ignored for batch <= 1), read in boxes
 // of 64 (inner) x box_outer rows x 1 matrix with 128-byte swizzle.
 int make_tmap_kmajor(CUtensorMap* m, const void* ptr, int64_t inner, int64_t outer, int64_t ld, int box_outer,
                      int64_t batch = 1, int64_t bstride = 0) {
-  EncodeTiledFn enc = get_encoder();
-  if (enc == nullptr) return ABFT_ERR_DRIVER;
   if (batch <= 1) {
     batch = 1;
     bstride = ld * outer;
   }
+  const TmapKey key{ptr, inner, outer, ld, batch, bstride, box_outer, 0};
+  TmapEntry& e = tmap_slot(key);
+  if (e.valid && e.key == key) {
+    *m = e.map;
+    return ABFT_OK;
+  }
+  EncodeTiledFn enc = get_encoder();
+  if (enc == nullptr) return ABFT_ERR_DRIVER;
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer), static_cast<cuuint64_t>(batch)};
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 2, static_cast<cuuint64_t>(bstride) * 2};
   cuuint32_t box[3] = {64u, static_cast<cuuint32_t>(box_outer), 1u};
@@ -144,7 +179,11 @@ int make_tmap_kmajor(CUtensorMap* m, const void* ptr, int64_t inner, int64_t out
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, es,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? ABFT_OK : ABFT_ERR_ALIGNMENT;
+  if (r != CUDA_SUCCESS) return ABFT_ERR_ALIGNMENT;
+  e.key = key;
+  e.map = *m;
+  e.valid = true;
+  return ABFT_OK;
 }
 
 // The output map: `batch` row-major [rows, ld] bf16 matrices (matrix b at
@@ -152,19 +191,29 @@ int make_tmap_kmajor(CUtensorMap* m, const void* ptr, int64_t inner, int64_t out
 // source uses the 64-byte swizzle (an epilogue warp's staging block).
 int make_tmap_store(CUtensorMap* m, void* ptr, int64_t cols, int64_t rows, int64_t ld, int64_t batch,
                     int64_t bstride) {
-  EncodeTiledFn enc = get_encoder();
-  if (enc == nullptr) return ABFT_ERR_DRIVER;
   if (batch <= 1) {
     batch = 1;
     bstride = ld * rows;
   }
+  const TmapKey key{ptr, cols, rows, ld, batch, bstride, 32, 1};
+  TmapEntry& e = tmap_slot(key);
+  if (e.valid && e.key == key) {
+    *m = e.map;
+    return ABFT_OK;
+  }
+  EncodeTiledFn enc = get_encoder();
+  if (enc == nullptr) return ABFT_ERR_DRIVER;
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(batch)};
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 2, static_cast<cuuint64_t>(bstride) * 2};
   cuuint32_t box[3] = {32u, 32u, 1u};
   cuuint32_t es[3] = {1u, 1u, 1u};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, ptr, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? ABFT_OK : ABFT_ERR_ALIGNMENT;
+  if (r != CUDA_SUCCESS) return ABFT_ERR_ALIGNMENT;
+  e.key = key;
+  e.map = *m;
+  e.valid = true;
+  return ABFT_OK;
 }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -402,7 +451,49 @@ struct Plan {
 };
 
 // dev < 0: no device to ask (co-resident pairs assumed sms / 2).
+int make_plan_uncached(const abft_gemm_args* a, int dev, int sms, Plan* pl);
+
+// Plans depend on the shape, mode, tile requests, batch and device only: a
+// per-thread direct-mapped cache keeps the tile search off repeated calls.
+struct PlanKey {
+  int64_t M, N, K, batch;
+  uint32_t mode;
+  int tile_n, tile_m, has_cks, dev, sms;
+  bool operator==(const PlanKey& o) const {
+    return M == o.M && N == o.N && K == o.K && batch == o.batch && mode == o.mode && tile_n == o.tile_n &&
+           tile_m == o.tile_m && has_cks == o.has_cks && dev == o.dev && sms == o.sms;
+  }
+};
+struct PlanEntry {
+  PlanKey key;
+  Plan plan;
+  bool valid;
+};
+constexpr int kPlanCacheSize = 32;
+thread_local PlanEntry t_plans[kPlanCacheSize];
+
 int make_plan(const abft_gemm_args* a, int dev, int sms, Plan* pl) {
+  const PlanKey key{a->M, a->N, a->K, batch_of(a), a->mode, a->tile_n, a->tile_m, a->checksums != nullptr ? 1 : 0,
+                    dev, sms};
+  uint64_t h = static_cast<uint64_t>(a->M) * 0x9E3779B97F4A7C15ull ^ static_cast<uint64_t>(a->N) * 0xC2B2AE3D27D4EB4Full ^
+               static_cast<uint64_t>(a->K) * 0x165667B19E3779F9ull ^ (static_cast<uint64_t>(key.batch) << 7) ^
+               (static_cast<uint64_t>(a->mode) << 3) ^ static_cast<uint64_t>(a->tile_n + a->tile_m + key.has_cks);
+  h ^= h >> 31;
+  PlanEntry& e = t_plans[h % kPlanCacheSize];
+  if (e.valid && e.key == key) {
+    *pl = e.plan;
+    return ABFT_OK;
+  }
+  const int rc = make_plan_uncached(a, dev, sms, pl);
+  if (rc == ABFT_OK) {
+    e.key = key;
+    e.plan = *pl;
+    e.valid = true;
+  }
+  return rc;
+}
+
+int make_plan_uncached(const abft_gemm_args* a, int dev, int sms, Plan* pl) {
   const int64_t nb = batch_of(a);
   pl->check = (a->mode & (ABFT_MODE_DETECT | ABFT_MODE_CORRECT)) != 0;
   pl->bn = a->tile_n ? a->tile_n : pick_tile_n(a->M, a->N, a->K, sms, a->mode, nb);

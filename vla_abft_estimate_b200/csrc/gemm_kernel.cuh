@@ -607,11 +607,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t tacc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
       const uint32_t tcol = tacc + static_cast<uint32_t>(h * NV);  // this thread's first column
+      // Accumulator columns the MMA wrote: BN, or the compact tail tile's
+      // width; stream-K partials carry only those.
+      const int acc_w = (p.tail_n != 0 && nt == p.tiles_n - 1) ? p.tail_n : BN;
 
       if (kb0 != 0) {
         // Stream-K contributor: the tile's first k-blocks belong to a lower
-        // CTA, which finishes the tile. Hand it the fp32 partial (all BN
-        // columns, checksum columns included), column-major so that each
+        // CTA, which finishes the tile. Hand it the fp32 partial (every
+        // column the MMA wrote, checksum columns included), column-major so that each
         // warp store is 32 consecutive words. A segment that starts inside
         // a tile is the first segment of this CTA, so it is stored before
         // this CTA waits for anything: the wait chain is one link long.
@@ -620,6 +623,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         float4* dst = reinterpret_cast<float4*>(p.partials) + (static_cast<size_t>(blockIdx.x) * (BN / 4) + h * NV / 4) * kBM + r;
 #pragma unroll 1
         for (int c = 0; c < NCH; ++c) {
+          if (h * NV + c * 32 >= acc_w) break;  // warp-uniform
           uint32_t v[32];
           __syncwarp();
           tmem_ld_32x32b_x32(tcol + c * 32, v);
@@ -678,6 +682,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float4* src = reinterpret_cast<const float4*>(p.partials) + static_cast<size_t>(cc) * (BN / 4) * kBM + r;
 #pragma unroll 1
           for (int c = 0; c < NCH; ++c) {
+            if (h * NV + c * 32 >= acc_w) break;  // warp-uniform: nothing stored from here on
             float4 q4[8];
 #pragma unroll
             for (int g = 0; g < 8; ++g) q4[g] = __ldcg(src + (h * NV / 4 + c * 8 + g) * kBM);

@@ -89,20 +89,45 @@ def _device_index(device: Optional[torch.device]) -> int:
 _WORKSPACES: dict = {}
 
 
-def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+def _workspace(device: torch.device, nbytes: int, stream: Optional[int] = None) -> torch.Tensor:
     """Scratch for the current stream of ``device``, grown on demand.
 
     One buffer per (device, stream): calls on one stream run in order, so
     reusing it is safe; a buffer replaced by a larger one is freed in stream
     order by the caching allocator.
     """
-    stream = torch.cuda.current_stream(device)
-    key = (device.index, stream.cuda_stream)
+    if stream is None:
+        stream = torch.cuda.current_stream(device).cuda_stream
+    key = (device.index, stream)
     ws = _WORKSPACES.get(key)
     if ws is None or ws.numel() < nbytes:
         ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
         _WORKSPACES[key] = ws
     return ws
+
+
+# abft_gemm_workspace_bytes depends on the shape, mode, tile requests and
+# layout only: remembered per key so a repeated call makes one library call.
+_WS_BYTES: dict = {}
+
+
+def _run_gemm(args: N.GemmArgs, dev: torch.device, key: tuple) -> None:
+    """Workspace, current stream and device guard around abft_gemm_bf16."""
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    stream = torch._C._cuda_getCurrentRawStream(idx)
+    L = N.lib()
+    if torch.cuda.current_device() != idx:
+        with torch.cuda.device(idx):
+            return _run_gemm(args, dev, key)
+    key = (idx,) + key
+    ws_bytes = _WS_BYTES.get(key)
+    if ws_bytes is None:
+        ws_bytes = _WS_BYTES[key] = int(L.abft_gemm_workspace_bytes(ctypes.byref(args)))
+    if ws_bytes:
+        ws = _workspace(dev, ws_bytes, stream)
+        args.workspace = ws.data_ptr()
+        args.workspace_bytes = ws.numel()
+    N.check("abft_gemm_bf16", L.abft_gemm_bf16(ctypes.byref(args), ctypes.c_void_p(stream)))
 
 
 def pick_tile_n(m: int, n: int, k: int, device: Optional[torch.device] = None,
@@ -215,8 +240,17 @@ def abft_gemm(
         need = int(N.lib().abft_checksum_bytes(n, k, int(tile_n)))
         if checksums.numel() * 2 < need:
             raise ValueError("checksums were encoded for a different weight shape or tile width")
-    inj = _Inject(inject, dev) if inject else None
+    _gemm_launch(a, weight, bias, out, m, n, k, mode, tile_n, tile_m, swap_ab, thr_scale, thr_abs, tol_abs, tol_rel,
+                 checksums, inject, report, num_sms)
+    return out, report
 
+
+def _gemm_launch(a, weight, bias, out, m, n, k, mode, tile_n, tile_m, swap_ab, thr_scale, thr_abs, tol_abs, tol_rel,
+                 checksums, inject, report, num_sms) -> None:
+    """abft_gemm after argument validation (callers that have checked the
+    operands themselves call this directly)."""
+    dev = a.device
+    inj = _Inject(inject, dev) if inject else None
     args = N.GemmArgs()
     args.A, args.B, args.C, args.bias = _ptr(a), _ptr(weight), _ptr(out), _ptr(bias)
     args.M, args.N, args.K = m, n, k
@@ -234,16 +268,8 @@ def abft_gemm(
     if inj is not None:
         args.inject_rows, args.inject_cols, args.inject_deltas = _ptr(inj.rows), _ptr(inj.cols), _ptr(inj.deltas)
         args.n_inject = inj.n
-    L = N.lib()
-    with torch.cuda.device(dev):
-        ws_bytes = int(L.abft_gemm_workspace_bytes(ctypes.byref(args)))
-        if ws_bytes:
-            ws = _workspace(dev, ws_bytes)
-            args.workspace = ws.data_ptr()
-            args.workspace_bytes = ws.numel()
-        rc = L.abft_gemm_bf16(ctypes.byref(args), _stream(dev))
-    N.check("abft_gemm_bf16", rc)
-    return out, report
+    _run_gemm(args, dev, (m, n, k, int(mode), int(tile_n), int(tile_m), int(swap_ab), checksums is None,
+                          int(num_sms), 1, 0))
 
 
 def _mat_layout(t: torch.Tensor) -> Optional[Tuple[int, int]]:
@@ -369,15 +395,8 @@ def _bmm_call(a, bmat, b_kn, bias, out, bsz, m, n, k, mode, tile_n, tile_m, swap
     if inj is not None:
         args.inject_rows, args.inject_cols, args.inject_deltas = _ptr(inj.rows), _ptr(inj.cols), _ptr(inj.deltas)
         args.n_inject = inj.n
-    L = N.lib()
-    with torch.cuda.device(dev):
-        ws_bytes = int(L.abft_gemm_workspace_bytes(ctypes.byref(args)))
-        if ws_bytes:
-            ws = _workspace(dev, ws_bytes)
-            args.workspace = ws.data_ptr()
-            args.workspace_bytes = ws.numel()
-        rc = L.abft_gemm_bf16(ctypes.byref(args), _stream(dev))
-    N.check("abft_gemm_bf16", rc)
+    _run_gemm(args, dev, (m, n, k, int(mode), int(tile_n), int(tile_m), int(swap_ab), True, int(num_sms), bsz,
+                          b_kn))
     return out, (report if mode != N.MODE_OFF else None)
 
 
