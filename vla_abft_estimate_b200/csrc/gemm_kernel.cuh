@@ -660,48 +660,78 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (kb1 != p.num_kb) {
         // Stream-K finisher (this unit owns the tile's first k-blocks): fold
         // in the partials of the units that own its later k-blocks (units
-        // unit+1, +2, ..., umax; in a pair, their CTAs of the same rank), in
-        // that order, writing the sums back to TMEM chunk by chunk.
-        // Each contributor is folded as soon as its flag holds this launch's
-        // nonce (units in increasing order: a fixed summation order).
+        // unit+1, ..., ulast; in a pair, their CTAs of the same rank). Every
+        // element gets acc + p[unit+1] + p[unit+2] + ... in that order (a
+        // fixed summation order). Once every contributor's flag holds this
+        // launch's nonce, the fold runs chunk by chunk with the loads of two
+        // contributors in flight at a time, one TMEM read and write per chunk.
         const int64_t tile_end = static_cast<int64_t>(tile - p.dp_tiles + 1) * p.num_kb;
+        int ulast = unit;
+        while (ulast + 1 < p.sk_ctas && SegmentIter::sk_begin(p, ulast + 1) < tile_end) ++ulast;
+        // this warp's rows and column half; with checks also the warp of
+        // the same rows that stored the checksum columns (the other half
+        // when chk_col lies there: 248 of a full tile, anywhere in a tail)
+        const int chk_ep = (ep & 3) + (chk_col >= NV ? 4 : 0);
         bool okp = true;
 #pragma unroll 1
-        for (int u = unit + 1; u < p.sk_ctas; ++u) {
-          if (SegmentIter::sk_begin(p, u) >= tile_end) break;
+        for (int u = unit + 1; u <= ulast; ++u) {
           const int cc = u * G + static_cast<int>(rank);
-          // this warp's rows and column half; with checks also the warp of
-          // the same rows that stored the checksum columns (the other half
-          // when chk_col lies there: 248 of a full tile, anywhere in a tail)
-          const int chk_ep = (ep & 3) + (chk_col >= NV ? 4 : 0);
           if (!wait_flag(&p.flags[cc * 8 + ep], p.nonce, abort_flag) ||
               (CHECK && chk_ep != ep && !wait_flag(&p.flags[cc * 8 + chk_ep], p.nonce, abort_flag))) {
             okp = false;
             break;
           }
-          const float4* src = reinterpret_cast<const float4*>(p.partials) + static_cast<size_t>(cc) * (BN / 4) * kBM + r;
+        }
+        if (!__all_sync(0xFFFFFFFFu, okp)) break;
+        const float4* part = reinterpret_cast<const float4*>(p.partials) + r;
+        constexpr size_t kPartF4 = static_cast<size_t>(BN / 4) * kBM;  // float4 of one CTA's partial
 #pragma unroll 1
-          for (int c = 0; c < NCH; ++c) {
-            if (h * NV + c * 32 >= acc_w) break;  // warp-uniform: nothing stored from here on
-            float4 q4[8];
+        for (int c = 0; c < NCH; ++c) {
+          if (h * NV + c * 32 >= acc_w) break;  // warp-uniform: nothing stored from here on
+          uint32_t v[32];
+          __syncwarp();
+          tmem_ld_32x32b_x32(tcol + c * 32, v);
+          tmem_ld_wait();
+          const size_t coff = static_cast<size_t>(h * NV / 4 + c * 8) * kBM;
+          int u = unit + 1;
+#pragma unroll 1
+          for (; u < ulast; u += 2) {
+            const float4* sa = part + static_cast<size_t>(u * G + static_cast<int>(rank)) * kPartF4 + coff;
+            const float4* sb = part + static_cast<size_t>((u + 1) * G + static_cast<int>(rank)) * kPartF4 + coff;
+            float4 qa[8], qb[8];
 #pragma unroll
-            for (int g = 0; g < 8; ++g) q4[g] = __ldcg(src + (h * NV / 4 + c * 8 + g) * kBM);
-            uint32_t v[32];
-            __syncwarp();
-            tmem_ld_32x32b_x32(tcol + c * 32, v);
-            tmem_ld_wait();
+            for (int g = 0; g < 8; ++g) qa[g] = __ldcg(sa + g * kBM);
+#pragma unroll
+            for (int g = 0; g < 8; ++g) qb[g] = __ldcg(sb + g * kBM);
 #pragma unroll
             for (int g = 0; g < 8; ++g) {
-              v[4 * g] = __float_as_uint(__uint_as_float(v[4 * g]) + q4[g].x);
-              v[4 * g + 1] = __float_as_uint(__uint_as_float(v[4 * g + 1]) + q4[g].y);
-              v[4 * g + 2] = __float_as_uint(__uint_as_float(v[4 * g + 2]) + q4[g].z);
-              v[4 * g + 3] = __float_as_uint(__uint_as_float(v[4 * g + 3]) + q4[g].w);
+              v[4 * g] = __float_as_uint((__uint_as_float(v[4 * g]) + qa[g].x) + qb[g].x);
+              v[4 * g + 1] = __float_as_uint((__uint_as_float(v[4 * g + 1]) + qa[g].y) + qb[g].y);
+              v[4 * g + 2] = __float_as_uint((__uint_as_float(v[4 * g + 2]) + qa[g].z) + qb[g].z);
+              v[4 * g + 3] = __float_as_uint((__uint_as_float(v[4 * g + 3]) + qa[g].w) + qb[g].w);
             }
-            __syncwarp();
-            tmem_st_32x32b_x32(tcol + c * 32, v);
           }
-          tmem_st_wait();
-          if (CHECK) {
+          if (u == ulast) {
+            const float4* sa = part + static_cast<size_t>(u * G + static_cast<int>(rank)) * kPartF4 + coff;
+            float4 qa[8];
+#pragma unroll
+            for (int g = 0; g < 8; ++g) qa[g] = __ldcg(sa + g * kBM);
+#pragma unroll
+            for (int g = 0; g < 8; ++g) {
+              v[4 * g] = __float_as_uint(__uint_as_float(v[4 * g]) + qa[g].x);
+              v[4 * g + 1] = __float_as_uint(__uint_as_float(v[4 * g + 1]) + qa[g].y);
+              v[4 * g + 2] = __float_as_uint(__uint_as_float(v[4 * g + 2]) + qa[g].z);
+              v[4 * g + 3] = __float_as_uint(__uint_as_float(v[4 * g + 3]) + qa[g].w);
+            }
+          }
+          __syncwarp();
+          tmem_st_32x32b_x32(tcol + c * 32, v);
+        }
+        tmem_st_wait();
+        if (CHECK) {
+#pragma unroll 1
+          for (int u = unit + 1; u <= ulast; ++u) {
+            const float4* src = part + static_cast<size_t>(u * G + static_cast<int>(rank)) * kPartF4;
             const float4 c0 = __ldcg(src + (chk_col / 4) * kBM);
             const float4 c1 = __ldcg(src + (chk_col / 4 + 1) * kBM);
             const float add[kChkRows] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
@@ -709,7 +739,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int e = 0; e < kChkRows; ++e) chk[e] = __float_as_uint(__uint_as_float(chk[e]) + add[e]);
           }
         }
-        if (!__all_sync(0xFFFFFFFFu, okp)) break;
       }
 
       const int row0 = mt * Cfg::kTileM + static_cast<int>(rank) * kBM;  // first row of this CTA's slab
