@@ -220,6 +220,16 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
+FastDiv make_fast_div(int64_t d) {
+  if (d < 1) d = 1;  // a divisor the kernel never uses (no tiles of that kind)
+  int l = 0;
+  while ((int64_t{1} << l) < d) ++l;
+  FastDiv f;
+  f.m = static_cast<uint64_t>((static_cast<unsigned __int128>(1) << (32 + l)) / static_cast<uint64_t>(d)) + 1;
+  f.s = 32 + l;
+  return f;
+}
+
 // A value unique to one fused launch: stream-K flags and report->launch_tag
 // carry it, so neither needs clearing before the launch (a stale value from
 // another launch differs). Distinct for 2^64 calls in a process (an odd
@@ -529,14 +539,14 @@ int make_plan_uncached(const abft_gemm_args* a, int dev, int sms, Plan* pl) {
     off = align256(off + 4 * colsum_partial_floats(a->N, a->K, sms, false));
     pl->vf_off = off;
     off = align256(off + 4 * static_cast<size_t>(a->K));
-    pl->parts_off = off;  // 8 partial sums per 128-row slab of a tile
-    off = align256(off + 4 * 8 * static_cast<size_t>(pl->tiles) * (pl->pair ? 2 : 1));
+    pl->parts_off = off;  // a partial sum per epilogue warp and 128-row slab of a tile
+    off = align256(off + 4 * kEpiWarps * static_cast<size_t>(pl->tiles) * (pl->pair ? 2 : 1));
   }
   if (pl->sch.sk) {
     pl->sk_part_off = off;
     off = align256(off + static_cast<size_t>(pl->grid) * kBM * pl->bn * sizeof(float));
     pl->sk_flag_off = off;
-    off = align256(off + static_cast<size_t>(pl->grid) * 8 * sizeof(unsigned long long));  // a flag per epilogue warp
+    off = align256(off + static_cast<size_t>(pl->grid) * kEpiWarps * sizeof(unsigned long long));  // a flag per epilogue warp
   }
   pl->total = off;
   return ABFT_OK;
@@ -844,6 +854,11 @@ int abft_gemm_bf16(const abft_gemm_args* args, void* stream) {
   // Tile order: full tiles first, then the tail column's (one per tile row).
   p.tiles_n_full = p.tiles_n - (p.tail_n ? 1 : 0);
   p.full_tiles = p.tiles_m * p.tiles_n_full;
+  p.fd_tiles_m = make_fast_div(p.tiles_m);
+  p.fd_full = make_fast_div(p.full_tiles);
+  p.fd_group = make_fast_div(static_cast<int64_t>(p.group_m) * p.tiles_n_full);
+  p.fd_gm = make_fast_div(p.group_m);
+  p.fd_gm_last = make_fast_div(p.tiles_m - (cdiv(p.tiles_m, p.group_m) - 1) * p.group_m);
 
   const Schedule& sch = ws.sch;
   const int grid = ws.grid;
@@ -898,7 +913,7 @@ int abft_gemm_bf16(const abft_gemm_args* args, void* stream) {
     // corner + (rows of C) * sum(bias): the bias runs along the kernel's
     // rows when the operands are swapped
     ref_finalize_kernel<<<1, 1024, 0, s>>>(u, vf, p.K, p.bias, swap ? p.M : p.N, swap ? p.N : p.M, p.tile_sumc,
-                                           p.num_tiles * 8 * (ws.pair ? 2 : 1), a->tol_abs,
+                                           p.num_tiles * kEpiWarps * (ws.pair ? 2 : 1), a->tol_abs,
                                            a->tol_rel, (a->mode & ABFT_MODE_REF_BF16) ? 1 : 0, p.report, p.capacity,
                                            ws.tile_m, bd);
     rc = launch_status();

@@ -19,11 +19,12 @@
 //               same instruction that forms the output (no second pass over
 //               the A tile). Two BN-column accumulators: the epilogue of tile
 //               t overlaps the main loop of tile t+1.
-//   warps 2-9   epilogue: warp w owns TMEM lane quadrant (w % 4), i.e. 32
-//               output rows, and column half (w - 2) / 4 of the tile. Each
-//               thread copies its BN/2 accumulator columns to registers and
-//               releases the accumulator, then reduces, checks, corrects,
-//               adds bias, rounds to bf16 and stores.
+//   warps 2-13  epilogue: warp w owns TMEM lane quadrant (w % 4), i.e. 32
+//               output rows, and every third 32-column chunk of the tile
+//               (from chunk (w - 2) / 4). Each thread streams its chunks from
+//               TMEM once: row checksums, bias, bf16 rounding and the store;
+//               the three partial checksums of a row are then combined, the
+//               row checked and a located fault corrected.
 //
 // Checksum algebra (extends the scalar corner check of
 // pytorch/abft/checkers.py:112-126, dot(sum_rows(A), sum_cols(B)) vs sum(C),
@@ -52,9 +53,13 @@ namespace abft {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kThreads = 320;
-constexpr int kEpiWarp0 = 2;
-constexpr int kEpiThreads = 256;
+constexpr int kEpiWarp0 = 2;  // warps 0 and 1: TMA producer, MMA issuer
+// Epilogue: kEpiSplit warps per TMEM lane quadrant, so three per scheduler;
+// warp (quadrant q, share t) owns the tile's 32-column chunks t, t + 3, ...
+constexpr int kEpiSplit = 3;
+constexpr int kEpiWarps = 4 * kEpiSplit;
+constexpr int kEpiThreads = 32 * kEpiWarps;
+constexpr int kThreads = 32 * (kEpiWarp0 + kEpiWarps);
 constexpr int kChkRows = 8;  // rows of the per-tile checksum block
 
 // PAIR: a 2-CTA cluster shares one 256 x BN output tile. Each CTA holds 128
@@ -73,15 +78,15 @@ struct GemmCfg {
   static constexpr int kTmemCols = 2 * BN;
   static constexpr int kOffA = 0;
   static constexpr int kOffB = kOffA + kStages * kABytes;
-  static constexpr int kOffX = kOffB + kStages * kBBytes;  // row-half partial exchange
-  static constexpr int kXBytes = 2 * 2 * kBM * 16;         // [tile parity][half][row] float4
+  static constexpr int kOffX = kOffB + kStages * kBBytes;  // row-partial exchange
+  static constexpr int kXBytes = kEpiSplit * kBM * 16;     // [share][row] float4, one tile at a time
   // Per epilogue warp, one 32-row x 32-column bf16 block of the output on
   // its way to global memory (rows transposed across lanes so that a warp
   // store covers 8 rows x 64 contiguous bytes).
   static constexpr int kStageBytes = 32 * 32 * 2;
   static constexpr int kOffStage = kOffX + (CHECK ? kXBytes : 0);
-  static constexpr int kOffBar = kOffStage + 8 * kStageBytes;
-  static constexpr int kNumBars = 2 * kStages + 2 * 3 + 1;  // full, empty, tfull, tempty, xbar, drain
+  static constexpr int kOffBar = kOffStage + kEpiWarps * kStageBytes;
+  static constexpr int kNumBars = 2 * kStages + 2 * 2 + 3;  // full, empty, tfull, tempty, xbar, xfree, drain
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffMisc + 64 + 1024;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
@@ -90,6 +95,17 @@ struct GemmCfg {
   static constexpr int kChkRow0 = PAIR ? kBD - kBRows : kBD;
   static_assert((kChkRow0 * 128) % 1024 == 0, "checksum rows must start on a swizzle atom");
 };
+
+// Division by a launch-constant d > 0 as a multiply and a shift, exact for
+// every numerator below 2^31: m = floor(2^(32+l) / d) + 1 with 2^l >= d, so
+// n * m / 2^(32+l) exceeds n / d by less than 1 / (2d) (Granlund-Montgomery).
+struct FastDiv {
+  uint64_t m;
+  int s;  // 32 + l
+};
+__host__ __device__ __forceinline__ int fast_div(int n, const FastDiv& d) {
+  return static_cast<int>((static_cast<uint64_t>(static_cast<uint32_t>(n)) * d.m) >> d.s);
+}
 
 struct GemmParams {
   __nv_bfloat16* C;
@@ -106,7 +122,7 @@ struct GemmParams {
   int n_inj;
   abft_report* report;
   int capacity;
-  float* tile_sumc;  // ABFT_MODE_REF: [num_tiles][8] partial sums of the stored outputs
+  float* tile_sumc;  // ABFT_MODE_REF: [num_tiles][kEpiWarps] partial sums of the stored outputs
   // Tile order: the full tiles [0, full_tiles) in grouped raster order over
   // tiles_n_full columns, then the tail column's tiles (one per tile row).
   int full_tiles, tiles_n_full;
@@ -119,7 +135,7 @@ struct GemmParams {
   int sk_ctas;  // stream-K units: CTAs, or CTA pairs
   int64_t sk_iters;
   float* partials;  // [G][BN/4][128][4] fp32: a CTA's share of a tile it does not finish
-  unsigned long long* flags;  // [G][8]: per epilogue warp, set to `nonce` once its share of the partial is visible
+  unsigned long long* flags;  // [G][kEpiWarps]: per epilogue warp, set to `nonce` once its share of the partial is visible
   uint64_t nonce;   // unique to this launch: stream-K flags and report->launch_tag carry it
   // Last tile column when it holds fewer than BD data columns (tail_n != 0):
   // its B-operand tile is compact (data rows, then with checks the 8
@@ -142,6 +158,10 @@ struct GemmParams {
   int batch;
   int c_rows;
   uint32_t* bcounts;
+  // Divisors of tile_coords (every warp maps every tile it meets): tile
+  // rows, full tiles per batch, tiles per raster group, and the height of
+  // a raster group (the last group may be shorter).
+  FastDiv fd_tiles_m, fd_full, fd_group, fd_gm, fd_gm_last;
 };
 
 // Walks the (tile, k-block range) segments one CTA owns. Data-parallel:
@@ -238,20 +258,21 @@ __device__ __forceinline__ void tile_coords(int tile, const GemmParams& p, int& 
   const int all_full = p.batch * p.full_tiles;
   if (tile >= all_full) {
     const int t = tile - all_full;
-    b = t / p.tiles_m;
+    b = fast_div(t, p.fd_tiles_m);
     mt = t - b * p.tiles_m;
     nt = p.tiles_n - 1;
     return;
   }
-  b = tile / p.full_tiles;
+  b = fast_div(tile, p.fd_full);
   tile -= b * p.full_tiles;
   const int group = p.group_m * p.tiles_n_full;
-  const int g = tile / group;
+  const int g = fast_div(tile, p.fd_group);
   const int first_m = g * p.group_m;
-  const int gm = min(p.tiles_m - first_m, p.group_m);
+  const bool last = first_m + p.group_m > p.tiles_m;  // the last raster group may be shorter
+  const int gm = last ? p.tiles_m - first_m : p.group_m;
   const int w = tile - g * group;
-  mt = first_m + w % gm;
-  nt = w / gm;
+  nt = fast_div(w, last ? p.fd_gm_last : p.fd_gm);
+  mt = first_m + (w - nt * gm);
 }
 
 // Bounded wait that ignores the abort flag (used only while unwinding).
@@ -356,7 +377,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int S = Cfg::kStages;
   constexpr int BD = Cfg::kBD;
   constexpr int G = PAIR ? 2 : 1;
-  constexpr int NV = BN / 2;  // accumulator columns per epilogue thread
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
@@ -365,8 +385,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = bars + S;
   uint64_t* tfull = bars + 2 * S;  // [2]
   uint64_t* tempty = tfull + 2;    // [2]
-  uint64_t* xbar = tempty + 2;     // [2] row-half partials exchanged
-  uint64_t* drain = xbar + 2;
+  uint64_t* xbar = tempty + 2;     // row partials written
+  uint64_t* xfree = xbar + 1;      // row partials read (the buffer may be rewritten)
+  uint64_t* drain = xfree + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::kOffMisc + 4);
 
@@ -384,9 +405,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
       // Pairs: one arrival per epilogue warp of either CTA, on the even CTA's barrier.
-      mbar_init(&tempty[b], PAIR ? 2 * (kEpiThreads / 32) : kEpiThreads);
-      mbar_init(&xbar[b], kEpiThreads);
+      mbar_init(&tempty[b], PAIR ? 2 * kEpiWarps : kEpiThreads);
     }
+    mbar_init(xbar, kEpiThreads);
+    mbar_init(xfree, kEpiThreads);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -559,16 +581,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
-    // Each thread owns one output row (TMEM lane) and one column half of the
-    // tile and streams it from TMEM in 32-column chunks: with checks, pass 1
-    // reduces the row's checksums and pass 2 writes the corrected output;
-    // the accumulator is released after pass 2 (the MMA meanwhile fills the
-    // other buffer).
-    const int q = warp & 3;                 // TMEM lane quadrant this warp may access
-    const int h = (warp - kEpiWarp0) >> 2;  // column half of the tile
-    const int r = q * 32 + lane;            // row within the tile
-    const int ep = warp - kEpiWarp0;        // 0..7
-    constexpr int NCH = NV / 32;            // 32-column chunks per thread
+    // Each thread owns one output row (TMEM lane) and every kEpiSplit-th
+    // 32-column chunk of the tile, and streams them from TMEM once; the
+    // accumulator is released after the row checks (the MMA meanwhile fills
+    // the other buffer).
+    const int q = warp & 3;              // TMEM lane quadrant this warp may access
+    const int ep = warp - kEpiWarp0;     // 0 .. kEpiWarps - 1
+    const int t = ep >> 2;               // column share: chunks t, t + kEpiSplit, ...
+    const int r = q * 32 + lane;         // row within the tile
+    constexpr int NCT = BN / 32;         // 32-column chunks per tile
     float4* xchg = reinterpret_cast<float4*>(smem + Cfg::kOffX);
     // This warp's staging block: 32 rows of 64 bytes, the four 16-byte
     // pieces of row y permuted by XOR with (y >> 1) & 3 so that both the
@@ -579,7 +600,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int rd_piece = lane & 3;
     int acc = 0;
     uint32_t acc_phase = 0;
-    int xuse = 0;  // uses of the row-half exchange buffers
+    int xuse = 0;  // uses of the row-partial exchange buffer
     // This warp's staging block is the source of a bulk store that may not
     // have read it yet (lane 0 issued it; warp-uniform).
     bool stg_busy = false;
@@ -606,7 +627,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!__all_sync(0xFFFFFFFFu, mbar_wait(&tfull[acc], acc_phase, abort_flag))) break;
       tc_fence_after();
       const uint32_t tacc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      const uint32_t tcol = tacc + static_cast<uint32_t>(h * NV);  // this thread's first column
       // Accumulator columns the MMA wrote: BN, or the compact tail tile's
       // width; stream-K partials carry only those.
       const int acc_w = (p.tail_n != 0 && nt == p.tiles_n - 1) ? p.tail_n : BN;
@@ -620,13 +640,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         // this CTA waits for anything: the wait chain is one link long.
         // Layout [cta][column group of 4][row][4]: a warp's float4 store
         // covers 32 consecutive rows, 512 contiguous bytes.
-        float4* dst = reinterpret_cast<float4*>(p.partials) + (static_cast<size_t>(blockIdx.x) * (BN / 4) + h * NV / 4) * kBM + r;
+        float4* dst = reinterpret_cast<float4*>(p.partials) + static_cast<size_t>(blockIdx.x) * (BN / 4) * kBM + r;
 #pragma unroll 1
-        for (int c = 0; c < NCH; ++c) {
-          if (h * NV + c * 32 >= acc_w) break;  // warp-uniform
+        for (int c = t; c < NCT; c += kEpiSplit) {
+          if (c * 32 >= acc_w) break;  // warp-uniform
           uint32_t v[32];
           __syncwarp();
-          tmem_ld_32x32b_x32(tcol + c * 32, v);
+          tmem_ld_32x32b_x32(tacc + c * 32, v);
           tmem_ld_wait();
 #pragma unroll
           for (int g = 0; g < 8; ++g)
@@ -638,13 +658,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           acc = 0;
           acc_phase ^= 1u;
         }
-        // Each warp publishes its own share (32 rows x one column half):
+        // Each warp publishes its own share (32 rows x its chunks):
         // every lane makes its stores visible device-wide, then lane 0
         // releases the warp's flag. A finisher warp waits only for the
         // warps whose rows and columns it reads; no CTA-wide hand-off.
         __threadfence();
         __syncwarp();
-        if (lane == 0) st_release_u64(&p.flags[blockIdx.x * 8 + ep], p.nonce);
+        if (lane == 0) st_release_u64(&p.flags[blockIdx.x * kEpiWarps + ep], p.nonce);
         continue;
       }
 
@@ -668,16 +688,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int64_t tile_end = static_cast<int64_t>(tile - p.dp_tiles + 1) * p.num_kb;
         int ulast = unit;
         while (ulast + 1 < p.sk_ctas && SegmentIter::sk_begin(p, ulast + 1) < tile_end) ++ulast;
-        // this warp's rows and column half; with checks also the warp of
-        // the same rows that stored the checksum columns (the other half
-        // when chk_col lies there: 248 of a full tile, anywhere in a tail)
-        const int chk_ep = (ep & 3) + (chk_col >= NV ? 4 : 0);
+        // this warp's rows and chunks; with checks also the warp of the same
+        // rows that stored the chunk holding the checksum columns
+        const int chk_ep = (ep & 3) + 4 * ((chk_col >> 5) % kEpiSplit);
         bool okp = true;
 #pragma unroll 1
         for (int u = unit + 1; u <= ulast; ++u) {
           const int cc = u * G + static_cast<int>(rank);
-          if (!wait_flag(&p.flags[cc * 8 + ep], p.nonce, abort_flag) ||
-              (CHECK && chk_ep != ep && !wait_flag(&p.flags[cc * 8 + chk_ep], p.nonce, abort_flag))) {
+          if (!wait_flag(&p.flags[cc * kEpiWarps + ep], p.nonce, abort_flag) ||
+              (CHECK && chk_ep != ep && !wait_flag(&p.flags[cc * kEpiWarps + chk_ep], p.nonce, abort_flag))) {
             okp = false;
             break;
           }
@@ -686,13 +705,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float4* part = reinterpret_cast<const float4*>(p.partials) + r;
         constexpr size_t kPartF4 = static_cast<size_t>(BN / 4) * kBM;  // float4 of one CTA's partial
 #pragma unroll 1
-        for (int c = 0; c < NCH; ++c) {
-          if (h * NV + c * 32 >= acc_w) break;  // warp-uniform: nothing stored from here on
+        for (int c = t; c < NCT; c += kEpiSplit) {
+          if (c * 32 >= acc_w) break;  // warp-uniform: nothing stored from here on
           uint32_t v[32];
           __syncwarp();
-          tmem_ld_32x32b_x32(tcol + c * 32, v);
+          tmem_ld_32x32b_x32(tacc + c * 32, v);
           tmem_ld_wait();
-          const size_t coff = static_cast<size_t>(h * NV / 4 + c * 8) * kBM;
+          const size_t coff = static_cast<size_t>(c * 8) * kBM;
           int u = unit + 1;
 #pragma unroll 1
           for (; u < ulast; u += 2) {
@@ -725,7 +744,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           __syncwarp();
-          tmem_st_32x32b_x32(tcol + c * 32, v);
+          tmem_st_32x32b_x32(tacc + c * 32, v);
         }
         tmem_st_wait();
         if (CHECK) {
@@ -745,24 +764,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int grow = row0 + r;
       const int col0 = nt * BD;
       const int ncols = min(BD, p.N - col0);
-      const int hcol0 = h * NV;  // first local column of this thread
       const bool row_ok = grow < p.M;
 
-      // Debug faults added to the fp32 accumulator: does this row (and
-      // column half) hold any? The rare rows that do scan the list again
+      // Debug faults added to the fp32 accumulator: does this row (in this
+      // thread's chunks) hold any? The rare rows that do scan the list again
       // per chunk (inj_add) rather than keep it in registers. Batch offsets
       // of the flattened fault coordinates: C's rows are the kernel's rows,
       // or its columns with swapped operands.
       const int inj_row = p.swap ? grow : bz * p.M + grow;
-      const int inj_cbase = (p.swap ? bz * p.N : 0) + col0 + hcol0;  // list column of local column 0 of this half
+      const int inj_cbase = (p.swap ? bz * p.N : 0) + col0;  // list column of the tile's local column 0
       bool n_my = false;
       if (p.n_inj > 0 && row_ok) {
         for (int i = 0; i < p.n_inj; ++i) {
           const int ic = p.inj_cols[i] - inj_cbase;
-          n_my |= p.inj_rows[i] == inj_row && ic >= 0 && ic < NV && hcol0 + ic < ncols;
+          n_my |= p.inj_rows[i] == inj_row && ic >= 0 && ic < ncols && ((ic >> 5) % kEpiSplit) == t;
         }
       }
-      // Sum of the injected deltas at local column lc (of this half).
+      // Sum of the injected deltas at local column lc of the tile.
       auto inj_add = [&](int lc) {
         float d = 0.f;
         for (int i = 0; i < p.n_inj; ++i)
@@ -773,34 +791,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       // One pass over the accumulator in 32-column chunks: each chunk feeds
       // the row checksums (with checks on) and is rounded, staged and stored
       // at once (swapped operands: straight to C's transposed position).
-      // The first column half starts its sums from the negated expected
-      // checksums (split checksum columns added up), so the two halves'
-      // partials add up to the residuals.
+      // Share 0 starts its sums from the negated expected checksums (split
+      // checksum columns added up), so the shares' partials add up to the
+      // residuals.
       float s1 = 0.f, s2 = 0.f, s3 = 0.f, amax = 0.f;
-      if (CHECK && h == 0) {
+      if (CHECK && t == 0) {
         s1 = -((__uint_as_float(chk[0]) + __uint_as_float(chk[1])) + __uint_as_float(chk[2]));
         s2 = -((__uint_as_float(chk[3]) + __uint_as_float(chk[4])) + __uint_as_float(chk[5]));
         s3 = -(__uint_as_float(chk[6]) + __uint_as_float(chk[7]));
       }
       float row_out_sum = 0.f;
-      const uint4* bp = reinterpret_cast<const uint4*>(p.bias + col0 + hcol0);
+      const uint4* bp = reinterpret_cast<const uint4*>(p.bias + col0);
       const int rd_grow = row0 + q * 32 + rd_row;  // global row of this lane's first read-side row
       const float row_bias = (p.swap && p.bias != nullptr && row_ok) ? __bfloat162float(p.bias[grow]) : 0.f;
       const int crow0 = bz * p.c_rows;  // this batch's first row of C
 #pragma unroll 1
-      for (int c = 0; c < NCH; ++c) {
-        const int base = hcol0 + c * 32;  // first local column of the chunk (a multiple of 32)
-        if (base >= ncols) break;         // warp-uniform: nothing valid from here on
+      for (int c = t; c < NCT; c += kEpiSplit) {
+        const int base = c * 32;  // first local column of the chunk
+        if (base >= ncols) break;  // warp-uniform: nothing valid from here on
         uint32_t v[32];
         __syncwarp();
-        tmem_ld_32x32b_x32(tcol + c * 32, v);
+        tmem_ld_32x32b_x32(tacc + base, v);
         tmem_ld_wait();
         float x[32];
 #pragma unroll
         for (int e = 0; e < 32; ++e) x[e] = __uint_as_float(v[e]);
         if (n_my) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) x[e] += inj_add(c * 32 + e);
+          for (int e = 0; e < 32; ++e) x[e] += inj_add(base + e);
         }
         if constexpr (CHECK) {
           if (base + 32 <= ncols) {
@@ -912,25 +930,32 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       bool aborted = false;
       if constexpr (CHECK) {
-        // Exchange the half-row partials with the partner thread (other
-        // half); amax >= 0 and s3 rides in .w. The barrier (release/acquire)
-        // also orders every chunk store of both halves before a rewrite.
+        // Exchange the row partials of the kEpiSplit shares through shared
+        // memory; amax >= 0 and s3 rides in .w. One buffer: before writing
+        // it a thread waits until every thread has read the previous tile's
+        // partials (xfree). The xbar barrier (release/acquire) also orders
+        // every chunk store of the row before a rewrite.
         int fix_col = -1;  // local column to correct, if any
         float fix_delta = 0.f;
-        const int xb = xuse & 1;
-        const uint32_t xphase = (xuse >> 1) & 1u;
+        const uint32_t xph = static_cast<uint32_t>(xuse & 1);
+        if (xuse > 0 && !mbar_wait(xfree, xph ^ 1u, abort_flag)) aborted = true;
         ++xuse;
-        xchg[(xb * 2 + h) * kBM + r] = make_float4(s1, s2, amax, s3);
-        mbar_arrive(&xbar[xb]);
-        if (!mbar_wait(&xbar[xb], xphase, abort_flag)) {
-          aborted = true;
-        } else {
-          const float4 p0 = xchg[(xb * 2 + 0) * kBM + r];
-          const float4 p1 = xchg[(xb * 2 + 1) * kBM + r];
-          const float res1 = p0.x + p1.x;
-          const float res2 = p0.y + p1.y;
-          const float res3 = p0.w + p1.w;
-          const float tmax = fmaxf(p0.z, p1.z);
+        if (!aborted) {
+          xchg[t * kBM + r] = make_float4(s1, s2, amax, s3);
+          mbar_arrive(xbar);
+          if (!mbar_wait(xbar, xph, abort_flag)) aborted = true;
+        }
+        if (!aborted) {
+          float res1 = 0.f, res2 = 0.f, res3 = 0.f, tmax = 0.f;
+#pragma unroll
+          for (int j = 0; j < kEpiSplit; ++j) {
+            const float4 pj = xchg[j * kBM + r];
+            res1 += pj.x;
+            res2 += pj.y;
+            res3 += pj.w;
+            tmax = fmaxf(tmax, pj.z);
+          }
+          mbar_arrive(xfree);
           const float thr = fmaf(p.thr_k, tmax, p.thr_abs);
           const bool det = row_ok && (fabsf(res1) > thr || fabsf(res2) > thr * static_cast<float>(ncols));
           if (det) {
@@ -953,7 +978,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               fix_delta = res1;
               flags |= ABFT_REC_CORRECTED;
             }
-            if (h == 0 && report_ready(p, abort_flag)) {
+            if (t == 0 && report_ready(p, abort_flag)) {
               abft_report* rep = p.report;
               const uint32_t slot = atomicAdd(&rep->n_faults, 1u);
               if (flags & ABFT_REC_LOCATED) atomicAdd(&rep->n_located, 1u);
@@ -986,13 +1011,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-        // Correction: the owner of the located column (this half) reads the
-        // fp32 accumulator of that element again -- the chunk holding it,
-        // warp-collectively -- and stores accumulator - residual (+ bias)
-        // over the value stored above, in the same arithmetic order as the
-        // chunk pass (injected delta, correction, bias).
-        const int fix_local = fix_col - hcol0;
-        const bool mine = fix_col >= 0 && fix_local >= 0 && fix_local < NV;
+        // Correction: the owner of the located column's chunk reads the fp32
+        // accumulator of that element again -- the chunk, warp-collectively
+        // -- and stores accumulator - residual (+ bias) over the value stored
+        // above, in the same arithmetic order as the chunk pass (injected
+        // delta, correction, bias).
+        const int fix_chunk = fix_col >> 5;
+        const bool mine = fix_col >= 0 && (fix_chunk % kEpiSplit) == t;
         uint32_t need = __ballot_sync(0xFFFFFFFFu, mine);
         if (need != 0u && stg_busy) {
           // The element was written by this warp's bulk stores: let them
@@ -1005,18 +1030,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           stg_busy = false;
         }
         while (need != 0u) {
-          const int cfix = __shfl_sync(0xFFFFFFFFu, fix_local >> 5, __ffs(need) - 1);
+          const int cfix = __shfl_sync(0xFFFFFFFFu, fix_chunk, __ffs(need) - 1);
           uint32_t v[32];
           __syncwarp();
-          tmem_ld_32x32b_x32(tcol + cfix * 32, v);
+          tmem_ld_32x32b_x32(tacc + cfix * 32, v);
           tmem_ld_wait();
-          const bool here = mine && (fix_local >> 5) == cfix;
+          const bool here = mine && fix_chunk == cfix;
           if (here) {
-            const int e0 = fix_local & 31;
+            const int e0 = fix_col & 31;
             float val = 0.f;
 #pragma unroll
             for (int e = 0; e < 32; ++e) val = (e == e0) ? __uint_as_float(v[e]) : val;
-            if (n_my) val += inj_add(fix_local);
+            if (n_my) val += inj_add(fix_col);
             const float bcol = p.swap ? row_bias : (p.bias != nullptr ? __bfloat162float(p.bias[col0 + fix_col]) : 0.f);
             const __nv_bfloat16 o_old = __float2bfloat16_rn(val + bcol);
             const __nv_bfloat16 o_new = __float2bfloat16_rn((val - fix_delta) + bcol);
@@ -1039,7 +1064,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // warp order by the finishing kernel.
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) row_out_sum += __shfl_xor_sync(0xFFFFFFFFu, row_out_sum, o);
-        if (lane == 0) p.tile_sumc[(tile * G + static_cast<int>(rank)) * 8 + ep] = row_out_sum;
+        if (lane == 0) p.tile_sumc[(tile * G + static_cast<int>(rank)) * kEpiWarps + ep] = row_out_sum;
       }
       // Leave the tile loop together: the TMEM loads above are warp-collective.
       if (__any_sync(0xFFFFFFFFu, aborted)) break;
