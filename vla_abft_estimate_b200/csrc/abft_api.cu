@@ -220,16 +220,6 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-FastDiv make_fast_div(int64_t d) {
-  if (d < 1) d = 1;  // a divisor the kernel never uses (no tiles of that kind)
-  int l = 0;
-  while ((int64_t{1} << l) < d) ++l;
-  FastDiv f;
-  f.m = static_cast<uint64_t>((static_cast<unsigned __int128>(1) << (32 + l)) / static_cast<uint64_t>(d)) + 1;
-  f.s = 32 + l;
-  return f;
-}
-
 // A value unique to one fused launch: stream-K flags and report->launch_tag
 // carry it, so neither needs clearing before the launch (a stale value from
 // another launch differs). Distinct for 2^64 calls in a process (an odd

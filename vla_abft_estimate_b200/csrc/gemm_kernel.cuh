@@ -106,6 +106,15 @@ struct FastDiv {
 __host__ __device__ __forceinline__ int fast_div(int n, const FastDiv& d) {
   return static_cast<int>((static_cast<uint64_t>(static_cast<uint32_t>(n)) * d.m) >> d.s);
 }
+inline FastDiv make_fast_div(int64_t d) {
+  if (d < 1) d = 1;  // a divisor the kernel never uses (no tiles of that kind)
+  int l = 0;
+  while ((int64_t{1} << l) < d) ++l;
+  FastDiv f;
+  f.m = static_cast<uint64_t>((static_cast<unsigned __int128>(1) << (32 + l)) / static_cast<uint64_t>(d)) + 1;
+  f.s = 32 + l;
+  return f;
+}
 
 struct GemmParams {
   __nv_bfloat16* C;
