@@ -680,8 +680,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Accumulator column of the expected checksums: BD, or right after the
       // data rows of a compact tail tile (its data columns rounded up to 8).
       const int chk_col = (p.tail_n != 0 && nt == p.tiles_n - 1) ? ((p.N - nt * BD + 7) & ~7) : BD;
+      // The expected checksums seed share 0's sums; the other shares need
+      // neither them nor their stream-K partials.
       uint32_t chk[kChkRows];
-      if (CHECK) {
+      if (CHECK && t == 0) {
         __syncwarp();
         tmem_ld_32x32b_x8(tacc + static_cast<uint32_t>(chk_col), chk);
         tmem_ld_wait();
@@ -697,15 +699,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int64_t tile_end = static_cast<int64_t>(tile - p.dp_tiles + 1) * p.num_kb;
         int ulast = unit;
         while (ulast + 1 < p.sk_ctas && SegmentIter::sk_begin(p, ulast + 1) < tile_end) ++ulast;
-        // this warp's rows and chunks; with checks also the warp of the same
-        // rows that stored the chunk holding the checksum columns
+        // this warp's rows and chunks; for share 0 with checks also the warp
+        // of the same rows that stored the chunk holding the checksum columns
         const int chk_ep = (ep & 3) + 4 * ((chk_col >> 5) % kEpiSplit);
         bool okp = true;
 #pragma unroll 1
         for (int u = unit + 1; u <= ulast; ++u) {
           const int cc = u * G + static_cast<int>(rank);
           if (!wait_flag(&p.flags[cc * kEpiWarps + ep], p.nonce, abort_flag) ||
-              (CHECK && chk_ep != ep && !wait_flag(&p.flags[cc * kEpiWarps + chk_ep], p.nonce, abort_flag))) {
+              (CHECK && t == 0 && chk_ep != ep && !wait_flag(&p.flags[cc * kEpiWarps + chk_ep], p.nonce, abort_flag))) {
             okp = false;
             break;
           }
@@ -756,7 +758,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_st_32x32b_x32(tacc + c * 32, v);
         }
         tmem_st_wait();
-        if (CHECK) {
+        if (CHECK && t == 0) {
 #pragma unroll 1
           for (int u = unit + 1; u <= ulast; ++u) {
             const float4* src = part + static_cast<size_t>(u * G + static_cast<int>(rank)) * kPartF4;
