@@ -13,7 +13,7 @@ import math
 import statistics
 from collections import Counter, defaultdict
 from dataclasses import dataclass, field
-from typing import Any, Dict, List, Tuple
+from typing import Any, Dict, List, Optional, Tuple
 
 
 @dataclass
@@ -70,6 +70,17 @@ def _err_entry(phase: str, op_name: str, shape_key: str, result: CheckResult) ->
     }
 
 
+# The error entries are kept as tuples (phase, op, shape key, abs_err,
+# rel_err, corner, sum_c) and turned into the dicts above at export: a
+# deferred flush records every check of a forward pass at once.
+def _entry_dict(e: tuple) -> Dict[str, Any]:
+    return {"phase": e[0], "op_name": e[1], "shape_key": e[2], "abs_err": e[3], "rel_err": e[4],
+            "abft_corner": e[5], "sum_c": e[6]}
+
+
+_TOP_KEEP = 100  # the reference keeps the 100 largest |err| entries (stats.py:137-139)
+
+
 class AbftStatsCollector:
     """Per-phase / per-op / per-shape counters (stats.py:51-220)."""
 
@@ -91,10 +102,13 @@ class AbftStatsCollector:
         self.shape_failures: Counter = Counter()
         self.max_abs_err: float = 0.0
         self.max_rel_err: float = 0.0
-        self.max_abs_err_meta: Dict[str, Any] = {}
-        self.max_rel_err_meta: Dict[str, Any] = {}
-        self.top_abs_errs: List[Dict[str, Any]] = []
-        self.shape_max_abs_err: Dict[str, Dict[str, Any]] = {}
+        self._max_abs_meta: Optional[tuple] = None
+        self._max_rel_meta: Optional[tuple] = None
+        # Largest-|err| entries. The reference re-sorts and trims to 100 on
+        # every check; trimming only when the list reaches 200 keeps exactly
+        # the same 100 (a stable sort by -abs_err: ties keep insertion order).
+        self._top: List[tuple] = []
+        self._shape_max: Dict[str, tuple] = {}
 
         self.prefill_ms: List[float] = []
         self.decode_step_ms: List[float] = []
@@ -129,19 +143,21 @@ class AbftStatsCollector:
             if injected:
                 self.total_detected_injections += 1
                 self.phase_detected_injections[phase] += 1
-        self.max_abs_err = max(self.max_abs_err, result.abs_err)
-        self.max_rel_err = max(self.max_rel_err, result.rel_err)
-        if result.abs_err >= self.max_abs_err:
-            self.max_abs_err_meta = _err_entry(phase, op_name, shape_key, result)
-        if result.rel_err >= self.max_rel_err:
-            self.max_rel_err_meta = _err_entry(phase, op_name, shape_key, result)
-        self.top_abs_errs.append(_err_entry(phase, op_name, shape_key, result))
-        if len(self.top_abs_errs) > 100:
-            self.top_abs_errs = sorted(self.top_abs_errs, key=lambda x: -x["abs_err"])[:100]
+        abs_err, rel_err = result.abs_err, result.rel_err
+        entry = (phase, op_name, shape_key, abs_err, rel_err, result.abft_corner, result.sum_c)
+        self.max_abs_err = max(self.max_abs_err, abs_err)
+        self.max_rel_err = max(self.max_rel_err, rel_err)
+        if abs_err >= self.max_abs_err:
+            self._max_abs_meta = entry
+        if rel_err >= self.max_rel_err:
+            self._max_rel_meta = entry
+        self._top.append(entry)
+        if len(self._top) >= 2 * _TOP_KEEP:
+            self._trim_top()
         bucket = f"{phase}|{op_name}|{shape_key}"
-        prev = self.shape_max_abs_err.get(bucket)
-        if prev is None or result.abs_err > float(prev["abs_err"]):
-            self.shape_max_abs_err[bucket] = _err_entry(phase, op_name, shape_key, result)
+        prev = self._shape_max.get(bucket)
+        if prev is None or abs_err > float(prev[3]):
+            self._shape_max[bucket] = entry
 
         self.total_faults += result.n_faults
         self.total_located += result.n_located
@@ -151,6 +167,27 @@ class AbftStatsCollector:
             if len(self.located_coords) < 100:
                 self.located_coords.append({"phase": phase, "op_name": op_name, "shape_key": shape_key,
                                             "row": int(r), "col": int(c)})
+
+    def _trim_top(self) -> None:
+        self._top = sorted(self._top, key=lambda e: -e[3])[:_TOP_KEEP]
+
+    @property
+    def max_abs_err_meta(self) -> Dict[str, Any]:
+        return _entry_dict(self._max_abs_meta) if self._max_abs_meta is not None else {}
+
+    @property
+    def max_rel_err_meta(self) -> Dict[str, Any]:
+        return _entry_dict(self._max_rel_meta) if self._max_rel_meta is not None else {}
+
+    @property
+    def top_abs_errs(self) -> List[Dict[str, Any]]:
+        """The (at most 100) largest-|err| entries, largest first."""
+        self._trim_top()
+        return [_entry_dict(e) for e in self._top]
+
+    @property
+    def shape_max_abs_err(self) -> Dict[str, Dict[str, Any]]:
+        return {k: _entry_dict(e) for k, e in self._shape_max.items()}
 
     def record_injection(self) -> None:
         self.total_injections += 1
