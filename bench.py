@@ -57,6 +57,9 @@ def parse_args():
     ap.add_argument("--bmm-sweep", action="store_true",
                     help="batched products (torch.bmm, attention-shaped): cuBLAS vs the fused kernel vs the "
                          "reference's per-batch check loop")
+    ap.add_argument("--tile-grid", action="store_true",
+                    help="every allowed tile shape (128x128, 128x256, CTA pairs) per GEMM shape, checks off and on, "
+                         "against the library's own pick")
     ap.add_argument("--profile-bmm", default=None, metavar="SHAPE",
                     help="two rounds (checks off, then on) of one --bmm-sweep shape: an ncu capture target")
     ap.add_argument("--model", choices=["qwen2-7b", "cogact"], default=None,
@@ -578,6 +581,65 @@ BMM_SHAPES = [
     ("decode_pv_kv4096", 28, 1, 128, 4096, "rowmajor"),
     ("batched_2048_b8", 8, 2048, 2048, 2048, "rowmajor"),
 ]
+
+
+TILE_GRID_SHAPES = [
+    ("qwen7b_o", 512, 3584, 3584), ("qwen7b_qkv", 512, 4608, 3584), ("qwen7b_gate_up", 512, 37888, 3584),
+    ("qwen7b_down", 512, 3584, 18944), ("qwen7b_lm_head", 512, 152064, 3584), ("single_512x4096x4096", 512, 4096, 4096),
+    ("square_2048", 2048, 2048, 2048), ("square_4096", 4096, 4096, 4096), ("vit_l_mlp_up", 256, 4096, 1024),
+    ("vit_l_qkv", 256, 3072, 1024), ("llama7b_288_gate_up", 288, 22016, 4096), ("llama7b_288_down", 288, 4096, 11008),
+    ("m1024_4096", 1024, 4096, 4096), ("square_8192", 8192, 8192, 8192),
+]
+
+
+def tile_grid(args):
+    """Kernel time (L2 flushed, median) of every allowed tile shape per GEMM
+    shape, checks off and on, next to the tile shape the library picks."""
+    import torch
+
+    from vla_abft_estimate_b200 import _native as N
+    from vla_abft_estimate_b200 import ops
+
+    dev = torch.device("cuda", 0)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    iters = max(min(args.steps, 50), 5)
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        torch.cuda._sleep(100_000_000)
+        ev = []
+        for _ in range(iters):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            ev.append((e0, e1))
+        torch.cuda.synchronize()
+        return sorted(a.elapsed_time(b) for a, b in ev)[iters // 2] * 1e3
+
+    for name, m, n, k in TILE_GRID_SHAPES:
+        a = (torch.randn(m, k, device=dev) * k ** -0.5).bfloat16()
+        w = (torch.randn(n, k, device=dev) * k ** -0.5).bfloat16()
+        out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+        rep = ops.ReportBuffer(64, dev)
+        row = {"shape": name, "M": m, "N": n, "K": k}
+        for mode, tag in ((N.MODE_OFF, "off"), (N.MODE_DETECT | N.MODE_CORRECT, "checked")):
+            tn = ops.pick_tile_n(m, n, k, dev, mode)
+            tm = ops.pick_tile_m(m, n, k, tn, dev, mode)
+            us = {}
+            for ctn, ctm in ((128, 128), (256, 128), (256, 256)):
+                cks = ops.encode_weight(w, ctn) if mode else None
+                us[f"{ctm}x{ctn}"] = round(timed(lambda: ops.abft_gemm(
+                    a, w, mode=mode, out=out, tile_n=ctn, tile_m=ctm, swap_ab=1, checksums=cks,
+                    report=rep if mode else None)), 2)
+            best = min(us, key=us.get)
+            pick = f"{tm}x{tn}"  # tile rows x columns
+            row[tag] = {"us": us, "pick": pick, "best": best, "pick_loss_pct": round(100 * (us[pick] / us[best] - 1), 1)}
+        print(json.dumps(row), flush=True)
+        del a, w, out
 
 
 def profile_bmm(args):
@@ -1198,6 +1260,9 @@ def main():
         return
     if args.profile_bmm:
         profile_bmm(args)
+        return
+    if args.tile_grid:
+        tile_grid(args)
         return
     if args.profile_case:
         profile_case(args)
