@@ -295,7 +295,11 @@ int rowdot(const void* X, int64_t ld, int64_t R, int64_t C, const float* vec, fl
 // store: a contributor writes its partial tile and publishes the flag, and
 // the finisher sees it; fold: the finisher adds one partial into TMEM.
 // Measured in microseconds; one k-block step of a 256-wide tile takes about
-// kKbUs256 (half that for a 128-wide tile).
+// kKbUs256 (kKbFrac128 of that for a 128-wide tile). The constants rank the
+// candidate schedules; they do not predict absolute times (the epilogue of
+// the last wave and the launch are left out), and over the Qwen2-7B,
+// ViT/Llama and square shapes the pick measured within 3% of the best tile
+// shape (bench.py --tile-grid).
 constexpr double kSkStoreUs = 3.0;
 constexpr double kSkFoldUs = 1.0;
 constexpr double kKbUs256 = 0.33;
