@@ -213,3 +213,25 @@ def test_bmm_heads_interleaved_along_rows(cuda_device):
     assert (c.float() - ref).abs().max().item() <= OUT_TOL * ref.abs().max().item()
     r = rep.read()
     assert r.coords() == [(3 * s_len + 17, 200)] and r.batch_counts[3] == (1, 1, 1)
+
+
+@pytest.mark.parametrize("bsz,m,n,k", [(4, 256, 512, 256), (3, 16, 1000, 520), (5, 300, 136, 72)])
+def test_bmm_with_bias_faults_per_batch(cuda_device, bsz, m, n, k):
+    """A bias (one per output column, shared by the batch) is added after the
+    checks, in the normal and the swapped frame (m = 16: out^T per batch)."""
+    a, w = seeded(bsz, m, n, k, 31)
+    g = torch.Generator().manual_seed(32)
+    bias = (torch.randn(n, generator=g) * 0.02).bfloat16()
+    acc = np.einsum("bmk,bnk->bmn", f32(a).astype(np.float64), f32(w).astype(np.float64))
+    delta = float(256.0 * np.abs(acc).max())
+    faults = batch_faults(bsz, m, n, sorted({0, bsz - 1}), 90 + m)
+    inj = [(b * m + r, c, delta) for (b, r, c) in faults]
+    c, rep = ops.abft_bmm(a.to(cuda_device), w.transpose(1, 2).contiguous().to(cuda_device), bias.to(cuda_device),
+                          inject=inj)
+    r = rep.read()
+    swapped = m <= 64 and n >= 2 * m
+    want, counts, _ = oracle_batches(a, w, faults, delta, r.tile_n, swapped=swapped)
+    assert sorted((x.row, x.col, x.flags) for x in r.records) == want
+    assert r.batch_counts == counts
+    ref = acc + f32(bias)[None, None, :]
+    assert max_rel_err(f32(c), ref) <= OUT_TOL
