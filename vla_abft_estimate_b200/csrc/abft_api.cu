@@ -756,7 +756,12 @@ int abft_gemm_bf16(const abft_gemm_args* args, void* stream) {
   // are swapped (the copy is then the kernel's A and the checksums come
   // from the rows of A), also forms the checksum block.
   const bool enc_kn = fr.kn && check && !swap;
-  const bool enc_plain = check && a->checksums == nullptr && !enc_kn;
+  // Swapped operands with at most 64 tokens (one compact tail tile): the
+  // kernel's build warp forms the token checksum rows of every stage in
+  // shared memory; nothing is encoded or loaded for them. More tokens (a
+  // forced swap) keep the encode pre-pass.
+  const bool build = check && swap && !ws.pair && a->N <= 64 && a->N < bd && tail_width(a->N, bd, bn, check) != 0;
+  const bool enc_plain = check && a->checksums == nullptr && !enc_kn && !build;
   const void* V = check ? (a->checksums != nullptr ? a->checksums : wsb + ws.v_off) : nullptr;
 
   // B-operand boxes: the whole data width of a tile, or in a pair the even
@@ -771,8 +776,8 @@ int abft_gemm_bf16(const abft_gemm_args* args, void* stream) {
     rc = make_tmap_kmajor(&tmB2, a->B, a->K, a->N, a->ldb, bd - bn / 2, nb, a->stride_b);
     if (rc != ABFT_OK) return rc;
   }
-  CUtensorMap tmV = tmA;  // placeholder when checks are off
-  if (check) {
+  CUtensorMap tmV = tmA;  // placeholder when checks are off or built in the kernel
+  if (check && !build) {
     const int64_t vrows = cdiv(a->N, bd) * kChkRows;
     rc = make_tmap_kmajor(&tmV, V, a->K, vrows, a->K, kChkRows, nb, vrows * a->K);
     if (rc != ABFT_OK) return rc;
@@ -807,6 +812,7 @@ int abft_gemm_bf16(const abft_gemm_args* args, void* stream) {
   p.capacity = a->report_capacity;
   p.tile_sumc = (a->mode & ABFT_MODE_REF) ? reinterpret_cast<float*>(wsb + ws.parts_off) : nullptr;
   p.swap = swap ? 1 : 0;
+  p.build_chk = build ? 1 : 0;
   p.batch = static_cast<int>(nb);
   p.c_rows = nb > 1 ? static_cast<int>(a->stride_c / a->ldc) : 0;
   p.bcounts = (nb > 1 && a->report != nullptr)
@@ -840,7 +846,7 @@ int abft_gemm_bf16(const abft_gemm_args* args, void* stream) {
           if (rc != ABFT_OK) return rc;
         }
         p.tail_tx = (ws.pair ? 2 * a_bytes + (bn / 2) * row_bytes : a_bytes) +
-                    static_cast<uint32_t>(box + kChkRows) * row_bytes;
+                    static_cast<uint32_t>(box + (build ? 0 : kChkRows)) * row_bytes;
       }
     }
   }

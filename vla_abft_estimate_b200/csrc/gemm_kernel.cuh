@@ -19,6 +19,10 @@
 //               same instruction that forms the output (no second pass over
 //               the A tile). Two BN-column accumulators: the epilogue of tile
 //               t overlaps the main loop of tile t+1.
+//   warps 14-15 with swapped operands, checks on and at most 64 tokens: per
+//               k-block, the 8 token checksum rows of the B-operand tile,
+//               summed in shared memory from the token rows the TMA just
+//               loaded (no encode launch, no checksum copy).
 //   warps 2-13  epilogue: warp w owns TMEM lane quadrant (w % 4), i.e. 32
 //               output rows, and every third 32-column chunk of the tile
 //               (from chunk (w - 2) / 4). Each thread streams its chunks from
@@ -47,6 +51,7 @@
 #include <cuda_bf16.h>
 
 #include "../../include/abft_b200.h"
+#include "aux_kernels.cuh"
 #include "ptx.cuh"
 
 namespace abft {
@@ -59,7 +64,11 @@ constexpr int kEpiWarp0 = 2;  // warps 0 and 1: TMA producer, MMA issuer
 constexpr int kEpiSplit = 3;
 constexpr int kEpiWarps = 4 * kEpiSplit;
 constexpr int kEpiThreads = 32 * kEpiWarps;
-constexpr int kThreads = 32 * (kEpiWarp0 + kEpiWarps);
+// With swapped operands and checks on: the two warps that form each
+// stage's token checksum rows in shared memory (idle otherwise).
+constexpr int kBuildWarp = kEpiWarp0 + kEpiWarps;
+constexpr int kBuildWarps = 2;
+constexpr int kThreads = 32 * (kBuildWarp + kBuildWarps);
 constexpr int kChkRows = 8;  // rows of the per-tile checksum block
 
 // PAIR: a 2-CTA cluster shares one 256 x BN output tile. Each CTA holds 128
@@ -86,7 +95,7 @@ struct GemmCfg {
   static constexpr int kStageBytes = 32 * 32 * 2;
   static constexpr int kOffStage = kOffX + (CHECK ? kXBytes : 0);
   static constexpr int kOffBar = kOffStage + kEpiWarps * kStageBytes;
-  static constexpr int kNumBars = 2 * kStages + 2 * 2 + 3;  // full, empty, tfull, tempty, xbar, xfree, drain
+  static constexpr int kNumBars = 3 * kStages + 2 * 2 + 3;  // full, empty, ready, tfull, tempty, xbar, xfree, drain
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffMisc + 64 + 1024;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
@@ -157,6 +166,11 @@ struct GemmParams {
   // stored transposed (C[col * ldc + row]), the bias is indexed by the
   // kernel row, and fault records carry C's coordinates.
   int swap;
+  // Swapped operands with checks and one compact token tile: the token
+  // checksum rows of each stage are formed in shared memory by the build
+  // warp (nothing is loaded for them); the MMA waits for that (ready
+  // barriers) instead of for the copies alone.
+  int build_chk;
   // Batched launch: `batch` products, C[b] at row b * c_rows of C (a batch
   // stride that is a whole number of ldc rows keeps the address arithmetic
   // in one 32-bit row index). Tile order:
@@ -295,6 +309,79 @@ __device__ __forceinline__ void mbar_wait_unwind(uint64_t* bar, uint32_t parity)
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
+// Token checksum rows of one stage of the swapped B-operand tile, formed by
+// two warps, warp wb for k columns [32 wb, 32 wb + 32) of the 64-wide
+// k-block. sb: the stage's tile, 128-byte rows with the 128-byte swizzle
+// (row j's 16-byte chunk c at chunk c ^ (j & 7)); r0: the first checksum
+// row, a multiple of 8; NG * 8 token rows are read (rows past the tokens
+// hold zeros). Writes the warp's half of rows r0 .. r0+7 in
+// encode_weight_kernel's format: split3(v1), split3(v2), split2(v3) of
+//   v1[k] = sum_j x_j[k], v2[k] = sum_j (j+1) x_j[k], v3[k] = sum_j sg(j) x_j[k].
+// Lane (hs, cw, e) = (lane >> 4, (lane >> 2) & 3, lane & 3) reads the two
+// k values 8c + 2e, 8c + 2e + 1 (c = 4 wb + cw) of rows j = i + 4 hs,
+// i = 8g + r (r < 4) known at compile time. The two halves of the warp
+// read chunk groups c ^ r and c ^ r ^ 4, so every load hits 32 distinct
+// banks. As i and 4 hs have disjoint bits, sg(j) = sg(i) sg(4 hs) and
+// j + 1 = (i + 1) + 4 hs: a lane keeps P = sum over sg(i) = +1,
+// Q = sum over sg(i) = -1 (one packed add) and W = sum (i + 1) x_j, forms
+//   v1 = P + Q, v3 = sg(4 hs) (P - Q), v2 = W + 4 hs v1,
+// and one exchange with lane ^ 16 gives both halves the totals.
+template <int NG>
+__device__ __forceinline__ void build_token_checksums(uint8_t* sb, int r0, int lane, int wb) {
+  const int hs = lane >> 4;
+  const int c = 4 * wb + ((lane >> 2) & 3);
+  const int wofs = (lane & 3) * 4;
+  const uint8_t* base[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) base[r] = sb + hs * 512 + ((c ^ (r + 4 * hs)) << 4) + wofs;
+  float2 P = make_float2(0.f, 0.f), Q = make_float2(0.f, 0.f);
+  float Wa = 0.f, Wb = 0.f;
+#pragma unroll
+  for (int g = 0; g < NG; ++g) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int i = 8 * g + r;
+      const uint32_t w = *reinterpret_cast<const uint32_t*>(base[r] + i * 128);
+      const float2 x = make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+      if (__builtin_popcount(i) & 1)
+        Q = __fadd2_rn(Q, x);
+      else
+        P = __fadd2_rn(P, x);
+      Wa = fmaf(static_cast<float>(i + 1), x.x, Wa);
+      Wb = fmaf(static_cast<float>(i + 1), x.y, Wb);
+    }
+  }
+  const float sh = hs ? -1.f : 1.f, w4 = 4.f * static_cast<float>(hs);
+  float v1a = P.x + Q.x, v1b = P.y + Q.y;
+  float v3a = sh * (P.x - Q.x), v3b = sh * (P.y - Q.y);
+  float v2a = fmaf(w4, v1a, Wa), v2b = fmaf(w4, v1b, Wb);
+  v1a += __shfl_xor_sync(0xffffffffu, v1a, 16);
+  v1b += __shfl_xor_sync(0xffffffffu, v1b, 16);
+  v2a += __shfl_xor_sync(0xffffffffu, v2a, 16);
+  v2b += __shfl_xor_sync(0xffffffffu, v2b, 16);
+  v3a += __shfl_xor_sync(0xffffffffu, v3a, 16);
+  v3b += __shfl_xor_sync(0xffffffffu, v3b, 16);
+  // Half 0 writes rows 0-2 (v1) and 6-7 (v3), half 1 rows 3-5 (v2).
+  const float ua = hs ? v2a : v1a, ub = hs ? v2b : v1b;
+  const int q0 = 3 * hs;
+  __nv_bfloat16 ha[3], hb[3];
+  split3_bf16(ua, ha[0], ha[1], ha[2]);
+  split3_bf16(ub, hb[0], hb[1], hb[2]);
+#pragma unroll
+  for (int q = 0; q < 3; ++q)
+    *reinterpret_cast<uint32_t*>(sb + (r0 + q0 + q) * 128 + ((c ^ (q0 + q)) << 4) + wofs) =
+        static_cast<uint32_t>(__bfloat16_as_ushort(ha[q])) | (static_cast<uint32_t>(__bfloat16_as_ushort(hb[q])) << 16);
+  if (!hs) {
+    const __nv_bfloat16 a6 = __float2bfloat16_rn(v3a), b6 = __float2bfloat16_rn(v3b);
+    const __nv_bfloat16 a7 = __float2bfloat16_rn(v3a - __bfloat162float(a6));
+    const __nv_bfloat16 b7 = __float2bfloat16_rn(v3b - __bfloat162float(b6));
+    *reinterpret_cast<uint32_t*>(sb + (r0 + 6) * 128 + ((c ^ 6) << 4) + wofs) =
+        static_cast<uint32_t>(__bfloat16_as_ushort(a6)) | (static_cast<uint32_t>(__bfloat16_as_ushort(b6)) << 16);
+    *reinterpret_cast<uint32_t*>(sb + (r0 + 7) * 128 + ((c ^ 7) << 4) + wofs) =
+        static_cast<uint32_t>(__bfloat16_as_ushort(a7)) | (static_cast<uint32_t>(__bfloat16_as_ushort(b7)) << 16);
+  }
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
@@ -392,7 +479,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
-  uint64_t* tfull = bars + 2 * S;  // [2]
+  uint64_t* ready = bars + 2 * S;  // [S] stage complete for the MMA (build_chk)
+  uint64_t* tfull = bars + 3 * S;  // [2]
   uint64_t* tempty = tfull + 2;    // [2]
   uint64_t* xbar = tempty + 2;     // row partials written
   uint64_t* xfree = xbar + 1;      // row partials read (the buffer may be rewritten)
@@ -410,6 +498,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+      mbar_init(&ready[s], kBuildWarps);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
@@ -524,7 +613,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (CHECK) tma_load_3d(sb + BD * 128, &tmV, &full[stage], kx, nt * kChkRows, bz);
             } else {
               if (p.tail_box > 0) tma_load_3d(sb, &tmBt, &full[stage], kx, nt * BD, bz);
-              tma_load_3d(sb + p.tail_box * 128, &tmV, &full[stage], kx, nt * kChkRows, bz);
+              if (!p.build_chk) tma_load_3d(sb + p.tail_box * 128, &tmV, &full[stage], kx, nt * kChkRows, bz);
             }
           }
           issued_mask |= 1u << stage;
@@ -569,10 +658,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
+        uint64_t* avail = p.build_chk ? ready : full;
         if (!tail)
-          ok = mma_mainloop<BN, CHECK, PAIR, BN>(smem, full, empty, stage, phase, kb0, kb1, d, abort_flag);
+          ok = mma_mainloop<BN, CHECK, PAIR, BN>(smem, avail, empty, stage, phase, kb0, kb1, d, abort_flag);
         else
-          ok = mma_mainloop_n<BN, CHECK, PAIR>(p.tail_n, smem, full, empty, stage, phase, kb0, kb1, d, abort_flag);
+          ok = mma_mainloop_n<BN, CHECK, PAIR>(p.tail_n, smem, avail, empty, stage, phase, kb0, kb1, d, abort_flag);
         if (!ok) break;
         if constexpr (PAIR)
           umma_commit_pair_both(&tfull[acc], 0x3);
@@ -586,6 +676,50 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Every MMA this thread issued must finish before TMEM is released.
       umma_commit_g<G>(drain);
       mbar_wait_unwind(drain, 0);
+    }
+    __syncwarp();
+  } else if (warp >= kBuildWarp) {
+    // ------------------------------------------------------------ token checksums
+    // Swapped operands: the B-operand tile is the compact tile of the
+    // p.N (<= 64) token rows, tail_box = round8(p.N) rows (the copy fills
+    // the rows past p.N with zeros), then its 8 checksum rows. Per stage the
+    // two warps (one half of the 64-wide k-block each) sum the token rows in
+    // shared memory and write the checksum rows, which the MMA reads after
+    // both have arrived on the ready barrier.
+    if (CHECK && !PAIR && p.build_chk) {
+      const int wb = warp - kBuildWarp;
+      int stage = 0;
+      uint32_t phase = 0;
+      SegmentIter seg(p, unit, nunits);
+      int tile, kb0, kb1;
+      bool ok = true;
+      while (ok && seg.next(p, tile, kb0, kb1)) {
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sb = smem + Cfg::kOffB + stage * Cfg::kBBytes;
+          switch (p.tail_box >> 3) {
+            case 1: build_token_checksums<1>(sb, p.tail_box, lane, wb); break;
+            case 2: build_token_checksums<2>(sb, p.tail_box, lane, wb); break;
+            case 3: build_token_checksums<3>(sb, p.tail_box, lane, wb); break;
+            case 4: build_token_checksums<4>(sb, p.tail_box, lane, wb); break;
+            case 5: build_token_checksums<5>(sb, p.tail_box, lane, wb); break;
+            case 6: build_token_checksums<6>(sb, p.tail_box, lane, wb); break;
+            case 7: build_token_checksums<7>(sb, p.tail_box, lane, wb); break;
+            default: build_token_checksums<8>(sb, p.tail_box, lane, wb); break;
+          }
+          // the MMA reads the rows through the async proxy
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&ready[stage]);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
     }
     __syncwarp();
   } else {
