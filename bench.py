@@ -62,6 +62,9 @@ def parse_args():
                          "against the library's own pick")
     ap.add_argument("--profile-bmm", default=None, metavar="SHAPE",
                     help="two rounds (checks off, then on) of one --bmm-sweep shape: an ncu capture target")
+    ap.add_argument("--profile-shape", default=None, metavar="SHAPE",
+                    help="two rounds (checks off, then on) of one --sweep shape with the library's tile "
+                         "pick: an ncu capture target")
     ap.add_argument("--model", choices=["qwen2-7b", "cogact"], default=None,
                     help="qwen2-7b: prefill-512 tokens/s and decode of a random-init Qwen2-7B-shaped decoder; "
                          "cogact: one CogACT-style VLA forward (ViT-L + SigLIP + Llama-2-7B + DiT-B, 10 "
@@ -495,6 +498,9 @@ SWEEP_SHAPES = [
     # decode: few token rows, HBM-bound on the weight (operands swapped)
     ("decode_m1_qkv", 1, 4608, 3584), ("decode_m1_gate_up", 1, 37888, 3584), ("decode_m1_down", 1, 3584, 18944),
     ("decode_m32_gate_up", 32, 37888, 3584), ("decode_m32_down", 32, 3584, 18944),
+    ("decode_m1_o", 1, 3584, 3584),
+    # DiT-B action head of the VLA: 16 action tokens through its MLP
+    ("dit_m16_fc1", 16, 3072, 768), ("dit_m16_fc2", 16, 768, 3072),
 ]
 
 
@@ -640,6 +646,26 @@ def tile_grid(args):
             row[tag] = {"us": us, "pick": pick, "best": best, "pick_loss_pct": round(100 * (us[pick] / us[best] - 1), 1)}
         print(json.dumps(row), flush=True)
         del a, w, out
+
+
+def profile_shape(args):
+    """Two rounds of one --sweep GEMM shape, checks off then on: the ncu target."""
+    import torch
+
+    from vla_abft_estimate_b200 import _native as N
+    from vla_abft_estimate_b200 import ops
+
+    _, m, n, k = {s[0]: s for s in SWEEP_SHAPES}[args.profile_shape]
+    dev = torch.device("cuda", 0)
+    a = (torch.randn(m, k, device=dev) * k ** -0.5).bfloat16()
+    w = (torch.randn(n, k, device=dev) * k ** -0.5).bfloat16()
+    out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+    rep = ops.ReportBuffer(64, dev)
+    for _ in range(2):
+        ops.abft_gemm(a, w, mode=N.MODE_OFF, out=out)
+        ops.abft_gemm(a, w, mode=N.MODE_DETECT | N.MODE_CORRECT, out=out, report=rep)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_shape": args.profile_shape, "faults": rep.read().n_faults}))
 
 
 def profile_bmm(args):
@@ -1260,6 +1286,9 @@ def main():
         return
     if args.profile_bmm:
         profile_bmm(args)
+        return
+    if args.profile_shape:
+        profile_shape(args)
         return
     if args.tile_grid:
         tile_grid(args)
