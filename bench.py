@@ -58,7 +58,8 @@ def parse_args():
                     help="batched products (torch.bmm, attention-shaped): cuBLAS vs the fused kernel vs the "
                          "reference's per-batch check loop")
     ap.add_argument("--tile-grid", action="store_true",
-                    help="every allowed tile shape (128x128, 128x256, CTA pairs) per GEMM shape, checks off and on, "
+                    help="every allowed tile shape (128x128, 128x256, CTA pairs 256x128 and 256x256) per GEMM shape, "
+                         "checks off and on, "
                          "against the library's own pick")
     ap.add_argument("--profile-bmm", default=None, metavar="SHAPE",
                     help="two rounds (checks off, then on) of one --bmm-sweep shape: an ncu capture target")
@@ -636,7 +637,7 @@ def tile_grid(args):
             tn = ops.pick_tile_n(m, n, k, dev, mode)
             tm = ops.pick_tile_m(m, n, k, tn, dev, mode)
             us = {}
-            for ctn, ctm in ((128, 128), (256, 128), (256, 256)):
+            for ctn, ctm in ((128, 128), (256, 128), (128, 256), (256, 256)):
                 cks = ops.encode_weight(w, ctn) if mode else None
                 us[f"{ctm}x{ctn}"] = round(timed(lambda: ops.abft_gemm(
                     a, w, mode=mode, out=out, tile_n=ctn, tile_m=ctm, swap_ab=1, checksums=cks,

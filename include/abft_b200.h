@@ -141,8 +141,8 @@ typedef struct abft_gemm_args {
   int32_t report_capacity;
   int32_t num_sms;        /* 0 = all SMs of the current device                */
   int32_t tile_m;         /* 0 = choose; 128; or 256: each tile is shared by  */
-                          /* a 2-CTA cluster (one pair MMA, M = 256), which    */
-                          /* needs tile_n 256                                 */
+                          /* a 2-CTA cluster (one pair MMA, M = 256), with     */
+                          /* either tile_n                                    */
   int32_t swap_ab;        /* 0 = choose; 1 = never; 2 = always: compute C^T =  */
                           /* B A^T with the weight on the MMA's 128-row side   */
                           /* and the few rows of A as a narrow tile (chosen    */
@@ -190,7 +190,8 @@ int32_t abft_pick_tile_n(int64_t M, int64_t N, int64_t K, int32_t num_sms, uint3
 
 /* Tile height (128, or 256 = CTA pairs) the library picks when tile_m == 0,
  * for a given tile_n: the shorter estimated schedule, pairs over num_sms / 2
- * units at a per-SM speed-up of 1.1 (128 whenever tile_n != 256). */
+ * units at a per-SM speed-up of 1.1 (128 whenever tile_n != 256: pairs of
+ * 128-wide tiles run only on request). */
 int32_t abft_pick_tile_m(int64_t M, int64_t N, int64_t K, int32_t num_sms, uint32_t mode, int32_t tile_n);
 
 /* Bytes of the per-tile checksum block of a [N, K] weight for tile_n. */

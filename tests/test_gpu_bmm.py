@@ -146,10 +146,11 @@ def test_bmm_detect_only_keeps_faults(cuda_device):
 
 
 # ------------------------------------------------- pairs, stream-K, swapped
-def test_bmm_cta_pairs(cuda_device):
+@pytest.mark.parametrize("tile_n", [256, 128])
+def test_bmm_cta_pairs(cuda_device, tile_n):
     bsz, m, n, k = 3, 512, 1000, 512
     faults = batch_faults(bsz, m, n, [0, 1, 2], 91)
-    a, w, acc, delta, c, r = run(cuda_device, bsz, m, n, k, faults, tile_n=256, tile_m=256)
+    a, w, acc, delta, c, r = run(cuda_device, bsz, m, n, k, faults, tile_n=tile_n, tile_m=256)
     assert r.tile_m == 256
     want, counts, out = oracle_batches(a, w, faults, delta, r.tile_n, swapped=False)
     assert sorted((x.row, x.col, x.flags) for x in r.records) == want and r.batch_counts == counts

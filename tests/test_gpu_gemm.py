@@ -277,28 +277,33 @@ def test_no_device_timeouts_reported(cuda_device):
     assert not rep.read().device_timeout
 
 
-# ------------------------------------------------ 2-CTA pairs (256-row tiles)
+# ------------------------------------- 2-CTA pairs (256-row tiles, 256 or 128 wide)
+PAIR_WIDTHS = [256, 128]
+
+
+@pytest.mark.parametrize("tile_n", PAIR_WIDTHS)
 @pytest.mark.parametrize("m,n,k,bias", [
     (256, 256, 64, False), (200, 136, 72, True), (300, 1000, 520, True), (1024, 1024, 1024, False),
     (1, 8, 8, False), (2048, 2048, 4096, True),
 ])
 @pytest.mark.parametrize("mode", [N.MODE_OFF, N.MODE_DETECT | N.MODE_CORRECT])
-def test_pair_tiles_match_fp32(cuda_device, m, n, k, bias, mode):
+def test_pair_tiles_match_fp32(cuda_device, m, n, k, bias, mode, tile_n):
     a, w, b = seeded(m, n, k, 12, bias)
     ref = f32(a) @ f32(w).T + (f32(b) if b is not None else 0)
     c, rep = ops.abft_gemm(a.to(cuda_device), w.to(cuda_device), None if b is None else b.to(cuda_device),
-                           mode=mode, tile_n=256, tile_m=256)
+                           mode=mode, tile_n=tile_n, tile_m=256)
     assert max_rel_err(f32(c), ref) <= OUT_TOL
     if mode != N.MODE_OFF:
         r = rep.read()
-        assert r.status == 0 and r.n_faults == 0 and r.tile_m == 256 and r.tile_n == 248
+        assert r.status == 0 and r.n_faults == 0 and r.tile_m == 256 and r.tile_n == tile_n - 8
 
 
+@pytest.mark.parametrize("tile_n", PAIR_WIDTHS)
 @pytest.mark.parametrize("count", [1, 4])
 @pytest.mark.parametrize("m,n,k", [(256, 512, 256), (512, 4096, 1024), (1024, 1024, 1024), (300, 1000, 520)])
-def test_pair_faults_located_and_corrected_bit_exact(cuda_device, count, m, n, k):
+def test_pair_faults_located_and_corrected_bit_exact(cuda_device, count, m, n, k, tile_n):
     faults = O.seeded_fault_positions(m, n, count, 13 * count + m)
-    a, w, b, c, r, orc = run_checked(cuda_device, m, n, k, faults, tile_n=256, tile_m=256)
+    a, w, b, c, r, orc = run_checked(cuda_device, m, n, k, faults, tile_n=tile_n, tile_m=256)
     got = sorted((x.row, x.col, x.flags) for x in r.records)
     assert got == orc.records
     assert r.n_faults == r.n_located == r.n_corrected == count
@@ -313,13 +318,14 @@ def test_pair_faults_located_and_corrected_bit_exact(cuda_device, count, m, n, k
     (4096, 4096, 4096),
 ])
 @pytest.mark.parametrize("mode", [N.MODE_OFF, N.MODE_DETECT | N.MODE_CORRECT])
-def test_pair_stream_k_schedules(cuda_device, m, n, k, mode):
+@pytest.mark.parametrize("tile_n", PAIR_WIDTHS)
+def test_pair_stream_k_schedules(cuda_device, m, n, k, mode, tile_n):
     torch.manual_seed(m * 5 + n + k)
     a = (torch.randn(m, k, device=cuda_device) * k ** -0.5).bfloat16()
     w = (torch.randn(n, k, device=cuda_device) * k ** -0.5).bfloat16()
     ref = a.float() @ w.float().T
-    c1, r1 = ops.abft_gemm(a, w, mode=mode, tile_n=256, tile_m=256)
-    c2, _ = ops.abft_gemm(a, w, mode=mode, tile_n=256, tile_m=256)
+    c1, r1 = ops.abft_gemm(a, w, mode=mode, tile_n=tile_n, tile_m=256)
+    c2, _ = ops.abft_gemm(a, w, mode=mode, tile_n=tile_n, tile_m=256)
     assert torch.equal(c1, c2)
     assert (c1.float() - ref).abs().max().item() <= OUT_TOL * ref.abs().max().item()
     if mode == N.MODE_OFF:
@@ -328,33 +334,34 @@ def test_pair_stream_k_schedules(cuda_device, m, n, k, mode):
     assert r1.n_faults == 0 and not r1.device_timeout
     delta = 256.0 * ref.abs().max().item()
     faults = O.seeded_fault_positions(m, n, 4, m + k + 1)
-    c3, r3 = ops.abft_gemm(a, w, mode=mode, tile_n=256, tile_m=256, inject=[(i, j, delta) for i, j in faults])
+    c3, r3 = ops.abft_gemm(a, w, mode=mode, tile_n=tile_n, tile_m=256, inject=[(i, j, delta) for i, j in faults])
     r3 = r3.read()
     assert r3.coords() == sorted(faults) and r3.n_corrected == 4
     assert (c3.float() - ref).abs().max().item() <= OUT_TOL * ref.abs().max().item()
 
 
+@pytest.mark.parametrize("tile_n", PAIR_WIDTHS)
 @pytest.mark.parametrize("fault", [None, 1.0])
-def test_pair_ref_mode_matches_oracle(cuda_device, fault):
+def test_pair_ref_mode_matches_oracle(cuda_device, fault, tile_n):
     m, n, k = 384, 512, 256
     a, w, b = seeded(m, n, k, 14, True)
     inj = [(300, 4, fault)] if fault else None
     c, rep = ops.abft_gemm(a.to(cuda_device), w.to(cuda_device), b.to(cuda_device), mode=N.MODE_REF, inject=inj,
-                           tile_n=256, tile_m=256)
+                           tile_n=tile_n, tile_m=256)
     r = rep.read()
     o = O.cheap_sum_check(f32(a), f32(w).T, f32(c), f32(b))
     assert (r.ref_ok == 1) == o.ok
     assert abs(r.sum_c - o.sum_c) <= 1e-4 * max(1.0, abs(o.sum_c))
 
 
-def test_pair_needs_256_wide_tiles(cuda_device):
+def test_tile_shape_rejected(cuda_device):
     a, w, _ = seeded(256, 256, 64, 15)
     with pytest.raises(N.AbftError):
-        ops.abft_gemm(a.to(cuda_device), w.to(cuda_device), tile_n=128, tile_m=256)
+        ops.abft_gemm(a.to(cuda_device), w.to(cuda_device), tile_n=128, tile_m=192)
 
 
 # --------------------------------------------- compact tail tiles (last column)
-@pytest.mark.parametrize("tile_n,tile_m", [(256, 128), (256, 256), (128, 128)])
+@pytest.mark.parametrize("tile_n,tile_m", [(256, 128), (256, 256), (128, 128), (128, 256)])
 @pytest.mark.parametrize("n", [8, 16, 24, 40, 136, 248 + 8, 248 + 128, 248 + 232, 4096, 120 + 112])
 @pytest.mark.parametrize("mode", [N.MODE_OFF, N.MODE_DETECT | N.MODE_CORRECT])
 def test_tail_tile_widths(cuda_device, tile_n, tile_m, n, mode):

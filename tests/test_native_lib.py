@@ -45,7 +45,7 @@ def test_host_only_helpers():
     assert L.abft_pick_tile_n(512, 4096, 4096, 148, 3) == 128  # 140 narrow tiles: one wave, no partials
     assert L.abft_pick_tile_m(512, 4608, 3584, 148, 3, 256) == 256  # 38 pair tiles beat 39 x 4 narrow ones
     assert L.abft_pick_tile_m(8192, 8192, 8192, 148, 3, 256) == 256
-    assert L.abft_pick_tile_m(1024, 1024, 1024, 148, 3, 128) == 128  # pairs need 256-wide tiles
+    assert L.abft_pick_tile_m(1024, 1024, 1024, 148, 3, 128) == 128  # 128-wide pairs run only on request
     assert L.abft_pick_tile_n(8192, 8192, 8192, 148, 3) == 256
     assert L.abft_pick_tile_n(4096, 4096, 4096, 148, 0) == 256  # 4 waves of 256 beat 7 waves of 128
     assert L.abft_pick_tile_n(512, 37888, 3584, 148, 0) == 256  # 592 tiles: exactly 4 waves

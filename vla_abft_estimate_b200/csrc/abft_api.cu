@@ -40,8 +40,8 @@ struct DeviceInfo {
   bool init;
   bool ok;
   int sms;
-  bool attr_set[6];
-  int pair_clusters[2];  // co-resident 2-CTA clusters of the pair kernels [check], 0 = not asked yet
+  bool attr_set[8];
+  int pair_clusters[2][2];  // co-resident 2-CTA clusters of the pair kernels [bn == 256][check], 0 = not asked yet
 };
 DeviceInfo g_dev[kMaxDevices];
 std::mutex g_mu;
@@ -88,7 +88,8 @@ int ensure_smem_attr(int dev, int slot) {
   return ensure_smem_attr_locked<BN, CHECK, PAIR>(dev, slot);
 }
 
-constexpr int kPairSlot[2] = {5, 4};  // attr_set slots of the pair kernels [check]
+// attr_set slots of the pair kernels [bn == 256][check]
+constexpr int kPairSlot[2][2] = {{7, 6}, {5, 4}};
 
 cudaLaunchAttribute pair_cluster_attr() {
   cudaLaunchAttribute at;
@@ -102,28 +103,29 @@ cudaLaunchAttribute pair_cluster_attr() {
 // How many 2-CTA clusters of the pair kernel can be resident at once on
 // device `dev` (every unit of a persistent launch must be resident: stream-K
 // finishers wait for later units). Falls back to sms / 2 if the query fails.
-template <bool CHECK>
+template <int BN, bool CHECK>
 int pair_units_on(int dev, int sms) {
   std::lock_guard<std::mutex> lk(g_mu);
   DeviceInfo& d = g_dev[dev];
-  if (d.pair_clusters[CHECK] == 0) {
+  int& cached = d.pair_clusters[BN == 256][CHECK];
+  if (cached == 0) {
     int n = 0;
-    if (ensure_smem_attr_locked<256, CHECK, true>(dev, kPairSlot[CHECK]) == ABFT_OK) {
+    if (ensure_smem_attr_locked<BN, CHECK, true>(dev, kPairSlot[BN == 256][CHECK]) == ABFT_OK) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(2 * static_cast<unsigned>(sms / 2));
       cfg.blockDim = dim3(kThreads);
-      cfg.dynamicSmemBytes = GemmCfg<256, CHECK, true>::kSmemBytes;
+      cfg.dynamicSmemBytes = GemmCfg<BN, CHECK, true>::kSmemBytes;
       cudaLaunchAttribute at = pair_cluster_attr();
       cfg.attrs = &at;
       cfg.numAttrs = 1;
-      if (cudaOccupancyMaxActiveClusters(&n, abft_gemm_kernel<256, CHECK, true>, &cfg) != cudaSuccess) {
+      if (cudaOccupancyMaxActiveClusters(&n, abft_gemm_kernel<BN, CHECK, true>, &cfg) != cudaSuccess) {
         cudaGetLastError();
         n = 0;
       }
     }
-    d.pair_clusters[CHECK] = n > 0 ? n : sms / 2;
+    cached = n > 0 ? n : sms / 2;
   }
-  return d.pair_clusters[CHECK] < sms / 2 ? d.pair_clusters[CHECK] : sms / 2;
+  return cached < sms / 2 ? cached : sms / 2;
 }
 
 // Encoded tensor maps are a pure function of (kind, address, extents,
@@ -373,6 +375,10 @@ Schedule schedule_for(int64_t M, int64_t N, int64_t K, int tile_m, int bn, int b
 
 // A CTA pair runs a 128 x 256 share of a tile per SM about this much faster
 // than a single CTA (each CTA stages half the B-operand tile per k-block).
+// Pairs of 128-wide tiles run a k-block no faster than single 128 x 128
+// CTAs (0.32 against 0.31 us, bench.py --tile-grid) and leave half the
+// units: they are available on request (tile_m 256, tile_n 128) but never
+// picked.
 constexpr double kPairSpeedup = 1.10;
 
 // Estimated time (microseconds) of an M x N x K launch with tile_m x bn
@@ -503,7 +509,7 @@ int make_plan_uncached(const abft_gemm_args* a, int dev, int sms, Plan* pl) {
   pl->bn = a->tile_n ? a->tile_n : pick_tile_n(a->M, a->N, a->K, sms, a->mode, nb);
   pl->tile_m = a->tile_m ? a->tile_m : pick_tile_m(a->M, a->N, a->K, sms, a->mode, pl->bn, nb);
   if (pl->tile_m != 128 && pl->tile_m != 256) return ABFT_ERR_UNSUPPORTED;
-  if (pl->tile_m == 256 && (pl->bn != 256 || sms < 2)) return ABFT_ERR_UNSUPPORTED;
+  if (pl->tile_m == 256 && sms < 2) return ABFT_ERR_UNSUPPORTED;
   pl->pair = pl->tile_m == 256;
   pl->bd = pl->check ? pl->bn - kChkRows : pl->bn;
   pl->num_kb = static_cast<int>(cdiv(a->K, kBK));
@@ -514,7 +520,8 @@ int make_plan_uncached(const abft_gemm_args* a, int dev, int sms, Plan* pl) {
   else if (dev < 0)
     pl->units = sms / 2;
   else
-    pl->units = pl->check ? pair_units_on<true>(dev, sms) : pair_units_on<false>(dev, sms);
+    pl->units = pl->bn == 256 ? (pl->check ? pair_units_on<256, true>(dev, sms) : pair_units_on<256, false>(dev, sms))
+                              : (pl->check ? pair_units_on<128, true>(dev, sms) : pair_units_on<128, false>(dev, sms));
   pl->sch = schedule_for(a->M, a->N, a->K, pl->tile_m, pl->bn, pl->bd, pl->units, nb);
   pl->grid = pl->sch.grid * (pl->pair ? 2 : 1);
 
@@ -569,7 +576,6 @@ int validate_gemm(const abft_gemm_args* a) {
   if (a->mode & ~(ABFT_MODE_DETECT | ABFT_MODE_CORRECT | ABFT_MODE_REF | ABFT_MODE_REF_BF16)) return ABFT_ERR_INVALID_ARG;
   if (a->tile_n != 0 && a->tile_n != 128 && a->tile_n != 256) return ABFT_ERR_UNSUPPORTED;
   if (a->tile_m != 0 && a->tile_m != 128 && a->tile_m != 256) return ABFT_ERR_UNSUPPORTED;
-  if (a->tile_m == 256 && a->tile_n == 128) return ABFT_ERR_UNSUPPORTED;
   if (a->swap_ab < 0 || a->swap_ab > 2) return ABFT_ERR_INVALID_ARG;
   if (a->mode != ABFT_MODE_OFF && (a->report == nullptr || a->report_capacity < 0)) return ABFT_ERR_INVALID_ARG;
   if (a->report != nullptr && !aligned16(a->report)) return ABFT_ERR_ALIGNMENT;
@@ -890,9 +896,12 @@ int abft_gemm_bf16(const abft_gemm_args* args, void* stream) {
                                     const_cast<void*>(V), stream);
     if (rc != ABFT_OK) return rc;
   }
-  if (ws.pair)
-    rc = check ? launch_gemm<256, true, true>(dev, kPairSlot[1], tmA, tmB, tmB2, tmV, tmBt, tmC, p, grid, s)
-               : launch_gemm<256, false, true>(dev, kPairSlot[0], tmA, tmB, tmB2, tmV, tmBt, tmC, p, grid, s);
+  if (ws.pair && bn == 256)
+    rc = check ? launch_gemm<256, true, true>(dev, kPairSlot[1][1], tmA, tmB, tmB2, tmV, tmBt, tmC, p, grid, s)
+               : launch_gemm<256, false, true>(dev, kPairSlot[1][0], tmA, tmB, tmB2, tmV, tmBt, tmC, p, grid, s);
+  else if (ws.pair)
+    rc = check ? launch_gemm<128, true, true>(dev, kPairSlot[0][1], tmA, tmB, tmB2, tmV, tmBt, tmC, p, grid, s)
+               : launch_gemm<128, false, true>(dev, kPairSlot[0][0], tmA, tmB, tmB2, tmV, tmBt, tmC, p, grid, s);
   else if (bn == 256)
     rc = check ? launch_gemm<256, true, false>(dev, 0, tmA, tmB, tmB2, tmV, tmBt, tmC, p, grid, s)
                : launch_gemm<256, false, false>(dev, 1, tmA, tmB, tmB2, tmV, tmBt, tmC, p, grid, s);

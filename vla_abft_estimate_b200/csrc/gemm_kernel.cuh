@@ -77,8 +77,10 @@ constexpr int kChkRows = 8;  // rows of the per-tile checksum block
 // each CTA's 128 rows into that CTA's own TMEM.
 template <int BN, bool CHECK, bool PAIR = false>
 struct GemmCfg {
-  static_assert(!PAIR || BN == 256, "CTA pairs use 256-wide tiles");
-  static constexpr int kStages = PAIR ? 6 : ((BN == 256) ? 4 : 6);
+  static_assert(BN == 128 || BN == 256, "tile widths");
+  // Stage = 16 KB of A + this CTA's B rows: 32 KB (pair of 256-wide tiles,
+  // single 128-wide), 48 KB (single 256-wide), 24 KB (pair of 128-wide).
+  static constexpr int kStages = PAIR ? ((BN == 256) ? 6 : 8) : ((BN == 256) ? 4 : 6);
   static constexpr int kBD = CHECK ? BN - kChkRows : BN;  // data columns per tile
   static constexpr int kTileM = PAIR ? 2 * kBM : kBM;    // output rows per tile
   static constexpr int kBRows = PAIR ? BN / 2 : BN;      // B-operand rows this CTA stages

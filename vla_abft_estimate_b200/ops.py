@@ -203,8 +203,8 @@ def abft_gemm(
     ``a`` is [M, K], ``weight`` [N, K] (nn.Linear layout), ``bias`` [N].
     ``checksums`` is ``encode_weight(weight, tile_n)`` (cache it for a fixed
     weight); when omitted and checks are on, the call encodes into its
-    workspace. ``tile_m`` 256 runs each 256-row tile on a 2-CTA pair (needs
-    tile_n 256); 0 lets the library choose. ``swap_ab`` (0 choose, 1 never,
+    workspace. ``tile_m`` 256 runs each 256-row tile on a 2-CTA pair (either
+    tile_n); 0 lets the library choose. ``swap_ab`` (0 choose, 1 never,
     2 always) computes out^T = weight a^T instead, for few rows of ``a``:
     the weight then streams through the MMA's 128-row side, the checksums
     come from ``a`` per call and fault records keep ``out``'s coordinates.
