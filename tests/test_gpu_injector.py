@@ -12,7 +12,7 @@ import torch
 import torch.nn as nn
 
 from oracle import abft_oracle as O
-from vla_abft_estimate_b200.abft import AbftConfig, AbftInjector, AbftStatsCollector, CheapSumChecker
+from vla_abft_estimate_b200.abft import AbftConfig, AbftInjector, AbftStatsCollector, CheapSumChecker, OpMeta
 
 pytestmark = pytest.mark.gpu
 
@@ -260,3 +260,55 @@ def test_matmul_two_d_fused_and_batched_rhs_follows_reference(cuda_device):
             assert abs(flat[i2].float().item() - clean[i2].item()) > 250.0
         else:
             assert (flat.float() - clean).abs().max().item() <= 1e-2 * clean.abs().max().item()
+
+
+@pytest.mark.parametrize("k,n,bias", [(7, 768, True), (768, 7, True), (5, 3, False), (12, 20, True)])
+def test_narrow_linears_checked_on_padded_copies(cuda_device, k, n, bias):
+    """K or N not a multiple of 8 (a VLA's 7-wide action projections): the
+    injector checks the call on zero-padded copies instead of skipping it,
+    the clean call passes, its corner and sum match the oracle on the
+    original operands, and a perturbed output fails the check."""
+    meta = OpMeta(op_name="linear", phase="prefill", shape_key="narrow")
+    torch.manual_seed(k * 31 + n)
+    x = torch.randn(16, k, device=cuda_device).bfloat16()
+    w = (torch.randn(n, k, device=cuda_device) * k ** -0.5).bfloat16()
+    b = (torch.randn(n, device=cuda_device) * 0.02).bfloat16() if bias else None
+    cfg = AbftConfig(enable=True, checker_backend="fused")
+    stats = AbftStatsCollector()
+    with torch.inference_mode(), AbftInjector(cfg, CheapSumChecker(cfg), stats):
+        y = torch.nn.functional.linear(x, w, b)
+    torch.cuda.synchronize()
+    assert stats.skipped_unsupported == 0 and stats.total_checks == 1 and stats.total_failures == 0
+
+    chk = CheapSumChecker(cfg)
+    res = chk.check(x, w.t(), y, meta, bias_1d=b)
+    o = O.cheap_sum_check(x.float().cpu().numpy(), w.float().cpu().numpy().T, y.float().cpu().numpy(),
+                          None if b is None else b.float().cpu().numpy())
+    assert res.ok and o.ok
+    assert abs(res.sum_c - o.sum_c) <= 1e-4 * max(1.0, abs(o.sum_c))
+    assert abs(res.abft_corner - o.abft_corner) <= 1e-4 * max(1.0, abs(o.abft_corner))
+
+    bad = y.clone()
+    bad[3, n - 1] += 64.0
+    assert not chk.check(x, w.t(), bad, meta, bias_1d=b).ok
+
+
+@pytest.mark.parametrize("seed", [1, 4])
+def test_narrow_linears_deferred_match_immediate(cuda_device, seed):
+    """A model with 7-wide layers (checked on padded copies): deferring the
+    checker's reports to flush() records the same checks, failures and
+    errors as reading each report at its call."""
+    torch.manual_seed(seed)
+    model = nn.Sequential(nn.Linear(7, 768), nn.Linear(768, 768), nn.Linear(768, 7))
+    model = model.to(device=cuda_device, dtype=torch.bfloat16).eval()
+    x = torch.randn(16, 7, device=cuda_device).bfloat16()
+    cfg = AbftConfig(enable=True, checker_backend="b200", inject_fault=True, inject_probability=0.5,
+                     inject_magnitude=500.0, seed=seed)
+    summaries = []
+    for defer in (False, True):
+        out, stats, _ = run(model, x, cfg, defer)
+        s = stats.export_summary()["abft"]
+        assert s["checks_total"] == 3 and s["faults"]["skipped_unsupported"] == 0
+        summaries.append((s["checks_total"], s["fail_total"], s["faults"]["detected_total"],
+                          stats.export_summary()["fault_injection"]))
+    assert summaries[0] == summaries[1]

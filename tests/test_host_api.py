@@ -206,3 +206,25 @@ def test_unsupported_operands_are_counted_not_fatal():
     with AbftInjector(cfg, CheapSumChecker(cfg), stats):
         F.linear(torch.randn(4, 8).bfloat16(), torch.randn(8, 8).bfloat16())
     assert stats.total_checks == 0 and stats.skipped_unsupported == 1
+
+
+@pytest.mark.parametrize("m,k,n", [(5, 7, 3), (16, 7, 768), (16, 768, 7), (4, 8, 12)])
+def test_narrow_operands_padded_with_zeros(m, k, n):
+    """K or N not a multiple of 8: the checker's operands are zero-padded
+    copies whose check sums (column sums of A times row sums of B, the sum
+    of C) equal the originals'."""
+    from vla_abft_estimate_b200.abft.checkers import _padded_operands
+
+    torch.manual_seed(m + k + n)
+    a = torch.randn(m, k).bfloat16()
+    w = torch.randn(n, k).bfloat16()
+    c = torch.randn(m, n).bfloat16()
+    pa, pb, layout, pc, pbias = _padded_operands(a, w.t(), c, None)
+    k8, n8 = -(-k // 8) * 8, -(-n // 8) * 8
+    assert layout == "nk" and pbias is None
+    assert tuple(pa.shape) == (m, k8) and tuple(pb.shape) == (n8, k8) and tuple(pc.shape) == (m, n8)
+    assert torch.equal(pa[:, :k], a) and torch.equal(pb[:n, :k], w) and torch.equal(pc[:, :n], c)
+    assert not pa[:, k:].any() and not pb[n:].any() and not pb[:, k:].any() and not pc[:, n:].any()
+    corner = (a.double().sum(0) * w.double().sum(0)).sum()
+    pcorner = (pa.double().sum(0) * pb.double().sum(0)).sum()
+    assert corner.item() == pcorner.item() and c.double().sum().item() == pc.double().sum().item()

@@ -18,6 +18,7 @@ from dataclasses import dataclass
 from typing import Optional, Tuple
 
 import torch
+import torch.nn.functional as F
 
 from .. import ops
 from .config import AbftConfig
@@ -65,7 +66,7 @@ def _as_lib_operands(
     k = a_2d.shape[1]
     n = b_2d.shape[1]
     if k % 8 or n % 8:
-        raise UnsupportedOperand(f"K={k} and N={n} must be multiples of 8")
+        return _padded_operands(a_2d, b_2d, c_2d, bias_1d)
     a = a_2d if a_2d.stride(1) == 1 and a_2d.stride(0) % 8 == 0 else a_2d.contiguous()
     c = c_2d if c_2d.stride(1) == 1 and c_2d.stride(0) % 8 == 0 else c_2d.contiguous()
     bt = b_2d.t()
@@ -81,6 +82,37 @@ def _as_lib_operands(
             raise UnsupportedOperand("bias must be a CUDA bfloat16 tensor")
         bias = bias_1d.contiguous()
     return a, b, layout, c, bias
+
+
+def _padded_operands(
+    a_2d: torch.Tensor, b_2d: torch.Tensor, c_2d: torch.Tensor, bias_1d: Optional[torch.Tensor]
+) -> Tuple[torch.Tensor, torch.Tensor, str, torch.Tensor, Optional[torch.Tensor]]:
+    """(A, B, C, bias) zero-padded to K and N multiples of 8.
+
+    The library reads rows in 16-byte pieces, so K and N must be multiples
+    of 8; a VLA's action projections (K or N = 7) are not. Zero rows and
+    columns add only +0 to the sums the check compares (column sums of A,
+    row sums of B, the sums of C and of the bias), so the padded copies are
+    checked for the same quantities as the original operands (up to fp32
+    summation order, like any other call).
+    """
+    if bias_1d is not None and (not bias_1d.is_cuda or bias_1d.dtype != torch.bfloat16):
+        raise UnsupportedOperand("bias must be a CUDA bfloat16 tensor")
+    k = a_2d.shape[1]
+    n = b_2d.shape[1]
+    pk, pn = -k % 8, -n % 8
+    a = F.pad(a_2d, (0, pk)) if pk else _rows_aligned(a_2d)
+    b = F.pad(b_2d.t(), (0, pk, 0, pn))  # [N, K] padded, contiguous
+    c = F.pad(c_2d, (0, pn)) if pn else _rows_aligned(c_2d)
+    bias = None
+    if bias_1d is not None:
+        bias = F.pad(bias_1d, (0, pn)) if pn else bias_1d.contiguous()
+    return a, b, "nk", c, bias
+
+
+def _rows_aligned(t: torch.Tensor) -> torch.Tensor:
+    """t itself when its rows are contiguous and 16-byte aligned, else a copy."""
+    return t if t.stride(1) == 1 and t.stride(0) % 8 == 0 and t.data_ptr() % 16 == 0 else t.contiguous()
 
 
 class CheapSumChecker(AbftChecker):
@@ -111,10 +143,24 @@ class CheapSumChecker(AbftChecker):
             # The reference computes and discards the sums here (:74-75);
             # the result it returns does not depend on them.
             return CheckResult(ok=True, abs_err=0.0, rel_err=0.0, abft_corner=0.0, sum_c=0.0)
+        return self.result(self.launch(a_2d, b_2d, c_2d, bias_1d).read())
+
+    def launch(
+        self,
+        a_2d: torch.Tensor,
+        b_2d: torch.Tensor,
+        c_2d: torch.Tensor,
+        bias_1d: Optional[torch.Tensor] = None,
+    ) -> "ops.ReportBuffer":
+        """Queue the check on the current stream; its report is read later
+        (``result(report.read())``), so a caller can defer the host read."""
         a, b, layout, c, bias = _as_lib_operands(a_2d, b_2d, c_2d, bias_1d)
-        rep = ops.check_only(a, b, c, bias, b_layout=layout, tol_abs=self.cfg.tol_abs, tol_rel=self.cfg.tol_rel,
-                             locate=self.locate, bf16_sums=self.cfg.bf16_sums, thr_scale=self.cfg.thr_scale,
-                             report=ops.ReportBuffer(self.cfg.report_capacity, a.device)).read()
+        return ops.check_only(a, b, c, bias, b_layout=layout, tol_abs=self.cfg.tol_abs, tol_rel=self.cfg.tol_rel,
+                              locate=self.locate, bf16_sums=self.cfg.bf16_sums, thr_scale=self.cfg.thr_scale,
+                              report=ops.ReportBuffer(self.cfg.report_capacity, a.device))
+
+    def result(self, rep: "N.FaultReport") -> CheckResult:
+        """The CheckResult of a report written by ``launch``."""
         located = tuple((r.row, r.col) for r in rep.records if r.row >= 0 and r.col >= 0)
         ok = rep.ref_ok == 1 and (not self.locate or rep.n_faults == 0)
         return CheckResult(ok=ok, abs_err=float(rep.abs_err), rel_err=float(rep.rel_err),

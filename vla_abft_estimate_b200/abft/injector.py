@@ -155,6 +155,17 @@ class _ReportArena:
         return results
 
 
+class _DeferredCheck:
+    """A checker call queued on the device (report buffer + the checker that
+    turns the read report into a CheckResult), recorded at flush."""
+
+    __slots__ = ("report", "checker")
+
+    def __init__(self, report, checker):
+        self.report = report
+        self.checker = checker
+
+
 class AbftInjector(AbstractContextManager):
     def __init__(self, cfg: AbftConfig, checker: AbftChecker, stats: AbftStatsCollector,
                  defer_reports: bool = False):
@@ -170,8 +181,9 @@ class AbftInjector(AbstractContextManager):
         self._orig_bmm: Optional[Callable[..., torch.Tensor]] = None
         self._dump_done: bool = False
         # deferred records: (device, op, phase, shape key, injected, batched)
-        # with batched = None (next report of the device's arena) or
-        # (report buffer, batches, rows per batch, gates)
+        # with batched = None (next report of the device's arena),
+        # (report buffer, batches, rows per batch, gates), or a _DeferredCheck
+        # (a checker call whose report is read at flush)
         self._pending: List[Tuple[int, str, str, Any, bool, Any]] = []
         self._arenas: dict = {}
         self._tile_n: dict = {}
@@ -221,6 +233,9 @@ class AbftInjector(AbstractContextManager):
                 if batched is None:
                     self.stats.record_check(op_name=op_name, shape_key=shape_key, result=next(reports[dev]),
                                             injected=injected)
+                elif isinstance(batched, _DeferredCheck):
+                    self.stats.record_check(op_name=op_name, shape_key=shape_key,
+                                            result=batched.checker.result(batched.report.read()), injected=injected)
                 else:
                     rb, nb, rows, gates = batched
                     self._record_batches(op_name, shape_key, rb.read(), nb, rows, gates, injected)
@@ -298,6 +313,17 @@ class AbftInjector(AbstractContextManager):
         if not self._check_gate(a_2d, b_2d, c_2d):
             return
         shape_key = _shape_key(a_2d, b_2d, c_2d)
+        if self.defer_reports and self.cfg.record_enable and hasattr(self.checker, "launch"):
+            # Same check, report read at flush: no host sync per call.
+            try:
+                rb = self.checker.launch(a_2d, b_2d, c_2d, bias_1d)
+            except UnsupportedOperand:
+                self.stats.record_skip_unsupported()
+                return
+            self._pending.append((a_2d.device.index, op_name, self.stats.current_phase, shape_key, injected,
+                                  _DeferredCheck(rb, self.checker)))
+            self._maybe_dump_tensors(op_name, shape_key, a_2d, b_2d, c_2d, bias_1d)
+            return
         try:
             result = self.checker.check(
                 a_2d, b_2d, c_2d, OpMeta(op_name=op_name, phase=self.stats.current_phase, shape_key=shape_key),
