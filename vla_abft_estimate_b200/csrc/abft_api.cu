@@ -839,8 +839,16 @@ int abft_gemm_bf16(const abft_gemm_args* args, void* stream) {
       const uint32_t a_bytes = static_cast<uint32_t>(kBM * kBK * 2);
       const uint32_t row_bytes = static_cast<uint32_t>(kBK * 2);  // one B row of one k-block
       p.tail_n = tn;
-      if (!check) {
-        p.tail_tx = ws.pair ? 2 * (a_bytes + (bn / 2) * row_bytes) : a_bytes + bn * row_bytes;
+      if (!check && ws.pair) {
+        p.tail_tx = 2 * (a_bytes + (bn / 2) * row_bytes);
+      } else if (!check) {
+        // The box of the tn rows the narrow MMA reads, not a whole tile:
+        // with few rows (decode) the zero fill of a full box costs more
+        // shared-memory bandwidth than the rows themselves.
+        rc = make_tmap_kmajor(&tmBt, a->B, a->K, a->N, a->ldb, tn, nb, a->stride_b);
+        if (rc != ABFT_OK) return rc;
+        p.tail_box = tn;
+        p.tail_tx = a_bytes + static_cast<uint32_t>(tn) * row_bytes;
       } else {
         // Data rows copied by the tail box into this CTA (a pair: the odd
         // CTA holds the rows from tn / 2 on; the even CTA keeps its usual box).

@@ -161,7 +161,7 @@ struct GemmParams {
   // its B-operand tile is compact (data rows, then with checks the 8
   // checksum rows) and one MMA of N = tail_n (a multiple of 16) covers it.
   int tail_n;
-  int tail_box;      // data rows the tail box copies into this CTA (odd CTA of a pair), 0 = none
+  int tail_box;      // rows the tail box copies into this CTA (checks: data rows, odd CTA of a pair; no checks, single CTA: tail_n), 0 = none
   uint32_t tail_tx;  // bytes one stage of a tail tile delivers (both CTAs of a pair)
   // Swapped operands (few output rows): the kernel computes C^T = W X^T, so
   // its rows are C's columns and its columns are C's rows. The output is
@@ -460,9 +460,10 @@ __device__ __forceinline__ bool mma_mainloop_n(int n, uint8_t* smem, uint64_t* f
 }
 
 // tmB2 (pairs with checks only): B rows for the odd CTA, whose share of a
-// tile's data rows is BD - 128 rather than 128. tmBt: the data rows of the
-// tail tile column that the compact tail tile needs in this CTA (box
-// p.tail_box rows), when checks are on. tmC: the output [batch][M][N] in
+// tile's data rows is BD - 128 rather than 128. tmBt: the rows of the tail
+// tile column that the compact tail tile needs in this CTA (box
+// p.tail_box rows): with checks its data rows; without checks (single CTA)
+// all tail_n rows the narrow MMA reads. tmC: the output [batch][M][N] in
 // 32 x 32 boxes with 64-byte swizzle, the layout of an epilogue warp's
 // staging block (unused with swapped operands).
 template <int BN, bool CHECK, bool PAIR>
@@ -524,7 +525,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmB);
     if (PAIR && CHECK) tma_prefetch_desc(&tmB2);
     if (CHECK) tma_prefetch_desc(&tmV);
-    if (CHECK && p.tail_box > 0) tma_prefetch_desc(&tmBt);
+    if (p.tail_box > 0) tma_prefetch_desc(&tmBt);
     if (!p.swap) tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
@@ -610,9 +611,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else {
             mbar_arrive_expect_tx(&full[stage], tx);
             tma_load_3d(sa, &tmA, &full[stage], kx, arow, bz);
-            if (!(CHECK && tail)) {
+            if (!tail) {
               tma_load_3d(sb, &tmB, &full[stage], kx, nt * BD, bz);
               if (CHECK) tma_load_3d(sb + BD * 128, &tmV, &full[stage], kx, nt * kChkRows, bz);
+            } else if (!CHECK) {
+              // compact tail: the tail_n rows the narrow MMA reads (rows past N read as zeros)
+              tma_load_3d(sb, &tmBt, &full[stage], kx, nt * BD, bz);
             } else {
               if (p.tail_box > 0) tma_load_3d(sb, &tmBt, &full[stage], kx, nt * BD, bz);
               if (!p.build_chk) tma_load_3d(sb + p.tail_box * 128, &tmV, &full[stage], kx, nt * kChkRows, bz);
