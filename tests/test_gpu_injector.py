@@ -312,3 +312,32 @@ def test_narrow_linears_deferred_match_immediate(cuda_device, seed):
         summaries.append((s["checks_total"], s["fail_total"], s["faults"]["detected_total"],
                           stats.export_summary()["fault_injection"]))
     assert summaries[0] == summaries[1]
+
+
+@pytest.mark.parametrize("layout", ["vector", "3d", "row_slice", "transposed"])
+def test_fused_linear_input_layouts(cuda_device, layout):
+    """The fused linear reads contiguous inputs of any rank in place and
+    strided ones through a view or a copy: the output keeps the input's
+    leading shape, matches torch, and a clean call records a passing check."""
+    torch.manual_seed(7)
+    k, n = 256, 384
+    w = (torch.randn(n, k, device=cuda_device) * k ** -0.5).bfloat16()
+    b = (torch.randn(n, device=cuda_device) * 0.02).bfloat16()
+    if layout == "vector":
+        x = torch.randn(k, device=cuda_device).bfloat16()
+    elif layout == "3d":
+        x = torch.randn(2, 5, k, device=cuda_device).bfloat16()
+    elif layout == "row_slice":
+        x = torch.randn(12, 2 * k, device=cuda_device).bfloat16()[:, :k]  # row stride 2k
+    else:
+        x = torch.randn(k, 12, device=cuda_device).bfloat16().t()  # column-major rows
+    ref = torch.nn.functional.linear(x, w, b)
+    cfg = AbftConfig(enable=True, checker_backend="b200")
+    stats = AbftStatsCollector()
+    with torch.inference_mode(), AbftInjector(cfg, CheapSumChecker(cfg), stats, defer_reports=True):
+        y = torch.nn.functional.linear(x, w, b)
+    torch.cuda.synchronize()
+    assert y.shape == ref.shape
+    assert (y.float() - ref.float()).abs().max().item() <= 1e-2 * ref.float().abs().max().item()
+    s = stats.export_summary()["abft"]
+    assert s["checks_total"] == 1 and s["fail_total"] == 0

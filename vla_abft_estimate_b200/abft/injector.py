@@ -379,10 +379,17 @@ class AbftInjector(AbstractContextManager):
 
     def _fused_linear(self, x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor]) -> torch.Tensor:
         n, k = weight.shape
-        x2 = x.reshape(-1, k)
-        if x2.stride(1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
-            x2 = x2.contiguous()
-        m = x2.shape[0]
+        # A contiguous input is read in place as m rows of k (no reshape
+        # dispatch per call); anything else as a 2-D view with its own row
+        # stride, or a copy when that view cannot be read in place.
+        if x.is_contiguous() and x.data_ptr() % 16 == 0:
+            x2, lda = x, k
+        else:
+            x2 = x.reshape(-1, k)
+            if x2.stride(1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
+                x2 = x2.contiguous()
+            lda = x2.stride(0)
+        m = x2.numel() // k
         dix = x2.get_device()
         # injection first, then the check gate: the reference's rng order
         idx = self._draw_fault(m * n)
@@ -412,10 +419,11 @@ class AbftInjector(AbstractContextManager):
                 rep = ops.ReportBuffer(self.cfg.report_capacity, x2.device)
         if bias is not None and not bias.is_contiguous():
             bias = bias.contiguous()
-        out = torch.empty((m, n), dtype=torch.bfloat16, device=x2.device)
+        # the output in its final shape: m contiguous rows of n
+        out = torch.empty(x.shape[:-1] + (n,), dtype=torch.bfloat16, device=x2.device)
         # operands checked by _fused_linear_ok: straight to the launch
         ops._gemm_launch(x2, weight, bias, out, m, n, k, mode, 0 if swapped else tile_n, 0, 0, self.cfg.thr_scale,
-                         self.cfg.thr_abs, 1e-2, 1e-2, cks, inject, rep, 0)
+                         self.cfg.thr_abs, 1e-2, 1e-2, cks, inject, rep, 0, lda=lda, ldc=n)
         if check:
             if self.cfg.record_enable:
                 if self.defer_reports:
@@ -424,8 +432,9 @@ class AbftInjector(AbstractContextManager):
                     self.stats.record_check(op_name="linear", shape_key=f"A{(m, k)}_B{(k, n)}_C{(m, n)}",
                                             result=result_from_report(rep.read()), injected=injected)
             if self.cfg.dump_file:
-                self._maybe_dump_tensors("linear", f"A{(m, k)}_B{(k, n)}_C{(m, n)}", x2, weight.t(), out, bias)
-        return out.reshape(*x.shape[:-1], n)
+                self._maybe_dump_tensors("linear", f"A{(m, k)}_B{(k, n)}_C{(m, n)}", x.reshape(m, k), weight.t(),
+                                         out.reshape(m, n), bias)
+        return out
 
     # -------------------------------------------------- fused bmm / matmul
     def _fused_mm_ok(self, a: torch.Tensor, b: torch.Tensor) -> bool:

@@ -246,15 +246,19 @@ def abft_gemm(
 
 
 def _gemm_launch(a, weight, bias, out, m, n, k, mode, tile_n, tile_m, swap_ab, thr_scale, thr_abs, tol_abs, tol_rel,
-                 checksums, inject, report, num_sms) -> None:
+                 checksums, inject, report, num_sms, lda=None, ldc=None) -> None:
     """abft_gemm after argument validation (callers that have checked the
-    operands themselves call this directly)."""
+    operands themselves call this directly). ``lda`` / ``ldc`` override the
+    leading dimensions read from 2-D ``a`` / ``out``, for callers that pass
+    contiguous tensors of any rank holding m rows."""
     dev = a.device
     inj = _Inject(inject, dev) if inject else None
     args = N.GemmArgs()
     args.A, args.B, args.C, args.bias = _ptr(a), _ptr(weight), _ptr(out), _ptr(bias)
     args.M, args.N, args.K = m, n, k
-    args.lda, args.ldb, args.ldc = a.stride(0), weight.stride(0), out.stride(0)
+    args.lda = a.stride(0) if lda is None else lda
+    args.ldb = weight.stride(0)
+    args.ldc = out.stride(0) if ldc is None else ldc
     args.mode = int(mode)
     args.tile_n = int(tile_n)
     args.tile_m = int(tile_m)
