@@ -228,3 +228,62 @@ def test_narrow_operands_padded_with_zeros(m, k, n):
     corner = (a.double().sum(0) * w.double().sum(0)).sum()
     pcorner = (pa.double().sum(0) * pb.double().sum(0)).sum()
     assert corner.item() == pcorner.item() and c.double().sum().item() == pc.double().sum().item()
+
+
+class DeferringOracleChecker(OracleChecker):
+    """Test double with the launch / result split of the library checker:
+    ``launch`` computes the oracle result at call time and returns a report
+    stand-in that is only read at flush; ``result`` turns it into the
+    CheckResult."""
+
+    class _Report:
+        def __init__(self, res):
+            self.res = res
+            self.reads = 0
+
+        def read(self):
+            self.reads += 1
+            return self.res
+
+    def __init__(self, cfg):
+        super().__init__(cfg)
+        self.reports = []
+
+    def launch(self, a_2d, b_2d, c_2d, bias_1d=None):
+        rep = self._Report(OracleChecker.check(self, a_2d, b_2d, c_2d, None, bias_1d))
+        self.reports.append(rep)
+        return rep
+
+    def result(self, rep):
+        return rep
+
+
+def test_deferred_checker_reports_recorded_at_flush_in_call_order():
+    """defer_reports with a checker that can launch: nothing is read during
+    the forward, flush() records every check in call order with the phase
+    of its call, and the statistics equal an immediate-mode run."""
+    conf = dict(inject_probability=0.5, sample_rate=1.0, seed=11)
+    shapes = [(4, 16, 8), (6, 8, 24), (3, 24, 16), (5, 16, 16)]
+    summaries = []
+    for defer in (False, True):
+        cfg = AbftConfig(enable=True, inject_fault=True, inject_magnitude=1.0, seed=conf["seed"],
+                         inject_probability=conf["inject_probability"], enable_matmul=False, enable_bmm=False,
+                         checker_backend="python")
+        stats = AbftStatsCollector()
+        checker = DeferringOracleChecker(cfg)
+        g = torch.Generator().manual_seed(3)
+        with AbftInjector(cfg, checker, stats, defer_reports=defer) as inj:
+            for i, (m, k, n) in enumerate(shapes):
+                stats.set_phase("prefill" if i < 2 else "decode")
+                F.linear((torch.randn(m, k, generator=g) * 0.1).bfloat16(),
+                         (torch.randn(n, k, generator=g) * 0.1).bfloat16())
+            if defer:
+                assert stats.total_checks == 0 and all(r.reads == 0 for r in checker.reports)
+                assert len(inj._pending) == len(shapes)
+        if defer:
+            assert all(r.reads == 1 for r in checker.reports) and len(checker.reports) == len(shapes)
+        s = stats.export_summary()
+        summaries.append((s["abft"]["checks_total"], s["abft"]["fail_total"], s["abft"]["checks_by_phase"],
+                          s["abft"]["fails_by_phase"], s["fault_injection"]))
+    assert summaries[0] == summaries[1]
+    assert summaries[0][2] == {"prefill": 2, "decode": 2}
