@@ -541,9 +541,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  if (blockIdx.x == 0 && threadIdx.x == 0 && p.report != nullptr) {
-    // Reset the header, then publish this launch's tag: other CTAs touch the
-    // report only after they have seen the tag (report_ready).
+  if (blockIdx.x == 0 && threadIdx.x == 32 * (kEpiWarp0 + kEpiWarps - 1) && p.report != nullptr) {
+    // Reset the header, then publish this launch's tag: every other write to
+    // the report waits for the tag (report_ready). An epilogue thread does
+    // it (idle until the first accumulator), so that the producer's first
+    // copy does not wait behind the fence.
     abft_report* r = p.report;
     r->status = 0;
     r->n_faults = 0;
