@@ -20,6 +20,7 @@ from typing import Optional, Tuple
 import torch
 import torch.nn.functional as F
 
+from .. import _native as N
 from .. import ops
 from .config import AbftConfig
 from .stats import CheckResult
@@ -151,7 +152,7 @@ class CheapSumChecker(AbftChecker):
         b_2d: torch.Tensor,
         c_2d: torch.Tensor,
         bias_1d: Optional[torch.Tensor] = None,
-    ) -> "ops.ReportBuffer":
+    ) -> ops.ReportBuffer:
         """Queue the check on the current stream; its report is read later
         (``result(report.read())``), so a caller can defer the host read."""
         a, b, layout, c, bias = _as_lib_operands(a_2d, b_2d, c_2d, bias_1d)
@@ -159,7 +160,7 @@ class CheapSumChecker(AbftChecker):
                               locate=self.locate, bf16_sums=self.cfg.bf16_sums, thr_scale=self.cfg.thr_scale,
                               report=ops.ReportBuffer(self.cfg.report_capacity, a.device))
 
-    def result(self, rep: "N.FaultReport") -> CheckResult:
+    def result(self, rep: N.FaultReport) -> CheckResult:
         """The CheckResult of a report written by ``launch``."""
         located = tuple((r.row, r.col) for r in rep.records if r.row >= 0 and r.col >= 0)
         ok = rep.ref_ok == 1 and (not self.locate or rep.n_faults == 0)
