@@ -67,11 +67,21 @@ enum abft_status {
 #define ABFT_STATUS_OVERFLOW       4u  /* more faults than record slots          */
 #define ABFT_STATUS_DEVICE_TIMEOUT 8u  /* a bounded device wait gave up          */
 #define ABFT_STATUS_REF_FAIL      16u  /* scalar reference-rule check failed     */
+/* Mismatches in so many rows of one 128-row slab of a tile segment (more
+ * than ABFT_SUSPECT_ROWS, or at least 4 and more than half of the slab's
+ * rows) that the checksums or an operand, not single output elements, are
+ * wrong -- e.g. a cached checksum block that no longer matches its weight.
+ * Nothing in such a slab is corrected (its records carry
+ * ABFT_REC_SUPPRESSED instead of ABFT_REC_CORRECTED), so the stored output
+ * is the plain product; re-encode the weight's checksums. */
+#define ABFT_STATUS_SUSPECT       32u
+#define ABFT_SUSPECT_ROWS         16
 
 /* ---- record flags ------------------------------------------------------- */
-#define ABFT_REC_DETECTED  1u
-#define ABFT_REC_LOCATED   2u
-#define ABFT_REC_CORRECTED 4u
+#define ABFT_REC_DETECTED   1u
+#define ABFT_REC_LOCATED    2u
+#define ABFT_REC_CORRECTED  4u
+#define ABFT_REC_SUPPRESSED 8u  /* located, but left uncorrected (ABFT_STATUS_SUSPECT) */
 
 /* One detected fault: the (row, tile-segment) whose checksums disagree.
  * `col` is the located global column, or -1 when the weighted residual did
@@ -199,14 +209,20 @@ size_t abft_checksum_bytes(int64_t N, int64_t K, int32_t tile_n);
 
 /* Per-tile weighted row checksums of B (the "Be" encoding of checkers.py:119,
  * restricted to each output tile and paired with a column-index-weighted
- * copy), as the 8 bf16 rows the fused GEMM appends to each B-operand tile.
- * With checks on, an output tile of width tile_n carries D = tile_n - 8 data
- * columns. out is bf16 [ceil(N/D) * 8, K] row-major; for tile t
- *   v1[k] = sum_j B[t*D + j, k],   v2[k] = sum_j (j+1) B[t*D + j, k]
- * (j over the tile's valid rows, fp32 sums), rows 8t+0..2 hold v1 split into
- * three bf16 terms (hi, mid, lo), rows 8t+3..5 the same for v2, rows 8t+6..7
- * are zero. Cache it per weight. Replaces the per-call `b_2d.sum(dim=1)`
- * of checkers.py:119. */
+ * and a signed copy), as the 8 bf16 rows the fused GEMM appends to each
+ * B-operand tile. With checks on, an output tile of width tile_n carries
+ * D = tile_n - 8 data columns. out is bf16 [ceil(N/D) * 8, K] row-major; for
+ * tile t, with j over the tile's valid rows and fp32 sums,
+ *   v1[k] = sum_j B[t*D + j, k]
+ *   v2[k] = sum_j (j+1) B[t*D + j, k]
+ *   v3[k] = sum_j sg(j) B[t*D + j, k],  sg(j) = (-1)^popcount(j)
+ *           (the Thue-Morse sign of the local column j)
+ * Rows 8t+0..2 hold v1 split into three bf16 terms (hi = bf16(v1),
+ * mid = bf16(v1 - hi), lo = bf16(v1 - hi - mid)), rows 8t+3..5 the same for
+ * v2, rows 8t+6..7 v3 as two terms (hi, v3 - hi). All eight rows are read by
+ * the fused check: a block built with any row left zero reports faults on
+ * clean outputs. Cache it per weight. Replaces the per-call
+ * `b_2d.sum(dim=1)` of checkers.py:119. */
 int abft_encode_weight(const void* B, int64_t N, int64_t K, int64_t ldb,
                        int32_t tile_n, void* out, void* stream);
 

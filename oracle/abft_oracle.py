@@ -30,8 +30,13 @@ import numpy as np
 REC_DETECTED = 1
 REC_LOCATED = 2
 REC_CORRECTED = 4
+REC_SUPPRESSED = 8
 
 TILE_M = 128
+# A slab of TILE_M rows in one tile column whose mismatching rows exceed
+# this count (or number at least 4 and more than half of its valid rows)
+# is left uncorrected: the checksums, not single elements, are wrong.
+SUSPECT_ROWS = 16
 
 
 # ---------------------------------------------------------------- bf16 helpers
@@ -235,6 +240,7 @@ def rowcheck_gemm(
     thr_abs: float = 0.0,
     inject: Sequence[Tuple[int, int, float]] = (),
     correct: bool = True,
+    checksum_weight: Optional[np.ndarray] = None,
 ) -> RowcheckResult:
     """Restatement of the fused kernel's checksum epilogue.
 
@@ -247,8 +253,14 @@ def rowcheck_gemm(
       detected: |res1| > thr or |res2| > thr * ncols
       located:  |res1| > thr, p = res2/res1 within 0.1 of an integer in [1, ncols]
                 and |res3 - sg(p-1) res1| <= res1 / 2
-                -> column p-1; corrected (if enabled) by acc[i, col] -= res1.
+                -> column p-1; corrected (if enabled) by acc[i, col] -= res1,
+                unless the slab of TILE_M rows holding row i has more than
+                SUSPECT_ROWS mismatching rows in this tile column (or at
+                least 4 and more than half of its valid rows): then the
+                record is flagged suppressed and nothing is changed.
     Output = bf16(acc (+ bias)).
+    ``checksum_weight`` (default ``w``) is the weight the checksums were
+    encoded from: another one models a stale cached checksum block.
     """
     a = np.asarray(a, dtype=np.float64)
     w = np.asarray(w, dtype=np.float64)
@@ -259,7 +271,7 @@ def rowcheck_gemm(
         acc[r, c] += d
     fixed = acc.copy()
     tk = thr_k(thr_scale, k)
-    v1, v2, v3 = encode_weight(w, tile_n)
+    v1, v2, v3 = encode_weight(w if checksum_weight is None else checksum_weight, tile_n)
     records: List[Tuple[int, int, int]] = []
     residuals: Dict[Tuple[int, int], Tuple[float, float, float]] = {}
     for t in range(v1.shape[0]):
@@ -293,8 +305,14 @@ def rowcheck_gemm(
                         col = c
                         flags |= REC_LOCATED
             if col >= 0 and correct:
-                fixed[i, c0 + col] -= res1[i]
-                flags |= REC_CORRECTED
+                s0 = (int(i) // TILE_M) * TILE_M
+                nd = int(det[s0:s0 + TILE_M].sum())
+                valid = min(TILE_M, m - s0)
+                if nd > SUSPECT_ROWS or (nd >= 4 and 2 * nd > valid):
+                    flags |= REC_SUPPRESSED
+                else:
+                    fixed[i, c0 + col] -= res1[i]
+                    flags |= REC_CORRECTED
             records.append((int(i), c0 + col if col >= 0 else -1, flags))
             residuals[(int(i), t)] = (float(res1[i]), float(res2[i]), float(thr[i]))
     out = fixed if bias is None else fixed + np.asarray(bias, np.float64)[None, :]

@@ -1,11 +1,12 @@
 """Write the golden fixtures of the reference's own ABFT path.
 
-Run in the build container, where the reference is mounted read-only:
+Run where a checkout of the reference is available (read-only is enough),
+giving its root directory:
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <reference checkout>
 
-It imports the reference package ``abft`` (pytorch/abft) and records, on
-seeded CPU bf16 inputs:
+(or set ABFT_REFERENCE_ROOT). It imports the reference package ``abft``
+(pytorch/abft) and records, on seeded CPU bf16 inputs:
 
   ref_checker_cases.npz / .json
       CheapSumChecker.check results (python backend,
@@ -16,6 +17,11 @@ seeded CPU bf16 inputs:
       (pytorch/abft/injector.py:19-189) produces for several seeds,
       probabilities and sample rates, plus one export_summary()
       (pytorch/abft/stats.py:175-220).
+  ref_config1_cases.json
+      CheapSumChecker.check results at the BASELINE config-1 size
+      (A[512 x 4096] . B[4096 x 4096], seeds 0-4, clean and with one
+      +2^8 max|C| fault), with SHA-256 digests of the regenerated inputs
+      (tests/golden/baseline_inputs.py) instead of the tensors.
 
 Nothing under tests/ reads the reference at test time: only these fixtures.
 """
@@ -23,6 +29,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import os
 import random
 import sys
 from pathlib import Path
@@ -139,11 +146,52 @@ def run_injector(abft):
     return out, summary
 
 
+CONFIG1_SEEDS = [0, 1, 2, 3, 4]
+
+
+def run_config1(abft):
+    """The reference's check at config 1, clean and with one seeded fault."""
+    import baseline_inputs as BI
+    from abft.checkers import OpMeta
+
+    checker = abft.CheapSumChecker(abft.AbftConfig(enable=True))
+    m, k, n = BI.CONFIG1["M"], BI.CONFIG1["K"], BI.CONFIG1["N"]
+    out = []
+    for seed in CONFIG1_SEEDS:
+        a_bits, w_bits = BI.gemm_inputs(seed, m, k, n)
+        c_bits = BI.product_bits(a_bits, w_bits)
+        idx, mag = BI.fault_for(seed, c_bits)
+
+        def t(bits):
+            return torch.from_numpy(bits.view(np.int16).copy()).view(torch.bfloat16)
+
+        a, w, c = t(a_bits), t(w_bits), t(c_bits)
+        cf = c.clone()
+        cf.view(-1)[idx] += mag  # the reference injector's update (injector.py:72-73)
+        for fault, cc in ((False, c), (True, cf)):
+            res = checker.check(a, w.t(), cc, OpMeta("linear", "prefill", "config1"))
+            out.append({
+                "seed": seed, "M": m, "K": k, "N": n, "fault": fault,
+                "fault_index": idx if fault else None, "fault_row": idx // n if fault else None,
+                "fault_col": idx % n if fault else None, "fault_magnitude": mag if fault else None,
+                "sha256_a": BI.sha256_bits(a_bits), "sha256_w": BI.sha256_bits(w_bits),
+                "sha256_c": BI.sha256_bits(bits(cc)),
+                "ok": bool(res.ok), "abs_err": res.abs_err, "rel_err": res.rel_err,
+                "abft_corner": res.abft_corner, "sum_c": res.sum_c,
+            })
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("ABFT_REFERENCE_ROOT"),
+                    help="root of a reference checkout (or set ABFT_REFERENCE_ROOT)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference <reference checkout> or set ABFT_REFERENCE_ROOT")
     sys.path.insert(0, str(Path(args.reference) / "pytorch"))
+    sys.path.insert(0, str(HERE))
+    sys.path.insert(0, str(HERE.parent.parent))  # the oracle's package root
     import abft  # the reference package
 
     torch.set_num_threads(1)
@@ -153,7 +201,9 @@ def main():
     inj, summary = run_injector(abft)
     (HERE / "ref_injector_sequences.json").write_text(json.dumps({"configs": inj, "summary_config0": summary},
                                                                  indent=1))
-    print(f"wrote {len(meta)} checker cases and {len(inj)} injector sequences to {HERE}")
+    cfg1 = run_config1(abft)
+    (HERE / "ref_config1_cases.json").write_text(json.dumps(cfg1, indent=1))
+    print(f"wrote {len(meta)} checker cases, {len(inj)} injector sequences and {len(cfg1)} config-1 cases to {HERE}")
 
 
 if __name__ == "__main__":

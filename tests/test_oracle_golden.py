@@ -183,3 +183,51 @@ def test_locate_post_hoc_single_fault():
     c2 = c.copy()
     c2[17, 33] += 5.0
     assert O.locate_post_hoc(a, w.T, c2, b) == [(17, 33)]
+
+
+# ------------------------------------------------ BASELINE config 1 (512x4096x4096)
+@pytest.fixture(scope="module")
+def config1_cases(golden_dir):
+    return json.load(open(os.path.join(golden_dir, "ref_config1_cases.json")))
+
+
+def _config1_tensors(seed):
+    from tests.golden import baseline_inputs as BI
+
+    c1 = BI.CONFIG1
+    a_bits, w_bits = BI.gemm_inputs(seed, c1["M"], c1["K"], c1["N"])
+    c_bits = BI.product_bits(a_bits, w_bits)
+    return BI, a_bits, w_bits, c_bits
+
+
+def test_config1_inputs_regenerate_bit_exact(config1_cases):
+    """The seeded inputs of the fixtures are reproduced here (digests)."""
+    for seed in sorted({c["seed"] for c in config1_cases})[:2]:
+        BI, a_bits, w_bits, c_bits = _config1_tensors(seed)
+        case = next(c for c in config1_cases if c["seed"] == seed and not c["fault"])
+        assert BI.sha256_bits(a_bits) == case["sha256_a"]
+        assert BI.sha256_bits(w_bits) == case["sha256_w"]
+        assert BI.sha256_bits(c_bits) == case["sha256_c"]
+
+
+def test_config1_cheap_sum_bf16_emulation_matches_reference(config1_cases):
+    """The oracle's bf16 emulation reproduces the reference's CheapSumChecker
+    (pytorch/abft/checkers.py:96-126) bit for bit at the config-1 size, clean
+    and with the seeded +2^8 max|C| fault -- including the seed whose clean
+    rel_err lands exactly on the bf16-rounded 1e-2 tolerance."""
+    for seed in sorted({c["seed"] for c in config1_cases}):
+        BI, a_bits, w_bits, c_bits = _config1_tensors(seed)
+        a = O.bf16_bits_to_f32(a_bits)
+        w = O.bf16_bits_to_f32(w_bits)
+        for case in (c for c in config1_cases if c["seed"] == seed):
+            cc = O.bf16_bits_to_f32(c_bits).copy()
+            if case["fault"]:
+                idx, mag = BI.fault_for(seed, c_bits)
+                assert (idx, mag) == (case["fault_index"], case["fault_magnitude"])
+                flat = cc.reshape(-1)
+                flat[idx] = O.bf16_round(np.array([flat[idx] + np.float32(mag)], np.float32))[0]
+                assert BI.sha256_bits(O.f32_to_bf16_bits(cc)) == case["sha256_c"]
+            r = O.cheap_sum_check(a, w.T, cc, emulate_bf16=True)
+            got = (r.ok, r.abs_err, r.rel_err, r.abft_corner, r.sum_c)
+            want = (case["ok"], case["abs_err"], case["rel_err"], case["abft_corner"], case["sum_c"])
+            assert got == want, (seed, case["fault"], got, want)

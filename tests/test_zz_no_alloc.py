@@ -22,12 +22,15 @@ pytestmark = pytest.mark.gpu
 
 
 def _args(a, b, c, bias, report, flags):
+    """B is [N, K] (an nn.Linear weight) when it has a's K columns, else
+    [K, N] (the reference checker's b_2d)."""
     args = N.CheckArgs()
     args.A, args.B, args.C = a.data_ptr(), b.data_ptr(), c.data_ptr()
     args.bias = None if bias is None else bias.data_ptr()
-    args.M, args.N, args.K = a.shape[0], b.shape[0], a.shape[1]
+    kn = 0 if b.shape[1] == a.shape[1] else 1
+    args.M, args.N, args.K = a.shape[0], c.shape[1], a.shape[1]
     args.lda, args.ldb, args.ldc = a.stride(0), b.stride(0), c.stride(0)
-    args.b_kn = 0
+    args.b_kn = kn
     args.flags = flags
     args.tol_abs, args.tol_rel, args.thr_scale = 1e-2, 1e-2, 1e-3
     args.report, args.report_capacity = report.data_ptr(), report.capacity
@@ -82,6 +85,29 @@ def test_noalloc_matches_workspace_entry_on_two_calls(cuda_device):
     _same(second, _with_workspace(a, w, faulty, bias, flags, dev))
     assert first.n_faults == 0 and first.ref_ok == 1
     assert second.coords() == [(17, 333)] and second.ref_ok == 0
+
+
+@pytest.mark.parametrize("flags", [N.CHECK_LOCATE, N.CHECK_BF16_SUMS, 0])
+def test_noalloc_kn_layout_matches_workspace_entry_on_two_calls(cuda_device, flags):
+    """B given as [K, N] (b_kn = 1): its column sums go through the part of
+    the array sized for the larger of the two partial-sum layouts."""
+    dev = cuda_device
+    g = torch.Generator().manual_seed(43)
+    m, n, k = 256, 1528, 776
+    a = (torch.randn(m, k, generator=g) * k ** -0.5).bfloat16().to(dev)
+    b_kn = (torch.randn(k, n, generator=g) * k ** -0.5).bfloat16().to(dev)
+    clean = (a.float() @ b_kn.float()).bfloat16()
+    faulty = clean.clone()
+    faulty[201, 1400] -= 6.0
+    first = _no_alloc(a, b_kn, faulty, None, flags, dev)
+    second = _no_alloc(a, b_kn, clean, None, flags, dev)
+    _same(first, _with_workspace(a, b_kn, faulty, None, flags, dev))
+    _same(second, _with_workspace(a, b_kn, clean, None, flags, dev))
+    assert first.ref_ok == 0 and second.n_faults == 0
+    if flags & N.CHECK_LOCATE:
+        assert first.coords() == [(201, 1400)]
+    else:
+        assert first.n_faults == 0 and first.records == []
 
 
 def test_noalloc_rejects_shapes_beyond_its_scratch(cuda_device):

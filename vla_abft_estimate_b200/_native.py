@@ -29,10 +29,13 @@ STATUS_UNLOCATED = 2
 STATUS_OVERFLOW = 4
 STATUS_DEVICE_TIMEOUT = 8
 STATUS_REF_FAIL = 16
+STATUS_SUSPECT = 32
+SUSPECT_ROWS = 16
 
 REC_DETECTED = 1
 REC_LOCATED = 2
 REC_CORRECTED = 4
+REC_SUPPRESSED = 8
 
 MAX_INJECT = 64
 REPORT_HEADER_BYTES = 64
@@ -213,6 +216,12 @@ class FaultRecord:
     def corrected(self) -> bool:
         return bool(self.flags & REC_CORRECTED)
 
+    @property
+    def suppressed(self) -> bool:
+        """Located, but left uncorrected: its slab mismatched in too many
+        rows for single faults (stale checksums or a bad operand)."""
+        return bool(self.flags & REC_SUPPRESSED)
+
 
 @dataclass
 class FaultReport:
@@ -242,6 +251,13 @@ class FaultReport:
     @property
     def device_timeout(self) -> bool:
         return bool(self.status & STATUS_DEVICE_TIMEOUT)
+
+    @property
+    def suspect(self) -> bool:
+        """Some slab mismatched in so many rows that nothing in it was
+        corrected: the checksums (e.g. a cached block of a weight changed
+        behind the cache's back) or an operand are wrong."""
+        return bool(self.status & STATUS_SUSPECT)
 
     def coords(self) -> List[tuple]:
         """Sorted (row, col) of every stored record."""
@@ -281,5 +297,7 @@ class FaultReport:
         status = (STATUS_FAULT if f else 0) | (STATUS_UNLOCATED if f > loc else 0)
         status |= STATUS_OVERFLOW if len(recs) < f and (self.status & STATUS_OVERFLOW) else 0
         status |= self.status & STATUS_DEVICE_TIMEOUT
+        if any(r.suppressed for r in recs) or (self.status & STATUS_SUSPECT and len(recs) < f):
+            status |= STATUS_SUSPECT
         return FaultReport(status, f, loc, cor, max(f - len(recs), 0), self.capacity, self.tile_m, self.tile_n,
                            records=recs)

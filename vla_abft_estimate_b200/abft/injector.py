@@ -33,6 +33,7 @@ instead of forcing a device->host sync per GEMM like the reference (:103).
 from __future__ import annotations
 
 import random
+import weakref
 from contextlib import AbstractContextManager
 from typing import Any, Callable, List, Optional, Tuple
 
@@ -75,23 +76,67 @@ def result_from_report(rep: N.FaultReport) -> CheckResult:
 class WeightChecksumCache:
     """Per-weight checksum blocks (``ops.encode_weight``), reused across calls.
 
-    Keyed by storage pointer, shape, strides, tile width and the tensor's
-    version counter, so an in-place update of the weight re-encodes it.
+    The reference recomputes ``b_2d.sum(dim=1)`` on every call
+    (pytorch/abft/checkers.py:119); this cache encodes a weight once. An
+    entry is found by (address, shape, strides, tile width, device) and is
+    used only while it still describes the same memory and contents:
+
+    * it holds a weak reference to the weight's storage (torch keeps one
+      storage object per allocation, shared by every view of it). When the
+      weight is freed the entry is dropped, so a new tensor that the
+      allocator places at the same address is encoded afresh instead of
+      inheriting another tensor's checksums;
+    * it records the tensor's version counter (shared with its views),
+      which every in-place op through them bumps (``copy_`` under
+      ``no_grad``, optimizer steps), so such an update re-encodes.
+
+    Writes that bypass the version counter (``weight.data.copy_(...)``,
+    writes through another framework or a raw pointer) cannot be seen here;
+    call ``invalidate(weight)`` (or ``clear()``) after them. If that is
+    forgotten, the kernel still does not corrupt the output: the stale
+    checksums make most rows of a slab mismatch, which the kernel reports
+    as ``STATUS_SUSPECT`` without correcting anything, and the injector
+    then clears this cache.
     """
 
     def __init__(self, max_entries: int = 4096):
         self.max_entries = max_entries
         self._d: dict = {}
 
+    @staticmethod
+    def _key(weight: torch.Tensor, tile_n: int) -> tuple:
+        return (weight.data_ptr(), tuple(weight.shape), weight.stride(), tile_n, weight.get_device())
+
     def get(self, weight: torch.Tensor, tile_n: int) -> torch.Tensor:
-        key = (weight.data_ptr(), weight.shape, weight.stride(), weight._version, tile_n, weight.get_device())
-        v = self._d.get(key)
-        if v is None:
-            if len(self._d) >= self.max_entries:
-                self._d.pop(next(iter(self._d)))
-            v = ops.encode_weight(weight, tile_n)
-            self._d[key] = v
+        key = self._key(weight, tile_n)
+        storage = weight.untyped_storage()
+        e = self._d.get(key)
+        if e is not None and e[0]() is storage and e[1] == weight._version:
+            return e[2]
+        if e is None and len(self._d) >= self.max_entries:
+            self._d.pop(next(iter(self._d)))
+        v = ops.encode_weight(weight, tile_n)
+        d = self._d
+
+        def _drop(ref, key=key, d=d):
+            # the storage is gone: forget its checksums (unless a newer
+            # entry for a new tensor at that address replaced this one)
+            cur = d.get(key)
+            if cur is not None and cur[0] is ref:
+                d.pop(key, None)
+
+        self._d[key] = (weakref.ref(storage, _drop), weight._version, v)
         return v
+
+    def invalidate(self, weight: torch.Tensor) -> None:
+        """Forget every entry of ``weight``'s address and shape (after a
+        write the version counter does not see, e.g. ``.data.copy_``)."""
+        ptr, shape, dev = weight.data_ptr(), tuple(weight.shape), weight.get_device()
+        for key in [k for k in list(self._d) if k[0] == ptr and k[1] == shape and k[4] == dev]:
+            self._d.pop(key, None)
+
+    def __len__(self) -> int:
+        return len(self._d)
 
     def clear(self) -> None:
         self._d.clear()
@@ -126,6 +171,7 @@ class _ReportArena:
         self.slots = slots
         self.chunks: List[torch.Tensor] = []
         self.used = 0  # slots taken in the last chunk
+        self.suspect = False  # a drained report had STATUS_SUSPECT (stale checksums?)
 
     def take(self) -> "_Slot":
         if not self.chunks or self.used == self.slots:
@@ -146,8 +192,12 @@ class _ReportArena:
             host = chunk[: n * self.slot_bytes].cpu().numpy().reshape(n, self.slot_bytes)
             n_faults = host[:, 4:8].copy().view(np.uint32)[:, 0]
             for j in range(n):
-                results.append(_CLEAN_RESULT if n_faults[j] == 0
-                               else result_from_report(N.FaultReport.from_bytes(host[j].tobytes())))
+                if n_faults[j] == 0:
+                    results.append(_CLEAN_RESULT)
+                    continue
+                rep = N.FaultReport.from_bytes(host[j].tobytes())
+                self.suspect |= rep.suspect
+                results.append(result_from_report(rep))
         # keep the first chunk for the next forward
         self.chunks = self.chunks[:1]
         self.base = self.chunks[0].data_ptr() if self.chunks else 0
@@ -219,6 +269,12 @@ class AbftInjector(AbstractContextManager):
         if not pending:
             return
         reports = {dev: iter(arena.drain()) for dev, arena in self._arenas.items()}
+        if any(arena.suspect for arena in self._arenas.values()):
+            # a slab mismatched in most rows: cached checksums may be stale
+            # (a weight written behind the version counter); re-encode all
+            self.checksums.clear()
+            for arena in self._arenas.values():
+                arena.suspect = False
         keys: dict = {}
         saved = self.stats.current_phase
         try:
@@ -429,8 +485,11 @@ class AbftInjector(AbstractContextManager):
                 if self.defer_reports:
                     self._pending.append((dix, "linear", self.stats.current_phase, (m, k, n), injected, None))
                 else:
+                    host_rep = rep.read()
+                    if host_rep.suspect:
+                        self.checksums.clear()
                     self.stats.record_check(op_name="linear", shape_key=f"A{(m, k)}_B{(k, n)}_C{(m, n)}",
-                                            result=result_from_report(rep.read()), injected=injected)
+                                            result=result_from_report(host_rep), injected=injected)
             if self.cfg.dump_file:
                 self._maybe_dump_tensors("linear", f"A{(m, k)}_B{(k, n)}_C{(m, n)}", x.reshape(m, k), weight.t(),
                                          out.reshape(m, n), bias)

@@ -490,6 +490,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* drain = xfree + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::kOffMisc + 4);
+  // Mismatching rows of the tile slab in the epilogue, one counter per
+  // parity of the row-partial exchange (two tiles in flight at most).
+  uint32_t* ndet = reinterpret_cast<uint32_t*>(smem + Cfg::kOffMisc + 8);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -512,6 +515,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(xfree, kEpiThreads);
     mbar_init(drain, 1);
     *abort_flag = 0;
+    ndet[0] = 0u;
+    ndet[1] = 0u;
     fence_barrier_init();
   }
   if (blockIdx.x == 0 && p.bcounts != nullptr) {
@@ -1097,6 +1102,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           xchg[t * kBM + r] = make_float4(s1, s2, amax, s3);
           mbar_arrive(xbar);
           if (!mbar_wait(xbar, xph, abort_flag)) aborted = true;
+          // Everyone has finished the previous tile, whose slab counter (the
+          // other parity) is free again: clear it for the tile after this one.
+          if (!aborted && ep == 0 && lane == 0) ndet[xph ^ 1u] = 0u;
         }
         if (!aborted) {
           float res1 = 0.f, res2 = 0.f, res3 = 0.f, tmax = 0.f;
@@ -1108,11 +1116,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             res3 += pj.w;
             tmax = fmaxf(tmax, pj.z);
           }
-          mbar_arrive(xfree);
           const float thr = fmaf(p.thr_k, tmax, p.thr_abs);
           const bool det = row_ok && (fabsf(res1) > thr || fabsf(res2) > thr * static_cast<float>(ncols));
+          // Count the slab's mismatching rows (one share per row) before
+          // releasing the exchange buffer: once every thread has arrived on
+          // xfree the count is complete.
+          if (det && t == 0) atomicAdd(&ndet[xph], 1u);
+          mbar_arrive(xfree);
           if (det) {
             uint32_t flags = ABFT_REC_DETECTED;
+            uint32_t st_extra = 0u;
             int col = -1;
             if (fabsf(res1) > thr) {
               const float pos = res2 / res1;
@@ -1127,16 +1140,27 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
             if (col >= 0 && (p.mode & ABFT_MODE_CORRECT)) {
-              fix_col = col;
-              fix_delta = res1;
-              flags |= ABFT_REC_CORRECTED;
+              // A single upset touches a few rows; a mismatch in most rows of
+              // the slab means stale checksums or a bad operand, where a
+              // "correction" would corrupt a right output: leave it as is.
+              uint32_t nd = ~0u;
+              if (mbar_wait(xfree, xph, abort_flag)) nd = ndet[xph];
+              const uint32_t valid = static_cast<uint32_t>(min(kBM, p.M - row0));
+              if (nd > static_cast<uint32_t>(ABFT_SUSPECT_ROWS) || (nd >= 4u && 2u * nd > valid)) {
+                flags |= ABFT_REC_SUPPRESSED;
+                st_extra = ABFT_STATUS_SUSPECT;
+              } else {
+                fix_col = col;
+                fix_delta = res1;
+                flags |= ABFT_REC_CORRECTED;
+              }
             }
             if (t == 0 && report_ready(p, abort_flag)) {
               abft_report* rep = p.report;
               const uint32_t slot = atomicAdd(&rep->n_faults, 1u);
               if (flags & ABFT_REC_LOCATED) atomicAdd(&rep->n_located, 1u);
               if (flags & ABFT_REC_CORRECTED) atomicAdd(&rep->n_corrected, 1u);
-              uint32_t st = ABFT_STATUS_FAULT | ((flags & ABFT_REC_LOCATED) ? 0u : ABFT_STATUS_UNLOCATED);
+              uint32_t st = ABFT_STATUS_FAULT | st_extra | ((flags & ABFT_REC_LOCATED) ? 0u : ABFT_STATUS_UNLOCATED);
               if (slot < static_cast<uint32_t>(p.capacity)) {
                 abft_fault_record* rec = reinterpret_cast<abft_fault_record*>(rep + 1) + slot;
                 if (!p.swap) {

@@ -13,6 +13,7 @@ Functions
 """
 from __future__ import annotations
 
+import collections
 import ctypes
 import functools
 import math
@@ -86,15 +87,25 @@ def _device_index(device: Optional[torch.device]) -> int:
     return device.index
 
 
-_WORKSPACES: dict = {}
+_WORKSPACES: "collections.OrderedDict[tuple, torch.Tensor]" = collections.OrderedDict()
+_MAX_WORKSPACES = 64
 
 
 def _workspace(device: torch.device, nbytes: int, stream: Optional[int] = None) -> torch.Tensor:
     """Scratch for the current stream of ``device``, grown on demand.
 
-    One buffer per (device, stream): calls on one stream run in order, so
-    reusing it is safe; a buffer replaced by a larger one is freed in stream
+    One buffer per (device, raw stream handle), allocated while that stream
+    is current. Calls on one stream run in order, so reusing the buffer is
+    safe, and a buffer that is replaced or evicted is freed in that stream's
     order by the caching allocator.
+
+    Keying on the raw handle is safe when a handle is recycled: torch's own
+    streams come from a fixed pool and are never destroyed (two Stream
+    objects with one handle share one in-order queue), and the driver only
+    hands out a destroyed stream's handle again once the work queued on it
+    has completed. The dictionary is bounded (least recently used first out)
+    so that callers cycling through many external streams do not keep one
+    buffer each alive.
     """
     if stream is None:
         stream = torch.cuda.current_stream(device).cuda_stream
@@ -103,6 +114,9 @@ def _workspace(device: torch.device, nbytes: int, stream: Optional[int] = None) 
     if ws is None or ws.numel() < nbytes:
         ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
         _WORKSPACES[key] = ws
+        if len(_WORKSPACES) > _MAX_WORKSPACES:
+            _WORKSPACES.popitem(last=False)
+    _WORKSPACES.move_to_end(key)
     return ws
 
 
@@ -147,9 +161,10 @@ def pick_tile_m(m: int, n: int, k: int, tile_n: int, device: Optional[torch.devi
 def encode_weight(weight: torch.Tensor, tile_n: int) -> torch.Tensor:
     """Per-tile checksum block of ``weight`` [N, K] for tile width ``tile_n``.
 
-    Returns bf16 [ceil(N / tile_n) * 8, K]: for each tile, the plain and the
-    column-index-weighted row checksums, each as three bf16 terms, and two
-    zero rows (the operand of the fused kernel's check MMA).
+    Returns bf16 [ceil(N / (tile_n - 8)) * 8, K]: for each tile, the plain
+    and the column-index-weighted row checksums, each as three bf16 terms,
+    and the Thue-Morse signed checksum as two bf16 terms (the 8 extra
+    B-operand rows of the fused kernel's tile).
     """
     _require_bf16_cuda("weight", weight, 2)
     n, k = weight.shape
