@@ -7,12 +7,17 @@ Workload (one step = one protected GEMM):
   detect + locate + correct in the kernel. A is replicated; B[N, K] with
   N = 8192 * n_gpus is split by columns across the ranks (weak scaling: at 8
   GPUs this is the sharded A[8192 x 8192] . B[8192 x 65536] configuration).
-  Each step ends with one all-gather of the ranks' fault reports (NCCL).
+  The fault reports of every 16 consecutive steps are exchanged in one
+  all-gather (NCCL); detection and correction need no exchange.
 
 Printed: one JSON line (rank 0). value = whole-job TFLOP/s (2 M N K / step
 time, max over ranks); roofline from CUDA-event timing of the fused kernel
 alone; e2e through the public API with A and B_r copied from pinned host
-memory every step and the gathered fault reports read back.
+memory every step and the gathered fault reports read back. On one GPU the
+line also carries the other BASELINE metrics, measured in the same process:
+config 1 (one 512x4096x4096 protected GEMM) and 16384^3, each against
+cuBLAS and the unchecked kernel, and the Qwen2-7B prefill-512 tokens/s with
+every linear protected (--no-extras skips them).
 
 ``--impl reference`` times the reference's CPU path (torch.matmul + the
 python-backend corner check, restated in oracle/ref_port.py) on a row sample
@@ -51,6 +56,8 @@ def parse_args():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--size", type=int, default=8192, help="M = K = per-GPU N")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the config-1, 16384^3 and Qwen2-7B prefill points of the default 1-GPU line")
     ap.add_argument("--sweep", action="store_true",
                     help="one JSON line per shape of the square sweep, the 512x4096x4096 case and the "
                          "Qwen2-7B layer GEMMs: checked / unchecked TFLOP/s and 1- and 4-fault outcomes")
@@ -96,38 +103,105 @@ def load_traffic(workload: str):
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons, sampled in the background."""
+    """SM clock, power and clock-event reasons of this process's GPUs,
+    polled about every millisecond by a background thread through NVML
+    (read-only queries), with a time stamp per sample so that a summary can
+    cover exactly a timed region. Falls back to ``nvidia-smi -lms`` when NVML
+    is unavailable."""
 
-    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4), ("hw_power_brake_slowdown", 0x80))
+    SMI_FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, uuids, period_ms=25):
-        self.uuids = {u.lower() for u in uuids}
-        self.period_ms = period_ms
-        self.samples = []
-        self.proc = None
+    def __init__(self, uuids, period_ms=1.0):
+        self.uuids = [u if u.lower().startswith("gpu-") else f"GPU-{u}" for u in uuids]
+        self.period = period_ms * 1e-3
+        self.samples = []  # (time.time(), sm_mhz, max_mhz, power_w, reasons bitmask or -1)
+        self.source = None
+        self.errors = 0
+        self.first_error = None
+        self._stop = threading.Event()
         self.thread = None
+        self.proc = None
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          f"-lms={self.period_ms}"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
-                                         text=True)
-        except OSError:
-            self.proc = None
+            import pynvml
+
+            pynvml.nvmlInit()
+            handles = [pynvml.nvmlDeviceGetHandleByUUID(u) for u in self.uuids]
+            if not handles:
+                raise RuntimeError("no device")
+            self._nvml = pynvml
+            self._handles = handles
+            self._max = [pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM) for h in handles]
+            self.source = f"nvml, {self.period * 1e3:.0f} ms"
+            self.thread = threading.Thread(target=self._poll_nvml, daemon=True)
+            self.thread.start()
             return
-        self.thread = threading.Thread(target=self._read, daemon=True)
+        except Exception:  # noqa: BLE001 - fall back to nvidia-smi
+            pass
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.SMI_FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms=25"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            return
+        self.source = "nvidia-smi, 25 ms"
+        self.thread = threading.Thread(target=self._read_smi, daemon=True)
         self.thread.start()
 
-    def _read(self):
-        for line in self.proc.stdout:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
+    def _reasons(self, h):
+        """Clock-event reason bits (newer drivers' name first), or None."""
+        nv = self._nvml
+        for fn in ("nvmlDeviceGetCurrentClocksEventReasons", "nvmlDeviceGetCurrentClocksThrottleReasons"):
+            f = getattr(nv, fn, None)
+            if f is None:
                 continue
-            self.samples.append((time.time(), parts))
+            try:
+                return int(f(h))
+            except Exception as e:  # noqa: BLE001
+                self._note_error(f"{fn}: {e}")
+        return None
+
+    def _note_error(self, msg):
+        self.errors += 1
+        if self.first_error is None:
+            self.first_error = msg
+
+    def _poll_nvml(self):
+        nv = self._nvml
+        while not self._stop.is_set():
+            t = time.time()
+            for h, mx in zip(self._handles, self._max):
+                try:
+                    sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                except Exception as e:  # noqa: BLE001
+                    self._note_error(f"clock: {e}")
+                    continue
+                try:
+                    pw = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+                except Exception:  # noqa: BLE001
+                    pw = float("nan")
+                rs = self._reasons(h)
+                self.samples.append((t, sm, float(mx), pw, -1 if rs is None else rs))
+            time.sleep(self.period)
+
+    def _read_smi(self):
+        wanted = {u.lower().replace("gpu-", "") for u in self.uuids}
+        for line in self.proc.stdout:
+            p = [x.strip() for x in line.split(",")]
+            if len(p) < 9 or (wanted and p[0].lower().replace("gpu-", "") not in wanted):
+                continue
+            try:
+                bits = sum(m for (_, m), v in zip(self.REASONS[:4], p[5:9]) if v.lower() == "active")
+                self.samples.append((time.time(), float(p[1]), float(p[2]), float(p[3]), bits))
+            except ValueError:
+                continue
 
     def stop(self):
+        self._stop.set()
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -138,34 +212,51 @@ class ClockSampler:
             self.thread.join(timeout=5)
 
     def summary(self, t0, t1):
-        def pick(lo, hi):
-            out = []
-            for t, p in self.samples:
-                if lo <= t <= hi and (not self.uuids or p[0].lower().replace("gpu-", "") in self.uuids
-                                      or p[0].lower() in self.uuids):
-                    out.append(p)
-            return out
-
-        window = "timed"
-        rows = pick(t0, t1)
-        if len(rows) < 3:  # timed region shorter than the sampling period: widen to the whole run
-            rows, window = pick(-math.inf, math.inf), "run"
+        """Median SM clock and the union of slowdown reasons over the samples
+        taken in [t0, t1] (wall-clock seconds)."""
+        rows = [s for s in self.samples if t0 <= s[0] <= t1]
+        out = {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": len(rows), "window": "timed",
+               "source": self.source, "window_s": round(t1 - t0, 4)}
+        if self.errors:
+            out["query_errors"] = self.errors
+            out["first_error"] = self.first_error
         if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "window": window}
+            out["samples_in_run"] = len(self.samples)
+            return out
+        out["sm_mhz"] = statistics.median(r[1] for r in rows)
+        out["sm_max_mhz"] = max(r[2] for r in rows)
+        known = [r for r in rows if r[4] >= 0]
+        out["reasons"] = [name for name, bit in self.REASONS if any(r[4] & bit for r in known)]
+        if len(known) < len(rows):
+            out["reasons_unavailable_samples"] = len(rows) - len(known)
+        out["power_w_max"] = max(r[3] for r in rows)
+        return out
 
-        def num(x):
-            try:
-                return float(x)
-            except ValueError:
-                return None
 
-        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
-        smax = [num(r[2]) for r in rows if num(r[2]) is not None]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(smax) if smax else None, "reasons": reasons, "samples": len(rows),
-                "window": window, "power_w_max": max((num(r[3]) or 0.0) for r in rows)}
+def timed_median(fn, iters, flush=None, sleep_cycles=100_000_000):
+    """Median CUDA-event time (ms) of ``fn`` over ``iters`` launches after 3
+    warm-up calls; ``flush`` (a tensor larger than L2) is overwritten before
+    every launch, outside the timed interval. A device-side sleep first lets
+    the host queue every launch ahead of the GPU, so no interval contains
+    host launch latency."""
+    import torch
+
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    torch.cuda._sleep(sleep_cycles)
+    pairs = []
+    for _ in range(iters):
+        if flush is not None:
+            flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        pairs.append((e0, e1))
+    torch.cuda.synchronize()
+    ms = sorted(e0.elapsed_time(e1) for e0, e1 in pairs)
+    return ms[len(ms) // 2]
 
 
 def init_dist(n_gpus):
@@ -231,13 +322,236 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def timed_medians_interleaved(fns, iters, flush, sleep_cycles=100_000_000):
+    """Median CUDA-event time (ms) of each of ``fns``, launched in rounds
+    (fn 0, fn 1, ... then again) so that every variant sees the same clocks
+    and power state; ``flush`` is overwritten before every launch."""
+    import torch
+
+    for fn in fns:
+        for _ in range(3):
+            fn()
+    torch.cuda.synchronize()
+    torch.cuda._sleep(sleep_cycles)
+    ev = [[] for _ in fns]
+    for _ in range(iters):
+        for i, fn in enumerate(fns):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            ev[i].append((e0, e1))
+    torch.cuda.synchronize()
+    out = []
+    for pairs in ev:
+        ms = sorted(e0.elapsed_time(e1) for e0, e1 in pairs)
+        out.append(ms[len(ms) // 2])
+    return out
+
+
+def gemm_point(m, n, k, iters, flush, seed=0):
+    """One BASELINE GEMM configuration on cuda:0: median kernel times (L2
+    flushed before each launch, the variants interleaved) of cuBLAS, the
+    fused kernel with checks off and on (weight checksums cached), and of
+    the checked call that encodes the checksums itself (a fresh weight);
+    then the BASELINE fault runs:
+    clean, 1 and 4 faults of 2^8 max|C| at seeded distinct rows and columns
+    (exact coordinates and corrections required)."""
+    import torch
+
+    from vla_abft_estimate_b200 import _native as N
+    from vla_abft_estimate_b200 import ops
+    from vla_abft_estimate_b200.faults import seeded_fault_positions
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    a = (torch.randn(m, k, device=dev, generator=g) * k ** -0.5).bfloat16()
+    w = (torch.randn(n, k, device=dev, generator=g) * k ** -0.5).bfloat16()
+    out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+    chk = N.MODE_DETECT | N.MODE_CORRECT
+    tn_chk = ops.pick_tile_n(m, n, k, dev, chk)
+    tn_off = ops.pick_tile_n(m, n, k, dev, N.MODE_OFF)
+    cks = ops.encode_weight(w, tn_chk)
+    rep = ops.ReportBuffer(64, dev)
+    t_cublas, t_off, t_chk, t_enc = timed_medians_interleaved([
+        lambda: torch.matmul(a, w.t(), out=out),
+        lambda: ops.abft_gemm(a, w, mode=N.MODE_OFF, out=out, tile_n=tn_off),
+        lambda: ops.abft_gemm(a, w, mode=chk, out=out, tile_n=tn_chk, checksums=cks, report=rep),
+        lambda: ops.abft_gemm(a, w, mode=chk, out=out, tile_n=tn_chk, report=rep),
+    ], iters, flush)
+    c0, r0 = ops.abft_gemm(a, w, mode=chk, tile_n=tn_chk, checksums=cks)
+    r0 = r0.read()
+    delta = 256.0 * c0.float().abs().max().item()
+    faults_ok = {"clean_no_record": r0.n_faults == 0 and r0.status == 0}
+    for count in (1, 4):
+        pos = seeded_fault_positions(m, n, count, seed + count)
+        c, r = ops.abft_gemm(a, w, mode=chk, tile_n=tn_chk, checksums=cks, inject=[(i, j, delta) for i, j in pos])
+        r = r.read()
+        err = (c.float() - c0.float()).abs().max().item() / max(c0.float().abs().max().item(), 1e-30)
+        faults_ok[f"{count}_fault_located_corrected"] = (r.coords() == sorted(pos) and r.n_corrected == count
+                                                          and err <= 1e-2)
+    fl = 2.0 * m * n * k
+    res = {"M": m, "N": n, "K": k, "tile_n": {"unchecked": tn_off, "checked": tn_chk},
+           "cublas_tflops": fl / t_cublas / 1e9, "unchecked_tflops": fl / t_off / 1e9,
+           "checked_tflops": fl / t_chk / 1e9, "overhead_pct": 100.0 * (t_chk / t_off - 1.0),
+           "checked_vs_cublas": t_cublas / t_chk,
+           "checked_encode_included_tflops": fl / t_enc / 1e9,
+           "overhead_encode_included_pct": 100.0 * (t_enc / t_off - 1.0),
+           "us": {"cublas": t_cublas * 1e3, "unchecked": t_off * 1e3, "checked": t_chk * 1e3,
+                  "checked_encode_included": t_enc * 1e3},
+           "fault_check": faults_ok}
+    del a, w, out, cks, c0
+    return res
+
+
+def qwen_prefill_point(reps, warmup, decode_steps=0, cpu_seconds=0.0):
+    """a Qwen2-7B-shaped decoder prefill of 512 tokens
+    (batch 1, random init N(0, 0.02), random token ids) with every nn.Linear
+    through AbftInjector's fused path (reports deferred to one read per
+    forward), against plain torch (cuBLAS) and the same kernel with checks
+    off. Times are medians over ``reps`` forwards: wall time around the
+    forward (host work included), and device time with the host queued
+    ahead behind a device sleep. Then one forward with the injector's
+    random faults (probability 0.05 per linear, +1.0 on the fp32
+    accumulator) and, with ``decode_steps``, single-token decode steps after
+    the prefill."""
+    import contextlib
+
+    import torch
+
+    from vla_abft_estimate_b200.abft import AbftConfig, AbftInjector, AbftStatsCollector, CheapSumChecker
+
+    cfg = QWEN2_7B
+    tokens = 512
+    dev = torch.device("cuda", 0)
+    model = build_qwen2(cfg, dev)
+    ids = torch.randint(0, cfg["vocab"], (tokens,), device=dev, generator=torch.Generator(device=dev).manual_seed(7))
+
+    def timed_forward(ctx_factory):
+        times, gpu_times = [], []
+        out = None
+        with torch.inference_mode():
+            for i in range(warmup + reps):
+                ctx = ctx_factory()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                torch.cuda.synchronize()
+                e0.record()
+                with ctx:
+                    out = model(ids)
+                e1.record()
+                torch.cuda.synchronize()
+                g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                torch.cuda._sleep(100_000_000)
+                g0.record()
+                with ctx:
+                    out = model(ids)
+                    g1.record()
+                torch.cuda.synchronize()
+                if i >= warmup:
+                    times.append(e0.elapsed_time(e1))
+                    gpu_times.append(g0.elapsed_time(g1))
+        return statistics.median(times), out, statistics.median(gpu_times)
+
+    # one injector per leg, reused across repetitions (its weight checksum
+    # cache is what a serving process keeps)
+    stats_chk = AbftStatsCollector()
+    cfg_chk = AbftConfig(enable=True, checker_backend="b200", detect_only=False)
+    inj_chk = AbftInjector(cfg_chk, CheapSumChecker(cfg_chk), stats_chk, defer_reports=True)
+    stats_off = AbftStatsCollector()
+    cfg_off = AbftConfig(enable=True, check_enable=False, checker_backend="b200")
+    inj_off = AbftInjector(cfg_off, CheapSumChecker(cfg_off), stats_off, defer_reports=True)
+
+    t_torch, ref_logits, g_torch = timed_forward(contextlib.nullcontext)
+    t_off, _, g_off = timed_forward(lambda: inj_off)
+    t_chk, chk_logits, g_chk = timed_forward(lambda: inj_chk)
+    summ = stats_chk.export_summary()
+    forwards = 2 * (warmup + reps)
+
+    stats_f = AbftStatsCollector()
+    cfg_f = AbftConfig(enable=True, checker_backend="b200", detect_only=False, inject_fault=True,
+                       inject_probability=0.05, inject_magnitude=1.0, seed=11)
+    inj_f = AbftInjector(cfg_f, CheapSumChecker(cfg_f), stats_f, defer_reports=True)
+    with torch.inference_mode(), inj_f:
+        f_logits = model(ids)
+    torch.cuda.synchronize()
+    fs = stats_f.export_summary()
+
+    res = {
+        "tokens_per_s": {"torch": tokens / (t_torch * 1e-3), "unchecked": tokens / (t_off * 1e-3),
+                         "abft": tokens / (t_chk * 1e-3)},
+        "ms": {"torch": t_torch, "unchecked": t_off, "abft": t_chk},
+        "device_ms": {"torch": g_torch, "unchecked": g_off, "abft": g_chk},
+        "overhead_vs_torch_pct": 100.0 * (t_chk / t_torch - 1.0),
+        "overhead_vs_unchecked_pct": 100.0 * (t_chk / t_off - 1.0),
+        "checked_linears_per_forward": summ["abft"]["checks_total"] // forwards,
+        "clean_detections": summ["abft"]["faults"]["detected_total"],
+        "fault_leg": {"injected": fs["fault_injection"]["injections_total"],
+                      "detected_injections": fs["fault_injection"]["detected_injections_total"],
+                      "faults": {k: v for k, v in fs["abft"]["faults"].items() if k != "located"},
+                      "max_abs_logit_diff_vs_clean": (f_logits.float() - chk_logits.float()).abs().max().item(),
+                      "max_abs_logit": chk_logits.float().abs().max().item(),
+                      "note": "+1.0 on the fp32 accumulator; a fault below the bound tau*sqrt(K)*max|C_row| "
+                              "of its row is by design not flagged"},
+        "logits_max_abs_diff_torch_vs_abft": (ref_logits.float() - chk_logits.float()).abs().max().item(),
+        "reps": reps, "warmup": warmup,
+        "reference_published": {"tokens_per_s_no_abft": 7217, "tokens_per_s_abft_python": 5909,
+                                "source": "pytorch/baseline_7b_prefill512.json:44, "
+                                          "pytorch/abft_7b_prefill512_nsys.json:44 (GPU unrecorded)"},
+    }
+
+    if decode_steps:
+        def timed_decode(ctx_factory):
+            caches = model.new_caches(tokens + decode_steps + 8)
+            with torch.inference_mode():
+                with ctx_factory():
+                    model(ids, caches, 0)
+                nxt = ids[-1:].clone()
+                for i in range(4):
+                    with ctx_factory():
+                        model(nxt, caches, tokens + i)
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for i in range(decode_steps):
+                    with ctx_factory():
+                        model(nxt, caches, tokens + 4 + i)
+                e1.record()
+                torch.cuda.synchronize()
+            return e0.elapsed_time(e1) / decode_steps
+
+        d_torch = timed_decode(contextlib.nullcontext)
+        d_off = timed_decode(lambda: inj_off)
+        d_chk = timed_decode(lambda: inj_chk)
+        res["decode_ms_per_token"] = {"torch": d_torch, "unchecked": d_off, "abft": d_chk,
+                                      "abft_overhead_vs_torch_pct": 100.0 * (d_chk / d_torch - 1.0),
+                                      "note": "after a 512-token prefill into a KV cache; every linear at M = 1 "
+                                              "(operands swapped: weight on the MMA's 128-row side)"}
+    if cpu_seconds > 0:
+        res["cpu_baseline"] = cpu_model_baseline(cfg, tokens, cpu_seconds)
+    linear_flops = 0.0
+    h, it, nh, nkv, hd, V = (cfg["hidden"], cfg["inter"], cfg["heads"], cfg["kv_heads"], cfg["head_dim"],
+                             cfg["vocab"])
+    for k, n in [(h, (nh + 2 * nkv) * hd), (nh * hd, h), (h, 2 * it), (it, h)]:
+        linear_flops += 2.0 * tokens * k * n * cfg["layers"]
+    linear_flops += 2.0 * tokens * h * V
+    res["linear_tflops_abft"] = linear_flops / (t_chk * 1e-3) / 1e12
+    del model
+    torch.cuda.empty_cache()
+    return res
+
+
+EXCHANGE_EVERY = 16  # GEMMs whose fault reports one all-gather exchanges
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
 
     from vla_abft_estimate_b200 import _native as N
     from vla_abft_estimate_b200 import ops
-    from vla_abft_estimate_b200.sharded import ShardedAbftGemm, gather_reports, shard_bounds
+    from vla_abft_estimate_b200.faults import seeded_fault_positions
+    from vla_abft_estimate_b200.sharded import ShardedAbftGemm, shard_bounds
 
     world, rank, local = init_dist(args.gpus)
     dev = torch.device("cuda", local if world > 1 else 0)
@@ -258,25 +572,30 @@ def run_ours(args):
     a = (torch.randn(s, s, device=dev, generator=ga) * s ** -0.5).bfloat16()
     w = (torch.randn(n_r, s, device=dev, generator=gb) * s ** -0.5).bfloat16()
     out = torch.empty(s, n_r, device=dev, dtype=torch.bfloat16)
-    gemm = ShardedAbftGemm(w, c0, mode=N.MODE_DETECT | N.MODE_CORRECT)
+    gemm = ShardedAbftGemm(w, c0, mode=N.MODE_DETECT | N.MODE_CORRECT, exchange_every=EXCHANGE_EVERY)
     off = ShardedAbftGemm(w, c0, mode=N.MODE_OFF)
     tile_n, _ = gemm._checksums_for(s)
     tile_m = ops.pick_tile_m(s, n_r, s, tile_n, dev)
 
-    # fault-detection sanity outside the timed region: one seeded fault per rank
-    from vla_abft_estimate_b200.faults import seeded_fault_positions
-
-    ref_out = gemm(a, out=out)
+    # fault detection outside the timed region: clean, then 1 and 4 seeded
+    # faults of 2^8 max|C| per rank (distinct rows and columns); every
+    # rank's faults must come back located, corrected, in global columns
+    gemm(a, out=out, gather=True)
+    clean_ok = gemm.global_report().n_faults == 0
     delta = 256.0 * out.float().abs().max().item()
-    (fr, fc), = seeded_fault_positions(s, n_r, 1, 100 + rank)
-    gemm(a, out=torch.empty_like(out), inject=[(fr, fc, delta)])
-    grep = gemm.global_report()
-    expected = sorted((r_fr, r_fc + shard_bounds(n_total, world, r)[0])
-                      for r, (r_fr, r_fc) in ((r, seeded_fault_positions(s, shard_bounds(n_total, world, r)[1]
-                                                                              - shard_bounds(n_total, world, r)[0],
-                                                                              1, 100 + r)[0]) for r in range(world)))
-    detect_ok = grep.coords() == expected and grep.n_corrected == world
-    del ref_out
+    faulty = torch.empty_like(out)
+    detect = {}
+    for count in (1, 4):
+        mine = seeded_fault_positions(s, n_r, count, 100 * count + rank)
+        gemm(a, out=faulty, inject=[(i, j, delta) for i, j in mine], gather=True)
+        grep = gemm.global_report()
+        want = []
+        for r in range(world):
+            r0, r1 = shard_bounds(n_total, world, r)
+            want += [(i, j + r0) for i, j in seeded_fault_positions(s, r1 - r0, count, 100 * count + r)]
+        err = (faulty.float() - out.float()).abs().max().item() / max(out.float().abs().max().item(), 1e-30)
+        detect[count] = grep.coords() == sorted(want) and grep.n_corrected == world * count and err <= 1e-2
+    del faulty
 
     # encode cost of B_r's checksums (a fresh weight pays it once)
     e_enc0, e_enc1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -295,10 +614,13 @@ def run_ours(args):
                 pass
         sampler = ClockSampler(uuids)
         sampler.start()
-        time.sleep(0.3)
 
+    # Timed steps: one fused GEMM each; the reports of EXCHANGE_EVERY
+    # consecutive GEMMs are all-gathered in one collective (the ring's last,
+    # partial batch inside the timed region too).
     for _ in range(max(args.warmup, 3)):
         gemm(a, out=out)
+    gemm.exchange()
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
@@ -307,29 +629,34 @@ def run_ours(args):
     t_begin, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     # untimed GPU spin: the host queues the first steps ahead of the GPU
     torch.cuda._sleep(50_000_000)
-    wall0 = time.time()
     t_begin.record()
     for i in range(args.steps):
         starts[i].record()
         gemm(a, out=out, gather=False)
         kends[i].record()
-        gather_reports(gemm.report.tensor, gemm.gathered, None)
+        if (i + 1) % EXCHANGE_EVERY == 0 or i + 1 == args.steps:
+            gemm.exchange()
     t_end.record()
+    # poll with sleeps (not a blocking synchronize) so that the clock
+    # sampler's thread gets the interpreter while the device works
+    while not t_end.query():
+        time.sleep(2e-4)
+    wall1 = time.time()
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
-    wall1 = time.time()
     step_ms = t_begin.elapsed_time(t_end) / args.steps
     kernel_ms = sum(s_.elapsed_time(e_) for s_, e_ in zip(starts, kends)) / args.steps
-    clean = gemm.global_report()
+    clean_timed = all(r.n_faults == 0 for r in gemm.global_reports())
+    wall0 = wall1 - step_ms * args.steps * 1e-3  # the device-timed region, on the wall clock
 
     # overhead: the same kernel with checksums compiled out, launches
     # interleaved with checked ones so that both see the same clocks
     for _ in range(3):
-        off(a, out=out)
+        off(a, out=out, gather=False)
     torch.cuda.synchronize()
     n_pair = min(args.steps, 100)
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(n_pair)]
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(n_pair)]
     torch.cuda._sleep(50_000_000)
     for e in ev:
         e[0].record()
@@ -342,15 +669,16 @@ def run_ours(args):
     chk_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / n_pair
 
     # End to end through the public API with host buffers: every step copies
-    # its A and B_r from pinned host memory and reads its gathered fault
-    # reports back. Two device buffer sets: step i+1's copies run on a copy
-    # stream while step i's GEMM runs (each copy waits until the GEMM that
-    # last read its buffers has finished).
+    # its A and B_r from pinned host memory, encodes B_r's checksums, runs
+    # the GEMM, exchanges the step's fault reports and reads them back. Two
+    # device buffer sets: step i+1's copies run on a copy stream while step
+    # i's GEMM runs (each copy waits until the GEMM that last read its
+    # buffers has finished).
     a_h = a.cpu().pin_memory()
     w_h = w.cpu().pin_memory()
     bufs = [(torch.empty_like(a), torch.empty_like(w)) for _ in range(2)]
     e2e_gemms = [ShardedAbftGemm(wd, c0, mode=N.MODE_DETECT | N.MODE_CORRECT) for _, wd in bufs]
-    rep_h = [torch.empty(gemm.gathered.shape, dtype=torch.uint8).pin_memory() for _ in range(2)]
+    rep_h = [torch.empty(e2e_gemms[0].gathered.shape, dtype=torch.uint8).pin_memory() for _ in range(2)]
     main_stream = torch.cuda.current_stream(dev)
     copy_stream = torch.cuda.Stream(dev)
     copied = [torch.cuda.Event() for _ in range(2)]
@@ -392,20 +720,32 @@ def run_ours(args):
     torch.cuda.synchronize()
     e2e_ms = x0.elapsed_time(x1) / e2e_steps
     enc_ms = e_enc0.elapsed_time(e_enc1) / 5
+    del bufs, e2e_gemms
 
     if sampler is not None:
         sampler.stop()
 
     # max over ranks
     vals = torch.tensor([step_ms, kernel_ms, off_ms, e2e_ms, chk_ms], device=dev, dtype=torch.float64)
+    oks = torch.tensor([int(detect[1]), int(detect[4]), int(clean_ok and clean_timed)], device=dev)
     if world > 1:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-        ok_t = torch.tensor([1 if detect_ok else 0, 1 if clean.n_faults == 0 else 0], device=dev)
-        dist.all_reduce(ok_t, op=dist.ReduceOp.MIN)
-        detect_ok, clean_ok = bool(ok_t[0].item()), bool(ok_t[1].item())
-    else:
-        clean_ok = clean.n_faults == 0
+        dist.all_reduce(oks, op=dist.ReduceOp.MIN)
     step_ms, kernel_ms, off_ms, e2e_ms, chk_ms = [float(x) for x in vals.cpu()]
+    one_ok, four_ok, clean_all = (bool(x) for x in oks.cpu())
+
+    extras = {}
+    if world == 1 and rank == 0 and not args.no_extras:
+        # The other BASELINE metrics, measured in the same process: config 1
+        # (one 512x4096x4096 protected GEMM), the largest square shape, and
+        # the Qwen2-7B prefill-512 tokens/s with every linear protected.
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        it = max(args.steps, 10)
+        extras["config1_512x4096x4096"] = gemm_point(512, 4096, 4096, it, flush)
+        extras["square_16384"] = gemm_point(16384, 16384, 16384, min(it, 10), flush)
+        del flush
+        torch.cuda.empty_cache()
+        extras["qwen2_7b_prefill512"] = qwen_prefill_point(reps=5, warmup=2)
 
     if rank == 0:
         flops_job = 2.0 * s * n_total * s
@@ -424,6 +764,9 @@ def run_ours(args):
             "metric": "ABFT GEMM TFLOP/s",
             "value": flops_job / (step_ms * 1e-3) / 1e12,
             "unit": "TFLOP/s",
+            "fault_check": {"clean_no_false_positive": clean_all, "injected_1_located_corrected": one_ok,
+                            "injected_4_located_corrected": four_ok,
+                            "per_rank_faults": "1 and 4 of 2^8 max|C|, distinct rows and columns, every rank"},
             "n_gpus": world,
             "steps": args.steps,
             "warmup": max(args.warmup, 3),
@@ -436,7 +779,9 @@ def run_ours(args):
             "config": {"workload": f"square ABFT GEMM {s}x{s}x{s} per GPU; B[{n_total}x{s}] split by columns",
                        "M": s, "K": s, "N": n_total, "N_per_gpu": n_r, "tile": [tile_m, tile_n],
                        "cta_pairs": tile_m == 256,
-                       "mode": "detect+locate+correct, weight checksums cached", "parallelism": f"dp{world} (column shards)",
+                       "mode": "detect+locate+correct, weight checksums cached",
+                       "parallelism": f"dp{world} (column shards)",
+                       "report_exchange": f"one all-gather per {EXCHANGE_EVERY} GEMMs",
                        "l2": "inputs exceed L2 (A+B_r = %d MB > 126 MB)" % ((s * s + n_r * s) * 2 // 2 ** 20)},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": load_traffic(workload),
@@ -447,7 +792,7 @@ def run_ours(args):
             "cpu_baseline": cpu,
             "e2e": {"value": flops_job / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                     "h2d_bytes_per_step": (s * s + n_r * s) * 2 * world,
-                    "d2h_bytes_per_step": int(gemm.gathered.numel()) * world,
+                    "d2h_bytes_per_step": int(rep_h[0].numel()) * world,
                     "note": "per step: A and B_r from pinned host memory + checksum encode + fused GEMM + report "
                             "gather + D2H; the next step's copies overlap this step's GEMM (two buffer sets)"},
             "gpu_launches": args.steps,
@@ -456,7 +801,10 @@ def run_ours(args):
             "overhead_pct": 100.0 * (chk_ms / off_ms - 1.0),
             "overhead_method": f"{n_pair} checked and {n_pair} unchecked launches interleaved",
             "encode_ms": enc_ms,
-            "fault_check": {"injected_located_corrected": detect_ok, "clean_no_false_positive": clean_ok},
+            "checked_encode_included_tflops": flops_job / ((chk_ms + enc_ms) * 1e-3) / 1e12,
+            "overhead_encode_included_pct": 100.0 * ((chk_ms + enc_ms) / off_ms - 1.0),
+            "step_minus_kernel_us": (step_ms - kernel_ms) * 1e3,
+            **extras,
         }
         print(json.dumps(line), flush=True)
 
@@ -528,23 +876,7 @@ def sweep(args):
         rep = ops.ReportBuffer(64, dev)
 
         def timed(fn):
-            for _ in range(3):
-                fn()
-            torch.cuda.synchronize()
-            # a GPU-side spin first, so the host queues every launch ahead of
-            # the GPU and no event interval contains host launch latency
-            torch.cuda._sleep(200_000_000)
-            pairs = []
-            for _ in range(iters):
-                flush.zero_()
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record()
-                fn()
-                e1.record()
-                pairs.append((e0, e1))
-            torch.cuda.synchronize()
-            ms = sorted(e0.elapsed_time(e1) for e0, e1 in pairs)
-            return ms[len(ms) // 2]
+            return timed_median(fn, iters, flush, 200_000_000)
 
         t_cublas = timed(lambda: torch.matmul(a, w.t(), out=out))
         t_off = timed(lambda: ops.abft_gemm(a, w, mode=N.MODE_OFF, out=out, tile_n=tn_off))
@@ -612,20 +944,7 @@ def tile_grid(args):
     iters = max(min(args.steps, 50), 5)
 
     def timed(fn):
-        for _ in range(3):
-            fn()
-        torch.cuda.synchronize()
-        torch.cuda._sleep(100_000_000)
-        ev = []
-        for _ in range(iters):
-            flush.zero_()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            fn()
-            e1.record()
-            ev.append((e0, e1))
-        torch.cuda.synchronize()
-        return sorted(a.elapsed_time(b) for a, b in ev)[iters // 2] * 1e3
+        return timed_median(fn, iters, flush) * 1e3
 
     for name, m, n, k in TILE_GRID_SHAPES:
         a = (torch.randn(m, k, device=dev) * k ** -0.5).bfloat16()
@@ -727,21 +1046,7 @@ def bmm_sweep(args):
     chk = N.MODE_DETECT | N.MODE_CORRECT
 
     def timed(fn):
-        for _ in range(3):
-            fn()
-        torch.cuda.synchronize()
-        torch.cuda._sleep(200_000_000)
-        pairs = []
-        for _ in range(iters):
-            flush.zero_()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            fn()
-            e1.record()
-            pairs.append((e0, e1))
-        torch.cuda.synchronize()
-        ms = sorted(e0.elapsed_time(e1) for e0, e1 in pairs)
-        return ms[len(ms) // 2]
+        return timed_median(fn, iters, flush, 200_000_000)
 
     def wall(fn, reps):
         for _ in range(3):
@@ -791,93 +1096,7 @@ def bmm_sweep(args):
 
 
 # ------------------------------------------------------------------ model path
-QWEN2_7B = dict(hidden=3584, inter=18944, layers=28, heads=28, kv_heads=4, head_dim=128, vocab=152064,
-                rope_theta=1000000.0, eps=1e-6)
-
-
-def build_qwen2(cfg, device, seed=0):
-    """Qwen2-style decoder: RMSNorm, fused QKV (with bias) + RoPE + GQA
-    attention (SDPA), SwiGLU MLP with fused gate+up, tied-free lm_head.
-    Every projection is an nn.Linear, so F.linear hooks see all of them."""
-    import torch
-    import torch.nn as nn
-    import torch.nn.functional as F
-
-    class RMSNorm(nn.Module):
-        def __init__(self, h):
-            super().__init__()
-            self.weight = nn.Parameter(torch.ones(h))
-
-        def forward(self, x):
-            xf = x.float()
-            return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + cfg["eps"])).to(x.dtype) * self.weight
-
-    def rope(x, cos, sin):  # x [T, H, D]
-        x1, x2 = x[..., : x.shape[-1] // 2], x[..., x.shape[-1] // 2:]
-        return x * cos + torch.cat((-x2, x1), dim=-1) * sin
-
-    class Layer(nn.Module):
-        def __init__(self):
-            super().__init__()
-            h, nh, nkv, hd, it = cfg["hidden"], cfg["heads"], cfg["kv_heads"], cfg["head_dim"], cfg["inter"]
-            self.ln1, self.ln2 = RMSNorm(h), RMSNorm(h)
-            self.qkv = nn.Linear(h, (nh + 2 * nkv) * hd, bias=True)
-            self.o = nn.Linear(nh * hd, h, bias=False)
-            self.gate_up = nn.Linear(h, 2 * it, bias=False)
-            self.down = nn.Linear(it, h, bias=False)
-
-        def forward(self, x, cos, sin, cache=None, pos=0):
-            nh, nkv, hd = cfg["heads"], cfg["kv_heads"], cfg["head_dim"]
-            t = x.shape[0]
-            q, k, v = self.qkv(self.ln1(x)).split([nh * hd, nkv * hd, nkv * hd], dim=-1)
-            q = rope(q.view(t, nh, hd), cos, sin).transpose(0, 1)
-            k = rope(k.view(t, nkv, hd), cos, sin).transpose(0, 1)
-            v = v.view(t, nkv, hd).transpose(0, 1)
-            if cache is not None:  # [2, nkv, T_max, hd]: keys and values of positions < pos + t
-                cache[0, :, pos:pos + t] = k
-                cache[1, :, pos:pos + t] = v
-                k, v = cache[0, :, :pos + t], cache[1, :, :pos + t]
-            a = F.scaled_dot_product_attention(q, k, v, is_causal=(t > 1), enable_gqa=True)
-            x = x + self.o(a.transpose(0, 1).reshape(t, nh * hd))
-            g, u = self.gate_up(self.ln2(x)).chunk(2, dim=-1)
-            return x + self.down(F.silu(g) * u)
-
-    class Model(nn.Module):
-        def __init__(self):
-            super().__init__()
-            self.embed = nn.Embedding(cfg["vocab"], cfg["hidden"])
-            self.layers = nn.ModuleList([Layer() for _ in range(cfg["layers"])])
-            self.norm = RMSNorm(cfg["hidden"])
-            self.lm_head = nn.Linear(cfg["hidden"], cfg["vocab"], bias=False)
-
-        def forward(self, ids, caches=None, pos=0):
-            t = ids.shape[0]
-            hd = cfg["head_dim"]
-            inv = 1.0 / (cfg["rope_theta"] ** (torch.arange(0, hd, 2, device=ids.device).float() / hd))
-            ang = torch.outer(torch.arange(pos, pos + t, device=ids.device).float(), inv)
-            ang = torch.cat((ang, ang), dim=-1)[:, None, :]
-            cos, sin = ang.cos().to(torch.bfloat16), ang.sin().to(torch.bfloat16)
-            x = self.embed(ids)
-            for i, layer in enumerate(self.layers):
-                x = layer(x, cos, sin, None if caches is None else caches[i], pos)
-            return self.lm_head(self.norm(x))
-
-        def new_caches(self, t_max):
-            return [torch.zeros(2, cfg["kv_heads"], t_max, cfg["head_dim"], dtype=torch.bfloat16,
-                                device=self.embed.weight.device) for _ in range(cfg["layers"])]
-
-    torch.manual_seed(seed)
-    with torch.device(device):
-        model = Model().to(torch.bfloat16)
-    with torch.no_grad():
-        for mod in model.modules():
-            if isinstance(mod, (nn.Linear, nn.Embedding)):
-                mod.weight.normal_(0.0, 0.02)
-                if getattr(mod, "bias", None) is not None:
-                    mod.bias.zero_()
-    return model.eval()
-
-
+from vla_abft_estimate_b200.workloads import COGACT, QWEN2_7B, build_cogact, build_qwen2  # noqa: E402
 def cpu_model_baseline(cfg, tokens, seconds):
     """Reference flow on the host CPU for one decoder layer's four linears
     (torch.matmul + corner check, oracle/ref_port.py), scaled to a full
@@ -906,295 +1125,31 @@ def cpu_model_baseline(cfg, tokens, seconds):
 
 
 def run_model(args):
+    """``--model qwen2-7b``: the prefill point of the default line, with
+    decode steps and the CPU reference flow, as its own JSON line."""
     import torch
 
-    from vla_abft_estimate_b200.abft import AbftConfig, AbftInjector, AbftStatsCollector, CheapSumChecker
-
-    cfg = QWEN2_7B
-    tokens = 512
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
-    model = build_qwen2(cfg, dev)
-    ids = torch.randint(0, cfg["vocab"], (tokens,), device=dev, generator=torch.Generator(device=dev).manual_seed(7))
+    torch.cuda.set_device(0)
     reps = max(args.steps, 3) if args.steps < 300 else 10
-
-    def timed_forward(ctx_factory):
-        """Median forward time (host work included: launches, report
-        reads), and the median device time of the forward's kernels alone
-        (host queued ahead behind a device sleep)."""
-        times, gpu_times = [], []
-        out = None
-        with torch.inference_mode():
-            for i in range(max(args.warmup, 2) + reps):
-                ctx = ctx_factory()
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                torch.cuda.synchronize()
-                e0.record()
-                with ctx:
-                    out = model(ids)
-                e1.record()
-                torch.cuda.synchronize()
-                g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                torch.cuda._sleep(100_000_000)
-                g0.record()
-                with ctx:
-                    out = model(ids)
-                    g1.record()
-                torch.cuda.synchronize()
-                if i >= max(args.warmup, 2):
-                    times.append(e0.elapsed_time(e1))
-                    gpu_times.append(g0.elapsed_time(g1))
-        return statistics.median(times), out, statistics.median(gpu_times)
-
-    import contextlib
-
-    # one injector per leg, reused across repetitions (its weight checksum
-    # cache is what a serving process keeps); flush() at exit reads the
-    # deferred reports once per forward
-    stats_chk = AbftStatsCollector()
-    cfg_chk = AbftConfig(enable=True, checker_backend="b200", detect_only=False)
-    inj_chk = AbftInjector(cfg_chk, CheapSumChecker(cfg_chk), stats_chk, defer_reports=True)
-    stats_off = AbftStatsCollector()
-    cfg_off = AbftConfig(enable=True, check_enable=False, checker_backend="b200")
-    inj_off = AbftInjector(cfg_off, CheapSumChecker(cfg_off), stats_off, defer_reports=True)
-
-    t_torch, ref_logits, g_torch = timed_forward(contextlib.nullcontext)
-    t_off, off_logits, g_off = timed_forward(lambda: inj_off)
-    t_chk, chk_logits, g_chk = timed_forward(lambda: inj_chk)
-    summ = stats_chk.export_summary()
-    n_checks = summ["abft"]["checks_total"] // 2  # two forwards per repetition
-
-    # fault leg: every linear of one forward may be hit (probability 0.05),
-    # each fault +1.0 on the fp32 accumulator; detect + locate + correct
-    stats_f = AbftStatsCollector()
-    cfg_f = AbftConfig(enable=True, checker_backend="b200", detect_only=False, inject_fault=True,
-                       inject_probability=0.05, inject_magnitude=1.0, seed=11)
-    inj_f = AbftInjector(cfg_f, CheapSumChecker(cfg_f), stats_f, defer_reports=True)
-    with torch.inference_mode(), inj_f:
-        f_logits = model(ids)
-    torch.cuda.synchronize()
-    fs = stats_f.export_summary()
-    flt = {k: v for k, v in fs["abft"]["faults"].items() if k != "located"}
-    max_diff = (f_logits.float() - chk_logits.float()).abs().max().item()
-    logits_scale = chk_logits.float().abs().max().item()
-
-    # decode: prefill 512 tokens into a KV cache, then time single-token steps
-    def timed_decode(ctx_factory, steps=32):
-        caches = model.new_caches(tokens + steps + 8)
-        with torch.inference_mode():
-            with ctx_factory():
-                model(ids, caches, 0)
-            nxt = ids[-1:].clone()
-            for i in range(4):  # warm-up steps
-                with ctx_factory():
-                    model(nxt, caches, tokens + i)
-            torch.cuda.synchronize()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            for i in range(steps):
-                with ctx_factory():
-                    model(nxt, caches, tokens + 4 + i)
-            e1.record()
-            torch.cuda.synchronize()
-        return e0.elapsed_time(e1) / steps
-
-    d_torch = timed_decode(contextlib.nullcontext)
-    d_off = timed_decode(lambda: inj_off)
-    d_chk = timed_decode(lambda: inj_chk)
-
-    linear_flops = 0.0
-    h, it, nh, nkv, hd, V = (cfg["hidden"], cfg["inter"], cfg["heads"], cfg["kv_heads"], cfg["head_dim"],
-                             cfg["vocab"])
-    for k, n in [(h, (nh + 2 * nkv) * hd), (nh * hd, h), (h, 2 * it), (it, h)]:
-        linear_flops += 2.0 * tokens * k * n * cfg["layers"]
-    linear_flops += 2.0 * tokens * h * V
-    cpu = None if args.no_cpu_baseline else cpu_model_baseline(cfg, tokens, 20.0)
+    warmup = max(args.warmup, 2)
+    res = qwen_prefill_point(reps, warmup, decode_steps=32, cpu_seconds=0.0 if args.no_cpu_baseline else 20.0)
+    cfg = QWEN2_7B
     line = {
         "metric": "Qwen2-7B prefill-512 tokens/s (every linear ABFT-protected)",
-        "value": tokens / (t_chk * 1e-3), "unit": "tokens/s", "n_gpus": 1, "steps": reps,
-        "warmup": max(args.warmup, 2), "ms_per_step": t_chk, "higher_is_better": True, "scaling": "none",
+        "value": res["tokens_per_s"]["abft"], "unit": "tokens/s", "n_gpus": 1, "steps": reps,
+        "warmup": warmup, "ms_per_step": res["ms"]["abft"], "higher_is_better": True, "scaling": "none",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random init N(0,0.02), random token ids)",
         "config": {"workload": "Qwen2-7B-shaped decoder prefill, batch 1, 512 tokens", **cfg,
                    "fused_shapes": "qkv 3584->4608 (bias), o 3584->3584, gate_up 3584->37888, down 18944->3584, "
                                    "lm_head 3584->152064",
                    "abft": "b200 backend: one fused GEMM + row-checksum check + correct per linear, "
                            "reports deferred to one read per forward"},
-        "torch_tokens_per_s": tokens / (t_torch * 1e-3),
-        "unchecked_kernel_tokens_per_s": tokens / (t_off * 1e-3),
-        "ms": {"torch": t_torch, "b200_unchecked": t_off, "b200_abft": t_chk},
-        "device_ms": {"torch": g_torch, "b200_unchecked": g_off, "b200_abft": g_chk,
-                      "note": "kernels only: the host queued the forward behind a device sleep"},
-        "decode_ms_per_token": {"torch": d_torch, "b200_unchecked": d_off, "b200_abft": d_chk,
-                                "abft_overhead_vs_torch_pct": 100.0 * (d_chk / d_torch - 1.0),
-                                "note": "after a 512-token prefill into a KV cache; every linear at M = 1 "
-                                        "(operands swapped: weight on the MMA's 128-row side)"},
-        "overhead_vs_torch_pct": 100.0 * (t_chk / t_torch - 1.0),
-        "overhead_vs_unchecked_pct": 100.0 * (t_chk / t_off - 1.0),
-        "linear_tflops_abft": linear_flops / (t_chk * 1e-3) / 1e12,
-        "checked_linears_per_forward": n_checks // (reps + max(args.warmup, 2)),
-        "clean_false_positives": summ["abft"]["faults"]["detected_total"],
-        "fault_leg": {"injected": fs["fault_injection"]["injections_total"],
-                      "detected_injections": fs["fault_injection"]["detected_injections_total"],
-                      "faults": flt,
-                      "max_abs_logit_diff_vs_clean": max_diff, "max_abs_logit": logits_scale},
-        "logits_max_abs_diff_torch_vs_abft": (ref_logits.float() - chk_logits.float()).abs().max().item(),
-        "cpu_baseline": cpu,
-        "reference_published": {"tokens_per_s_no_abft": 7217, "tokens_per_s_abft_python": 5909,
-                                "decode_ms_no_abft": 29.90, "decode_ms_abft_python": 73.97,
-                                "source": "pytorch/baseline_7b_prefill512.json:44, "
-                                          "pytorch/abft_7b_prefill512_nsys.json:44 (GPU unrecorded)"},
+        **res,
     }
     print(json.dumps(line), flush=True)
 
 
 # ----------------------------------------------------------- VLA (CogACT-style)
-COGACT = dict(
-    vit=dict(hidden=1024, mlp=4096, layers=24, heads=16),        # ViT-L/14 at 224^2
-    siglip=dict(hidden=1152, mlp=4304, layers=27, heads=16),     # SigLIP-So400m/14 at 224^2
-    llm=dict(hidden=4096, mlp=11008, layers=32, heads=32),       # Llama-2-7B
-    dit=dict(hidden=768, mlp=3072, layers=12, heads=12),         # DiT-B action head
-    patches=256, text_tokens=32, action_tokens=16, action_dim=7, denoise_steps=10, vocab=32000)
-
-
-def build_cogact(cfg, device, seed=0):
-    """Random-init CogACT-style VLA: two ViT encoders (patch conv, pre-norm
-    blocks with fused QKV + GELU MLP), an MLP projector, a Llama-style
-    decoder (RMSNorm, RoPE, fused QKV, SwiGLU with fused gate+up) and a
-    DiT-B action head (adaLN-zero blocks conditioned on the decoder's last
-    hidden state and the denoising step). Every projection is an nn.Linear."""
-    import torch
-    import torch.nn as nn
-    import torch.nn.functional as F
-
-    class RMSNorm(nn.Module):
-        def __init__(self, h):
-            super().__init__()
-            self.weight = nn.Parameter(torch.ones(h))
-
-        def forward(self, x):
-            xf = x.float()
-            return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)).to(x.dtype) * self.weight
-
-    def attend(qkv, heads, causal, cos=None, sin=None):
-        t, three_h = qkv.shape
-        hd = three_h // 3 // heads
-        q, k, v = qkv.view(t, 3, heads, hd).unbind(1)
-        if cos is not None:
-            def rope(x):
-                x1, x2 = x[..., : hd // 2], x[..., hd // 2:]
-                return x * cos + torch.cat((-x2, x1), dim=-1) * sin
-            q, k = rope(q), rope(k)
-        o = F.scaled_dot_product_attention(q.transpose(0, 1), k.transpose(0, 1), v.transpose(0, 1), is_causal=causal)
-        return o.transpose(0, 1).reshape(t, heads * hd)
-
-    class VitBlock(nn.Module):
-        def __init__(self, c):
-            super().__init__()
-            h = c["hidden"]
-            self.heads = c["heads"]
-            self.n1, self.n2 = nn.LayerNorm(h), nn.LayerNorm(h)
-            self.qkv, self.o = nn.Linear(h, 3 * h), nn.Linear(h, h)
-            self.fc1, self.fc2 = nn.Linear(h, c["mlp"]), nn.Linear(c["mlp"], h)
-
-        def forward(self, x):
-            x = x + self.o(attend(self.qkv(self.n1(x)), self.heads, False))
-            return x + self.fc2(F.gelu(self.fc1(self.n2(x)), approximate="tanh"))
-
-    class Vit(nn.Module):
-        def __init__(self, c):
-            super().__init__()
-            self.patch = nn.Conv2d(3, c["hidden"], kernel_size=14, stride=14)
-            self.pos = nn.Parameter(torch.zeros(cfg["patches"], c["hidden"]))
-            self.blocks = nn.ModuleList([VitBlock(c) for _ in range(c["layers"])])
-            self.norm = nn.LayerNorm(c["hidden"])
-
-        def forward(self, img):
-            x = self.patch(img).flatten(2).transpose(1, 2)[0] + self.pos
-            for b in self.blocks:
-                x = b(x)
-            return self.norm(x)
-
-    class LlamaBlock(nn.Module):
-        def __init__(self, c):
-            super().__init__()
-            h = c["hidden"]
-            self.heads = c["heads"]
-            self.n1, self.n2 = RMSNorm(h), RMSNorm(h)
-            self.qkv, self.o = nn.Linear(h, 3 * h, bias=False), nn.Linear(h, h, bias=False)
-            self.gate_up, self.down = nn.Linear(h, 2 * c["mlp"], bias=False), nn.Linear(c["mlp"], h, bias=False)
-
-        def forward(self, x, cos, sin):
-            x = x + self.o(attend(self.qkv(self.n1(x)), self.heads, True, cos, sin))
-            g, u = self.gate_up(self.n2(x)).chunk(2, dim=-1)
-            return x + self.down(F.silu(g) * u)
-
-    class DitBlock(nn.Module):
-        def __init__(self, c):
-            super().__init__()
-            h = c["hidden"]
-            self.heads = c["heads"]
-            self.n1 = nn.LayerNorm(h, elementwise_affine=False)
-            self.n2 = nn.LayerNorm(h, elementwise_affine=False)
-            self.qkv, self.o = nn.Linear(h, 3 * h), nn.Linear(h, h)
-            self.fc1, self.fc2 = nn.Linear(h, c["mlp"]), nn.Linear(c["mlp"], h)
-            self.ada = nn.Linear(h, 6 * h)
-
-        def forward(self, x, c):
-            s1, b1, g1, s2, b2, g2 = self.ada(F.silu(c)).chunk(6, dim=-1)
-            x = x + g1 * self.o(attend(self.qkv(self.n1(x) * (1 + s1) + b1), self.heads, False))
-            return x + g2 * self.fc2(F.gelu(self.fc1(self.n2(x) * (1 + s2) + b2), approximate="tanh"))
-
-    class Vla(nn.Module):
-        def __init__(self):
-            super().__init__()
-            v, s, l, d = cfg["vit"], cfg["siglip"], cfg["llm"], cfg["dit"]
-            self.vit, self.siglip = Vit(v), Vit(s)
-            self.proj1 = nn.Linear(v["hidden"] + s["hidden"], l["hidden"])
-            self.proj2 = nn.Linear(l["hidden"], l["hidden"])
-            self.embed = nn.Embedding(cfg["vocab"], l["hidden"])
-            self.llm = nn.ModuleList([LlamaBlock(l) for _ in range(l["layers"])])
-            self.llm_norm = RMSNorm(l["hidden"])
-            self.cond = nn.Linear(l["hidden"], d["hidden"])
-            self.t_embed = nn.Linear(256, d["hidden"])
-            self.act_in = nn.Linear(cfg["action_dim"], d["hidden"])
-            self.dit = nn.ModuleList([DitBlock(d) for _ in range(d["layers"])])
-            self.act_out = nn.Linear(d["hidden"], cfg["action_dim"])
-
-        def forward(self, img, text_ids, noise):
-            vis = torch.cat((self.vit(img), self.siglip(img)), dim=-1)
-            vis = self.proj2(F.gelu(self.proj1(vis), approximate="tanh"))
-            x = torch.cat((vis, self.embed(text_ids)), dim=0)
-            t, hd = x.shape[0], cfg["llm"]["hidden"] // cfg["llm"]["heads"]
-            inv = 1.0 / (10000.0 ** (torch.arange(0, hd, 2, device=x.device).float() / hd))
-            ang = torch.outer(torch.arange(t, device=x.device).float(), inv)
-            ang = torch.cat((ang, ang), dim=-1)[:, None, :]
-            cos, sin = ang.cos().to(x.dtype), ang.sin().to(x.dtype)
-            for b in self.llm:
-                x = b(x, cos, sin)
-            cog = self.cond(self.llm_norm(x)[-1:])  # cognition feature of the last token
-            a = noise
-            for step in range(cfg["denoise_steps"]):
-                freq = torch.exp(-torch.arange(128, device=x.device).float() * (9.21 / 128)) * (1000.0 * step)
-                temb = torch.cat((freq.sin(), freq.cos()))[None].to(x.dtype)
-                c = cog + self.t_embed(temb)
-                h = self.act_in(a)
-                for b in self.dit:
-                    h = b(h, c)
-                a = a - 0.1 * self.act_out(h)
-            return a
-
-    torch.manual_seed(seed)
-    with torch.device(device):
-        model = Vla().to(torch.bfloat16)
-    with torch.no_grad():
-        for mod in model.modules():
-            if isinstance(mod, (nn.Linear, nn.Embedding, nn.Conv2d)):
-                mod.weight.normal_(0.0, 0.02)
-                if getattr(mod, "bias", None) is not None:
-                    mod.bias.zero_()
-    return model.eval()
-
-
 def run_cogact(args):
     import contextlib
 

@@ -141,3 +141,12 @@ def test_binding_constants_match_the_header(name, value):
 def test_oracle_suspect_rule_matches_the_header():
     assert O.SUSPECT_ROWS == _header_defines()["ABFT_SUSPECT_ROWS"]
     assert O.REC_SUPPRESSED == N.REC_SUPPRESSED
+
+
+def test_cache_takes_inference_tensors(counting_encoder):
+    cache = inj_mod.WeightChecksumCache()
+    with torch.inference_mode():
+        w = torch.randn(64, 32)
+        v1 = cache.get(w, 256)
+        assert cache.get(w, 256) is v1
+    assert len(counting_encoder) == 1

@@ -341,3 +341,32 @@ def test_fused_linear_input_layouts(cuda_device, layout):
     assert (y.float() - ref.float()).abs().max().item() <= 1e-2 * ref.float().abs().max().item()
     s = stats.export_summary()["abft"]
     assert s["checks_total"] == 1 and s["fail_total"] == 0
+
+
+@pytest.mark.parametrize("k,n,bias", [(7, 768, True), (768, 7, True), (5, 3, False), (12, 20, True)])
+def test_b200_narrow_linears_fused_on_padded_copies(cuda_device, k, n, bias):
+    """checker_backend "b200": a linear with K or N not a multiple of 8 runs
+    the fused kernel on zero-padded copies. Clean: no detection and the
+    F.linear result; with the reference's random fault (probability 1): the
+    drawn (row, col) of the caller's output is located and corrected."""
+    torch.manual_seed(k * 17 + n)
+    x = torch.randn(16, k, device=cuda_device).bfloat16()
+    w = (torch.randn(n, k, device=cuda_device) * k ** -0.5).bfloat16()
+    b = (torch.randn(n, device=cuda_device) * 0.02).bfloat16() if bias else None
+    ref = torch.nn.functional.linear(x.float(), w.float(), None if b is None else b.float())
+    for inject in (False, True):
+        cfg = AbftConfig(enable=True, checker_backend="b200", detect_only=False, inject_fault=inject,
+                         inject_probability=1.0, inject_magnitude=64.0, seed=5)
+        stats = AbftStatsCollector()
+        with torch.inference_mode(), AbftInjector(cfg, CheapSumChecker(cfg), stats, defer_reports=True):
+            y = torch.nn.functional.linear(x, w, b)
+        torch.cuda.synchronize()
+        s = stats.export_summary()["abft"]
+        assert tuple(y.shape) == (16, n) and s["checks_total"] == 1 and stats.skipped_unsupported == 0
+        assert (y.float() - ref).abs().max().item() <= 1e-2 * ref.abs().max().item() + 1e-3
+        if not inject:
+            assert s["faults"]["detected_total"] == 0
+        else:
+            idx = O.InjectorRng(5).maybe_inject(16 * n, True, 1.0)
+            assert [(c["row"], c["col"]) for c in s["faults"]["located"]] == [(idx // n, idx % n)]
+            assert s["faults"]["corrected_total"] == 1

@@ -108,3 +108,63 @@ def test_rank_leaving_is_detected_by_timeout():
     out = _run("leave")
     assert out[1] == "left"
     assert isinstance(out.get(0), str) and out[0].startswith("error:")
+
+
+def _ring_worker(rank, world, port, q):
+    """ShardedAbftGemm's report ring and batched exchange, with the GEMM
+    replaced by a stand-in that writes a known report (no GPU here)."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    try:
+        from vla_abft_estimate_b200 import sharded
+
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+        calls = []
+
+        def fake_gemm(a, w, *, report=None, out=None, **kw):
+            step = len(calls)
+            calls.append(step)
+            buf = fake_report([(100 * step + rank, rank)], capacity=report.capacity)
+            report.tensor[: buf.numel()].copy_(buf)
+            return out, report
+
+        sharded.ops.abft_gemm = fake_gemm
+        sharded.ops.pick_tile_n = lambda *a, **k: 256
+        n = 16
+        c0, c1 = shard_bounds(n, world, rank)
+        g = sharded.ShardedAbftGemm(torch.zeros(c1 - c0, 8, dtype=torch.bfloat16), c0, mode=N.MODE_DETECT,
+                                    capacity=4, exchange_every=2)
+        g.checksums = (256, None)  # no encode on the CPU
+        a = torch.zeros(4, 8, dtype=torch.bfloat16)
+        seen = []
+        for _ in range(5):  # exchanges after calls 2 and 4 (ring full), then one forced for call 5
+            g(a)
+            seen.append(len(g.global_reports()))
+        g.exchange()
+        last = [r.coords() for r in g.global_reports()]
+        q.put((rank, (seen, last)))
+        dist.destroy_process_group()
+    except Exception as e:  # noqa: BLE001 - reported to the parent
+        q.put((rank, f"error:{type(e).__name__}:{e}"))
+
+
+def test_two_rank_report_ring_exchanged_in_batches():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ring_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=90)
+        if p.is_alive():
+            p.kill()
+    out = {}
+    while not q.empty():
+        r, v = q.get()
+        out[r] = v
+    # after call 1 nothing is exchanged yet; calls 2 and 4 fill the ring
+    want_seen = [0, 2, 2, 2, 2]
+    # the forced exchange holds call 5 (step 4): rank 0 at column 0, rank 1 at column 8 + 1
+    want_last = [[(400, 0), (401, 9)]]
+    assert out == {0: (want_seen, want_last), 1: (want_seen, want_last)}

@@ -16,10 +16,13 @@ in the reference (injector.py:31-51), and restored on exit.
   (injector.py:176-187). ``torch.matmul`` with a batched right operand is
   unchecked in the reference (its ``b_2d`` is None, checkers.py:145-149);
   ``check_batched_matmul`` checks it per batch.
-* Other backends, operands the library cannot take (CPU, non-bf16, K or N
-  not a multiple of 8) and calls that need autograd follow the reference
-  flow: run the op, maybe perturb one output element, then
-  ``checker.check`` on the flattened operands (injector.py:152-187).
+* A linear with K or N not a multiple of 8 (the library reads rows in
+  16-byte pieces; e.g. a VLA's 7-wide action projections) runs the same
+  fused kernel on zero-padded copies of its operands.
+* Other backends, operands the library cannot take (CPU, non-bf16) and
+  calls that need autograd follow the reference flow: run the op, maybe
+  perturb one output element, then ``checker.check`` on the flattened
+  operands (injector.py:152-187).
 
 The random stream is the reference's: one ``random.Random(cfg.seed)`` per
 injector, consumed in the same order -- the injection coin and index after
@@ -91,7 +94,9 @@ class WeightChecksumCache:
       ``no_grad``, optimizer steps), so such an update re-encodes.
 
     Writes that bypass the version counter (``weight.data.copy_(...)``,
-    writes through another framework or a raw pointer) cannot be seen here;
+    in-place writes to a weight created under ``inference_mode``, which has
+    no counter, writes through another framework or a raw pointer) cannot
+    be seen here;
     call ``invalidate(weight)`` (or ``clear()``) after them. If that is
     forgotten, the kernel still does not corrupt the output: the stale
     checksums make most rows of a slab mismatch, which the kernel reports
@@ -107,11 +112,17 @@ class WeightChecksumCache:
     def _key(weight: torch.Tensor, tile_n: int) -> tuple:
         return (weight.data_ptr(), tuple(weight.shape), weight.stride(), tile_n, weight.get_device())
 
+    @staticmethod
+    def _version(weight: torch.Tensor) -> int:
+        # tensors made under inference_mode carry no version counter
+        return -1 if weight.is_inference() else weight._version
+
     def get(self, weight: torch.Tensor, tile_n: int) -> torch.Tensor:
         key = self._key(weight, tile_n)
         storage = weight.untyped_storage()
+        version = self._version(weight)
         e = self._d.get(key)
-        if e is not None and e[0]() is storage and e[1] == weight._version:
+        if e is not None and e[0]() is storage and e[1] == version:
             return e[2]
         if e is None and len(self._d) >= self.max_entries:
             self._d.pop(next(iter(self._d)))
@@ -125,7 +136,7 @@ class WeightChecksumCache:
             if cur is not None and cur[0] is ref:
                 d.pop(key, None)
 
-        self._d[key] = (weakref.ref(storage, _drop), weight._version, v)
+        self._d[key] = (weakref.ref(storage, _drop), version, v)
         return v
 
     def invalidate(self, weight: torch.Tensor) -> None:
@@ -425,16 +436,42 @@ class AbftInjector(AbstractContextManager):
         if weight.dim() != 2 or x.dim() < 1 or x.shape[-1] != weight.shape[1]:
             return False
         n, k = weight.shape
-        if k % 8 or n % 8 or k == 0 or x.numel() == 0:
-            return False
-        if weight.stride(1) != 1 or weight.stride(0) % 8 or weight.data_ptr() % 16:
+        if k == 0 or n == 0 or x.numel() == 0:
             return False
         if bias is not None and (not bias.is_cuda or bias.dtype != torch.bfloat16 or bias.dim() != 1):
             return False
+        if k % 8 or n % 8:
+            return True  # run on zero-padded copies (_fused_linear_padded)
+        if weight.stride(1) != 1 or weight.stride(0) % 8 or weight.data_ptr() % 16:
+            return False
         return True
 
-    def _fused_linear(self, x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor]) -> torch.Tensor:
+    def _fused_linear_padded(self, x: torch.Tensor, weight: torch.Tensor,
+                             bias: Optional[torch.Tensor]) -> torch.Tensor:
+        """A linear whose K or N is not a multiple of 8 (the library reads
+        rows in 16-byte pieces), e.g. a VLA's 7-wide action projections:
+        the fused kernel runs on copies zero-padded to multiples of 8 and the
+        output is the first N columns. Zero rows and columns change no
+        product and no checksum, so the padded call detects, locates and
+        corrects exactly the faults of the original one (the reference can
+        only run its scalar check on such a linear). The copies are made
+        per call: a cached padded weight could go stale behind a write the
+        version counter does not see, and these weights are small."""
         n, k = weight.shape
+        pk, pn = -k % 8, -n % 8
+        xp = F.pad(x, (0, pk)) if pk else x
+        wp = F.pad(weight, (0, pk, 0, pn))
+        bp = None if bias is None else (F.pad(bias, (0, pn)) if pn else bias)
+        out = self._fused_linear(xp, wp, bp, real=(k, n))
+        return out[..., :n] if pn else out
+
+    def _fused_linear(self, x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor],
+                      real: Optional[Tuple[int, int]] = None) -> torch.Tensor:
+        """``real``: (K, N) of the caller's linear when ``x`` and ``weight``
+        are zero-padded copies (the fault draw and the shape key use the
+        caller's shape; the kernel encodes the copy's checksums itself)."""
+        n, k = weight.shape
+        k_key, n_key = real if real is not None else (k, n)
         # A contiguous input is read in place as m rows of k (no reshape
         # dispatch per call); anything else as a 2-D view with its own row
         # stride, or a copy when that view cannot be read in place.
@@ -448,9 +485,9 @@ class AbftInjector(AbstractContextManager):
         m = x2.numel() // k
         dix = x2.get_device()
         # injection first, then the check gate: the reference's rng order
-        idx = self._draw_fault(m * n)
+        idx = self._draw_fault(m * n_key)
         injected = idx is not None
-        check = self._check_gate_dims(m, k, n)
+        check = self._check_gate_dims(m, k_key, n_key)
         mode = N.MODE_OFF
         if check:
             mode = N.MODE_DETECT | (0 if self.cfg.detect_only else N.MODE_CORRECT)
@@ -461,8 +498,8 @@ class AbftInjector(AbstractContextManager):
         # few rows: the library swaps the operands and checksums the tokens
         # itself, so the weight's checksum block is not needed
         swapped = m <= 64 and n >= 2 * m
-        cks = self.checksums.get(weight, tile_n) if check and not swapped else None
-        inject = [(idx // n, idx % n, float(self.cfg.inject_magnitude))] if injected else None
+        cks = self.checksums.get(weight, tile_n) if check and not swapped and real is None else None
+        inject = [(idx // n_key, idx % n_key, float(self.cfg.inject_magnitude))] if injected else None
         rep = None
         if check:
             if self.defer_reports and self.cfg.record_enable:
@@ -483,16 +520,19 @@ class AbftInjector(AbstractContextManager):
         if check:
             if self.cfg.record_enable:
                 if self.defer_reports:
-                    self._pending.append((dix, "linear", self.stats.current_phase, (m, k, n), injected, None))
+                    self._pending.append((dix, "linear", self.stats.current_phase, (m, k_key, n_key), injected,
+                                          None))
                 else:
                     host_rep = rep.read()
                     if host_rep.suspect:
                         self.checksums.clear()
-                    self.stats.record_check(op_name="linear", shape_key=f"A{(m, k)}_B{(k, n)}_C{(m, n)}",
+                    self.stats.record_check(op_name="linear",
+                                            shape_key=f"A{(m, k_key)}_B{(k_key, n_key)}_C{(m, n_key)}",
                                             result=result_from_report(host_rep), injected=injected)
             if self.cfg.dump_file:
-                self._maybe_dump_tensors("linear", f"A{(m, k)}_B{(k, n)}_C{(m, n)}", x.reshape(m, k), weight.t(),
-                                         out.reshape(m, n), bias)
+                self._maybe_dump_tensors("linear", f"A{(m, k_key)}_B{(k_key, n_key)}_C{(m, n_key)}",
+                                         x.reshape(m, k)[:, :k_key], weight.t()[:k_key, :n_key],
+                                         out.reshape(m, n)[:, :n_key], None if bias is None else bias[:n_key])
         return out
 
     # -------------------------------------------------- fused bmm / matmul
@@ -595,6 +635,8 @@ class AbftInjector(AbstractContextManager):
     def _wrap_linear(self, fn: Callable[..., torch.Tensor]) -> Callable[..., torch.Tensor]:
         def wrapped(input: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
             if self._fused_linear_ok(input, weight, bias):
+                if weight.shape[0] % 8 or weight.shape[1] % 8:
+                    return self._fused_linear_padded(input, weight, bias)
                 return self._fused_linear(input, weight, bias)
             out = fn(input, weight, bias)
             out2, injected = self._maybe_inject_fault(out)

@@ -83,10 +83,13 @@ __global__ void __launch_bounds__(256) encode_weight_kernel(const __nv_bfloat16*
 #pragma unroll
   for (int e = 0; e < 8; ++e) s1[e] = s2[e] = s3[e] = 0.f;
   if (k0 < K) {
-    for (int j = rg; j < bd; j += 32) {
-      const int gj = nt * bd + j;
-      if (gj >= N) break;
-      const uint4 w = __ldg(reinterpret_cast<const uint4*>(B + static_cast<int64_t>(gj) * ldb + k0));
+    // Rows rg, rg + 32, ... of the tile, added in that order. Four rows'
+    // loads are issued before any is used (memory-level parallelism: the
+    // pass is bound by HBM latency otherwise); the order of the sums, and
+    // so every bit of the result, is that of a one-row-at-a-time loop.
+    const int nrows = min(bd, N - nt * bd);
+    const __nv_bfloat16* base = B + static_cast<int64_t>(nt) * bd * ldb + k0;
+    auto add_row = [&](const uint4& w, int j) {
       float x[8];
       unpack8(w, x);
       const float wt = static_cast<float>(j + 1);
@@ -97,7 +100,16 @@ __global__ void __launch_bounds__(256) encode_weight_kernel(const __nv_bfloat16*
         s2[e] = fmaf(wt, x[e], s2[e]);
         s3[e] = fmaf(sg, x[e], s3[e]);
       }
+    };
+    int j = rg;
+    for (; j + 96 < nrows; j += 128) {
+      uint4 w[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) w[u] = __ldg(reinterpret_cast<const uint4*>(base + static_cast<int64_t>(j + 32 * u) * ldb));
+#pragma unroll
+      for (int u = 0; u < 4; ++u) add_row(w[u], j + 32 * u);
     }
+    for (; j < nrows; j += 32) add_row(__ldg(reinterpret_cast<const uint4*>(base + static_cast<int64_t>(j) * ldb)), j);
   }
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
