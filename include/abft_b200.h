@@ -20,8 +20,9 @@
  *
  * Conventions
  *   - Every pointer argument that names tensor data is a DEVICE pointer.
- *     Matrices are row-major bf16 (raw 16-bit storage); leading dimensions are
- *     in elements.
+ *     Matrices are row-major bf16 (raw 16-bit storage) -- the post-hoc check
+ *     also takes fp16 and fp32 (abft_check_args.dtype); leading dimensions
+ *     are in elements.
  *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
  *   - The library allocates nothing per call.  Scratch space, when a call needs
  *     any, comes from the caller through `workspace`.
@@ -40,7 +41,7 @@
 extern "C" {
 #endif
 
-#define ABFT_B200_VERSION 2
+#define ABFT_B200_VERSION 3
 
 /* ---- return codes ------------------------------------------------------- */
 enum abft_status {
@@ -53,6 +54,11 @@ enum abft_status {
   ABFT_ERR_NO_DEVICE = -6,     /* no sm_100 device current                   */
   ABFT_ERR_DRIVER = -7         /* tensor-map encoder unavailable             */
 };
+
+/* ---- element types of the post-hoc check (abft_check_args.dtype) -------- */
+#define ABFT_DTYPE_BF16 0      /* bfloat16 (raw 16-bit storage)                */
+#define ABFT_DTYPE_F16  1      /* IEEE half                                    */
+#define ABFT_DTYPE_F32  2      /* IEEE single                                  */
 
 /* ---- mode bits for abft_gemm_bf16 -------------------------------------- */
 #define ABFT_MODE_OFF      0u  /* plain GEMM (+bias); same kernel, checks compiled out */
@@ -247,22 +253,28 @@ int abft_gemm_bf16(const abft_gemm_args* args, void* stream);
  *   sum_c  = sum(C)
  *   ok     = |corner - sum_c| <= tol_abs  or  |corner - sum_c| / max(|sum_c|, 1) <= tol_rel
  * Results land in report->corner/sum_c/abs_err/rel_err/ref_ok.
- * ABFT_CHECK_BF16_SUMS rounds every intermediate (both sum vectors, the dot,
- * the bias term, sum_c, the errors and the tolerances) to bf16, as the
- * reference's python backend does on bf16 tensors; otherwise all sums are
- * fp32 (the reference's force_fp32_check intent, pytorch/abft/config.py:21).
+ * A, B, C and bias all have the element type `dtype` (bf16, fp16 or fp32,
+ * the types the reference's extension dispatches on, abft_fused.cu:116-118);
+ * sums accumulate in fp32.
+ * ABFT_CHECK_NATIVE_SUMS rounds every intermediate (both sum vectors, the
+ * dot, the bias term, sum_c, the errors and the tolerances) to that element
+ * type, as the reference's python backend does on tensors of that type (a
+ * no-op for fp32); otherwise all sums are fp32 (the reference's
+ * force_fp32_check intent, pytorch/abft/config.py:21). Its older name
+ * ABFT_CHECK_BF16_SUMS is the same bit.
  * ABFT_CHECK_LOCATE also compares every row and column sum of C with
  * A (B e) and (e^T A) B and records mismatches: a row and a column whose
  * residuals agree are one located fault (row, col); an unpaired row is
  * recorded as (row, -1) and an unpaired column as (-1, col). */
-#define ABFT_CHECK_LOCATE    1u
-#define ABFT_CHECK_BF16_SUMS 2u
+#define ABFT_CHECK_LOCATE      1u
+#define ABFT_CHECK_NATIVE_SUMS 2u
+#define ABFT_CHECK_BF16_SUMS   ABFT_CHECK_NATIVE_SUMS
 
 typedef struct abft_check_args {
-  const void* A;          /* bf16 [M, lda]                                    */
-  const void* B;          /* bf16 [N, ldb] (b_kn == 0) or [K, ldb] (b_kn == 1) */
-  const void* C;          /* bf16 [M, ldc]                                    */
-  const void* bias;       /* bf16 [N] or NULL                                 */
+  const void* A;          /* [M, lda] of `dtype`                              */
+  const void* B;          /* [N, ldb] (b_kn == 0) or [K, ldb] (b_kn == 1)     */
+  const void* C;          /* [M, ldc]                                         */
+  const void* bias;       /* [N] or NULL                                      */
   int64_t M, N, K;
   int64_t lda, ldb, ldc;
   int32_t b_kn;           /* layout of B, see above                           */
@@ -273,6 +285,7 @@ typedef struct abft_check_args {
   void* report;           /* abft_report + records                            */
   void* workspace;        /* device scratch, abft_check_workspace_bytes()     */
   size_t workspace_bytes;
+  int32_t dtype;          /* ABFT_DTYPE_* of A, B, C and bias (0 = bf16)      */
 } abft_check_args;
 
 size_t abft_check_workspace_bytes(const abft_check_args* args);

@@ -79,6 +79,7 @@ def cheap_sum_check(
     tol_abs: float = 1e-2,
     tol_rel: float = 1e-2,
     emulate_bf16: bool = False,
+    emulate_f16: bool = False,
 ) -> CheapSumResult:
     """pytorch/abft/checkers.py:112-126 and :96-110.
 
@@ -86,11 +87,12 @@ def cheap_sum_check(
     sum_c = C.sum(); ok = |corner - sum_c| <= tol_abs or
     |corner - sum_c| / max(|sum_c|, 1) <= tol_rel.
 
-    With ``emulate_bf16`` every intermediate is rounded to bf16 the way the
-    reference's python backend does on bf16 tensors (its results are bf16
-    tensors; the survey confirmed ``a.sum(0).dtype == bfloat16``). Otherwise
-    the arithmetic is float64, the fp32-accumulating "triton" backend's
-    intent (pytorch/abft/triton_backend.py:42-49) without its rounding.
+    With ``emulate_bf16`` (``emulate_f16``) every intermediate is rounded to
+    bf16 (fp16) the way the reference's python backend does on tensors of
+    that type (its results are tensors of the input type; the survey
+    confirmed ``a.sum(0).dtype == bfloat16``). Otherwise the arithmetic is
+    float64, the fp32-accumulating "triton" backend's intent
+    (pytorch/abft/triton_backend.py:42-49) without its rounding.
     """
     a = np.asarray(a, dtype=np.float64)
     b = np.asarray(b_kn, dtype=np.float64)
@@ -98,7 +100,11 @@ def cheap_sum_check(
 
     def r(x):
         x = np.asarray(x, dtype=np.float64)
-        return bf16_round(x).astype(np.float64) if emulate_bf16 else x
+        if emulate_bf16:
+            return bf16_round(x).astype(np.float64)
+        if emulate_f16:
+            return x.astype(np.float32).astype(np.float16).astype(np.float64)
+        return x
 
     def f(x) -> float:
         return float(np.asarray(x).reshape(-1)[0])
@@ -114,10 +120,10 @@ def cheap_sum_check(
     diff = f(r(abs(corner - sum_c)))
     denom = max(abs(sum_c), 1.0)
     rel = f(r(diff / denom))
-    if emulate_bf16:
-        # torch compares a bf16 tensor with a Python float in bf16
-        tol_abs = f(bf16_round(np.float32(tol_abs)))
-        tol_rel = f(bf16_round(np.float32(tol_rel)))
+    if emulate_bf16 or emulate_f16:
+        # torch compares a tensor of the input type with a Python float in that type
+        tol_abs = f(r(np.float32(tol_abs)))
+        tol_rel = f(r(np.float32(tol_rel)))
     ok = bool(diff <= tol_abs or rel <= tol_rel)
     return CheapSumResult(ok, float(diff), float(rel), float(corner), float(sum_c))
 
@@ -326,13 +332,15 @@ def locate_post_hoc(
     c: np.ndarray,
     bias: Optional[np.ndarray] = None,
     thr_scale: float = 1e-3,
+    unit: float = 2.0 ** -9,
 ) -> List[Tuple[int, int]]:
     """Classic row/column checksum locate on an existing output C.
 
     Row i mismatches when |sum_j C[i,j] - (A (B e))_i - sum(bias)| >
     tau sqrt(K) max_j |C[i,j]| + u sum_j |C[i,j]|; column j when
     |sum_i C[i,j] - ((e^T A) B)_j - M bias_j| > tau sqrt(K) max_i |C[i,j]| +
-    u sum_i |C[i,j]|, u = 2^-9 (worst-case rounding of a stored bf16 value).
+    u sum_i |C[i,j]|, u = 2^-9 for bf16 outputs (2^-(p+1) for p significand
+    bits: 2^-12 for fp16, 2^-25 for fp32).
     A mismatching row pairs with the unique mismatching column whose residual
     agrees within the two thresholds. Returns sorted (row, col) with -1 for an
     unpaired side.
@@ -345,7 +353,6 @@ def locate_post_hoc(
     bsum = 0.0 if bias is None else float(np.asarray(bias, np.float64).sum())
     bcol = np.zeros(c.shape[1]) if bias is None else m * np.asarray(bias, np.float64)
     rres = c.sum(axis=1) - (a @ b.sum(axis=1) + bsum)
-    unit = 2.0 ** -9
     rthr = tk * np.abs(c).max(axis=1) + unit * np.abs(c).sum(axis=1)
     cres = c.sum(axis=0) - (a.sum(axis=0) @ b + bcol)
     cthr = tk * np.abs(c).max(axis=0) + unit * np.abs(c).sum(axis=0)

@@ -17,6 +17,9 @@ giving its root directory:
       (pytorch/abft/injector.py:19-189) produces for several seeds,
       probabilities and sample rates, plus one export_summary()
       (pytorch/abft/stats.py:175-220).
+  ref_checker_cases_f16_f32.npz / .json
+      the same check on fp16 and fp32 operands (its sums then have the
+      operands' type), including a ragged shape and a bias.
   ref_config1_cases.json
       CheapSumChecker.check results at the BASELINE config-1 size
       (A[512 x 4096] . B[4096 x 4096], seeds 0-4, clean and with one
@@ -146,6 +149,51 @@ def run_injector(abft):
     return out, summary
 
 
+DTYPE_CASES = [
+    # name, M, K, N, bias, seed, fault magnitude (as CASES)
+    ("clean", 64, 128, 96, False, 0, None),
+    ("fault_1", 64, 128, 96, False, 0, 1.0),
+    ("ragged_bias_clean", 200, 136, 72, True, 1, None),
+    ("bias_fault_max", 200, 136, 72, True, 1, "max"),
+    ("mid_clean", 256, 256, 128, False, 3, None),
+    ("mid_fault_small", 256, 256, 128, False, 3, 0.05),
+]
+
+
+def run_dtype_cases(abft):
+    """CheapSumChecker.check on fp16 and fp32 CPU tensors (the python
+    backend's sums then have the operands' type)."""
+    from abft.checkers import OpMeta
+
+    checker = abft.CheapSumChecker(abft.AbftConfig(enable=True))
+    arrays, meta = {}, []
+    for dt, tag in ((torch.float16, "f16"), (torch.float32, "f32")):
+        for name, m, k, n, with_bias, seed, fault in DTYPE_CASES:
+            g = torch.Generator().manual_seed(seed)
+            a = (torch.randn(m, k, generator=g) * k ** -0.5).to(dt)
+            w = (torch.randn(n, k, generator=g) * k ** -0.5).to(dt)
+            b = (torch.randn(n, generator=g) * 0.02).to(dt) if with_bias else None
+            c = F.linear(a, w, b)
+            idx, mag = None, None
+            if fault is not None:
+                idx = random.Random(seed).randrange(c.numel())
+                mag = float(2.0 ** 8 * c.float().abs().max().item()) if fault == "max" else float(fault)
+                c = c.clone()
+                c.view(-1)[idx] += mag
+            res = checker.check(a, w.t(), c, OpMeta("linear", "prefill", "golden"), bias_1d=b)
+            key = f"{tag}_{name}"
+            view = torch.int16 if dt == torch.float16 else torch.int32
+            for suffix, t in (("a", a), ("w", w), ("c", c), ("bias", b)):
+                if t is not None:
+                    arrays[f"{key}_{suffix}"] = t.contiguous().view(view).numpy().copy()
+            meta.append({"name": key, "dtype": tag, "M": m, "K": k, "N": n, "bias": with_bias, "seed": seed,
+                         "fault_index": idx, "fault_row": None if idx is None else idx // n,
+                         "fault_col": None if idx is None else idx % n, "fault_magnitude": mag,
+                         "ok": bool(res.ok), "abs_err": res.abs_err, "rel_err": res.rel_err,
+                         "abft_corner": res.abft_corner, "sum_c": res.sum_c})
+    return arrays, meta
+
+
 CONFIG1_SEEDS = [0, 1, 2, 3, 4]
 
 
@@ -201,6 +249,9 @@ def main():
     inj, summary = run_injector(abft)
     (HERE / "ref_injector_sequences.json").write_text(json.dumps({"configs": inj, "summary_config0": summary},
                                                                  indent=1))
+    d_arrays, d_meta = run_dtype_cases(abft)
+    np.savez_compressed(HERE / "ref_checker_cases_f16_f32.npz", **d_arrays)
+    (HERE / "ref_checker_cases_f16_f32.json").write_text(json.dumps(d_meta, indent=1))
     cfg1 = run_config1(abft)
     (HERE / "ref_config1_cases.json").write_text(json.dumps(cfg1, indent=1))
     print(f"wrote {len(meta)} checker cases, {len(inj)} injector sequences and {len(cfg1)} config-1 cases to {HERE}")

@@ -131,11 +131,18 @@ def _header_defines():
     ("ABFT_STATUS_SUSPECT", N.STATUS_SUSPECT), ("ABFT_SUSPECT_ROWS", N.SUSPECT_ROWS),
     ("ABFT_REC_DETECTED", N.REC_DETECTED), ("ABFT_REC_LOCATED", N.REC_LOCATED),
     ("ABFT_REC_CORRECTED", N.REC_CORRECTED), ("ABFT_REC_SUPPRESSED", N.REC_SUPPRESSED),
-    ("ABFT_CHECK_LOCATE", N.CHECK_LOCATE), ("ABFT_CHECK_BF16_SUMS", N.CHECK_BF16_SUMS),
-    ("ABFT_MAX_INJECT", N.MAX_INJECT),
+    ("ABFT_CHECK_LOCATE", N.CHECK_LOCATE), ("ABFT_CHECK_NATIVE_SUMS", N.CHECK_NATIVE_SUMS),
+    ("ABFT_MAX_INJECT", N.MAX_INJECT), ("ABFT_DTYPE_BF16", N.DTYPE_BF16), ("ABFT_DTYPE_F16", N.DTYPE_F16),
+    ("ABFT_DTYPE_F32", N.DTYPE_F32), ("ABFT_B200_VERSION", N.LIB_VERSION),
 ])
 def test_binding_constants_match_the_header(name, value):
     assert _header_defines()[name] == value
+
+
+def test_bf16_sums_flag_is_the_native_sums_bit():
+    text = (_build.INCLUDE_DIR / "abft_b200.h").read_text()
+    assert re.search(r"#define\s+ABFT_CHECK_BF16_SUMS\s+ABFT_CHECK_NATIVE_SUMS", text)
+    assert N.CHECK_BF16_SUMS == N.CHECK_NATIVE_SUMS
 
 
 def test_oracle_suspect_rule_matches_the_header():

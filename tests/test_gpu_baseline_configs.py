@@ -178,3 +178,44 @@ def test_no_false_positive_on_llm_like_data(cuda_device, m, n, k, kind, seed):
     r2 = rep2.read()
     assert r2.coords() == [(i, j)] and r2.n_corrected == 1
     assert (c2.float() - ref).abs().max().item() / ref.abs().max().item() <= OUT_TOL
+
+
+def test_b200_and_reference_rules_disagree_exactly_where_predicted(cuda_device, config1):
+    """The fused kernel's per-row rule (|residual| > tau sqrt(K) max|C_row
+    segment|) and the reference's scalar rule (|corner - sum_c| > 1e-2 and
+    relative > 1e-2, pytorch/abft/checkers.py:96-110) flag different faults:
+    a fault small against the whole output's sum but large against its row
+    is caught by the row rule only, and the scalar rule misses it. Faults at
+    half and twice each rule's bound (config-1 inputs, seed 0) must give
+    each rule's flag exactly as the oracle predicts, so the calls on which
+    the two backends disagree are the predicted ones."""
+    clean_case = next(c for c in config1 if c["seed"] == 0 and not c["fault"])
+    a, w, c = config1_operands(0, clean_case, cuda_device)
+    af, wf = a.float().cpu().numpy(), w.float().cpu().numpy()
+    c_np = c.float().cpu().numpy()
+    m, n, k = af.shape[0], wf.shape[0], af.shape[1]
+    # the scalar rule's bound on the whole output; the row rule's bound of
+    # the fault's 120-column row segment (128-wide tiles)
+    ref_bound = 1e-2 * max(abs(float(c_np.astype(np.float64).sum())), 1.0)
+    tk = float(np.float32(1e-3 * np.sqrt(k)))
+    disagree = 0
+    for (i, j) in [(7, 100), (300, 2000)]:
+        s0 = (j // 120) * 120
+        row_bound = tk * float(np.abs(c_np[i, s0:s0 + 120]).max())
+        for delta in (0.5 * row_bound, 2.0 * row_bound, 0.5 * ref_bound, 2.0 * ref_bound):
+            # predictions of the two oracles
+            row = O.rowcheck_gemm(af[i:i + 1], wf, tile_n=120, inject=[(0, j, float(delta))])
+            b200_pred = len(row.records) == 1
+            cf = c_np.copy()
+            cf[i, j] = O.bf16_round(np.array([cf[i, j] + np.float32(delta)], np.float32))[0]
+            ref_pred = not O.cheap_sum_check(af, wf.T, cf, emulate_bf16=True).ok
+            # the library: the fused kernel (fault on the accumulator) and the
+            # bf16-sum post-hoc check of the reference rule (fault in C)
+            _, rep = ops.abft_gemm(a, w, mode=CHECKED, tile_n=128, inject=[(i, j, float(delta))])
+            b200_got = rep.read().coords() == [(i, j)]
+            cc = c.clone()
+            cc[i, j] += float(delta)
+            ref_got = ops.check_only(a, w, cc, b_layout="nk", bf16_sums=True).read().ref_ok == 0
+            assert (b200_got, ref_got) == (b200_pred, ref_pred), (delta, i, j)
+            disagree += b200_got != ref_got
+    assert disagree > 0  # the rules do differ on this data: between the two bounds

@@ -460,3 +460,56 @@ def test_back_to_back_stream_k_launches_stay_clean(cuda_device, m, n, k, tile_m)
         r = N.FaultReport.from_bytes(host[i * 2048:(i + 1) * 2048])
         assert r.n_faults == 0 and r.status == 0, (i, r.records[:3])
         assert torch.equal(outs[i], outs[0]), i
+
+
+# ------------------------------------------- post-hoc check on fp16 / fp32 operands
+def _dtype_golden(golden_dir, device):
+    import json
+    import os
+
+    meta = json.load(open(os.path.join(golden_dir, "ref_checker_cases_f16_f32.json")))
+    arrays = np.load(os.path.join(golden_dir, "ref_checker_cases_f16_f32.npz"))
+    for case in meta:
+        dt = torch.float16 if case["dtype"] == "f16" else torch.float32
+
+        def dev(name, dt=dt):
+            return torch.from_numpy(arrays[name]).view(dt).to(device)
+
+        n = case["name"]
+        yield case, dev(n + "_a"), dev(n + "_w"), dev(n + "_c"), (dev(n + "_bias") if case["bias"] else None)
+
+
+def test_check_only_f16_f32_reproduce_reference(cuda_device, golden_dir):
+    """The reference's native checker dispatches on fp16, bf16 and fp32
+    (pytorch/abft/kernels/abft_fused.cu:116-118): on its own fp16 / fp32
+    (A, B, C, bias) the library gives its flags, with native-type sums for
+    fp16 (as the python backend's fp16 tensors) and fp32 sums for fp32."""
+    for case, a, w, c, b in _dtype_golden(golden_dir, cuda_device):
+        native = case["dtype"] == "f16"
+        tol = 2 ** -10 if native else 1e-5
+        for layout, bb in (("nk", w), ("kn", w.t().contiguous())):
+            r = ops.check_only(a, bb, c, b, b_layout=layout, bf16_sums=native).read()
+            assert (r.ref_ok == 1) == case["ok"], (case["name"], layout)
+            for key, ref in (("corner", "abft_corner"), ("sum_c", "sum_c")):
+                got = getattr(r, key)
+                assert abs(got - case[ref]) <= tol * max(abs(case[ref]), 1.0), (case["name"], key, got, case[ref])
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_check_only_f16_f32_locate_post_hoc_fault(cuda_device, dtype):
+    m, n, k = 300, 264, 136
+    g = torch.Generator().manual_seed(9)
+    a = (torch.randn(m, k, generator=g) * k ** -0.5).to(dtype)
+    w = (torch.randn(n, k, generator=g) * k ** -0.5).to(dtype)
+    b = (torch.randn(n, generator=g) * 0.02).to(dtype)
+    c = (a.double() @ w.double().T + b.double()).to(dtype)
+    c2 = c.clone()
+    c2[17, 33] += 5.0
+    unit = 2.0 ** -12 if dtype == torch.float16 else 2.0 ** -25
+    for cc, want in ((c, []), (c2, [(17, 33)])):
+        for layout, bb in (("nk", w), ("kn", w.t().contiguous())):
+            r = ops.check_only(a.to(cuda_device), bb.to(cuda_device), cc.to(cuda_device), b.to(cuda_device),
+                               b_layout=layout, locate=True).read()
+            f64 = [t.double().numpy() for t in (a, w, cc, b)]
+            o = O.locate_post_hoc(f64[0], f64[1].T, f64[2], f64[3], unit=unit)
+            assert r.coords() == o == want, (dtype, layout)

@@ -370,3 +370,24 @@ def test_b200_narrow_linears_fused_on_padded_copies(cuda_device, k, n, bias):
             idx = O.InjectorRng(5).maybe_inject(16 * n, True, 1.0)
             assert [(c["row"], c["col"]) for c in s["faults"]["located"]] == [(idx // n, idx % n)]
             assert s["faults"]["corrected_total"] == 1
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_f16_f32_linears_checked_not_skipped(cuda_device, dtype):
+    """fp16 / fp32 linears (the reference's --dtype float16|float32) take the
+    reference flow -- torch GEMM, then the native scalar check on operands
+    of that type -- instead of being counted as unsupported; a perturbed
+    output fails the check."""
+    torch.manual_seed(3)
+    x = torch.randn(64, 256, device=cuda_device).to(dtype)
+    w = (torch.randn(512, 256, device=cuda_device) * 256 ** -0.5).to(dtype)
+    b = (torch.randn(512, device=cuda_device) * 0.02).to(dtype)
+    for backend in ("b200", "fused", "python"):
+        cfg = AbftConfig(enable=True, checker_backend=backend, inject_fault=True, inject_probability=1.0,
+                         inject_magnitude=64.0, seed=3)
+        stats = AbftStatsCollector()
+        with torch.inference_mode(), AbftInjector(cfg, CheapSumChecker(cfg), stats):
+            torch.nn.functional.linear(x, w, b)
+        torch.cuda.synchronize()
+        assert stats.skipped_unsupported == 0 and stats.total_checks == 1, backend
+        assert stats.total_failures == 1 and stats.total_detected_injections == 1, backend

@@ -27,7 +27,7 @@ def test_library_exports_every_declared_symbol():
     L = N.lib()
     for name in declared_functions():
         assert hasattr(L, name), name
-    assert L.abft_version() == N.LIB_VERSION == 2
+    assert L.abft_version() == N.LIB_VERSION == 3
 
 
 def test_status_strings():

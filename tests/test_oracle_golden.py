@@ -231,3 +231,47 @@ def test_config1_cheap_sum_bf16_emulation_matches_reference(config1_cases):
             got = (r.ok, r.abs_err, r.rel_err, r.abft_corner, r.sum_c)
             want = (case["ok"], case["abs_err"], case["rel_err"], case["abft_corner"], case["sum_c"])
             assert got == want, (seed, case["fault"], got, want)
+
+
+# ------------------------------------------------ fp16 and fp32 operands
+def _dtype_cases(golden_dir):
+    meta = json.load(open(os.path.join(golden_dir, "ref_checker_cases_f16_f32.json")))
+    arrays = np.load(os.path.join(golden_dir, "ref_checker_cases_f16_f32.npz"))
+
+    def val(key, tag):
+        raw = arrays[key]
+        return raw.view(np.float16).astype(np.float32) if tag == "f16" else raw.view(np.float32)
+
+    for c in meta:
+        n, tag = c["name"], c["dtype"]
+        yield (c, val(n + "_a", tag), val(n + "_w", tag), val(n + "_c", tag),
+               val(n + "_bias", tag) if c["bias"] else None)
+
+
+def test_cheap_sum_f16_emulation_matches_reference(golden_dir):
+    """fp16 operands: the python backend's sums are fp16 tensors; the oracle's
+    fp16 rounding of every intermediate reproduces its results bit for bit."""
+    n = 0
+    for c, a, w, cc, b in _dtype_cases(golden_dir):
+        if c["dtype"] != "f16":
+            continue
+        r = O.cheap_sum_check(a, w.T, cc, b, emulate_f16=True)
+        assert (r.ok, r.abs_err, r.rel_err, r.abft_corner, r.sum_c) == \
+            (c["ok"], c["abs_err"], c["rel_err"], c["abft_corner"], c["sum_c"]), c["name"]
+        n += 1
+    assert n == 6
+
+
+def test_cheap_sum_f32_matches_reference(golden_dir):
+    """fp32 operands: fp32 sums in the reference, float64 here -- same flags,
+    values within fp32 rounding."""
+    n = 0
+    for c, a, w, cc, b in _dtype_cases(golden_dir):
+        if c["dtype"] != "f32":
+            continue
+        r = O.cheap_sum_check(a, w.T, cc, b)
+        assert r.ok == c["ok"], c["name"]
+        for got, want in ((r.abft_corner, c["abft_corner"]), (r.sum_c, c["sum_c"])):
+            assert abs(got - want) <= 1e-5 * max(1.0, abs(want)), c["name"]
+        n += 1
+    assert n == 6

@@ -22,7 +22,12 @@ MODE_REF = 4
 MODE_REF_BF16 = 8
 
 CHECK_LOCATE = 1
-CHECK_BF16_SUMS = 2
+CHECK_NATIVE_SUMS = 2  # round sums to the operands' type (bf16 / fp16), as the python backend does
+CHECK_BF16_SUMS = CHECK_NATIVE_SUMS
+
+DTYPE_BF16 = 0
+DTYPE_F16 = 1
+DTYPE_F32 = 2
 
 STATUS_FAULT = 1
 STATUS_UNLOCATED = 2
@@ -41,7 +46,7 @@ MAX_INJECT = 64
 REPORT_HEADER_BYTES = 64
 RECORD_BYTES = 24
 BATCH_COUNT_BYTES = 16  # uint32 {faults, located, corrected, 0} per batch after the records
-LIB_VERSION = 2
+LIB_VERSION = 3
 
 EXPORTED_SYMBOLS = (
     "abft_version",
@@ -135,6 +140,7 @@ class CheckArgs(ctypes.Structure):
         ("report", ctypes.c_void_p),
         ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_size_t),
+        ("dtype", ctypes.c_int32),
     ]
 
 

@@ -62,8 +62,9 @@ def _as_lib_operands(
     for name, t in (("a", a_2d), ("b", b_2d), ("c", c_2d)):
         if not t.is_cuda:
             raise UnsupportedOperand(f"{name} is not a CUDA tensor; the library has no CPU path")
-        if t.dtype != torch.bfloat16:
-            raise UnsupportedOperand(f"{name} is {t.dtype}; the library checks bfloat16 operands")
+        if t.dtype not in ops.CHECK_DTYPES or t.dtype != a_2d.dtype:
+            raise UnsupportedOperand(f"{name} is {t.dtype}; the library checks bfloat16, float16 or float32 "
+                                     "operands of one type")
     k = a_2d.shape[1]
     n = b_2d.shape[1]
     if k % 8 or n % 8:
@@ -79,8 +80,8 @@ def _as_lib_operands(
         b, layout = b_2d.contiguous(), "kn"
     bias = None
     if bias_1d is not None:
-        if not bias_1d.is_cuda or bias_1d.dtype != torch.bfloat16:
-            raise UnsupportedOperand("bias must be a CUDA bfloat16 tensor")
+        if not bias_1d.is_cuda or bias_1d.dtype != a_2d.dtype:
+            raise UnsupportedOperand(f"bias must be a CUDA {a_2d.dtype} tensor")
         bias = bias_1d.contiguous()
     return a, b, layout, c, bias
 
@@ -97,8 +98,8 @@ def _padded_operands(
     checked for the same quantities as the original operands (up to fp32
     summation order, like any other call).
     """
-    if bias_1d is not None and (not bias_1d.is_cuda or bias_1d.dtype != torch.bfloat16):
-        raise UnsupportedOperand("bias must be a CUDA bfloat16 tensor")
+    if bias_1d is not None and (not bias_1d.is_cuda or bias_1d.dtype != a_2d.dtype):
+        raise UnsupportedOperand(f"bias must be a CUDA {a_2d.dtype} tensor")
     k = a_2d.shape[1]
     n = b_2d.shape[1]
     pk, pn = -k % 8, -n % 8
@@ -121,10 +122,13 @@ class CheapSumChecker(AbftChecker):
 
     s_a = A.sum(0), s_b = B.sum(1), corner = dot(s_a, s_b) (+ M * sum(bias)),
     sum_c = C.sum(); ok = |corner - sum_c| <= tol_abs or
-    |corner - sum_c| / max(|sum_c|, 1) <= tol_rel. Sums are fp32 unless
+    |corner - sum_c| / max(|sum_c|, 1) <= tol_rel. Operands are bf16, fp16
+    or fp32 (the reference's native checker dispatches on the same three,
+    pytorch/abft/kernels/abft_fused.cu:116-118). Sums are fp32 unless
     ``cfg.bf16_sums`` (checker_backend "python" or force_fp32_check=False),
-    which rounds them to bf16 exactly as the reference's python backend.
-    The result is read back to the host, as in the reference (:103).
+    which rounds them to the operands' type exactly as the reference's
+    python backend does. The result is read back to the host, as in the
+    reference (:103).
     """
 
     locate: bool = False

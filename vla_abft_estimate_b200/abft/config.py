@@ -81,5 +81,6 @@ class AbftConfig:
 
     @property
     def bf16_sums(self) -> bool:
-        """Whether the scalar check rounds its sums to bf16 (python backend)."""
+        """Whether the scalar check rounds its sums to the operands' type
+        (bf16 or fp16), as the python backend's torch reductions do."""
         return self.checker_backend == "python" or not self.force_fp32_check

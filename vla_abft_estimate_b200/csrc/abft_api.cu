@@ -253,19 +253,24 @@ int rows_per_block(int64_t R, int64_t C, int sms) {
   return static_cast<int>(rpb);
 }
 
-// Column sums of a row-major [R, C] bf16 matrix into out[C] (with stats also
-// out_max[C] and out_abs[C]), through partials in `partial` ([nrb][C], and
-// 2 * [nrb][C] more with stats).
+// Column sums of a row-major [R, C] matrix of element type `dtype` into
+// out[C] (with stats also out_max[C] and out_abs[C]), through partials in
+// `partial` ([nrb][C], and 2 * [nrb][C] more with stats).
 int colsum(const void* X, int64_t ld, int64_t R, int64_t C, const float* w, float* partial, float* out,
-           float* out_max, float* out_abs, int sms, cudaStream_t s) {
+           float* out_max, float* out_abs, int sms, cudaStream_t s, int dtype = ABFT_DTYPE_BF16) {
   const int rpb = rows_per_block(R, C, sms);
   const int nrb = static_cast<int>(cdiv(R, rpb));
   float* pstat = out_max != nullptr ? partial + static_cast<int64_t>(nrb) * C : nullptr;
   dim3 g(static_cast<unsigned>(cdiv(C, 64)), static_cast<unsigned>(nrb));
-  colsum_partial_kernel<<<g, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(X), ld, static_cast<int>(R),
-                                          static_cast<int>(C), rpb, w, partial, pstat);
-  reduce_partials_kernel<<<static_cast<unsigned>(cdiv(C, 256)), 256, 0, s>>>(partial, pstat, nrb, static_cast<int>(C),
-                                                                             out, out_max, out_abs);
+  const int r = static_cast<int>(R), c = static_cast<int>(C);
+  if (dtype == ABFT_DTYPE_F16)
+    colsum_partial_kernel<<<g, 256, 0, s>>>(static_cast<const __half*>(X), ld, r, c, rpb, w, partial, pstat);
+  else if (dtype == ABFT_DTYPE_F32)
+    colsum_partial_kernel<<<g, 256, 0, s>>>(static_cast<const float*>(X), ld, r, c, rpb, w, partial, pstat);
+  else
+    colsum_partial_kernel<<<g, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(X), ld, r, c, rpb, w, partial, pstat);
+  reduce_partials_kernel<<<static_cast<unsigned>(cdiv(C, 256)), 256, 0, s>>>(partial, pstat, nrb, c, out, out_max,
+                                                                             out_abs);
   return launch_status();
 }
 
@@ -275,11 +280,40 @@ size_t colsum_partial_floats(int64_t R, int64_t C, int sms, bool with_stats) {
 }
 
 int rowdot(const void* X, int64_t ld, int64_t R, int64_t C, const float* vec, float* out, float* out_max,
-           float* out_abs, cudaStream_t s) {
-  rowdot_kernel<<<static_cast<unsigned>(cdiv(R, 8)), 256, 0, s>>>(static_cast<const __nv_bfloat16*>(X), ld,
-                                                                   static_cast<int>(R), static_cast<int>(C), vec, out,
-                                                                   out_max, out_abs);
+           float* out_abs, cudaStream_t s, int dtype = ABFT_DTYPE_BF16) {
+  const unsigned g = static_cast<unsigned>(cdiv(R, 8));
+  const int r = static_cast<int>(R), c = static_cast<int>(C);
+  if (dtype == ABFT_DTYPE_F16)
+    rowdot_kernel<<<g, 256, 0, s>>>(static_cast<const __half*>(X), ld, r, c, vec, out, out_max, out_abs);
+  else if (dtype == ABFT_DTYPE_F32)
+    rowdot_kernel<<<g, 256, 0, s>>>(static_cast<const float*>(X), ld, r, c, vec, out, out_max, out_abs);
+  else
+    rowdot_kernel<<<g, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(X), ld, r, c, vec, out, out_max, out_abs);
   return launch_status();
+}
+
+// ref_finalize_kernel / locate_finalize_kernel with the bias (and the
+// rounding of native sums) of element type `dtype`.
+void ref_finalize(int dtype, const float* u, const float* v, int K, const void* bias, int N, int M, const float* parts,
+                  int n_parts, float tol_abs, float tol_rel, int native_sums, abft_report* rep, int capacity,
+                  int tile_m, int tile_n, cudaStream_t s) {
+  if (dtype == ABFT_DTYPE_F16)
+    ref_finalize_kernel<<<1, 1024, 0, s>>>(u, v, K, static_cast<const __half*>(bias), N, M, parts, n_parts, tol_abs,
+                                           tol_rel, native_sums, rep, capacity, tile_m, tile_n);
+  else if (dtype == ABFT_DTYPE_F32)
+    ref_finalize_kernel<<<1, 1024, 0, s>>>(u, v, K, static_cast<const float*>(bias), N, M, parts, n_parts, tol_abs,
+                                           tol_rel, native_sums, rep, capacity, tile_m, tile_n);
+  else
+    ref_finalize_kernel<<<1, 1024, 0, s>>>(u, v, K, static_cast<const __nv_bfloat16*>(bias), N, M, parts, n_parts,
+                                           tol_abs, tol_rel, native_sums, rep, capacity, tile_m, tile_n);
+}
+
+int elem_bytes(int dtype) { return dtype == ABFT_DTYPE_F32 ? 4 : 2; }
+
+// Rounding bound of a stored element relative to its magnitude, 2^-(p+1)
+// for p significand bits (the convention the bf16 bound 2^-9 set).
+float unit_roundoff(int dtype) {
+  return dtype == ABFT_DTYPE_F32 ? 1.0f / 33554432.0f : (dtype == ABFT_DTYPE_F16 ? 1.0f / 4096.0f : 1.0f / 512.0f);
 }
 
 // Tile schedule of one launch. Whole-tile (data-parallel) waves first; when
@@ -929,10 +963,9 @@ int abft_gemm_bf16(const abft_gemm_args* args, void* stream) {
     if (rc != ABFT_OK) return rc;
     // corner + (rows of C) * sum(bias): the bias runs along the kernel's
     // rows when the operands are swapped
-    ref_finalize_kernel<<<1, 1024, 0, s>>>(u, vf, p.K, p.bias, swap ? p.M : p.N, swap ? p.N : p.M, p.tile_sumc,
-                                           p.num_tiles * kEpiWarps * (ws.pair ? 2 : 1), a->tol_abs,
-                                           a->tol_rel, (a->mode & ABFT_MODE_REF_BF16) ? 1 : 0, p.report, p.capacity,
-                                           ws.tile_m, bd);
+    ref_finalize(ABFT_DTYPE_BF16, u, vf, p.K, p.bias, swap ? p.M : p.N, swap ? p.N : p.M, p.tile_sumc,
+                 p.num_tiles * kEpiWarps * (ws.pair ? 2 : 1), a->tol_abs, a->tol_rel,
+                 (a->mode & ABFT_MODE_REF_BF16) ? 1 : 0, p.report, p.capacity, ws.tile_m, bd, s);
     rc = launch_status();
   }
   return rc;
@@ -987,9 +1020,12 @@ int abft_check_only(const abft_check_args* c, void* stream) {
   const int64_t M = c->M, N = c->N, K = c->K;
   if (M <= 0 || N <= 0 || K <= 0 || c->report_capacity < 0 || (c->b_kn != 0 && c->b_kn != 1))
     return ABFT_ERR_INVALID_ARG;
-  if (c->flags & ~(ABFT_CHECK_LOCATE | ABFT_CHECK_BF16_SUMS)) return ABFT_ERR_INVALID_ARG;
+  if (c->flags & ~(ABFT_CHECK_LOCATE | ABFT_CHECK_NATIVE_SUMS)) return ABFT_ERR_INVALID_ARG;
+  if (c->dtype != ABFT_DTYPE_BF16 && c->dtype != ABFT_DTYPE_F16 && c->dtype != ABFT_DTYPE_F32)
+    return ABFT_ERR_INVALID_ARG;
   if (M > (1ll << 30) || N > (1ll << 30) || K > (1ll << 30)) return ABFT_ERR_UNSUPPORTED;
   if (c->lda < K || c->ldc < N || c->ldb < (c->b_kn ? N : K)) return ABFT_ERR_INVALID_ARG;
+  // rows are read 8 elements at a time (16 or 32 bytes): every row start aligned
   if ((K % 8) || (N % 8) || (c->lda % 8) || (c->ldb % 8) || (c->ldc % 8)) return ABFT_ERR_ALIGNMENT;
   if (!aligned16(c->A) || !aligned16(c->B) || !aligned16(c->C) || !aligned16(c->report)) return ABFT_ERR_ALIGNMENT;
   if (c->bias != nullptr && !aligned16(c->bias)) return ABFT_ERR_ALIGNMENT;
@@ -1004,43 +1040,51 @@ int abft_check_only(const abft_check_args* c, void* stream) {
   const int sms = info.sms;
   CheckWs w;
   check_ws_layout(static_cast<float*>(c->workspace), M, N, K, sms, &w);
-  const __nv_bfloat16* bias = static_cast<const __nv_bfloat16*>(c->bias);
+  const int dt = c->dtype;
 
   if (cudaMemsetAsync(c->report, 0, sizeof(abft_report), s) != cudaSuccess) return launch_status(), ABFT_ERR_CUDA;
   abft_report* rep = static_cast<abft_report*>(c->report);
 
   // s_a = A.sum(0) and s_b = B.sum(1)   (pytorch/abft/checkers.py:117-118)
-  rc = colsum(c->A, c->lda, M, K, nullptr, w.pa, w.u, nullptr, nullptr, sms, s);
+  rc = colsum(c->A, c->lda, M, K, nullptr, w.pa, w.u, nullptr, nullptr, sms, s, dt);
   if (rc != ABFT_OK) return rc;
   if (c->b_kn == 0)
-    rc = colsum(c->B, c->ldb, N, K, nullptr, w.pb, w.v, nullptr, nullptr, sms, s);
+    rc = colsum(c->B, c->ldb, N, K, nullptr, w.pb, w.v, nullptr, nullptr, sms, s, dt);
   else
-    rc = rowdot(c->B, c->ldb, K, N, nullptr, w.v, nullptr, nullptr, s);
+    rc = rowdot(c->B, c->ldb, K, N, nullptr, w.v, nullptr, nullptr, s, dt);
   if (rc != ABFT_OK) return rc;
   // row sums of C (sum_c = sum of the row sums, fixed order)
-  rc = rowdot(c->C, c->ldc, M, N, nullptr, w.rsum, w.rmax, w.rabs, s);
+  rc = rowdot(c->C, c->ldc, M, N, nullptr, w.rsum, w.rmax, w.rabs, s, dt);
   if (rc != ABFT_OK) return rc;
-  ref_finalize_kernel<<<1, 1024, 0, s>>>(w.u, w.v, static_cast<int>(K), bias, static_cast<int>(N), static_cast<int>(M),
-                                         w.rsum, static_cast<int>(M), c->tol_abs, c->tol_rel,
-                                         (c->flags & ABFT_CHECK_BF16_SUMS) ? 1 : 0, rep, c->report_capacity, 0, 0);
+  ref_finalize(dt, w.u, w.v, static_cast<int>(K), c->bias, static_cast<int>(N), static_cast<int>(M), w.rsum,
+               static_cast<int>(M), c->tol_abs, c->tol_rel, (c->flags & ABFT_CHECK_NATIVE_SUMS) ? 1 : 0, rep,
+               c->report_capacity, 0, 0, s);
   rc = launch_status();
   if (rc != ABFT_OK || !(c->flags & ABFT_CHECK_LOCATE)) return rc;
 
   // Expected row sums A (B e), expected column sums (e^T A) B, actual column sums.
-  rc = rowdot(c->A, c->lda, M, K, w.v, w.rexp, nullptr, nullptr, s);
+  rc = rowdot(c->A, c->lda, M, K, w.v, w.rexp, nullptr, nullptr, s, dt);
   if (rc != ABFT_OK) return rc;
   if (c->b_kn == 0)
-    rc = rowdot(c->B, c->ldb, N, K, w.u, w.cexp, nullptr, nullptr, s);
+    rc = rowdot(c->B, c->ldb, N, K, w.u, w.cexp, nullptr, nullptr, s, dt);
   else
-    rc = colsum(c->B, c->ldb, K, N, w.u, w.pb, w.cexp, nullptr, nullptr, sms, s);
+    rc = colsum(c->B, c->ldb, K, N, w.u, w.pb, w.cexp, nullptr, nullptr, sms, s, dt);
   if (rc != ABFT_OK) return rc;
-  rc = colsum(c->C, c->ldc, M, N, nullptr, w.pc, w.csum, w.cmax, w.cabs, sms, s);
+  rc = colsum(c->C, c->ldc, M, N, nullptr, w.pc, w.csum, w.cmax, w.cabs, sms, s, dt);
   if (rc != ABFT_OK) return rc;
   const float thr_k = static_cast<float>(static_cast<double>(c->thr_scale) * sqrt(static_cast<double>(K)));
-  constexpr float kBf16Unit = 1.0f / 512.0f;  // worst-case relative rounding of a stored bf16 element
-  locate_finalize_kernel<<<1, 1024, 0, s>>>(w.rsum, w.rmax, w.rabs, w.rexp, static_cast<int>(M), w.csum, w.cmax,
-                                            w.cabs, w.cexp, static_cast<int>(N), bias, thr_k, kBf16Unit, rep,
-                                            c->report_capacity);
+  const float unit = unit_roundoff(dt);  // worst-case relative rounding of a stored element
+  const int m32 = static_cast<int>(M), n32 = static_cast<int>(N);
+  if (dt == ABFT_DTYPE_F16)
+    locate_finalize_kernel<<<1, 1024, 0, s>>>(w.rsum, w.rmax, w.rabs, w.rexp, m32, w.csum, w.cmax, w.cabs, w.cexp, n32,
+                                              static_cast<const __half*>(c->bias), thr_k, unit, rep, c->report_capacity);
+  else if (dt == ABFT_DTYPE_F32)
+    locate_finalize_kernel<<<1, 1024, 0, s>>>(w.rsum, w.rmax, w.rabs, w.rexp, m32, w.csum, w.cmax, w.cabs, w.cexp, n32,
+                                              static_cast<const float*>(c->bias), thr_k, unit, rep, c->report_capacity);
+  else
+    locate_finalize_kernel<<<1, 1024, 0, s>>>(w.rsum, w.rmax, w.rabs, w.rexp, m32, w.csum, w.cmax, w.cabs, w.cexp, n32,
+                                              static_cast<const __nv_bfloat16*>(c->bias), thr_k, unit, rep,
+                                              c->report_capacity);
   return launch_status();
 }
 

@@ -6,7 +6,8 @@
 //   transpose_encode_kernel  K-major copy of an N-major right operand
 //                          B[K, N] (torch.bmm's mat2), with the same
 //                          checksum block computed on the way
-//   colsum_partial_kernel  column sums of a row-major [R, C] bf16 matrix over
+//   colsum_partial_kernel  column sums of a row-major [R, C] matrix (bf16, fp16
+//                          or fp32) over
 //                          blocks of rows (optionally row-weighted, with |x| max)
 //   reduce_partials_kernel sum (and max) of those partials in fixed order
 //   rowdot_kernel          per-row sum or dot with a vector (warp per row)
@@ -19,6 +20,7 @@
 #pragma once
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include "../../include/abft_b200.h"
 
@@ -34,6 +36,42 @@ __device__ __forceinline__ void unpack8(const uint4 w, float (&x)[8]) {
   x[6] = __uint_as_float(w.w << 16);
   x[7] = __uint_as_float(w.w & 0xFFFF0000u);
 }
+
+// Eight consecutive elements of a row as fp32 (16- or 32-byte aligned),
+// for the element types of the post-hoc check: bf16, fp16 or fp32.
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&x)[8]) {
+  unpack8(__ldg(reinterpret_cast<const uint4*>(p)), x);
+}
+__device__ __forceinline__ void load8(const __half* p, float (&x)[8]) {
+  const uint4 q = __ldg(reinterpret_cast<const uint4*>(p));
+  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+    x[2 * i] = f.x;
+    x[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void load8(const float* p, float (&x)[8]) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+  const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+  x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+  x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+}
+__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
+__device__ __forceinline__ float to_f32(float v) { return v; }
+
+// Round an fp32 value to the element type T (and back): the rounding of a
+// torch reduction whose result has type T (fp32 accumulation inside).
+template <typename T>
+__device__ __forceinline__ float round_to(float x);
+template <>
+__device__ __forceinline__ float round_to<__nv_bfloat16>(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+template <>
+__device__ __forceinline__ float round_to<__half>(float x) { return __half2float(__float2half_rn(x)); }
+template <>
+__device__ __forceinline__ float round_to<float>(float x) { return x; }
 
 // Split v into three bf16 terms whose sum carries 24 significant bits:
 // hi = rn(v), mid = rn(v - hi), lo = rn(v - hi - mid); both differences are
@@ -215,7 +253,8 @@ __global__ void __launch_bounds__(256) transpose_encode_kernel(const __nv_bfloat
 // out_sum[rb*Cc + c] = sum_{r in block rb} w[r] * X[r, c]   (w == nullptr: 1)
 // with stats (out_stat != nullptr): out_stat[rb*Cc + c] = max |X[r, c]| and
 // out_stat[(nrb + rb)*Cc + c] = sum |X[r, c]|.
-__global__ void __launch_bounds__(256) colsum_partial_kernel(const __nv_bfloat16* __restrict__ X, int64_t ld, int R,
+template <typename T>
+__global__ void __launch_bounds__(256) colsum_partial_kernel(const T* __restrict__ X, int64_t ld, int R,
                                                              int Cc, int rows_per_block, const float* __restrict__ w,
                                                              float* __restrict__ out_sum, float* __restrict__ out_stat) {
   __shared__ float red[3][32][65];
@@ -229,9 +268,8 @@ __global__ void __launch_bounds__(256) colsum_partial_kernel(const __nv_bfloat16
   for (int e = 0; e < 8; ++e) s[e] = m[e] = a[e] = 0.f;
   if (col0 < Cc) {
     for (int r = r0 + rg; r < r1; r += 32) {
-      const uint4 q = __ldg(reinterpret_cast<const uint4*>(X + static_cast<int64_t>(r) * ld + col0));
       float x[8];
-      unpack8(q, x);
+      load8(X + static_cast<int64_t>(r) * ld + col0, x);
       const float wr = (w != nullptr) ? __ldg(w + r) : 1.f;
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
@@ -291,18 +329,18 @@ __global__ void __launch_bounds__(256) reduce_partials_kernel(const float* __res
 // Warp per row: out[r] = sum_c X[r,c] * (vec ? vec[c] : 1); with stats
 // out_max[r] = max_c |X[r,c]| and out_abs[r] = sum_c |X[r,c]|.
 // 256 threads (8 rows) per block. Cc % 8 == 0, vec 16-byte aligned.
-__global__ void __launch_bounds__(256) rowdot_kernel(const __nv_bfloat16* __restrict__ X, int64_t ld, int R, int Cc,
+template <typename T>
+__global__ void __launch_bounds__(256) rowdot_kernel(const T* __restrict__ X, int64_t ld, int R, int Cc,
                                                      const float* __restrict__ vec, float* __restrict__ out,
                                                      float* __restrict__ out_max, float* __restrict__ out_abs) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = blockIdx.x * 8 + warp;
   if (r >= R) return;
-  const __nv_bfloat16* row = X + static_cast<int64_t>(r) * ld;
+  const T* row = X + static_cast<int64_t>(r) * ld;
   float acc = 0.f, mx = 0.f, ab = 0.f;
   for (int c = lane * 8; c < Cc; c += 256) {
-    const uint4 q = __ldg(reinterpret_cast<const uint4*>(row + c));
     float x[8];
-    unpack8(q, x);
+    load8(row + c, x);
     if (vec != nullptr) {
       const float4 va = __ldg(reinterpret_cast<const float4*>(vec + c));
       const float4 vb = __ldg(reinterpret_cast<const float4*>(vec + c + 4));
@@ -357,52 +395,45 @@ __device__ __forceinline__ float block_sum_1024(float v, float* scratch /*32*/) 
   return scratch[0];
 }
 
-__device__ __forceinline__ float round_bf16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
-
 // One block of 1024 threads. Follows pytorch/abft/checkers.py:112-126
 // (corner = dot(s_a, s_b) + m * sum(bias), sum_c = sum(C)) and :96-110
 // (diff, rel = diff / max(|sum_c|, 1), ok = diff <= tol_abs or rel <= tol_rel).
-// With bf16_sums every intermediate is rounded to bf16, as the python
-// backend's bf16 tensors are (s_a, s_b, dot, bias sum, m * bias sum,
-// corner, sum_c, diff, rel) and the tolerances are compared as bf16 values.
+// With native_sums every intermediate is rounded to the operands' type T,
+// as the python backend's tensors of that type are (s_a, s_b, dot, bias
+// sum, m * bias sum, corner, sum_c, diff, rel), and the tolerances are
+// compared as values of type T (for fp32 operands nothing changes).
+template <typename T>
 __global__ void __launch_bounds__(1024) ref_finalize_kernel(const float* __restrict__ u, const float* __restrict__ v,
-                                                            int K, const __nv_bfloat16* __restrict__ bias, int N,
+                                                            int K, const T* __restrict__ bias, int N,
                                                             int M, const float* __restrict__ parts, int n_parts,
-                                                            float tol_abs, float tol_rel, int bf16_sums,
+                                                            float tol_abs, float tol_rel, int native_sums,
                                                             abft_report* rep, int capacity, int tile_m, int tile_n) {
   __shared__ float scratch[32];
+  auto rn = [&](float x) { return native_sums ? round_to<T>(x) : x; };
   float c = 0.f;
-  for (int k = threadIdx.x; k < K; k += 1024) {
-    const float uk = bf16_sums ? round_bf16(u[k]) : u[k];
-    const float vk = bf16_sums ? round_bf16(v[k]) : v[k];
-    c = fmaf(uk, vk, c);
-  }
-  float corner = block_sum_1024(c, scratch);
-  if (bf16_sums) corner = round_bf16(corner);
+  for (int k = threadIdx.x; k < K; k += 1024) c = fmaf(rn(u[k]), rn(v[k]), c);
+  float corner = rn(block_sum_1024(c, scratch));
   if (bias != nullptr) {
     float b = 0.f;
-    for (int j = threadIdx.x; j < N; j += 1024) b += __bfloat162float(bias[j]);
-    float bs = block_sum_1024(b, scratch);
-    if (bf16_sums) {
-      bs = round_bf16(bs);
-      corner = round_bf16(corner + round_bf16(static_cast<float>(M) * bs));
-    } else {
+    for (int j = threadIdx.x; j < N; j += 1024) b += to_f32(bias[j]);
+    const float bs = rn(block_sum_1024(b, scratch));
+    if (native_sums)
+      corner = rn(corner + rn(static_cast<float>(M) * bs));
+    else
       corner += static_cast<float>(M) * bs;
-    }
   }
   float s = 0.f;
   for (int i = threadIdx.x; i < n_parts; i += 1024) s += parts[i];
-  float sum_c = block_sum_1024(s, scratch);
-  if (bf16_sums) sum_c = round_bf16(sum_c);
+  const float sum_c = rn(block_sum_1024(s, scratch));
   if (threadIdx.x == 0) {
     float diff = fabsf(corner - sum_c);
     float rel = diff / fmaxf(fabsf(sum_c), 1.f);
     float ta = tol_abs, tr = tol_rel;
-    if (bf16_sums) {
-      diff = round_bf16(diff);
-      rel = round_bf16(diff / fmaxf(fabsf(sum_c), 1.f));
-      ta = round_bf16(tol_abs);
-      tr = round_bf16(tol_rel);
+    if (native_sums) {
+      diff = rn(diff);
+      rel = rn(diff / fmaxf(fabsf(sum_c), 1.f));
+      ta = rn(tol_abs);
+      tr = rn(tol_rel);
     }
     const bool ok = (diff <= ta) || (rel <= tr);
     rep->corner = corner;
@@ -424,12 +455,14 @@ __global__ void __launch_bounds__(1024) ref_finalize_kernel(const float* __restr
 // each bound adds the worst-case rounding of the summed elements:
 //   row i:  thr = thr_k * max_j |C[i,j]| + unit_out * sum_j |C[i,j]|
 //   col j:  thr = thr_k * max_i |C[i,j]| + unit_out * sum_i |C[i,j]|
-// with thr_k = tau * sqrt(K) and unit_out = 2^-9 for bf16.
+// with thr_k = tau * sqrt(K) and unit_out the relative rounding bound of
+// the type (2^-9 bf16, 2^-12 fp16, 2^-25 fp32).
 constexpr int kLocateMax = 256;
+template <typename T>
 __global__ void __launch_bounds__(1024) locate_finalize_kernel(
     const float* __restrict__ row_sum, const float* __restrict__ row_max, const float* __restrict__ row_abs,
     const float* __restrict__ row_exp, int M, const float* __restrict__ col_sum, const float* __restrict__ col_max,
-    const float* __restrict__ col_abs, const float* __restrict__ col_exp, int N, const __nv_bfloat16* __restrict__ bias,
+    const float* __restrict__ col_abs, const float* __restrict__ col_exp, int N, const T* __restrict__ bias,
     float thr_k, float unit_out, abft_report* rep, int capacity) {
   __shared__ int rows[kLocateMax], cols[kLocateMax];
   __shared__ float rres[kLocateMax], cres[kLocateMax], rthr[kLocateMax], cthr[kLocateMax];
@@ -439,7 +472,7 @@ __global__ void __launch_bounds__(1024) locate_finalize_kernel(
   float bsum = 0.f;
   if (bias != nullptr) {
     float b = 0.f;
-    for (int j = threadIdx.x; j < N; j += 1024) b += __bfloat162float(bias[j]);
+    for (int j = threadIdx.x; j < N; j += 1024) b += to_f32(bias[j]);
     bsum = block_sum_1024(b, scratch);
   }
   if (threadIdx.x == 0) nr = nc = dropped = 0;
@@ -459,7 +492,7 @@ __global__ void __launch_bounds__(1024) locate_finalize_kernel(
     }
   }
   for (int j = threadIdx.x; j < N; j += 1024) {
-    const float bj = bias != nullptr ? static_cast<float>(M) * __bfloat162float(bias[j]) : 0.f;
+    const float bj = bias != nullptr ? static_cast<float>(M) * to_f32(bias[j]) : 0.f;
     const float res = col_sum[j] - (col_exp[j] + bj);
     const float thr = fmaf(thr_k, col_max[j], unit_out * col_abs[j]);
     if (fabsf(res) > thr) {

@@ -419,6 +419,9 @@ def _bmm_call(a, bmat, b_kn, bias, out, bsz, m, n, k, mode, tile_n, tile_m, swap
     return out, (report if mode != N.MODE_OFF else None)
 
 
+CHECK_DTYPES = {torch.bfloat16: N.DTYPE_BF16, torch.float16: N.DTYPE_F16, torch.float32: N.DTYPE_F32}
+
+
 def check_only(
     a: torch.Tensor,
     b: torch.Tensor,
@@ -435,16 +438,23 @@ def check_only(
 ) -> ReportBuffer:
     """Check an existing ``c`` against ``a`` and ``b`` (no GEMM).
 
+    Operands are CUDA tensors of one type: bfloat16, float16 or float32 (the
+    types the reference's native checker dispatches on).
     ``b_layout="kn"``: b is [K, N] (the reference checker's b_2d);
     ``b_layout="nk"``: b is an nn.Linear weight [N, K] (no transpose copy).
     Fills report.corner / sum_c / abs_err / rel_err / ref_ok; ``bf16_sums``
-    rounds the intermediates to bf16 like the reference's python backend;
-    ``locate`` also records mismatching rows and columns.
+    rounds the intermediates to the operands' type (bf16 or fp16) like the
+    reference's python backend on tensors of that type; ``locate`` also
+    records mismatching rows and columns.
     """
-    _require_bf16_cuda("a", a, 2)
-    _require_bf16_cuda("c", c, 2)
-    if b.dim() != 2 or not b.is_cuda or b.dtype != torch.bfloat16:
-        raise ValueError("b must be a 2-D CUDA bfloat16 tensor")
+    dtype = a.dtype
+    if dtype not in CHECK_DTYPES:
+        raise ValueError(f"check_only takes bfloat16, float16 or float32 operands, got {dtype}")
+    for name, t in (("a", a), ("c", c)):
+        if not t.is_cuda or t.dtype != dtype or t.dim() != 2 or t.stride(-1) != 1:
+            raise ValueError(f"{name} must be a 2-D CUDA {dtype} tensor with unit stride in its last dimension")
+    if b.dim() != 2 or not b.is_cuda or b.dtype != dtype:
+        raise ValueError(f"b must be a 2-D CUDA {dtype} tensor")
     m, k = a.shape
     if b_layout == "kn":
         kn = 1
@@ -462,12 +472,13 @@ def check_only(
         b = b.contiguous()
     if tuple(c.shape) != (m, n):
         raise ValueError(f"c must be [{m}, {n}]")
-    if bias is not None:
-        _require_bf16_cuda("bias", bias, 1)
+    if bias is not None and (not bias.is_cuda or bias.dtype != dtype or bias.dim() != 1 or bias.stride(0) != 1):
+        raise ValueError(f"bias must be a contiguous 1-D CUDA {dtype} tensor")
     dev = a.device
     if report is None:
         report = ReportBuffer(DEFAULT_CAPACITY, dev)
     args = N.CheckArgs()
+    args.dtype = CHECK_DTYPES[dtype]
     args.A, args.B, args.C, args.bias = _ptr(a), _ptr(b), _ptr(c), _ptr(bias)
     args.M, args.N, args.K = m, n, k
     args.lda, args.ldb, args.ldc = a.stride(0), b.stride(0), c.stride(0)
