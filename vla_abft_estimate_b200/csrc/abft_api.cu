@@ -308,8 +308,6 @@ void ref_finalize(int dtype, const float* u, const float* v, int K, const void* 
                                            tol_abs, tol_rel, native_sums, rep, capacity, tile_m, tile_n);
 }
 
-int elem_bytes(int dtype) { return dtype == ABFT_DTYPE_F32 ? 4 : 2; }
-
 // Rounding bound of a stored element relative to its magnitude, 2^-(p+1)
 // for p significand bits (the convention the bf16 bound 2^-9 set).
 float unit_roundoff(int dtype) {

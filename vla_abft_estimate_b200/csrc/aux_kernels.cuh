@@ -121,15 +121,25 @@ __global__ void __launch_bounds__(256) encode_weight_kernel(const __nv_bfloat16*
 #pragma unroll
   for (int e = 0; e < 8; ++e) s1[e] = s2[e] = s3[e] = 0.f;
   if (k0 < K) {
-    // Rows rg, rg + 32, ... of the tile, added in that order. Four rows'
-    // loads are issued before any is used (memory-level parallelism: the
-    // pass is bound by HBM latency otherwise); the order of the sums, and
-    // so every bit of the result, is that of a one-row-at-a-time loop.
+    // Rows rg, rg + 32, ... of the tile (at most 8: a tile has at most 256
+    // rows), added in that order. Every load of the thread is issued before
+    // the first is used, so the pass waits for one memory round trip rather
+    // than one per row; the order of the sums is that of a row-at-a-time loop.
     const int nrows = min(bd, N - nt * bd);
     const __nv_bfloat16* base = B + static_cast<int64_t>(nt) * bd * ldb + k0;
-    auto add_row = [&](const uint4& w, int j) {
+    uint4 w[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int j = rg + 32 * u;
+      w[u] = j < nrows ? __ldg(reinterpret_cast<const uint4*>(base + static_cast<int64_t>(j) * ldb))
+                       : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int j = rg + 32 * u;
+      if (j >= nrows) break;
       float x[8];
-      unpack8(w, x);
+      unpack8(w[u], x);
       const float wt = static_cast<float>(j + 1);
       const float sg = col_sign(j);
 #pragma unroll
@@ -138,16 +148,7 @@ __global__ void __launch_bounds__(256) encode_weight_kernel(const __nv_bfloat16*
         s2[e] = fmaf(wt, x[e], s2[e]);
         s3[e] = fmaf(sg, x[e], s3[e]);
       }
-    };
-    int j = rg;
-    for (; j + 96 < nrows; j += 128) {
-      uint4 w[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) w[u] = __ldg(reinterpret_cast<const uint4*>(base + static_cast<int64_t>(j + 32 * u) * ldb));
-#pragma unroll
-      for (int u = 0; u < 4; ++u) add_row(w[u], j + 32 * u);
     }
-    for (; j < nrows; j += 32) add_row(__ldg(reinterpret_cast<const uint4*>(base + static_cast<int64_t>(j) * ldb)), j);
   }
 #pragma unroll
   for (int e = 0; e < 8; ++e) {

@@ -983,23 +983,29 @@ __global__ void __launch_bounds__(kThreads, 1)
             // Whole chunk valid: the column weights split into the chunk's
             // base plus a compile-time offset, and the Thue-Morse sign of
             // base + e is sg(base) * sg(e) (base has its low 5 bits clear).
-            float a0 = 0.f, a1 = 0.f, w0 = 0.f, w1 = 0.f, t0 = 0.f, t1 = 0.f;
+            // Columns e, e + 1 (e even) always have opposite signs, so each
+            // pair goes with one packed add into the accumulator of its sign
+            // (sg(e) = +1: pp, -1: pn); the plain and the signed sums both
+            // follow from those two, and one packed FMA forms the weighted
+            // sum: three checksums for about one instruction per element.
+            float2 pp = make_float2(0.f, 0.f), pn = make_float2(0.f, 0.f), pw = make_float2(0.f, 0.f);
+            float m0 = 0.f, m1 = 0.f;
 #pragma unroll
             for (int e = 0; e < 32; e += 2) {
-              const float x0 = x[e];
-              const float x1 = x[e + 1];
-              a0 += x0;
-              a1 += x1;
-              w0 = fmaf(static_cast<float>(e), x0, w0);
-              w1 = fmaf(static_cast<float>(e + 1), x1, w1);
-              t0 += (__builtin_popcount(e) & 1) ? -x0 : x0;
-              t1 += (__builtin_popcount(e + 1) & 1) ? -x1 : x1;
-              amax = fmaxf(amax, fmaxf(fabsf(x0), fabsf(x1)));
+              const float2 xx = make_float2(x[e], x[e + 1]);
+              if (__builtin_popcount(e) & 1)
+                pn = __fadd2_rn(pn, xx);
+              else
+                pp = __fadd2_rn(pp, xx);
+              pw = __ffma2_rn(make_float2(static_cast<float>(e), static_cast<float>(e + 1)), xx, pw);
+              m0 = fmaxf(m0, fabsf(xx.x));
+              m1 = fmaxf(m1, fabsf(xx.y));
             }
-            const float a = a0 + a1;
-            const float t = t0 + t1;
+            const float a = (pp.x + pp.y) + (pn.x + pn.y);
+            const float t = (pp.x - pp.y) - (pn.x - pn.y);
+            amax = fmaxf(amax, fmaxf(m0, m1));
             s1 += a;
-            s2 += fmaf(static_cast<float>(base + 1), a, w0 + w1);
+            s2 += fmaf(static_cast<float>(base + 1), a, pw.x + pw.y);
             s3 += (__popc(base) & 1) ? -t : t;
           } else {
 #pragma unroll
