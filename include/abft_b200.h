@@ -20,9 +20,9 @@
  *
  * Conventions
  *   - Every pointer argument that names tensor data is a DEVICE pointer.
- *     Matrices are row-major bf16 (raw 16-bit storage) -- the post-hoc check
- *     also takes fp16 and fp32 (abft_check_args.dtype); leading dimensions
- *     are in elements.
+ *     Matrices are row-major bf16 (raw 16-bit storage) -- the fused GEMM also
+ *     takes fp16 (abft_gemm_args.dtype) and the post-hoc check fp16 and fp32
+ *     (abft_check_args.dtype); leading dimensions are in elements.
  *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
  *   - The library allocates nothing per call.  Scratch space, when a call needs
  *     any, comes from the caller through `workspace`.
@@ -41,7 +41,7 @@
 extern "C" {
 #endif
 
-#define ABFT_B200_VERSION 3
+#define ABFT_B200_VERSION 4
 
 /* ---- return codes ------------------------------------------------------- */
 enum abft_status {
@@ -135,10 +135,10 @@ typedef struct abft_report {
  *   C[M, N] = A[M, K] * B[N, K]^T (+ bias[N])
  * B is stored like nn.Linear.weight: N rows of K contiguous elements.       */
 typedef struct abft_gemm_args {
-  const void* A;          /* bf16 [M, lda]                                    */
-  const void* B;          /* bf16 [N, ldb]                                    */
-  void* C;                /* bf16 [M, ldc] output                             */
-  const void* bias;       /* bf16 [N] or NULL                                 */
+  const void* A;          /* [M, lda], element type `dtype` (bf16 or fp16)    */
+  const void* B;          /* [N, ldb]                                         */
+  void* C;                /* [M, ldc] output                                  */
+  const void* bias;       /* [N] or NULL                                      */
   int64_t M, N, K;
   int64_t lda, ldb, ldc;
   uint32_t mode;          /* ABFT_MODE_* bits                                 */
@@ -146,7 +146,8 @@ typedef struct abft_gemm_args {
   float thr_scale;        /* tau in thr = tau * sqrt(K) * max|C_row_segment|  */
   float thr_abs;          /* absolute floor added to thr                      */
   float tol_abs, tol_rel; /* ABFT_MODE_REF tolerances (checkers.py:96-110)    */
-  const void* checksums;  /* abft_encode_weight(B, tile_n) output, or NULL    */
+  const void* checksums;  /* abft_encode_weight_typed(B, tile_n, dtype)      */
+                          /* output, or NULL                                  */
   void* workspace;        /* device scratch, abft_gemm_workspace_bytes()      */
   size_t workspace_bytes;
   const int32_t* inject_rows;   /* debug: faults added to the fp32 accumulator */
@@ -182,6 +183,11 @@ typedef struct abft_gemm_args {
    * `checksums` must then be NULL). */
   int32_t b_kn;
   int64_t stride_a, stride_b, stride_c;
+  /* Element type of A, B, C and bias: ABFT_DTYPE_BF16 (0) or ABFT_DTYPE_F16;
+   * fp32 operands return ABFT_ERR_UNSUPPORTED (check them post hoc). Both
+   * types run the same kind::f16 MMAs with fp32 accumulation; fp16 checksum
+   * rows carry a per-tile scale (abft_encode_weight_typed). */
+  int32_t dtype;
 } abft_gemm_args;
 
 #define ABFT_MAX_INJECT 64
@@ -238,12 +244,33 @@ int abft_encode_weight(const void* B, int64_t N, int64_t K, int64_t ldb,
 int abft_encode_weight_batched(const void* B, int64_t N, int64_t K, int64_t ldb, int64_t stride_b,
                                int32_t batch, int32_t tile_n, void* out, void* stream);
 
+/* Bytes of one batch's checksum block for element type `dtype`: for bf16
+ * abft_checksum_bytes; for fp16 the same rows (fp16 terms) followed by a
+ * scale table of 8 floats per tile; 0 for other types or tile widths. */
+size_t abft_checksum_bytes_typed(int64_t N, int64_t K, int32_t tile_n, int32_t dtype);
+
+/* abft_encode_weight_batched for B of element type `dtype`; block b lands
+ * at out + b * abft_checksum_bytes_typed(N, K, tile_n, dtype).
+ * fp16 has a narrow exponent range (largest finite 65504), so for each tile
+ * and each of v1, v2, v3 an exponent e is chosen that puts the largest
+ * |value| over k in [2^14, 2^15) (e = 0 when that value is 0 or not
+ * finite; e within [-100, 100]); the rows hold the fp16 terms of v * 2^-e
+ * (three for v1 and v2, two for v3, as above) and table entries 8t+4..6 the
+ * factors 2^e, which the fused check multiplies back (exact). Entries
+ * 8t+0..2 hold the largest |v1|, |v2|, |v3|; 8t+3 and 8t+7 are 0. */
+int abft_encode_weight_typed(const void* B, int64_t N, int64_t K, int64_t ldb, int64_t stride_b,
+                             int32_t batch, int32_t tile_n, int32_t dtype, void* out, void* stream);
+
 /* Workspace the fused GEMM needs for these arguments (0 when none). */
 size_t abft_gemm_workspace_bytes(const abft_gemm_args* args);
 
 /* The fused checksum-protected GEMM. Replaces F.linear + CheapSumChecker.check
  * (pytorch/abft/injector.py:152-161 -> pytorch/abft/checkers.py:55-126). */
 int abft_gemm_bf16(const abft_gemm_args* args, void* stream);
+
+/* The same entry under a type-neutral name (args->dtype selects the type in
+ * both). */
+int abft_gemm(const abft_gemm_args* args, void* stream);
 
 /* Post-hoc check of an existing output C = A * B^T (+ bias), the drop-in for
  * the reference's abft_fused(a, b, c, bias) -> [corner, sum_c]

@@ -56,6 +56,12 @@ def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
     return out
 
 
+def f16_round(x: np.ndarray) -> np.ndarray:
+    """Round float values to the nearest IEEE half (ties to even; beyond
+    65504 to infinity), returned as float32."""
+    return np.asarray(x, dtype=np.float32).astype(np.float16).astype(np.float32)
+
+
 def bf16_round(x: np.ndarray) -> np.ndarray:
     """Round float values to the nearest bf16 value (returned as float32)."""
     return bf16_bits_to_f32(f32_to_bf16_bits(np.asarray(x, dtype=np.float32)))
@@ -223,6 +229,72 @@ def encode_weight(w: np.ndarray, tile_n: int) -> Tuple[np.ndarray, np.ndarray, n
     return v1, v2, v3
 
 
+def encode_weight_f32_order(w: np.ndarray, tile_n: int) -> Tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """v1, v2, v3 of ``encode_weight`` as the library's encode pass forms them
+    in fp32: within a tile, group g (0..31) adds rows g, g + 32, ... in that
+    order, then the 32 group sums are added in order of g. The products
+    (j+1) * w and +-w of 16-bit inputs are exact in fp32, so separate
+    multiply and add round as the kernel's fused multiply-add does."""
+    w = np.asarray(w, dtype=np.float32)
+    n, k = w.shape
+    tiles = -(-n // tile_n)
+    out = np.zeros((3, tiles, k), dtype=np.float32)
+    for t in range(tiles):
+        blk = w[t * tile_n:(t + 1) * tile_n]
+        nr = blk.shape[0]
+        sg = col_signs(nr).astype(np.float32)
+        acc = np.zeros((3, k), dtype=np.float32)
+        for g in range(32):
+            part = np.zeros((3, k), dtype=np.float32)
+            for j in range(g, nr, 32):
+                x = blk[j]
+                part[0] = part[0] + x
+                part[1] = part[1] + np.float32(j + 1) * x
+                part[2] = part[2] + sg[j] * x
+            acc = acc + part
+        out[:, t] = acc
+    return out[0], out[1], out[2]
+
+
+def f16_checksum_exponent(m: float) -> int:
+    """Exponent e of an fp16 checksum scale for largest magnitude m (a
+    float32): 2^-e m in [2^14, 2^15) for normal m; 0 for zero, subnormal or
+    non-finite m; limited to [-100, 100]."""
+    bits = int(np.float32(m).view(np.uint32))
+    be = (bits >> 23) & 0xFF
+    if be == 0 or be == 0xFF:
+        return 0
+    return max(-100, min(100, be - 127 - 14))
+
+
+def encode_weight_f16_block(w: np.ndarray, tile_n: int) -> bytes:
+    """The bytes of the fp16 checksum block of a [N, K] fp16 weight for
+    output tiles of ``tile_n`` data columns: per tile 8 rows of K halves
+    (v1 and v2 each as three fp16 terms, v3 as two, each checksum scaled by
+    2^-e), then a table of 8 float32 per tile: [max|v1|, max|v2|, max|v3|,
+    0, 2^e1, 2^e2, 2^e3, 0]."""
+    v = encode_weight_f32_order(w, tile_n)
+    tiles, k = v[0].shape
+    rows = np.zeros((tiles, 8, k), dtype=np.float16)
+    table = np.zeros((tiles, 8), dtype=np.float32)
+    for t in range(tiles):
+        for q in range(3):
+            m = np.float32(np.abs(v[q][t]).max())
+            e = f16_checksum_exponent(m)
+            x = (v[q][t] * np.float32(2.0 ** -e)).astype(np.float32)
+            hi = x.astype(np.float16)
+            r1 = (x - hi.astype(np.float32)).astype(np.float32)
+            mid = r1.astype(np.float16)
+            if q < 2:
+                lo = (r1 - mid.astype(np.float32)).astype(np.float16)
+                rows[t, 3 * q:3 * q + 3] = np.stack([hi, mid, lo])
+            else:
+                rows[t, 6:8] = np.stack([hi, mid])
+            table[t, q] = m
+            table[t, 4 + q] = np.float32(2.0 ** e)
+    return rows.tobytes() + table.tobytes()
+
+
 @dataclass
 class RowcheckResult:
     records: List[Tuple[int, int, int]]  # (row, col or -1, flags), sorted
@@ -247,6 +319,7 @@ def rowcheck_gemm(
     inject: Sequence[Tuple[int, int, float]] = (),
     correct: bool = True,
     checksum_weight: Optional[np.ndarray] = None,
+    out_dtype: str = "bf16",
 ) -> RowcheckResult:
     """Restatement of the fused kernel's checksum epilogue.
 
@@ -264,7 +337,7 @@ def rowcheck_gemm(
                 SUSPECT_ROWS mismatching rows in this tile column (or at
                 least 4 and more than half of its valid rows): then the
                 record is flagged suppressed and nothing is changed.
-    Output = bf16(acc (+ bias)).
+    Output = bf16(acc (+ bias)), or fp16 with ``out_dtype="f16"``.
     ``checksum_weight`` (default ``w``) is the weight the checksums were
     encoded from: another one models a stale cached checksum block.
     """
@@ -322,7 +395,8 @@ def rowcheck_gemm(
             records.append((int(i), c0 + col if col >= 0 else -1, flags))
             residuals[(int(i), t)] = (float(res1[i]), float(res2[i]), float(thr[i]))
     out = fixed if bias is None else fixed + np.asarray(bias, np.float64)[None, :]
-    return RowcheckResult(sorted(records), residuals, bf16_round(out.astype(np.float32)), acc)
+    rnd = f16_round if out_dtype == "f16" else bf16_round
+    return RowcheckResult(sorted(records), residuals, rnd(out.astype(np.float32)), acc)
 
 
 # -------------------------------------------------- post-hoc row / column locate

@@ -20,7 +20,7 @@ SHAPES = [(256, 512, True), (512, 384, False), (384, 1000, True), (1000, 248, Fa
 TOKENS = 96
 
 
-def make_model(device, seed=0):
+def make_model(device, seed=0, dtype=torch.bfloat16):
     torch.manual_seed(seed)
     layers = []
     for k, n, bias in SHAPES:
@@ -30,7 +30,7 @@ def make_model(device, seed=0):
             if bias:
                 lin.bias.normal_(0.0, 0.02)
         layers.append(lin)
-    return nn.Sequential(*layers).to(device=device, dtype=torch.bfloat16).eval()
+    return nn.Sequential(*layers).to(device=device, dtype=dtype).eval()
 
 
 def run(model, x, cfg, defer):
@@ -67,10 +67,14 @@ def test_clean_model_has_no_detections(cuda_device):
         assert (out.float() - ref.float()).abs().max().item() <= 1e-2 * ref.float().abs().max().item()
 
 
-@pytest.mark.parametrize("seed,prob", [(3, 1.0), (11, 0.5), (2026, 0.7)])
-def test_injected_faults_located_corrected_with_reference_rng(cuda_device, seed, prob):
-    model = make_model(cuda_device)
-    x = torch.randn(TOKENS, SHAPES[0][0], device=cuda_device).bfloat16()
+@pytest.mark.parametrize("seed,prob,dtype", [(3, 1.0, torch.bfloat16), (11, 0.5, torch.bfloat16),
+                                             (2026, 0.7, torch.bfloat16), (3, 1.0, torch.float16),
+                                             (11, 0.5, torch.float16)])
+def test_injected_faults_located_corrected_with_reference_rng(cuda_device, seed, prob, dtype):
+    """Both fused element types: every fault the reference's random stream
+    draws is located at its coordinates and corrected."""
+    model = make_model(cuda_device, dtype=dtype)
+    x = torch.randn(TOKENS, SHAPES[0][0], device=cuda_device).to(dtype)
     with torch.inference_mode():
         clean = model(x)
     cfg = AbftConfig(enable=True, checker_backend="b200", detect_only=False, inject_fault=True,
@@ -374,10 +378,11 @@ def test_b200_narrow_linears_fused_on_padded_copies(cuda_device, k, n, bias):
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
 def test_f16_f32_linears_checked_not_skipped(cuda_device, dtype):
-    """fp16 / fp32 linears (the reference's --dtype float16|float32) take the
-    reference flow -- torch GEMM, then the native scalar check on operands
-    of that type -- instead of being counted as unsupported; a perturbed
-    output fails the check."""
+    """fp16 / fp32 linears (the reference's --dtype float16|float32) are
+    checked, never counted as unsupported: fp16 under "b200" runs the fused
+    kernel; fp32 (and every type under the other backends) takes the
+    reference flow -- torch GEMM, then the native scalar check on operands of
+    that type. A perturbed output fails the check."""
     torch.manual_seed(3)
     x = torch.randn(64, 256, device=cuda_device).to(dtype)
     w = (torch.randn(512, 256, device=cuda_device) * 256 ** -0.5).to(dtype)

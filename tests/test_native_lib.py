@@ -27,7 +27,7 @@ def test_library_exports_every_declared_symbol():
     L = N.lib()
     for name in declared_functions():
         assert hasattr(L, name), name
-    assert L.abft_version() == N.LIB_VERSION == 3
+    assert L.abft_version() == N.LIB_VERSION == 4
 
 
 def test_status_strings():
@@ -115,6 +115,34 @@ def test_gemm_argument_validation_without_gpu():
 
     if not torch.cuda.is_available():
         assert L.abft_gemm_bf16(ctypes.byref(a), None) == -6
+
+
+def test_fp16_gemm_and_typed_encode_validation_without_gpu():
+    L = N.lib()
+    k, n, tiles = 4096, 4096, 17
+    assert L.abft_checksum_bytes_typed(n, k, 256, N.DTYPE_BF16) == L.abft_checksum_bytes(n, k, 256)
+    # fp16: the same rows, then 8 float32 scale entries per tile
+    assert L.abft_checksum_bytes_typed(n, k, 256, N.DTYPE_F16) == tiles * 8 * k * 2 + tiles * 8 * 4
+    assert L.abft_checksum_bytes_typed(n, k, 256, N.DTYPE_F32) == 0
+    assert L.abft_checksum_bytes_typed(n, k, 64, N.DTYPE_F16) == 0
+    B, out = ctypes.c_void_p(0x10000), ctypes.c_void_p(0x20000)
+    assert L.abft_encode_weight_typed(B, 8, 8, 8, 0, 1, 256, N.DTYPE_F32, out, None) == -3
+    assert L.abft_encode_weight_typed(B, 8, 8, 8, 0, 1, 256, 7, out, None) == -1
+    assert L.abft_encode_weight_typed(B, 8, 12, 16, 0, 1, 256, N.DTYPE_F16, out, None) == -2  # K % 8
+    assert L.abft_encode_weight_typed(B, 8, 8, 8, 0, 1, 100, N.DTYPE_F16, out, None) == -3
+    a = N.GemmArgs()
+    a.A, a.B, a.C = 0x10000, 0x20000, 0x30000
+    a.M, a.N, a.K, a.lda, a.ldb, a.ldc = 128, 256, 72, 72, 72, 256
+    a.dtype = N.DTYPE_F32
+    assert L.abft_gemm(ctypes.byref(a), None) == -3  # fp32 operands: post-hoc check only
+    a.dtype = 5
+    assert L.abft_gemm(ctypes.byref(a), None) == -1
+    a.dtype = N.DTYPE_F16
+    import torch
+
+    if not torch.cuda.is_available():
+        assert L.abft_gemm(ctypes.byref(a), None) == -6
+        assert L.abft_encode_weight_typed(B, 8, 8, 8, 0, 1, 256, N.DTYPE_F16, out, None) == -6
 
 
 def test_check_argument_validation_without_gpu():

@@ -46,7 +46,7 @@ MAX_INJECT = 64
 REPORT_HEADER_BYTES = 64
 RECORD_BYTES = 24
 BATCH_COUNT_BYTES = 16  # uint32 {faults, located, corrected, 0} per batch after the records
-LIB_VERSION = 3
+LIB_VERSION = 4
 
 EXPORTED_SYMBOLS = (
     "abft_version",
@@ -58,8 +58,11 @@ EXPORTED_SYMBOLS = (
     "abft_checksum_bytes",
     "abft_encode_weight",
     "abft_encode_weight_batched",
+    "abft_checksum_bytes_typed",
+    "abft_encode_weight_typed",
     "abft_gemm_workspace_bytes",
     "abft_gemm_bf16",
+    "abft_gemm",
     "abft_check_workspace_bytes",
     "abft_check_only",
     "abft_check_only_noalloc",
@@ -114,6 +117,7 @@ class GemmArgs(ctypes.Structure):
         ("stride_a", ctypes.c_int64),
         ("stride_b", ctypes.c_int64),
         ("stride_c", ctypes.c_int64),
+        ("dtype", ctypes.c_int32),
     ]
 
 
@@ -181,10 +185,16 @@ def lib() -> ctypes.CDLL:
     L.abft_encode_weight.argtypes = [vp, i64, i64, i64, i32, vp, vp]
     L.abft_encode_weight_batched.restype = ctypes.c_int
     L.abft_encode_weight_batched.argtypes = [vp, i64, i64, i64, i64, i32, i32, vp, vp]
+    L.abft_checksum_bytes_typed.restype = sz
+    L.abft_checksum_bytes_typed.argtypes = [i64, i64, i32, i32]
+    L.abft_encode_weight_typed.restype = ctypes.c_int
+    L.abft_encode_weight_typed.argtypes = [vp, i64, i64, i64, i64, i32, i32, i32, vp, vp]
     L.abft_gemm_workspace_bytes.restype = sz
     L.abft_gemm_workspace_bytes.argtypes = [ctypes.POINTER(GemmArgs)]
     L.abft_gemm_bf16.restype = ctypes.c_int
     L.abft_gemm_bf16.argtypes = [ctypes.POINTER(GemmArgs), vp]
+    L.abft_gemm.restype = ctypes.c_int
+    L.abft_gemm.argtypes = [ctypes.POINTER(GemmArgs), vp]
     L.abft_check_workspace_bytes.restype = sz
     L.abft_check_workspace_bytes.argtypes = [ctypes.POINTER(CheckArgs)]
     L.abft_check_only.restype = ctypes.c_int

@@ -6,10 +6,10 @@ in the reference (injector.py:31-51), and restored on exit.
 
 * ``F.linear`` with ``checker_backend="b200"`` and ``fused_linear`` replaces
   "torch GEMM, then check" by one call of the fused kernel
-  (``abft_gemm_bf16``): the GEMM, its per-tile weighted row checksums and
-  the compare run in one launch, a drawn fault is added to the fp32
-  accumulator before the compare, and with ``detect_only=False`` located
-  faults are corrected before the bf16 store.
+  (``abft_gemm``, bf16 or fp16 operands): the GEMM, its per-tile weighted
+  row checksums and the compare run in one launch, a drawn fault is added
+  to the fp32 accumulator before the compare, and with
+  ``detect_only=False`` located faults are corrected before the store.
 * ``torch.bmm`` and ``torch.matmul`` with a 2-D right operand, with
   ``fused_matmul``, run the same way as one batched launch; a bmm records
   one check per batch, as the reference's per-batch loop does
@@ -19,7 +19,8 @@ in the reference (injector.py:31-51), and restored on exit.
 * A linear with K or N not a multiple of 8 (the library reads rows in
   16-byte pieces; e.g. a VLA's 7-wide action projections) runs the same
   fused kernel on zero-padded copies of its operands.
-* Other backends, operands the library cannot take (CPU, non-bf16) and
+* Other backends, operands the library cannot take (CPU, fp32, mixed
+  types) and
   calls that need autograd follow the reference flow: run the op, maybe
   perturb one output element, then ``checker.check`` on the flattened
   operands (injector.py:152-187).
@@ -110,7 +111,7 @@ class WeightChecksumCache:
 
     @staticmethod
     def _key(weight: torch.Tensor, tile_n: int) -> tuple:
-        return (weight.data_ptr(), tuple(weight.shape), weight.stride(), tile_n, weight.get_device())
+        return (weight.data_ptr(), tuple(weight.shape), weight.stride(), tile_n, weight.get_device(), weight.dtype)
 
     @staticmethod
     def _version(weight: torch.Tensor) -> int:
@@ -431,14 +432,14 @@ class AbftInjector(AbstractContextManager):
             return False
         if self._needs_grad(x, weight, bias):
             return False
-        if not (x.is_cuda and weight.is_cuda) or x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        if not (x.is_cuda and weight.is_cuda) or x.dtype not in ops.GEMM_DTYPES or weight.dtype != x.dtype:
             return False
         if weight.dim() != 2 or x.dim() < 1 or x.shape[-1] != weight.shape[1]:
             return False
         n, k = weight.shape
         if k == 0 or n == 0 or x.numel() == 0:
             return False
-        if bias is not None and (not bias.is_cuda or bias.dtype != torch.bfloat16 or bias.dim() != 1):
+        if bias is not None and (not bias.is_cuda or bias.dtype != x.dtype or bias.dim() != 1):
             return False
         if k % 8 or n % 8:
             return True  # run on zero-padded copies (_fused_linear_padded)
@@ -513,7 +514,7 @@ class AbftInjector(AbstractContextManager):
         if bias is not None and not bias.is_contiguous():
             bias = bias.contiguous()
         # the output in its final shape: m contiguous rows of n
-        out = torch.empty(x.shape[:-1] + (n,), dtype=torch.bfloat16, device=x2.device)
+        out = torch.empty(x.shape[:-1] + (n,), dtype=x2.dtype, device=x2.device)
         # operands checked by _fused_linear_ok: straight to the launch
         ops._gemm_launch(x2, weight, bias, out, m, n, k, mode, 0 if swapped else tile_n, 0, 0, self.cfg.thr_scale,
                          self.cfg.thr_abs, 1e-2, 1e-2, cks, inject, rep, 0, lda=lda, ldc=n)
@@ -544,7 +545,7 @@ class AbftInjector(AbstractContextManager):
             return False
         if not (a.is_cuda and b.is_cuda) or a.device != b.device:
             return False
-        if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16 or self._needs_grad(a, b):
+        if a.dtype not in ops.GEMM_DTYPES or b.dtype != a.dtype or self._needs_grad(a, b):
             return False
         k, n = b.shape[-2], b.shape[-1]
         return a.shape[-1] == k and k % 8 == 0 and n % 8 == 0 and k > 0 and n > 0 and a.numel() > 0

@@ -7,6 +7,8 @@
 #include <cuda_runtime.h>
 #include <math.h>
 
+#include <string.h>
+
 #include <atomic>
 #include <mutex>
 #include <random>
@@ -40,7 +42,7 @@ struct DeviceInfo {
   bool init;
   bool ok;
   int sms;
-  bool attr_set[8];
+  bool attr_set[16];  // slots 8..15: the fp16 instances of slots 0..7
   int pair_clusters[2][2];  // co-resident 2-CTA clusters of the pair kernels [bn == 256][check], 0 = not asked yet
 };
 DeviceInfo g_dev[kMaxDevices];
@@ -70,10 +72,11 @@ int current_device(int* dev_out, DeviceInfo* info) {
   return ABFT_OK;
 }
 
-template <int BN, bool CHECK, bool PAIR>
+template <int BN, bool CHECK, bool PAIR, bool F16 = false>
 int ensure_smem_attr_locked(int dev, int slot) {
+  if (F16) slot += 8;
   if (g_dev[dev].attr_set[slot]) return ABFT_OK;
-  if (cudaFuncSetAttribute(abft_gemm_kernel<BN, CHECK, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  if (cudaFuncSetAttribute(abft_gemm_kernel<BN, CHECK, PAIR, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            GemmCfg<BN, CHECK, PAIR>::kSmemBytes) != cudaSuccess) {
     cudaGetLastError();
     return ABFT_ERR_CUDA;
@@ -82,10 +85,10 @@ int ensure_smem_attr_locked(int dev, int slot) {
   return ABFT_OK;
 }
 
-template <int BN, bool CHECK, bool PAIR>
+template <int BN, bool CHECK, bool PAIR, bool F16>
 int ensure_smem_attr(int dev, int slot) {
   std::lock_guard<std::mutex> lk(g_mu);
-  return ensure_smem_attr_locked<BN, CHECK, PAIR>(dev, slot);
+  return ensure_smem_attr_locked<BN, CHECK, PAIR, F16>(dev, slot);
 }
 
 // attr_set slots of the pair kernels [bn == 256][check]
@@ -103,6 +106,8 @@ cudaLaunchAttribute pair_cluster_attr() {
 // How many 2-CTA clusters of the pair kernel can be resident at once on
 // device `dev` (every unit of a persistent launch must be resident: stream-K
 // finishers wait for later units). Falls back to sms / 2 if the query fails.
+// The bf16 instance answers for both element types: the fp16 one has the
+// same block, shared-memory footprint and register bound (128 per thread).
 template <int BN, bool CHECK>
 int pair_units_on(int dev, int sms) {
   std::lock_guard<std::mutex> lk(g_mu);
@@ -118,7 +123,7 @@ int pair_units_on(int dev, int sms) {
       cudaLaunchAttribute at = pair_cluster_attr();
       cfg.attrs = &at;
       cfg.numAttrs = 1;
-      if (cudaOccupancyMaxActiveClusters(&n, abft_gemm_kernel<BN, CHECK, true>, &cfg) != cudaSuccess) {
+      if (cudaOccupancyMaxActiveClusters(&n, abft_gemm_kernel<BN, CHECK, true, false>, &cfg) != cudaSuccess) {
         cudaGetLastError();
         n = 0;
       }
@@ -135,7 +140,7 @@ int pair_units_on(int dev, int sms) {
 struct TmapKey {
   const void* ptr;
   int64_t inner, outer, ld, batch, bstride;
-  int box, kind;
+  int box, kind;  // kind: 0 operand, 1 output; + 2 for fp16 elements
   bool operator==(const TmapKey& o) const {
     return ptr == o.ptr && inner == o.inner && outer == o.outer && ld == o.ld && batch == o.batch &&
            bstride == o.bstride && box == o.box && kind == o.kind;
@@ -157,16 +162,21 @@ TmapEntry& tmap_slot(const TmapKey& k) {
   return t_tmaps[h % kTmapCacheSize];
 }
 
-// A 3-D map over `batch` row-major [outer, ld] bf16 matrices, matrix b at
-// ptr + b * bstride elements (bstride ignored for batch <= 1), read in boxes
-// of 64 (inner) x box_outer rows x 1 matrix with 128-byte swizzle.
+inline CUtensorMapDataType tmap_type(int dtype) {
+  return dtype == ABFT_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+}
+
+// A 3-D map over `batch` row-major [outer, ld] matrices of 16-bit elements
+// (bf16 or fp16, `dtype`), matrix b at ptr + b * bstride elements (bstride
+// ignored for batch <= 1), read in boxes of 64 (inner) x box_outer rows x 1
+// matrix with 128-byte swizzle.
 int make_tmap_kmajor(CUtensorMap* m, const void* ptr, int64_t inner, int64_t outer, int64_t ld, int box_outer,
-                     int64_t batch = 1, int64_t bstride = 0) {
+                     int64_t batch = 1, int64_t bstride = 0, int dtype = ABFT_DTYPE_BF16) {
   if (batch <= 1) {
     batch = 1;
     bstride = ld * outer;
   }
-  const TmapKey key{ptr, inner, outer, ld, batch, bstride, box_outer, 0};
+  const TmapKey key{ptr, inner, outer, ld, batch, bstride, box_outer, dtype == ABFT_DTYPE_F16 ? 2 : 0};
   TmapEntry& e = tmap_slot(key);
   if (e.valid && e.key == key) {
     *m = e.map;
@@ -178,7 +188,7 @@ int make_tmap_kmajor(CUtensorMap* m, const void* ptr, int64_t inner, int64_t out
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 2, static_cast<cuuint64_t>(bstride) * 2};
   cuuint32_t box[3] = {64u, static_cast<cuuint32_t>(box_outer), 1u};
   cuuint32_t es[3] = {1u, 1u, 1u};
-  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, es,
+  CUresult r = enc(m, tmap_type(dtype), 3, const_cast<void*>(ptr), dims, strides, box, es,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return ABFT_ERR_ALIGNMENT;
@@ -188,16 +198,17 @@ int make_tmap_kmajor(CUtensorMap* m, const void* ptr, int64_t inner, int64_t out
   return ABFT_OK;
 }
 
-// The output map: `batch` row-major [rows, ld] bf16 matrices (matrix b at
-// ptr + b * bstride elements), stored in 32 x 32 boxes whose shared-memory
-// source uses the 64-byte swizzle (an epilogue warp's staging block).
+// The output map: `batch` row-major [rows, ld] bf16 or fp16 matrices
+// (matrix b at ptr + b * bstride elements), stored in 32 x 32 boxes whose
+// shared-memory source uses the 64-byte swizzle (an epilogue warp's staging
+// block).
 int make_tmap_store(CUtensorMap* m, void* ptr, int64_t cols, int64_t rows, int64_t ld, int64_t batch,
-                    int64_t bstride) {
+                    int64_t bstride, int dtype) {
   if (batch <= 1) {
     batch = 1;
     bstride = ld * rows;
   }
-  const TmapKey key{ptr, cols, rows, ld, batch, bstride, 32, 1};
+  const TmapKey key{ptr, cols, rows, ld, batch, bstride, 32, dtype == ABFT_DTYPE_F16 ? 3 : 1};
   TmapEntry& e = tmap_slot(key);
   if (e.valid && e.key == key) {
     *m = e.map;
@@ -209,7 +220,7 @@ int make_tmap_store(CUtensorMap* m, void* ptr, int64_t cols, int64_t rows, int64
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 2, static_cast<cuuint64_t>(bstride) * 2};
   cuuint32_t box[3] = {32u, 32u, 1u};
   cuuint32_t es[3] = {1u, 1u, 1u};
-  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, ptr, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+  CUresult r = enc(m, tmap_type(dtype), 3, ptr, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return ABFT_ERR_ALIGNMENT;
   e.key = key;
@@ -500,10 +511,10 @@ int make_plan_uncached(const abft_gemm_args* a, int dev, int sms, Plan* pl);
 struct PlanKey {
   int64_t M, N, K, batch;
   uint32_t mode;
-  int tile_n, tile_m, has_cks, dev, sms;
+  int tile_n, tile_m, has_cks, dev, sms, dtype;
   bool operator==(const PlanKey& o) const {
     return M == o.M && N == o.N && K == o.K && batch == o.batch && mode == o.mode && tile_n == o.tile_n &&
-           tile_m == o.tile_m && has_cks == o.has_cks && dev == o.dev && sms == o.sms;
+           tile_m == o.tile_m && has_cks == o.has_cks && dev == o.dev && sms == o.sms && dtype == o.dtype;
   }
 };
 struct PlanEntry {
@@ -516,7 +527,7 @@ thread_local PlanEntry t_plans[kPlanCacheSize];
 
 int make_plan(const abft_gemm_args* a, int dev, int sms, Plan* pl) {
   const PlanKey key{a->M, a->N, a->K, batch_of(a), a->mode, a->tile_n, a->tile_m, a->checksums != nullptr ? 1 : 0,
-                    dev, sms};
+                    dev, sms, a->dtype};
   uint64_t h = static_cast<uint64_t>(a->M) * 0x9E3779B97F4A7C15ull ^ static_cast<uint64_t>(a->N) * 0xC2B2AE3D27D4EB4Full ^
                static_cast<uint64_t>(a->K) * 0x165667B19E3779F9ull ^ (static_cast<uint64_t>(key.batch) << 7) ^
                (static_cast<uint64_t>(a->mode) << 3) ^ static_cast<uint64_t>(a->tile_n + a->tile_m + key.has_cks);
@@ -561,7 +572,7 @@ int make_plan_uncached(const abft_gemm_args* a, int dev, int sms, Plan* pl) {
   pl->v_off = pl->pa_off = pl->u_off = pl->pb_off = pl->vf_off = pl->parts_off = pl->sk_part_off = pl->sk_flag_off = 0;
   if (pl->check && a->checksums == nullptr) {
     pl->v_off = off;
-    off = align256(off + static_cast<size_t>(nb) * abft_checksum_bytes(a->N, a->K, pl->bn));
+    off = align256(off + static_cast<size_t>(nb) * abft_checksum_bytes_typed(a->N, a->K, pl->bn, a->dtype));
   }
   if (a->mode & ABFT_MODE_REF) {
     pl->pa_off = off;
@@ -590,6 +601,7 @@ int validate_gemm(const abft_gemm_args* a) {
   if (a->M < 0 || a->N < 0 || a->K < 0 || a->batch < 0) return ABFT_ERR_INVALID_ARG;
   if (a->M > (1ll << 30) || a->N > (1ll << 30) || a->K > (1ll << 30)) return ABFT_ERR_UNSUPPORTED;
   if (a->b_kn != 0 && a->b_kn != 1) return ABFT_ERR_INVALID_ARG;
+  if (a->dtype != ABFT_DTYPE_BF16 && a->dtype != ABFT_DTYPE_F16) return a->dtype == ABFT_DTYPE_F32 ? ABFT_ERR_UNSUPPORTED : ABFT_ERR_INVALID_ARG;
   if (a->lda < a->K || a->ldb < (a->b_kn ? a->N : a->K) || a->ldc < a->N) return ABFT_ERR_INVALID_ARG;
   if (a->b_kn && a->checksums != nullptr) return ABFT_ERR_INVALID_ARG;
   if (a->batch > 1) {
@@ -645,15 +657,15 @@ void make_frames(const abft_gemm_args* a, void* copy, Frames* f) {
   f->k = f->swap ? swapped_args(&f->r) : f->r;
 }
 
-template <int BN, bool CHECK, bool PAIR>
+template <int BN, bool CHECK, bool PAIR, bool F16>
 int launch_gemm(int dev, int slot, const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmB2,
                 const CUtensorMap& tmV, const CUtensorMap& tmBt, const CUtensorMap& tmC, const GemmParams& p, int grid,
                 cudaStream_t s) {
-  int rc = ensure_smem_attr<BN, CHECK, PAIR>(dev, slot);
+  int rc = ensure_smem_attr<BN, CHECK, PAIR, F16>(dev, slot);
   if (rc != ABFT_OK) return rc;
   constexpr size_t smem = GemmCfg<BN, CHECK, PAIR>::kSmemBytes;
   if constexpr (!PAIR) {
-    abft_gemm_kernel<BN, CHECK, false><<<grid, kThreads, smem, s>>>(tmA, tmB, tmB2, tmV, tmBt, tmC, p);
+    abft_gemm_kernel<BN, CHECK, false, F16><<<grid, kThreads, smem, s>>>(tmA, tmB, tmB2, tmV, tmBt, tmC, p);
   } else {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(grid));
@@ -663,10 +675,35 @@ int launch_gemm(int dev, int slot, const CUtensorMap& tmA, const CUtensorMap& tm
     cudaLaunchAttribute at = pair_cluster_attr();
     cfg.attrs = &at;
     cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, abft_gemm_kernel<BN, CHECK, true>, tmA, tmB, tmB2, tmV, tmBt, tmC, p) != cudaSuccess)
+    if (cudaLaunchKernelEx(&cfg, abft_gemm_kernel<BN, CHECK, true, F16>, tmA, tmB, tmB2, tmV, tmBt, tmC, p) !=
+        cudaSuccess)
       return launch_status(), ABFT_ERR_CUDA;
   }
   return launch_status();
+}
+
+template <bool F16>
+int launch_gemm_typed(const Plan& ws, bool check, int dev, const CUtensorMap& tmA, const CUtensorMap& tmB,
+                      const CUtensorMap& tmB2, const CUtensorMap& tmV, const CUtensorMap& tmBt, const CUtensorMap& tmC,
+                      const GemmParams& p, cudaStream_t s) {
+  const int grid = ws.grid;
+  if (ws.pair && ws.bn == 256)
+    return check ? launch_gemm<256, true, true, F16>(dev, kPairSlot[1][1], tmA, tmB, tmB2, tmV, tmBt, tmC, p, grid, s)
+                 : launch_gemm<256, false, true, F16>(dev, kPairSlot[1][0], tmA, tmB, tmB2, tmV, tmBt, tmC, p, grid, s);
+  if (ws.pair)
+    return check ? launch_gemm<128, true, true, F16>(dev, kPairSlot[0][1], tmA, tmB, tmB2, tmV, tmBt, tmC, p, grid, s)
+                 : launch_gemm<128, false, true, F16>(dev, kPairSlot[0][0], tmA, tmB, tmB2, tmV, tmBt, tmC, p, grid, s);
+  if (ws.bn == 256)
+    return check ? launch_gemm<256, true, false, F16>(dev, 0, tmA, tmB, tmB2, tmV, tmBt, tmC, p, grid, s)
+                 : launch_gemm<256, false, false, F16>(dev, 1, tmA, tmB, tmB2, tmV, tmBt, tmC, p, grid, s);
+  return check ? launch_gemm<128, true, false, F16>(dev, 2, tmA, tmB, tmB2, tmV, tmBt, tmC, p, grid, s)
+               : launch_gemm<128, false, false, F16>(dev, 3, tmA, tmB, tmB2, tmV, tmBt, tmC, p, grid, s);
+}
+
+// Rows part of one batch's checksum block, then (fp16) its scale table of
+// 8 floats per tile.
+size_t checksum_rows_bytes(int64_t N, int64_t K, int32_t tile_n) {
+  return static_cast<size_t>(cdiv(N, tile_n - kChkRows)) * kChkRows * static_cast<size_t>(K) * 2;
 }
 
 }  // namespace
@@ -704,13 +741,22 @@ int32_t abft_pick_tile_n(int64_t M, int64_t N, int64_t K, int32_t num_sms, uint3
 
 size_t abft_checksum_bytes(int64_t N, int64_t K, int32_t tile_n) {
   if (tile_n != 128 && tile_n != 256) return 0;
-  return static_cast<size_t>(cdiv(N, tile_n - kChkRows)) * kChkRows * static_cast<size_t>(K) * 2;
+  return checksum_rows_bytes(N, K, tile_n);
 }
 
-int abft_encode_weight_batched(const void* B, int64_t N, int64_t K, int64_t ldb, int64_t stride_b, int32_t batch,
-                               int32_t tile_n, void* out, void* stream) {
+size_t abft_checksum_bytes_typed(int64_t N, int64_t K, int32_t tile_n, int32_t dtype) {
+  if (tile_n != 128 && tile_n != 256) return 0;
+  if (dtype == ABFT_DTYPE_BF16) return checksum_rows_bytes(N, K, tile_n);
+  if (dtype != ABFT_DTYPE_F16) return 0;
+  return checksum_rows_bytes(N, K, tile_n) + static_cast<size_t>(cdiv(N, tile_n - kChkRows)) * 8 * sizeof(float);
+}
+
+int abft_encode_weight_typed(const void* B, int64_t N, int64_t K, int64_t ldb, int64_t stride_b, int32_t batch,
+                             int32_t tile_n, int32_t dtype, void* out, void* stream) {
   if (B == nullptr || out == nullptr || N <= 0 || K <= 0 || ldb < K || batch < 1 || stride_b < 0)
     return ABFT_ERR_INVALID_ARG;
+  if (dtype != ABFT_DTYPE_BF16 && dtype != ABFT_DTYPE_F16)
+    return dtype == ABFT_DTYPE_F32 ? ABFT_ERR_UNSUPPORTED : ABFT_ERR_INVALID_ARG;
   if ((K % 8) || (ldb % 8) || (stride_b % 8) || !aligned16(B) || !aligned16(out)) return ABFT_ERR_ALIGNMENT;
   if (tile_n != 128 && tile_n != 256) return ABFT_ERR_UNSUPPORTED;
   if (N > (1ll << 30) || K > (1ll << 30) || batch > 65535) return ABFT_ERR_UNSUPPORTED;
@@ -721,15 +767,41 @@ int abft_encode_weight_batched(const void* B, int64_t N, int64_t K, int64_t ldb,
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int bd = tile_n - kChkRows;
   const int num_kb = static_cast<int>(cdiv(K, kBK));
-  dim3 g(static_cast<unsigned>(num_kb), static_cast<unsigned>(cdiv(N, bd)), static_cast<unsigned>(batch));
-  encode_weight_kernel<<<g, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(B), ldb, static_cast<int>(N),
-                                         static_cast<int>(K), bd, static_cast<__nv_bfloat16*>(out), stride_b,
-                                         static_cast<int64_t>(abft_checksum_bytes(N, K, tile_n) / 2));
+  const int64_t tiles = cdiv(N, bd);
+  const size_t bytes = abft_checksum_bytes_typed(N, K, tile_n, dtype);  // one batch's block
+  dim3 g(static_cast<unsigned>(num_kb), static_cast<unsigned>(tiles), static_cast<unsigned>(batch));
+  if (dtype == ABFT_DTYPE_BF16) {
+    encode_weight_kernel<__nv_bfloat16, 0><<<g, 256, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(B), ldb, static_cast<int>(N), static_cast<int>(K), bd,
+        static_cast<__nv_bfloat16*>(out), stride_b, static_cast<int64_t>(bytes / 2), nullptr, 0);
+    return launch_status();
+  }
+  // fp16: zero the scale tables (one row of tiles * 8 floats per batch),
+  // find each tile's largest checksum magnitudes, then write the scaled rows.
+  float* table = reinterpret_cast<float*>(static_cast<uint8_t*>(out) + checksum_rows_bytes(N, K, tile_n));
+  if (cudaMemset2DAsync(table, bytes, 0, static_cast<size_t>(tiles) * 8 * sizeof(float), static_cast<size_t>(batch),
+                        s) != cudaSuccess)
+    return launch_status(), ABFT_ERR_CUDA;
+  const __half* Bh = static_cast<const __half*>(B);
+  __half* oh = static_cast<__half*>(out);
+  encode_weight_kernel<__half, 1><<<g, 256, 0, s>>>(Bh, ldb, static_cast<int>(N), static_cast<int>(K), bd, oh,
+                                                    stride_b, static_cast<int64_t>(bytes / 2), table,
+                                                    static_cast<int64_t>(bytes / 4));
+  rc = launch_status();
+  if (rc != ABFT_OK) return rc;
+  encode_weight_kernel<__half, 2><<<g, 256, 0, s>>>(Bh, ldb, static_cast<int>(N), static_cast<int>(K), bd, oh,
+                                                    stride_b, static_cast<int64_t>(bytes / 2), table,
+                                                    static_cast<int64_t>(bytes / 4));
   return launch_status();
 }
 
+int abft_encode_weight_batched(const void* B, int64_t N, int64_t K, int64_t ldb, int64_t stride_b, int32_t batch,
+                               int32_t tile_n, void* out, void* stream) {
+  return abft_encode_weight_typed(B, N, K, ldb, stride_b, batch, tile_n, ABFT_DTYPE_BF16, out, stream);
+}
+
 int abft_encode_weight(const void* B, int64_t N, int64_t K, int64_t ldb, int32_t tile_n, void* out, void* stream) {
-  return abft_encode_weight_batched(B, N, K, ldb, 0, 1, tile_n, out, stream);
+  return abft_encode_weight_typed(B, N, K, ldb, 0, 1, tile_n, ABFT_DTYPE_BF16, out, stream);
 }
 
 size_t abft_gemm_workspace_bytes(const abft_gemm_args* args) {
@@ -751,6 +823,8 @@ int32_t abft_pick_tile_m(int64_t M, int64_t N, int64_t K, int32_t num_sms, uint3
   if (num_sms <= 0) num_sms = 148;
   return pick_tile_m(M, N, K, num_sms, mode, tile_n);
 }
+
+int abft_gemm(const abft_gemm_args* args, void* stream) { return abft_gemm_bf16(args, stream); }
 
 int abft_gemm_bf16(const abft_gemm_args* args, void* stream) {
   int rc = validate_gemm(args);
@@ -793,43 +867,57 @@ int abft_gemm_bf16(const abft_gemm_args* args, void* stream) {
   // An N-major B is copied K-major by a pre-pass that, unless the operands
   // are swapped (the copy is then the kernel's A and the checksums come
   // from the rows of A), also forms the checksum block.
-  const bool enc_kn = fr.kn && check && !swap;
+  const bool f16 = a->dtype == ABFT_DTYPE_F16;
+  // fp16 checksum rows are scaled per tile from the largest sum over all of
+  // K, which neither the transposing pre-pass nor the in-kernel token
+  // builder sees: they use the two-pass encode (after the copy, if any).
+  const bool enc_kn = fr.kn && check && !swap && !f16;
   // Swapped operands with at most 64 tokens (one compact tail tile): the
   // kernel's build warp forms the token checksum rows of every stage in
   // shared memory; nothing is encoded or loaded for them. More tokens (a
   // forced swap) keep the encode pre-pass.
-  const bool build = check && swap && !ws.pair && a->N <= 64 && a->N < bd && tail_width(a->N, bd, bn, check) != 0;
+  const bool build =
+      check && swap && !f16 && !ws.pair && a->N <= 64 && a->N < bd && tail_width(a->N, bd, bn, check) != 0;
   const bool enc_plain = check && a->checksums == nullptr && !enc_kn && !build;
   const void* V = check ? (a->checksums != nullptr ? a->checksums : wsb + ws.v_off) : nullptr;
 
   // B-operand boxes: the whole data width of a tile, or in a pair the even
   // CTA's 128 rows (tmB) and the odd CTA's remaining data rows (tmB2).
   CUtensorMap tmA, tmB, tmB2;
-  rc = make_tmap_kmajor(&tmA, a->A, a->K, a->M, a->lda, kBM, nb, a->stride_a);
+  const int dt = a->dtype;
+  rc = make_tmap_kmajor(&tmA, a->A, a->K, a->M, a->lda, kBM, nb, a->stride_a, dt);
   if (rc != ABFT_OK) return rc;
-  rc = make_tmap_kmajor(&tmB, a->B, a->K, a->N, a->ldb, ws.pair ? bn / 2 : bd, nb, a->stride_b);
+  rc = make_tmap_kmajor(&tmB, a->B, a->K, a->N, a->ldb, ws.pair ? bn / 2 : bd, nb, a->stride_b, dt);
   if (rc != ABFT_OK) return rc;
   tmB2 = tmB;
   if (ws.pair && check) {
-    rc = make_tmap_kmajor(&tmB2, a->B, a->K, a->N, a->ldb, bd - bn / 2, nb, a->stride_b);
+    rc = make_tmap_kmajor(&tmB2, a->B, a->K, a->N, a->ldb, bd - bn / 2, nb, a->stride_b, dt);
     if (rc != ABFT_OK) return rc;
   }
+  // A batch's checksum block: its rows, then (fp16) its scale table.
+  const size_t chk_bytes = check ? abft_checksum_bytes_typed(a->N, a->K, bn, dt) : 0;
   CUtensorMap tmV = tmA;  // placeholder when checks are off or built in the kernel
   if (check && !build) {
     const int64_t vrows = cdiv(a->N, bd) * kChkRows;
-    rc = make_tmap_kmajor(&tmV, V, a->K, vrows, a->K, kChkRows, nb, vrows * a->K);
+    rc = make_tmap_kmajor(&tmV, V, a->K, vrows, a->K, kChkRows, nb, static_cast<int64_t>(chk_bytes / 2), dt);
     if (rc != ABFT_OK) return rc;
   }
   CUtensorMap tmC = tmA;  // placeholder with swapped operands (transposed plain stores)
   if (!swap) {
-    rc = make_tmap_store(&tmC, a->C, a->N, a->M, a->ldc, nb, nb > 1 ? (a->stride_c / a->ldc) * a->ldc : 0);
+    rc = make_tmap_store(&tmC, a->C, a->N, a->M, a->ldc, nb, nb > 1 ? (a->stride_c / a->ldc) * a->ldc : 0, dt);
     if (rc != ABFT_OK) return rc;
   }
 
   GemmParams p;
-  p.C = static_cast<__nv_bfloat16*>(a->C);
+  p.C = a->C;
   p.ldc = a->ldc;
-  p.bias = static_cast<const __nv_bfloat16*>(a->bias);
+  p.bias = a->bias;
+  p.chk_scale = nullptr;
+  p.chk_scale_bstride = 0;
+  if (check && f16) {
+    p.chk_scale = reinterpret_cast<const float*>(static_cast<const uint8_t*>(V) + checksum_rows_bytes(a->N, a->K, bn));
+    p.chk_scale_bstride = static_cast<int64_t>(chk_bytes / 4);
+  }
   p.M = static_cast<int>(a->M);
   p.N = static_cast<int>(a->N);
   p.K = static_cast<int>(a->K);
@@ -907,7 +995,6 @@ int abft_gemm_bf16(const abft_gemm_args* args, void* stream) {
   p.fd_gm_last = make_fast_div(p.tiles_m - (cdiv(p.tiles_m, p.group_m) - 1) * p.group_m);
 
   const Schedule& sch = ws.sch;
-  const int grid = ws.grid;
   p.dp_tiles = sch.dp_tiles;
   p.sk = sch.sk;
   p.sk_ctas = sch.sk_ctas;
@@ -920,34 +1007,24 @@ int abft_gemm_bf16(const abft_gemm_args* args, void* stream) {
     p.flags = reinterpret_cast<unsigned long long*>(wsb + ws.sk_flag_off);
   }
   if (fr.kn) {
-    const int cbd = enc_kn ? bd : 256;
+    const int cbd = enc_kn ? bd : 256;  // copies 16-bit elements of either type
     dim3 g(static_cast<unsigned>(cdiv(args->K, kBK)), static_cast<unsigned>(cdiv(args->N, cbd)),
            static_cast<unsigned>(nb));
     transpose_encode_kernel<<<g, 256, 0, s>>>(
         static_cast<const __nv_bfloat16*>(args->B), args->ldb, nb > 1 ? args->stride_b : 0, static_cast<int>(args->N),
         static_cast<int>(args->K), cbd, static_cast<__nv_bfloat16*>(args->workspace),
         enc_kn ? static_cast<__nv_bfloat16*>(const_cast<void*>(V)) : nullptr,
-        enc_kn ? static_cast<int64_t>(abft_checksum_bytes(args->N, args->K, bn) / 2) : 0);
+        enc_kn ? static_cast<int64_t>(chk_bytes / 2) : 0);
     rc = launch_status();
     if (rc != ABFT_OK) return rc;
   }
   if (enc_plain) {
-    rc = abft_encode_weight_batched(a->B, a->N, a->K, a->ldb, nb > 1 ? a->stride_b : 0, static_cast<int32_t>(nb), bn,
-                                    const_cast<void*>(V), stream);
+    rc = abft_encode_weight_typed(a->B, a->N, a->K, a->ldb, nb > 1 ? a->stride_b : 0, static_cast<int32_t>(nb), bn, dt,
+                                  const_cast<void*>(V), stream);
     if (rc != ABFT_OK) return rc;
   }
-  if (ws.pair && bn == 256)
-    rc = check ? launch_gemm<256, true, true>(dev, kPairSlot[1][1], tmA, tmB, tmB2, tmV, tmBt, tmC, p, grid, s)
-               : launch_gemm<256, false, true>(dev, kPairSlot[1][0], tmA, tmB, tmB2, tmV, tmBt, tmC, p, grid, s);
-  else if (ws.pair)
-    rc = check ? launch_gemm<128, true, true>(dev, kPairSlot[0][1], tmA, tmB, tmB2, tmV, tmBt, tmC, p, grid, s)
-               : launch_gemm<128, false, true>(dev, kPairSlot[0][0], tmA, tmB, tmB2, tmV, tmBt, tmC, p, grid, s);
-  else if (bn == 256)
-    rc = check ? launch_gemm<256, true, false>(dev, 0, tmA, tmB, tmB2, tmV, tmBt, tmC, p, grid, s)
-               : launch_gemm<256, false, false>(dev, 1, tmA, tmB, tmB2, tmV, tmBt, tmC, p, grid, s);
-  else
-    rc = check ? launch_gemm<128, true, false>(dev, 2, tmA, tmB, tmB2, tmV, tmBt, tmC, p, grid, s)
-               : launch_gemm<128, false, false>(dev, 3, tmA, tmB, tmB2, tmV, tmBt, tmC, p, grid, s);
+  rc = f16 ? launch_gemm_typed<true>(ws, check, dev, tmA, tmB, tmB2, tmV, tmBt, tmC, p, s)
+           : launch_gemm_typed<false>(ws, check, dev, tmA, tmB, tmB2, tmV, tmBt, tmC, p, s);
   if (rc != ABFT_OK) return rc;
 
   if (a->mode & ABFT_MODE_REF) {
@@ -955,13 +1032,13 @@ int abft_gemm_bf16(const abft_gemm_args* args, void* stream) {
     float* u = reinterpret_cast<float*>(wsb + ws.u_off);
     float* pb = reinterpret_cast<float*>(wsb + ws.pb_off);
     float* vf = reinterpret_cast<float*>(wsb + ws.vf_off);
-    rc = colsum(a->A, a->lda, a->M, a->K, nullptr, pa, u, nullptr, nullptr, sms, s);
+    rc = colsum(a->A, a->lda, a->M, a->K, nullptr, pa, u, nullptr, nullptr, sms, s, dt);
     if (rc != ABFT_OK) return rc;
-    rc = colsum(a->B, a->ldb, a->N, a->K, nullptr, pb, vf, nullptr, nullptr, sms, s);
+    rc = colsum(a->B, a->ldb, a->N, a->K, nullptr, pb, vf, nullptr, nullptr, sms, s, dt);
     if (rc != ABFT_OK) return rc;
     // corner + (rows of C) * sum(bias): the bias runs along the kernel's
     // rows when the operands are swapped
-    ref_finalize(ABFT_DTYPE_BF16, u, vf, p.K, p.bias, swap ? p.M : p.N, swap ? p.N : p.M, p.tile_sumc,
+    ref_finalize(dt, u, vf, p.K, p.bias, swap ? p.M : p.N, swap ? p.N : p.M, p.tile_sumc,
                  p.num_tiles * kEpiWarps * (ws.pair ? 2 : 1), a->tol_abs, a->tol_rel,
                  (a->mode & ABFT_MODE_REF_BF16) ? 1 : 0, p.report, p.capacity, ws.tile_m, bd, s);
     rc = launch_status();

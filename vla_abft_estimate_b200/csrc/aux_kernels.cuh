@@ -2,7 +2,8 @@
 //
 //   encode_weight_kernel   per-tile plain and column-index-weighted row
 //                          checksums of B[N, K] (the "Be" of checkers.py:119),
-//                          split into bf16 terms for the check MMA
+//                          split into bf16 or (scaled) fp16 terms for the
+//                          check MMA
 //   transpose_encode_kernel  K-major copy of an N-major right operand
 //                          B[K, N] (torch.bmm's mat2), with the same
 //                          checksum block computed on the way
@@ -91,13 +92,21 @@ __host__ __device__ __forceinline__ float col_sign(int j) { return (__builtin_po
 
 // Per-tile checksum block of B[N, K]: the 8 rows the fused GEMM appends to
 // each B-operand tile of bd data rows.
-// out is bf16 [tiles_n * 8, K] row-major; rows of tile t:
+// out is [tiles_n * 8, K] row-major in B's element type; rows of tile t:
 //   8t+0..2 = split3(v1), 8t+3..5 = split3(v2), 8t+6..7 = split2(v3), with
 //   v1[k] = sum_j B[t*bd + j, k],  v2[k] = sum_j (j+1) B[t*bd + j, k],
 //   v3[k] = sum_j col_sign(j) B[t*bd + j, k]
 // (j over the tile's valid rows; fp32 sums in a fixed order).
+// bf16 has fp32's exponent range, so the terms are the sums themselves.
+// fp16 does not (largest finite 65504): each of v1, v2, v3 of a tile is
+// scaled by 2^-e, e chosen so that its largest |value| over k lands in
+// [2^14, 2^15), before the split; the scale table after the rows holds
+// 8 floats per tile, [0..2] the largest |v1|, |v2|, |v3| (pass 1, an atomic
+// max on the bit patterns of non-negative floats, zeroed beforehand) and
+// [4..6] the factors 2^e (pass 2). Multiplying by a power of two is exact,
+// so the check MMA's sums times 2^e equal the unscaled ones.
 // grid (ceil(K/64), tiles_n, batch), 256 threads. K % 8 == 0. Batch z reads
-// B + z * b_stride and writes out + z * out_stride.
+// B + z * b_stride, writes out + z * out_stride and table + z * table_stride.
 __device__ __forceinline__ void write_checksum_rows(float a1, float a2, float a3, __nv_bfloat16* o, int K) {
   __nv_bfloat16 h[8];
   split3_bf16(a1, h[0], h[1], h[2]);
@@ -108,9 +117,58 @@ __device__ __forceinline__ void write_checksum_rows(float a1, float a2, float a3
   for (int q = 0; q < 8; ++q) o[static_cast<int64_t>(q) * K] = h[q];
 }
 
-__global__ void __launch_bounds__(256) encode_weight_kernel(const __nv_bfloat16* __restrict__ B, int64_t ldb, int N,
-                                                            int K, int bd, __nv_bfloat16* __restrict__ out,
-                                                            int64_t b_stride, int64_t out_stride) {
+// fp16 terms: hi = rn(x), mid = rn(x - hi), lo = rn(x - hi - mid); with
+// |x| < 2^15 no term overflows and both differences are exact in fp32.
+__device__ __forceinline__ void split3_f16(float x, __half& hi, __half& mid, __half& lo) {
+  hi = __float2half_rn(x);
+  const float r1 = x - __half2float(hi);
+  mid = __float2half_rn(r1);
+  lo = __float2half_rn(r1 - __half2float(mid));
+}
+
+__device__ __forceinline__ void write_checksum_rows_f16(float a1, float a2, float a3, __half* o, int K) {
+  __half h[8];
+  split3_f16(a1, h[0], h[1], h[2]);
+  split3_f16(a2, h[3], h[4], h[5]);
+  h[6] = __float2half_rn(a3);
+  h[7] = __float2half_rn(a3 - __half2float(h[6]));
+#pragma unroll
+  for (int q = 0; q < 8; ++q) o[static_cast<int64_t>(q) * K] = h[q];
+}
+
+// The exponent e of an fp16 checksum scale for largest magnitude m: 2^-e m
+// in [2^14, 2^15) for normal m; 0 for zero, subnormal or non-finite m;
+// limited to [-100, 100] so that 2^e and 2^-e are normal floats.
+__host__ __device__ __forceinline__ int f16_chk_exponent(uint32_t mbits) {
+  const int be = static_cast<int>((mbits >> 23) & 0xFFu);
+  if (be == 0 || be == 0xFF) return 0;
+  const int e = (be - 127) - 14;
+  return e < -100 ? -100 : (e > 100 ? 100 : e);
+}
+__host__ __device__ __forceinline__ float pow2f_exact(int e) {  // 2^e, e in [-126, 127]
+  const uint32_t bits = static_cast<uint32_t>(e + 127) << 23;
+  float f;
+  memcpy(&f, &bits, 4);
+  return f;
+}
+
+__device__ __forceinline__ void unpack8_as(const uint4 w, float (&x)[8], const __nv_bfloat16*) { unpack8(w, x); }
+__device__ __forceinline__ void unpack8_as(const uint4 w, float (&x)[8], const __half*) {
+  const uint32_t q[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&q[i]));
+    x[2 * i] = f.x;
+    x[2 * i + 1] = f.y;
+  }
+}
+
+// PASS 0: bf16 rows. PASS 1: fp16 largest magnitudes into the table.
+// PASS 2: fp16 scaled rows and the table's factors.
+template <typename T, int PASS>
+__global__ void __launch_bounds__(256) encode_weight_kernel(const T* __restrict__ B, int64_t ldb, int N, int K, int bd,
+                                                            T* __restrict__ out, int64_t b_stride, int64_t out_stride,
+                                                            float* __restrict__ table, int64_t table_stride) {
   __shared__ float red[3][32][65];
   B += static_cast<int64_t>(blockIdx.z) * b_stride;
   out += static_cast<int64_t>(blockIdx.z) * out_stride;
@@ -126,7 +184,7 @@ __global__ void __launch_bounds__(256) encode_weight_kernel(const __nv_bfloat16*
     // the first is used, so the pass waits for one memory round trip rather
     // than one per row; the order of the sums is that of a row-at-a-time loop.
     const int nrows = min(bd, N - nt * bd);
-    const __nv_bfloat16* base = B + static_cast<int64_t>(nt) * bd * ldb + k0;
+    const T* base = B + static_cast<int64_t>(nt) * bd * ldb + k0;
     uint4 w[8];
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
@@ -139,7 +197,7 @@ __global__ void __launch_bounds__(256) encode_weight_kernel(const __nv_bfloat16*
       const int j = rg + 32 * u;
       if (j >= nrows) break;
       float x[8];
-      unpack8(w[u], x);
+      unpack8_as(w[u], x, B);
       const float wt = static_cast<float>(j + 1);
       const float sg = col_sign(j);
 #pragma unroll
@@ -157,16 +215,45 @@ __global__ void __launch_bounds__(256) encode_weight_kernel(const __nv_bfloat16*
     red[2][rg][c8 * 8 + e] = s3[e];
   }
   __syncthreads();
-  if (t < 64) {
-    const int col = kb * 64 + t;
-    if (col < K) {
-      float a1 = 0.f, a2 = 0.f, a3 = 0.f;
-      for (int g = 0; g < 32; ++g) {
-        a1 += red[0][g][t];
-        a2 += red[1][g][t];
-        a3 += red[2][g][t];
+  if (t >= 64) return;
+  const int col = kb * 64 + t;
+  float a1 = 0.f, a2 = 0.f, a3 = 0.f;
+  if (col < K) {
+    for (int g = 0; g < 32; ++g) {
+      a1 += red[0][g][t];
+      a2 += red[1][g][t];
+      a3 += red[2][g][t];
+    }
+  }
+  T* const o = out + static_cast<int64_t>(nt) * 8 * K + col;
+  if constexpr (PASS == 0) {
+    if (col < K) write_checksum_rows(a1, a2, a3, o, K);
+  } else {
+    float* const tb = table + static_cast<int64_t>(blockIdx.z) * table_stride + static_cast<int64_t>(nt) * 8;
+    if constexpr (PASS == 1) {
+      float m1 = fabsf(a1), m2 = fabsf(a2), m3 = fabsf(a3);
+#pragma unroll
+      for (int d = 16; d > 0; d >>= 1) {
+        m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, d));
+        m2 = fmaxf(m2, __shfl_xor_sync(0xffffffffu, m2, d));
+        m3 = fmaxf(m3, __shfl_xor_sync(0xffffffffu, m3, d));
       }
-      write_checksum_rows(a1, a2, a3, out + static_cast<int64_t>(nt) * 8 * K + col, K);
+      if ((t & 31) == 0) {
+        atomicMax(reinterpret_cast<unsigned int*>(tb + 0), __float_as_uint(m1));
+        atomicMax(reinterpret_cast<unsigned int*>(tb + 1), __float_as_uint(m2));
+        atomicMax(reinterpret_cast<unsigned int*>(tb + 2), __float_as_uint(m3));
+      }
+    } else {
+      const int e1 = f16_chk_exponent(__float_as_uint(tb[0]));
+      const int e2 = f16_chk_exponent(__float_as_uint(tb[1]));
+      const int e3 = f16_chk_exponent(__float_as_uint(tb[2]));
+      if (kb == 0 && t == 0) {
+        tb[4] = pow2f_exact(e1);
+        tb[5] = pow2f_exact(e2);
+        tb[6] = pow2f_exact(e3);
+      }
+      if (col < K)
+        write_checksum_rows_f16(a1 * pow2f_exact(-e1), a2 * pow2f_exact(-e2), a3 * pow2f_exact(-e3), o, K);
     }
   }
 }

@@ -49,6 +49,7 @@
 #pragma once
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include "../../include/abft_b200.h"
 #include "aux_kernels.cuh"
@@ -128,9 +129,9 @@ inline FastDiv make_fast_div(int64_t d) {
 }
 
 struct GemmParams {
-  __nv_bfloat16* C;
+  void* C;            // bf16 or fp16, the kernel instance's element type
   int64_t ldc;
-  const __nv_bfloat16* bias;
+  const void* bias;   // same type
   int M, N, K;
   int num_kb, tiles_m, tiles_n, num_tiles, group_m;
   uint32_t mode;
@@ -183,6 +184,11 @@ struct GemmParams {
   int batch;
   int c_rows;
   uint32_t* bcounts;
+  // fp16 checksum blocks carry a power-of-two scale per (tile, checksum):
+  // float [tiles_n][8] whose entries 4..6 multiply the expected sums of v1,
+  // v2, v3 (batch b at chk_scale + b * chk_scale_bstride); null for bf16.
+  const float* chk_scale;
+  int64_t chk_scale_bstride;
   // Divisors of tile_coords (every warp maps every tile it meets): tile
   // rows, full tiles per batch, tiles per raster group, and the height of
   // a raster group (the last group may be shorter).
@@ -311,6 +317,42 @@ __device__ __forceinline__ void mbar_wait_unwind(uint64_t* bar, uint32_t parity)
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
+// The operand / output element type of a kernel instance: bf16 (F16 =
+// false) or fp16. Both use kind::f16 MMAs with fp32 accumulation; one MMA
+// takes one type for A and B, so the checksum rows have the operands' type.
+template <bool F16>
+struct Elem;
+template <>
+struct Elem<false> {
+  using T = __nv_bfloat16;
+  static constexpr uint32_t kFmt = 1u;  // instruction-descriptor format
+  static __device__ __forceinline__ float lo(uint32_t w) { return bf16_lo(w); }
+  static __device__ __forceinline__ float hi(uint32_t w) { return bf16_hi(w); }
+  static __device__ __forceinline__ uint32_t pack2(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  static __device__ __forceinline__ T from_f(float x) { return __float2bfloat16_rn(x); }
+  static __device__ __forceinline__ float to_f(T x) { return __bfloat162float(x); }
+};
+template <>
+struct Elem<true> {
+  using T = __half;
+  static constexpr uint32_t kFmt = 0u;
+  static __device__ __forceinline__ float lo(uint32_t w) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(w & 0xFFFFu)));
+  }
+  static __device__ __forceinline__ float hi(uint32_t w) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(w >> 16)));
+  }
+  static __device__ __forceinline__ uint32_t pack2(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  static __device__ __forceinline__ T from_f(float x) { return __float2half_rn(x); }
+  static __device__ __forceinline__ float to_f(T x) { return __half2float(x); }
+};
+
 // Token checksum rows of one stage of the swapped B-operand tile, formed by
 // two warps, warp wb for k columns [32 wb, 32 wb + 32) of the 64-wide
 // k-block. sb: the stage's tile, 128-byte rows with the 128-byte swizzle
@@ -412,14 +454,14 @@ __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.
 // four K=16 MMAs of width NM and release the stage when they complete. NM is
 // a template argument so that every instruction descriptor is a compile-time
 // constant (a runtime descriptor slowed the issue loop down severalfold).
-template <int BN, bool CHECK, bool PAIR, int NM>
+template <int BN, bool CHECK, bool PAIR, bool F16, int NM>
 __device__ __forceinline__ bool mma_mainloop(uint8_t* smem, uint64_t* full, uint64_t* empty, int& stage,
                                              uint32_t& phase, int kb0, int kb1, uint32_t d,
                                              volatile int* abort_flag) {
   using Cfg = GemmCfg<BN, CHECK, PAIR>;
   constexpr int S = Cfg::kStages;
   constexpr int G = PAIR ? 2 : 1;
-  constexpr uint32_t idesc = umma_idesc_bf16(Cfg::kTileM, NM);
+  constexpr uint32_t idesc = umma_idesc(Cfg::kTileM, NM, Elem<F16>::kFmt);
   static_assert(NM % 16 == 0 && NM >= 16 && NM <= BN, "MMA width");
   for (int kb = kb0; kb < kb1; ++kb) {
     if (!mbar_wait(&full[stage], phase, abort_flag)) return false;
@@ -447,13 +489,14 @@ __device__ __forceinline__ bool mma_mainloop(uint8_t* smem, uint64_t* full, uint
 
 // mma_mainloop for a runtime width n (a multiple of 16 in [16, BN]): one
 // compile-time instance per width.
-template <int BN, bool CHECK, bool PAIR, int NM = 16>
+template <int BN, bool CHECK, bool PAIR, bool F16, int NM = 16>
 __device__ __forceinline__ bool mma_mainloop_n(int n, uint8_t* smem, uint64_t* full, uint64_t* empty, int& stage,
                                                uint32_t& phase, int kb0, int kb1, uint32_t d,
                                                volatile int* abort_flag) {
   if constexpr (NM <= BN) {
-    if (n == NM) return mma_mainloop<BN, CHECK, PAIR, NM>(smem, full, empty, stage, phase, kb0, kb1, d, abort_flag);
-    return mma_mainloop_n<BN, CHECK, PAIR, NM + 16>(n, smem, full, empty, stage, phase, kb0, kb1, d, abort_flag);
+    if (n == NM)
+      return mma_mainloop<BN, CHECK, PAIR, F16, NM>(smem, full, empty, stage, phase, kb0, kb1, d, abort_flag);
+    return mma_mainloop_n<BN, CHECK, PAIR, F16, NM + 16>(n, smem, full, empty, stage, phase, kb0, kb1, d, abort_flag);
   } else {
     return false;
   }
@@ -466,16 +509,20 @@ __device__ __forceinline__ bool mma_mainloop_n(int n, uint8_t* smem, uint64_t* f
 // all tail_n rows the narrow MMA reads. tmC: the output [batch][M][N] in
 // 32 x 32 boxes with 64-byte swizzle, the layout of an epilogue warp's
 // staging block (unused with swapped operands).
-template <int BN, bool CHECK, bool PAIR>
+template <int BN, bool CHECK, bool PAIR, bool F16>
 __global__ void __launch_bounds__(kThreads, 1)
     abft_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmB2, const __grid_constant__ CUtensorMap tmV,
                      const __grid_constant__ CUtensorMap tmBt, const __grid_constant__ CUtensorMap tmC,
                      const GemmParams p) {
   using Cfg = GemmCfg<BN, CHECK, PAIR>;
+  using E = Elem<F16>;
+  using T = typename E::T;
   constexpr int S = Cfg::kStages;
   constexpr int BD = Cfg::kBD;
   constexpr int G = PAIR ? 2 : 1;
+  T* const Cout = static_cast<T*>(p.C);
+  const T* const biasp = static_cast<const T*>(p.bias);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
@@ -673,9 +720,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
         uint64_t* avail = p.build_chk ? ready : full;
         if (!tail)
-          ok = mma_mainloop<BN, CHECK, PAIR, BN>(smem, avail, empty, stage, phase, kb0, kb1, d, abort_flag);
+          ok = mma_mainloop<BN, CHECK, PAIR, F16, BN>(smem, avail, empty, stage, phase, kb0, kb1, d, abort_flag);
         else
-          ok = mma_mainloop_n<BN, CHECK, PAIR>(p.tail_n, smem, avail, empty, stage, phase, kb0, kb1, d, abort_flag);
+          ok = mma_mainloop_n<BN, CHECK, PAIR, F16>(p.tail_n, smem, avail, empty, stage, phase, kb0, kb1, d,
+                                                    abort_flag);
         if (!ok) break;
         if constexpr (PAIR)
           umma_commit_pair_both(&tfull[acc], 0x3);
@@ -699,7 +747,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // two warps (one half of the 64-wide k-block each) sum the token rows in
     // shared memory and write the checksum rows, which the MMA reads after
     // both have arrived on the ready barrier.
-    if (CHECK && !PAIR && p.build_chk) {
+    // fp16 instances never build: their token checksums need a scale taken
+    // over all of K, which the host's encode pass supplies instead.
+    if (CHECK && !PAIR && !F16 && p.build_chk) {
       const int wb = warp - kBuildWarp;
       int stage = 0;
       uint32_t phase = 0;
@@ -957,11 +1007,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         s1 = -((__uint_as_float(chk[0]) + __uint_as_float(chk[1])) + __uint_as_float(chk[2]));
         s2 = -((__uint_as_float(chk[3]) + __uint_as_float(chk[4])) + __uint_as_float(chk[5]));
         s3 = -(__uint_as_float(chk[6]) + __uint_as_float(chk[7]));
+        if constexpr (F16) {
+          // fp16 checksum rows hold v * 2^-e (each checksum's largest value
+          // scaled below 2^15): the expected sums are 2^e times the MMA's,
+          // exact powers of two.
+          const float* sc = p.chk_scale + bz * p.chk_scale_bstride + nt * 8;
+          s1 *= __ldg(sc + 4);
+          s2 *= __ldg(sc + 5);
+          s3 *= __ldg(sc + 6);
+        }
       }
       float row_out_sum = 0.f;
-      const uint4* bp = reinterpret_cast<const uint4*>(p.bias + col0);
+      const uint4* bp = reinterpret_cast<const uint4*>(biasp + col0);
       const int rd_grow = row0 + q * 32 + rd_row;  // global row of this lane's first read-side row
-      const float row_bias = (p.swap && p.bias != nullptr && row_ok) ? __bfloat162float(p.bias[grow]) : 0.f;
+      const float row_bias = (p.swap && p.bias != nullptr && row_ok) ? E::to_f(biasp[grow]) : 0.f;
       const int crow0 = bz * p.c_rows;  // this batch's first row of C
 #pragma unroll 1
       for (int c = t; c < NCT; c += kEpiSplit) {
@@ -1024,13 +1083,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           // Lane l holds kernel row row0 + q*32 + l = C column: for each of
           // this chunk's C rows a warp writes 32 consecutive columns.
           if (row_ok) {
-            __nv_bfloat16* cc = p.C + static_cast<int64_t>(crow0 + col0 + base) * p.ldc + grow;
+            T* cc = Cout + static_cast<int64_t>(crow0 + col0 + base) * p.ldc + grow;
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
               if (base + e < ncols) {
-                const __nv_bfloat16 o = __float2bfloat16_rn(x[e] + row_bias);
+                const T o = E::from_f(x[e] + row_bias);
                 cc[static_cast<int64_t>(e) * p.ldc] = o;
-                if (p.mode & ABFT_MODE_REF) row_out_sum += __bfloat162float(o);
+                if (p.mode & ABFT_MODE_REF) row_out_sum += E::to_f(o);
               }
             }
           }
@@ -1046,22 +1105,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           const bool gvalid = row_ok && (base + g * 8 < ncols);
           if (p.bias != nullptr && gvalid) {
             const uint4 bw = __ldg(bp + c * 4 + g);
-            x[g * 8 + 0] += bf16_lo(bw.x);
-            x[g * 8 + 1] += bf16_hi(bw.x);
-            x[g * 8 + 2] += bf16_lo(bw.y);
-            x[g * 8 + 3] += bf16_hi(bw.y);
-            x[g * 8 + 4] += bf16_lo(bw.z);
-            x[g * 8 + 5] += bf16_hi(bw.z);
-            x[g * 8 + 6] += bf16_lo(bw.w);
-            x[g * 8 + 7] += bf16_hi(bw.w);
+            x[g * 8 + 0] += E::lo(bw.x);
+            x[g * 8 + 1] += E::hi(bw.x);
+            x[g * 8 + 2] += E::lo(bw.y);
+            x[g * 8 + 3] += E::hi(bw.y);
+            x[g * 8 + 4] += E::lo(bw.z);
+            x[g * 8 + 5] += E::hi(bw.z);
+            x[g * 8 + 6] += E::lo(bw.w);
+            x[g * 8 + 7] += E::hi(bw.w);
           }
           const uint4 packed =
-              make_uint4(pack_bf16x2(x[g * 8 + 0], x[g * 8 + 1]), pack_bf16x2(x[g * 8 + 2], x[g * 8 + 3]),
-                         pack_bf16x2(x[g * 8 + 4], x[g * 8 + 5]), pack_bf16x2(x[g * 8 + 6], x[g * 8 + 7]));
+              make_uint4(E::pack2(x[g * 8 + 0], x[g * 8 + 1]), E::pack2(x[g * 8 + 2], x[g * 8 + 3]),
+                         E::pack2(x[g * 8 + 4], x[g * 8 + 5]), E::pack2(x[g * 8 + 6], x[g * 8 + 7]));
           *reinterpret_cast<uint4*>(stg + lane * 64 + ((g ^ ((lane >> 1) & 3)) << 4)) = packed;
           if ((p.mode & ABFT_MODE_REF) && gvalid) {
-            row_out_sum += ((bf16_lo(packed.x) + bf16_hi(packed.x)) + (bf16_lo(packed.y) + bf16_hi(packed.y))) +
-                           ((bf16_lo(packed.z) + bf16_hi(packed.z)) + (bf16_lo(packed.w) + bf16_hi(packed.w)));
+            row_out_sum += ((E::lo(packed.x) + E::hi(packed.x)) + (E::lo(packed.y) + E::hi(packed.y))) +
+                           ((E::lo(packed.z) + E::hi(packed.z)) + (E::lo(packed.w) + E::hi(packed.w)));
           }
         }
         if (base + 32 <= ncols) {
@@ -1083,7 +1142,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // block, four lanes per row, each lane one 16-byte piece (8 columns).
         const int lcol = base + rd_piece * 8;  // local column of this lane's piece
         const bool col_ok = lcol < ncols;
-        __nv_bfloat16* cbase = p.C + static_cast<int64_t>(crow0 + rd_grow) * p.ldc + col0 + lcol;
+        T* cbase = Cout + static_cast<int64_t>(crow0 + rd_grow) * p.ldc + col0 + lcol;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int y = i * 8 + rd_row;
@@ -1225,13 +1284,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int e = 0; e < 32; ++e) val = (e == e0) ? __uint_as_float(v[e]) : val;
             if (n_my) val += inj_add(fix_col);
-            const float bcol = p.swap ? row_bias : (p.bias != nullptr ? __bfloat162float(p.bias[col0 + fix_col]) : 0.f);
-            const __nv_bfloat16 o_old = __float2bfloat16_rn(val + bcol);
-            const __nv_bfloat16 o_new = __float2bfloat16_rn((val - fix_delta) + bcol);
+            const float bcol = p.swap ? row_bias : (p.bias != nullptr ? E::to_f(biasp[col0 + fix_col]) : 0.f);
+            const T o_old = E::from_f(val + bcol);
+            const T o_new = E::from_f((val - fix_delta) + bcol);
             const int64_t off = p.swap ? static_cast<int64_t>(crow0 + col0 + fix_col) * p.ldc + grow
                                        : static_cast<int64_t>(crow0 + grow) * p.ldc + col0 + fix_col;
-            p.C[off] = o_new;
-            if (p.mode & ABFT_MODE_REF) row_out_sum += __bfloat162float(o_new) - __bfloat162float(o_old);
+            Cout[off] = o_new;
+            if (p.mode & ABFT_MODE_REF) row_out_sum += E::to_f(o_new) - E::to_f(o_old);
           }
           need &= ~__ballot_sync(0xFFFFFFFFu, here);
         }

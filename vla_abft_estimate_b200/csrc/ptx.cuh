@@ -273,13 +273,15 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
   return d;
 }
 
-// Instruction descriptor of tcgen05.mma kind::f16 with bf16 A/B, fp32 D,
-// both operands K-major: D format [4,6)=1, A format [7,10)=1, B format
-// [10,13)=1, N>>3 at [17,23), M>>4 at [24,29).
-__host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
+// Instruction descriptor of tcgen05.mma kind::f16 with fp32 D, both
+// operands K-major and of one type (fmt 1 = bf16, 0 = fp16; one MMA never
+// mixes them): D format [4,6)=1, A format [7,10)=fmt, B format [10,13)=fmt,
+// N>>3 at [17,23), M>>4 at [24,29).
+__host__ __device__ constexpr uint32_t umma_idesc(int M, int N, uint32_t fmt) {
+  return (1u << 4) | (fmt << 7) | (fmt << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
          (static_cast<uint32_t>(M >> 4) << 24);
 }
+__host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N) { return umma_idesc(M, N, 1u); }
 
 __device__ __forceinline__ void umma_bf16_ss(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                              uint32_t accumulate) {

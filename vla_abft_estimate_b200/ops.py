@@ -2,7 +2,8 @@
 
 PyTorch supplies device memory, the current stream and the caching allocator
 for workspaces; every computation runs in libabft_b200.so. Inputs must be CUDA
-bf16 tensors on an sm_100 device; anything else raises (no CPU fallback).
+bf16 or fp16 tensors (the post-hoc check also fp32) on an sm_100 device;
+anything else raises (no CPU fallback).
 
 Functions
   encode_weight(weight, tile_n)          per-tile checksums of a [N, K] weight
@@ -36,13 +37,19 @@ def _stream(device: torch.device) -> ctypes.c_void_p:
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
 
 
-def _require_bf16_cuda(name: str, t: torch.Tensor, dim: int) -> None:
+# Element types of the fused GEMM (the post-hoc check adds fp32).
+GEMM_DTYPES = {torch.bfloat16: N.DTYPE_BF16, torch.float16: N.DTYPE_F16}
+
+
+def _require_bf16_cuda(name: str, t: torch.Tensor, dim: int, dtype: torch.dtype = torch.bfloat16) -> None:
+    """``t`` is a CUDA tensor of ``dtype`` with ``dim`` dimensions and unit
+    stride in its last one."""
     if not isinstance(t, torch.Tensor):
         raise TypeError(f"{name} must be a torch.Tensor")
     if not t.is_cuda:
         raise ValueError(f"{name} must be a CUDA tensor (the library has no CPU path)")
-    if t.dtype != torch.bfloat16:
-        raise ValueError(f"{name} must be bfloat16, got {t.dtype}")
+    if t.dtype != dtype:
+        raise ValueError(f"{name} must be {str(dtype).replace('torch.', '')}, got {t.dtype}")
     if t.dim() != dim:
         raise ValueError(f"{name} must be {dim}-D, got shape {tuple(t.shape)}")
     if t.stride(-1) != 1:
@@ -126,7 +133,7 @@ _WS_BYTES: dict = {}
 
 
 def _run_gemm(args: N.GemmArgs, dev: torch.device, key: tuple) -> None:
-    """Workspace, current stream and device guard around abft_gemm_bf16."""
+    """Workspace, current stream and device guard around abft_gemm."""
     idx = dev.index if dev.index is not None else torch.cuda.current_device()
     stream = torch._C._cuda_getCurrentRawStream(idx)
     L = N.lib()
@@ -141,7 +148,7 @@ def _run_gemm(args: N.GemmArgs, dev: torch.device, key: tuple) -> None:
         ws = _workspace(dev, ws_bytes, stream)
         args.workspace = ws.data_ptr()
         args.workspace_bytes = ws.numel()
-    N.check("abft_gemm_bf16", L.abft_gemm_bf16(ctypes.byref(args), ctypes.c_void_p(stream)))
+    N.check("abft_gemm", L.abft_gemm(ctypes.byref(args), ctypes.c_void_p(stream)))
 
 
 def pick_tile_n(m: int, n: int, k: int, device: Optional[torch.device] = None,
@@ -158,24 +165,44 @@ def pick_tile_m(m: int, n: int, k: int, tile_n: int, device: Optional[torch.devi
     return int(N.lib().abft_pick_tile_m(int(m), int(n), int(k), int(sms), int(mode), int(tile_n)))
 
 
+def _gemm_dtype(t: torch.Tensor) -> int:
+    code = GEMM_DTYPES.get(t.dtype) if isinstance(t, torch.Tensor) else None
+    if code is None:
+        got = t.dtype if isinstance(t, torch.Tensor) else type(t)
+        raise ValueError(f"the fused GEMM takes bfloat16 or float16 operands, got {got}")
+    return code
+
+
+def checksum_bytes(n: int, k: int, tile_n: int, dtype: torch.dtype = torch.bfloat16) -> int:
+    """Bytes of the checksum block of an [n, k] weight of ``dtype``."""
+    return int(N.lib().abft_checksum_bytes_typed(int(n), int(k), int(tile_n), GEMM_DTYPES.get(dtype, -1)))
+
+
 def encode_weight(weight: torch.Tensor, tile_n: int) -> torch.Tensor:
     """Per-tile checksum block of ``weight`` [N, K] for tile width ``tile_n``.
 
-    Returns bf16 [ceil(N / (tile_n - 8)) * 8, K]: for each tile, the plain
-    and the column-index-weighted row checksums, each as three bf16 terms,
-    and the Thue-Morse signed checksum as two bf16 terms (the 8 extra
-    B-operand rows of the fused kernel's tile).
+    bf16 weights: returns bf16 [ceil(N / (tile_n - 8)) * 8, K]: for each
+    tile, the plain and the column-index-weighted row checksums, each as
+    three bf16 terms, and the Thue-Morse signed checksum as two bf16 terms
+    (the 8 extra B-operand rows of the fused kernel's tile).
+    fp16 weights: returns the block as flat uint8 bytes: the same rows in
+    fp16 terms, each checksum of a tile scaled by a power of two that keeps
+    it inside fp16's range, followed by the table of those factors.
     """
-    _require_bf16_cuda("weight", weight, 2)
+    dt = _gemm_dtype(weight)
+    _require_bf16_cuda("weight", weight, 2, weight.dtype)
     n, k = weight.shape
-    nbytes = int(N.lib().abft_checksum_bytes(n, k, int(tile_n)))
+    nbytes = checksum_bytes(n, k, tile_n, weight.dtype)
     if nbytes == 0:
         raise ValueError(f"tile_n must be 128 or 256, got {tile_n}")
-    out = torch.empty((nbytes // (2 * k), k), dtype=torch.bfloat16, device=weight.device)
+    if weight.dtype == torch.bfloat16:
+        out = torch.empty((nbytes // (2 * k), k), dtype=torch.bfloat16, device=weight.device)
+    else:
+        out = torch.empty((nbytes,), dtype=torch.uint8, device=weight.device)
     with torch.cuda.device(weight.device):
-        rc = N.lib().abft_encode_weight(_ptr(weight), n, k, weight.stride(0), int(tile_n), _ptr(out),
-                                        _stream(weight.device))
-    N.check("abft_encode_weight", rc)
+        rc = N.lib().abft_encode_weight_typed(_ptr(weight), n, k, weight.stride(0), 0, 1, int(tile_n), dt, _ptr(out),
+                                              _stream(weight.device))
+    N.check("abft_encode_weight_typed", rc)
     return out
 
 
@@ -215,7 +242,8 @@ def abft_gemm(
 ) -> Tuple[torch.Tensor, Optional[ReportBuffer]]:
     """``out = a @ weight.T (+ bias)`` with the fused checksum epilogue.
 
-    ``a`` is [M, K], ``weight`` [N, K] (nn.Linear layout), ``bias`` [N].
+    ``a`` is [M, K], ``weight`` [N, K] (nn.Linear layout), ``bias`` [N], all
+    bfloat16 or all float16 (``out`` too).
     ``checksums`` is ``encode_weight(weight, tile_n)`` (cache it for a fixed
     weight); when omitted and checks are on, the call encodes into its
     workspace. ``tile_m`` 256 runs each 256-row tile on a 2-CTA pair (either
@@ -226,8 +254,10 @@ def abft_gemm(
     ``inject`` adds debug faults to the fp32 accumulator.
     Returns the output and the report buffer (None when mode == MODE_OFF).
     """
-    _require_bf16_cuda("a", a, 2)
-    _require_bf16_cuda("weight", weight, 2)
+    _gemm_dtype(a)
+    dtype = a.dtype
+    _require_bf16_cuda("a", a, 2, dtype)
+    _require_bf16_cuda("weight", weight, 2, dtype)
     m, k = a.shape
     n, k2 = weight.shape
     if k != k2:
@@ -235,25 +265,26 @@ def abft_gemm(
     if weight.device != a.device:
         raise ValueError("a and weight must be on the same device")
     if bias is not None:
-        _require_bf16_cuda("bias", bias, 1)
+        _require_bf16_cuda("bias", bias, 1, dtype)
         if bias.shape[0] != n:
             raise ValueError(f"bias has {bias.shape[0]} entries, expected {n}")
     dev = a.device
     if out is None:
-        out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+        out = torch.empty((m, n), dtype=dtype, device=dev)
     else:
-        _require_bf16_cuda("out", out, 2)
+        _require_bf16_cuda("out", out, 2, dtype)
         if tuple(out.shape) != (m, n):
             raise ValueError(f"out must be [{m}, {n}]")
     if mode != N.MODE_OFF and report is None:
         report = ReportBuffer(DEFAULT_CAPACITY, dev)
     if checksums is not None:
-        if checksums.dtype != torch.bfloat16 or not checksums.is_cuda:
-            raise ValueError("checksums must be the CUDA bf16 tensor encode_weight() returns")
+        block = torch.bfloat16 if dtype == torch.bfloat16 else torch.uint8
+        if checksums.dtype != block or not checksums.is_cuda:
+            raise ValueError(f"checksums must be the CUDA {block} tensor encode_weight() returns for a {dtype} weight")
         if tile_n == 0:
             raise ValueError("pass the tile_n the checksums were encoded for")
-        need = int(N.lib().abft_checksum_bytes(n, k, int(tile_n)))
-        if checksums.numel() * 2 < need:
+        need = checksum_bytes(n, k, tile_n, dtype)
+        if checksums.numel() * checksums.element_size() < need:
             raise ValueError("checksums were encoded for a different weight shape or tile width")
     _gemm_launch(a, weight, bias, out, m, n, k, mode, tile_n, tile_m, swap_ab, thr_scale, thr_abs, tol_abs, tol_rel,
                  checksums, inject, report, num_sms)
@@ -284,11 +315,12 @@ def _gemm_launch(a, weight, bias, out, m, n, k, mode, tile_n, tile_m, swap_ab, t
     args.report = report.data_ptr() if report is not None else None
     args.report_capacity = report.capacity if report is not None else 0
     args.num_sms = int(num_sms)
+    args.dtype = GEMM_DTYPES[a.dtype]
     if inj is not None:
         args.inject_rows, args.inject_cols, args.inject_deltas = _ptr(inj.rows), _ptr(inj.cols), _ptr(inj.deltas)
         args.n_inject = inj.n
     _run_gemm(args, dev, (m, n, k, int(mode), int(tile_n), int(tile_m), int(swap_ab), checksums is None,
-                          int(num_sms), 1, 0))
+                          int(num_sms), 1, 0, args.dtype))
 
 
 def _mat_layout(t: torch.Tensor) -> Optional[Tuple[int, int]]:
@@ -331,6 +363,7 @@ def abft_bmm(
     [B, N, K] tensor, e.g. ``k.transpose(1, 2)``) is read in place, a
     row-major one is copied K-major by the call (with its checksums formed
     on the way). ``b_layout="nk"``: ``b`` is [B, N, K] (weight layout).
+    Operands (and ``bias``, ``out``) are all bfloat16 or all float16.
     ``inject`` rows and the report's record rows are flattened over the
     batch (row ``i`` of batch ``j`` is ``j * M + i``); ``report.read()
     .batch_view(j, M)`` gives batch ``j`` alone. Returns ``out`` [B, M, N]
@@ -338,9 +371,11 @@ def abft_bmm(
     """
     if a.dim() != 3 or b.dim() != 3:
         raise ValueError(f"abft_bmm takes 3-D operands, got {tuple(a.shape)} and {tuple(b.shape)}")
+    _gemm_dtype(a)
+    dtype = a.dtype
     for name, t in (("a", a), ("b", b)):
-        if not t.is_cuda or t.dtype != torch.bfloat16:
-            raise ValueError(f"{name} must be a CUDA bfloat16 tensor (the library has no CPU path)")
+        if not t.is_cuda or t.dtype != dtype:
+            raise ValueError(f"{name} must be a CUDA {dtype} tensor (the library has no CPU path)")
     bsz, m, k = a.shape
     n_dim = 2 if b_layout == "kn" else 1
     if k % 8 or b.shape[n_dim] % 8:
@@ -366,14 +401,14 @@ def abft_bmm(
     if _mat_layout(a) is None:
         a = a.contiguous()
     if bias is not None:
-        _require_bf16_cuda("bias", bias, 1)
+        _require_bf16_cuda("bias", bias, 1, dtype)
         if bias.shape[0] != n:
             raise ValueError(f"bias has {bias.shape[0]} entries, expected {n}")
     dev = a.device
     if out is None:
-        out = torch.empty((bsz, m, n), dtype=torch.bfloat16, device=dev)
-    elif (out.dtype != torch.bfloat16 or tuple(out.shape) != (bsz, m, n) or not out.is_contiguous()):
-        raise ValueError(f"out must be a contiguous bf16 [{bsz}, {m}, {n}] tensor")
+        out = torch.empty((bsz, m, n), dtype=dtype, device=dev)
+    elif (out.dtype != dtype or tuple(out.shape) != (bsz, m, n) or not out.is_contiguous()):
+        raise ValueError(f"out must be a contiguous {dtype} [{bsz}, {m}, {n}] tensor")
     if mode != N.MODE_OFF:
         if report is None:
             report = ReportBuffer(DEFAULT_CAPACITY, dev, batch=bsz)
@@ -411,11 +446,12 @@ def _bmm_call(a, bmat, b_kn, bias, out, bsz, m, n, k, mode, tile_n, tile_m, swap
     args.report = report.data_ptr() if report is not None and mode != N.MODE_OFF else None
     args.report_capacity = report.capacity if report is not None and mode != N.MODE_OFF else 0
     args.num_sms = int(num_sms)
+    args.dtype = GEMM_DTYPES[a.dtype]
     if inj is not None:
         args.inject_rows, args.inject_cols, args.inject_deltas = _ptr(inj.rows), _ptr(inj.cols), _ptr(inj.deltas)
         args.n_inject = inj.n
     _run_gemm(args, dev, (m, n, k, int(mode), int(tile_n), int(tile_m), int(swap_ab), True, int(num_sms), bsz,
-                          b_kn))
+                          b_kn, args.dtype))
     return out, (report if mode != N.MODE_OFF else None)
 
 
