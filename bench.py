@@ -350,14 +350,15 @@ def timed_medians_interleaved(fns, iters, flush, sleep_cycles=100_000_000):
     return out
 
 
-def gemm_point(m, n, k, iters, flush, seed=0):
+def gemm_point(m, n, k, iters, flush, seed=0, dtype="bf16"):
     """One BASELINE GEMM configuration on cuda:0: median kernel times (L2
     flushed before each launch, the variants interleaved) of cuBLAS, the
     fused kernel with checks off and on (weight checksums cached), and of
     the checked call that encodes the checksums itself (a fresh weight);
     then the BASELINE fault runs:
     clean, 1 and 4 faults of 2^8 max|C| at seeded distinct rows and columns
-    (exact coordinates and corrections required)."""
+    (exact coordinates and corrections required). ``dtype`` "f16" runs the
+    same on fp16 operands (cuBLAS fp16 beside it)."""
     import torch
 
     from vla_abft_estimate_b200 import _native as N
@@ -365,10 +366,11 @@ def gemm_point(m, n, k, iters, flush, seed=0):
     from vla_abft_estimate_b200.faults import seeded_fault_positions
 
     dev = torch.device("cuda", 0)
+    tdt = torch.float16 if dtype == "f16" else torch.bfloat16
     g = torch.Generator(device=dev).manual_seed(seed)
-    a = (torch.randn(m, k, device=dev, generator=g) * k ** -0.5).bfloat16()
-    w = (torch.randn(n, k, device=dev, generator=g) * k ** -0.5).bfloat16()
-    out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+    a = (torch.randn(m, k, device=dev, generator=g) * k ** -0.5).to(tdt)
+    w = (torch.randn(n, k, device=dev, generator=g) * k ** -0.5).to(tdt)
+    out = torch.empty(m, n, device=dev, dtype=tdt)
     chk = N.MODE_DETECT | N.MODE_CORRECT
     tn_chk = ops.pick_tile_n(m, n, k, dev, chk)
     tn_off = ops.pick_tile_n(m, n, k, dev, N.MODE_OFF)
@@ -392,7 +394,7 @@ def gemm_point(m, n, k, iters, flush, seed=0):
         faults_ok[f"{count}_fault_located_corrected"] = (r.coords() == sorted(pos) and r.n_corrected == count
                                                           and err <= 1e-2)
     fl = 2.0 * m * n * k
-    res = {"M": m, "N": n, "K": k, "tile_n": {"unchecked": tn_off, "checked": tn_chk},
+    res = {"M": m, "N": n, "K": k, "dtype": dtype, "tile_n": {"unchecked": tn_off, "checked": tn_chk},
            "cublas_tflops": fl / t_cublas / 1e9, "unchecked_tflops": fl / t_off / 1e9,
            "checked_tflops": fl / t_chk / 1e9, "overhead_pct": 100.0 * (t_chk / t_off - 1.0),
            "checked_vs_cublas": t_cublas / t_chk,
@@ -738,11 +740,13 @@ def run_ours(args):
     if world == 1 and rank == 0 and not args.no_extras:
         # The other BASELINE metrics, measured in the same process: config 1
         # (one 512x4096x4096 protected GEMM), the largest square shape, and
-        # the Qwen2-7B prefill-512 tokens/s with every linear protected.
+        # the Qwen2-7B prefill-512 tokens/s with every linear protected; plus
+        # the headline shape on fp16 operands.
         flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
         it = max(args.steps, 10)
         extras["config1_512x4096x4096"] = gemm_point(512, 4096, 4096, it, flush)
         extras["square_16384"] = gemm_point(16384, 16384, 16384, min(it, 10), flush)
+        extras["fp16_8192"] = gemm_point(8192, 8192, 8192, it, flush, dtype="f16")
         del flush
         torch.cuda.empty_cache()
         extras["qwen2_7b_prefill512"] = qwen_prefill_point(reps=5, warmup=2)

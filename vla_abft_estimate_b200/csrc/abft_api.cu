@@ -777,7 +777,8 @@ int abft_encode_weight_typed(const void* B, int64_t N, int64_t K, int64_t ldb, i
     return launch_status();
   }
   // fp16: zero the scale tables (one row of tiles * 8 floats per batch),
-  // find each tile's largest checksum magnitudes, then write the scaled rows.
+  // form the sums (staged in the rows' own bytes) and each tile's largest
+  // magnitudes, then write the scaled rows.
   float* table = reinterpret_cast<float*>(static_cast<uint8_t*>(out) + checksum_rows_bytes(N, K, tile_n));
   if (cudaMemset2DAsync(table, bytes, 0, static_cast<size_t>(tiles) * 8 * sizeof(float), static_cast<size_t>(batch),
                         s) != cudaSuccess)
@@ -789,9 +790,8 @@ int abft_encode_weight_typed(const void* B, int64_t N, int64_t K, int64_t ldb, i
                                                     static_cast<int64_t>(bytes / 4));
   rc = launch_status();
   if (rc != ABFT_OK) return rc;
-  encode_weight_kernel<__half, 2><<<g, 256, 0, s>>>(Bh, ldb, static_cast<int>(N), static_cast<int>(K), bd, oh,
-                                                    stride_b, static_cast<int64_t>(bytes / 2), table,
-                                                    static_cast<int64_t>(bytes / 4));
+  encode_f16_finish_kernel<<<g, 64, 0, s>>>(oh, static_cast<int>(K), static_cast<int64_t>(bytes / 2), table,
+                                             static_cast<int64_t>(bytes / 4));
   return launch_status();
 }
 

@@ -104,7 +104,9 @@ __host__ __device__ __forceinline__ float col_sign(int j) { return (__builtin_po
 // 8 floats per tile, [0..2] the largest |v1|, |v2|, |v3| (pass 1, an atomic
 // max on the bit patterns of non-negative floats, zeroed beforehand) and
 // [4..6] the factors 2^e (pass 2). Multiplying by a power of two is exact,
-// so the check MMA's sums times 2^e equal the unscaled ones.
+// so the check MMA's sums times 2^e equal the unscaled ones. Pass 1 leaves
+// its fp32 sums in the rows it will own (f16_stage_slot), so pass 2 reads
+// 12 bytes per column instead of the weight again.
 // grid (ceil(K/64), tiles_n, batch), 256 threads. K % 8 == 0. Batch z reads
 // B + z * b_stride, writes out + z * out_stride and table + z * table_stride.
 __device__ __forceinline__ void write_checksum_rows(float a1, float a2, float a3, __nv_bfloat16* o, int K) {
@@ -163,8 +165,23 @@ __device__ __forceinline__ void unpack8_as(const uint4 w, float (&x)[8], const _
   }
 }
 
-// PASS 0: bf16 rows. PASS 1: fp16 largest magnitudes into the table.
-// PASS 2: fp16 scaled rows and the table's factors.
+// Where pass 1 of an fp16 encode keeps sum q (0..2) of k column kb*64 + t:
+// inside the bytes the block's final rows occupy (8 rows x c columns x 2
+// bytes, c = the block's valid columns, a multiple of 8), read as 8
+// segments of 2c bytes; the 3c floats fill the first 12c of those 16c
+// bytes. No other block writes there, so pass 2 may read them and then
+// overwrite them with the rows. rows_tile: the tile's first checksum row.
+__device__ __forceinline__ float* f16_stage_slot(__half* rows_tile, int K, int kb, int c, int q, int t) {
+  const int f = q * c + t;
+  const int seg = (2 * f) / c;           // (4 f) / (2 c): row of the segment, < 6
+  const int off = 4 * f - seg * 2 * c;   // byte offset inside it, a multiple of 4
+  return reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(rows_tile + static_cast<int64_t>(seg) * K + kb * 64) +
+                                  off);
+}
+
+// PASS 0: bf16 rows. PASS 1 (fp16): sums staged in place (f16_stage_slot)
+// and the largest magnitudes into the table; encode_f16_finish_kernel then
+// writes the scaled rows.
 template <typename T, int PASS>
 __global__ void __launch_bounds__(256) encode_weight_kernel(const T* __restrict__ B, int64_t ldb, int N, int K, int bd,
                                                             T* __restrict__ out, int64_t b_stride, int64_t out_stride,
@@ -225,12 +242,11 @@ __global__ void __launch_bounds__(256) encode_weight_kernel(const T* __restrict_
       a3 += red[2][g][t];
     }
   }
-  T* const o = out + static_cast<int64_t>(nt) * 8 * K + col;
   if constexpr (PASS == 0) {
-    if (col < K) write_checksum_rows(a1, a2, a3, o, K);
+    if (col < K) write_checksum_rows(a1, a2, a3, out + static_cast<int64_t>(nt) * 8 * K + col, K);
   } else {
     float* const tb = table + static_cast<int64_t>(blockIdx.z) * table_stride + static_cast<int64_t>(nt) * 8;
-    if constexpr (PASS == 1) {
+    {
       float m1 = fabsf(a1), m2 = fabsf(a2), m3 = fabsf(a3);
 #pragma unroll
       for (int d = 16; d > 0; d >>= 1) {
@@ -243,19 +259,45 @@ __global__ void __launch_bounds__(256) encode_weight_kernel(const T* __restrict_
         atomicMax(reinterpret_cast<unsigned int*>(tb + 1), __float_as_uint(m2));
         atomicMax(reinterpret_cast<unsigned int*>(tb + 2), __float_as_uint(m3));
       }
-    } else {
-      const int e1 = f16_chk_exponent(__float_as_uint(tb[0]));
-      const int e2 = f16_chk_exponent(__float_as_uint(tb[1]));
-      const int e3 = f16_chk_exponent(__float_as_uint(tb[2]));
-      if (kb == 0 && t == 0) {
-        tb[4] = pow2f_exact(e1);
-        tb[5] = pow2f_exact(e2);
-        tb[6] = pow2f_exact(e3);
+      if (col < K) {
+        __half* const rows_tile = reinterpret_cast<__half*>(out) + static_cast<int64_t>(nt) * 8 * K;
+        const int c = min(64, K - kb * 64);
+        *f16_stage_slot(rows_tile, K, kb, c, 0, t) = a1;
+        *f16_stage_slot(rows_tile, K, kb, c, 1, t) = a2;
+        *f16_stage_slot(rows_tile, K, kb, c, 2, t) = a3;
       }
-      if (col < K)
-        write_checksum_rows_f16(a1 * pow2f_exact(-e1), a2 * pow2f_exact(-e2), a3 * pow2f_exact(-e3), o, K);
     }
   }
+}
+
+// Pass 2 of an fp16 encode: per (k block, tile, batch) the 64 threads read
+// the block's staged sums, then write the scaled fp16 rows over them; the
+// first k block also writes the tile's factors 2^e into the table.
+__global__ void __launch_bounds__(64) encode_f16_finish_kernel(__half* __restrict__ out, int K, int64_t out_stride,
+                                                              float* __restrict__ table, int64_t table_stride) {
+  const int kb = blockIdx.x, nt = blockIdx.y, t = threadIdx.x;
+  out += static_cast<int64_t>(blockIdx.z) * out_stride;
+  float* const tb = table + static_cast<int64_t>(blockIdx.z) * table_stride + static_cast<int64_t>(nt) * 8;
+  __half* const rows_tile = out + static_cast<int64_t>(nt) * 8 * K;
+  const int c = min(64, K - kb * 64);
+  float a1 = 0.f, a2 = 0.f, a3 = 0.f;
+  if (t < c) {
+    a1 = *f16_stage_slot(rows_tile, K, kb, c, 0, t);
+    a2 = *f16_stage_slot(rows_tile, K, kb, c, 1, t);
+    a3 = *f16_stage_slot(rows_tile, K, kb, c, 2, t);
+  }
+  __syncthreads();  // every staged sum read before any row overwrites it
+  const int e1 = f16_chk_exponent(__float_as_uint(tb[0]));
+  const int e2 = f16_chk_exponent(__float_as_uint(tb[1]));
+  const int e3 = f16_chk_exponent(__float_as_uint(tb[2]));
+  if (kb == 0 && t == 0) {
+    tb[4] = pow2f_exact(e1);
+    tb[5] = pow2f_exact(e2);
+    tb[6] = pow2f_exact(e3);
+  }
+  if (t < c)
+    write_checksum_rows_f16(a1 * pow2f_exact(-e1), a2 * pow2f_exact(-e2), a3 * pow2f_exact(-e3),
+                            rows_tile + kb * 64 + t, K);
 }
 
 // K-major copy of an N-major right operand plus (out != nullptr) its
