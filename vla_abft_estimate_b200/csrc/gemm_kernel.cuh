@@ -317,6 +317,40 @@ __device__ __forceinline__ void mbar_wait_unwind(uint64_t* bar, uint32_t parity)
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
+// Row checksums of the first NV (even) columns of a 32-column chunk whose
+// first local column is base (a multiple of 32): s1 += sum x, s2 +=
+// sum (base + e + 1) x[e], s3 += sum sg(base + e) x[e], amax = max |x|.
+// The Thue-Morse sign of base + e is sg(base) * sg(e) (base has its low 5
+// bits clear), and columns e, e + 1 (e even) always have opposite signs, so
+// each pair goes with one packed add into the accumulator of its sign
+// (sg(e) = +1: pp, -1: pn); the plain and the signed sums both follow from
+// those two, and one packed FMA forms the weighted sum: three checksums for
+// about one instruction per element.
+template <int NV>
+__device__ __forceinline__ void chunk_checksums(const float (&x)[32], int base, float& s1, float& s2, float& s3,
+                                                float& amax) {
+  static_assert(NV % 2 == 0 && NV <= 32, "pairs of columns");
+  float2 pp = make_float2(0.f, 0.f), pn = make_float2(0.f, 0.f), pw = make_float2(0.f, 0.f);
+  float m0 = 0.f, m1 = 0.f;
+#pragma unroll
+  for (int e = 0; e < NV; e += 2) {
+    const float2 xx = make_float2(x[e], x[e + 1]);
+    if (__builtin_popcount(e) & 1)
+      pn = __fadd2_rn(pn, xx);
+    else
+      pp = __fadd2_rn(pp, xx);
+    pw = __ffma2_rn(make_float2(static_cast<float>(e), static_cast<float>(e + 1)), xx, pw);
+    m0 = fmaxf(m0, fabsf(xx.x));
+    m1 = fmaxf(m1, fabsf(xx.y));
+  }
+  const float a = (pp.x + pp.y) + (pn.x + pn.y);
+  const float t = (pp.x - pp.y) - (pn.x - pn.y);
+  amax = fmaxf(amax, fmaxf(m0, m1));
+  s1 += a;
+  s2 += fmaf(static_cast<float>(base + 1), a, pw.x + pw.y);
+  s3 += (__popc(base) & 1) ? -t : t;
+}
+
 // The operand / output element type of a kernel instance: bf16 (F16 =
 // false) or fp16. Both use kind::f16 MMAs with fp32 accumulation; one MMA
 // takes one type for A and B, so the checksum rows have the operands' type.
@@ -1038,35 +1072,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int e = 0; e < 32; ++e) x[e] += inj_add(base + e);
         }
         if constexpr (CHECK) {
-          if (base + 32 <= ncols) {
-            // Whole chunk valid: the column weights split into the chunk's
-            // base plus a compile-time offset, and the Thue-Morse sign of
-            // base + e is sg(base) * sg(e) (base has its low 5 bits clear).
-            // Columns e, e + 1 (e even) always have opposite signs, so each
-            // pair goes with one packed add into the accumulator of its sign
-            // (sg(e) = +1: pp, -1: pn); the plain and the signed sums both
-            // follow from those two, and one packed FMA forms the weighted
-            // sum: three checksums for about one instruction per element.
-            float2 pp = make_float2(0.f, 0.f), pn = make_float2(0.f, 0.f), pw = make_float2(0.f, 0.f);
-            float m0 = 0.f, m1 = 0.f;
-#pragma unroll
-            for (int e = 0; e < 32; e += 2) {
-              const float2 xx = make_float2(x[e], x[e + 1]);
-              if (__builtin_popcount(e) & 1)
-                pn = __fadd2_rn(pn, xx);
-              else
-                pp = __fadd2_rn(pp, xx);
-              pw = __ffma2_rn(make_float2(static_cast<float>(e), static_cast<float>(e + 1)), xx, pw);
-              m0 = fmaxf(m0, fabsf(xx.x));
-              m1 = fmaxf(m1, fabsf(xx.y));
-            }
-            const float a = (pp.x + pp.y) + (pn.x + pn.y);
-            const float t = (pp.x - pp.y) - (pn.x - pn.y);
-            amax = fmaxf(amax, fmaxf(m0, m1));
-            s1 += a;
-            s2 += fmaf(static_cast<float>(base + 1), a, pw.x + pw.y);
-            s3 += (__popc(base) & 1) ? -t : t;
-          } else {
+          if (base + 32 <= ncols)
+            chunk_checksums<32>(x, base, s1, s2, s3, amax);
+          else if (base + 24 == ncols)  // the chunk of a full tile that holds its 8 checksum columns
+            chunk_checksums<24>(x, base, s1, s2, s3, amax);
+          else {
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
               const int col = base + e;
