@@ -31,6 +31,7 @@ from __future__ import annotations
 
 import argparse
 import datetime
+import functools
 import json
 import math
 import os
@@ -946,9 +947,7 @@ def tile_grid(args):
     dev = torch.device("cuda", 0)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     iters = max(min(args.steps, 50), 5)
-
-    def timed(fn):
-        return timed_median(fn, iters, flush) * 1e3
+    shapes = ((128, 128), (256, 128), (128, 256), (256, 256))  # (tile_n, tile_m)
 
     for name, m, n, k in TILE_GRID_SHAPES:
         a = (torch.randn(m, k, device=dev) * k ** -0.5).bfloat16()
@@ -959,12 +958,12 @@ def tile_grid(args):
         for mode, tag in ((N.MODE_OFF, "off"), (N.MODE_DETECT | N.MODE_CORRECT, "checked")):
             tn = ops.pick_tile_n(m, n, k, dev, mode)
             tm = ops.pick_tile_m(m, n, k, tn, dev, mode)
-            us = {}
-            for ctn, ctm in ((128, 128), (256, 128), (128, 256), (256, 256)):
-                cks = ops.encode_weight(w, ctn) if mode else None
-                us[f"{ctm}x{ctn}"] = round(timed(lambda: ops.abft_gemm(
-                    a, w, mode=mode, out=out, tile_n=ctn, tile_m=ctm, swap_ab=1, checksums=cks,
-                    report=rep if mode else None)), 2)
+            # the tile shapes interleaved round by round: each sees the same clocks
+            cks = {ctn: (ops.encode_weight(w, ctn) if mode else None) for ctn in (128, 256)}
+            fns = [functools.partial(ops.abft_gemm, a, w, mode=mode, out=out, tile_n=ctn, tile_m=ctm, swap_ab=1,
+                                     checksums=cks[ctn], report=rep if mode else None) for ctn, ctm in shapes]
+            ts = timed_medians_interleaved(fns, iters, flush)
+            us = {f"{ctm}x{ctn}": round(t * 1e3, 2) for (ctn, ctm), t in zip(shapes, ts)}
             best = min(us, key=us.get)
             pick = f"{tm}x{tn}"  # tile rows x columns
             row[tag] = {"us": us, "pick": pick, "best": best, "pick_loss_pct": round(100 * (us[pick] / us[best] - 1), 1)}

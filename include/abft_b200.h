@@ -206,13 +206,13 @@ size_t abft_report_bytes_batched(int32_t capacity, int32_t batch);
 /* Tile width (256 or 128) the library picks for an M x N x K GEMM in `mode`
  * when tile_n == 0: the shorter estimated time over num_sms (whole-tile
  * waves, with stream-K for a last wave that would leave SMs idle; a 128-wide
- * tile's k-block counted as 0.6 of a 256-wide one; for 256-wide tiles the
+ * tile's k-block counted as 0.7 of a 256-wide one; for 256-wide tiles the
  * better of 128-row tiles and CTA pairs). */
 int32_t abft_pick_tile_n(int64_t M, int64_t N, int64_t K, int32_t num_sms, uint32_t mode);
 
 /* Tile height (128, or 256 = CTA pairs) the library picks when tile_m == 0,
  * for a given tile_n: the shorter estimated schedule, pairs over num_sms / 2
- * units at a per-SM speed-up of 1.1 (128 whenever tile_n != 256: pairs of
+ * units at a per-SM speed-up of 1.15 (128 whenever tile_n != 256: pairs of
  * 128-wide tiles run only on request). */
 int32_t abft_pick_tile_m(int64_t M, int64_t N, int64_t K, int32_t num_sms, uint32_t mode, int32_t tile_n);
 

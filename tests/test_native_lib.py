@@ -42,7 +42,10 @@ def test_host_only_helpers():
     assert L.abft_report_bytes(10) == 64 + 10 * 24
     assert L.abft_report_bytes_batched(10, 1) == 64 + 10 * 24
     assert L.abft_report_bytes_batched(10, 32) == 64 + 10 * 24 + 32 * 16  # counters after the records
-    assert L.abft_pick_tile_n(512, 4096, 4096, 148, 3) == 128  # 140 narrow tiles: one wave, no partials
+    # 34 pair tiles with stream-K beat 140 narrow tiles in one wave (bench.py --tile-grid: 34.9 vs 38.9 us)
+    assert L.abft_pick_tile_n(512, 4096, 4096, 148, 3) == 256
+    assert L.abft_pick_tile_m(512, 4096, 4096, 148, 3, 256) == 256
+    assert L.abft_pick_tile_n(256, 4096, 1024, 148, 3) == 128  # ViT-L MLP: narrow tiles stay faster
     assert L.abft_pick_tile_m(512, 4608, 3584, 148, 3, 256) == 256  # 38 pair tiles beat 39 x 4 narrow ones
     assert L.abft_pick_tile_m(8192, 8192, 8192, 148, 3, 256) == 256
     assert L.abft_pick_tile_m(1024, 1024, 1024, 148, 3, 128) == 128  # 128-wide pairs run only on request

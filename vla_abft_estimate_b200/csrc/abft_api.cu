@@ -342,15 +342,16 @@ float unit_roundoff(int dtype) {
 // Measured in microseconds; one k-block step of a 256-wide tile takes about
 // kKbUs256 (kKbFrac128 of that for a 128-wide tile). The constants rank the
 // candidate schedules; they do not predict absolute times (the epilogue of
-// the last wave and the launch are left out), and over the Qwen2-7B,
-// ViT/Llama and square shapes the pick measured within 3% of the best tile
-// shape (bench.py --tile-grid).
+// the last wave and the launch are left out). Fitted to bench.py
+// --tile-grid (all four tile shapes interleaved, 14 GEMM shapes, checks off
+// and on): the pick is the fastest tile shape or within 3.2% of it (one
+// timer step) on every shape.
 constexpr double kSkStoreUs = 3.0;
 constexpr double kSkFoldUs = 1.0;
 constexpr double kKbUs256 = 0.33;
 // A 128-wide tile's k-block takes this fraction of a 256-wide one: half the
 // MMA work, but the same A slice streams from shared memory.
-constexpr double kKbFrac128 = 0.6;
+constexpr double kKbFrac128 = 0.7;
 
 double kb_us(int bn) { return bn == 256 ? kKbUs256 : kKbUs256 * kKbFrac128; }
 
@@ -422,7 +423,7 @@ Schedule schedule_for(int64_t M, int64_t N, int64_t K, int tile_m, int bn, int b
 // CTAs (0.32 against 0.31 us, bench.py --tile-grid) and leave half the
 // units: they are available on request (tile_m 256, tile_n 128) but never
 // picked.
-constexpr double kPairSpeedup = 1.10;
+constexpr double kPairSpeedup = 1.15;
 
 // Estimated time (microseconds) of an M x N x K launch with tile_m x bn
 // tiles (tile_m 256: CTA pairs over `units` pairs).
