@@ -62,6 +62,8 @@ def parse_args():
     ap.add_argument("--sweep", action="store_true",
                     help="one JSON line per shape of the square sweep, the 512x4096x4096 case and the "
                          "Qwen2-7B layer GEMMs: checked / unchecked TFLOP/s and 1- and 4-fault outcomes")
+    ap.add_argument("--dtype", choices=["bf16", "f16"], default="bf16",
+                    help="operand type of --model qwen2-7b (the reference driver's --dtype)")
     ap.add_argument("--bmm-sweep", action="store_true",
                     help="batched products (torch.bmm, attention-shaped): cuBLAS vs the fused kernel vs the "
                          "reference's per-batch check loop")
@@ -408,7 +410,7 @@ def gemm_point(m, n, k, iters, flush, seed=0, dtype="bf16"):
     return res
 
 
-def qwen_prefill_point(reps, warmup, decode_steps=0, cpu_seconds=0.0):
+def qwen_prefill_point(reps, warmup, decode_steps=0, cpu_seconds=0.0, dtype="bf16"):
     """a Qwen2-7B-shaped decoder prefill of 512 tokens
     (batch 1, random init N(0, 0.02), random token ids) with every nn.Linear
     through AbftInjector's fused path (reports deferred to one read per
@@ -418,7 +420,8 @@ def qwen_prefill_point(reps, warmup, decode_steps=0, cpu_seconds=0.0):
     ahead behind a device sleep. Then one forward with the injector's
     random faults (probability 0.05 per linear, +1.0 on the fp32
     accumulator) and, with ``decode_steps``, single-token decode steps after
-    the prefill."""
+    the prefill. ``dtype`` "f16" builds the model in fp16 (the reference
+    driver's --dtype float16)."""
     import contextlib
 
     import torch
@@ -428,7 +431,7 @@ def qwen_prefill_point(reps, warmup, decode_steps=0, cpu_seconds=0.0):
     cfg = QWEN2_7B
     tokens = 512
     dev = torch.device("cuda", 0)
-    model = build_qwen2(cfg, dev)
+    model = build_qwen2(cfg, dev, dtype=torch.float16 if dtype == "f16" else torch.bfloat16)
     ids = torch.randint(0, cfg["vocab"], (tokens,), device=dev, generator=torch.Generator(device=dev).manual_seed(7))
 
     def timed_forward(ctx_factory):
@@ -1135,13 +1138,14 @@ def run_model(args):
     torch.cuda.set_device(0)
     reps = max(args.steps, 3) if args.steps < 300 else 10
     warmup = max(args.warmup, 2)
-    res = qwen_prefill_point(reps, warmup, decode_steps=32, cpu_seconds=0.0 if args.no_cpu_baseline else 20.0)
+    res = qwen_prefill_point(reps, warmup, decode_steps=32, cpu_seconds=0.0 if args.no_cpu_baseline else 20.0,
+                             dtype=args.dtype)
     cfg = QWEN2_7B
     line = {
         "metric": "Qwen2-7B prefill-512 tokens/s (every linear ABFT-protected)",
         "value": res["tokens_per_s"]["abft"], "unit": "tokens/s", "n_gpus": 1, "steps": reps,
         "warmup": warmup, "ms_per_step": res["ms"]["abft"], "higher_is_better": True, "scaling": "none",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random init N(0,0.02), random token ids)",
+        "vs_baseline": None, "dtype": args.dtype, "data": "synthetic (random init N(0,0.02), random token ids)",
         "config": {"workload": "Qwen2-7B-shaped decoder prefill, batch 1, 512 tokens", **cfg,
                    "fused_shapes": "qkv 3584->4608 (bias), o 3584->3584, gate_up 3584->37888, down 18944->3584, "
                                    "lm_head 3584->152064",

@@ -124,11 +124,13 @@ def check_clean_and_faults(model_fn, calls, prob, magnitude, want_narrow=False):
     assert rel_err(out_f, out) <= OUT_TOL
 
 
-def test_qwen2_prefill_clean_and_reference_rng_faults(cuda_device):
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_qwen2_prefill_clean_and_reference_rng_faults(cuda_device, dtype):
     """Config 3 at 2 of its 28 layers (every layer GEMM and the lm_head at
-    their real shapes, 512 tokens)."""
+    their real shapes, 512 tokens), in bf16 and in fp16 (the reference
+    driver's --dtype float16: the fused kernel runs on fp16 operands)."""
     cfg = qwen_cfg(2)
-    model = W.build_qwen2(cfg, cuda_device)
+    model = W.build_qwen2(cfg, cuda_device, dtype=dtype)
     ids = torch.randint(0, cfg["vocab"], (512,), device=cuda_device,
                         generator=torch.Generator(device=cuda_device).manual_seed(7))
     calls = []

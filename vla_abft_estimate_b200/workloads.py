@@ -25,10 +25,12 @@ QWEN2_7B = dict(hidden=3584, inter=18944, layers=28, heads=28, kv_heads=4, head_
                 rope_theta=1000000.0, eps=1e-6)
 
 
-def build_qwen2(cfg, device, seed=0):
+def build_qwen2(cfg, device, seed=0, dtype=None):
     """Qwen2-style decoder: RMSNorm, fused QKV (with bias) + RoPE + GQA
     attention (SDPA), SwiGLU MLP with fused gate+up, tied-free lm_head.
-    Every projection is an nn.Linear, so F.linear hooks see all of them."""
+    Every projection is an nn.Linear, so F.linear hooks see all of them.
+    ``dtype``: bfloat16 (default) or float16, the reference driver's
+    ``--dtype`` (qwen_abft_benchmark.py:26)."""
     import torch
     import torch.nn as nn
     import torch.nn.functional as F
@@ -86,19 +88,20 @@ def build_qwen2(cfg, device, seed=0):
             inv = 1.0 / (cfg["rope_theta"] ** (torch.arange(0, hd, 2, device=ids.device).float() / hd))
             ang = torch.outer(torch.arange(pos, pos + t, device=ids.device).float(), inv)
             ang = torch.cat((ang, ang), dim=-1)[:, None, :]
-            cos, sin = ang.cos().to(torch.bfloat16), ang.sin().to(torch.bfloat16)
+            cos, sin = ang.cos().to(dt), ang.sin().to(dt)
             x = self.embed(ids)
             for i, layer in enumerate(self.layers):
                 x = layer(x, cos, sin, None if caches is None else caches[i], pos)
             return self.lm_head(self.norm(x))
 
         def new_caches(self, t_max):
-            return [torch.zeros(2, cfg["kv_heads"], t_max, cfg["head_dim"], dtype=torch.bfloat16,
+            return [torch.zeros(2, cfg["kv_heads"], t_max, cfg["head_dim"], dtype=dt,
                                 device=self.embed.weight.device) for _ in range(cfg["layers"])]
 
+    dt = torch.bfloat16 if dtype is None else dtype
     torch.manual_seed(seed)
     with torch.device(device):
-        model = Model().to(torch.bfloat16)
+        model = Model().to(dt)
     with torch.no_grad():
         for mod in model.modules():
             if isinstance(mod, (nn.Linear, nn.Embedding)):
