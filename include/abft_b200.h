@@ -257,7 +257,8 @@ size_t abft_checksum_bytes_typed(int64_t N, int64_t K, int32_t tile_n, int32_t d
  * finite; e within [-100, 100]); the rows hold the fp16 terms of v * 2^-e
  * (three for v1 and v2, two for v3, as above) and table entries 8t+4..6 the
  * factors 2^e, which the fused check multiplies back (exact). Entries
- * 8t+0..2 hold the largest |v1|, |v2|, |v3|; 8t+3 and 8t+7 are 0. */
+ * 8t+0..2 hold the largest |v1|, |v2|, |v3| (NaN sums passed over); 8t+3
+ * and 8t+7 are 0. One launch (an 8-CTA cluster per tile and batch). */
 int abft_encode_weight_typed(const void* B, int64_t N, int64_t K, int64_t ldb, int64_t stride_b,
                              int32_t batch, int32_t tile_n, int32_t dtype, void* out, void* stream);
 

@@ -272,14 +272,16 @@ def encode_weight_f16_block(w: np.ndarray, tile_n: int) -> bytes:
     output tiles of ``tile_n`` data columns: per tile 8 rows of K halves
     (v1 and v2 each as three fp16 terms, v3 as two, each checksum scaled by
     2^-e), then a table of 8 float32 per tile: [max|v1|, max|v2|, max|v3|,
-    0, 2^e1, 2^e2, 2^e3, 0]."""
+    0, 2^e1, 2^e2, 2^e3, 0] (maxima over the non-NaN sums)."""
     v = encode_weight_f32_order(w, tile_n)
     tiles, k = v[0].shape
     rows = np.zeros((tiles, 8, k), dtype=np.float16)
     table = np.zeros((tiles, 8), dtype=np.float32)
     for t in range(tiles):
         for q in range(3):
-            m = np.float32(np.abs(v[q][t]).max())
+            mags = np.abs(v[q][t])
+            mags = mags[~np.isnan(mags)]  # NaN sums are passed over, as fmaxf does
+            m = np.float32(mags.max() if mags.size else 0.0)
             e = f16_checksum_exponent(m)
             x = (v[q][t] * np.float32(2.0 ** -e)).astype(np.float32)
             hi = x.astype(np.float16)

@@ -43,7 +43,7 @@ def max_rel_err(got, ref):
 # ------------------------------------------------------------------ encode
 @pytest.mark.parametrize("tile_n", [128, 256])
 @pytest.mark.parametrize("n,k,w_scale", [(300, 200, 1.0), (1024, 512, 1.0), (136, 72, 1.0), (496, 256, 3e4),
-                                         (300, 64, 1e-3)])
+                                         (300, 64, 1e-3), (4096, 4104, 1.0)])  # the last: the many-CTA path
 def test_encode_block_bit_identical_to_oracle(cuda_device, tile_n, n, k, w_scale):
     _, w, _ = seeded(8, n, k, 1, w_scale=w_scale)
     blk = ops.encode_weight(w.to(cuda_device), tile_n)
@@ -52,6 +52,23 @@ def test_encode_block_bit_identical_to_oracle(cuda_device, tile_n, n, k, w_scale
     got = blk.cpu().numpy()
     assert got.shape == want.shape
     assert np.array_equal(got, want)
+
+
+def test_encode_passes_over_nan_sums(cuda_device):
+    """A NaN weight makes its k column's sums NaN; the tile's scales come
+    from the other columns (as the oracle's restatement has it)."""
+    n, k = 300, 136
+    _, w, _ = seeded(8, n, k, 12)
+    w[5, 70] = float("nan")
+    blk = ops.encode_weight(w.to(cuda_device), 128).cpu().numpy()
+    want = np.frombuffer(O.encode_weight_f16_block(f32(w), 120), dtype=np.uint8)
+    tiles = -(-n // 120)
+    rows_b = tiles * 8 * k * 2
+    got_rows = blk[:rows_b].view(np.float16)
+    want_rows = want[:rows_b].view(np.float16)
+    assert np.array_equal(got_rows, want_rows, equal_nan=True)
+    assert np.isnan(got_rows.reshape(tiles, 8, k)[0, :, 70]).all()
+    assert np.array_equal(blk[rows_b:], want[rows_b:])
 
 
 def test_encode_batched_blocks_and_cached_checksums(cuda_device):
@@ -66,7 +83,8 @@ def test_encode_batched_blocks_and_cached_checksums(cuda_device):
     c1, r1 = ops.abft_gemm(ad, wd, tile_n=256, checksums=cks, inject=inj)
     c2, r2 = ops.abft_gemm(ad, wd, tile_n=256, inject=inj)
     assert torch.equal(c1, c2)
-    assert r1.read().records == r2.read().records
+    key = lambda x: (x.row, x.col)  # noqa: E731  (records land in atomic-slot order)
+    assert sorted(r1.read().records, key=key) == sorted(r2.read().records, key=key)
     with pytest.raises(ValueError):
         ops.abft_gemm(ad, wd, tile_n=256, checksums=cks.view(torch.float16))
 

@@ -701,6 +701,12 @@ int launch_gemm_typed(const Plan& ws, bool check, int dev, const CUtensorMap& tm
                : launch_gemm<128, false, false, F16>(dev, 3, tmA, tmB, tmB2, tmV, tmBt, tmC, p, grid, s);
 }
 
+// fp16 encodes with at most this many (k-block, tile, batch) triples run as
+// one cluster launch; larger ones as memset + two launches of a CTA each
+// (the cluster kernel's CTAs walk kEncCluster times fewer k-blocks in
+// parallel: 132 against 59 us for an 8192^2 weight).
+constexpr int64_t kEncOneLaunchCtas = 1024;
+
 // Rows part of one batch's checksum block, then (fp16) its scale table of
 // 8 floats per tile.
 size_t checksum_rows_bytes(int64_t N, int64_t K, int32_t tile_n) {
@@ -770,29 +776,47 @@ int abft_encode_weight_typed(const void* B, int64_t N, int64_t K, int64_t ldb, i
   const int num_kb = static_cast<int>(cdiv(K, kBK));
   const int64_t tiles = cdiv(N, bd);
   const size_t bytes = abft_checksum_bytes_typed(N, K, tile_n, dtype);  // one batch's block
-  dim3 g(static_cast<unsigned>(num_kb), static_cast<unsigned>(tiles), static_cast<unsigned>(batch));
   if (dtype == ABFT_DTYPE_BF16) {
-    encode_weight_kernel<__nv_bfloat16, 0><<<g, 256, 0, s>>>(
-        static_cast<const __nv_bfloat16*>(B), ldb, static_cast<int>(N), static_cast<int>(K), bd,
-        static_cast<__nv_bfloat16*>(out), stride_b, static_cast<int64_t>(bytes / 2), nullptr, 0);
+    dim3 g(static_cast<unsigned>(num_kb), static_cast<unsigned>(tiles), static_cast<unsigned>(batch));
+    encode_weight_kernel<<<g, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(B), ldb, static_cast<int>(N),
+                                           static_cast<int>(K), bd, static_cast<__nv_bfloat16*>(out), stride_b,
+                                           static_cast<int64_t>(bytes / 2));
     return launch_status();
   }
-  // fp16: zero the scale tables (one row of tiles * 8 floats per batch),
-  // form the sums (staged in the rows' own bytes) and each tile's largest
-  // magnitudes, then write the scaled rows.
   float* table = reinterpret_cast<float*>(static_cast<uint8_t*>(out) + checksum_rows_bytes(N, K, tile_n));
-  if (cudaMemset2DAsync(table, bytes, 0, static_cast<size_t>(tiles) * 8 * sizeof(float), static_cast<size_t>(batch),
-                        s) != cudaSuccess)
-    return launch_status(), ABFT_ERR_CUDA;
   const __half* Bh = static_cast<const __half*>(B);
   __half* oh = static_cast<__half*>(out);
-  encode_weight_kernel<__half, 1><<<g, 256, 0, s>>>(Bh, ldb, static_cast<int>(N), static_cast<int>(K), bd, oh,
-                                                    stride_b, static_cast<int64_t>(bytes / 2), table,
-                                                    static_cast<int64_t>(bytes / 4));
-  rc = launch_status();
-  if (rc != ABFT_OK) return rc;
-  encode_f16_finish_kernel<<<g, 64, 0, s>>>(oh, static_cast<int>(K), static_cast<int64_t>(bytes / 2), table,
-                                             static_cast<int64_t>(bytes / 4));
+  if (static_cast<int64_t>(num_kb) * tiles * batch > kEncOneLaunchCtas) {
+    // Large: a CTA per k-block of each tile; the tables are zeroed first
+    // (one row of tiles * 8 floats per batch).
+    if (cudaMemset2DAsync(table, bytes, 0, static_cast<size_t>(tiles) * 8 * sizeof(float),
+                          static_cast<size_t>(batch), s) != cudaSuccess)
+      return launch_status(), ABFT_ERR_CUDA;
+    dim3 g(static_cast<unsigned>(num_kb), static_cast<unsigned>(tiles), static_cast<unsigned>(batch));
+    encode_f16_sums_kernel<<<g, 256, 0, s>>>(Bh, ldb, static_cast<int>(N), static_cast<int>(K), bd, oh, stride_b,
+                                             static_cast<int64_t>(bytes / 2), table, static_cast<int64_t>(bytes / 4));
+    rc = launch_status();
+    if (rc != ABFT_OK) return rc;
+    encode_f16_finish_kernel<<<g, 64, 0, s>>>(oh, static_cast<int>(K), static_cast<int64_t>(bytes / 2), table,
+                                               static_cast<int64_t>(bytes / 4));
+    return launch_status();
+  }
+  // Small: one cluster of kEncCluster CTAs per tile and batch forms the
+  // sums, agrees on the tile's scales and writes the rows and the table.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(tiles * kEncCluster), static_cast<unsigned>(batch));
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cudaLaunchAttribute at;
+  at.id = cudaLaunchAttributeClusterDimension;
+  at.val.clusterDim.x = kEncCluster;
+  at.val.clusterDim.y = 1;
+  at.val.clusterDim.z = 1;
+  cfg.attrs = &at;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, encode_f16_cluster_kernel, Bh, ldb, static_cast<int>(N), static_cast<int>(K), bd, oh,
+                         stride_b, static_cast<int64_t>(bytes / 2), table, static_cast<int64_t>(bytes / 4)) != cudaSuccess)
+    return launch_status(), ABFT_ERR_CUDA;
   return launch_status();
 }
 

@@ -24,6 +24,7 @@
 #include <cuda_fp16.h>
 
 #include "../../include/abft_b200.h"
+#include "ptx.cuh"
 
 namespace abft {
 
@@ -101,12 +102,10 @@ __host__ __device__ __forceinline__ float col_sign(int j) { return (__builtin_po
 // fp16 does not (largest finite 65504): each of v1, v2, v3 of a tile is
 // scaled by 2^-e, e chosen so that its largest |value| over k lands in
 // [2^14, 2^15), before the split; the scale table after the rows holds
-// 8 floats per tile, [0..2] the largest |v1|, |v2|, |v3| (pass 1, an atomic
-// max on the bit patterns of non-negative floats, zeroed beforehand) and
-// [4..6] the factors 2^e (pass 2). Multiplying by a power of two is exact,
-// so the check MMA's sums times 2^e equal the unscaled ones. Pass 1 leaves
-// its fp32 sums in the rows it will own (f16_stage_slot), so pass 2 reads
-// 12 bytes per column instead of the weight again.
+// 8 floats per tile, [0..2] the largest |v1|, |v2|, |v3| (NaN sums are
+// passed over, as fmaxf does) and [4..6] the factors 2^e. Multiplying by a
+// power of two is exact, so the check MMA's sums times 2^e equal the
+// unscaled ones.
 // grid (ceil(K/64), tiles_n, batch), 256 threads. K % 8 == 0. Batch z reads
 // B + z * b_stride, writes out + z * out_stride and table + z * table_stride.
 __device__ __forceinline__ void write_checksum_rows(float a1, float a2, float a3, __nv_bfloat16* o, int K) {
@@ -165,12 +164,13 @@ __device__ __forceinline__ void unpack8_as(const uint4 w, float (&x)[8], const _
   }
 }
 
-// Where pass 1 of an fp16 encode keeps sum q (0..2) of k column kb*64 + t:
-// inside the bytes the block's final rows occupy (8 rows x c columns x 2
-// bytes, c = the block's valid columns, a multiple of 8), read as 8
-// segments of 2c bytes; the 3c floats fill the first 12c of those 16c
-// bytes. No other block writes there, so pass 2 may read them and then
-// overwrite them with the rows. rows_tile: the tile's first checksum row.
+// Where the fp16 encode keeps sum q (0..2) of k column kb*64 + t until the
+// tile's scale is known: inside the bytes that k-block's final rows occupy
+// (8 rows x c columns x 2 bytes, c = its valid columns, a multiple of 8),
+// read as 8 segments of 2c bytes; the 3c floats fill the first 12c of
+// those 16c bytes. Only the CTA that handles the k-block touches them, so
+// it may read them back and then overwrite them with the rows.
+// rows_tile: the tile's first checksum row.
 __device__ __forceinline__ float* f16_stage_slot(__half* rows_tile, int K, int kb, int c, int q, int t) {
   const int f = q * c + t;
   const int seg = (2 * f) / c;           // (4 f) / (2 c): row of the segment, < 6
@@ -179,17 +179,12 @@ __device__ __forceinline__ float* f16_stage_slot(__half* rows_tile, int K, int k
                                   off);
 }
 
-// PASS 0: bf16 rows. PASS 1 (fp16): sums staged in place (f16_stage_slot)
-// and the largest magnitudes into the table; encode_f16_finish_kernel then
-// writes the scaled rows.
-template <typename T, int PASS>
-__global__ void __launch_bounds__(256) encode_weight_kernel(const T* __restrict__ B, int64_t ldb, int N, int K, int bd,
-                                                            T* __restrict__ out, int64_t b_stride, int64_t out_stride,
-                                                            float* __restrict__ table, int64_t table_stride) {
-  __shared__ float red[3][32][65];
-  B += static_cast<int64_t>(blockIdx.z) * b_stride;
-  out += static_cast<int64_t>(blockIdx.z) * out_stride;
-  const int kb = blockIdx.x, nt = blockIdx.y;
+// The three checksums of k columns [kb*64, kb*64 + 64) of tile nt, for
+// thread t < 64 (column kb*64 + t; zero past K). 256 threads; starts with a
+// block barrier, so that a caller may loop over k-blocks reusing `red`.
+template <typename T>
+__device__ __forceinline__ void kblock_checksums(const T* __restrict__ B, int64_t ldb, int N, int K, int bd, int nt,
+                                                 int kb, float (&red)[3][32][65], float& a1, float& a2, float& a3) {
   const int t = threadIdx.x, c8 = t & 7, rg = t >> 3;
   const int k0 = kb * 64 + c8 * 8;
   float s1[8], s2[8], s3[8];
@@ -225,6 +220,7 @@ __global__ void __launch_bounds__(256) encode_weight_kernel(const T* __restrict_
       }
     }
   }
+  __syncthreads();  // the previous k-block's reads of red are done
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
     red[0][rg][c8 * 8 + e] = s1[e];
@@ -232,47 +228,74 @@ __global__ void __launch_bounds__(256) encode_weight_kernel(const T* __restrict_
     red[2][rg][c8 * 8 + e] = s3[e];
   }
   __syncthreads();
-  if (t >= 64) return;
-  const int col = kb * 64 + t;
-  float a1 = 0.f, a2 = 0.f, a3 = 0.f;
-  if (col < K) {
+  a1 = a2 = a3 = 0.f;
+  if (t < 64 && kb * 64 + t < K) {
     for (int g = 0; g < 32; ++g) {
       a1 += red[0][g][t];
       a2 += red[1][g][t];
       a3 += red[2][g][t];
     }
   }
-  if constexpr (PASS == 0) {
-    if (col < K) write_checksum_rows(a1, a2, a3, out + static_cast<int64_t>(nt) * 8 * K + col, K);
-  } else {
-    float* const tb = table + static_cast<int64_t>(blockIdx.z) * table_stride + static_cast<int64_t>(nt) * 8;
-    {
-      float m1 = fabsf(a1), m2 = fabsf(a2), m3 = fabsf(a3);
+}
+
+// bf16 checksum block: one k-block of one tile per CTA.
+__global__ void __launch_bounds__(256) encode_weight_kernel(const __nv_bfloat16* __restrict__ B, int64_t ldb, int N,
+                                                            int K, int bd, __nv_bfloat16* __restrict__ out,
+                                                            int64_t b_stride, int64_t out_stride) {
+  __shared__ float red[3][32][65];
+  B += static_cast<int64_t>(blockIdx.z) * b_stride;
+  out += static_cast<int64_t>(blockIdx.z) * out_stride;
+  const int kb = blockIdx.x, nt = blockIdx.y, t = threadIdx.x;
+  float a1, a2, a3;
+  kblock_checksums(B, ldb, N, K, bd, nt, kb, red, a1, a2, a3);
+  const int col = kb * 64 + t;
+  if (t < 64 && col < K) write_checksum_rows(a1, a2, a3, out + static_cast<int64_t>(nt) * 8 * K + col, K);
+}
+
+// fp16 checksum block of a large weight, in two launches after the table
+// is zeroed: encode_f16_sums_kernel (one k-block of one tile per CTA) keeps
+// the sums in the rows' own bytes and raises the tile's maxima with an
+// atomic max on the bit patterns of non-negative floats (NaN sums passed
+// over); encode_f16_finish_kernel writes the scaled rows and the factors.
+__global__ void __launch_bounds__(256) encode_f16_sums_kernel(const __half* __restrict__ B, int64_t ldb, int N, int K,
+                                                              int bd, __half* __restrict__ out, int64_t b_stride,
+                                                              int64_t out_stride, float* __restrict__ table,
+                                                              int64_t table_stride) {
+  __shared__ float red[3][32][65];
+  B += static_cast<int64_t>(blockIdx.z) * b_stride;
+  out += static_cast<int64_t>(blockIdx.z) * out_stride;
+  const int kb = blockIdx.x, nt = blockIdx.y, t = threadIdx.x;
+  float a1, a2, a3;
+  kblock_checksums(B, ldb, N, K, bd, nt, kb, red, a1, a2, a3);
+  if (t >= 64) return;  // whole warps
+  const int c = min(64, K - kb * 64);
+  float m1 = 0.f, m2 = 0.f, m3 = 0.f;
+  if (t < c) {
+    __half* const rows_tile = out + static_cast<int64_t>(nt) * 8 * K;
+    *f16_stage_slot(rows_tile, K, kb, c, 0, t) = a1;
+    *f16_stage_slot(rows_tile, K, kb, c, 1, t) = a2;
+    *f16_stage_slot(rows_tile, K, kb, c, 2, t) = a3;
+    m1 = fmaxf(m1, fabsf(a1));
+    m2 = fmaxf(m2, fabsf(a2));
+    m3 = fmaxf(m3, fabsf(a3));
+  }
 #pragma unroll
-      for (int d = 16; d > 0; d >>= 1) {
-        m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, d));
-        m2 = fmaxf(m2, __shfl_xor_sync(0xffffffffu, m2, d));
-        m3 = fmaxf(m3, __shfl_xor_sync(0xffffffffu, m3, d));
-      }
-      if ((t & 31) == 0) {
-        atomicMax(reinterpret_cast<unsigned int*>(tb + 0), __float_as_uint(m1));
-        atomicMax(reinterpret_cast<unsigned int*>(tb + 1), __float_as_uint(m2));
-        atomicMax(reinterpret_cast<unsigned int*>(tb + 2), __float_as_uint(m3));
-      }
-      if (col < K) {
-        __half* const rows_tile = reinterpret_cast<__half*>(out) + static_cast<int64_t>(nt) * 8 * K;
-        const int c = min(64, K - kb * 64);
-        *f16_stage_slot(rows_tile, K, kb, c, 0, t) = a1;
-        *f16_stage_slot(rows_tile, K, kb, c, 1, t) = a2;
-        *f16_stage_slot(rows_tile, K, kb, c, 2, t) = a3;
-      }
-    }
+  for (int d = 16; d > 0; d >>= 1) {
+    m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, d));
+    m2 = fmaxf(m2, __shfl_xor_sync(0xffffffffu, m2, d));
+    m3 = fmaxf(m3, __shfl_xor_sync(0xffffffffu, m3, d));
+  }
+  if ((t & 31) == 0) {
+    float* const tb = table + static_cast<int64_t>(blockIdx.z) * table_stride + static_cast<int64_t>(nt) * 8;
+    atomicMax(reinterpret_cast<unsigned int*>(tb + 0), __float_as_uint(m1));
+    atomicMax(reinterpret_cast<unsigned int*>(tb + 1), __float_as_uint(m2));
+    atomicMax(reinterpret_cast<unsigned int*>(tb + 2), __float_as_uint(m3));
   }
 }
 
-// Pass 2 of an fp16 encode: per (k block, tile, batch) the 64 threads read
-// the block's staged sums, then write the scaled fp16 rows over them; the
-// first k block also writes the tile's factors 2^e into the table.
+// Per (k-block, tile, batch), 64 threads: read the k-block's staged sums,
+// then write the scaled fp16 rows over them; the first k-block also writes
+// the tile's factors 2^e into the table.
 __global__ void __launch_bounds__(64) encode_f16_finish_kernel(__half* __restrict__ out, int K, int64_t out_stride,
                                                               float* __restrict__ table, int64_t table_stride) {
   const int kb = blockIdx.x, nt = blockIdx.y, t = threadIdx.x;
@@ -298,6 +321,92 @@ __global__ void __launch_bounds__(64) encode_f16_finish_kernel(__half* __restric
   if (t < c)
     write_checksum_rows_f16(a1 * pow2f_exact(-e1), a2 * pow2f_exact(-e2), a3 * pow2f_exact(-e3),
                             rows_tile + kb * 64 + t, K);
+}
+
+// fp16 checksum block in one launch (small encodes, e.g. the tokens of a
+// decode step, where launches and host calls cost more than the bytes):
+// the kEncCluster CTAs of a cluster
+// share one tile of one batch (grid (tiles * kEncCluster, batch)). CTA r
+// forms the sums of k-blocks r, r + kEncCluster, ... and keeps them in the
+// rows' own bytes (f16_stage_slot) with their largest magnitudes; the
+// cluster then combines those maxima through distributed shared memory,
+// and each CTA writes the scaled rows of its k-blocks. CTA 0 writes the
+// tile's table entries. Both cluster barriers are reached by every thread.
+constexpr int kEncCluster = 8;
+
+__global__ void __launch_bounds__(256) encode_f16_cluster_kernel(const __half* __restrict__ B, int64_t ldb, int N,
+                                                                 int K, int bd, __half* __restrict__ out,
+                                                                 int64_t b_stride, int64_t out_stride,
+                                                                 float* __restrict__ table, int64_t table_stride) {
+  __shared__ float red[3][32][65];
+  __shared__ float wmax[2][3];
+  __shared__ float cmax[3];
+  const int rank = static_cast<int>(cluster_ctarank());
+  const int nt = static_cast<int>(blockIdx.x) / kEncCluster;
+  B += static_cast<int64_t>(blockIdx.y) * b_stride;
+  out += static_cast<int64_t>(blockIdx.y) * out_stride;
+  const int t = threadIdx.x;
+  const int num_kb = (K + 63) / 64;
+  __half* const rows_tile = out + static_cast<int64_t>(nt) * 8 * K;
+  float m1 = 0.f, m2 = 0.f, m3 = 0.f;
+  for (int kb = rank; kb < num_kb; kb += kEncCluster) {
+    float a1, a2, a3;
+    kblock_checksums(B, ldb, N, K, bd, nt, kb, red, a1, a2, a3);
+    const int c = min(64, K - kb * 64);
+    if (t < c) {
+      *f16_stage_slot(rows_tile, K, kb, c, 0, t) = a1;
+      *f16_stage_slot(rows_tile, K, kb, c, 1, t) = a2;
+      *f16_stage_slot(rows_tile, K, kb, c, 2, t) = a3;
+      m1 = fmaxf(m1, fabsf(a1));
+      m2 = fmaxf(m2, fabsf(a2));
+      m3 = fmaxf(m3, fabsf(a3));
+    }
+  }
+  if (t < 64) {
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) {
+      m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, d));
+      m2 = fmaxf(m2, __shfl_xor_sync(0xffffffffu, m2, d));
+      m3 = fmaxf(m3, __shfl_xor_sync(0xffffffffu, m3, d));
+    }
+    if ((t & 31) == 0) {
+      wmax[t >> 5][0] = m1;
+      wmax[t >> 5][1] = m2;
+      wmax[t >> 5][2] = m3;
+    }
+  }
+  __syncthreads();
+  if (t < 3) cmax[t] = fmaxf(wmax[0][t], wmax[1][t]);
+  cluster_sync_all();  // every CTA's maxima are in its shared memory
+  float g[3] = {0.f, 0.f, 0.f};
+#pragma unroll
+  for (int q = 0; q < 3; ++q)
+    for (int r = 0; r < kEncCluster; ++r)
+      g[q] = fmaxf(g[q], ld_shared_cluster_f32(mapa_shared(smem_u32(&cmax[q]), static_cast<uint32_t>(r))));
+  cluster_sync_all();  // no CTA leaves while another still reads its maxima
+  const int e1 = f16_chk_exponent(__float_as_uint(g[0]));
+  const int e2 = f16_chk_exponent(__float_as_uint(g[1]));
+  const int e3 = f16_chk_exponent(__float_as_uint(g[2]));
+  if (rank == 0 && t < 8) {
+    float* const tb = table + static_cast<int64_t>(blockIdx.y) * table_stride + static_cast<int64_t>(nt) * 8;
+    const float v[8] = {g[0], g[1], g[2], 0.f, pow2f_exact(e1), pow2f_exact(e2), pow2f_exact(e3), 0.f};
+    float x = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) x = (i == t) ? v[i] : x;
+    tb[t] = x;
+  }
+  const float f1 = pow2f_exact(-e1), f2 = pow2f_exact(-e2), f3 = pow2f_exact(-e3);
+  for (int kb = rank; kb < num_kb; kb += kEncCluster) {
+    const int c = min(64, K - kb * 64);
+    float a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    if (t < c) {
+      a1 = *f16_stage_slot(rows_tile, K, kb, c, 0, t);
+      a2 = *f16_stage_slot(rows_tile, K, kb, c, 1, t);
+      a3 = *f16_stage_slot(rows_tile, K, kb, c, 2, t);
+    }
+    __syncthreads();  // every staged sum of this k-block read before any row overwrites it
+    if (t < c) write_checksum_rows_f16(a1 * f1, a2 * f2, a3 * f3, rows_tile + kb * 64 + t, K);
+  }
 }
 
 // K-major copy of an N-major right operand plus (out != nullptr) its

@@ -155,6 +155,13 @@ __device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t caddr) {
   asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
 }
 
+// Load a float from another CTA's shared memory (shared::cluster address).
+__device__ __forceinline__ float ld_shared_cluster_f32(uint32_t caddr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(caddr) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
