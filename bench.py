@@ -63,7 +63,7 @@ def parse_args():
                     help="one JSON line per shape of the square sweep, the 512x4096x4096 case and the "
                          "Qwen2-7B layer GEMMs: checked / unchecked TFLOP/s and 1- and 4-fault outcomes")
     ap.add_argument("--dtype", choices=["bf16", "f16"], default="bf16",
-                    help="operand type of --model qwen2-7b (the reference driver's --dtype)")
+                    help="operand type of --model qwen2-7b (the reference driver's --dtype) and --profile-case")
     ap.add_argument("--bmm-sweep", action="store_true",
                     help="batched products (torch.bmm, attention-shaped): cuBLAS vs the fused kernel vs the "
                          "reference's per-batch check loop")
@@ -821,7 +821,8 @@ def run_ours(args):
 
 
 def profile_case(args):
-    """Two rounds of the fused GEMM at --size: the capture target of ncu."""
+    """Two rounds of the fused GEMM at --size (operands of --dtype): the
+    capture target of ncu."""
     import torch
 
     from vla_abft_estimate_b200 import _native as N
@@ -829,9 +830,10 @@ def profile_case(args):
 
     dev = torch.device("cuda", 0)
     s = args.size
-    a = (torch.randn(s, s, device=dev) * s ** -0.5).bfloat16()
-    w = (torch.randn(s, s, device=dev) * s ** -0.5).bfloat16()
-    out = torch.empty(s, s, device=dev, dtype=torch.bfloat16)
+    tdt = torch.float16 if args.dtype == "f16" else torch.bfloat16
+    a = (torch.randn(s, s, device=dev) * s ** -0.5).to(tdt)
+    w = (torch.randn(s, s, device=dev) * s ** -0.5).to(tdt)
+    out = torch.empty(s, s, device=dev, dtype=tdt)
     tile_n = ops.pick_tile_n(s, s, s, dev, N.MODE_DETECT | N.MODE_CORRECT)
     cks = ops.encode_weight(w, tile_n)
     rep = ops.ReportBuffer(64, dev)
@@ -842,7 +844,8 @@ def profile_case(args):
             ops.abft_gemm(a, w, mode=N.MODE_DETECT | N.MODE_CORRECT, out=out, tile_n=tile_n, checksums=cks,
                           report=rep)
     torch.cuda.synchronize()
-    print(json.dumps({"profile_case": args.profile_case, "size": s, "faults": rep.read().n_faults}))
+    print(json.dumps({"profile_case": args.profile_case, "size": s, "dtype": args.dtype,
+                      "faults": rep.read().n_faults}))
 
 
 SWEEP_SHAPES = [
