@@ -12,7 +12,8 @@
   1e-2 of an fp32 GEMM on sampled rows.
 * No false positives on data shaped like a real model's: outlier
   activation channels, weights with non-zero row means, SwiGLU products,
-  bias, at the Qwen2-7B layer shapes including K = 18944.
+  bias, at the Qwen2-7B layer shapes including K = 18944, on bf16 and on
+  fp16 operands.
 """
 import json
 import os
@@ -135,7 +136,7 @@ def test_square_sweep_clean_one_and_four_faults(cuda_device, size):
             assert abs(c[i, j].float().item() - exact) <= OUT_TOL * max(abs(exact), delta / 256.0)
 
 
-def llm_like(kind, m, n, k, seed, dev):
+def llm_like(kind, m, n, k, seed, dev, dtype=torch.bfloat16):
     """Activations and weights with the structure of a trained decoder's."""
     g = torch.Generator(device=dev).manual_seed(seed)
     if kind == "swiglu":  # the down projection's input: silu(gate) * up, heavy-tailed
@@ -151,7 +152,7 @@ def llm_like(kind, m, n, k, seed, dev):
     mu = torch.randn(n, 1, device=dev, generator=g) * (3 * sigma)  # non-zero row means
     w = mu + sigma * torch.randn(n, k, device=dev, generator=g)
     bias = torch.randn(n, device=dev, generator=g) * 0.1
-    return x.bfloat16(), w.bfloat16(), bias.bfloat16()
+    return x.to(dtype), w.to(dtype), bias.to(dtype)
 
 
 @pytest.mark.parametrize("m,n,k,kind", [
@@ -162,9 +163,10 @@ def llm_like(kind, m, n, k, seed, dev):
     (4096, 4096, 4096, "swiglu"),
     (16, 3584, 18944, "swiglu"),     # decode-sized (swapped operands)
 ])
-@pytest.mark.parametrize("seed", [0, 1, 2])
-def test_no_false_positive_on_llm_like_data(cuda_device, m, n, k, kind, seed):
-    a, w, b = llm_like(kind, m, n, k, seed, cuda_device)
+@pytest.mark.parametrize("seed,dtype", [(0, torch.bfloat16), (1, torch.bfloat16), (2, torch.bfloat16),
+                                        (0, torch.float16), (1, torch.float16)])
+def test_no_false_positive_on_llm_like_data(cuda_device, m, n, k, kind, seed, dtype):
+    a, w, b = llm_like(kind, m, n, k, seed, cuda_device, dtype)
     c, rep = ops.abft_gemm(a, w, b, mode=CHECKED)
     r = rep.read()
     assert r.status == 0 and r.n_faults == 0, (r.status, r.records[:4])

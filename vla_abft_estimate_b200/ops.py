@@ -41,7 +41,7 @@ def _stream(device: torch.device) -> ctypes.c_void_p:
 GEMM_DTYPES = {torch.bfloat16: N.DTYPE_BF16, torch.float16: N.DTYPE_F16}
 
 
-def _require_bf16_cuda(name: str, t: torch.Tensor, dim: int, dtype: torch.dtype = torch.bfloat16) -> None:
+def _require_cuda(name: str, t: torch.Tensor, dim: int, dtype: torch.dtype = torch.bfloat16) -> None:
     """``t`` is a CUDA tensor of ``dtype`` with ``dim`` dimensions and unit
     stride in its last one."""
     if not isinstance(t, torch.Tensor):
@@ -190,7 +190,7 @@ def encode_weight(weight: torch.Tensor, tile_n: int) -> torch.Tensor:
     it inside fp16's range, followed by the table of those factors.
     """
     dt = _gemm_dtype(weight)
-    _require_bf16_cuda("weight", weight, 2, weight.dtype)
+    _require_cuda("weight", weight, 2, weight.dtype)
     n, k = weight.shape
     nbytes = checksum_bytes(n, k, tile_n, weight.dtype)
     if nbytes == 0:
@@ -256,8 +256,8 @@ def abft_gemm(
     """
     _gemm_dtype(a)
     dtype = a.dtype
-    _require_bf16_cuda("a", a, 2, dtype)
-    _require_bf16_cuda("weight", weight, 2, dtype)
+    _require_cuda("a", a, 2, dtype)
+    _require_cuda("weight", weight, 2, dtype)
     m, k = a.shape
     n, k2 = weight.shape
     if k != k2:
@@ -265,14 +265,14 @@ def abft_gemm(
     if weight.device != a.device:
         raise ValueError("a and weight must be on the same device")
     if bias is not None:
-        _require_bf16_cuda("bias", bias, 1, dtype)
+        _require_cuda("bias", bias, 1, dtype)
         if bias.shape[0] != n:
             raise ValueError(f"bias has {bias.shape[0]} entries, expected {n}")
     dev = a.device
     if out is None:
         out = torch.empty((m, n), dtype=dtype, device=dev)
     else:
-        _require_bf16_cuda("out", out, 2, dtype)
+        _require_cuda("out", out, 2, dtype)
         if tuple(out.shape) != (m, n):
             raise ValueError(f"out must be [{m}, {n}]")
     if mode != N.MODE_OFF and report is None:
@@ -401,7 +401,7 @@ def abft_bmm(
     if _mat_layout(a) is None:
         a = a.contiguous()
     if bias is not None:
-        _require_bf16_cuda("bias", bias, 1, dtype)
+        _require_cuda("bias", bias, 1, dtype)
         if bias.shape[0] != n:
             raise ValueError(f"bias has {bias.shape[0]} entries, expected {n}")
     dev = a.device
