@@ -2,8 +2,11 @@
 //
 //   encode_weight_kernel   per-tile plain and column-index-weighted row
 //                          checksums of B[N, K] (the "Be" of checkers.py:119),
-//                          split into bf16 or (scaled) fp16 terms for the
-//                          check MMA
+//                          split into bf16 terms for the check MMA
+//   encode_f16_cluster_kernel  the same block for fp16 B, each checksum of a
+//                          tile scaled by a power of two (one launch, an
+//                          8-CTA cluster per tile); encode_f16_sums_kernel +
+//                          encode_f16_finish_kernel do it for large weights
 //   transpose_encode_kernel  K-major copy of an N-major right operand
 //                          B[K, N] (torch.bmm's mat2), with the same
 //                          checksum block computed on the way
@@ -16,8 +19,9 @@
 //                          (pytorch/abft/checkers.py:96-126)
 //   locate_finalize_kernel global row/column mismatch search and pairing
 //
-// Every reduction runs in a fixed order, so results are bit-reproducible run
-// to run (the reference's fp32 atomics, abft_fused.cu:45-46 and :71-88, are not).
+// Every sum runs in a fixed order, so results are bit-reproducible run to
+// run (the reference's fp32 atomics, abft_fused.cu:45-46 and :71-88, are
+// not); the only atomics here take maxima, which do not depend on order.
 #pragma once
 
 #include <cuda_bf16.h>
