@@ -2,7 +2,8 @@
 
 Same exported names; the checks run on libabft_b200.so.
 """
-from .checkers import AbftChecker, CheapSumChecker, OpMeta, RowColChecker, UnsupportedOperand, flatten_to_2d_for_mm
+from .checkers import (AbftChecker, CheapSumChecker, FusedB200Checker, OpMeta, RowColChecker, UnsupportedOperand,
+                       flatten_to_2d_for_mm)
 from .config import AbftConfig
 from .injector import AbftInjector, WeightChecksumCache, result_from_report
 from .stats import AbftStatsCollector, CheckResult, percentile, summarize_ms
@@ -15,6 +16,7 @@ __all__ = [
     "CheapSumChecker",
     # additions
     "CheckResult",
+    "FusedB200Checker",
     "OpMeta",
     "RowColChecker",
     "UnsupportedOperand",

@@ -9,7 +9,9 @@ torch ops, a JIT CUDA extension or torch fp32 reductions depending on
 sequence and a failure raises -- there is no fallback path.
 
 ``RowColChecker`` is new: the same post-hoc check plus row and column
-checksums of C that locate single faults.
+checksums of C that locate single faults. ``FusedB200Checker`` is the
+scalar check with fp32 sums whatever ``checker_backend`` says, for checking
+an existing C next to the fused path.
 """
 from __future__ import annotations
 
@@ -34,7 +36,7 @@ class OpMeta:
 
 
 class UnsupportedOperand(ValueError):
-    """An operand the bf16 library cannot take (dtype, device, alignment)."""
+    """An operand the library cannot take (dtype, device, alignment)."""
 
 
 class AbftChecker(ABC):
@@ -171,6 +173,28 @@ class CheapSumChecker(AbftChecker):
         return CheckResult(ok=ok, abs_err=float(rep.abs_err), rel_err=float(rep.rel_err),
                            abft_corner=float(rep.corner), sum_c=float(rep.sum_c), n_faults=int(rep.n_faults),
                            n_located=len(located), n_corrected=0, located=located)
+
+
+class FusedB200Checker(CheapSumChecker):
+    """The scalar check of an existing C (the fused kernel's reference mode,
+    as a checker plugin): CheapSumChecker's rule with fp32 sums on the
+    native kernels, whatever ``cfg.checker_backend`` and
+    ``cfg.force_fp32_check`` select. The reference's fused and triton
+    backends sum in fp32 too (abft_fused.cu:23-88, triton_backend.py:25-51);
+    use CheapSumChecker with the "python" backend for its bf16-rounded sums.
+    """
+
+    def launch(
+        self,
+        a_2d: torch.Tensor,
+        b_2d: torch.Tensor,
+        c_2d: torch.Tensor,
+        bias_1d: Optional[torch.Tensor] = None,
+    ) -> ops.ReportBuffer:
+        a, b, layout, c, bias = _as_lib_operands(a_2d, b_2d, c_2d, bias_1d)
+        return ops.check_only(a, b, c, bias, b_layout=layout, tol_abs=self.cfg.tol_abs, tol_rel=self.cfg.tol_rel,
+                              locate=self.locate, bf16_sums=False, thr_scale=self.cfg.thr_scale,
+                              report=ops.ReportBuffer(self.cfg.report_capacity, a.device))
 
 
 class RowColChecker(CheapSumChecker):

@@ -8,6 +8,8 @@ anything else raises (no CPU fallback).
 Functions
   encode_weight(weight, tile_n)          per-tile checksums of a [N, K] weight
   abft_gemm(a, weight, bias, ...)        fused checksum-protected GEMM
+  abft_linear(x, weight, bias, ...)      the same with F.linear's shapes:
+                                         any leading dimensions, any K, N
   abft_bmm(a, b, ...)                    the same for a batch of products
                                          (torch.bmm), one launch
   check_only(a, b, c, bias, ...)         post-hoc check of an existing output
@@ -321,6 +323,65 @@ def _gemm_launch(a, weight, bias, out, m, n, k, mode, tile_n, tile_m, swap_ab, t
         args.n_inject = inj.n
     _run_gemm(args, dev, (m, n, k, int(mode), int(tile_n), int(tile_m), int(swap_ab), checksums is None,
                           int(num_sms), 1, 0, args.dtype))
+
+
+def abft_linear(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    bias: Optional[torch.Tensor] = None,
+    *,
+    cfg=None,
+    mode: Optional[int] = None,
+    checksums: Optional[torch.Tensor] = None,
+    tile_n: int = 0,
+    thr_scale: Optional[float] = None,
+    thr_abs: Optional[float] = None,
+    inject: Optional[Sequence[Tuple[int, int, float]]] = None,
+    report: Optional[ReportBuffer] = None,
+) -> Tuple[torch.Tensor, Optional[ReportBuffer]]:
+    """``F.linear(x, weight, bias)`` with the fused checksum check: the op
+    the reference's linear hook runs followed by its check
+    (pytorch/abft/injector.py:152-161), in one launch.
+
+    ``x`` is [..., K] and the output [..., N], bfloat16 or float16 like
+    ``weight`` [N, K] and ``bias`` [N]. Fault coordinates (``inject`` and the
+    report's records) index the output flattened to [rows, N]. ``cfg`` (an
+    ``AbftConfig``) supplies the mode (``detect_only``), thresholds and
+    report capacity unless they are given here; by default faults are
+    detected, located and corrected. K or N not a multiple of 8 (the
+    library reads rows in 16-byte pieces) runs on zero-padded copies, which
+    change no product and no checksum; ``checksums`` must then be None.
+    Returns the output and the report (None when mode is MODE_OFF).
+    """
+    _gemm_dtype(x)
+    if weight.dim() != 2 or x.shape[-1] != weight.shape[1]:
+        raise ValueError(f"x {tuple(x.shape)} and weight {tuple(weight.shape)} do not match as F.linear operands")
+    n, k = weight.shape
+    if mode is None:
+        mode = N.MODE_DETECT | (0 if (cfg is not None and cfg.detect_only) else N.MODE_CORRECT)
+    if thr_scale is None:
+        thr_scale = cfg.thr_scale if cfg is not None else DEFAULT_THR_SCALE
+    if thr_abs is None:
+        thr_abs = cfg.thr_abs if cfg is not None else 0.0
+    if report is None and mode != N.MODE_OFF:
+        report = ReportBuffer(cfg.report_capacity if cfg is not None else DEFAULT_CAPACITY, x.device)
+    x2 = x.reshape(-1, k)
+    pk, pn = -k % 8, -n % 8
+    if pk or pn:
+        if checksums is not None:
+            raise ValueError("checksums cannot be used when K or N needs padding to a multiple of 8")
+        x2 = torch.nn.functional.pad(x2, (0, pk))
+        weight = torch.nn.functional.pad(weight, (0, pk, 0, pn))
+        bias = None if bias is None else (torch.nn.functional.pad(bias, (0, pn)) if pn else bias)
+    elif x2.stride(1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+    if bias is not None and not bias.is_contiguous():
+        bias = bias.contiguous()
+    out, rep = abft_gemm(x2, weight, bias, mode=mode, tile_n=tile_n, thr_scale=thr_scale, thr_abs=thr_abs,
+                         checksums=checksums, inject=inject, report=report)
+    if pn:
+        out = out[:, :n]
+    return out.reshape(*x.shape[:-1], n), rep
 
 
 def _mat_layout(t: torch.Tensor) -> Optional[Tuple[int, int]]:
