@@ -1,4 +1,4 @@
-// gemm_kernel.cuh - fused checksum-protected bf16 GEMM for sm_100a.
+// gemm_kernel.cuh - fused checksum-protected bf16 / fp16 GEMM for sm_100a.
 //
 //   C[M, N] = A[M, K] * B[N, K]^T (+ bias)      (B = nn.Linear weight layout)
 //
@@ -26,7 +26,8 @@
 //   warps 2-13  epilogue: warp w owns TMEM lane quadrant (w % 4), i.e. 32
 //               output rows, and every third 32-column chunk of the tile
 //               (from chunk (w - 2) / 4). Each thread streams its chunks from
-//               TMEM once: row checksums, bias, bf16 rounding and the store;
+//               TMEM once: row checksums, bias, rounding to the element
+//               type and the store;
 //               the three partial checksums of a row are then combined, the
 //               row checked and a located fault corrected.
 //
@@ -39,13 +40,15 @@
 //   actual    s1 = sum_j C[i,j],  s2 = sum_j (j+1) C[i,j]       (fp32 accumulator)
 // and a third pair with column signs sg(j) = +-1 (Thue-Morse parity of j):
 //   e3 = A[i,:] . v3,   v3[k] = sum_j sg(j) B[j,k];   s3 = sum_j sg(j) C[i,j]
-// The checksum block holds v1 and v2 each split into three bf16 terms
-// (hi + mid + lo, 24 significant bits) and v3 in two. A single corrupted
+// The checksum block holds v1 and v2 each split into three terms of the
+// operands' type (hi + mid + lo: 24 significant bits in bf16; in fp16, whose
+// range is narrow, each checksum of a tile is first scaled by a power of
+// two that the epilogue multiplies back) and v3 in two. A single corrupted
 // C[i,j*] (+delta) gives s1 - e1 = delta, s2 - e2 = (j*+1) delta and
 // s3 - e3 = sg(j*) delta: the ratio of the first two pins the column, the
 // third must agree with it (several faults in one row segment whose
 // weighted mean column is an integer are rejected this way), and delta is
-// subtracted before the bf16 store.
+// subtracted before the store.
 #pragma once
 
 #include <cuda_bf16.h>

@@ -288,7 +288,6 @@ __host__ __device__ constexpr uint32_t umma_idesc(int M, int N, uint32_t fmt) {
   return (1u << 4) | (fmt << 7) | (fmt << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
          (static_cast<uint32_t>(M >> 4) << 24);
 }
-__host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N) { return umma_idesc(M, N, 1u); }
 
 __device__ __forceinline__ void umma_bf16_ss(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                              uint32_t accumulate) {
