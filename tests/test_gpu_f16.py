@@ -181,7 +181,8 @@ def test_swapped_few_rows(cuda_device, m, n, k):
 
 # ----------------------------------------------------------------- batched
 @pytest.mark.parametrize("layout", ["kn_rowmajor", "kn_view", "nk"])
-@pytest.mark.parametrize("bsz,m,n,k", [(4, 256, 512, 256), (3, 300, 1000, 520), (6, 16, 256, 128)])
+@pytest.mark.parametrize("bsz,m,n,k", [(4, 256, 512, 256), (3, 300, 1000, 520), (6, 16, 256, 128),
+                                      (3, 256, 4096, 2048)])  # the last encodes on the many-CTA path, batched
 def test_bmm_faults_per_batch(cuda_device, layout, bsz, m, n, k):
     a, w, _ = seeded(m, n, k, 40 + bsz, bsz=bsz)
     acc = np.einsum("bmk,bnk->bmn", f32(a).astype(np.float64), f32(w).astype(np.float64))
