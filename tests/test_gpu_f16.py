@@ -54,6 +54,17 @@ def test_encode_block_bit_identical_to_oracle(cuda_device, tile_n, n, k, w_scale
     assert np.array_equal(got, want)
 
 
+@pytest.mark.parametrize("n", [1, 8, 32])
+@pytest.mark.parametrize("k", [64, 3584, 18944, 32768, 32776])
+def test_encode_few_rows_bit_identical_to_oracle(cuda_device, n, k):
+    """Token tiles of a decode step (at most 32 rows: the column-parallel
+    one-launch encode; K past 32768 takes the general cluster kernel)."""
+    _, w, _ = seeded(8, n, k, 3 + n)
+    blk = ops.encode_weight(w.to(cuda_device), 128).cpu().numpy()
+    want = np.frombuffer(O.encode_weight_f16_block(f32(w), 120), dtype=np.uint8)
+    assert np.array_equal(blk, want)
+
+
 def test_encode_passes_over_nan_sums(cuda_device):
     """A NaN weight makes its k column's sums NaN; the tile's scales come
     from the other columns (as the oracle's restatement has it)."""

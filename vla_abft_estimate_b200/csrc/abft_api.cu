@@ -802,7 +802,9 @@ int abft_encode_weight_typed(const void* B, int64_t N, int64_t K, int64_t ldb, i
     return launch_status();
   }
   // Small: one cluster of kEncCluster CTAs per tile and batch forms the
-  // sums, agrees on the tile's scales and writes the rows and the table.
+  // sums, agrees on the tile's scales and writes the rows and the table
+  // (column-parallel for at most 32 rows: a decode step's tokens).
+  const bool few_rows = N <= 32 && K <= kFewRowsMaxK;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(tiles * kEncCluster), static_cast<unsigned>(batch));
   cfg.blockDim = dim3(256);
@@ -814,8 +816,9 @@ int abft_encode_weight_typed(const void* B, int64_t N, int64_t K, int64_t ldb, i
   at.val.clusterDim.z = 1;
   cfg.attrs = &at;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, encode_f16_cluster_kernel, Bh, ldb, static_cast<int>(N), static_cast<int>(K), bd, oh,
-                         stride_b, static_cast<int64_t>(bytes / 2), table, static_cast<int64_t>(bytes / 4)) != cudaSuccess)
+  if (cudaLaunchKernelEx(&cfg, few_rows ? encode_f16_few_rows_kernel : encode_f16_cluster_kernel, Bh, ldb,
+                         static_cast<int>(N), static_cast<int>(K), bd, oh, stride_b, static_cast<int64_t>(bytes / 2),
+                         table, static_cast<int64_t>(bytes / 4)) != cudaSuccess)
     return launch_status(), ABFT_ERR_CUDA;
   return launch_status();
 }

@@ -5,8 +5,10 @@
 //                          split into bf16 terms for the check MMA
 //   encode_f16_cluster_kernel  the same block for fp16 B, each checksum of a
 //                          tile scaled by a power of two (one launch, an
-//                          8-CTA cluster per tile); encode_f16_sums_kernel +
-//                          encode_f16_finish_kernel do it for large weights
+//                          8-CTA cluster per tile); encode_f16_few_rows_kernel
+//                          for tiles of at most 32 rows (decode tokens);
+//                          encode_f16_sums_kernel + encode_f16_finish_kernel
+//                          for large weights
 //   transpose_encode_kernel  K-major copy of an N-major right operand
 //                          B[K, N] (torch.bmm's mat2), with the same
 //                          checksum block computed on the way
@@ -410,6 +412,133 @@ __global__ void __launch_bounds__(256) encode_f16_cluster_kernel(const __half* _
     }
     __syncthreads();  // every staged sum of this k-block read before any row overwrites it
     if (t < c) write_checksum_rows_f16(a1 * f1, a2 * f2, a3 * f3, rows_tile + kb * 64 + t, K);
+  }
+}
+
+// fp16 checksum block of a tile of at most 32 rows (the tokens of a decode
+// step), in one launch: a cluster of kEncCluster CTAs per tile and batch,
+// thread t of CTA r owning the 8-column chunks r * 256 + t + i * 2048
+// (i < kFewRowsChunks). A thread adds its chunk's rows in order, from +0,
+// with all of their loads in flight, and keeps the sums in registers while
+// the cluster agrees on the tile's scales. With 32 rows or fewer every row
+// is its own group in kblock_checksums' order and the groups past the last
+// row add +0 to a sum that cannot be -0, so the sums are bit-identical.
+// Requires N - nt * bd <= 32 for every tile and K <= kFewRowsMaxK.
+constexpr int kFewRowsChunks = 2;
+constexpr int kFewRowsMaxK = kEncCluster * 256 * 8 * kFewRowsChunks;
+
+__global__ void __launch_bounds__(256) encode_f16_few_rows_kernel(const __half* __restrict__ B, int64_t ldb, int N,
+                                                                  int K, int bd, __half* __restrict__ out,
+                                                                  int64_t b_stride, int64_t out_stride,
+                                                                  float* __restrict__ table, int64_t table_stride) {
+  __shared__ float wmax[8][3];
+  __shared__ float cmax[3];
+  const int rank = static_cast<int>(cluster_ctarank());
+  const int nt = static_cast<int>(blockIdx.x) / kEncCluster;
+  B += static_cast<int64_t>(blockIdx.y) * b_stride + static_cast<int64_t>(nt) * bd * ldb;
+  out += static_cast<int64_t>(blockIdx.y) * out_stride;
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int nrows = min(bd, N - nt * bd);
+  const int nchunks = K / 8;
+  float a1[kFewRowsChunks][8], a2[kFewRowsChunks][8], a3[kFewRowsChunks][8];
+  float m1 = 0.f, m2 = 0.f, m3 = 0.f;
+#pragma unroll
+  for (int i = 0; i < kFewRowsChunks; ++i) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) a1[i][e] = a2[i][e] = a3[i][e] = 0.f;
+    const int c = rank * 256 + t + i * kEncCluster * 256;
+    if (c < nchunks) {
+      const __half* col = B + static_cast<int64_t>(c) * 8;
+      for (int j0 = 0; j0 < nrows; j0 += 8) {
+        uint4 w[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          w[u] = j0 + u < nrows ? __ldg(reinterpret_cast<const uint4*>(col + static_cast<int64_t>(j0 + u) * ldb))
+                                : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int j = j0 + u;
+          if (j >= nrows) break;
+          float x[8];
+          unpack8_as(w[u], x, B);
+          const float wt = static_cast<float>(j + 1);
+          const float sg = col_sign(j);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            a1[i][e] += x[e];
+            a2[i][e] = fmaf(wt, x[e], a2[i][e]);
+            a3[i][e] = fmaf(sg, x[e], a3[i][e]);
+          }
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        m1 = fmaxf(m1, fabsf(a1[i][e]));
+        m2 = fmaxf(m2, fabsf(a2[i][e]));
+        m3 = fmaxf(m3, fabsf(a3[i][e]));
+      }
+    }
+  }
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) {
+    m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, d));
+    m2 = fmaxf(m2, __shfl_xor_sync(0xffffffffu, m2, d));
+    m3 = fmaxf(m3, __shfl_xor_sync(0xffffffffu, m3, d));
+  }
+  if (lane == 0) {
+    wmax[warp][0] = m1;
+    wmax[warp][1] = m2;
+    wmax[warp][2] = m3;
+  }
+  __syncthreads();
+  if (t < 3) {
+    float m = 0.f;
+    for (int w8 = 0; w8 < 8; ++w8) m = fmaxf(m, wmax[w8][t]);
+    cmax[t] = m;
+  }
+  cluster_sync_all();  // every CTA's maxima are in its shared memory
+  float g[3] = {0.f, 0.f, 0.f};
+#pragma unroll
+  for (int q = 0; q < 3; ++q)
+    for (int r = 0; r < kEncCluster; ++r)
+      g[q] = fmaxf(g[q], ld_shared_cluster_f32(mapa_shared(smem_u32(&cmax[q]), static_cast<uint32_t>(r))));
+  cluster_sync_all();  // no CTA leaves while another still reads its maxima
+  const int e1 = f16_chk_exponent(__float_as_uint(g[0]));
+  const int e2 = f16_chk_exponent(__float_as_uint(g[1]));
+  const int e3 = f16_chk_exponent(__float_as_uint(g[2]));
+  if (rank == 0 && t < 8) {
+    float* const tb = table + static_cast<int64_t>(blockIdx.y) * table_stride + static_cast<int64_t>(nt) * 8;
+    const float v[8] = {g[0], g[1], g[2], 0.f, pow2f_exact(e1), pow2f_exact(e2), pow2f_exact(e3), 0.f};
+    float x = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) x = (i == t) ? v[i] : x;
+    tb[t] = x;
+  }
+  const float f1 = pow2f_exact(-e1), f2 = pow2f_exact(-e2), f3 = pow2f_exact(-e3);
+  __half* const rows_tile = out + static_cast<int64_t>(nt) * 8 * K;
+#pragma unroll
+  for (int i = 0; i < kFewRowsChunks; ++i) {
+    const int c = rank * 256 + t + i * kEncCluster * 256;
+    if (c >= nchunks) continue;
+    __half h[8][8];  // [checksum row][column]
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      split3_f16(a1[i][e] * f1, h[0][e], h[1][e], h[2][e]);
+      split3_f16(a2[i][e] * f2, h[3][e], h[4][e], h[5][e]);
+      const float x3 = a3[i][e] * f3;
+      h[6][e] = __float2half_rn(x3);
+      h[7][e] = __float2half_rn(x3 - __half2float(h[6][e]));
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      uint32_t wd[4];
+#pragma unroll
+      for (int p2 = 0; p2 < 4; ++p2)
+        wd[p2] = static_cast<uint32_t>(__half_as_ushort(h[q][2 * p2])) |
+                 (static_cast<uint32_t>(__half_as_ushort(h[q][2 * p2 + 1])) << 16);
+      *reinterpret_cast<uint4*>(rows_tile + static_cast<int64_t>(q) * K + static_cast<int64_t>(c) * 8) =
+          make_uint4(wd[0], wd[1], wd[2], wd[3]);
+    }
   }
 }
 
