@@ -135,11 +135,15 @@ _WS_BYTES: dict = {}
 
 
 def _run_gemm(args: N.GemmArgs, dev: torch.device, key: tuple) -> None:
-    """Workspace, current stream and device guard around abft_gemm."""
-    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    """Workspace, current stream and device guard around abft_gemm. (The
+    operands are CUDA tensors, so CUDA is initialised: the raw device query
+    skips torch.cuda.current_device()'s lazy-init checks, a few hundred ns of
+    a decode step's every linear.)"""
+    cur = torch._C._cuda_getDevice()
+    idx = dev.index if dev.index is not None else cur
     stream = torch._C._cuda_getCurrentRawStream(idx)
     L = N.lib()
-    if torch.cuda.current_device() != idx:
+    if cur != idx:
         with torch.cuda.device(idx):
             return _run_gemm(args, dev, key)
     key = (idx,) + key
