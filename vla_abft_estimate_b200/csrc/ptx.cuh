@@ -90,6 +90,30 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* map, uint64_t
       : "memory");
 }
 
+// L2 cache policies for hinted loads: evict_first for data read once (the
+// weight streaming through a decode step's GEMM), evict_last for data read
+// again (its token tile).
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// tma_load_3d with an L2 cache policy (l2_policy_*).
+__device__ __forceinline__ void tma_load_3d_hint(void* dst, const void* map, uint64_t* bar, int32_t x, int32_t y,
+                                                 int32_t z, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%3, %4, "
+      "%5}], [%2], %6;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "l"(pol)
+      : "memory");
+}
+
 // 3-D tiled store of a shared-memory box to global memory (bulk async-group
 // completion); the map clips rows and columns outside the tensor.
 __device__ __forceinline__ void tma_store_3d(const void* map, const void* src, int32_t x, int32_t y, int32_t z) {
