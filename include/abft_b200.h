@@ -273,6 +273,16 @@ int abft_gemm_bf16(const abft_gemm_args* args, void* stream);
  * both). */
 int abft_gemm(const abft_gemm_args* args, void* stream);
 
+/* Self-test of the library's bounded device waits (failure detection
+ * without a fault): one small launch waits for a device flag that nothing
+ * sets and for an mbarrier phase that never completes, through the same
+ * bounded waits the fused kernel uses. Each gives up after its limit (2 s)
+ * instead of hanging; the report (abft_report_bytes(0) bytes, 16-byte
+ * aligned, zeroed by the call) then holds ABFT_STATUS_DEVICE_TIMEOUT and
+ * n_faults = 2 (the waits that gave up). The launch takes about 4 s; the
+ * context stays usable. */
+int abft_wait_selftest(void* report, void* stream);
+
 /* Post-hoc check of an existing output C = A * B^T (+ bias), the drop-in for
  * the reference's abft_fused(a, b, c, bias) -> [corner, sum_c]
  * (pytorch/abft/kernels/abft_fused.cpp:11-31, abft_fused.cu:92-141) and the

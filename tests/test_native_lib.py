@@ -148,6 +148,16 @@ def test_fp16_gemm_and_typed_encode_validation_without_gpu():
         assert L.abft_encode_weight_typed(B, 8, 8, 8, 0, 1, 256, N.DTYPE_F16, out, None) == -6
 
 
+def test_wait_selftest_validation_without_gpu():
+    L = N.lib()
+    assert L.abft_wait_selftest(None, None) == -1
+    assert L.abft_wait_selftest(ctypes.c_void_p(0x10008), None) == -2
+    import torch
+
+    if not torch.cuda.is_available():
+        assert L.abft_wait_selftest(ctypes.c_void_p(0x10000), None) == -6
+
+
 def test_check_argument_validation_without_gpu():
     L = N.lib()
     c = N.CheckArgs()

@@ -63,6 +63,7 @@ EXPORTED_SYMBOLS = (
     "abft_gemm_workspace_bytes",
     "abft_gemm_bf16",
     "abft_gemm",
+    "abft_wait_selftest",
     "abft_check_workspace_bytes",
     "abft_check_only",
     "abft_check_only_noalloc",
@@ -195,6 +196,8 @@ def lib() -> ctypes.CDLL:
     L.abft_gemm_bf16.argtypes = [ctypes.POINTER(GemmArgs), vp]
     L.abft_gemm.restype = ctypes.c_int
     L.abft_gemm.argtypes = [ctypes.POINTER(GemmArgs), vp]
+    L.abft_wait_selftest.restype = ctypes.c_int
+    L.abft_wait_selftest.argtypes = [vp, vp]
     L.abft_check_workspace_bytes.restype = sz
     L.abft_check_workspace_bytes.argtypes = [ctypes.POINTER(CheckArgs)]
     L.abft_check_only.restype = ctypes.c_int

@@ -852,6 +852,19 @@ int32_t abft_pick_tile_m(int64_t M, int64_t N, int64_t K, int32_t num_sms, uint3
   return pick_tile_m(M, N, K, num_sms, mode, tile_n);
 }
 
+int abft_wait_selftest(void* report, void* stream) {
+  if (report == nullptr) return ABFT_ERR_INVALID_ARG;
+  if (!aligned16(report)) return ABFT_ERR_ALIGNMENT;
+  int dev;
+  DeviceInfo info;
+  const int rc = current_device(&dev, &info);
+  if (rc != ABFT_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(report, 0, sizeof(abft_report), s) != cudaSuccess) return launch_status(), ABFT_ERR_CUDA;
+  wait_selftest_kernel<<<1, 32, 0, s>>>(static_cast<abft_report*>(report));
+  return launch_status();
+}
+
 int abft_gemm(const abft_gemm_args* args, void* stream) { return abft_gemm_bf16(args, stream); }
 
 int abft_gemm_bf16(const abft_gemm_args* args, void* stream) {

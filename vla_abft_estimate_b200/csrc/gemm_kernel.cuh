@@ -274,6 +274,38 @@ __device__ __forceinline__ bool wait_flag(const unsigned long long* f, uint64_t 
   return ok != 0;
 }
 
+// A flag no code path writes: the target of the bounded-wait self-test.
+__device__ unsigned long long g_wait_selftest_flag = 0ull;
+
+// Self-test of the bounded device waits every fused launch relies on: one
+// warp waits through wait_flag (the stream-K hand-off) for a value the
+// flag above never takes, then one thread through mbar_wait (the pipeline's
+// barriers) for a phase of a fresh mbarrier that nothing arrives on. Each
+// gives up after kWaitTimeoutNs and raises the abort flag instead of
+// spinning on; the kernel then records ABFT_STATUS_DEVICE_TIMEOUT and, in
+// n_faults, how many waits gave up (2 expected), and returns normally.
+// One CTA of 32 threads; the host zeroes the report header first.
+__global__ void __launch_bounds__(32) wait_selftest_kernel(abft_report* rep) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  const int lane = threadIdx.x;
+  if (lane == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+    abort_flag = 0;
+  }
+  __syncwarp();
+  const bool flag_ok = wait_flag(&g_wait_selftest_flag, 1ull, &abort_flag);
+  __syncwarp();
+  if (lane == 0) {
+    abort_flag = 0;  // let the second wait run to its own limit
+    const bool bar_ok = mbar_wait(&bar, 0u, &abort_flag);
+    const uint32_t gave_up = (flag_ok ? 0u : 1u) + (bar_ok ? 0u : 1u);
+    rep->n_faults = gave_up;
+    rep->status = gave_up ? ABFT_STATUS_DEVICE_TIMEOUT : 0u;
+  }
+}
+
 // Bounded wait (one thread) until CTA 0 has reset the report header of this
 // launch; every atomic on the report comes after it.
 __device__ __forceinline__ bool report_ready(const GemmParams& p, volatile int* abort_flag) {

@@ -13,6 +13,8 @@ Functions
   abft_bmm(a, b, ...)                    the same for a batch of products
                                          (torch.bmm), one launch
   check_only(a, b, c, bias, ...)         post-hoc check of an existing output
+  wait_selftest()                        the bounded device waits giving up
+                                         (failure detection, no fault)
 """
 from __future__ import annotations
 
@@ -596,6 +598,18 @@ def check_only(
     N.check("abft_check_only", rc)
     ws.record_stream(torch.cuda.current_stream(dev))
     return report
+
+
+def wait_selftest(device: Optional[torch.device] = None) -> FaultReport:
+    """Run the library's bounded-wait self-test on ``device`` (default: the
+    current one) and return its report: ``device_timeout`` set and
+    ``n_faults`` 2 when both test waits gave up after their limit, as they
+    must. Takes about 4 s; synchronises the device."""
+    dev = torch.device("cuda", _device_index(device))
+    rep = ReportBuffer(0, dev)
+    with torch.cuda.device(dev):
+        N.check("abft_wait_selftest", N.lib().abft_wait_selftest(ctypes.c_void_p(rep.data_ptr()), _stream(dev)))
+    return rep.read()
 
 
 def flops(m: int, n: int, k: int) -> float:
