@@ -41,7 +41,7 @@
 extern "C" {
 #endif
 
-#define ABFT_B200_VERSION 4
+#define ABFT_B200_VERSION 5
 
 /* ---- return codes ------------------------------------------------------- */
 enum abft_status {
@@ -264,6 +264,31 @@ int abft_encode_weight_typed(const void* B, int64_t N, int64_t K, int64_t ldb, i
 
 /* Workspace the fused GEMM needs for these arguments (0 when none). */
 size_t abft_gemm_workspace_bytes(const abft_gemm_args* args);
+
+/* What abft_gemm launches for these arguments on the current device, in the
+ * frame the kernel runs in (with swapped operands, few output rows: the
+ * weight on the kernel's row side). No device work. */
+typedef struct abft_plan_info {
+  int32_t tile_n;         /* MMA tile width: 256 or 128                           */
+  int32_t tile_m;         /* output rows per tile: 128, or 256 (CTA pairs)        */
+  int32_t data_cols;      /* data columns per tile (tile_n - 8 with checks)       */
+  int32_t tiles_n;        /* tile columns                                          */
+  int32_t last_cols;      /* data columns of the last tile column (a compact tail
+                             tile when fewer than data_cols)                       */
+  int32_t swapped;        /* 1: operands swapped                                   */
+  int32_t units;          /* CTAs, or CTA pairs, the schedule spreads tiles over   */
+  int32_t grid;           /* CTAs launched                                         */
+  int32_t dp_tiles;       /* tiles run whole (data-parallel waves)                 */
+  int32_t sk_units;       /* units sharing the remaining tiles stream-K (0: none)  */
+  int64_t tiles;          /* output tiles of the launch (all batches)              */
+  uint64_t workspace_bytes;
+} abft_plan_info;
+
+/* Fills *info for the arguments abft_gemm would take (validated the same
+ * way; only sizes are read, so placeholder addresses do). Returns ABFT_OK
+ * (info all zero when M or N is 0: nothing launches) or the error abft_gemm
+ * would return first. */
+int abft_gemm_plan(const abft_gemm_args* args, abft_plan_info* info);
 
 /* The fused checksum-protected GEMM. Replaces F.linear + CheapSumChecker.check
  * (pytorch/abft/injector.py:152-161 -> pytorch/abft/checkers.py:55-126). */

@@ -27,7 +27,7 @@ def test_library_exports_every_declared_symbol():
     L = N.lib()
     for name in declared_functions():
         assert hasattr(L, name), name
-    assert L.abft_version() == N.LIB_VERSION == 4
+    assert L.abft_version() == N.LIB_VERSION == 5
 
 
 def test_status_strings():
@@ -57,6 +57,7 @@ def test_host_only_helpers():
     assert L.abft_checksum_bytes(4096, 4096, 256) == 17 * 8 * 4096 * 2  # ceil(4096/248) tiles
     assert L.abft_checksum_bytes(4096, 4096, 128) == 35 * 8 * 4096 * 2  # ceil(4096/120) tiles
     assert L.abft_checksum_bytes(4096, 4096, 64) == 0
+    assert L.abft_gemm_plan(None, None) == -1
 
 
 def test_gemm_argument_validation_without_gpu():

@@ -46,7 +46,7 @@ MAX_INJECT = 64
 REPORT_HEADER_BYTES = 64
 RECORD_BYTES = 24
 BATCH_COUNT_BYTES = 16  # uint32 {faults, located, corrected, 0} per batch after the records
-LIB_VERSION = 4
+LIB_VERSION = 5
 
 EXPORTED_SYMBOLS = (
     "abft_version",
@@ -61,6 +61,7 @@ EXPORTED_SYMBOLS = (
     "abft_checksum_bytes_typed",
     "abft_encode_weight_typed",
     "abft_gemm_workspace_bytes",
+    "abft_gemm_plan",
     "abft_gemm_bf16",
     "abft_gemm",
     "abft_wait_selftest",
@@ -120,6 +121,28 @@ class GemmArgs(ctypes.Structure):
         ("stride_c", ctypes.c_int64),
         ("dtype", ctypes.c_int32),
     ]
+
+
+class PlanInfo(ctypes.Structure):
+    """Mirror of ``abft_plan_info``."""
+
+    _fields_ = [
+        ("tile_n", ctypes.c_int32),
+        ("tile_m", ctypes.c_int32),
+        ("data_cols", ctypes.c_int32),
+        ("tiles_n", ctypes.c_int32),
+        ("last_cols", ctypes.c_int32),
+        ("swapped", ctypes.c_int32),
+        ("units", ctypes.c_int32),
+        ("grid", ctypes.c_int32),
+        ("dp_tiles", ctypes.c_int32),
+        ("sk_units", ctypes.c_int32),
+        ("tiles", ctypes.c_int64),
+        ("workspace_bytes", ctypes.c_uint64),
+    ]
+
+    def as_dict(self) -> dict:
+        return {name: int(getattr(self, name)) for name, _ in self._fields_}
 
 
 class CheckArgs(ctypes.Structure):
@@ -192,6 +215,8 @@ def lib() -> ctypes.CDLL:
     L.abft_encode_weight_typed.argtypes = [vp, i64, i64, i64, i64, i32, i32, i32, vp, vp]
     L.abft_gemm_workspace_bytes.restype = sz
     L.abft_gemm_workspace_bytes.argtypes = [ctypes.POINTER(GemmArgs)]
+    L.abft_gemm_plan.restype = ctypes.c_int
+    L.abft_gemm_plan.argtypes = [ctypes.POINTER(GemmArgs), ctypes.POINTER(PlanInfo)]
     L.abft_gemm_bf16.restype = ctypes.c_int
     L.abft_gemm_bf16.argtypes = [ctypes.POINTER(GemmArgs), vp]
     L.abft_gemm.restype = ctypes.c_int

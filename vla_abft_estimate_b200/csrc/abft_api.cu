@@ -867,6 +867,40 @@ int abft_wait_selftest(void* report, void* stream) {
 
 int abft_gemm(const abft_gemm_args* args, void* stream) { return abft_gemm_bf16(args, stream); }
 
+int abft_gemm_plan(const abft_gemm_args* args, abft_plan_info* info) {
+  if (info == nullptr) return ABFT_ERR_INVALID_ARG;
+  int rc = validate_gemm(args);
+  if (rc != ABFT_OK) return rc;
+  int dev;
+  DeviceInfo dinfo;
+  rc = current_device(&dev, &dinfo);
+  if (rc != ABFT_OK) return rc;
+  memset(info, 0, sizeof(*info));
+  if (args->M == 0 || args->N == 0) return ABFT_OK;  // abft_gemm launches nothing
+  if (args->K == 0) return ABFT_ERR_UNSUPPORTED;
+  int sms = dinfo.sms;
+  if (args->num_sms > 0 && args->num_sms < sms) sms = args->num_sms;
+  Frames fr;
+  make_frames(args, args->workspace, &fr);
+  Plan pl;
+  rc = make_plan(&fr.k, dev, sms, &pl);
+  if (rc != ABFT_OK) return rc;
+  const int64_t cols = cdiv(fr.k.N, pl.bd);
+  info->tile_n = pl.bn;
+  info->tile_m = pl.tile_m;
+  info->data_cols = pl.bd;
+  info->tiles_n = static_cast<int32_t>(cols);
+  info->last_cols = static_cast<int32_t>(fr.k.N - (cols - 1) * pl.bd);
+  info->swapped = fr.swap ? 1 : 0;
+  info->units = pl.units;
+  info->grid = pl.grid;
+  info->dp_tiles = pl.sch.dp_tiles;
+  info->sk_units = pl.sch.sk ? pl.sch.sk_ctas : 0;
+  info->tiles = pl.tiles;
+  info->workspace_bytes = fr.copy_bytes + pl.total;
+  return ABFT_OK;
+}
+
 int abft_gemm_bf16(const abft_gemm_args* args, void* stream) {
   int rc = validate_gemm(args);
   if (rc != ABFT_OK) return rc;

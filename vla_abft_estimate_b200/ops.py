@@ -173,6 +173,40 @@ def pick_tile_m(m: int, n: int, k: int, tile_n: int, device: Optional[torch.devi
     return int(N.lib().abft_pick_tile_m(int(m), int(n), int(k), int(sms), int(mode), int(tile_n)))
 
 
+def gemm_plan(m: int, n: int, k: int, *, dtype: torch.dtype = torch.bfloat16,
+              mode: int = N.MODE_DETECT | N.MODE_CORRECT, tile_n: int = 0, tile_m: int = 0, swap_ab: int = 0,
+              num_sms: int = 0, batch: int = 1, cached_checksums: bool = True,
+              device: Optional[torch.device] = None) -> dict:
+    """What ``abft_gemm`` would launch for an m x n x k product (x ``batch``)
+    of contiguous ``dtype`` operands on ``device``: tile shape, tile columns,
+    the last column's width, schedule and workspace (abft_gemm_plan). No
+    device work: the call sees only placeholder addresses."""
+    code = GEMM_DTYPES.get(dtype)
+    if code is None:
+        raise ValueError(f"the fused GEMM takes bfloat16 or float16 operands, got {dtype}")
+    fake = 1 << 20  # an aligned placeholder address; nothing is read or written
+    args = N.GemmArgs()
+    args.A = args.B = args.C = fake
+    args.M, args.N, args.K = int(m), int(n), int(k)
+    args.lda = args.ldb = int(k)
+    args.ldc = int(n)
+    args.mode = int(mode)
+    args.tile_n, args.tile_m, args.swap_ab = int(tile_n), int(tile_m), int(swap_ab)
+    args.thr_scale = DEFAULT_THR_SCALE
+    args.checksums = fake if (cached_checksums and mode != N.MODE_OFF) else None
+    args.report = fake if mode != N.MODE_OFF else None
+    args.report_capacity = DEFAULT_CAPACITY
+    args.num_sms = int(num_sms)
+    args.batch = int(batch)
+    if batch > 1:
+        args.stride_a, args.stride_b, args.stride_c = int(m) * int(k), int(n) * int(k), int(m) * int(n)
+    args.dtype = code
+    info = N.PlanInfo()
+    with torch.cuda.device(_device_index(device)):
+        N.check("abft_gemm_plan", N.lib().abft_gemm_plan(ctypes.byref(args), ctypes.byref(info)))
+    return info.as_dict()
+
+
 def _gemm_dtype(t: torch.Tensor) -> int:
     code = GEMM_DTYPES.get(t.dtype) if isinstance(t, torch.Tensor) else None
     if code is None:
