@@ -513,3 +513,55 @@ def test_check_only_f16_f32_locate_post_hoc_fault(cuda_device, dtype):
             f64 = [t.double().numpy() for t in (a, w, cc, b)]
             o = O.locate_post_hoc(f64[0], f64[1].T, f64[2], f64[3], unit=unit)
             assert r.coords() == o == want, (dtype, layout)
+
+
+# ------------------------------------------------- output offsets and strides
+def _strided_out(m, n, c_off, ld_pad, device, dtype=torch.bfloat16):
+    """An [m, n] view whose rows start c_off elements into a 32-byte sector
+    (0 or 8 bf16) with leading dimension n + ld_pad, inside a buffer filled
+    with a sentinel (so that any write outside the view shows)."""
+    ldc = n + ld_pad
+    flat = torch.full((m * ldc + c_off + 64,), 7.0, dtype=dtype, device=device)
+    assert flat.data_ptr() % 256 == 0
+    return flat, torch.as_strided(flat, (m, n), (ldc, 1), c_off)
+
+
+@pytest.mark.parametrize("mode", [N.MODE_OFF, N.MODE_DETECT | N.MODE_CORRECT])
+@pytest.mark.parametrize("c_off,ld_pad", [(8, 0), (8, 16), (0, 8), (8, 8)])
+@pytest.mark.parametrize("m,n,k,tile_n,tile_m", [
+    (300, 1000, 136, 256, 0), (512, 4096, 512, 256, 256), (256, 744, 64, 128, 0), (200, 520, 72, 256, 128),
+])
+def test_output_sector_offsets_and_strides(cuda_device, mode, c_off, ld_pad, m, n, k, tile_n, tile_m):
+    """C's rows starting 16 bytes into a 32-byte sector, or a leading
+    dimension that is not a multiple of 16 elements: every element
+    bit-identical to the call with a packed C, faults found as the oracle
+    finds them, and nothing written outside C (the bulk stores' boxes and the
+    plain stores of partial chunks both honour the view)."""
+    a, w, b = seeded(m, n, k, 21, bias=True)
+    ad, wd, bd = a.to(cuda_device), w.to(cuda_device), b.to(cuda_device)
+    acc = f32(a).astype(np.float64) @ f32(w).astype(np.float64).T
+    faults = [] if mode == N.MODE_OFF else O.seeded_fault_positions(m, n, 3, m + n)
+    # one fault among the first columns of the second tile column
+    if faults and tile_n:
+        faults[0] = (faults[0][0], (tile_n - 8) + 5)
+    delta = float(256.0 * np.abs(acc).max())
+    inj = [(i, j, delta) for i, j in faults] or None
+    ref_c, ref_rep = ops.abft_gemm(ad, wd, bd, mode=mode, tile_n=tile_n, tile_m=tile_m, inject=inj)
+    flat, c = _strided_out(m, n, c_off, ld_pad, cuda_device)
+    _, rep = ops.abft_gemm(ad, wd, bd, mode=mode, tile_n=tile_n, tile_m=tile_m, inject=inj, out=c)
+    torch.cuda.synchronize()
+    # nothing outside the view changed
+    mask = torch.ones_like(flat, dtype=torch.bool)
+    mask[c_off:c_off + m * (n + ld_pad)].view(m, n + ld_pad)[:, :n] = False
+    assert bool((flat[mask] == 7.0).all())
+    assert torch.equal(c, ref_c)
+    ref = acc + f32(b)[None, :]
+    assert max_rel_err(f32(c), ref) <= OUT_TOL
+    if mode == N.MODE_OFF:
+        assert rep is None
+        return
+    r = rep.read()
+    orc = O.rowcheck_gemm(f32(a), f32(w), f32(b), tile_n=r.tile_n, inject=inj)
+    assert sorted((x.row, x.col, x.flags) for x in r.records) == orc.records
+    assert r.coords() == sorted(faults) and r.n_corrected == len(faults)
+    assert sorted((x.row, x.col, x.flags) for x in ref_rep.read().records) == orc.records
