@@ -65,3 +65,30 @@ def test_plan_few_rows_and_empty(cuda_device):
     assert all(v == 0 for v in ops.gemm_plan(0, 4096, 4096, device=cuda_device).values())
     with pytest.raises(N.AbftError):
         ops.gemm_plan(64, 100, 64, device=cuda_device)  # N % 8
+
+
+def test_plan_batched_and_n_major_right_operand(cuda_device):
+    """Batched products count every batch's tiles, and an N-major right
+    operand (torch.bmm's mat2) needs its K-major copy in the workspace: the
+    plan's workspace is what abft_gemm_workspace_bytes asks for."""
+    import ctypes
+
+    one = ops.gemm_plan(1024, 1024, 128, tile_n=256, tile_m=256, device=cuda_device)
+    four = ops.gemm_plan(1024, 1024, 128, batch=4, tile_n=256, tile_m=256, device=cuda_device)
+    assert four["tiles"] == 4 * one["tiles"] and four["tile_n"] == one["tile_n"]
+    L = N.lib()
+    args = N.GemmArgs()
+    fake = 1 << 20
+    args.A = args.B = args.C = args.report = fake
+    args.M, args.N, args.K = 1024, 1024, 128
+    args.lda, args.ldb, args.ldc = 128, 1024, 1024
+    args.mode, args.report_capacity, args.thr_scale = CHK, 16, 1e-3
+    args.batch, args.b_kn = 4, 1
+    args.tile_n, args.tile_m = 256, 256
+    args.stride_a, args.stride_b, args.stride_c = 1024 * 128, 128 * 1024, 1024 * 1024
+    info = N.PlanInfo()
+    with torch.cuda.device(cuda_device):
+        N.check("abft_gemm_plan", L.abft_gemm_plan(ctypes.byref(args), ctypes.byref(info)))
+        ws = int(L.abft_gemm_workspace_bytes(ctypes.byref(args)))
+    assert info.workspace_bytes == ws >= 4 * 1024 * 128 * 2  # the K-major copy of B at least
+    assert info.tiles == four["tiles"]
