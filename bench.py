@@ -545,6 +545,62 @@ def qwen_prefill_point(reps, warmup, decode_steps=0, cpu_seconds=0.0, dtype="bf1
                                       "abft_overhead_vs_torch_pct": 100.0 * (d_chk / d_torch - 1.0),
                                       "note": "after a 512-token prefill into a KV cache; every linear at M = 1 "
                                               "(operands swapped: weight on the MMA's 128-row side)"}
+
+        def graph_decode(inj):
+            """One decode step captured as a CUDA graph (position on the
+            device, attention over the whole cache, masked), replayed
+            ``decode_steps`` times; with an injector, each replay's reports
+            are read and recorded before the next step."""
+            t_max = tokens + decode_steps + 8
+            caches = model.new_caches(t_max)
+            pos = torch.full((), tokens, dtype=torch.long, device=dev)
+            nxt = ids[-1:].clone()
+            ctx = inj if inj is not None else contextlib.nullcontext()
+            with torch.inference_mode(), ctx:
+                model(ids, caches, 0)
+                s = torch.cuda.Stream()
+                s.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(s):
+                    for _ in range(3):
+                        model(nxt, caches, pos)
+                torch.cuda.current_stream().wait_stream(s)
+                g = torch.cuda.CUDAGraph()
+                cap = inj.capture(g) if inj is not None else torch.cuda.graph(g)
+                with cap as checks:
+                    model(nxt, caches, pos)
+                    pos.add_(1)
+                pos.fill_(tokens)
+                for _ in range(3):
+                    g.replay()
+                    if inj is not None:
+                        checks.record()
+                pos.fill_(tokens)
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(decode_steps):
+                    g.replay()
+                    if inj is not None:
+                        checks.record()
+                e1.record()
+                torch.cuda.synchronize()
+                ms = e0.elapsed_time(e1) / decode_steps
+                n_checked = len(checks) if inj is not None else 0
+            del g
+            return ms, n_checked
+
+        gd_torch, _ = graph_decode(None)
+        gd_off, _ = graph_decode(inj_off)
+        before = stats_chk.export_summary()["abft"]["faults"]["detected_total"]
+        gd_chk, n_checked = graph_decode(inj_chk)
+        res["decode_graph_ms_per_token"] = {
+            "torch": gd_torch, "unchecked": gd_off, "abft": gd_chk,
+            "abft_overhead_vs_torch_pct": 100.0 * (gd_chk / gd_torch - 1.0),
+            "checked_linears_per_step": n_checked,
+            "clean_detections": stats_chk.export_summary()["abft"]["faults"]["detected_total"] - before,
+            "note": "one decode step per CUDA graph replay (fixed shapes: position on the device, attention over "
+                    f"the {tokens + decode_steps + 8}-slot cache, masked), the same for all three legs; "
+                    "ABFT reads and records every step's reports before the next replay"}
     if cpu_seconds > 0:
         res["cpu_baseline"] = cpu_model_baseline(cfg, tokens, cpu_seconds)
     linear_flops = 0.0

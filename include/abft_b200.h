@@ -30,6 +30,14 @@
  *     throws.  abft_status_string() turns a code into text.
  *   - Calls are reentrant: distinct calls on distinct buffers may run
  *     concurrently on different streams.
+ *   - abft_gemm_bf16 / abft_gemm and abft_check_only may be captured in a
+ *     CUDA graph. Under stream capture the fused GEMM adds two memset nodes
+ *     ahead of its kernel (the stream-K flags in the workspace and the
+ *     report's launch_tag), because a replay reuses the launch tag frozen
+ *     in the kernel node; every replay then writes a fresh report. The
+ *     caller keeps the workspace, report and operands alive for as long as
+ *     the graph may replay, and does not overlap replays with other calls
+ *     that use the same workspace.
  */
 #ifndef ABFT_B200_H_
 #define ABFT_B200_H_

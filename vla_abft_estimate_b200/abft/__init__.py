@@ -5,7 +5,7 @@ Same exported names; the checks run on libabft_b200.so.
 from .checkers import (AbftChecker, CheapSumChecker, FusedB200Checker, OpMeta, RowColChecker, UnsupportedOperand,
                        flatten_to_2d_for_mm)
 from .config import AbftConfig
-from .injector import AbftInjector, WeightChecksumCache, result_from_report
+from .injector import AbftInjector, CapturedChecks, WeightChecksumCache, result_from_report
 from .stats import AbftStatsCollector, CheckResult, percentile, summarize_ms
 
 __all__ = [
@@ -15,6 +15,7 @@ __all__ = [
     "AbftStatsCollector",
     "CheapSumChecker",
     # additions
+    "CapturedChecks",
     "CheckResult",
     "FusedB200Checker",
     "OpMeta",

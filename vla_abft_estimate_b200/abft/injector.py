@@ -33,10 +33,14 @@ the op (:58-75), then the sampling coin inside the check gate (:53-56,
 Reports of fused calls can be deferred (``defer_reports=True``): the fault
 report stays on the device and is read at ``flush()`` (called on exit)
 instead of forcing a device->host sync per GEMM like the reference (:103).
+
+``capture(graph)`` captures a forward's calls, checks included, in a CUDA
+graph; the returned ``CapturedChecks`` records each replay's reports.
 """
 from __future__ import annotations
 
 import random
+import warnings
 import weakref
 from contextlib import AbstractContextManager
 from typing import Any, Callable, List, Optional, Tuple
@@ -195,6 +199,15 @@ class _ReportArena:
         return _Slot(self.capacity, ptr)
 
     def drain(self) -> List[CheckResult]:
+        """``read()``, then the slots are free for the next forward."""
+        results = self.read()
+        # keep the first chunk for the next forward
+        self.chunks = self.chunks[:1]
+        self.base = self.chunks[0].data_ptr() if self.chunks else 0
+        self.used = 0
+        return results
+
+    def read(self) -> List[CheckResult]:
         """The CheckResult of every used slot, in order. A report without
         faults always gives the same clean result, so only the slots whose
         fault count (header word 1) is non-zero are parsed."""
@@ -210,10 +223,6 @@ class _ReportArena:
                 rep = N.FaultReport.from_bytes(host[j].tobytes())
                 self.suspect |= rep.suspect
                 results.append(result_from_report(rep))
-        # keep the first chunk for the next forward
-        self.chunks = self.chunks[:1]
-        self.base = self.chunks[0].data_ptr() if self.chunks else 0
-        self.used = 0
         return results
 
 
@@ -249,6 +258,9 @@ class AbftInjector(AbstractContextManager):
         self._pending: List[Tuple[int, str, str, Any, bool, Any]] = []
         self._arenas: dict = {}
         self._tile_n: dict = {}
+        # checksum blocks read by the calls of a CUDA-graph capture in
+        # progress (None outside one): the graph keeps their addresses
+        self._graph_keep: Optional[list] = None
 
     # ------------------------------------------------------------------ context
     def __enter__(self) -> "AbftInjector":
@@ -287,6 +299,11 @@ class AbftInjector(AbstractContextManager):
             self.checksums.clear()
             for arena in self._arenas.values():
                 arena.suspect = False
+        self._record_pending(pending, reports)
+
+    def _record_pending(self, pending: list, reports: dict) -> None:
+        """Record deferred calls in order; ``reports`` maps a device to an
+        iterator over its arena's results."""
         keys: dict = {}
         saved = self.stats.current_phase
         try:
@@ -316,6 +333,32 @@ class AbftInjector(AbstractContextManager):
             if gates[bi]:
                 self.stats.record_check(op_name=op_name, shape_key=shape_key,
                                         result=result_from_report(rep.batch_view(bi, rows)), injected=injected)
+
+    # ------------------------------------------------------------ CUDA graphs
+    def capture(self, graph: "torch.cuda.CUDAGraph", **graph_kwargs: Any) -> "_GraphCapture":
+        """Context manager capturing the calls made inside it into ``graph``
+        (``torch.cuda.graph(graph, **graph_kwargs)``), checks included. It
+        yields a ``CapturedChecks``; after each ``graph.replay()`` its
+        ``record()`` reads that replay's reports into the stats::
+
+            with injector:
+                model(x)                    # eager first: encodes the checksums
+                g = torch.cuda.CUDAGraph()
+                with injector.capture(g) as checks:
+                    y = model(x)
+                for _ in range(steps):
+                    g.replay()
+                    checks.record()
+
+        A replay repeats the captured decisions, so configurations that
+        draw from the random stream per call are refused: fault injection
+        and ``sample_rate`` < 1 (the reference's per-call coins,
+        injector.py:53-75), and ``dump_file``, which copies operands to the
+        host. Reports are deferred during the capture whatever
+        ``defer_reports`` says. The weights' checksum blocks are captured as
+        they are: after a weight update, capture again (a replay that finds
+        them stale reports it, and ``record()`` warns)."""
+        return _GraphCapture(self, graph, graph_kwargs)
 
     # -------------------------------------------------------- reference gates
     def _sample(self) -> bool:
@@ -500,6 +543,8 @@ class AbftInjector(AbstractContextManager):
         # itself, so the weight's checksum block is not needed
         swapped = m <= 64 and n >= 2 * m
         cks = self.checksums.get(weight, tile_n) if check and not swapped and real is None else None
+        if cks is not None and self._graph_keep is not None:
+            self._graph_keep.append(cks)
         inject = [(idx // n_key, idx % n_key, float(self.cfg.inject_magnitude))] if injected else None
         rep = None
         if check:
@@ -678,3 +723,90 @@ class AbftInjector(AbstractContextManager):
             return out2
 
         return wrapped
+
+
+class CapturedChecks:
+    """The checks of one captured graph (``AbftInjector.capture``).
+
+    ``record()`` after a replay copies the reports that replay wrote to the
+    host (one copy per arena chunk and per batched call) and records them in
+    the injector's stats in call order, as ``flush()`` does for an eager
+    forward. The object keeps the report slots and checksum blocks the graph
+    addresses alive."""
+
+    def __init__(self, injector: AbftInjector):
+        self._inj = injector
+        self._pending: list = []
+        self._arenas: dict = {}
+        self._keep: list = []
+        self.replays_recorded = 0
+        self.stale_checksums = False
+
+    def _adopt(self, pending: list, arenas: dict, keep: Optional[list]) -> None:
+        self._pending, self._arenas, self._keep = pending, arenas, keep or []
+
+    def __len__(self) -> int:
+        """Checked calls in the graph."""
+        return len(self._pending)
+
+    def record(self) -> None:
+        """Record the reports of the latest replay (synchronises with it)."""
+        if not self._pending:
+            return
+        reports = {dev: iter(arena.read()) for dev, arena in self._arenas.items()}
+        if any(arena.suspect for arena in self._arenas.values()):
+            self.stale_checksums = True
+            for arena in self._arenas.values():
+                arena.suspect = False
+            warnings.warn("a replay found checksum blocks that no longer match their weights (a weight was "
+                          "written after the capture): capture the graph again", RuntimeWarning, stacklevel=2)
+        self._inj._record_pending(self._pending, reports)
+        self.replays_recorded += 1
+
+
+class _GraphCapture:
+    """``AbftInjector.capture``: swaps in empty deferred-report state for the
+    capture, and hands what the captured calls queued to a CapturedChecks."""
+
+    def __init__(self, injector: AbftInjector, graph: "torch.cuda.CUDAGraph", graph_kwargs: dict):
+        self._inj = injector
+        self._graph = graph
+        self._kwargs = graph_kwargs
+        self._ctx = None
+        self._saved = None
+        self.checks = CapturedChecks(injector)
+
+    def __enter__(self) -> CapturedChecks:
+        inj, cfg = self._inj, self._inj.cfg
+        if cfg.inject_fault and cfg.inject_probability > 0.0:
+            raise RuntimeError("fault injection draws per call from the random stream, which a graph replay "
+                               "cannot repeat: capture with inject_fault off")
+        if cfg.sample_rate < 1.0:
+            raise RuntimeError("sample_rate < 1 draws a coin per call, which a graph replay cannot repeat")
+        if cfg.dump_file:
+            raise RuntimeError("dump_file copies operands to the host, which a graph cannot capture")
+        inj.flush()  # eager calls' reports first
+        self._saved = (inj._pending, inj._arenas, inj.defer_reports)
+        inj._pending, inj._arenas, inj.defer_reports = [], {}, True
+        inj._graph_keep = []
+        self._ctx = torch.cuda.graph(self._graph, **self._kwargs)
+        try:
+            self._ctx.__enter__()
+        except BaseException:
+            self._restore()
+            raise
+        return self.checks
+
+    def _restore(self) -> None:
+        inj = self._inj
+        inj._pending, inj._arenas, inj.defer_reports = self._saved
+        inj._graph_keep = None
+
+    def __exit__(self, exc_type, exc, tb) -> bool:
+        try:
+            self._ctx.__exit__(exc_type, exc, tb)
+        finally:
+            inj = self._inj
+            self.checks._adopt(inj._pending, inj._arenas, inj._graph_keep)
+            self._restore()
+        return False

@@ -1098,6 +1098,23 @@ int abft_gemm_bf16(const abft_gemm_args* args, void* stream) {
                                   const_cast<void*>(V), stream);
     if (rc != ABFT_OK) return rc;
   }
+  // A CUDA graph replays this launch with the nonce frozen in its kernel
+  // node, so the stream-K flags and the report tag that the previous replay
+  // left would already match it: a finisher would fold a stale partial and
+  // report atomics could run ahead of the header reset. Under stream capture
+  // both are cleared in the graph, ahead of the kernel. (An eager launch
+  // draws a fresh nonce and needs no clearing.)
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &cap) != cudaSuccess) return launch_status(), ABFT_ERR_CUDA;
+  if (cap != cudaStreamCaptureStatusNone) {
+    if (p.report != nullptr &&
+        cudaMemsetAsync(&p.report->launch_tag, 0, sizeof(p.report->launch_tag), s) != cudaSuccess)
+      return launch_status(), ABFT_ERR_CUDA;
+    if (p.flags != nullptr &&
+        cudaMemsetAsync(p.flags, 0, static_cast<size_t>(ws.grid) * kEpiWarps * sizeof(unsigned long long), s) !=
+            cudaSuccess)
+      return launch_status(), ABFT_ERR_CUDA;
+  }
   rc = f16 ? launch_gemm_typed<true>(ws, check, dev, tmA, tmB, tmB2, tmV, tmBt, tmC, p, s)
            : launch_gemm_typed<false>(ws, check, dev, tmA, tmB, tmB2, tmV, tmBt, tmC, p, s);
   if (rc != ABFT_OK) return rc;

@@ -15,6 +15,12 @@ Functions
   check_only(a, b, c, bias, ...)         post-hoc check of an existing output
   wait_selftest()                        the bounded device waits giving up
                                          (failure detection, no fault)
+
+abft_gemm, abft_linear, abft_bmm and check_only may be captured in a CUDA
+graph (``torch.cuda.graph``): under capture the library clears its
+stream-K flags and the report's launch tag inside the graph, so every
+replay writes a fresh report, and the workspace a capture used is kept for
+the graph's replays.
 """
 from __future__ import annotations
 
@@ -100,6 +106,12 @@ def _device_index(device: Optional[torch.device]) -> int:
 
 _WORKSPACES: "collections.OrderedDict[tuple, torch.Tensor]" = collections.OrderedDict()
 _MAX_WORKSPACES = 64
+# Workspaces used while a CUDA graph was being captured, by address. A
+# graph's kernel nodes hold their addresses for every replay, so they are
+# never freed, even once the per-stream cache above replaces or evicts them.
+# (Replays must not overlap on the GPU with other fused calls on the capture
+# stream's workspace: like those calls, they share it.)
+_GRAPH_HELD: dict = {}
 
 
 def _workspace(device: torch.device, nbytes: int, stream: Optional[int] = None) -> torch.Tensor:
@@ -156,6 +168,9 @@ def _run_gemm(args: N.GemmArgs, dev: torch.device, key: tuple) -> None:
         ws = _workspace(dev, ws_bytes, stream)
         args.workspace = ws.data_ptr()
         args.workspace_bytes = ws.numel()
+        if torch._C._cuda_isCurrentStreamCapturing():
+            # the captured kernel nodes keep this address for every replay
+            _GRAPH_HELD[ws.data_ptr()] = ws
     N.check("abft_gemm", L.abft_gemm(ctypes.byref(args), ctypes.c_void_p(stream)))
 
 
@@ -248,8 +263,12 @@ def encode_weight(weight: torch.Tensor, tile_n: int) -> torch.Tensor:
     return out
 
 
-class _Inject:
-    """Device copy of a debug fault list [(row, col, delta), ...]."""
+class DeviceFaults:
+    """Device copy of a debug fault list [(row, col, delta), ...] for the
+    ``inject`` argument of the fused calls. A plain list is copied to the
+    device on every call; build this once instead to reuse the copy, or
+    before a CUDA graph capture, whose replays then inject the same faults
+    (the copy is made here, outside the capture)."""
 
     def __init__(self, faults: Sequence[Tuple[int, int, float]], device: torch.device):
         if len(faults) > N.MAX_INJECT:
@@ -293,7 +312,8 @@ def abft_gemm(
     2 always) computes out^T = weight a^T instead, for few rows of ``a``:
     the weight then streams through the MMA's 128-row side, the checksums
     come from ``a`` per call and fault records keep ``out``'s coordinates.
-    ``inject`` adds debug faults to the fp32 accumulator.
+    ``inject`` adds debug faults to the fp32 accumulator (a list of
+    (row, col, delta), or a ``DeviceFaults`` built ahead).
     Returns the output and the report buffer (None when mode == MODE_OFF).
     """
     _gemm_dtype(a)
@@ -340,7 +360,7 @@ def _gemm_launch(a, weight, bias, out, m, n, k, mode, tile_n, tile_m, swap_ab, t
     leading dimensions read from 2-D ``a`` / ``out``, for callers that pass
     contiguous tensors of any rank holding m rows."""
     dev = a.device
-    inj = _Inject(inject, dev) if inject else None
+    inj = inject if isinstance(inject, DeviceFaults) else (DeviceFaults(inject, dev) if inject else None)
     args = N.GemmArgs()
     args.A, args.B, args.C, args.bias = _ptr(a), _ptr(weight), _ptr(out), _ptr(bias)
     args.M, args.N, args.K = m, n, k
@@ -531,7 +551,7 @@ def abft_bmm(
 def _bmm_call(a, bmat, b_kn, bias, out, bsz, m, n, k, mode, tile_n, tile_m, swap_ab, thr_scale, thr_abs, inject,
               report, num_sms):
     dev = a.device
-    inj = _Inject(inject, dev) if inject else None
+    inj = inject if isinstance(inject, DeviceFaults) else (DeviceFaults(inject, dev) if inject else None)
     lda, sa = _mat_layout(a)
     ldb, sb = _mat_layout(bmat)
     args = N.GemmArgs()

@@ -29,6 +29,10 @@ def build_qwen2(cfg, device, seed=0, dtype=None):
     """Qwen2-style decoder: RMSNorm, fused QKV (with bias) + RoPE + GQA
     attention (SDPA), SwiGLU MLP with fused gate+up, tied-free lm_head.
     Every projection is an nn.Linear, so F.linear hooks see all of them.
+    ``model(ids, caches, pos)`` appends to KV caches from position ``pos``;
+    a 0-d device tensor ``pos`` keeps every shape fixed (attention over the
+    whole cache, later positions masked), so a decode step can be captured
+    in a CUDA graph and replayed as ``pos`` advances.
     ``dtype``: bfloat16 (default) or float16, the reference driver's
     ``--dtype`` (qwen_abft_benchmark.py:26)."""
     import torch
@@ -65,11 +69,21 @@ def build_qwen2(cfg, device, seed=0, dtype=None):
             q = rope(q.view(t, nh, hd), cos, sin).transpose(0, 1)
             k = rope(k.view(t, nkv, hd), cos, sin).transpose(0, 1)
             v = v.view(t, nkv, hd).transpose(0, 1)
-            if cache is not None:  # [2, nkv, T_max, hd]: keys and values of positions < pos + t
+            mask = None
+            if cache is not None and torch.is_tensor(pos):
+                # fixed shapes for a CUDA graph: pos lives on the device, and
+                # attention runs over the whole cache with later positions masked
+                at = pos + torch.arange(t, device=x.device)
+                cache[0].index_copy_(1, at, k)
+                cache[1].index_copy_(1, at, v)
+                k, v = cache[0], cache[1]
+                mask = torch.arange(cache.shape[2], device=x.device)[None, :] <= at[:, None]
+            elif cache is not None:  # [2, nkv, T_max, hd]: keys and values of positions < pos + t
                 cache[0, :, pos:pos + t] = k
                 cache[1, :, pos:pos + t] = v
                 k, v = cache[0, :, :pos + t], cache[1, :, :pos + t]
-            a = F.scaled_dot_product_attention(q, k, v, is_causal=(t > 1), enable_gqa=True)
+            a = F.scaled_dot_product_attention(q, k, v, attn_mask=mask, is_causal=(t > 1 and mask is None),
+                                               enable_gqa=True)
             x = x + self.o(a.transpose(0, 1).reshape(t, nh * hd))
             g, u = self.gate_up(self.ln2(x)).chunk(2, dim=-1)
             return x + self.down(F.silu(g) * u)
@@ -86,7 +100,9 @@ def build_qwen2(cfg, device, seed=0, dtype=None):
             t = ids.shape[0]
             hd = cfg["head_dim"]
             inv = 1.0 / (cfg["rope_theta"] ** (torch.arange(0, hd, 2, device=ids.device).float() / hd))
-            ang = torch.outer(torch.arange(pos, pos + t, device=ids.device).float(), inv)
+            at = pos + torch.arange(t, device=ids.device) if torch.is_tensor(pos) else \
+                torch.arange(pos, pos + t, device=ids.device)
+            ang = torch.outer(at.float(), inv)
             ang = torch.cat((ang, ang), dim=-1)[:, None, :]
             cos, sin = ang.cos().to(dt), ang.sin().to(dt)
             x = self.embed(ids)
