@@ -546,11 +546,14 @@ def qwen_prefill_point(reps, warmup, decode_steps=0, cpu_seconds=0.0, dtype="bf1
                                       "note": "after a 512-token prefill into a KV cache; every linear at M = 1 "
                                               "(operands swapped: weight on the MMA's 128-row side)"}
 
-        def graph_decode(inj):
+        def graph_decode(inj, record="sync"):
             """One decode step captured as a CUDA graph (position on the
             device, attention over the whole cache, masked), replayed
-            ``decode_steps`` times; with an injector, each replay's reports
-            are read and recorded before the next step."""
+            ``decode_steps`` times. With an injector, ``record`` says when
+            each replay's reports are read and recorded: "sync" before the
+            next replay, "overlap" one replay late from pinned copies (the
+            host work runs under the next replay), "end" only the last
+            replay's, after the timed loop (device cost alone)."""
             t_max = tokens + decode_steps + 8
             caches = model.new_caches(t_max)
             pos = torch.full((), tokens, dtype=torch.long, device=dev)
@@ -570,19 +573,26 @@ def qwen_prefill_point(reps, warmup, decode_steps=0, cpu_seconds=0.0, dtype="bf1
                     model(nxt, caches, pos)
                     pos.add_(1)
                 pos.fill_(tokens)
+                per_step = inj is not None and record != "end"
                 for _ in range(3):
                     g.replay()
-                    if inj is not None:
-                        checks.record()
+                    if per_step:
+                        checks.record(overlap=record == "overlap")
+                if per_step:
+                    checks.finish()
                 pos.fill_(tokens)
                 torch.cuda.synchronize()
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record()
                 for _ in range(decode_steps):
                     g.replay()
-                    if inj is not None:
-                        checks.record()
+                    if per_step:
+                        checks.record(overlap=record == "overlap")
                 e1.record()
+                if per_step:
+                    checks.finish()
+                elif inj is not None:
+                    checks.record()
                 torch.cuda.synchronize()
                 ms = e0.elapsed_time(e1) / decode_steps
                 n_checked = len(checks) if inj is not None else 0
@@ -593,14 +603,20 @@ def qwen_prefill_point(reps, warmup, decode_steps=0, cpu_seconds=0.0, dtype="bf1
         gd_off, _ = graph_decode(inj_off)
         before = stats_chk.export_summary()["abft"]["faults"]["detected_total"]
         gd_chk, n_checked = graph_decode(inj_chk)
+        gd_ovl, _ = graph_decode(inj_chk, "overlap")
+        gd_end, _ = graph_decode(inj_chk, "end")
         res["decode_graph_ms_per_token"] = {
-            "torch": gd_torch, "unchecked": gd_off, "abft": gd_chk,
+            "torch": gd_torch, "unchecked": gd_off, "abft": gd_chk, "abft_overlapped_reports": gd_ovl,
+            "abft_reports_after_last_step": gd_end,
             "abft_overhead_vs_torch_pct": 100.0 * (gd_chk / gd_torch - 1.0),
+            "abft_overlapped_overhead_vs_torch_pct": 100.0 * (gd_ovl / gd_torch - 1.0),
             "checked_linears_per_step": n_checked,
             "clean_detections": stats_chk.export_summary()["abft"]["faults"]["detected_total"] - before,
             "note": "one decode step per CUDA graph replay (fixed shapes: position on the device, attention over "
                     f"the {tokens + decode_steps + 8}-slot cache, masked), the same for all three legs; "
-                    "ABFT reads and records every step's reports before the next replay"}
+                    "abft: every step's reports read and recorded before the next replay; abft_overlapped_reports: "
+                    "recorded one step late from pinned copies queued behind each replay (record(overlap=True)), "
+                    "the host work under the next replay; abft_reports_after_last_step: device cost alone"}
     if cpu_seconds > 0:
         res["cpu_baseline"] = cpu_model_baseline(cfg, tokens, cpu_seconds)
     linear_flops = 0.0

@@ -252,3 +252,50 @@ def test_injector_capture_flags_a_weight_written_after_capture(cuda_device):
         inj.flush()
         assert torch.equal(logits, eager) and not torch.equal(logits, good)
     del g
+
+
+def test_injector_capture_overlapped_recording(cuda_device):
+    """record(overlap=True) records each replay one call late, from pinned
+    copies queued behind it; the counts match synchronous recording, and a
+    stale checksum block is still reported (a non-clean report parsed from
+    the host copy)."""
+    import torch.nn.functional as F
+
+    w = _randn((1024, 512), 21, cuda_device, scale=512 ** -0.5)
+    bm = _randn((4, 256, 384), 22, cuda_device, scale=256 ** -0.5)
+    x_static = torch.zeros(192, 512, device=cuda_device, dtype=torch.bfloat16)
+    a_static = torch.zeros(4, 128, 256, device=cuda_device, dtype=torch.bfloat16)
+
+    def fwd():
+        return F.linear(x_static, w), torch.bmm(a_static, bm)
+
+    inj, stats = _injector()
+    with torch.inference_mode(), inj:
+        fwd()
+        g = torch.cuda.CUDAGraph()
+        with inj.capture(g) as checks:
+            y, z = fwd()
+        assert len(checks) == 2  # the linear, and the bmm's one launch
+        for seed in range(5):
+            x = _randn((192, 512), 30 + seed, cuda_device)
+            a = _randn((4, 128, 256), 40 + seed, cuda_device)
+            x_static.copy_(x)
+            a_static.copy_(a)
+            g.replay()
+            checks.record(overlap=True)
+            assert checks.replays_recorded == seed  # one replay behind
+            assert torch.equal(y, F.linear(x, w)) and torch.equal(z, torch.bmm(a, bm))
+            inj.flush()
+        checks.finish()
+        assert checks.replays_recorded == 5
+        summ = stats.export_summary()["abft"]
+        # eager forward + 5 replays + 5 eager checks inside the loop, 1 linear + 4 batches each
+        assert summ["checks_total"] == 11 * 5 and summ["faults"]["detected_total"] == 0
+        w.mul_(2.0)
+        g.replay()
+        with warnings.catch_warnings(record=True) as caught:
+            warnings.simplefilter("always")
+            checks.record(overlap=True)
+            checks.finish()
+        assert checks.stale_checksums and any("capture the graph again" in str(m.message) for m in caught)
+    del g

@@ -207,14 +207,20 @@ class _ReportArena:
         self.used = 0
         return results
 
-    def read(self) -> List[CheckResult]:
-        """The CheckResult of every used slot, in order. A report without
+    def used_views(self) -> List[torch.Tensor]:
+        """The used bytes of each chunk (device tensors), in order."""
+        return [chunk[: (self.slots if i < len(self.chunks) - 1 else self.used) * self.slot_bytes]
+                for i, chunk in enumerate(self.chunks)]
+
+    def read(self, host_chunks: Optional[List[np.ndarray]] = None) -> List[CheckResult]:
+        """The CheckResult of every used slot, in order (from ``host_chunks``,
+        host copies of ``used_views()``, when given). A report without
         faults always gives the same clean result, so only the slots whose
         fault count (header word 1) is non-zero are parsed."""
         results: List[CheckResult] = []
-        for i, chunk in enumerate(self.chunks):
-            n = self.slots if i < len(self.chunks) - 1 else self.used
-            host = chunk[: n * self.slot_bytes].cpu().numpy().reshape(n, self.slot_bytes)
+        for i, view in enumerate(self.used_views()):
+            n = view.numel() // self.slot_bytes
+            host = (view.cpu().numpy() if host_chunks is None else host_chunks[i]).reshape(n, self.slot_bytes)
             n_faults = host[:, 4:8].copy().view(np.uint32)[:, 0]
             for j in range(n):
                 if n_faults[j] == 0:
@@ -301,9 +307,14 @@ class AbftInjector(AbstractContextManager):
                 arena.suspect = False
         self._record_pending(pending, reports)
 
-    def _record_pending(self, pending: list, reports: dict) -> None:
+    def _record_pending(self, pending: list, reports: dict, reads: Optional[dict] = None) -> None:
         """Record deferred calls in order; ``reports`` maps a device to an
-        iterator over its arena's results."""
+        iterator over its arena's results, ``reads`` (optional) the id of a
+        batched or post-hoc report buffer to its host copy."""
+
+        def read(rb):
+            return rb.read() if reads is None else reads[id(rb)]
+
         keys: dict = {}
         saved = self.stats.current_phase
         try:
@@ -320,10 +331,10 @@ class AbftInjector(AbstractContextManager):
                                             injected=injected)
                 elif isinstance(batched, _DeferredCheck):
                     self.stats.record_check(op_name=op_name, shape_key=shape_key,
-                                            result=batched.checker.result(batched.report.read()), injected=injected)
+                                            result=batched.checker.result(read(batched.report)), injected=injected)
                 else:
                     rb, nb, rows, gates = batched
-                    self._record_batches(op_name, shape_key, rb.read(), nb, rows, gates, injected)
+                    self._record_batches(op_name, shape_key, read(rb), nb, rows, gates, injected)
         finally:
             self.stats.current_phase = saved
 
@@ -741,6 +752,11 @@ class CapturedChecks:
         self._keep: list = []
         self.replays_recorded = 0
         self.stale_checksums = False
+        # overlapped recording: two sets of pinned host copies of every
+        # report the graph writes, the set in flight and its event
+        self._host_sets: List[Optional[tuple]] = [None, None]
+        self._next_set = 0
+        self._in_flight: Optional[Tuple[tuple, Any]] = None
 
     def _adopt(self, pending: list, arenas: dict, keep: Optional[list]) -> None:
         self._pending, self._arenas, self._keep = pending, arenas, keep or []
@@ -749,18 +765,77 @@ class CapturedChecks:
         """Checked calls in the graph."""
         return len(self._pending)
 
-    def record(self) -> None:
-        """Record the reports of the latest replay (synchronises with it)."""
+    def record(self, overlap: bool = False) -> None:
+        """Record the reports of the latest replay.
+
+        By default this waits for the replay. With ``overlap=True`` it
+        queues a copy of the reports into pinned host memory on the current
+        stream (behind the replay) and records the copy that the previous
+        call queued instead, so the host work runs while the GPU runs the
+        next replay; ``finish()`` records the last copy. Replays and these
+        calls must then alternate on one stream."""
         if not self._pending:
             return
-        reports = {dev: iter(arena.read()) for dev, arena in self._arenas.items()}
+        if not overlap:
+            self.finish()
+            self._record({dev: iter(arena.read()) for dev, arena in self._arenas.items()}, None)
+            return
+        host = self._host_set()
+        stream = torch.cuda.current_stream()
+        for (dst, src) in zip(host[0], [v for a in self._arenas.values() for v in a.used_views()]):
+            dst.copy_(src, non_blocking=True)
+        for rb, dst in host[1].items():
+            dst.copy_(rb.tensor, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(stream)
+        prev, self._in_flight = self._in_flight, (host, ev)
+        if prev is not None:
+            self._record_copy(*prev)
+
+    def finish(self) -> None:
+        """Record the copy the last overlapped ``record()`` queued, if any."""
+        prev, self._in_flight = self._in_flight, None
+        if prev is not None:
+            self._record_copy(*prev)
+
+    def _host_set(self) -> tuple:
+        """The next of two sets of pinned buffers: one per arena chunk view
+        (in ``_arenas`` order) and one per batched or post-hoc report."""
+        i = self._next_set
+        self._next_set ^= 1
+        if self._host_sets[i] is None:
+            chunks = [torch.empty(v.numel(), dtype=torch.uint8, pin_memory=True)
+                      for a in self._arenas.values() for v in a.used_views()]
+            rbs = {}
+            for entry in self._pending:
+                batched = entry[5]
+                rb = batched.report if isinstance(batched, _DeferredCheck) else (
+                    batched[0] if isinstance(batched, tuple) else None)
+                if rb is not None:
+                    rbs[rb] = torch.empty(rb.tensor.numel(), dtype=torch.uint8, pin_memory=True)
+            self._host_sets[i] = (chunks, rbs)
+        return self._host_sets[i]
+
+    def _record_copy(self, host: tuple, ev: Any) -> None:
+        ev.synchronize()
+        chunks, rbs = host
+        arrays = [c.numpy() for c in chunks]
+        reports, at = {}, 0
+        for dev, arena in self._arenas.items():
+            n = len(arena.chunks)
+            reports[dev] = iter(arena.read(arrays[at:at + n]))
+            at += n
+        reads = {id(rb): N.FaultReport.from_bytes(t.numpy().tobytes()) for rb, t in rbs.items()}
+        self._record(reports, reads)
+
+    def _record(self, reports: dict, reads: Optional[dict]) -> None:
         if any(arena.suspect for arena in self._arenas.values()):
             self.stale_checksums = True
             for arena in self._arenas.values():
                 arena.suspect = False
             warnings.warn("a replay found checksum blocks that no longer match their weights (a weight was "
                           "written after the capture): capture the graph again", RuntimeWarning, stacklevel=2)
-        self._inj._record_pending(self._pending, reports)
+        self._inj._record_pending(self._pending, reports, reads)
         self.replays_recorded += 1
 
 
