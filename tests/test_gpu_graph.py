@@ -299,3 +299,36 @@ def test_injector_capture_overlapped_recording(cuda_device):
             checks.finish()
         assert checks.stale_checksums and any("capture the graph again" in str(m.message) for m in caught)
     del g
+
+
+def test_injector_capture_vla_forward(cuda_device):
+    """The CogACT-style VLA (2 ViT / SigLIP layers, 2 decoder layers, the
+    full DiT-B head over 10 denoising steps, its 7-wide action projections
+    on zero-padded copies) captured as one graph through the injector:
+    every replay equals the eager checked forward and records as many
+    checks."""
+    from vla_abft_estimate_b200 import workloads as W
+
+    cfg = {k: (dict(v) if isinstance(v, dict) else v) for k, v in W.COGACT.items()}
+    cfg["vit"]["layers"] = cfg["siglip"]["layers"] = 2
+    cfg["llm"]["layers"] = 2
+    model = W.build_cogact(cfg, cuda_device)
+    gen = torch.Generator(device=cuda_device).manual_seed(6)
+    img = torch.randn(1, 3, 224, 224, device=cuda_device, generator=gen).bfloat16()
+    text = torch.randint(0, cfg["vocab"], (cfg["text_tokens"],), device=cuda_device, generator=gen)
+    noise = torch.randn(cfg["action_tokens"], cfg["action_dim"], device=cuda_device, generator=gen).bfloat16()
+    inj, stats = _injector()
+    with torch.inference_mode(), inj:
+        eager = model(img, text, noise)
+        inj.flush()
+        per_forward = stats.export_summary()["abft"]["checks_total"]
+        g = torch.cuda.CUDAGraph()
+        with inj.capture(g) as checks:
+            out = model(img, text, noise)
+        for _ in range(2):
+            g.replay()
+            checks.record()
+            assert torch.equal(out, eager)
+        summ = stats.export_summary()["abft"]
+        assert summ["checks_total"] == 3 * per_forward and summ["faults"]["detected_total"] == 0
+    del g

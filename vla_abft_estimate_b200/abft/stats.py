@@ -81,6 +81,24 @@ def _entry_dict(e: tuple) -> Dict[str, Any]:
 _TOP_KEEP = 100  # the reference keeps the 100 largest |err| entries (stats.py:137-139)
 
 
+class CleanChecks:
+    """A fixed sequence of checks, given as (phase, op name, shape key),
+    whose results are all clean (no fault, zero error). Built once, it lets
+    ``AbftStatsCollector.record_clean`` record the whole sequence again and
+    again, as a replayed CUDA graph does, at the cost of its distinct keys
+    rather than one ``record_check`` per check."""
+
+    def __init__(self, calls: List[Tuple[str, str, str]]):
+        self.n = len(calls)
+        self.phase = Counter(p for p, _, _ in calls)
+        self.op = Counter(o for _, o, _ in calls)
+        self.shape = Counter((p, f"{o}:{k}") for p, o, k in calls)
+        self.entries = [(p, o, k, 0.0, 0.0, 0.0, 0.0) for p, o, k in calls]
+        self.first: Dict[str, tuple] = {}
+        for e in self.entries:
+            self.first.setdefault(f"{e[0]}|{e[1]}|{e[2]}", e)
+
+
 class AbftStatsCollector:
     """Per-phase / per-op / per-shape counters (stats.py:51-220)."""
 
@@ -127,6 +145,32 @@ class AbftStatsCollector:
 
     def set_phase(self, phase: str) -> None:
         self.current_phase = phase
+
+    def record_clean(self, checks: CleanChecks) -> None:
+        """``record_check`` of every check in ``checks`` with a clean result
+        (ok, zero errors, no fault), in order: the same counters, maxima,
+        kept entries and per-shape maxima, in bulk. (A zero error ties with
+        a zero maximum, so the maxima's metadata moves to the last entry only
+        while no error has been seen; the top list keeps the same entries
+        because a stable top-k of a concatenation does not depend on where
+        the list was trimmed in between.)"""
+        if not checks.n:
+            return
+        self.total_checks += checks.n
+        self.phase_checks.update(checks.phase)
+        self.op_checks.update(checks.op)
+        self.shape_checks.update(checks.shape)
+        last = checks.entries[-1]
+        if self.max_abs_err <= 0.0:
+            self._max_abs_meta = last
+        if self.max_rel_err <= 0.0:
+            self._max_rel_meta = last
+        self._top.extend(checks.entries)
+        if len(self._top) >= 2 * _TOP_KEEP:
+            self._trim_top()
+        for bucket, e in checks.first.items():
+            if bucket not in self._shape_max:
+                self._shape_max[bucket] = e
 
     def record_check(self, op_name: str, shape_key: str, result: CheckResult, injected: bool = False) -> None:
         phase = self.current_phase
