@@ -30,10 +30,14 @@
  *     throws.  abft_status_string() turns a code into text.
  *   - Calls are reentrant: distinct calls on distinct buffers may run
  *     concurrently on different streams.
+ *   - The fused GEMM kernel is launched with programmatic stream
+ *     serialization: its prologue may overlap the previous kernel on the
+ *     stream, and it reads or writes global memory only after that kernel
+ *     has completed (griddepcontrol.wait).
  *   - abft_gemm_bf16 / abft_gemm and abft_check_only may be captured in a
- *     CUDA graph. Under stream capture the fused GEMM adds two memset nodes
- *     ahead of its kernel (the stream-K flags in the workspace and the
- *     report's launch_tag), because a replay reuses the launch tag frozen
+ *     CUDA graph. Under stream capture the fused GEMM adds one small kernel
+ *     ahead of its own that clears the stream-K flags in the workspace and
+ *     the report's launch_tag, because a replay reuses the launch tag frozen
  *     in the kernel node; every replay then writes a fresh report. The
  *     caller keeps the workspace, report and operands alive for as long as
  *     the graph may replay, and does not overlap replays with other calls

@@ -665,21 +665,28 @@ int launch_gemm(int dev, int slot, const CUtensorMap& tmA, const CUtensorMap& tm
   int rc = ensure_smem_attr<BN, CHECK, PAIR, F16>(dev, slot);
   if (rc != ABFT_OK) return rc;
   constexpr size_t smem = GemmCfg<BN, CHECK, PAIR>::kSmemBytes;
-  if constexpr (!PAIR) {
-    abft_gemm_kernel<BN, CHECK, false, F16><<<grid, kThreads, smem, s>>>(tmA, tmB, tmB2, tmV, tmBt, tmC, p);
-  } else {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(grid));
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute at = pair_cluster_attr();
-    cfg.attrs = &at;
-    cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, abft_gemm_kernel<BN, CHECK, true, F16>, tmA, tmB, tmB2, tmV, tmBt, tmC, p) !=
-        cudaSuccess)
-      return launch_status(), ABFT_ERR_CUDA;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  // Programmatic serialization: the kernel's prologue (barriers, TMEM,
+  // tensor-map prefetch) may start before the previous kernel on the stream
+  // has finished; it waits (griddepcontrol.wait) before any global access.
+  // The kernel never signals its own dependents early, so the next kernel
+  // starts only once every CTA of this one has exited.
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  if constexpr (PAIR) {
+    at[1] = pair_cluster_attr();
+    cfg.numAttrs = 2;
   }
+  if (cudaLaunchKernelEx(&cfg, abft_gemm_kernel<BN, CHECK, PAIR, F16>, tmA, tmB, tmB2, tmV, tmBt, tmC, p) !=
+      cudaSuccess)
+    return launch_status(), ABFT_ERR_CUDA;
   return launch_status();
 }
 
@@ -1102,18 +1109,18 @@ int abft_gemm_bf16(const abft_gemm_args* args, void* stream) {
   // node, so the stream-K flags and the report tag that the previous replay
   // left would already match it: a finisher would fold a stale partial and
   // report atomics could run ahead of the header reset. Under stream capture
-  // both are cleared in the graph, ahead of the kernel. (An eager launch
-  // draws a fresh nonce and needs no clearing.)
+  // one small kernel clears both in the graph, ahead of the GEMM (a kernel,
+  // not memset nodes: one node, and the GEMM's griddepcontrol.wait covers
+  // it). An eager launch draws a fresh nonce and needs no clearing.
   cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
   if (cudaStreamIsCapturing(s, &cap) != cudaSuccess) return launch_status(), ABFT_ERR_CUDA;
-  if (cap != cudaStreamCaptureStatusNone) {
-    if (p.report != nullptr &&
-        cudaMemsetAsync(&p.report->launch_tag, 0, sizeof(p.report->launch_tag), s) != cudaSuccess)
-      return launch_status(), ABFT_ERR_CUDA;
-    if (p.flags != nullptr &&
-        cudaMemsetAsync(p.flags, 0, static_cast<size_t>(ws.grid) * kEpiWarps * sizeof(unsigned long long), s) !=
-            cudaSuccess)
-      return launch_status(), ABFT_ERR_CUDA;
+  if (cap != cudaStreamCaptureStatusNone && (p.report != nullptr || p.flags != nullptr)) {
+    const int nflags = p.flags != nullptr ? ws.grid * kEpiWarps : 0;
+    clear_launch_state_kernel<<<static_cast<unsigned>(cdiv(nflags > 0 ? nflags : 1, 256)), 256, 0, s>>>(
+        p.report != nullptr ? reinterpret_cast<unsigned long long*>(&p.report->launch_tag) : nullptr, p.flags,
+        nflags);
+    rc = launch_status();
+    if (rc != ABFT_OK) return rc;
   }
   rc = f16 ? launch_gemm_typed<true>(ws, check, dev, tmA, tmB, tmB2, tmV, tmBt, tmC, p, s)
            : launch_gemm_typed<false>(ws, check, dev, tmA, tmB, tmB2, tmV, tmBt, tmC, p, s);

@@ -244,6 +244,17 @@ __device__ __forceinline__ void kblock_checksums(const T* __restrict__ B, int64_
   }
 }
 
+// Under CUDA-graph capture, the fused GEMM's launch tag is frozen in its
+// node, so every replay must start from cleared state: the report's
+// launch_tag (when `tag` is set) and the `n` stream-K flags (when `flags`
+// is set) are zeroed here, one graph node ahead of the GEMM.
+__global__ void __launch_bounds__(256) clear_launch_state_kernel(unsigned long long* tag,
+                                                                 unsigned long long* flags, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (flags != nullptr && i < n) flags[i] = 0ull;
+  if (tag != nullptr && i == 0) *tag = 0ull;
+}
+
 // bf16 checksum block: one k-block of one tile per CTA.
 __global__ void __launch_bounds__(256) encode_weight_kernel(const __nv_bfloat16* __restrict__ B, int64_t ldb, int N,
                                                             int K, int bd, __nv_bfloat16* __restrict__ out,

@@ -635,12 +635,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     ndet[1] = 0u;
     fence_barrier_init();
   }
-  if (blockIdx.x == 0 && p.bcounts != nullptr) {
-    // Per-batch counters, zeroed before CTA 0 publishes the report header
-    // (other CTAs touch them only after report_ready).
-    for (int i = threadIdx.x; i < 4 * p.batch; i += kThreads) p.bcounts[i] = 0u;
-    __threadfence();
-  }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -662,6 +656,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Everything above touches only shared memory, TMEM and the tensor maps
+  // in parameter space, so it may overlap the previous kernel on the stream
+  // (the launch allows programmatic serialization). Global memory is read
+  // and written only after this wait.
+  griddep_wait();
+  if (blockIdx.x == 0 && p.bcounts != nullptr) {
+    // Per-batch counters, zeroed before CTA 0 publishes the report header
+    // (other CTAs touch them only after report_ready).
+    for (int i = threadIdx.x; i < 4 * p.batch; i += kThreads) p.bcounts[i] = 0u;
+    __threadfence();
+    __syncthreads();  // CTA 0 only (a uniform branch), before its header thread publishes the tag
+  }
   if (blockIdx.x == 0 && threadIdx.x == 32 * (kEpiWarp0 + kEpiWarps - 1) && p.report != nullptr) {
     // Reset the header, then publish this launch's tag: every other write to
     // the report waits for the tag (report_ready). An epilogue thread does

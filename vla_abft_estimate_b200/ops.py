@@ -18,7 +18,8 @@ Functions
 
 abft_gemm, abft_linear, abft_bmm and check_only may be captured in a CUDA
 graph (``torch.cuda.graph``): under capture the library clears its
-stream-K flags and the report's launch tag inside the graph, so every
+stream-K flags and the report's launch tag in the graph (one small kernel
+ahead of the GEMM), so every
 replay writes a fresh report, and the workspace a capture used is kept for
 the graph's replays.
 """
