@@ -828,8 +828,9 @@ def run_ours(args):
     if world == 1 and rank == 0 and not args.no_extras:
         # The other BASELINE metrics, measured in the same process: config 1
         # (one 512x4096x4096 protected GEMM), the largest square shape, and
-        # the Qwen2-7B prefill-512 tokens/s with every linear protected; plus
-        # the headline shape on fp16 operands.
+        # the Qwen2-7B prefill-512 tokens/s with every linear protected (and
+        # its decode steps, eager and as one CUDA graph per step); plus the
+        # headline shape on fp16 operands.
         flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
         it = max(args.steps, 10)
         extras["config1_512x4096x4096"] = gemm_point(512, 4096, 4096, it, flush)
@@ -837,7 +838,7 @@ def run_ours(args):
         extras["fp16_8192"] = gemm_point(8192, 8192, 8192, it, flush, dtype="f16")
         del flush
         torch.cuda.empty_cache()
-        extras["qwen2_7b_prefill512"] = qwen_prefill_point(reps=5, warmup=2)
+        extras["qwen2_7b_prefill512"] = qwen_prefill_point(reps=5, warmup=2, decode_steps=16)
 
     if rank == 0:
         flops_job = 2.0 * s * n_total * s
