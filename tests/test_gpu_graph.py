@@ -11,6 +11,9 @@ eager call on the same inputs bit for bit, report included:
 - the injector's ``capture()`` over a small decoder, for a prefill forward
   and a fixed-shape decode step. Each replay's reports are recorded, and a
   weight written after the capture is flagged as stale, not corrected.
+- the VLA forward as one graph, and overlapped report recording.
+The last test covers the programmatic dependent launch of the fused GEMM:
+a host->device copy queued right before it must still finish first.
 """
 import warnings
 
@@ -332,3 +335,26 @@ def test_injector_capture_vla_forward(cuda_device):
         summ = stats.export_summary()["abft"]
         assert summ["checks_total"] == 3 * per_forward and summ["faults"]["detected_total"] == 0
     del g
+
+
+def test_fused_call_right_after_host_copies_sees_the_copied_data(cuda_device):
+    """The fused GEMM launches with programmatic stream serialization; a
+    host->device copy queued just before it (no kernel in between) must
+    still complete before the kernel reads its operand."""
+    m, n, k = 512, 4096, 4096
+    w = _randn((n, k), 7, cuda_device, scale=k ** -0.5)
+    tile_n = ops.pick_tile_n(m, n, k, cuda_device)
+    cks = ops.encode_weight(w, tile_n)
+    hosts = [_randn((m, k), 50 + i, cuda_device).cpu().pin_memory() for i in range(4)]
+    refs = [ops.abft_gemm(h.to(cuda_device), w, checksums=cks, tile_n=tile_n)[0] for h in hosts]
+    x = torch.empty(m, k, device=cuda_device, dtype=torch.bfloat16)
+    outs = []
+    for rnd in range(3):
+        for h in hosts:
+            x.copy_(h, non_blocking=True)
+            y, rep = ops.abft_gemm(x, w, checksums=cks, tile_n=tile_n)
+            outs.append((y, rep))
+    torch.cuda.synchronize()
+    for i, (y, rep) in enumerate(outs):
+        assert torch.equal(y, refs[i % len(hosts)]), f"call {i} read a stale operand"
+        assert rep.read().n_faults == 0
