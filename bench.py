@@ -57,6 +57,9 @@ def parse_args():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--size", type=int, default=8192, help="M = K = per-GPU N")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--nvtx-enable", action="store_true",
+                    help="--model qwen2-7b: NVTX ranges prefill_len_<n> / decode_len_<n> around the timed work, as "
+                         "the reference driver marks them, and abft.<op> MxNxK around every hooked call")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the config-1, 16384^3 and Qwen2-7B prefill points of the default 1-GPU line")
     ap.add_argument("--sweep", action="store_true",
@@ -422,7 +425,28 @@ def gemm_point(m, n, k, iters, flush, seed=0, dtype="bf16"):
     return res
 
 
-def qwen_prefill_point(reps, warmup, decode_steps=0, cpu_seconds=0.0, dtype="bf16"):
+def _nvtx_range(enabled, name):
+    """An NVTX range when ``enabled`` (the reference driver's --nvtx-enable,
+    pytorch/qwen_abft_benchmark.py:120-127), else nothing."""
+    import contextlib
+
+    import torch
+
+    if not enabled:
+        return contextlib.nullcontext()
+
+    @contextlib.contextmanager
+    def rng():
+        torch.cuda.nvtx.range_push(name)
+        try:
+            yield
+        finally:
+            torch.cuda.nvtx.range_pop()
+
+    return rng()
+
+
+def qwen_prefill_point(reps, warmup, decode_steps=0, cpu_seconds=0.0, dtype="bf16", nvtx=False):
     """a Qwen2-7B-shaped decoder prefill of 512 tokens
     (batch 1, random init N(0, 0.02), random token ids) with every nn.Linear
     through AbftInjector's fused path (reports deferred to one read per
@@ -455,7 +479,7 @@ def qwen_prefill_point(reps, warmup, decode_steps=0, cpu_seconds=0.0, dtype="bf1
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 torch.cuda.synchronize()
                 e0.record()
-                with ctx:
+                with ctx, _nvtx_range(nvtx, f"prefill_len_{tokens}"):
                     out = model(ids)
                 e1.record()
                 torch.cuda.synchronize()
@@ -474,10 +498,10 @@ def qwen_prefill_point(reps, warmup, decode_steps=0, cpu_seconds=0.0, dtype="bf1
     # one injector per leg, reused across repetitions (its weight checksum
     # cache is what a serving process keeps)
     stats_chk = AbftStatsCollector()
-    cfg_chk = AbftConfig(enable=True, checker_backend="b200", detect_only=False)
+    cfg_chk = AbftConfig(enable=True, checker_backend="b200", detect_only=False, nvtx=nvtx)
     inj_chk = AbftInjector(cfg_chk, CheapSumChecker(cfg_chk), stats_chk, defer_reports=True)
     stats_off = AbftStatsCollector()
-    cfg_off = AbftConfig(enable=True, check_enable=False, checker_backend="b200")
+    cfg_off = AbftConfig(enable=True, check_enable=False, checker_backend="b200", nvtx=nvtx)
     inj_off = AbftInjector(cfg_off, CheapSumChecker(cfg_off), stats_off, defer_reports=True)
 
     t_torch, ref_logits, g_torch = timed_forward(contextlib.nullcontext)
@@ -531,9 +555,10 @@ def qwen_prefill_point(reps, warmup, decode_steps=0, cpu_seconds=0.0, dtype="bf1
                 torch.cuda.synchronize()
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record()
-                for i in range(decode_steps):
-                    with ctx_factory():
-                        model(nxt, caches, tokens + 4 + i)
+                with _nvtx_range(nvtx, f"decode_len_{decode_steps}"):
+                    for i in range(decode_steps):
+                        with ctx_factory():
+                            model(nxt, caches, tokens + 4 + i)
                 e1.record()
                 torch.cuda.synchronize()
             return e0.elapsed_time(e1) / decode_steps
@@ -1227,7 +1252,7 @@ def run_model(args):
     reps = max(args.steps, 3) if args.steps < 300 else 10
     warmup = max(args.warmup, 2)
     res = qwen_prefill_point(reps, warmup, decode_steps=32, cpu_seconds=0.0 if args.no_cpu_baseline else 20.0,
-                             dtype=args.dtype)
+                             dtype=args.dtype, nvtx=args.nvtx_enable)
     cfg = QWEN2_7B
     line = {
         "metric": "Qwen2-7B prefill-512 tokens/s (every linear ABFT-protected)",

@@ -59,6 +59,11 @@ class AbftConfig:
     thr_scale: float = 1e-3  # tau of the per-tile row-checksum bound tau*sqrt(K)*max|C|
     thr_abs: float = 0.0  # absolute floor added to that bound
     report_capacity: int = 64  # fault records kept per call
+    # an NVTX range around every hooked F.linear / matmul / bmm call, named
+    # "abft.<op> MxNxK" (profilers can select the checked GEMMs of a model
+    # with it, e.g. ncu --nvtx --nvtx-include "regex:abft.*/"); read when the
+    # injector is entered
+    nvtx: bool = False
 
     def __post_init__(self) -> None:
         if self.checker_backend not in CHECKER_BACKENDS:

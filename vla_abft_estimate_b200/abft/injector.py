@@ -689,8 +689,31 @@ class AbftInjector(AbstractContextManager):
         return out.reshape(*a.shape[:-1], n)
 
     # ------------------------------------------------------------- wrappers
+    @staticmethod
+    def _nvtx_name(op: str, a: Any, b: Any, linear: bool = False) -> str:
+        """"abft.<op> MxNxK" of a hooked call (rows of the flattened left
+        operand; N from the weight's rows for a linear)."""
+        try:
+            k = a.shape[-1]
+            m = a.numel() // k if k else 0
+            n = b.shape[0] if linear else b.shape[-1]
+            return f"abft.{op} {m}x{n}x{k}"
+        except (AttributeError, IndexError, TypeError):
+            return f"abft.{op}"
+
+    def _in_nvtx_range(self, name: str, fn: Callable[..., torch.Tensor], *args: Any, **kwargs: Any) -> Any:
+        torch.cuda.nvtx.range_push(name)
+        try:
+            return fn(*args, **kwargs)
+        finally:
+            torch.cuda.nvtx.range_pop()
+
     def _wrap_linear(self, fn: Callable[..., torch.Tensor]) -> Callable[..., torch.Tensor]:
         def wrapped(input: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+            return self._in_nvtx_range(self._nvtx_name("linear", input, weight, linear=True), body, input, weight,
+                                       bias)
+
+        def body(input: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
             if self._fused_linear_ok(input, weight, bias):
                 if weight.shape[0] % 8 or weight.shape[1] % 8:
                     return self._fused_linear_padded(input, weight, bias)
@@ -703,10 +726,14 @@ class AbftInjector(AbstractContextManager):
             self._maybe_check("linear", a2, b2, c2, injected, bias_1d=bias)
             return out2
 
-        return wrapped
+        # cfg.nvtx is read when the injector is entered
+        return wrapped if self.cfg.nvtx else body
 
     def _wrap_matmul(self, fn: Callable[..., torch.Tensor]) -> Callable[..., torch.Tensor]:
         def wrapped(input: torch.Tensor, other: torch.Tensor, *args: Any, **kwargs: Any) -> torch.Tensor:
+            return self._in_nvtx_range(self._nvtx_name("matmul", input, other), body, input, other, *args, **kwargs)
+
+        def body(input: torch.Tensor, other: torch.Tensor, *args: Any, **kwargs: Any) -> torch.Tensor:
             if not args and not kwargs and self._fused_mm_ok(input, other):
                 out = self._fused_matmul(input, other)
                 if out is not None:
@@ -719,10 +746,14 @@ class AbftInjector(AbstractContextManager):
             self._maybe_check("matmul", a2, b2, c2, injected)
             return out2
 
-        return wrapped
+        # cfg.nvtx is read when the injector is entered
+        return wrapped if self.cfg.nvtx else body
 
     def _wrap_bmm(self, fn: Callable[..., torch.Tensor]) -> Callable[..., torch.Tensor]:
         def wrapped(input: torch.Tensor, mat2: torch.Tensor, *args: Any, **kwargs: Any) -> torch.Tensor:
+            return self._in_nvtx_range(self._nvtx_name("bmm", input, mat2), body, input, mat2, *args, **kwargs)
+
+        def body(input: torch.Tensor, mat2: torch.Tensor, *args: Any, **kwargs: Any) -> torch.Tensor:
             if (not args and not kwargs and self._fused_mm_ok(input, mat2) and input.dim() == 3 and mat2.dim() == 3
                     and input.shape[0] == mat2.shape[0] and 0 < input.shape[0] <= 65535):
                 return self._fused_bmm(input, mat2)
@@ -733,7 +764,8 @@ class AbftInjector(AbstractContextManager):
                 self._maybe_check("bmm", input[bi], mat2[bi], out2[bi], injected)
             return out2
 
-        return wrapped
+        # cfg.nvtx is read when the injector is entered
+        return wrapped if self.cfg.nvtx else body
 
 
 class CapturedChecks:
