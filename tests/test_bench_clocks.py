@@ -2,7 +2,9 @@
 
 The sampler polls NVML in a thread; here the samples are planted directly,
 so the summary logic (window, median, slowdown reasons, samples whose
-reasons could not be read) is checked without a GPU.
+reasons could not be read) is checked without a GPU. So is the paired
+check-overhead estimator, which compares the two variants within each
+round of interleaved launches.
 """
 import importlib.util
 import os
@@ -49,3 +51,13 @@ def test_summary_reports_an_empty_window_and_unreadable_reasons(bench):
 def test_uuids_get_the_nvml_prefix(bench):
     s = bench.ClockSampler(["58a0e2b8-0000", "GPU-1234"])
     assert s.uuids == ["GPU-58a0e2b8-0000", "GPU-1234"]
+
+
+def test_paired_overhead_cancels_drift_between_rounds(bench):
+    """Each round's checked / unchecked ratio is taken within the round, so a
+    clock step between rounds (every launch of round 3 slower) does not move
+    the estimate, while the ratio of medians would."""
+    off = [100.0, 100.0, 100.0, 150.0, 150.0]
+    chk = [107.0, 107.0, 107.0, 160.5, 160.5]
+    assert bench.paired_overhead_pct(chk, off) == pytest.approx(7.0)
+    assert bench.paired_overhead_pct([110.0, 90.0, 105.0], [100.0, 100.0, 100.0]) == pytest.approx(5.0)
